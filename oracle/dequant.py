@@ -1,0 +1,106 @@
+"""ggml block dequantisation, restated in numpy (oracle; test infrastructure).
+
+All three formats dequantise EXACTLY in fp32: every weight is a product of an
+fp16 scale with small integers whose significands fit in 24 bits, so the fp32
+values below equal the real-number values.  The reference's dense GEMVs round
+each weight to fp16 before use (engine/ffn8v11.cu:115-117 ``__float2half``);
+that rounding is an artefact of its fp16-product kernels, not of the format, and
+is not part of this oracle (the golden fixtures keep the reference's
+fp16-rounded port too, and the tests relate the two).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .tables import iq3xxs_grid_bytes, iq4nl_kvalues, ksigns_iq2xs
+
+QK = 256
+
+
+def _f16(b: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(b).view(np.float16)[..., 0].astype(np.float32)
+
+
+def dequant_iq3xxs(raw: np.ndarray, k: int) -> np.ndarray:
+    """IQ3_XXS rows (GGUF block order d | qs[64] | scales[32]) -> f32 [n, k].
+
+    Per 32-weight group ib: sw = scales word ib, db = d*(0.5 + (sw>>28))*0.5;
+    unit l (8 weights) takes sign field (sw >> 7l) & 127 expanded to 8 bits
+    with even parity, and two grid entries qs[8ib+2l], qs[8ib+2l+1].
+    Follows reference engine/pack_w4.py:39-69 (``dequant_iq3xxs``) and the
+    lane math of engine/ffn8v11.cu:103-116, without the final fp16 round.
+    """
+    n = raw.shape[0]
+    nb = k // QK
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 98)
+    d = _f16(blk[..., 0:2])                                            # [n, nb]
+    qs = blk[..., 2:66]                                                # [n, nb, 64]
+    sw = np.ascontiguousarray(blk[..., 66:98]).view(np.uint32)         # [n, nb, 8]
+    db = d[..., None] * ((sw >> 28).astype(np.float32) + np.float32(0.5)) * np.float32(0.5)
+    fields = (sw[..., None] >> (np.arange(4, dtype=np.uint32) * 7)) & 0x7F   # [n, nb, 8, 4]
+    s8 = ksigns_iq2xs()[fields]                                        # [n, nb, 8, 4]
+    bits = (s8[..., None] >> np.arange(8, dtype=np.uint8)) & 1          # [n, nb, 8, 4, 8]
+    sign = np.where(bits != 0, np.float32(-1.0), np.float32(1.0))
+    g = iq3xxs_grid_bytes()[qs].astype(np.float32).reshape(n, nb, 8, 4, 8)
+    w = (db[..., None, None] * g) * sign
+    return w.reshape(n, k).astype(np.float32)
+
+
+def dequant_q6k(raw: np.ndarray, k: int) -> np.ndarray:
+    """Q6_K rows (ql[128] | qh[64] | sc[16] int8 | d f16) -> f32 [n, k].
+
+    Weight i = 128h + 32j + l (h half, j quarter, l 0..31):
+    q = ((ql[64h + 32(j&1) + l] >> 4(j>>1)) & 15) | (((qh[32h + l] >> 2j) & 3) << 4),
+    w = (d * sc[i >> 4]) * (q - 32).  Reference engine/mm/MM_P2_ports.py:21-45
+    (``dq_q6_k``) and engine/mm/MM_P6_h6kam.cu:45-56.
+    """
+    n = raw.shape[0]
+    nb = k // QK
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 210)
+    ql = blk[..., 0:128].astype(np.int32)
+    qh = blk[..., 128:192].astype(np.int32)
+    sc = blk[..., 192:208].view(np.int8).astype(np.float32)
+    d = _f16(blk[..., 208:210])
+    i = np.arange(QK)
+    h, j, l = i >> 7, (i >> 5) & 3, i & 31
+    lo = (ql[..., 64 * h + 32 * (j & 1) + l] >> (4 * (j >> 1))) & 15
+    hi = (qh[..., 32 * h + l] >> (2 * j)) & 3
+    q = (lo | (hi << 4)) - 32                                          # [n, nb, 256]
+    t = d[..., None] * sc                                              # [n, nb, 16] (d*sc first)
+    w = t[..., i >> 4] * q.astype(np.float32)
+    return w.reshape(n, k).astype(np.float32)
+
+
+def dequant_iq4xs(raw: np.ndarray, k: int) -> np.ndarray:
+    """IQ4_XS rows (d f16 | scales_h u16 | scales_l[4] | qs[128]) -> f32 [n, k].
+
+    Group ib (32 weights): ls = ((scales_l[ib>>1] >> 4(ib&1)) & 15) | (((scales_h >> 2ib) & 3) << 4),
+    dl = d * (ls - 32); element e < 16 is the low nibble of qs[16ib + e], e >= 16
+    the high nibble of qs[16ib + e - 16]; w = dl * kvalues[nibble].
+    Reference engine/mm/MM_P0_d2_repack.py:78-93 (``dq_iq4_xs``).
+    """
+    n = raw.shape[0]
+    nb = k // QK
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 136)
+    d = _f16(blk[..., 0:2])
+    sh = np.ascontiguousarray(blk[..., 2:4]).view(np.uint16)[..., 0].astype(np.int32)
+    sl = blk[..., 4:8].astype(np.int32)
+    qs = blk[..., 8:136].reshape(n, nb, 8, 16).astype(np.int32)
+    ib = np.arange(8)
+    ls = ((sl[..., ib >> 1] >> (4 * (ib & 1))) & 15) | (((sh[..., None] >> (2 * ib)) & 3) << 4)
+    dl = d[..., None] * (ls - 32).astype(np.float32)                   # [n, nb, 8]
+    nib = np.concatenate([qs & 15, qs >> 4], axis=-1)                  # [n, nb, 8, 32]
+    w = dl[..., None] * iq4nl_kvalues()[nib]
+    return w.reshape(n, k).astype(np.float32)
+
+
+_DQ = {"iq3_xxs": dequant_iq3xxs, "q6_k": dequant_q6k, "iq4_xs": dequant_iq4xs}
+
+
+def dequant(qtype: str, raw: np.ndarray, k: int, chunk_rows: int = 8192) -> np.ndarray:
+    """Dequantise in row chunks (bounded temporary memory)."""
+    n = raw.shape[0]
+    out = np.empty((n, k), dtype=np.float32)
+    for r0 in range(0, n, chunk_rows):
+        out[r0:r0 + chunk_rows] = _DQ[qtype](raw[r0:r0 + chunk_rows], k)
+    return out
