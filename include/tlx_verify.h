@@ -1,0 +1,152 @@
+/* ThunderLlamaX speculative-verify path on B200 (sm_100a) -- C ABI.
+ *
+ * Plain pointers and sizes only.  Every device entry point is stream-ordered,
+ * allocates nothing, performs no host synchronisation (graph-capturable),
+ * checks its arguments on the host before launching, and returns 0 or a
+ * negative TLX_ERR_* code.  Device pointers are CUDA device addresses on the
+ * current device; `stream` is a cudaStream_t (NULL = legacy default stream).
+ *
+ * Reference boundary being replaced: the per-kernel NVProgram call surface
+ * prog(*device_buffers, global_size, local_size) of engine/engine0.py:99-106
+ * with graph entries (prog, (bufs...), grid) of engine/gcycle.py:39-47; buffer
+ * ownership per engine/engine0.py:65-95 (caller preallocates, kernels never
+ * allocate).  Launch geometry is chosen here instead of being encoded in
+ * kernel names (engine/gcycle.py:45).
+ */
+#ifndef TLX_VERIFY_H
+#define TLX_VERIFY_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids (GGUF tensor types) */
+#define TLX_Q6_K 14
+#define TLX_IQ3_XXS 18
+#define TLX_IQ4_XS 23
+/* activation dtypes (ggml ids) */
+#define TLX_DT_F32 0
+#define TLX_DT_F16 1
+#define TLX_DT_BF16 30
+/* gemv modes for tlx_gemv_workspace_bytes */
+#define TLX_MODE_STORE 0
+#define TLX_MODE_GATE_UP 1
+#define TLX_MODE_ARGMAX 2
+
+#define TLX_OK 0
+#define TLX_ERR_SHAPE (-1)
+#define TLX_ERR_ALIGN (-2)
+#define TLX_ERR_DTYPE (-3)
+#define TLX_ERR_QTYPE (-4)
+#define TLX_ERR_WORKSPACE (-5)
+#define TLX_ERR_LAUNCH (-6)
+#define TLX_ERR_DEVICE (-7)
+#define TLX_ERR_NULL (-8)
+
+/* workspace error word bits (read with tlx_workspace_error) */
+#define TLX_WS_ERR_MBAR_TIMEOUT 1u
+
+const char* tlx_error_string(int code);
+/* 0 if the current device is an sm_100 part this library was built for */
+int tlx_device_check(void);
+int tlx_version(void);
+/* cap on CTAs per launch (0 = one per SM).  Tuning/testing knob: smaller values
+ * force split tiles and k-segments on small shapes. */
+void tlx_set_max_ctas(int n);
+
+/* ---- weight layout ------------------------------------------------------------
+ * GGUF rows (ggml block_iq3_xxs 98 B / block_q6_K 210 B per 256 weights) ->
+ * B200 tile layout (16-row tiles, one 16*block_bytes chunk per tile and block,
+ * same byte count as GGUF plus zero rows up to a multiple of 16).  Replaces the
+ * offline repackers engine/pack_w1c.py:18-45 (IQ3 row regions, Q6_K 212-B pad)
+ * and engine/pack_w7.py (packed7 units). */
+size_t tlx_tiled_bytes(int qtype, int64_t n_rows, int64_t k);
+/* host -> host; src rows are src_row_stride bytes apart */
+int tlx_pack_tiles(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst);
+/* device -> device (same layout), stream-ordered */
+int tlx_pack_tiles_device(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst,
+                          void* stream);
+/* inverse of tlx_pack_tiles (host), for round-trip checks */
+int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, void* dst);
+
+/* ---- workspace -----------------------------------------------------------------
+ * Caller-owned scratch for split-tile partial sums, per-tile arrival counters and
+ * argmax partials.  Zero it once (tlx_workspace_init) before first use; every
+ * successful launch leaves its counters at zero again.  One workspace must not be
+ * used by two launches that can overlap on the GPU. */
+size_t tlx_gemv_workspace_bytes(int mode, int qtype, int64_t n_rows, int64_t k, int m, int x_dtype);
+int tlx_workspace_init(void* ws, size_t ws_bytes, void* stream);
+/* launch plan for a shape: info[] = {tiles, blocks/row, k-segments, blocks/segment,
+ * CTAs, CTAs/segment, max pieces/tile-segment, columns, n-tiles, warps/CTA,
+ * ring stages, shared bytes} */
+int tlx_gemv_plan(int mode, int qtype, int64_t n_rows, int64_t k, int m, int x_dtype, int32_t* info, int n_info);
+/* synchronous read of the workspace error word (TLX_WS_ERR_* bits) */
+int tlx_workspace_error(const void* ws, uint32_t* err_out);
+
+/* ---- K-row dequantised matvec ----------------------------------------------------
+ * y[t][r] = sum_k W[r][k] * x[t][k] (+ residual[t][r]), t < m <= 16 (m <= 5 for
+ * fp32 x), fp32 accumulate; y is fp32 or fp16 (y_dtype).  W tiled
+ * (tlx_pack_tiles), grid = the 256 u32 IQ3_XXS grid entries (device; NULL for
+ * Q6_K).  bf16/fp16 activations are carried as fp16 inside the kernel (exact for
+ * |x| in [2^-24 * 2^7, 65504]); fp32 activations are split exactly into three
+ * fp16 parts.
+ * Replaces down8nw32_11(wd, gridf, gact, hh, y) engine/down8nw32_11.cu:88-126
+ * (residual = hh) and head8v11(w, xh, logits) engine/head8v11.cu:88-121. */
+int tlx_gemv(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+             int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y, int y_dtype, int64_t ldy,
+             void* ws, size_t ws_bytes, void* stream);
+
+/* ---- fused gate/up + SiLU ------------------------------------------------------------
+ * gact[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r], stored fp32 or fp16 (gact_dtype; fp16
+ * is what the down projection consumes, like the reference's fp16 gact).
+ * Replaces ffn8v11(wg, wu, gridf, hhx, gact) engine/ffn8v11.cu:88-133 and the r7
+ * twin engine/ffn8v11r7.cu:261. */
+int tlx_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,
+                    int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* gact, int gact_dtype,
+                    int64_t ldg, void* ws, size_t ws_bytes, void* stream);
+
+/* ---- LM head fused with per-row argmax (+ greedy accept) ---------------------------
+ * For each token t: (max_r logit[t][r], lowest r attaining it) over the rows of W,
+ * reported as global ids row_offset + r (vocab sharding).  No logits reach HBM.
+ * out_keys[t] (optional) = the packed u64 key used for cross-shard merging.  If
+ * accept_out != NULL: m = longest prefix with idx[s] == drafts[s] (s < n_drafts),
+ * accept_out[0] = m, accept_out[1] = idx[m] (needs m_tokens >= n_drafts + 1).
+ * Replaces head8v11 + amx3 (engine/head8v11.cu:88-121, engine/amx3.cu:117-142),
+ * the fused h6kam_PP + amred36 (engine/mm/MM_P6_h6kam.cu:18-95,
+ * engine/mm/MM_P6_amred36.cu:4-30) and acc36 (engine/mm/MM_P7_acc36.cu:11-25). */
+int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                    int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
+                    uint64_t* out_keys, const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws,
+                    size_t ws_bytes, void* stream);
+
+/* ---- argmax over materialised logits (amx3 / h_argmax) -----------------------------
+ * amds[t] = argmax_v logits[t*ld + v] (fp32 or fp16 logits), strict '>' so the
+ * lowest index wins ties and NaN never wins.  engine/amx3.cu:117-142. */
+int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld, int32_t* amds, void* stream);
+
+/* merge per-shard argmax keys [n_shards][m] (after an all-gather) -> global
+ * (max, idx) and optional accept, same rules as tlx_head_argmax. */
+int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
+                     const int32_t* drafts, int n_drafts, int32_t* accept_out, void* stream);
+
+/* ---- greedy acceptance ------------------------------------------------------------
+ * acc36: m = longest prefix amds[s] == drafts[s], s < k; mb[0] = m;
+ * eb[0] = m, eb[1] = amds[m].  engine/mm/MM_P7_acc36.cu:11-25. */
+int tlx_accept(const int32_t* amds, const int32_t* drafts, int k, int32_t* mb, int32_t* eb, void* stream);
+
+/* accept11k with its commit side effects (engine/accept11k.cu:11-58): drafts[10]
+ * replace the ten 1-int dring0..9 buffers; writes tok_hist[pos..pos+m],
+ * cur_slot, pos_slot += m+1, m_slot, m_hist[cyc], emit[0..15], cyc_slot += 1,
+ * h_seed = xA[m*dim ..], dhd_seed = m == 0 ? hd_d0 : hd_d1. */
+int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, int32_t* m_slot, int32_t* m_hist,
+                  int32_t* cyc_slot, int32_t* pos_slot, int32_t* cur_slot, int32_t* tok_hist, float* h_seed,
+                  const float* hd_d0, const float* hd_d1, float* dhd_seed, int32_t* emit, const int32_t* l_hist,
+                  int dim, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TLX_VERIFY_H */

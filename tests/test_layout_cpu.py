@@ -1,0 +1,159 @@
+"""CPU checks of the C library: it loads, exports the header's symbols, and its
+tile packer + the decoder arithmetic (restated here in numpy, lane by lane, the
+way formats.cuh's q6_group / iq3_mma compute) reproduce the oracle's exact fp32
+weights.  No GPU calls."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle
+from thunderllamax_b200 import _lib, ops, synth
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "tlx_verify.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:[\w\*]+\s+)+\**(tlx_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) >= 15
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    assert lib.tlx_version() >= 1
+
+
+def test_error_strings_and_host_argument_checks():
+    lib = _lib.lib()
+    assert lib.tlx_error_string(-1).decode().startswith("unsupported")
+    assert lib.tlx_tiled_bytes(14, 10, 300) == 0          # k not a multiple of 256
+    assert lib.tlx_tiled_bytes(99, 16, 256) == 0          # unknown qtype
+    assert lib.tlx_tiled_bytes(14, 17, 512) == 2 * 2 * 3360
+    assert lib.tlx_gemv_workspace_bytes(0, 14, 16, 256, 17, 30) == 0   # m > 16
+    assert lib.tlx_gemv_workspace_bytes(0, 14, 16, 256, 6, 0) == 0     # fp32 x: m <= 5
+
+
+@pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98)])
+def test_pack_unpack_round_trip(qtype, gen, bb):
+    rng = np.random.default_rng(1)
+    for n in (1, 16, 37):
+        raw = gen(rng, n, 512)
+        t = ops.pack_tiles_host(qtype, raw, 512)
+        assert t.size == ((n + 15) // 16) * 2 * 16 * bb
+        back = ops.unpack_tiles_host(qtype, t, n, 512, raw.shape[1])
+        assert np.array_equal(back, raw)
+
+
+def _f16(x):
+    return np.float32(np.float16(x))
+
+
+def emulate_q6(tiled, n_rows, k):
+    """Weights as the device decodes them: d * fp16((q-32)*sc) per (row, k)."""
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    ch = tiled.reshape(T, nb, 3360)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            d16 = c[3328:3360].view(np.float16).astype(np.float32).reshape(8, 2)
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                w = np.array([c[((i >> 2) * 32 + lane) * 16 + (i & 3) * 4:][:4].view(np.uint32)[0]
+                              for i in range(24)], dtype=np.uint64)
+                sc = (c[3072 + lane * 8:3080 + lane * 8] ^ 0x80).view(np.int8).astype(np.float32)
+                for gam in range(8):
+                    W0, W1, W2 = (int(v) for v in w[3 * gam:3 * gam + 3])
+                    magic = 0x64006400
+                    p = [(W0 & 0x003F003F) | magic, ((W0 >> 6) & 0x003F003F) | magic,
+                         (W1 & 0x003F003F) | magic, ((W1 >> 6) & 0x003F003F) | magic,
+                         (W2 & 0x003F003F) | magic, ((W2 >> 6) & 0x003F003F) | magic,
+                         ((W0 >> 12) & 0x000F000F) | ((W2 >> 8) & 0x00300030) | magic,
+                         ((W1 >> 12) & 0x000F000F) | ((W2 >> 10) & 0x00300030) | magic]
+                    for pi, pv in enumerate(p):
+                        mu, r = pi >> 2, pi & 3
+                        m = 2 * gam + mu
+                        rr = r & 1
+                        row = t * 16 + g + 8 * rr
+                        s = sc[(gam >> 1) * 2 + rr]
+                        for h in range(2):
+                            half = (pv >> (16 * h)) & 0xFFFF
+                            v = np.frombuffer(np.uint16(half).tobytes(), np.float16)[0].astype(np.float32)
+                            a = _f16(_f16(v - 1056.0) * s)
+                            kk = b * 256 + 64 * q + 4 * m + 2 * (r >> 1) + h
+                            W[row, kk] = d16[g, rr] * a
+    return W[:n_rows]
+
+
+def emulate_iq3(tiled, n_rows, k):
+    grid = oracle.iq3xxs_grid_u32()
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    ch = tiled.reshape(T, nb, 1568)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            d16 = c[1536:1568].view(np.float16).astype(np.float32).reshape(8, 2)
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                sw = c[1024 + lane * 16:1040 + lane * 16].view(np.uint32).reshape(2, 2)
+                for m in range(16):
+                    cc, l, e = m >> 3, (m >> 1) & 3, m & 1
+                    for rr in range(2):
+                        idx = c[rr * 512 + lane * 16 + m]
+                        G = int(grid[idx])
+                        v = int(sw[rr, cc])
+                        ms = 2 * (v >> 28) + 1
+                        t_ = v ^ (v >> 1)
+                        t_ ^= t_ >> 2
+                        t_ ^= t_ >> 4
+                        par = t_ ^ (v >> 7)
+                        s8 = ((v >> (7 * l)) & 0x7F) | (((par >> (7 * l)) & 1) << 7)
+                        for j in range(4):
+                            mag = (G >> (8 * j)) & 0xFF
+                            a = float(mag * ms) * (-1.0 if (s8 >> (4 * e + j)) & 1 else 1.0)
+                            row = t * 16 + g + 8 * rr
+                            kk = b * 256 + 64 * q + 4 * m + j
+                            W[row, kk] = (d16[g, rr] * np.float32(0.25)) * np.float32(a)
+    return W[:n_rows]
+
+
+def test_q6_tile_decode_matches_oracle_exactly():
+    rng = np.random.default_rng(7)
+    raw = synth.q6k_blocks(rng, 19, 512)
+    tiled = ops.pack_tiles_host("q6_k", raw, 512)
+    got = emulate_q6(tiled, 19, 512)
+    ref = oracle.dequant_q6k(raw, 512)
+    assert np.array_equal(got, ref)
+
+
+def test_q6_tile_decode_full_range_scales():
+    # real checkpoints use int8 sub-scales in [-128, 127]: integer products in
+    # (2048, 4096] round to even (<= 2^-11 relative), exact for |(q-32)*sc| <= 2048
+    rng = np.random.default_rng(8)
+    raw = synth.q6k_blocks(rng, 16, 256).reshape(16, 1, 210)
+    raw[:, :, 192:208] = rng.integers(-128, 128, (16, 1, 16)).astype(np.int8).view(np.uint8)
+    raw = raw.reshape(16, 210)
+    got = emulate_q6(ops.pack_tiles_host("q6_k", raw, 256), 16, 256)
+    ref = oracle.dequant_q6k(raw, 256)
+    rel = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-30)
+    assert rel.max() <= 2.0 ** -11
+    d = raw[:, 208:210].copy().view(np.float16).astype(np.float32)
+    small = np.abs(ref) <= 2048 * d
+    assert np.array_equal(got[small], ref[small])
+
+
+def test_iq3_tile_decode_matches_oracle_exactly():
+    rng = np.random.default_rng(9)
+    raw = synth.iq3xxs_blocks(rng, 21, 512)
+    tiled = ops.pack_tiles_host("iq3_xxs", raw, 512)
+    got = emulate_iq3(tiled, 21, 512)
+    ref = oracle.dequant_iq3xxs(raw, 512)
+    assert np.array_equal(got, ref)

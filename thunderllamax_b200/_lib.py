@@ -1,0 +1,82 @@
+"""ctypes binding of libtlx_b200.so (the C ABI declared in include/tlx_verify.h).
+
+There is no fallback: if the library is missing or no sm_100 device is present,
+every call raises.  Build it with ``python -m thunderllamax_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("TLX_LIB", os.path.join(_HERE, "libtlx_b200.so"))
+
+TLX_Q6_K, TLX_IQ3_XXS, TLX_IQ4_XS = 14, 18, 23
+TLX_DT_F32, TLX_DT_F16, TLX_DT_BF16 = 0, 1, 30
+MODE_STORE, MODE_GATE_UP, MODE_ARGMAX = 0, 1, 2
+QTYPES = {"q6_k": TLX_Q6_K, "iq3_xxs": TLX_IQ3_XXS, "iq4_xs": TLX_IQ4_XS}
+
+
+class TLXError(RuntimeError):
+    pass
+
+
+_lock = threading.Lock()
+_lib = None
+
+c_i64, c_int, c_size, c_vp, c_u32p = ctypes.c_int64, ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p
+
+_SIGS = {
+    "tlx_error_string": (ctypes.c_char_p, [c_int]),
+    "tlx_device_check": (c_int, []),
+    "tlx_version": (c_int, []),
+    "tlx_set_max_ctas": (None, [c_int]),
+    "tlx_tiled_bytes": (c_size, [c_int, c_i64, c_i64]),
+    "tlx_pack_tiles": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "tlx_pack_tiles_device": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "tlx_unpack_tiles": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp]),
+    "tlx_gemv_workspace_bytes": (c_size, [c_int, c_int, c_i64, c_i64, c_int, c_int]),
+    "tlx_workspace_init": (c_int, [c_vp, c_size, c_vp]),
+    "tlx_gemv_plan": (c_int, [c_int, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_int]),
+    "tlx_workspace_error": (c_int, [c_vp, c_vp]),
+    "tlx_gemv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp, c_int,
+                         c_i64, c_vp, c_size, c_vp]),
+    "tlx_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_int,
+                                c_i64, c_vp, c_size, c_vp]),
+    "tlx_head_argmax": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                c_vp, c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
+    "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
+    "tlx_argmax_merge": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
+    "tlx_accept": (c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
+    "tlx_accept11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, c_int, c_vp]),
+}
+
+
+def lib():
+    """Load the library once; raises TLXError if it is not built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise TLXError(f"{LIB_PATH} not found: build it with `python -m thunderllamax_b200.build`")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(handle, name, None)
+                if fn is None:
+                    continue
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return [n for n in _SIGS if hasattr(lib(), n)]
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().tlx_error_string(rc).decode()
+        raise TLXError(f"{what}: {msg} ({rc})")

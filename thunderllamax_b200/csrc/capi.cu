@@ -1,0 +1,378 @@
+// C ABI of the verify-path library (declarations in include/tlx_verify.h).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "formats.cuh"
+#include "tlx_internal.h"
+
+using namespace tlx;
+
+namespace {
+
+constexpr int kEpiStore = 0, kEpiGateUp = 1, kEpiArgmax = 2;
+int g_max_ctas = 0;  // 0 = one CTA per SM
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool valid_qtype(int qt) { return qt == QT_Q6_K || qt == QT_IQ3_XXS; }
+
+// ---- small kernels -----------------------------------------------------------------
+
+// acc36 semantics (engine/mm/MM_P7_acc36.cu:18-24)
+__global__ void accept_kernel(const int32_t* __restrict__ amds, const int32_t* __restrict__ drafts, int k,
+                              int32_t* __restrict__ mb, int32_t* __restrict__ eb) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int m = 0;
+    while (m < k && amds[m] == drafts[m]) ++m;
+    if (mb) mb[0] = m;
+    if (eb) {
+      eb[0] = m;
+      eb[1] = amds[m];
+    }
+  }
+}
+
+// accept11k semantics (engine/accept11k.cu:23-57); the m ladder is a loop over the
+// ten draft ids, the state copies are spread over the CTA
+__global__ void accept11k_kernel(const int32_t* __restrict__ amds, const int32_t* __restrict__ drafts,
+                                 const float* __restrict__ xA, int32_t* __restrict__ m_slot,
+                                 int32_t* __restrict__ m_hist, int32_t* __restrict__ cyc_slot,
+                                 int32_t* __restrict__ pos_slot, int32_t* __restrict__ cur_slot,
+                                 int32_t* __restrict__ tok_hist, float* __restrict__ h_seed,
+                                 const float* __restrict__ hd_d0, const float* __restrict__ hd_d1,
+                                 float* __restrict__ dhd_seed, int32_t* __restrict__ emit,
+                                 const int32_t* __restrict__ l_hist, int dim) {
+  __shared__ int ms;
+  if (threadIdx.x == 0) {
+    int m = 0;
+    while (m < 10 && amds[m] == drafts[m]) ++m;
+    const int pos = pos_slot[0];
+    for (int t = 0; t <= m; ++t) tok_hist[pos + t] = amds[t];
+    cur_slot[0] = amds[m];
+    pos_slot[0] = pos + m + 1;
+    m_slot[0] = m;
+    const int cyc = cyc_slot[0];
+    m_hist[cyc] = m;
+    emit[0] = pos + m + 1;
+    emit[1] = m;
+    for (int t = 0; t < 11; ++t) emit[2 + t] = amds[t];
+    emit[13] = 0;
+    emit[14] = cyc;
+    emit[15] = l_hist[cyc];
+    cyc_slot[0] = cyc + 1;
+    ms = m;
+  }
+  __syncthreads();
+  const int m = ms;
+  const float* dh = m == 0 ? hd_d0 : hd_d1;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    if (h_seed && xA) h_seed[i] = xA[static_cast<int64_t>(m) * dim + i];
+    if (dhd_seed && dh) dhd_seed[i] = dh[i];
+  }
+}
+
+// per-row argmax over materialised logits (engine/amx3.cu:117-142): one CTA per row
+template <typename T>
+__global__ void argmax_rows_kernel(const T* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ amds) {
+  const T* row = logits + blockIdx.x * ld;
+  uint64_t best = 0ull;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    float v;
+    if constexpr (sizeof(T) == 2) v = __half2float(row[i]);
+    else v = row[i];
+    const uint64_t k = argmax_key(v, static_cast<uint32_t>(i));
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ uint64_t wb[32];
+  if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t b = 0ull;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = wb[w] > b ? wb[w] : b;
+    amds[blockIdx.x] = key_index(b);
+  }
+}
+
+__global__ void argmax_merge_kernel(const uint64_t* __restrict__ keys, int n_shards, int m,
+                                    float* __restrict__ out_max, int32_t* __restrict__ out_idx,
+                                    const int32_t* __restrict__ drafts, int n_drafts,
+                                    int32_t* __restrict__ accept_out) {
+  __shared__ int32_t ids[16];
+  const int t = threadIdx.x;
+  if (t < m) {
+    uint64_t b = 0ull;
+    for (int s = 0; s < n_shards; ++s) {
+      const uint64_t k = keys[s * m + t];
+      b = k > b ? k : b;
+    }
+    if (out_max) out_max[t] = key_value(b);
+    if (out_idx) out_idx[t] = key_index(b);
+    ids[t] = key_index(b);
+  }
+  __syncthreads();
+  if (t == 0 && accept_out) {
+    int mm = 0;
+    while (mm < n_drafts && ids[mm] == drafts[mm]) ++mm;
+    accept_out[0] = mm;
+    accept_out[1] = ids[mm];
+  }
+}
+
+// device packer: one CTA of 32 threads per (tile, block) chunk
+__global__ void pack_tiles_kernel(int qt, const uint8_t* __restrict__ src, int64_t n_rows, int nb, int64_t stride,
+                                  uint8_t* __restrict__ dst) {
+  const int64_t chunk_id = blockIdx.x;
+  const int64_t t = chunk_id / nb;
+  const int b = static_cast<int>(chunk_id - t * nb);
+  const uint32_t bb = block_bytes(qt);
+  const uint8_t* rows[16];
+  for (int r = 0; r < 16; ++r) {
+    const int64_t row = t * 16 + r;
+    rows[r] = row < n_rows ? src + row * stride + static_cast<int64_t>(b) * bb : nullptr;
+  }
+  uint8_t* out = dst + chunk_id * chunk_bytes(qt);
+  if (qt == QT_Q6_K) pack_q6_lane(rows, threadIdx.x, out);
+  else pack_iq3_lane(rows, threadIdx.x, out);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tlx_error_string(int code) {
+  switch (code) {
+    case TLX_OK: return "ok";
+    case TLX_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case TLX_ERR_ALIGN: return "pointer or stride misaligned";
+    case TLX_ERR_DTYPE: return "unsupported activation dtype";
+    case TLX_ERR_QTYPE: return "unsupported quantisation type";
+    case TLX_ERR_WORKSPACE: return "workspace too small";
+    case TLX_ERR_LAUNCH: return "CUDA launch failed";
+    case TLX_ERR_DEVICE: return "no sm_100 device";
+    case TLX_ERR_NULL: return "required pointer is NULL";
+    default: return "unknown error";
+  }
+}
+
+int tlx_version(void) { return 1; }
+
+int tlx_device_check(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TLX_ERR_DEVICE;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return (major == 10 && minor == 0) ? TLX_OK : TLX_ERR_DEVICE;
+}
+
+// 0 = one CTA per SM; tests lower it to force split tiles on small shapes
+void tlx_set_max_ctas(int n) { g_max_ctas = n < 0 ? 0 : n; }
+
+size_t tlx_tiled_bytes(int qtype, int64_t n_rows, int64_t k) {
+  if (!valid_qtype(qtype) || n_rows <= 0 || k <= 0 || k % kQK) return 0;
+  const int64_t tiles = (n_rows + 15) / 16;
+  return static_cast<size_t>(tiles) * (k / kQK) * chunk_bytes(qtype);
+}
+
+int tlx_pack_tiles(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst) {
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!src || !dst) return TLX_ERR_NULL;
+  if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
+  const int nb = static_cast<int>(k / kQK);
+  const uint32_t bb = block_bytes(qtype);
+  if (src_row_stride < static_cast<int64_t>(nb) * bb) return TLX_ERR_SHAPE;
+  const int64_t tiles = (n_rows + 15) / 16;
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  for (int64_t t = 0; t < tiles; ++t)
+    for (int b = 0; b < nb; ++b) {
+      const uint8_t* rows[16];
+      for (int r = 0; r < 16; ++r) {
+        const int64_t row = t * 16 + r;
+        rows[r] = row < n_rows ? s + row * src_row_stride + static_cast<int64_t>(b) * bb : nullptr;
+      }
+      uint8_t* out = d + (t * nb + b) * static_cast<int64_t>(chunk_bytes(qtype));
+      for (int lane = 0; lane < 32; ++lane) {
+        if (qtype == QT_Q6_K) pack_q6_lane(rows, lane, out);
+        else pack_iq3_lane(rows, lane, out);
+      }
+    }
+  return TLX_OK;
+}
+
+int tlx_pack_tiles_device(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst,
+                          void* stream) {
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!src || !dst) return TLX_ERR_NULL;
+  if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
+  const int nb = static_cast<int>(k / kQK);
+  if (src_row_stride < static_cast<int64_t>(nb) * block_bytes(qtype)) return TLX_ERR_SHAPE;
+  const int64_t chunks = (n_rows + 15) / 16 * nb;
+  if (chunks > 0x7FFFFFFF) return TLX_ERR_SHAPE;
+  pack_tiles_kernel<<<static_cast<unsigned>(chunks), 32, 0, as_stream(stream)>>>(
+      qtype, static_cast<const uint8_t*>(src), n_rows, nb, src_row_stride, static_cast<uint8_t*>(dst));
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, void* dst) {
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!tiled || !dst) return TLX_ERR_NULL;
+  if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
+  const int nb = static_cast<int>(k / kQK);
+  const uint32_t bb = block_bytes(qtype), ch = chunk_bytes(qtype);
+  const uint8_t* s = static_cast<const uint8_t*>(tiled);
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  const int64_t row_bytes = static_cast<int64_t>(nb) * bb;
+  for (int64_t row = 0; row < n_rows; ++row) {
+    const int64_t t = row / 16;
+    const int r = static_cast<int>(row % 16), g = r & 7, rr = r >> 3;
+    for (int b = 0; b < nb; ++b) {
+      const uint8_t* c = s + (t * nb + b) * static_cast<int64_t>(ch);
+      uint8_t* blk = d + row * row_bytes + static_cast<int64_t>(b) * bb;
+      if (qtype == QT_IQ3_XXS) {
+        blk[0] = c[1536 + g * 4 + rr * 2];
+        blk[1] = c[1536 + g * 4 + rr * 2 + 1];
+        for (int q = 0; q < 4; ++q) {
+          const int lane = 4 * g + q;
+          for (int cc = 0; cc < 2; ++cc) {
+            const int ib = 2 * q + cc;
+            for (int j = 0; j < 8; ++j) blk[2 + 8 * ib + j] = c[rr * 512 + lane * 16 + cc * 8 + j];
+            for (int j = 0; j < 4; ++j) blk[66 + 4 * ib + j] = c[1024 + lane * 16 + (rr * 2 + cc) * 4 + j];
+          }
+        }
+      } else {
+        std::memset(blk, 0, 192);
+        blk[208] = c[3328 + g * 4 + rr * 2];
+        blk[209] = c[3328 + g * 4 + rr * 2 + 1];
+        for (int q = 0; q < 4; ++q) {
+          const int lane = 4 * g + q;
+          for (int j = 0; j < 4; ++j) blk[192 + 4 * q + j] = c[3072 + lane * 8 + j * 2 + rr] ^ 0x80u;
+          uint32_t w[24];
+          for (int i = 0; i < 24; ++i) std::memcpy(&w[i], c + ((i >> 2) * 32 + lane) * 16 + (i & 3) * 4, 4);
+          for (int gam = 0; gam < 8; ++gam) {
+            const uint32_t W0 = w[3 * gam], W1 = w[3 * gam + 1], W2 = w[3 * gam + 2];
+            uint32_t P[8][2];
+            for (int h = 0; h < 2; ++h) {
+              const int sh = 16 * h;
+              P[0][h] = (W0 >> sh) & 63u;
+              P[1][h] = (W0 >> (sh + 6)) & 63u;
+              P[2][h] = (W1 >> sh) & 63u;
+              P[3][h] = (W1 >> (sh + 6)) & 63u;
+              P[4][h] = (W2 >> sh) & 63u;
+              P[5][h] = (W2 >> (sh + 6)) & 63u;
+              P[6][h] = ((W0 >> (sh + 12)) & 15u) | (((W2 >> (sh + 12)) & 3u) << 4);
+              P[7][h] = ((W1 >> (sh + 12)) & 15u) | (((W2 >> (sh + 14)) & 3u) << 4);
+            }
+            for (int p = 0; p < 8; ++p) {
+              const int mu = p >> 2, rsel = p & 3;
+              if ((rsel & 1) != rr) continue;
+              const int m = 2 * gam + mu;
+              for (int h = 0; h < 2; ++h) {
+                const int i = 64 * q + 4 * m + 2 * (rsel >> 1) + h;
+                const uint32_t v = P[p][h];
+                const int hh = i >> 7, j = (i >> 5) & 3, l = i & 31;
+                blk[64 * hh + 32 * (j & 1) + l] |= static_cast<uint8_t>((v & 15u) << (4 * (j >> 1)));
+                blk[128 + 32 * hh + l] |= static_cast<uint8_t>(((v >> 4) & 3u) << (2 * j));
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  return TLX_OK;
+}
+
+size_t tlx_gemv_workspace_bytes(int mode, int qtype, int64_t n_rows, int64_t k, int m, int x_dtype) {
+  return gemv_workspace_bytes(mode, qtype, n_rows, k, m, x_dtype, g_max_ctas);
+}
+
+int tlx_gemv_plan(int mode, int qtype, int64_t n_rows, int64_t k, int m, int x_dtype, int32_t* info, int n_info) {
+  return gemv_plan_info(mode, qtype, n_rows, k, m, x_dtype, g_max_ctas, info, n_info);
+}
+
+int tlx_workspace_init(void* ws, size_t ws_bytes, void* stream) {
+  if (!ws) return TLX_ERR_NULL;
+  return cudaMemsetAsync(ws, 0, ws_bytes, as_stream(stream)) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_workspace_error(const void* ws, uint32_t* err_out) {
+  if (!ws || !err_out) return TLX_ERR_NULL;
+  return cudaMemcpy(err_out, ws, 4, cudaMemcpyDeviceToHost) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_gemv(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+             int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y, int y_dtype, int64_t ldy,
+             void* ws, size_t ws_bytes, void* stream) {
+  return run_gemv(kEpiStore, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, residual, ldr, y, y_dtype, ldy, 0,
+                  nullptr, nullptr, nullptr, nullptr, 0, nullptr, ws, ws_bytes, g_max_ctas, as_stream(stream));
+}
+
+int tlx_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,
+                    int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* gact, int gact_dtype,
+                    int64_t ldg, void* ws, size_t ws_bytes, void* stream) {
+  return run_gemv(kEpiGateUp, qtype, w_gate, w_up, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, gact, gact_dtype,
+                  ldg, 0,
+                  nullptr, nullptr, nullptr, nullptr, 0, nullptr, ws, ws_bytes, g_max_ctas, as_stream(stream));
+}
+
+int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                    int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
+                    uint64_t* out_keys, const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws,
+                    size_t ws_bytes, void* stream) {
+  return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
+                  TLX_DT_F32, 0, row_offset, out_max, out_idx, out_keys, drafts, n_drafts, accept_out, ws, ws_bytes, g_max_ctas,
+                  as_stream(stream));
+}
+
+int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld, int32_t* amds, void* stream) {
+  if (!logits || !amds) return TLX_ERR_NULL;
+  if (m <= 0 || n <= 0 || ld < n || n > 0xFFFFFFFFll) return TLX_ERR_SHAPE;
+  if (dtype == TLX_DT_F32)
+    argmax_rows_kernel<float><<<m, 1024, 0, as_stream(stream)>>>(static_cast<const float*>(logits), n, ld, amds);
+  else if (dtype == TLX_DT_F16)
+    argmax_rows_kernel<__half><<<m, 1024, 0, as_stream(stream)>>>(static_cast<const __half*>(logits), n, ld, amds);
+  else
+    return TLX_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
+                     const int32_t* drafts, int n_drafts, int32_t* accept_out, void* stream) {
+  if (!keys) return TLX_ERR_NULL;
+  if (n_shards <= 0 || m <= 0 || m > 16) return TLX_ERR_SHAPE;
+  if (accept_out && (!drafts || n_drafts < 0 || n_drafts + 1 > m)) return TLX_ERR_SHAPE;
+  argmax_merge_kernel<<<1, 32, 0, as_stream(stream)>>>(keys, n_shards, m, out_max, out_idx, drafts, n_drafts,
+                                                       accept_out);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_accept(const int32_t* amds, const int32_t* drafts, int k, int32_t* mb, int32_t* eb, void* stream) {
+  if (!amds || (k > 0 && !drafts)) return TLX_ERR_NULL;
+  if (k < 0) return TLX_ERR_SHAPE;
+  accept_kernel<<<1, 32, 0, as_stream(stream)>>>(amds, drafts, k, mb, eb);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, int32_t* m_slot, int32_t* m_hist,
+                  int32_t* cyc_slot, int32_t* pos_slot, int32_t* cur_slot, int32_t* tok_hist, float* h_seed,
+                  const float* hd_d0, const float* hd_d1, float* dhd_seed, int32_t* emit, const int32_t* l_hist,
+                  int dim, void* stream) {
+  if (!amds || !drafts || !m_slot || !m_hist || !cyc_slot || !pos_slot || !cur_slot || !tok_hist || !emit ||
+      !l_hist)
+    return TLX_ERR_NULL;
+  if (dim < 0) return TLX_ERR_SHAPE;
+  accept11k_kernel<<<1, 256, 0, as_stream(stream)>>>(amds, drafts, xA, m_slot, m_hist, cyc_slot, pos_slot, cur_slot,
+                                                     tok_hist, h_seed, hd_d0, hd_d1, dhd_seed, emit, l_hist, dim);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+}  // extern "C"

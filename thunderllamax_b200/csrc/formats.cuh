@@ -1,0 +1,258 @@
+// B200 tile layouts for IQ3_XXS and Q6_K weights, and their device decoders.
+//
+// Rows are grouped in tiles of 16 (the M of one mma.sync.m16n8k16).  For tile t
+// and 256-weight block b the layout holds one contiguous CHUNK of
+// 16 * block_bytes bytes (IQ3_XXS: 16*98 = 1568, Q6_K: 16*210 = 3360), so the
+// HBM footprint equals the GGUF footprint exactly and every chunk starts on a
+// 16-byte boundary (chunk-major: offset (t*NB + b) * chunk_bytes).  Inside a
+// chunk the bytes are permuted (and, for the Q6_K sub-scales, XOR-biased) so
+// that lane l = 4g + q of a warp reads everything it needs with conflict-free
+// 16-byte shared-memory loads and dequantises straight into the A fragment of
+// mma.m16n8k16: rows g and g+8, block-local k in [64q, 64q+64).
+//
+// The k order inside an mma is free (a dot product is invariant under a
+// consistent permutation of k), so every mma m (0..15) of lane quarter q takes
+// weights k = 64q + 4m + {0,1,2,3} and the activations are staged to match:
+// B fragment of (lane quarter q, mma m, token t) = x[t][256b + 64q + 4m + 0..3].
+//
+// Exactness: both decoders produce fp16 values that are exact small integers
+// (IQ3_XXS: +-grid * (2s+1) <= 1922; Q6_K: (q-32) * sc, exact whenever
+// |(q-32)*sc| <= 2048, i.e. always for |sc| <= 64; larger integer products are
+// rounded to even, <= 2^-11 relative) and the remaining per-block
+// scale (d/4 resp. d) is applied to the fp32 mma result, so products and sums
+// are fp32-accurate.  References: the IQ3_XXS lane math of
+// engine/ffn8v11.cu:103-116 and the Q6_K lane math of engine/aq6k8v11.cu:96-118 /
+// engine/mm/MM_P6_h6kam.cu:45-56.
+#pragma once
+#include <cstdint>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace tlx {
+
+enum QType : int { QT_Q6_K = 14, QT_IQ3_XXS = 18, QT_IQ4_XS = 23 };
+
+constexpr int kTileRows = 16;
+constexpr int kQK = 256;
+constexpr uint32_t kChunkQ6 = 16 * 210;     // 3360
+constexpr uint32_t kChunkIq3 = 16 * 98;     // 1568
+
+__host__ __device__ constexpr uint32_t chunk_bytes(int qt) { return qt == QT_Q6_K ? kChunkQ6 : kChunkIq3; }
+__host__ __device__ constexpr uint32_t block_bytes(int qt) { return qt == QT_Q6_K ? 210u : 98u; }
+
+// ------------------------------------------------------------------------------------
+// Host packers (plain C++; also used by the C-ABI tlx_pack_tiles).
+// ------------------------------------------------------------------------------------
+
+#if defined(__CUDACC__)
+#define TLX_HD __host__ __device__
+#else
+#define TLX_HD
+#endif
+
+// 6-bit Q6_K quant of block-local weight i (0..255) of a GGUF block
+TLX_HD inline uint32_t q6_value(const uint8_t* blk, int i) {
+  const int h = i >> 7, j = (i >> 5) & 3, l = i & 31;
+  const uint32_t lo = (blk[64 * h + 32 * (j & 1) + l] >> (4 * (j >> 1))) & 15u;
+  const uint32_t hi = (blk[128 + 32 * h + l] >> (2 * j)) & 3u;
+  return lo | (hi << 4);
+}
+
+// Q6_K chunk, the part owned by one lane: rows[r] = r-th row's GGUF block b
+// (nullptr = zero row, stored as q = 32, sc = 0, d = 0)
+TLX_HD inline void pack_q6_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int gam = 0; gam < 8; ++gam) {
+    uint32_t P[8][2];  // pair P -> (u, v)
+    for (int p = 0; p < 8; ++p) {
+      const int mu = p >> 2, r = p & 3;
+      const int m = 2 * gam + mu;
+      const uint8_t* blk = rows[g + 8 * (r & 1)];
+      const int k = 64 * q + 4 * m + 2 * (r >> 1);
+      P[p][0] = blk ? q6_value(blk, k) : 32u;
+      P[p][1] = blk ? q6_value(blk, k + 1) : 32u;
+    }
+    uint32_t w[3];
+    w[0] = P[0][0] | (P[1][0] << 6) | ((P[6][0] & 15u) << 12) | (P[0][1] << 16) | (P[1][1] << 22) |
+           ((P[6][1] & 15u) << 28);
+    w[1] = P[2][0] | (P[3][0] << 6) | ((P[7][0] & 15u) << 12) | (P[2][1] << 16) | (P[3][1] << 22) |
+           ((P[7][1] & 15u) << 28);
+    w[2] = P[4][0] | (P[5][0] << 6) | ((P[6][0] >> 4) << 12) | ((P[7][0] >> 4) << 14) | (P[4][1] << 16) |
+           (P[5][1] << 22) | ((P[6][1] >> 4) << 28) | ((P[7][1] >> 4) << 30);
+    for (int i3 = 0; i3 < 3; ++i3) {
+      const int i = 3 * gam + i3;
+      uint8_t* dst = out + ((i >> 2) * 32 + lane) * 16 + (i & 3) * 4;
+      for (int bt = 0; bt < 4; ++bt) dst[bt] = static_cast<uint8_t>(w[i3] >> (8 * bt));
+    }
+  }
+  for (int j = 0; j < 4; ++j)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      const uint8_t sc = blk ? blk[192 + 4 * q + j] : 0;
+      out[3072 + lane * 8 + j * 2 + rr] = static_cast<uint8_t>(sc ^ 0x80u);
+    }
+  if (q == 0)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      out[3328 + g * 4 + rr * 2 + 0] = blk ? blk[208] : 0;
+      out[3328 + g * 4 + rr * 2 + 1] = blk ? blk[209] : 0;
+    }
+}
+
+// IQ3_XXS chunk (GGUF block order d | qs[64] | scales[32]), the part owned by one lane
+TLX_HD inline void pack_iq3_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint8_t* blk = rows[g + 8 * rr];
+    for (int c = 0; c < 2; ++c) {
+      const int ib = 2 * q + c;
+      for (int j = 0; j < 8; ++j) out[rr * 512 + lane * 16 + c * 8 + j] = blk ? blk[2 + 8 * ib + j] : 0;
+      for (int j = 0; j < 4; ++j) out[1024 + lane * 16 + (rr * 2 + c) * 4 + j] = blk ? blk[66 + 4 * ib + j] : 0;
+    }
+  }
+  if (q == 0)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      out[1536 + g * 4 + rr * 2 + 0] = blk ? blk[0] : 0;
+      out[1536 + g * 4 + rr * 2 + 1] = blk ? blk[1] : 0;
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// Device decoders.  Each works on one chunk in shared memory for the calling lane.
+// A fragments: a[m][0] = row g k+0/1, a[m][1] = row g+8 k+0/1, a[m][2] = row g k+2/3,
+// a[m][3] = row g+8 k+2/3 (k = 64q + 4m).
+// ------------------------------------------------------------------------------------
+#ifdef __CUDACC__
+
+constexpr uint32_t kMagic = 0x64006400u;      // fp16x2 (1024, 1024)
+constexpr uint32_t kMinus1056 = 0xE420E420u;  // fp16x2 (-1056, -1056)
+constexpr uint32_t kMinus1152 = 0xE480E480u;  // fp16x2 (-1152, -1152)
+constexpr uint32_t kMinus1024 = 0xE400E400u;  // fp16x2 (-1024, -1024)
+
+// Q6_K: per-block lane state
+struct Q6Lane {
+  uint32_t w[24];
+  uint32_t sc2[4][2];  // fp16x2 (sc, sc) for sub-block 4q+j, row g / g+8
+  uint32_t d;          // fp16 d of row g (lo) and row g+8 (hi)
+};
+
+__device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& s) {
+#pragma unroll
+  for (int p = 0; p < 6; ++p) {
+    const uint4 v = lds128(chunk + (p * 32 + lane) * 16);
+    s.w[4 * p + 0] = v.x;
+    s.w[4 * p + 1] = v.y;
+    s.w[4 * p + 2] = v.z;
+    s.w[4 * p + 3] = v.w;
+  }
+  const uint2 sc = lds64(chunk + 3072 + lane * 8);
+  // biased byte b = sc + 128 -> fp16 1024 + b -> minus 1152 = sc (exact)
+  s.sc2[0][0] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4040u), kMinus1152);
+  s.sc2[0][1] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4141u), kMinus1152);
+  s.sc2[1][0] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4242u), kMinus1152);
+  s.sc2[1][1] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4343u), kMinus1152);
+  s.sc2[2][0] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4040u), kMinus1152);
+  s.sc2[2][1] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4141u), kMinus1152);
+  s.sc2[3][0] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4242u), kMinus1152);
+  s.sc2[3][1] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4343u), kMinus1152);
+  s.d = lds32(chunk + 3328 + (lane >> 2) * 4);
+}
+
+// decode group gam (mmas 2*gam, 2*gam+1)
+__device__ __forceinline__ void q6_group(const Q6Lane& s, int gam, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+  const uint32_t W0 = s.w[3 * gam], W1 = s.w[3 * gam + 1], W2 = s.w[3 * gam + 2];
+  const uint32_t sg = s.sc2[gam >> 1][0], sg8 = s.sc2[gam >> 1][1];
+  uint32_t p0 = (W0 & 0x003F003Fu) | kMagic;
+  uint32_t p1 = ((W0 >> 6) & 0x003F003Fu) | kMagic;
+  uint32_t p2 = (W1 & 0x003F003Fu) | kMagic;
+  uint32_t p3 = ((W1 >> 6) & 0x003F003Fu) | kMagic;
+  uint32_t p4 = (W2 & 0x003F003Fu) | kMagic;
+  uint32_t p5 = ((W2 >> 6) & 0x003F003Fu) | kMagic;
+  uint32_t p6 = ((W0 >> 12) & 0x000F000Fu) | ((W2 >> 8) & 0x00300030u) | kMagic;
+  uint32_t p7 = ((W1 >> 12) & 0x000F000Fu) | ((W2 >> 10) & 0x00300030u) | kMagic;
+  a0[0] = hmul2_u(hadd2_u(p0, kMinus1056), sg);
+  a0[1] = hmul2_u(hadd2_u(p1, kMinus1056), sg8);
+  a0[2] = hmul2_u(hadd2_u(p2, kMinus1056), sg);
+  a0[3] = hmul2_u(hadd2_u(p3, kMinus1056), sg8);
+  a1[0] = hmul2_u(hadd2_u(p4, kMinus1056), sg);
+  a1[1] = hmul2_u(hadd2_u(p5, kMinus1056), sg8);
+  a1[2] = hmul2_u(hadd2_u(p6, kMinus1056), sg);
+  a1[3] = hmul2_u(hadd2_u(p7, kMinus1056), sg8);
+}
+
+__device__ __forceinline__ float2 q6_block_scale(const Q6Lane& s) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&s.d);
+  return __half22float2(h);  // (row g, row g+8)
+}
+
+// IQ3_XXS: per-block lane state
+struct Iq3Lane {
+  uint4 qs0, qs1;      // grid indices: row g / row g+8, groups 2q (bytes 0..7) and 2q+1 (8..15)
+  uint32_t sw[2][2];   // scale/sign words [row][group]
+  uint32_t m2[2][2];   // fp16x2 (2s+1)
+  uint32_t c2[2][2];   // fp16x2 -1024*(2s+1)
+  uint32_t par[2][2];  // parity of sign field l at bit 7l
+  uint32_t d;
+};
+
+__device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane& s) {
+  s.qs0 = lds128(chunk + lane * 16);
+  s.qs1 = lds128(chunk + 512 + lane * 16);
+  const uint4 sw = lds128(chunk + 1024 + lane * 16);
+  s.sw[0][0] = sw.x;
+  s.sw[0][1] = sw.y;
+  s.sw[1][0] = sw.z;
+  s.sw[1][1] = sw.w;
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint32_t v = s.sw[r][c];
+      const uint32_t mm = ((v >> 28) << 1) | 1u;                    // 2s+1
+      const uint32_t m2 = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
+      s.m2[r][c] = m2;
+      s.c2[r][c] = hmul2_u(m2, kMinus1024);
+      uint32_t t = v ^ (v >> 1);
+      t ^= t >> 2;
+      t ^= t >> 4;                                                 // bit i = xor of bits i..i+7
+      s.par[r][c] = t ^ (v >> 7);                                  // bit 7l = parity of field l
+    }
+  s.d = lds32(chunk + 1536 + (lane >> 2) * 4);
+}
+
+// sign masks for sign pair i (s8 bits 2i, 2i+1) -> fp16x2 sign bits 15 / 31
+__device__ __forceinline__ uint32_t sign_mask(uint32_t s8, int i) {
+  const uint32_t mul = (1u << (15 - 2 * i)) + (1u << (30 - 2 * i));
+  return (s8 * mul) & 0x80008000u;
+}
+
+// decode mma m (0..15) for both rows
+__device__ __forceinline__ void iq3_mma(const Iq3Lane& s, const uint32_t* grid_rep, int lane, int m,
+                                        uint32_t (&a)[4]) {
+  const int c = m >> 3, l = (m >> 1) & 3, e = m & 1;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint4 qs = r == 0 ? s.qs0 : s.qs1;
+    const uint32_t word = (m >> 2) == 0 ? qs.x : (m >> 2) == 1 ? qs.y : (m >> 2) == 2 ? qs.z : qs.w;
+    const uint32_t idx = (word >> (8 * (m & 3))) & 0xFFu;
+    const uint32_t G = grid_rep[idx * 32 + lane];
+    const uint32_t v = s.sw[r][c];
+    const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | (((s.par[r][c] >> (7 * l)) & 1u) << 7);
+    const uint32_t lo = hfma2_u(prmt(G, 0x64646464u, 0x4140u), s.m2[r][c], s.c2[r][c]);
+    const uint32_t hi = hfma2_u(prmt(G, 0x64646464u, 0x4342u), s.m2[r][c], s.c2[r][c]);
+    a[r] = lo ^ sign_mask(s8, 2 * e);
+    a[r + 2] = hi ^ sign_mask(s8, 2 * e + 1);
+  }
+}
+
+__device__ __forceinline__ float2 iq3_block_scale(const Iq3Lane& s) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&s.d);
+  const float2 f = __half22float2(h);
+  return make_float2(f.x * 0.25f, f.y * 0.25f);   // d * (2s+1)/4 = (d/4) * (2s+1)
+}
+
+#endif  // __CUDACC__
+
+}  // namespace tlx

@@ -1,0 +1,705 @@
+// K-row dequantised GEMV over IQ3_XXS / Q6_K tiles on sm_100a.
+//
+// One persistent launch covers the whole matrix.  Work item = (k-segment s,
+// row tile t, block bb): 16 rows x 256 weights.  Items are dealt to warps as
+// contiguous ranges ("stream-K"), so every warp streams the same number of
+// weight bytes +-1 chunk regardless of how tiles divide into warps.  A tile
+// whose k range was split between warps (or k-segments) is finished by the last
+// piece to arrive: pieces write fragment-ordered fp32 partials to the
+// workspace, bump a per-tile counter, and the last arriver adds all pieces in
+// fixed k order (so results are bit-identical run to run) and runs the
+// epilogue.
+//
+// Per warp: a STAGES-deep ring of chunks in shared memory filled by
+// cp.async.bulk (lane 0 issues, completion on an mbarrier with tx count).
+// Per CTA: the activations of its k-segment staged once as fp16 in mma B
+// fragment order.  Inner loop: decode a chunk into exact-integer fp16 A
+// fragments (formats.cuh), mma.sync.m16n8k16 into fp32, scale by the block's
+// fp16 d after each 256-weight block.
+//
+// Epilogues: STORE  y[t][row] = acc (+ residual)       (down8nw32_11 / head8v11)
+//            GATEUP y[t][row] = silu(gate) * up         (ffn8v11)
+//            ARGMAX per-token (max, lowest index) over all rows, reduced across
+//                   CTAs by the last CTA, which can also run greedy accept
+//                   (h6kam + amred36 + acc36, fused)
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "formats.cuh"
+#include "tlx_internal.h"
+
+namespace tlx {
+
+enum Epi : int { EPI_STORE = 0, EPI_GATEUP = 1, EPI_ARGMAX = 2 };
+
+struct GemvParams {
+  const uint8_t* w0;
+  const uint8_t* w1;
+  const uint32_t* grid;
+  const void* x;
+  int x_dtype;
+  int M;
+  int MC;
+  int CG;  // columns per token (1, or 3 for fp32 activations split into fp16 parts)
+  int64_t ldx;
+  int64_t n_rows;
+  int T, NB, S, Bs, Cs, J;
+  void* y;
+  int y_f16;  // store y as fp16 instead of fp32
+  int64_t ldy;
+  const float* residual;
+  int64_t ldr;
+  float* out_max;
+  int32_t* out_idx;
+  uint64_t* out_keys;
+  int64_t row_offset;
+  const int32_t* drafts;
+  int n_drafts;
+  int32_t* accept_out;
+  float* partials;
+  uint32_t* tile_cnt;
+  uint64_t* cta_best;
+  uint32_t* done_cnt;
+  uint32_t* err;
+};
+
+// ---- shared-memory layout (same arithmetic on host and device) ----
+struct SmemLayout {
+  uint32_t xs, grid, ring, bars, epi, best, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int stages, int Bs, int MC) {
+  SmemLayout L;
+  uint32_t off = 0;
+  L.xs = off;
+  off += static_cast<uint32_t>(Bs) * 16u * static_cast<uint32_t>(MC) * 32u;
+  off = (off + 127u) & ~127u;
+  L.grid = off;
+  if (qt == QT_IQ3_XXS) off += 256u * 32u * 4u;
+  L.ring = off;
+  off += static_cast<uint32_t>(wpc) * stages * chunk_bytes(qt) * nmat;
+  off = (off + 15u) & ~15u;
+  L.bars = off;
+  off += static_cast<uint32_t>(wpc) * stages * 8u;
+  L.epi = off;
+  off += static_cast<uint32_t>(wpc) * nmat * 16u * 16u * 4u;
+  L.best = off;
+  off += static_cast<uint32_t>(wpc) * 16u * 8u + 128u;  // + done flag and 16 final ids
+  L.total = off;
+  return L;
+}
+
+// warp (segment-local) whose item range contains segment-local item f
+__device__ __forceinline__ int warp_of(int64_t f, int64_t Fs, int Ws) {
+  return static_cast<int>(((f + 1) * Ws - 1) / Fs);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+// ---- activation staging: x[M][K] (f32 / f16 / bf16) -> fp16 B fragments ----
+__device__ void stage_x(const GemvParams& p, int seg, uint2* xs) {
+  const int groups_per_tok = p.Bs * 64;  // 4-element groups
+  const int total = p.M * groups_per_tok;
+  const int64_t k_base = static_cast<int64_t>(seg) * p.Bs * kQK;
+  for (int gi = threadIdx.x; gi < total; gi += blockDim.x) {
+    const int t = gi / groups_per_tok;
+    const int kk = (gi - t * groups_per_tok) * 4;
+    const int bb = kk >> 8, kin = kk & 255, q = kin >> 6, m = (kin & 63) >> 2;
+    const int64_t src = t * p.ldx + k_base + kk;
+    float v[4];
+    if (p.x_dtype == DT_F32) {
+      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + src);
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+      const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + src);
+      const uint32_t h[2] = {raw.x, raw.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t bits = (h[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        v[e] = p.x_dtype == DT_BF16 ? __uint_as_float(bits << 16)
+                                    : __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+      }
+    }
+    const int base = (bb * 16 + m) * p.MC;
+    if (p.CG == 1) {
+      const __half2 h01 = __floats2half2_rn(v[0], v[1]);
+      const __half2 h23 = __floats2half2_rn(v[2], v[3]);
+      xs[(base + t) * 4 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                                          *reinterpret_cast<const uint32_t*>(&h23));
+    } else {
+      // fp32 -> hi + mid + lo fp16 parts (33 significand bits >= 24)
+#pragma unroll
+      for (int part = 0; part < 3; ++part) {
+        float hpart[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hpart[e] = __half2float(__float2half_rn(v[e]));
+          v[e] -= hpart[e];
+        }
+        const __half2 h01 = __floats2half2_rn(hpart[0], hpart[1]);
+        const __half2 h23 = __floats2half2_rn(hpart[2], hpart[3]);
+        xs[(base + 3 * t + part) * 4 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                                                       *reinterpret_cast<const uint32_t*>(&h23));
+      }
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void load_b(const uint2* xs, int bb, int m, int MC, int lane, uint32_t (&b)[NT][2]) {
+  const int g = lane >> 2, q = lane & 3;
+  const uint2* base = xs + (bb * 16 + m) * MC * 4;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int col = nt * 8 + g;
+    if (col < MC) {
+      const uint2 v = lds64(base + col * 4 + q);
+      b[nt][0] = v.x;
+      b[nt][1] = v.y;
+    } else {
+      b[nt][0] = 0u;
+      b[nt][1] = 0u;
+    }
+  }
+}
+
+// one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B)
+template <int QT, int NT, int NMAT>
+__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xs,
+                                              const uint32_t* grid_rep, int bb, int MC, int lane,
+                                              float (&acc)[NMAT][NT][4]) {
+  float tmp[NMAT][NT][4];
+#pragma unroll
+  for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmp[a][nt][i] = 0.f;
+  float2 scale[NMAT];
+  if constexpr (QT == QT_Q6_K) {
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) {
+      Q6Lane s;
+      q6_load(chunk[a], lane, s);
+#pragma unroll
+      for (int gam = 0; gam < 8; ++gam) {
+        uint32_t a0[4], a1[4];
+        q6_group(s, gam, a0, a1);
+        uint32_t b[NT][2];
+        load_b<NT>(xs, bb, 2 * gam, MC, lane, b);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a0, b[nt][0], b[nt][1]);
+        load_b<NT>(xs, bb, 2 * gam + 1, MC, lane, b);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a1, b[nt][0], b[nt][1]);
+      }
+      scale[a] = q6_block_scale(s);
+    }
+  } else {
+    Iq3Lane s[NMAT];
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) {
+      iq3_load(chunk[a], lane, s[a]);
+      scale[a] = iq3_block_scale(s[a]);
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      uint32_t b[NT][2];
+      load_b<NT>(xs, bb, m, MC, lane, b);
+#pragma unroll
+      for (int a = 0; a < NMAT; ++a) {
+        uint32_t af[4];
+        iq3_mma(s[a], grid_rep, lane, m, af);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], af, b[nt][0], b[nt][1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[a][nt][0] = fmaf(scale[a].x, tmp[a][nt][0], acc[a][nt][0]);
+      acc[a][nt][1] = fmaf(scale[a].x, tmp[a][nt][1], acc[a][nt][1]);
+      acc[a][nt][2] = fmaf(scale[a].y, tmp[a][nt][2], acc[a][nt][2]);
+      acc[a][nt][3] = fmaf(scale[a].y, tmp[a][nt][3], acc[a][nt][3]);
+    }
+}
+
+// tile epilogue on complete sums (fragment order in registers)
+template <int NT, int NMAT, int EPI>
+__device__ __forceinline__ void tile_epilogue(const GemvParams& p, int t, const float (&v)[NMAT][NT][4],
+                                              float* epi, int lane, uint64_t& best) {
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + 2 * q;
+      *reinterpret_cast<float2*>(epi + a * 256 + g * 16 + col) = make_float2(v[a][nt][0], v[a][nt][1]);
+      *reinterpret_cast<float2*>(epi + a * 256 + (g + 8) * 16 + col) = make_float2(v[a][nt][2], v[a][nt][3]);
+    }
+  __syncwarp();
+  const int64_t row0 = static_cast<int64_t>(t) * kTileRows;
+  if constexpr (EPI == EPI_ARGMAX) {
+    const int tk = lane & 15, rh = lane >> 4;
+    if (tk < p.M) {
+#pragma unroll
+      for (int r8 = 0; r8 < 8; ++r8) {
+        const int r = rh * 8 + r8;
+        if (row0 + r < p.n_rows) {
+          float val = 0.f;
+          for (int c = 0; c < p.CG; ++c) val += epi[r * 16 + tk * p.CG + c];
+          const uint64_t key = argmax_key(val, static_cast<uint32_t>(p.row_offset + row0 + r));
+          best = key > best ? key : best;
+        }
+      }
+    }
+  } else {
+    for (int idx = lane; idx < 16 * p.M; idx += 32) {
+      const int r = idx & 15, tk = idx >> 4;
+      const int64_t row = row0 + r;
+      if (row < p.n_rows) {
+        float val = 0.f;
+        for (int c = 0; c < p.CG; ++c) val += epi[r * 16 + tk * p.CG + c];
+        if constexpr (EPI == EPI_GATEUP) {
+          float u = 0.f;
+          for (int c = 0; c < p.CG; ++c) u += epi[256 + r * 16 + tk * p.CG + c];
+          val = silu_f(val) * u;
+        } else {
+          if (p.residual) val += p.residual[tk * p.ldr + row];
+        }
+        if (p.y_f16)
+          static_cast<__half*>(p.y)[tk * p.ldy + row] = __float2half_rn(val);
+        else
+          static_cast<float*>(p.y)[tk * p.ldy + row] = val;
+      }
+    }
+  }
+  __syncwarp();
+}
+
+template <int QT, int NT, int EPI, int WPC, int STAGES>
+__global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams p) {
+  constexpr int NMAT = EPI == EPI_GATEUP ? 2 : 1;
+  constexpr uint32_t CH = chunk_bytes(QT);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout L = smem_layout(QT, NMAT, WPC, STAGES, p.Bs, p.MC);
+  uint2* xs = reinterpret_cast<uint2*>(smem + L.xs);
+  uint32_t* grid_rep = reinterpret_cast<uint32_t*>(smem + L.grid);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem + L.ring + static_cast<uint32_t>(warp) * STAGES * CH * NMAT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * STAGES;
+  float* epi = reinterpret_cast<float*>(smem + L.epi) + warp * NMAT * 256;
+  uint64_t* wbest = reinterpret_cast<uint64_t*>(smem + L.best);
+
+  const int seg = blockIdx.x / p.Cs;
+  const int cta_in_seg = blockIdx.x - seg * p.Cs;
+  const int64_t Fs = static_cast<int64_t>(p.T) * p.Bs;
+  // warps beyond the item count idle, so every partition warp owns >= 1 item
+  const int Ws = static_cast<int>(Fs < static_cast<int64_t>(p.Cs) * WPC ? Fs : static_cast<int64_t>(p.Cs) * WPC);
+  const int wseg = cta_in_seg * WPC + warp;
+  const bool active = wseg < Ws;
+  const int64_t f0 = active ? static_cast<int64_t>(wseg) * Fs / Ws : 0;
+  const int64_t f1 = active ? static_cast<int64_t>(wseg + 1) * Fs / Ws : 0;
+  const int64_t n_items = f1 - f0;
+
+  auto issue = [&](int64_t f, int st) {
+    const int64_t t = f / p.Bs;
+    const int b = seg * p.Bs + static_cast<int>(f - t * p.Bs);
+    const int64_t off = (t * p.NB + b) * static_cast<int64_t>(CH);
+    mbar_arrive_expect_tx(&bars[st], CH * NMAT);
+    bulk_g2s(ring + st * CH * NMAT, p.w0 + off, CH, &bars[st]);
+    if constexpr (NMAT == 2) bulk_g2s(ring + st * CH * NMAT + CH, p.w1 + off, CH, &bars[st]);
+  };
+
+  if (lane == 0) {
+#pragma unroll
+    for (int st = 0; st < STAGES; ++st) mbar_init(&bars[st], 1);
+    mbar_fence_init();
+    for (int st = 0; st < STAGES && st < n_items; ++st) issue(f0 + st, st);
+  }
+  __syncwarp();
+
+  if constexpr (QT == QT_IQ3_XXS) {
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) grid_rep[i] = __ldg(p.grid + (i >> 5));
+  }
+  stage_x(p, seg, xs);
+  __syncthreads();
+
+  float acc[NMAT][NT][4];
+#pragma unroll
+  for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[a][nt][i] = 0.f;
+  uint64_t best = 0ull;
+  bool failed = false;
+  int64_t piece_start = f0;
+  int64_t i_fail = n_items;
+
+  for (int64_t i = 0; i < n_items; ++i) {
+    const int64_t f = f0 + i;
+    const int st = static_cast<int>(i % STAGES);
+    const uint32_t ph = static_cast<uint32_t>((i / STAGES) & 1);
+    if (!mbar_wait_bounded(&bars[st], ph, lane == 0 ? p.err : nullptr)) {
+      failed = true;
+      i_fail = i;
+      break;
+    }
+    const int64_t t = f / p.Bs;
+    const int bb = static_cast<int>(f - t * p.Bs);
+    const uint8_t* chunk[NMAT];
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) chunk[a] = ring + st * CH * NMAT + a * CH;
+    compute_block<QT, NT, NMAT>(chunk, xs, grid_rep, bb, p.MC, lane, acc);
+    __syncwarp();
+    if (lane == 0 && i + STAGES < n_items) {
+      fence_proxy_async_smem();
+      issue(f + STAGES, st);
+    }
+    const bool run_end = (bb == p.Bs - 1) || (i == n_items - 1);
+    if (!run_end) continue;
+
+    // ---- a piece of tile t ends here ----
+    const int64_t run0 = t * p.Bs;
+    const bool whole = (p.S == 1) && (piece_start == run0) && (bb == p.Bs - 1);
+    if (whole) {
+      tile_epilogue<NT, NMAT, EPI>(p, static_cast<int>(t), acc, epi, lane, best);
+    } else {
+      const int w_first = warp_of(run0, Fs, Ws);
+      const int w_last = warp_of(run0 + p.Bs - 1, Fs, Ws);
+      const int pieces = w_last - w_first + 1;
+      const int my_j = wseg - w_first;
+      const int total = pieces * p.S;
+      const int64_t slot_stride = static_cast<int64_t>(NMAT) * NT * 4 * 32;
+      float* my_slot = p.partials + ((t * p.S + seg) * p.J + my_j) * slot_stride;
+#pragma unroll
+      for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) my_slot[((a * NT + nt) * 4 + e) * 32 + lane] = acc[a][nt][e];
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(p.tile_cnt + t, 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == static_cast<uint32_t>(total - 1)) {
+        __threadfence();
+        float v[NMAT][NT][4];
+#pragma unroll
+        for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
+        for (int s = 0; s < p.S; ++s)
+          for (int j = 0; j < pieces; ++j) {
+            if (s == seg && j == my_j) {
+#pragma unroll
+              for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) v[a][nt][e] += acc[a][nt][e];
+            } else {
+              const float* sl = p.partials + ((t * p.S + s) * p.J + j) * slot_stride;
+#pragma unroll
+              for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) v[a][nt][e] += __ldcg(sl + ((a * NT + nt) * 4 + e) * 32 + lane);
+            }
+          }
+        tile_epilogue<NT, NMAT, EPI>(p, static_cast<int>(t), v, epi, lane, best);
+        if (lane == 0) p.tile_cnt[t] = 0u;
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[a][nt][e] = 0.f;
+    piece_start = f + 1;
+  }
+
+  if (failed) {
+    // let every copy this warp issued land before the CTA can exit
+    for (int64_t i = i_fail; i < n_items && i < i_fail + STAGES; ++i)
+      mbar_wait_bounded(&bars[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr);
+  }
+
+  if constexpr (EPI == EPI_ARGMAX) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, 16);
+    best = other > best ? other : best;
+    if (lane < 16) wbest[warp * 16 + lane] = best;
+    __syncthreads();
+    uint32_t* flag = reinterpret_cast<uint32_t*>(wbest + WPC * 16);
+    if (threadIdx.x < 16) {
+      uint64_t b = 0ull;
+      for (int w = 0; w < WPC; ++w) {
+        const uint64_t c = wbest[w * 16 + threadIdx.x];
+        b = c > b ? c : b;
+      }
+      p.cta_best[blockIdx.x * 16 + threadIdx.x] = b;
+      __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t old = atomicAdd(p.done_cnt, 1u);
+      flag[0] = old == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (flag[0]) {
+      __threadfence();
+      int32_t* idx_s = reinterpret_cast<int32_t*>(flag + 2);
+      if (threadIdx.x < p.M) {
+        uint64_t b = 0ull;
+        for (int c = 0; c < gridDim.x; ++c) {
+          const uint64_t k = __ldcg(p.cta_best + c * 16 + threadIdx.x);
+          b = k > b ? k : b;
+        }
+        if (p.out_max) p.out_max[threadIdx.x] = key_value(b);
+        if (p.out_idx) p.out_idx[threadIdx.x] = key_index(b);
+        if (p.out_keys) p.out_keys[threadIdx.x] = b;
+        idx_s[threadIdx.x] = key_index(b);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (p.accept_out) {
+          int m = 0;
+          while (m < p.n_drafts && idx_s[m] == p.drafts[m]) ++m;
+          p.accept_out[0] = m;
+          p.accept_out[1] = idx_s[m];
+        }
+        *p.done_cnt = 0u;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Host side: planning, workspace layout, dispatch
+// ------------------------------------------------------------------------------------
+struct Plan {
+  int T, NB, S, Bs, C, Cs, J, MC, CG, NT, nmat, wpc, stages;
+  size_t smem;
+  size_t off_cnt, off_best, off_part, ws_bytes;
+};
+
+static int sm_count() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  });
+  return n;
+}
+
+static int smem_optin() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || n <= 0)
+      n = 232448;  // sm_100: 227 KB
+  });
+  return n;
+}
+
+static constexpr uint32_t kXsBudget = 120u * 1024u;
+
+template <int QT, int EPI>
+struct Cfg;
+// warps per CTA and ring depth per (format, epilogue); sized so that the
+// verify-step shapes (k = 5120 with 11 rows; k = 17408 in 4 segments) fit the
+// 227 KB shared-memory opt-in without splitting k further
+template <> struct Cfg<QT_Q6_K, EPI_STORE> { static constexpr int WPC = 16, STAGES = 2; };
+template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 2; };
+template <> struct Cfg<QT_Q6_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 8, STAGES = 4; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_ARGMAX> { static constexpr int WPC = 8, STAGES = 4; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
+
+static void cfg_for(int qt, int epi, int& wpc, int& stages) {
+#define TLX_CFG(Q, E)            \
+  if (qt == Q && epi == E) {     \
+    wpc = Cfg<Q, E>::WPC;        \
+    stages = Cfg<Q, E>::STAGES;  \
+    return;                      \
+  }
+  TLX_CFG(QT_Q6_K, EPI_STORE)
+  TLX_CFG(QT_Q6_K, EPI_ARGMAX)
+  TLX_CFG(QT_Q6_K, EPI_GATEUP)
+  TLX_CFG(QT_IQ3_XXS, EPI_STORE)
+  TLX_CFG(QT_IQ3_XXS, EPI_ARGMAX)
+  TLX_CFG(QT_IQ3_XXS, EPI_GATEUP)
+#undef TLX_CFG
+  wpc = 8;
+  stages = 2;
+}
+
+static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, Plan& P) {
+  if (qt != QT_Q6_K && qt != QT_IQ3_XXS) return TLX_ERR_QTYPE;
+  if (n_rows <= 0 || k <= 0 || (k % kQK) != 0) return TLX_ERR_SHAPE;
+  if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
+  P.CG = x_dtype == DT_F32 ? 3 : 1;
+  if (m < 1 || m * P.CG > 16) return TLX_ERR_SHAPE;
+  if (n_rows > (int64_t(1) << 31) - 16 || k / kQK > (1 << 20)) return TLX_ERR_SHAPE;
+  P.MC = m * P.CG;
+  P.NT = P.MC <= 8 ? 1 : 2;
+  P.nmat = epi == EPI_GATEUP ? 2 : 1;
+  cfg_for(qt, epi, P.wpc, P.stages);
+  P.T = static_cast<int>((n_rows + kTileRows - 1) / kTileRows);
+  P.NB = static_cast<int>(k / kQK);
+  // smallest k split whose activations fit the staging budget and whose whole
+  // shared-memory layout fits the device's opt-in limit
+  P.S = 0;
+  const uint32_t smem_limit = static_cast<uint32_t>(smem_optin());
+  for (int s = 1; s <= P.NB; ++s) {
+    if (P.NB % s) continue;
+    const uint32_t xs = static_cast<uint32_t>(P.NB / s) * 16u * P.MC * 32u;
+    const SmemLayout Ls = smem_layout(qt, P.nmat, P.wpc, P.stages, P.NB / s, P.MC);
+    if (xs <= kXsBudget && Ls.total <= smem_limit) {
+      P.S = s;
+      break;
+    }
+  }
+  if (P.S == 0) return TLX_ERR_SHAPE;
+  P.Bs = P.NB / P.S;
+  int ctas = max_ctas > 0 ? max_ctas : sm_count();
+  P.Cs = std::max(1, ctas / P.S);
+  const int64_t Fs = static_cast<int64_t>(P.T) * P.Bs;
+  // no more CTAs than needed to give every warp an item (the last CTA may idle warps)
+  while (P.Cs > 1 && static_cast<int64_t>(P.Cs - 1) * P.wpc >= Fs) --P.Cs;
+  P.C = P.Cs * P.S;
+  const int64_t weff = std::min<int64_t>(Fs, static_cast<int64_t>(P.Cs) * P.wpc);
+  const int64_t per_warp = Fs / weff;
+  P.J = static_cast<int>(std::min<int64_t>(P.Bs, P.Bs / std::max<int64_t>(1, per_warp) + 2));
+  const SmemLayout L = smem_layout(qt, P.nmat, P.wpc, P.stages, P.Bs, P.MC);
+  P.smem = L.total;
+  size_t off = 256;
+  P.off_cnt = off;
+  off += (static_cast<size_t>(P.T) * 4 + 255) & ~size_t(255);
+  P.off_best = off;
+  off += (static_cast<size_t>(P.C) * 16 * 8 + 255) & ~size_t(255);
+  P.off_part = off;
+  off += static_cast<size_t>(P.T) * P.S * P.J * P.nmat * P.NT * 4 * 32 * sizeof(float);
+  P.ws_bytes = off;
+  return TLX_OK;
+}
+
+template <int QT, int NT, int EPI>
+static int launch_t(const Plan& P, const GemvParams& gp, cudaStream_t stream) {
+  constexpr int WPC = Cfg<QT, EPI>::WPC, STAGES = Cfg<QT, EPI>::STAGES;
+  auto kern = tile_gemv_kernel<QT, NT, EPI, WPC, STAGES>;
+  static size_t configured = 0;
+  if (P.smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
+    if (e != cudaSuccess) return TLX_ERR_LAUNCH;
+    configured = P.smem;
+  }
+  kern<<<P.C, WPC * 32, P.smem, stream>>>(gp);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+template <int EPI>
+static int dispatch(int qt, const Plan& P, const GemvParams& gp, cudaStream_t s) {
+  if (qt == QT_Q6_K) return P.NT == 1 ? launch_t<QT_Q6_K, 1, EPI>(P, gp, s) : launch_t<QT_Q6_K, 2, EPI>(P, gp, s);
+  return P.NT == 1 ? launch_t<QT_IQ3_XXS, 1, EPI>(P, gp, s) : launch_t<QT_IQ3_XXS, 2, EPI>(P, gp, s);
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
+             int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,
+             int y_dtype, int64_t ldy, int64_t row_offset, float* out_max, int32_t* out_idx, uint64_t* out_keys,
+             const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
+             cudaStream_t stream) {
+  Plan P;
+  int rc = make_plan(qt, epi, n_rows, k, m, x_dtype, max_ctas, P);
+  if (rc) return rc;
+  if (!w0 || !x || !ws) return TLX_ERR_NULL;
+  if (epi == EPI_GATEUP && !w1) return TLX_ERR_NULL;
+  if (qt == QT_IQ3_XXS && !grid) return TLX_ERR_NULL;
+  if (epi != EPI_ARGMAX && !y) return TLX_ERR_NULL;
+  if (epi != EPI_ARGMAX && y_dtype != DT_F32 && y_dtype != DT_F16) return TLX_ERR_DTYPE;
+  if (ws_bytes < P.ws_bytes) return TLX_ERR_WORKSPACE;
+  if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(ws, 256)) return TLX_ERR_ALIGN;
+  const size_t xe = x_dtype == DT_F32 ? 4 : 2;
+  if (!aligned(x, xe * 4) || ldx < k || (ldx % 4) != 0) return TLX_ERR_ALIGN;
+  if (epi != EPI_ARGMAX && ldy < n_rows) return TLX_ERR_SHAPE;
+  if (residual && ldr < n_rows) return TLX_ERR_SHAPE;
+  if (epi == EPI_ARGMAX && accept_out && (!drafts || n_drafts < 0 || n_drafts + 1 > m)) return TLX_ERR_SHAPE;
+  if (epi == EPI_ARGMAX && (row_offset < 0 || row_offset + n_rows > (int64_t(1) << 32) - 1)) return TLX_ERR_SHAPE;
+
+  GemvParams gp{};
+  gp.w0 = static_cast<const uint8_t*>(w0);
+  gp.w1 = static_cast<const uint8_t*>(w1);
+  gp.grid = grid;
+  gp.x = x;
+  gp.x_dtype = x_dtype;
+  gp.M = m;
+  gp.MC = P.MC;
+  gp.CG = P.CG;
+  gp.ldx = ldx;
+  gp.n_rows = n_rows;
+  gp.T = P.T;
+  gp.NB = P.NB;
+  gp.S = P.S;
+  gp.Bs = P.Bs;
+  gp.Cs = P.Cs;
+  gp.J = P.J;
+  gp.y = y;
+  gp.y_f16 = y_dtype == DT_F16 ? 1 : 0;
+  gp.ldy = ldy;
+  gp.residual = residual;
+  gp.ldr = ldr;
+  gp.out_max = out_max;
+  gp.out_idx = out_idx;
+  gp.out_keys = out_keys;
+  gp.row_offset = row_offset;
+  gp.drafts = drafts;
+  gp.n_drafts = n_drafts;
+  gp.accept_out = accept_out;
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  gp.err = reinterpret_cast<uint32_t*>(wsb);
+  gp.done_cnt = reinterpret_cast<uint32_t*>(wsb + 4);
+  gp.tile_cnt = reinterpret_cast<uint32_t*>(wsb + P.off_cnt);
+  gp.cta_best = reinterpret_cast<uint64_t*>(wsb + P.off_best);
+  gp.partials = reinterpret_cast<float*>(wsb + P.off_part);
+  if (epi == EPI_STORE) return dispatch<EPI_STORE>(qt, P, gp, stream);
+  if (epi == EPI_GATEUP) return dispatch<EPI_GATEUP>(qt, P, gp, stream);
+  return dispatch<EPI_ARGMAX>(qt, P, gp, stream);
+}
+
+size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas) {
+  Plan P;
+  if (make_plan(qt, epi, n_rows, k, m, x_dtype, max_ctas, P)) return 0;
+  return P.ws_bytes;
+}
+
+int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
+                   int n_info) {
+  Plan P;
+  int rc = make_plan(qt, epi, n_rows, k, m, x_dtype, max_ctas, P);
+  if (rc) return rc;
+  const int32_t v[] = {P.T, P.NB, P.S, P.Bs, P.C, P.Cs, P.J, P.MC, P.NT, P.wpc, P.stages, static_cast<int32_t>(P.smem)};
+  for (int i = 0; i < n_info && i < static_cast<int>(sizeof(v) / sizeof(v[0])); ++i) info[i] = v[i];
+  return TLX_OK;
+}
+
+}  // namespace tlx

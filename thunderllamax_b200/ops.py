@@ -1,0 +1,228 @@
+"""Torch-buffer front end of the CUDA library.
+
+Torch tensors are used only as device buffers: every call passes raw pointers
+to the C ABI (``_lib``) on the tensor's current stream.  Nothing here computes
+on the CPU or falls back to torch kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import functools
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (MODE_ARGMAX, MODE_GATE_UP, MODE_STORE, QTYPES, TLX_DT_BF16, TLX_DT_F16, TLX_DT_F32,
+                   TLXError, check)
+
+_DT = {torch.float32: TLX_DT_F32, torch.float16: TLX_DT_F16, torch.bfloat16: TLX_DT_BF16}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t=None):
+    dev = t.device if t is not None else torch.device("cuda")
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def require_device():
+    if not torch.cuda.is_available():
+        raise TLXError("no CUDA device: the verify path has no CPU implementation")
+    check(_lib.lib().tlx_device_check(), "device check (needs an sm_100 B200)")
+
+
+def qtype_id(q) -> int:
+    return QTYPES[q] if isinstance(q, str) else int(q)
+
+
+@functools.lru_cache(maxsize=None)
+def _grid_numpy():
+    from .tables import iq3xxs_grid_u32
+
+    return iq3xxs_grid_u32()
+
+
+@functools.lru_cache(maxsize=None)
+def grid(device: str = "cuda") -> torch.Tensor:
+    """The IQ3_XXS grid (256 u32, from gguf-py) resident on the device
+    (the reference's ``gridf`` buffer, engine/engine0.py:108-112)."""
+    return torch.from_numpy(_grid_numpy().view(np.int32).copy()).to(device)
+
+
+def tiled_bytes(qtype, n_rows: int, k: int) -> int:
+    return int(_lib.lib().tlx_tiled_bytes(qtype_id(qtype), n_rows, k))
+
+
+def pack_tiles_host(qtype, rows: np.ndarray, k: int) -> np.ndarray:
+    """GGUF rows (uint8 [n, row_bytes]) -> tile layout (uint8, host)."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    n = rows.shape[0]
+    out = np.empty(tiled_bytes(qtype, n, k), dtype=np.uint8)
+    check(_lib.lib().tlx_pack_tiles(qtype_id(qtype), rows.ctypes.data, n, k, rows.shape[1], out.ctypes.data),
+          "pack_tiles")
+    return out
+
+
+def unpack_tiles_host(qtype, tiled: np.ndarray, n_rows: int, k: int, row_bytes: int) -> np.ndarray:
+    out = np.zeros((n_rows, row_bytes), dtype=np.uint8)
+    tiled = np.ascontiguousarray(tiled, dtype=np.uint8)
+    check(_lib.lib().tlx_unpack_tiles(qtype_id(qtype), tiled.ctypes.data, n_rows, k, out.ctypes.data), "unpack")
+    return out
+
+
+def pack_tiles(qtype, rows, k: int) -> torch.Tensor:
+    """GGUF rows (numpy or CUDA uint8 [n, row_bytes]) -> tiled device buffer."""
+    require_device()
+    if isinstance(rows, np.ndarray):
+        rows = torch.from_numpy(np.ascontiguousarray(rows, dtype=np.uint8)).cuda()
+    rows = rows.contiguous()
+    n = rows.shape[0]
+    out = torch.empty(tiled_bytes(qtype, n, k), dtype=torch.uint8, device=rows.device)
+    check(_lib.lib().tlx_pack_tiles_device(qtype_id(qtype), _ptr(rows), n, k, rows.stride(0), _ptr(out),
+                                           _stream(rows)), "pack_tiles_device")
+    return out
+
+
+class Workspace:
+    """Caller-owned scratch (split-tile partials, counters, argmax partials).
+    Zeroed once; kernels leave it zeroed after each launch."""
+
+    def __init__(self, nbytes: int, device="cuda"):
+        self.nbytes = max(int(nbytes), 256)
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        check(_lib.lib().tlx_workspace_init(_ptr(self.buf), self.nbytes, _stream(self.buf)), "workspace_init")
+
+    @classmethod
+    def for_shape(cls, mode: int, qtype, n_rows: int, k: int, m: int, x_dtype=torch.bfloat16, device="cuda"):
+        nb = _lib.lib().tlx_gemv_workspace_bytes(mode, qtype_id(qtype), n_rows, k, m, _DT[x_dtype])
+        if nb == 0:
+            raise TLXError(f"unsupported shape for workspace: mode={mode} {qtype} n={n_rows} k={k} m={m}")
+        return cls(nb, device)
+
+    def error(self) -> int:
+        v = ctypes.c_uint32(0)
+        check(_lib.lib().tlx_workspace_error(_ptr(self.buf), ctypes.byref(v)), "workspace_error")
+        return int(v.value)
+
+    def reset(self):
+        check(_lib.lib().tlx_workspace_init(_ptr(self.buf), self.nbytes, _stream(self.buf)), "workspace_init")
+
+
+def plan(mode: int, qtype, n_rows: int, k: int, m: int, x_dtype=torch.bfloat16) -> dict:
+    info = (ctypes.c_int32 * 12)()
+    check(_lib.lib().tlx_gemv_plan(mode, qtype_id(qtype), n_rows, k, m, _DT[x_dtype], info, 12), "plan")
+    keys = ["tiles", "blocks", "segments", "blocks_per_segment", "ctas", "ctas_per_segment", "max_pieces",
+            "columns", "ntiles", "warps_per_cta", "stages", "smem"]
+    return dict(zip(keys, list(info)))
+
+
+def set_max_ctas(n: int) -> None:
+    _lib.lib().tlx_set_max_ctas(int(n))
+
+
+def _x_args(x: torch.Tensor):
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise TLXError("x must be a row-major [m, k] tensor")
+    if x.dtype not in _DT:
+        raise TLXError(f"unsupported activation dtype {x.dtype}")
+    return _DT[x.dtype], x.stride(0)
+
+
+def _y_dtype(y):
+    if y.dtype not in (torch.float32, torch.float16):
+        raise TLXError("outputs are fp32 or fp16")
+    return _DT[y.dtype]
+
+
+def gemv(qtype, w: torch.Tensor, x: torch.Tensor, n_rows: int, ws: Workspace, y: torch.Tensor = None,
+         residual: torch.Tensor = None, out_dtype=torch.float32) -> torch.Tensor:
+    """y[t][r] = (W x_t)[r] (+ residual[t][r]); W tiled."""
+    q = qtype_id(qtype)
+    dt, ldx = _x_args(x)
+    m, k = x.shape
+    if y is None:
+        y = torch.empty((m, n_rows), dtype=out_dtype, device=x.device)
+    g = grid(str(x.device)) if q == _lib.TLX_IQ3_XXS else None
+    rc = _lib.lib().tlx_gemv(q, _ptr(w), _ptr(g), _ptr(x), dt, ldx, m, n_rows, k, _ptr(residual),
+                             residual.stride(0) if residual is not None else 0, _ptr(y), _y_dtype(y), y.stride(0),
+                             _ptr(ws.buf), ws.nbytes, _stream(x))
+    check(rc, "gemv")
+    return y
+
+
+def ffn_gate_up(qtype, w_gate: torch.Tensor, w_up: torch.Tensor, x: torch.Tensor, n_rows: int, ws: Workspace,
+                gact: torch.Tensor = None, out_dtype=torch.float32) -> torch.Tensor:
+    q = qtype_id(qtype)
+    dt, ldx = _x_args(x)
+    m, k = x.shape
+    if gact is None:
+        gact = torch.empty((m, n_rows), dtype=out_dtype, device=x.device)
+    g = grid(str(x.device)) if q == _lib.TLX_IQ3_XXS else None
+    rc = _lib.lib().tlx_ffn_gate_up(q, _ptr(w_gate), _ptr(w_up), _ptr(g), _ptr(x), dt, ldx, m, n_rows, k,
+                                    _ptr(gact), _y_dtype(gact), gact.stride(0), _ptr(ws.buf), ws.nbytes,
+                                    _stream(x))
+    check(rc, "ffn_gate_up")
+    return gact
+
+
+def head_argmax(qtype, w: torch.Tensor, x: torch.Tensor, n_rows: int, ws: Workspace, row_offset: int = 0,
+                out_max=None, out_idx=None, out_keys=None, drafts=None, accept_out=None):
+    q = qtype_id(qtype)
+    dt, ldx = _x_args(x)
+    m, k = x.shape
+    dev = x.device
+    if out_max is None:
+        out_max = torch.empty(m, dtype=torch.float32, device=dev)
+    if out_idx is None:
+        out_idx = torch.empty(m, dtype=torch.int32, device=dev)
+    g = grid(str(dev)) if q == _lib.TLX_IQ3_XXS else None
+    nd = 0 if drafts is None else int(drafts.numel())
+    rc = _lib.lib().tlx_head_argmax(q, _ptr(w), _ptr(g), _ptr(x), dt, ldx, m, n_rows, k, row_offset,
+                                    _ptr(out_max), _ptr(out_idx), _ptr(out_keys), _ptr(drafts), nd,
+                                    _ptr(accept_out), _ptr(ws.buf), ws.nbytes, _stream(x))
+    check(rc, "head_argmax")
+    return out_max, out_idx
+
+
+def argmax_rows(logits: torch.Tensor, amds: torch.Tensor = None) -> torch.Tensor:
+    m, n = logits.shape
+    if amds is None:
+        amds = torch.empty(m, dtype=torch.int32, device=logits.device)
+    dt = {torch.float32: TLX_DT_F32, torch.float16: TLX_DT_F16}.get(logits.dtype)
+    if dt is None:
+        raise TLXError("logits must be fp32 or fp16")
+    check(_lib.lib().tlx_argmax_rows(_ptr(logits), dt, m, n, logits.stride(0), _ptr(amds), _stream(logits)),
+          "argmax_rows")
+    return amds
+
+
+def argmax_merge(keys: torch.Tensor, out_max=None, out_idx=None, drafts=None, accept_out=None):
+    n_shards, m = keys.shape
+    dev = keys.device
+    if out_max is None:
+        out_max = torch.empty(m, dtype=torch.float32, device=dev)
+    if out_idx is None:
+        out_idx = torch.empty(m, dtype=torch.int32, device=dev)
+    nd = 0 if drafts is None else int(drafts.numel())
+    check(_lib.lib().tlx_argmax_merge(_ptr(keys), n_shards, m, _ptr(out_max), _ptr(out_idx), _ptr(drafts), nd,
+                                      _ptr(accept_out), _stream(keys)), "argmax_merge")
+    return out_max, out_idx
+
+
+def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=None):
+    dev = amds.device
+    k = int(drafts.numel()) if k is None else int(k)
+    if mb is None:
+        mb = torch.empty(1, dtype=torch.int32, device=dev)
+    if eb is None:
+        eb = torch.empty(2, dtype=torch.int32, device=dev)
+    check(_lib.lib().tlx_accept(_ptr(amds), _ptr(drafts), k, _ptr(mb), _ptr(eb), _stream(amds)), "accept")
+    return mb, eb
+
+
+__all__ = ["Workspace", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
+           "head_argmax", "argmax_rows", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]

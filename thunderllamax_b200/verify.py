@@ -1,0 +1,152 @@
+"""The K-row speculative verify step on one GPU.
+
+One step = the dense FFN of the probe trunk followed by the LM head:
+
+    gact = silu(Wg X) * (Wu X)        IQ3_XXS, 11 x 5120 -> 11 x 17408 (fp16)
+    Y    = R + Wd gact                Q6_K,   11 x 17408 -> 11 x 5120  (fp32)
+    (max, idx)[t] = argmax_v (Wh H)   Q6_K,   11 x 5120 -> 151936 vocab, no logits
+    m, bonus = accept(idx, drafts)    greedy draft acceptance
+
+which is the reference's per-layer ffn8v11r7 -> down8nw32v11r7 pair
+(engine/mtp.py:1127-1128) and its head8v11 -> amx3 -> accept11k tail
+(engine/mtp.py:1159-1161, :749-753).  Three kernel launches per step, captured
+in a CUDA graph (the reference's pre-recorded ParityGraph, engine/gcycle.py:22-73).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops, synth
+
+
+@dataclass
+class VerifyShape:
+    dim: int = 5120
+    ffn: int = 17408
+    vocab: int = 151936
+    rows: int = 11           # K + 1 probe rows
+    ffn_q: str = "iq3_xxs"
+    down_q: str = "q6_k"
+    head_q: str = "q6_k"
+
+    @property
+    def n_drafts(self) -> int:
+        return self.rows - 1
+
+    def weight_bytes(self) -> dict:
+        return {"gate": self.ffn * synth.row_bytes(self.ffn_q, self.dim),
+                "up": self.ffn * synth.row_bytes(self.ffn_q, self.dim),
+                "down": self.dim * synth.row_bytes(self.down_q, self.ffn),
+                "head": self.vocab * synth.row_bytes(self.head_q, self.dim)}
+
+    def algorithmic_bytes(self) -> dict:
+        """Bytes a roofline-optimal step must move: weights once, activations in, results out."""
+        wb = self.weight_bytes()
+        r, d, f = self.rows, self.dim, self.ffn
+        return {"ffn_gate_up": wb["gate"] + wb["up"] + r * d * 2 + r * f * 2,
+                "ffn_down": wb["down"] + r * f * 2 + r * d * 4 * 2,
+                "head_argmax": wb["head"] + r * d * 2 + r * 8}
+
+
+def synth_tiled(qtype: str, n_rows: int, k: int, seed: int, chunk_rows: int = 8192) -> torch.Tensor:
+    """Seeded synthetic GGUF blocks, generated in row chunks and repacked on the
+    device straight into one tiled buffer (no full-size host copy)."""
+    out = torch.empty(ops.tiled_bytes(qtype, n_rows, k), dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(seed)
+    per_tile = ops.tiled_bytes(qtype, 16, k)
+    chunk_rows -= chunk_rows % 16
+    for r0 in range(0, n_rows, chunk_rows):
+        n = min(chunk_rows, n_rows - r0)
+        raw = synth.BLOCK_GEN[qtype](rng, n, k)
+        t = ops.pack_tiles(qtype, raw, k)
+        off = (r0 // 16) * per_tile
+        out[off:off + t.numel()].copy_(t)
+    return out
+
+
+class VerifyStep:
+    def __init__(self, shape: VerifyShape = VerifyShape(), seed: int = 0, weights: dict | None = None):
+        ops.require_device()
+        self.shape = s = shape
+        self.w = weights if weights is not None else {
+            "gate": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 1),
+            "up": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 2),
+            "down": synth_tiled(s.down_q, s.dim, s.ffn, seed + 3),
+            "head": synth_tiled(s.head_q, s.vocab, s.dim, seed + 4),
+        }
+        dev = "cuda"
+        self.x = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self.h = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self.res = torch.zeros((s.rows, s.dim), dtype=torch.float32, device=dev)
+        self.drafts = torch.zeros(s.n_drafts, dtype=torch.int32, device=dev)
+        self.gact = torch.empty((s.rows, s.ffn), dtype=torch.float16, device=dev)
+        self.y = torch.empty((s.rows, s.dim), dtype=torch.float32, device=dev)
+        self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
+        self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
+        self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
+        self.ws = {
+            "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, s.ffn, s.dim, s.rows),
+            "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, s.ffn, s.rows, torch.float16),
+            "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, s.vocab, s.dim, s.rows),
+        }
+        self.graph = None
+
+    # ---- the three launches ----
+    def launch_ffn_gate_up(self):
+        s = self.shape
+        ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, s.ffn, self.ws["ffn_gate_up"], gact=self.gact)
+
+    def launch_ffn_down(self):
+        s = self.shape
+        ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, self.ws["ffn_down"], y=self.y, residual=self.res)
+
+    def launch_head_argmax(self):
+        s = self.shape
+        ops.head_argmax(s.head_q, self.w["head"], self.h, s.vocab, self.ws["head_argmax"], out_max=self.out_max,
+                        out_idx=self.out_idx, drafts=self.drafts, accept_out=self.accept_out)
+
+    KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
+    LAUNCHES_PER_STEP = 3
+
+    def launch(self):
+        self.launch_ffn_gate_up()
+        self.launch_ffn_down()
+        self.launch_head_argmax()
+
+    def capture(self):
+        """Record the step once as a CUDA graph (after a warm-up launch)."""
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            self.launch()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.launch()
+        self.graph = g
+        return g
+
+    def replay(self):
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+
+    def set_inputs(self, x, h, res=None, drafts=None):
+        self.x.copy_(x, non_blocking=True)
+        self.h.copy_(h, non_blocking=True)
+        if res is not None:
+            self.res.copy_(res, non_blocking=True)
+        if drafts is not None:
+            self.drafts.copy_(drafts, non_blocking=True)
+
+    def step_host(self, x_pinned, h_pinned, drafts_pinned, out_pinned):
+        """End-to-end step through host buffers: H2D inputs, graph replay, D2H of
+        the accept record (m, bonus) and the 11 argmax ids."""
+        self.set_inputs(x_pinned, h_pinned, drafts=drafts_pinned)
+        self.replay()
+        out_pinned[:2].copy_(self.accept_out, non_blocking=True)
+        out_pinned[2:].copy_(self.out_idx, non_blocking=True)
