@@ -122,6 +122,26 @@ int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* 
                     uint64_t* out_keys, const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws,
                     size_t ws_bytes, void* stream);
 
+/* ---- allocation-free head argmax --------------------------------------------------
+ * Same computation and results as tlx_head_argmax, for callers that cannot call
+ * cudaMalloc where they run the head (a runtime that owns all device memory in a
+ * fixed pool and forbids allocation after start-up, a plug-in given no memory
+ * budget, a loop that cannot afford cudaMalloc's implicit synchronisation).  No
+ * reference counterpart: the reference's kernels take no workspace.
+ * Scratch is a fixed array of TLX_NOALLOC_SCRATCH_BYTES inside the library, held
+ * on every GPU that loads it until process exit; shapes needing more return
+ * TLX_ERR_WORKSPACE (the full 151936 x 5120, 11-row head needs ~19.5 MB).  The
+ * first call on a device looks the array's address up (make it before any stream
+ * capture); every call clears the array's counters on `stream` and allocates
+ * nothing.  All calls share the one array: calls that can overlap on the GPU
+ * (different streams, concurrent graphs) race and must be serialised by the
+ * caller. */
+#define TLX_NOALLOC_SCRATCH_BYTES (24u << 20)
+int tlx_head_argmax_noalloc(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
+                            int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
+                            uint64_t* out_keys, const int32_t* drafts, int n_drafts, int32_t* accept_out,
+                            void* stream);
+
 /* ---- argmax over materialised logits (amx3 / h_argmax) -----------------------------
  * amds[t] = argmax_v logits[t*ld + v] (fp32 or fp16 logits), strict '>' so the
  * lowest index wins ties and NaN never wins.  engine/amx3.cu:117-142. */

@@ -692,6 +692,14 @@ size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, i
   return P.ws_bytes;
 }
 
+// bytes at the front of the workspace that must be zero before a launch (error
+// word, done counter, per-tile arrival counters); the rest is written before read
+size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas) {
+  Plan P;
+  if (make_plan(qt, epi, n_rows, k, m, x_dtype, max_ctas, P)) return 0;
+  return P.off_best;
+}
+
 int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
                    int n_info) {
   Plan P;

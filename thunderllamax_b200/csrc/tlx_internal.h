@@ -17,6 +17,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
              const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
              cudaStream_t stream);
 size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
+size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
 int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
                    int n_info);
 
