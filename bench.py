@@ -56,7 +56,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -372,7 +372,7 @@ def run_ours(args):
                          "rows": shape.rows, "weight_bytes_per_step": total_w,
                          "parallelism": f"tp{ws}" if ws > 1 else "single",
                          "l2": f"weights {total_w / 1e6:.0f} MB > 126 MB L2 (no flush needed)",
-                         "graph": "CUDA graph replay, 3 launches/step" + (" + 2 NCCL collectives" if ws > 1 else "")},
+                         "graph": f"CUDA graph replay, {step.LAUNCHES_PER_STEP} launches/step" + (" + 2 NCCL collectives" if ws > 1 else "")},
               "frac_of_hbm": round(value / ws / peak, 4), "frac_of_8tbs": round(value / ws / 8000.0, 4),
               "roofline": {"bound": "hbm", "kernel": "head_argmax", "achieved": round(achieved, 1),
                            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -394,7 +394,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-port baseline")

@@ -31,6 +31,10 @@ extern "C" {
 #define TLX_DT_F32 0
 #define TLX_DT_F16 1
 #define TLX_DT_BF16 30
+/* activations already staged as an fp16 activation image (tlx_stage_activations,
+ * or tlx_ffn_gate_up with gact_dtype = TLX_DT_IMAGE): x points at the image, ldx
+ * is ignored, one column per token */
+#define TLX_DT_IMAGE 100
 /* gemv modes for tlx_gemv_workspace_bytes */
 #define TLX_MODE_STORE 0
 #define TLX_MODE_GATE_UP 1
@@ -86,6 +90,16 @@ int tlx_gemv_plan(int mode, int qtype, int64_t n_rows, int64_t k, int m, int x_d
 /* synchronous read of the workspace error word (TLX_WS_ERR_* bits) */
 int tlx_workspace_error(const void* ws, uint32_t* err_out);
 
+/* ---- activation image --------------------------------------------------------------
+ * The GEMV kernels read activations as an fp16 image in mma-fragment order
+ * ([k/256][16][columns][4][4 halves]) that each CTA pulls into shared memory with
+ * one bulk copy.  Raw bf16/fp16/fp32 activations are staged into the workspace by
+ * each call; a caller that feeds the same activations to several GEMVs, or chains
+ * gate/up -> down, can stage once and pass TLX_DT_IMAGE.  fp32 activations use 3
+ * columns per token (exact hi+mid+lo fp16 split). */
+size_t tlx_activation_image_bytes(int m, int64_t k, int x_dtype);
+int tlx_stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, void* stream);
+
 /* ---- K-row dequantised matvec ----------------------------------------------------
  * y[t][r] = sum_k W[r][k] * x[t][k] (+ residual[t][r]), t < m <= 16 (m <= 5 for
  * fp32 x), fp32 accumulate; y is fp32 or fp16 (y_dtype).  W tiled
@@ -100,8 +114,10 @@ int tlx_gemv(int qtype, const void* w, const uint32_t* grid, const void* x, int 
              void* ws, size_t ws_bytes, void* stream);
 
 /* ---- fused gate/up + SiLU ------------------------------------------------------------
- * gact[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r], stored fp32 or fp16 (gact_dtype; fp16
- * is what the down projection consumes, like the reference's fp16 gact).
+ * gact[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r], stored fp32 or fp16 (gact_dtype), or
+ * (gact_dtype = TLX_DT_IMAGE, n_rows % 256 == 0) directly as the fp16 activation
+ * image a following GEMV over k = n_rows reads (the reference's fp16 gact feeding
+ * down8; ldg ignored, gact must hold tlx_activation_image_bytes(m, n_rows, F16)).
  * Replaces ffn8v11(wg, wu, gridf, hhx, gact) engine/ffn8v11.cu:88-133 and the r7
  * twin engine/ffn8v11r7.cu:261. */
 int tlx_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,

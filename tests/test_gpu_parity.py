@@ -144,9 +144,29 @@ def test_ffn_config2_end_to_end():
     ws2 = ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", H, F, m, torch.float16)
     gact = ops.ffn_gate_up("iq3_xxs", wg, wu, x, F, ws1, out_dtype=torch.float16)
     y = ops.gemv("q6_k", wd, gact, H, ws2, residual=torch.from_numpy(res).cuda())
+    # same chain through the activation image: gate/up writes gact as down's image
+    img = ops.Image(m, F)
+    ws3 = ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", H, F, m, "image")
+    ops.ffn_gate_up("iq3_xxs", wg, wu, x, F, ws1, gact=img)
+    y_img = ops.gemv("q6_k", wd, img, H, ws3, residual=torch.from_numpy(res).cuda())
     torch.cuda.synchronize()
     check_rows(gact.float().cpu().numpy(), gact_ref, tight=1e-3)
     check_rows(y.cpu().numpy(), y_ref, tight=1e-4)
+    assert torch.equal(y, y_img)
+
+
+def test_staged_activation_image_matches_raw_path():
+    rng = np.random.default_rng(12)
+    n, k, m = 500, 2048, 11
+    raw = synth.q6k_blocks(rng, n, k)
+    x, x64 = x_tensor(rng, m, k, torch.bfloat16)
+    w = ops.pack_tiles("q6_k", raw, k)
+    y_raw = ops.gemv("q6_k", w, x, n, ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", n, k, m))
+    img = ops.stage(x)
+    y_img = ops.gemv("q6_k", w, img, n, ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", n, k, m, "image"))
+    torch.cuda.synchronize()
+    assert torch.equal(y_raw, y_img)
+    check_rows(y_img.cpu().numpy(), oracle.matvec_f64(oracle.dequant("q6_k", raw, k), x64))
 
 
 @pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs"])
@@ -294,3 +314,32 @@ def test_host_argument_errors_raise():
     ws = ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", 32, 256, 2)
     with pytest.raises(ops.TLXError):
         ops.gemv("q6_k", w, x[:, 1:], 32, ws)        # misaligned activations
+
+
+def test_verify_step_pipeline_vs_oracle():
+    # the graph-captured verify step (stage -> gate/up -> gact image -> down; stage ->
+    # head argmax + accept) at reduced width against the oracle
+    from thunderllamax_b200.verify import VerifyShape, VerifyStep
+
+    rng = np.random.default_rng(99)
+    s = VerifyShape(dim=1024, ffn=2048, vocab=7001, rows=11)
+    rg, ru = synth.iq3xxs_blocks(rng, s.ffn, s.dim), synth.iq3xxs_blocks(rng, s.ffn, s.dim)
+    rd, rh = synth.q6k_blocks(rng, s.dim, s.ffn), synth.q6k_blocks(rng, s.vocab, s.dim)
+    w = {"gate": ops.pack_tiles("iq3_xxs", rg, s.dim), "up": ops.pack_tiles("iq3_xxs", ru, s.dim),
+         "down": ops.pack_tiles("q6_k", rd, s.ffn), "head": ops.pack_tiles("q6_k", rh, s.dim)}
+    step = VerifyStep(s, weights=w)
+    x, x64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+    h, h64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+    res = rng.standard_normal((s.rows, s.dim), dtype=np.float32)
+    _, y_ref = oracle.ffn_f64(x64, rg, ru, rd, residual=res)
+    _, idx_ref, _ = oracle.head_argmax(h64, rh, "q6_k")
+    drafts_np = idx_ref[:10].copy()
+    drafts_np[7] = (drafts_np[7] + 3) % s.vocab
+    step.set_inputs(x, h, res=torch.from_numpy(res).cuda(), drafts=torch.from_numpy(drafts_np).cuda())
+    step.capture()
+    for _ in range(3):
+        step.replay()
+    torch.cuda.synchronize()
+    check_rows(step.y.cpu().numpy(), y_ref, tight=1e-4)
+    assert np.array_equal(step.out_idx.cpu().numpy(), idx_ref)
+    assert step.accept_out.cpu().tolist() == list(oracle.accept(idx_ref, drafts_np))

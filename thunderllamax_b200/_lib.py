@@ -13,7 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("TLX_LIB", os.path.join(_HERE, "libtlx_b200.so"))
 
 TLX_Q6_K, TLX_IQ3_XXS, TLX_IQ4_XS = 14, 18, 23
-TLX_DT_F32, TLX_DT_F16, TLX_DT_BF16 = 0, 1, 30
+TLX_DT_F32, TLX_DT_F16, TLX_DT_BF16, TLX_DT_IMAGE = 0, 1, 30, 100
 MODE_STORE, MODE_GATE_UP, MODE_ARGMAX = 0, 1, 2
 QTYPES = {"q6_k": TLX_Q6_K, "iq3_xxs": TLX_IQ3_XXS, "iq4_xs": TLX_IQ4_XS}
 
@@ -40,6 +40,10 @@ _SIGS = {
     "tlx_workspace_init": (c_int, [c_vp, c_size, c_vp]),
     "tlx_gemv_plan": (c_int, [c_int, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_int]),
     "tlx_workspace_error": (c_int, [c_vp, c_vp]),
+    "tlx_activation_image_bytes": (c_size, [c_int, c_i64, c_int]),
+    "tlx_stage_activations": (c_int, [c_vp, c_int, c_i64, c_int, c_i64, c_vp, c_vp]),
+    "tlx_head_argmax_noalloc": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp,
+                                        c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
     "tlx_gemv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp, c_int,
                          c_i64, c_vp, c_size, c_vp]),
     "tlx_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_int,

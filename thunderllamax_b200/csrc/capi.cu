@@ -309,6 +309,14 @@ int tlx_workspace_error(const void* ws, uint32_t* err_out) {
   return cudaMemcpy(err_out, ws, 4, cudaMemcpyDeviceToHost) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
+size_t tlx_activation_image_bytes(int m, int64_t k, int x_dtype) {
+  return activation_image_bytes(m, k, x_dtype);
+}
+
+int tlx_stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, void* stream) {
+  return stage_activations(x, x_dtype, ldx, m, k, image, as_stream(stream));
+}
+
 int tlx_gemv(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
              int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y, int y_dtype, int64_t ldy,
              void* ws, size_t ws_bytes, void* stream) {

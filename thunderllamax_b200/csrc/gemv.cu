@@ -41,17 +41,16 @@ struct GemvParams {
   const uint8_t* w0;
   const uint8_t* w1;
   const uint32_t* grid;
-  const void* x;
-  int x_dtype;
+  const uint2* ximg;  // fp16 activation image [NB][16 mma][MC cols][4 quarters] of 4 halves
   int M;
   int MC;
   int CG;  // columns per token (1, or 3 for fp32 activations split into fp16 parts)
-  int64_t ldx;
   int64_t n_rows;
   int T, NB, S, Bs, Cs, J;
   void* y;
   int y_f16;  // store y as fp16 instead of fp32
   int64_t ldy;
+  uint2* y_img;  // GATEUP: write gact as an fp16 activation image for the consumer GEMV
   const float* residual;
   int64_t ldr;
   float* out_max;
@@ -69,8 +68,11 @@ struct GemvParams {
 };
 
 // ---- shared-memory layout (same arithmetic on host and device) ----
+// The epilogue of a tile reuses the ring stage its last block was read from (the
+// next copy into that stage is issued only after the epilogue), so there is no
+// separate scratch region.
 struct SmemLayout {
-  uint32_t xs, grid, ring, bars, epi, best, total;
+  uint32_t xs, grid, ring, bars, best, total;
 };
 
 __host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int stages, int Bs, int MC) {
@@ -78,6 +80,7 @@ __host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int
   uint32_t off = 0;
   L.xs = off;
   off += static_cast<uint32_t>(Bs) * 16u * static_cast<uint32_t>(MC) * 32u;
+  off += 512u;  // slack: the unused token columns of the last mma read past the image
   off = (off + 127u) & ~127u;
   L.grid = off;
   if (qt == QT_IQ3_XXS) off += 256u * 32u * 4u;
@@ -85,9 +88,7 @@ __host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int
   off += static_cast<uint32_t>(wpc) * stages * chunk_bytes(qt) * nmat;
   off = (off + 15u) & ~15u;
   L.bars = off;
-  off += static_cast<uint32_t>(wpc) * stages * 8u;
-  L.epi = off;
-  off += static_cast<uint32_t>(wpc) * nmat * 16u * 16u * 4u;
+  off += static_cast<uint32_t>(wpc) * stages * 8u + 8u;  // + the activation-image barrier
   L.best = off;
   off += static_cast<uint32_t>(wpc) * 16u * 8u + 128u;  // + done flag and 16 final ids
   L.total = off;
@@ -101,78 +102,59 @@ __device__ __forceinline__ int warp_of(int64_t f, int64_t Fs, int Ws) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// ---- activation staging: x[M][K] (f32 / f16 / bf16) -> fp16 B fragments ----
-__device__ void stage_x(const GemvParams& p, int seg, uint2* xs) {
-  const int groups_per_tok = p.Bs * 64;  // 4-element groups
-  const int total = p.M * groups_per_tok;
-  const int64_t k_base = static_cast<int64_t>(seg) * p.Bs * kQK;
-  for (int gi = threadIdx.x; gi < total; gi += blockDim.x) {
-    const int t = gi / groups_per_tok;
-    const int kk = (gi - t * groups_per_tok) * 4;
-    const int bb = kk >> 8, kin = kk & 255, q = kin >> 6, m = (kin & 63) >> 2;
-    const int64_t src = t * p.ldx + k_base + kk;
+// image index (uint2 units) of the 4-halves entry holding x[t][k..k+3], k % 4 == 0
+__host__ __device__ __forceinline__ int64_t image_index(int64_t k, int col, int MC) {
+  const int64_t b = k >> 8;
+  const int kin = static_cast<int>(k & 255), q = kin >> 6, m = (kin & 63) >> 2;
+  return ((b * 16 + m) * MC + col) * 4 + q;
+}
+
+// ---- activation staging: x[M][K] (f32 / f16 / bf16) -> fp16 image ----
+__global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_t ldx, int M, int CG, int MC, int64_t K,
+                                   uint2* __restrict__ img) {
+  const int64_t per_tok = K >> 2;
+  const int64_t total = static_cast<int64_t>(M) * per_tok;
+  for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < total;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(gi / per_tok);
+    const int64_t k = (gi - t * per_tok) * 4;
+    const int64_t src = t * ldx + k;
     float v[4];
-    if (p.x_dtype == DT_F32) {
-      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + src);
+    if (dtype == DT_F32) {
+      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
       v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
     } else {
-      const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + src);
+      const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + src);
       const uint32_t h[2] = {raw.x, raw.y};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const uint32_t bits = (h[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-        v[e] = p.x_dtype == DT_BF16 ? __uint_as_float(bits << 16)
-                                    : __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+        v[e] = dtype == DT_BF16 ? __uint_as_float(bits << 16)
+                                : __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
       }
     }
-    const int base = (bb * 16 + m) * p.MC;
-    if (p.CG == 1) {
-      const __half2 h01 = __floats2half2_rn(v[0], v[1]);
-      const __half2 h23 = __floats2half2_rn(v[2], v[3]);
-      xs[(base + t) * 4 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
-                                          *reinterpret_cast<const uint32_t*>(&h23));
-    } else {
-      // fp32 -> hi + mid + lo fp16 parts (33 significand bits >= 24)
+    for (int part = 0; part < CG; ++part) {
+      // CG == 3: fp32 -> hi + mid + lo fp16 parts (33 significand bits >= 24)
+      float hp[4];
 #pragma unroll
-      for (int part = 0; part < 3; ++part) {
-        float hpart[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hpart[e] = __half2float(__float2half_rn(v[e]));
-          v[e] -= hpart[e];
-        }
-        const __half2 h01 = __floats2half2_rn(hpart[0], hpart[1]);
-        const __half2 h23 = __floats2half2_rn(hpart[2], hpart[3]);
-        xs[(base + 3 * t + part) * 4 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
-                                                       *reinterpret_cast<const uint32_t*>(&h23));
+      for (int e = 0; e < 4; ++e) {
+        hp[e] = __half2float(__float2half_rn(v[e]));
+        v[e] -= hp[e];
       }
+      const __half2 h01 = __floats2half2_rn(hp[0], hp[1]);
+      const __half2 h23 = __floats2half2_rn(hp[2], hp[3]);
+      img[image_index(k, t * CG + part, MC)] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                                                          *reinterpret_cast<const uint32_t*>(&h23));
     }
   }
 }
 
-template <int NT>
-__device__ __forceinline__ void load_b(const uint2* xs, int bb, int m, int MC, int lane, uint32_t (&b)[NT][2]) {
-  const int g = lane >> 2, q = lane & 3;
-  const uint2* base = xs + (bb * 16 + m) * MC * 4;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int col = nt * 8 + g;
-    if (col < MC) {
-      const uint2 v = lds64(base + col * 4 + q);
-      b[nt][0] = v.x;
-      b[nt][1] = v.y;
-    } else {
-      b[nt][0] = 0u;
-      b[nt][1] = 0u;
-    }
-  }
-}
-
-// one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B)
+// one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B).
+// xb: this lane's B entries of the block (token g, quarter q); mma m at xb[m*mstride],
+// token g+8 at +32 (columns >= MC read garbage that only feeds unused columns)
 template <int QT, int NT, int NMAT>
-__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xs,
-                                              const uint32_t* grid_rep, int bb, int MC, int lane,
-                                              float (&acc)[NMAT][NT][4]) {
+__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xb, int mstride,
+                                              const uint32_t* grid_rep, int lane, float (&acc)[NMAT][NT][4]) {
   float tmp[NMAT][NT][4];
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
@@ -181,6 +163,14 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
 #pragma unroll
       for (int i = 0; i < 4; ++i) tmp[a][nt][i] = 0.f;
   float2 scale[NMAT];
+  auto load_b = [&](int m, uint32_t (&b)[NT][2]) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint2 v = lds64(xb + m * mstride + nt * 32);
+      b[nt][0] = v.x;
+      b[nt][1] = v.y;
+    }
+  };
   if constexpr (QT == QT_Q6_K) {
 #pragma unroll
     for (int a = 0; a < NMAT; ++a) {
@@ -191,10 +181,10 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
         uint32_t a0[4], a1[4];
         q6_group(s, gam, a0, a1);
         uint32_t b[NT][2];
-        load_b<NT>(xs, bb, 2 * gam, MC, lane, b);
+        load_b(2 * gam, b);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a0, b[nt][0], b[nt][1]);
-        load_b<NT>(xs, bb, 2 * gam + 1, MC, lane, b);
+        load_b(2 * gam + 1, b);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a1, b[nt][0], b[nt][1]);
       }
@@ -210,7 +200,7 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
       uint32_t b[NT][2];
-      load_b<NT>(xs, bb, m, MC, lane, b);
+      load_b(m, b);
 #pragma unroll
       for (int a = 0; a < NMAT; ++a) {
         uint32_t af[4];
@@ -231,9 +221,10 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
     }
 }
 
-// tile epilogue on complete sums (fragment order in registers)
+// tile epilogue on complete sums (fragment order in registers); epi = 1 KB per matrix of
+// shared scratch owned by this warp
 template <int NT, int NMAT, int EPI>
-__device__ __forceinline__ void tile_epilogue(const GemvParams& p, int t, const float (&v)[NMAT][NT][4],
+__device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4],
                                               float* epi, int lane, uint64_t& best) {
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
@@ -245,7 +236,12 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int t, const 
       *reinterpret_cast<float2*>(epi + a * 256 + (g + 8) * 16 + col) = make_float2(v[a][nt][2], v[a][nt][3]);
     }
   __syncwarp();
-  const int64_t row0 = static_cast<int64_t>(t) * kTileRows;
+  const int64_t row0 = t * kTileRows;
+  auto value = [&](int a, int r, int tk) {
+    float val = 0.f;
+    for (int c = 0; c < p.CG; ++c) val += epi[a * 256 + r * 16 + tk * p.CG + c];
+    return val;
+  };
   if constexpr (EPI == EPI_ARGMAX) {
     const int tk = lane & 15, rh = lane >> 4;
     if (tk < p.M) {
@@ -253,10 +249,34 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int t, const 
       for (int r8 = 0; r8 < 8; ++r8) {
         const int r = rh * 8 + r8;
         if (row0 + r < p.n_rows) {
-          float val = 0.f;
-          for (int c = 0; c < p.CG; ++c) val += epi[r * 16 + tk * p.CG + c];
-          const uint64_t key = argmax_key(val, static_cast<uint32_t>(p.row_offset + row0 + r));
+          const uint64_t key = argmax_key(value(0, r, tk), static_cast<uint32_t>(p.row_offset + row0 + r));
           best = key > best ? key : best;
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_GATEUP) {
+    if (p.y_img) {
+      // 4 consecutive rows of one token -> one image entry of the consumer's activations
+      for (int idx = lane; idx < 4 * p.M; idx += 32) {
+        const int r4 = idx & 3, tk = idx >> 2;
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = silu_f(value(0, 4 * r4 + e, tk)) * value(1, 4 * r4 + e, tk);
+        const __half2 h01 = __floats2half2_rn(o[0], o[1]);
+        const __half2 h23 = __floats2half2_rn(o[2], o[3]);
+        p.y_img[image_index(row0 + 4 * r4, tk, p.M)] =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+      }
+    } else {
+      for (int idx = lane; idx < 16 * p.M; idx += 32) {
+        const int r = idx & 15, tk = idx >> 4;
+        const int64_t row = row0 + r;
+        if (row < p.n_rows) {
+          const float val = silu_f(value(0, r, tk)) * value(1, r, tk);
+          if (p.y_f16)
+            static_cast<__half*>(p.y)[tk * p.ldy + row] = __float2half_rn(val);
+          else
+            static_cast<float*>(p.y)[tk * p.ldy + row] = val;
         }
       }
     }
@@ -265,15 +285,8 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int t, const 
       const int r = idx & 15, tk = idx >> 4;
       const int64_t row = row0 + r;
       if (row < p.n_rows) {
-        float val = 0.f;
-        for (int c = 0; c < p.CG; ++c) val += epi[r * 16 + tk * p.CG + c];
-        if constexpr (EPI == EPI_GATEUP) {
-          float u = 0.f;
-          for (int c = 0; c < p.CG; ++c) u += epi[256 + r * 16 + tk * p.CG + c];
-          val = silu_f(val) * u;
-        } else {
-          if (p.residual) val += p.residual[tk * p.ldr + row];
-        }
+        float val = value(0, r, tk);
+        if (p.residual) val += p.residual[tk * p.ldr + row];
         if (p.y_f16)
           static_cast<__half*>(p.y)[tk * p.ldy + row] = __float2half_rn(val);
         else
@@ -288,14 +301,15 @@ template <int QT, int NT, int EPI, int WPC, int STAGES>
 __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams p) {
   constexpr int NMAT = EPI == EPI_GATEUP ? 2 : 1;
   constexpr uint32_t CH = chunk_bytes(QT);
+  constexpr uint32_t STAGE_BYTES = CH * NMAT;
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout L = smem_layout(QT, NMAT, WPC, STAGES, p.Bs, p.MC);
   uint2* xs = reinterpret_cast<uint2*>(smem + L.xs);
   uint32_t* grid_rep = reinterpret_cast<uint32_t*>(smem + L.grid);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* ring = smem + L.ring + static_cast<uint32_t>(warp) * STAGES * CH * NMAT;
+  uint8_t* ring = smem + L.ring + static_cast<uint32_t>(warp) * STAGES * STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * STAGES;
-  float* epi = reinterpret_cast<float*>(smem + L.epi) + warp * NMAT * 256;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + L.bars) + WPC * STAGES;
   uint64_t* wbest = reinterpret_cast<uint64_t*>(smem + L.best);
 
   const int seg = blockIdx.x / p.Cs;
@@ -308,29 +322,46 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   const int64_t f0 = active ? static_cast<int64_t>(wseg) * Fs / Ws : 0;
   const int64_t f1 = active ? static_cast<int64_t>(wseg + 1) * Fs / Ws : 0;
   const int64_t n_items = f1 - f0;
+  const int64_t t_first = f0 / p.Bs;
+  const int bb_first = static_cast<int>(f0 - t_first * p.Bs);
 
-  auto issue = [&](int64_t f, int st) {
-    const int64_t t = f / p.Bs;
-    const int b = seg * p.Bs + static_cast<int>(f - t * p.Bs);
-    const int64_t off = (t * p.NB + b) * static_cast<int64_t>(CH);
-    mbar_arrive_expect_tx(&bars[st], CH * NMAT);
-    bulk_g2s(ring + st * CH * NMAT, p.w0 + off, CH, &bars[st]);
-    if constexpr (NMAT == 2) bulk_g2s(ring + st * CH * NMAT + CH, p.w1 + off, CH, &bars[st]);
+  // activations of this k-segment: one bulk copy of the image slice
+  const uint32_t xbytes = static_cast<uint32_t>(p.Bs) * 16u * static_cast<uint32_t>(p.MC) * 32u;
+  if (threadIdx.x == 0) {
+    mbar_init(xbar, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(xbar, xbytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg) + static_cast<size_t>(seg) * xbytes;
+    for (uint32_t off = 0; off < xbytes; off += 32768u)
+      bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
+  }
+
+  // weight ring: issue cursor (it, ibb) walks the same items as the compute cursor
+  int64_t it = t_first;
+  int ibb = bb_first;
+  auto issue = [&](int st) {
+    const int64_t off = (it * p.NB + seg * p.Bs + ibb) * static_cast<int64_t>(CH);
+    mbar_arrive_expect_tx(&bars[st], STAGE_BYTES);
+    bulk_g2s(ring + st * STAGE_BYTES, p.w0 + off, CH, &bars[st]);
+    if constexpr (NMAT == 2) bulk_g2s(ring + st * STAGE_BYTES + CH, p.w1 + off, CH, &bars[st]);
+    if (++ibb == p.Bs) {
+      ibb = 0;
+      ++it;
+    }
   };
-
   if (lane == 0) {
 #pragma unroll
     for (int st = 0; st < STAGES; ++st) mbar_init(&bars[st], 1);
     mbar_fence_init();
-    for (int st = 0; st < STAGES && st < n_items; ++st) issue(f0 + st, st);
+    for (int st = 0; st < STAGES && st < n_items; ++st) issue(st);
   }
   __syncwarp();
 
   if constexpr (QT == QT_IQ3_XXS) {
     for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) grid_rep[i] = __ldg(p.grid + (i >> 5));
   }
-  stage_x(p, seg, xs);
   __syncthreads();
+  bool failed = !mbar_wait_bounded(xbar, 0, threadIdx.x == 0 ? p.err : nullptr);
 
   float acc[NMAT][NT][4];
 #pragma unroll
@@ -340,12 +371,14 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[a][nt][i] = 0.f;
   uint64_t best = 0ull;
-  bool failed = false;
-  int64_t piece_start = f0;
-  int64_t i_fail = n_items;
+  int64_t i_fail = failed ? 0 : n_items;
 
-  for (int64_t i = 0; i < n_items; ++i) {
-    const int64_t f = f0 + i;
+  const int mstride = p.MC * 4;                                    // uint2 entries per mma row of the image
+  const uint2* xlane = xs + (lane >> 2) * 4 + (lane & 3);          // token g, quarter q
+  int64_t t = t_first;
+  int bb = bb_first;
+  int piece_bb0 = bb_first;                                        // first block of the current piece
+  for (int64_t i = 0; i < n_items && !failed; ++i) {
     const int st = static_cast<int>(i % STAGES);
     const uint32_t ph = static_cast<uint32_t>((i / STAGES) & 1);
     if (!mbar_wait_bounded(&bars[st], ph, lane == 0 ? p.err : nullptr)) {
@@ -353,83 +386,88 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       i_fail = i;
       break;
     }
-    const int64_t t = f / p.Bs;
-    const int bb = static_cast<int>(f - t * p.Bs);
+    uint8_t* stage = ring + st * STAGE_BYTES;
     const uint8_t* chunk[NMAT];
 #pragma unroll
-    for (int a = 0; a < NMAT; ++a) chunk[a] = ring + st * CH * NMAT + a * CH;
-    compute_block<QT, NT, NMAT>(chunk, xs, grid_rep, bb, p.MC, lane, acc);
+    for (int a = 0; a < NMAT; ++a) chunk[a] = stage + a * CH;
+    compute_block<QT, NT, NMAT>(chunk, xlane + bb * 16 * mstride, mstride, grid_rep, lane, acc);
     __syncwarp();
-    if (lane == 0 && i + STAGES < n_items) {
-      fence_proxy_async_smem();
-      issue(f + STAGES, st);
-    }
-    const bool run_end = (bb == p.Bs - 1) || (i == n_items - 1);
-    if (!run_end) continue;
 
-    // ---- a piece of tile t ends here ----
-    const int64_t run0 = t * p.Bs;
-    const bool whole = (p.S == 1) && (piece_start == run0) && (bb == p.Bs - 1);
-    if (whole) {
-      tile_epilogue<NT, NMAT, EPI>(p, static_cast<int>(t), acc, epi, lane, best);
-    } else {
-      const int w_first = warp_of(run0, Fs, Ws);
-      const int w_last = warp_of(run0 + p.Bs - 1, Fs, Ws);
-      const int pieces = w_last - w_first + 1;
-      const int my_j = wseg - w_first;
-      const int total = pieces * p.S;
-      const int64_t slot_stride = static_cast<int64_t>(NMAT) * NT * 4 * 32;
-      float* my_slot = p.partials + ((t * p.S + seg) * p.J + my_j) * slot_stride;
-#pragma unroll
-      for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) my_slot[((a * NT + nt) * 4 + e) * 32 + lane] = acc[a][nt][e];
-      __threadfence();
-      __syncwarp();
-      uint32_t old = 0;
-      if (lane == 0) old = atomicAdd(p.tile_cnt + t, 1u);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == static_cast<uint32_t>(total - 1)) {
-        __threadfence();
-        float v[NMAT][NT][4];
+    const bool run_end = (bb == p.Bs - 1) || (i == n_items - 1);
+    if (run_end) {
+      // ---- a piece of tile t ends here; the stage just read is the epilogue scratch ----
+      float* epi = reinterpret_cast<float*>(stage);
+      const int64_t run0 = t * p.Bs;
+      const bool whole = (p.S == 1) && (piece_bb0 == 0) && (bb == p.Bs - 1);
+      if (whole) {
+        tile_epilogue<NT, NMAT, EPI>(p, t, acc, epi, lane, best);
+      } else {
+        const int w_first = warp_of(run0, Fs, Ws);
+        const int w_last = warp_of(run0 + p.Bs - 1, Fs, Ws);
+        const int pieces = w_last - w_first + 1;
+        const int my_j = wseg - w_first;
+        const int total = pieces * p.S;
+        const int64_t slot_stride = static_cast<int64_t>(NMAT) * NT * 4 * 32;
+        float* my_slot = p.partials + ((t * p.S + seg) * p.J + my_j) * slot_stride;
 #pragma unroll
         for (int a = 0; a < NMAT; ++a)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
-        for (int s = 0; s < p.S; ++s)
-          for (int j = 0; j < pieces; ++j) {
-            if (s == seg && j == my_j) {
+            for (int e = 0; e < 4; ++e) my_slot[((a * NT + nt) * 4 + e) * 32 + lane] = acc[a][nt][e];
+        __threadfence();
+        __syncwarp();
+        uint32_t old = 0;
+        if (lane == 0) old = atomicAdd(p.tile_cnt + t, 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == static_cast<uint32_t>(total - 1)) {
+          __threadfence();
+          float v[NMAT][NT][4];
 #pragma unroll
-              for (int a = 0; a < NMAT; ++a)
+          for (int a = 0; a < NMAT; ++a)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+            for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) v[a][nt][e] += acc[a][nt][e];
-            } else {
-              const float* sl = p.partials + ((t * p.S + s) * p.J + j) * slot_stride;
+              for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
+          for (int s = 0; s < p.S; ++s)
+            for (int j = 0; j < pieces; ++j) {
+              if (s == seg && j == my_j) {
 #pragma unroll
-              for (int a = 0; a < NMAT; ++a)
+                for (int a = 0; a < NMAT; ++a)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) v[a][nt][e] += __ldcg(sl + ((a * NT + nt) * 4 + e) * 32 + lane);
+                    for (int e = 0; e < 4; ++e) v[a][nt][e] += acc[a][nt][e];
+              } else {
+                const float* sl = p.partials + ((t * p.S + s) * p.J + j) * slot_stride;
+#pragma unroll
+                for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[a][nt][e] += __ldcg(sl + ((a * NT + nt) * 4 + e) * 32 + lane);
+              }
             }
-          }
-        tile_epilogue<NT, NMAT, EPI>(p, static_cast<int>(t), v, epi, lane, best);
-        if (lane == 0) p.tile_cnt[t] = 0u;
+          tile_epilogue<NT, NMAT, EPI>(p, t, v, epi, lane, best);
+          if (lane == 0) p.tile_cnt[t] = 0u;
+        }
       }
+#pragma unroll
+      for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[a][nt][e] = 0.f;
     }
-#pragma unroll
-    for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[a][nt][e] = 0.f;
-    piece_start = f + 1;
+    // refill the stage (after its last generic-proxy use) with the item STAGES ahead
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && i + STAGES < n_items) issue(st);
+    if (++bb == p.Bs) {
+      bb = 0;
+      ++t;
+    }
+    if (run_end) piece_bb0 = bb;
   }
 
   if (failed) {
@@ -493,7 +531,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 struct Plan {
   int T, NB, S, Bs, C, Cs, J, MC, CG, NT, nmat, wpc, stages;
   size_t smem;
-  size_t off_cnt, off_best, off_part, ws_bytes;
+  size_t off_cnt, off_best, off_img, off_part, ws_bytes;
 };
 
 static int sm_count() {
@@ -522,17 +560,17 @@ static int smem_optin() {
 
 static constexpr uint32_t kXsBudget = 120u * 1024u;
 
+// warps per CTA and ring depth per (format, epilogue), sized so the verify-step
+// shapes (k = 5120 with 11 rows; k = 17408 in 4 segments) fit the 227 KB
+// shared-memory opt-in without splitting k further
 template <int QT, int EPI>
 struct Cfg;
-// warps per CTA and ring depth per (format, epilogue); sized so that the
-// verify-step shapes (k = 5120 with 11 rows; k = 17408 in 4 segments) fit the
-// 227 KB shared-memory opt-in without splitting k further
 template <> struct Cfg<QT_Q6_K, EPI_STORE> { static constexpr int WPC = 16, STAGES = 2; };
-template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 2; };
+template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 16, STAGES = 2; };
 template <> struct Cfg<QT_Q6_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
-template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 8, STAGES = 4; };
-template <> struct Cfg<QT_IQ3_XXS, EPI_ARGMAX> { static constexpr int WPC = 8, STAGES = 4; };
-template <> struct Cfg<QT_IQ3_XXS, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_IQ3_XXS, EPI_GATEUP> { static constexpr int WPC = 12, STAGES = 2; };
 
 static void cfg_for(int qt, int epi, int& wpc, int& stages) {
 #define TLX_CFG(Q, E)            \
@@ -552,11 +590,13 @@ static void cfg_for(int qt, int epi, int& wpc, int& stages) {
   stages = 2;
 }
 
+static int cols_per_token(int x_dtype) { return x_dtype == DT_F32 ? 3 : 1; }
+
 static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, Plan& P) {
   if (qt != QT_Q6_K && qt != QT_IQ3_XXS) return TLX_ERR_QTYPE;
   if (n_rows <= 0 || k <= 0 || (k % kQK) != 0) return TLX_ERR_SHAPE;
-  if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
-  P.CG = x_dtype == DT_F32 ? 3 : 1;
+  if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16 && x_dtype != DT_IMAGE) return TLX_ERR_DTYPE;
+  P.CG = cols_per_token(x_dtype);
   if (m < 1 || m * P.CG > 16) return TLX_ERR_SHAPE;
   if (n_rows > (int64_t(1) << 31) - 16 || k / kQK > (1 << 20)) return TLX_ERR_SHAPE;
   P.MC = m * P.CG;
@@ -596,6 +636,8 @@ static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dt
   off += (static_cast<size_t>(P.T) * 4 + 255) & ~size_t(255);
   P.off_best = off;
   off += (static_cast<size_t>(P.C) * 16 * 8 + 255) & ~size_t(255);
+  P.off_img = off;
+  if (x_dtype != DT_IMAGE) off += (static_cast<size_t>(P.NB) * 16 * P.MC * 32 + 255) & ~size_t(255);
   P.off_part = off;
   off += static_cast<size_t>(P.T) * P.S * P.J * P.nmat * P.NT * 4 * 32 * sizeof(float);
   P.ws_bytes = off;
@@ -624,6 +666,26 @@ static int dispatch(int qt, const Plan& P, const GemvParams& gp, cudaStream_t s)
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+size_t activation_image_bytes(int m, int64_t k, int x_dtype) {
+  if (m < 1 || k <= 0 || k % kQK) return 0;
+  const int mc = m * cols_per_token(x_dtype);
+  if (mc > 16) return 0;
+  return static_cast<size_t>(k / kQK) * 16 * mc * 32;
+}
+
+int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream) {
+  if (!x || !image) return TLX_ERR_NULL;
+  if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
+  if (activation_image_bytes(m, k, x_dtype) == 0) return TLX_ERR_SHAPE;
+  const size_t xe = x_dtype == DT_F32 ? 4 : 2;
+  if (!aligned(x, xe * 4) || ldx < k || (ldx % 4) != 0 || !aligned(image, 16)) return TLX_ERR_ALIGN;
+  const int cg = cols_per_token(x_dtype);
+  const int64_t groups = static_cast<int64_t>(m) * (k / 4);
+  const int blocks = static_cast<int>(std::min<int64_t>((groups + 255) / 256, 4096));
+  stage_image_kernel<<<blocks, 256, 0, stream>>>(x, x_dtype, ldx, m, cg, m * cg, k, static_cast<uint2*>(image));
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
              int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,
              int y_dtype, int64_t ldy, int64_t row_offset, float* out_max, int32_t* out_idx, uint64_t* out_keys,
@@ -636,26 +698,39 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   if (epi == EPI_GATEUP && !w1) return TLX_ERR_NULL;
   if (qt == QT_IQ3_XXS && !grid) return TLX_ERR_NULL;
   if (epi != EPI_ARGMAX && !y) return TLX_ERR_NULL;
-  if (epi != EPI_ARGMAX && y_dtype != DT_F32 && y_dtype != DT_F16) return TLX_ERR_DTYPE;
+  if (epi == EPI_STORE && y_dtype != DT_F32 && y_dtype != DT_F16) return TLX_ERR_DTYPE;
+  if (epi == EPI_GATEUP && y_dtype != DT_F32 && y_dtype != DT_F16 && y_dtype != DT_IMAGE) return TLX_ERR_DTYPE;
+  if (epi == EPI_GATEUP && y_dtype == DT_IMAGE && (n_rows % kQK) != 0) return TLX_ERR_SHAPE;
   if (ws_bytes < P.ws_bytes) return TLX_ERR_WORKSPACE;
   if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(ws, 256)) return TLX_ERR_ALIGN;
-  const size_t xe = x_dtype == DT_F32 ? 4 : 2;
-  if (!aligned(x, xe * 4) || ldx < k || (ldx % 4) != 0) return TLX_ERR_ALIGN;
-  if (epi != EPI_ARGMAX && ldy < n_rows) return TLX_ERR_SHAPE;
+  if (x_dtype == DT_IMAGE) {
+    if (!aligned(x, 16)) return TLX_ERR_ALIGN;
+  } else {
+    const size_t xe = x_dtype == DT_F32 ? 4 : 2;
+    if (!aligned(x, xe * 4) || ldx < k || (ldx % 4) != 0) return TLX_ERR_ALIGN;
+  }
+  if (epi != EPI_ARGMAX && y_dtype != DT_IMAGE && ldy < n_rows) return TLX_ERR_SHAPE;
+  if (epi == EPI_GATEUP && y_dtype == DT_IMAGE && !aligned(y, 16)) return TLX_ERR_ALIGN;
   if (residual && ldr < n_rows) return TLX_ERR_SHAPE;
   if (epi == EPI_ARGMAX && accept_out && (!drafts || n_drafts < 0 || n_drafts + 1 > m)) return TLX_ERR_SHAPE;
   if (epi == EPI_ARGMAX && (row_offset < 0 || row_offset + n_rows > (int64_t(1) << 32) - 1)) return TLX_ERR_SHAPE;
+
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const uint2* ximg = static_cast<const uint2*>(x);
+  if (x_dtype != DT_IMAGE) {
+    rc = stage_activations(x, x_dtype, ldx, m, k, wsb + P.off_img, stream);
+    if (rc) return rc;
+    ximg = reinterpret_cast<const uint2*>(wsb + P.off_img);
+  }
 
   GemvParams gp{};
   gp.w0 = static_cast<const uint8_t*>(w0);
   gp.w1 = static_cast<const uint8_t*>(w1);
   gp.grid = grid;
-  gp.x = x;
-  gp.x_dtype = x_dtype;
+  gp.ximg = ximg;
   gp.M = m;
   gp.MC = P.MC;
   gp.CG = P.CG;
-  gp.ldx = ldx;
   gp.n_rows = n_rows;
   gp.T = P.T;
   gp.NB = P.NB;
@@ -663,9 +738,10 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   gp.Bs = P.Bs;
   gp.Cs = P.Cs;
   gp.J = P.J;
-  gp.y = y;
+  gp.y = y_dtype == DT_IMAGE ? nullptr : y;
   gp.y_f16 = y_dtype == DT_F16 ? 1 : 0;
   gp.ldy = ldy;
+  gp.y_img = y_dtype == DT_IMAGE ? static_cast<uint2*>(y) : nullptr;
   gp.residual = residual;
   gp.ldr = ldr;
   gp.out_max = out_max;
@@ -675,7 +751,6 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   gp.drafts = drafts;
   gp.n_drafts = n_drafts;
   gp.accept_out = accept_out;
-  uint8_t* wsb = static_cast<uint8_t*>(ws);
   gp.err = reinterpret_cast<uint32_t*>(wsb);
   gp.done_cnt = reinterpret_cast<uint32_t*>(wsb + 4);
   gp.tile_cnt = reinterpret_cast<uint32_t*>(wsb + P.off_cnt);

@@ -9,7 +9,7 @@
 
 namespace tlx {
 
-enum : int { DT_F32 = TLX_DT_F32, DT_F16 = TLX_DT_F16, DT_BF16 = TLX_DT_BF16 };
+enum : int { DT_F32 = TLX_DT_F32, DT_F16 = TLX_DT_F16, DT_BF16 = TLX_DT_BF16, DT_IMAGE = TLX_DT_IMAGE };
 
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
              int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,
@@ -17,6 +17,8 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
              const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
              cudaStream_t stream);
 size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
+size_t activation_image_bytes(int m, int64_t k, int x_dtype);
+int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream);
 size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
 int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
                    int n_info);

@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import (MODE_ARGMAX, MODE_GATE_UP, MODE_STORE, QTYPES, TLX_DT_BF16, TLX_DT_F16, TLX_DT_F32,
-                   TLXError, check)
+                   TLX_DT_IMAGE, TLXError, check)
 
 _DT = {torch.float32: TLX_DT_F32, torch.float16: TLX_DT_F16, torch.bfloat16: TLX_DT_BF16}
 
@@ -97,7 +97,8 @@ class Workspace:
 
     @classmethod
     def for_shape(cls, mode: int, qtype, n_rows: int, k: int, m: int, x_dtype=torch.bfloat16, device="cuda"):
-        nb = _lib.lib().tlx_gemv_workspace_bytes(mode, qtype_id(qtype), n_rows, k, m, _DT[x_dtype])
+        dt = TLX_DT_IMAGE if x_dtype == "image" else _DT[x_dtype]
+        nb = _lib.lib().tlx_gemv_workspace_bytes(mode, qtype_id(qtype), n_rows, k, m, dt)
         if nb == 0:
             raise TLXError(f"unsupported shape for workspace: mode={mode} {qtype} n={n_rows} k={k} m={m}")
         return cls(nb, device)
@@ -123,7 +124,39 @@ def set_max_ctas(n: int) -> None:
     _lib.lib().tlx_set_max_ctas(int(n))
 
 
-def _x_args(x: torch.Tensor):
+class Image:
+    """Activations staged as the fp16 mma-fragment image the GEMV kernels bulk-copy
+    (``tlx_stage_activations``, or gate/up writing gact for the down projection)."""
+
+    def __init__(self, m: int, k: int, device="cuda", buf: torch.Tensor = None):
+        self.m, self.k = int(m), int(k)
+        nb = int(_lib.lib().tlx_activation_image_bytes(self.m, self.k, TLX_DT_F16))
+        if nb == 0:
+            raise TLXError(f"unsupported activation image shape m={m} k={k}")
+        self.buf = buf if buf is not None else torch.empty(nb, dtype=torch.uint8, device=device)
+        self.shape = (self.m, self.k)
+
+    def data_ptr(self):
+        return self.buf.data_ptr()
+
+    @property
+    def device(self):
+        return self.buf.device
+
+
+def stage(x: torch.Tensor, image: "Image" = None) -> "Image":
+    dt, ldx = _x_args(x)
+    if dt == TLX_DT_F32:
+        raise TLXError("fp32 activations are staged inside each call (3 columns per token)")
+    m, k = x.shape
+    image = image if image is not None else Image(m, k, x.device)
+    check(_lib.lib().tlx_stage_activations(_ptr(x), dt, ldx, m, k, _ptr(image.buf), _stream(x)), "stage")
+    return image
+
+
+def _x_args(x):
+    if isinstance(x, Image):
+        return TLX_DT_IMAGE, 0
     if x.dim() != 2 or x.stride(1) != 1:
         raise TLXError("x must be a row-major [m, k] tensor")
     if x.dtype not in _DT:
@@ -132,6 +165,8 @@ def _x_args(x: torch.Tensor):
 
 
 def _y_dtype(y):
+    if isinstance(y, Image):
+        return TLX_DT_IMAGE
     if y.dtype not in (torch.float32, torch.float16):
         raise TLXError("outputs are fp32 or fp16")
     return _DT[y.dtype]
@@ -162,7 +197,8 @@ def ffn_gate_up(qtype, w_gate: torch.Tensor, w_up: torch.Tensor, x: torch.Tensor
         gact = torch.empty((m, n_rows), dtype=out_dtype, device=x.device)
     g = grid(str(x.device)) if q == _lib.TLX_IQ3_XXS else None
     rc = _lib.lib().tlx_ffn_gate_up(q, _ptr(w_gate), _ptr(w_up), _ptr(g), _ptr(x), dt, ldx, m, n_rows, k,
-                                    _ptr(gact), _y_dtype(gact), gact.stride(0), _ptr(ws.buf), ws.nbytes,
+                                    _ptr(gact), _y_dtype(gact), 0 if isinstance(gact, Image) else gact.stride(0),
+                                    _ptr(ws.buf), ws.nbytes,
                                     _stream(x))
     check(rc, "ffn_gate_up")
     return gact
@@ -223,6 +259,6 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
     return mb, eb
 
 
-__all__ = ["Workspace", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
+__all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
            "head_argmax", "argmax_rows", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]

@@ -9,8 +9,10 @@ One step = the dense FFN of the probe trunk followed by the LM head:
 
 which is the reference's per-layer ffn8v11r7 -> down8nw32v11r7 pair
 (engine/mtp.py:1127-1128) and its head8v11 -> amx3 -> accept11k tail
-(engine/mtp.py:1159-1161, :749-753).  Three kernel launches per step, captured
-in a CUDA graph (the reference's pre-recorded ParityGraph, engine/gcycle.py:22-73).
+(engine/mtp.py:1159-1161, :749-753).  Five launches per step (two tiny
+activation-staging kernels and the three GEMVs; gate/up writes gact directly in
+the image format down reads), captured in a CUDA graph (the reference's
+pre-recorded ParityGraph, engine/gcycle.py:22-73).
 """
 from __future__ import annotations
 
@@ -82,14 +84,15 @@ class VerifyStep:
         self.h = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
         self.res = torch.zeros((s.rows, s.dim), dtype=torch.float32, device=dev)
         self.drafts = torch.zeros(s.n_drafts, dtype=torch.int32, device=dev)
-        self.gact = torch.empty((s.rows, s.ffn), dtype=torch.float16, device=dev)
+        # gate/up writes gact straight into the fp16 activation image down reads
+        self.gact = ops.Image(s.rows, s.ffn, dev)
         self.y = torch.empty((s.rows, s.dim), dtype=torch.float32, device=dev)
         self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
         self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
         self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
         self.ws = {
             "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, s.ffn, s.dim, s.rows),
-            "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, s.ffn, s.rows, torch.float16),
+            "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, s.ffn, s.rows, "image"),
             "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, s.vocab, s.dim, s.rows),
         }
         self.graph = None
@@ -109,7 +112,8 @@ class VerifyStep:
                         out_idx=self.out_idx, drafts=self.drafts, accept_out=self.accept_out)
 
     KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
-    LAUNCHES_PER_STEP = 3
+    # stage(X) + gate/up, down, stage(H) + head
+    LAUNCHES_PER_STEP = 5
 
     def launch(self):
         self.launch_ffn_gate_up()
