@@ -1,0 +1,99 @@
+"""The sharded verify step on 2 GPUs (NCCL) against the oracle: FFN rows/k split
+with one all-reduce, vocabulary split with one key all-gather, merge + accept on
+every rank.  Skipped on single-GPU boxes."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import oracle
+    from thunderllamax_b200 import dist as tdist
+    from thunderllamax_b200 import ops, synth
+    from thunderllamax_b200.verify import VerifyShape
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        rng = np.random.default_rng(7)
+        s = VerifyShape(dim=1024, ffn=3072, vocab=7001, rows=11)
+        rg, ru = synth.iq3xxs_blocks(rng, s.ffn, s.dim), synth.iq3xxs_blocks(rng, s.ffn, s.dim)
+        rd, rh = synth.q6k_blocks(rng, s.dim, s.ffn), synth.q6k_blocks(rng, s.vocab, s.dim)
+        xb, hb = synth.bf16_normal(rng, (s.rows, s.dim)), synth.bf16_normal(rng, (s.rows, s.dim))
+        res = rng.standard_normal((s.rows, s.dim), dtype=np.float32)
+        b0, b1 = tdist.block_ranges(s.ffn // 256, world)[rank]
+        f0, f1 = 256 * b0, 256 * b1
+        v0, v1 = tdist.row_ranges(s.vocab, world)[rank]
+        w = {"gate": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(rg, f0, f1), s.dim),
+             "up": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(ru, f0, f1), s.dim),
+             "down": ops.pack_tiles("q6_k", tdist.shard_gguf_cols(rd, f0, f1, 210), f1 - f0),
+             "head": ops.pack_tiles("q6_k", tdist.shard_gguf_rows(rh, v0, v1), s.dim)}
+        step = tdist.ShardedVerifyStep(s, rank, world, weights=w)
+        x64 = synth.bf16_bits_to_f32(xb).astype(np.float64)
+        h64 = synth.bf16_bits_to_f32(hb).astype(np.float64)
+        _, idx_ref, _ = oracle.head_argmax(h64, rh, "q6_k")
+        drafts = idx_ref[:10].copy()
+        drafts[5] = (drafts[5] + 1) % s.vocab
+        step.set_inputs(torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16),
+                        torch.from_numpy(hb.view(np.int16)).cuda().view(torch.bfloat16),
+                        res=torch.from_numpy(res).cuda(), drafts=torch.from_numpy(drafts).cuda())
+        step.capture()
+        for _ in range(3):
+            step.replay()
+        torch.cuda.synchronize()
+        _, y_ref = oracle.ffn_f64(x64, rg, ru, rd, residual=res)
+        y = step.y.cpu().numpy()
+        err = float((np.abs(y - y_ref).max(axis=1) / np.linalg.norm(y_ref, axis=1)).max())
+        out = (rank, err, step.out_idx.cpu().tolist(), idx_ref.tolist(), step.accept_out.cpu().tolist(),
+               list(oracle.accept(idx_ref, drafts)))
+        step.release()
+        q.put(out)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_verify_step_two_gpus():
+    world = 2
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.path.join(here, "golden"),
+                                                os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p_ in procs:
+        p_.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=240))
+    finally:
+        for p_ in procs:
+            p_.join(timeout=60)
+    assert all(p_.exitcode == 0 for p_ in procs)
+    for rank, err, idx, idx_ref, acc, acc_ref in results:
+        assert err <= 2e-3 and err <= 1e-4, (rank, err)
+        assert idx == idx_ref, rank
+        assert acc == acc_ref, rank

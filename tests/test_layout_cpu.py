@@ -71,21 +71,24 @@ def emulate_q6(tiled, n_rows, k):
                 for gam in range(8):
                     W0, W1, W2 = (int(v) for v in w[3 * gam:3 * gam + 3])
                     magic = 0x64006400
-                    p = [(W0 & 0x003F003F) | magic, ((W0 >> 6) & 0x003F003F) | magic,
-                         (W1 & 0x003F003F) | magic, ((W1 >> 6) & 0x003F003F) | magic,
-                         (W2 & 0x003F003F) | magic, ((W2 >> 6) & 0x003F003F) | magic,
-                         ((W0 >> 12) & 0x000F000F) | ((W2 >> 8) & 0x00300030) | magic,
-                         ((W1 >> 12) & 0x000F000F) | ((W2 >> 10) & 0x00300030) | magic]
+                    # every field at mantissa offset 4 (value 1024 + 16q), one fma
+                    # (1024 + 16q) * (sc/16) - 96 sc per formats.cuh q6_group
+                    p = [(W0 & 0x03F003F0) | magic, ((W0 >> 6) & 0x03F003F0) | magic,
+                         (W1 & 0x03F003F0) | magic, ((W1 >> 6) & 0x03F003F0) | magic,
+                         (W2 & 0x03F003F0) | magic, ((W2 >> 6) & 0x03F003F0) | magic,
+                         ((W0 << 4) & 0x00F000F0) | ((W2 << 8) & 0x03000300) | magic,
+                         ((W1 << 4) & 0x00F000F0) | ((W2 << 6) & 0x03000300) | magic]
                     for pi, pv in enumerate(p):
                         mu, r = pi >> 2, pi & 3
                         m = 2 * gam + mu
                         rr = r & 1
                         row = t * 16 + g + 8 * rr
-                        s = sc[(gam >> 1) * 2 + rr]
+                        s = np.float64(sc[(gam >> 1) * 2 + rr])
                         for h in range(2):
                             half = (pv >> (16 * h)) & 0xFFFF
-                            v = np.frombuffer(np.uint16(half).tobytes(), np.float16)[0].astype(np.float32)
-                            a = _f16(_f16(v - 1056.0) * s)
+                            v = np.float64(np.frombuffer(np.uint16(half).tobytes(), np.float16)[0])
+                            # fused multiply-add: exact product and sum, one fp16 rounding
+                            a = _f16(v * (s / 16.0) - 96.0 * s)
                             kk = b * 256 + 64 * q + 4 * m + 2 * (r >> 1) + h
                             W[row, kk] = d16[g, rr] * a
     return W[:n_rows]

@@ -262,14 +262,14 @@ int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, vo
             uint32_t P[8][2];
             for (int h = 0; h < 2; ++h) {
               const int sh = 16 * h;
-              P[0][h] = (W0 >> sh) & 63u;
-              P[1][h] = (W0 >> (sh + 6)) & 63u;
-              P[2][h] = (W1 >> sh) & 63u;
-              P[3][h] = (W1 >> (sh + 6)) & 63u;
-              P[4][h] = (W2 >> sh) & 63u;
-              P[5][h] = (W2 >> (sh + 6)) & 63u;
-              P[6][h] = ((W0 >> (sh + 12)) & 15u) | (((W2 >> (sh + 12)) & 3u) << 4);
-              P[7][h] = ((W1 >> (sh + 12)) & 15u) | (((W2 >> (sh + 14)) & 3u) << 4);
+              P[0][h] = (W0 >> (sh + 4)) & 63u;
+              P[1][h] = (W0 >> (sh + 10)) & 63u;
+              P[2][h] = (W1 >> (sh + 4)) & 63u;
+              P[3][h] = (W1 >> (sh + 10)) & 63u;
+              P[4][h] = (W2 >> (sh + 4)) & 63u;
+              P[5][h] = (W2 >> (sh + 10)) & 63u;
+              P[6][h] = ((W0 >> sh) & 15u) | (((W2 >> sh) & 3u) << 4);
+              P[7][h] = ((W1 >> sh) & 15u) | (((W2 >> (sh + 2)) & 3u) << 4);
             }
             for (int p = 0; p < 8; ++p) {
               const int mu = p >> 2, rsel = p & 3;

@@ -72,6 +72,13 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       : "memory");
 }
 
+// programmatic dependent launch: wait for the preceding grid in the stream to
+// complete (and its memory to be visible); allow the next grid to start launching
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // order this thread's generic-proxy shared accesses before later async-proxy ones
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -95,27 +102,15 @@ __device__ __forceinline__ uint32_t lds32(const void* p) {
   return v;
 }
 
-// ---- fp16x2 on raw registers ----
-__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
+// ---- fp16x2 on raw registers (intrinsics, so the compiler can fold constants) ----
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) { return h2_bits(__hadd2(bits_h2(a), bits_h2(b))); }
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) { return h2_bits(__hmul2(bits_h2(a), bits_h2(b))); }
 __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
+  return h2_bits(__hfma2(bits_h2(a), bits_h2(b), bits_h2(c)));
 }
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
 
 // D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {

@@ -73,13 +73,14 @@ TLX_HD inline void pack_q6_lane(const uint8_t* const rows[16], int lane, uint8_t
       P[p][0] = blk ? q6_value(blk, k) : 32u;
       P[p][1] = blk ? q6_value(blk, k + 1) : 32u;
     }
+    // per half: field A at bits 4-9 (in place), field B at bits 10-15, spare bits 0-3
     uint32_t w[3];
-    w[0] = P[0][0] | (P[1][0] << 6) | ((P[6][0] & 15u) << 12) | (P[0][1] << 16) | (P[1][1] << 22) |
-           ((P[6][1] & 15u) << 28);
-    w[1] = P[2][0] | (P[3][0] << 6) | ((P[7][0] & 15u) << 12) | (P[2][1] << 16) | (P[3][1] << 22) |
-           ((P[7][1] & 15u) << 28);
-    w[2] = P[4][0] | (P[5][0] << 6) | ((P[6][0] >> 4) << 12) | ((P[7][0] >> 4) << 14) | (P[4][1] << 16) |
-           (P[5][1] << 22) | ((P[6][1] >> 4) << 28) | ((P[7][1] >> 4) << 30);
+    w[0] = (P[0][0] << 4) | (P[1][0] << 10) | (P[6][0] & 15u) | (P[0][1] << 20) | (P[1][1] << 26) |
+           ((P[6][1] & 15u) << 16);
+    w[1] = (P[2][0] << 4) | (P[3][0] << 10) | (P[7][0] & 15u) | (P[2][1] << 20) | (P[3][1] << 26) |
+           ((P[7][1] & 15u) << 16);
+    w[2] = (P[4][0] << 4) | (P[5][0] << 10) | (P[6][0] >> 4) | ((P[7][0] >> 4) << 2) | (P[4][1] << 20) |
+           (P[5][1] << 26) | ((P[6][1] >> 4) << 16) | ((P[7][1] >> 4) << 18);
     for (int i3 = 0; i3 < 3; ++i3) {
       const int i = 3 * gam + i3;
       uint8_t* dst = out + ((i >> 2) * 32 + lane) * 16 + (i & 3) * 4;
@@ -121,65 +122,82 @@ TLX_HD inline void pack_iq3_lane(const uint8_t* const rows[16], int lane, uint8_
 
 // ------------------------------------------------------------------------------------
 // Device decoders.  Each works on one chunk in shared memory for the calling lane.
-// A fragments: a[m][0] = row g k+0/1, a[m][1] = row g+8 k+0/1, a[m][2] = row g k+2/3,
-// a[m][3] = row g+8 k+2/3 (k = 64q + 4m).
+// A fragments: a[0] = row g k+0/1, a[1] = row g+8 k+0/1, a[2] = row g k+2/3,
+// a[3] = row g+8 k+2/3 (k = 64q + 4m).
 // ------------------------------------------------------------------------------------
 #ifdef __CUDACC__
 
 constexpr uint32_t kMagic = 0x64006400u;      // fp16x2 (1024, 1024)
-constexpr uint32_t kMinus1056 = 0xE420E420u;  // fp16x2 (-1056, -1056)
-constexpr uint32_t kMinus1152 = 0xE480E480u;  // fp16x2 (-1152, -1152)
+constexpr uint32_t kMinus1056 = 0xE420E420u;  // fp16x2 (-1056, -1056) = -(1024 + 32)
+constexpr uint32_t kMinus1536 = 0xE600E600u;  // fp16x2 (-1536, -1536) = -(1024 + 16 * 32)
+constexpr uint32_t kMinus1152 = 0xE480E480u;  // fp16x2 (-1152, -1152) = -(1024 + 128)
 constexpr uint32_t kMinus1024 = 0xE400E400u;  // fp16x2 (-1024, -1024)
+constexpr uint32_t kSixteenth = 0x2C002C00u;  // fp16x2 (1/16, 1/16)
 
-// Q6_K: per-block lane state
+// Q6_K: per-block lane state.  Every 6-bit field is decoded at mantissa offset 4 of
+// an fp16 half (value 1024 + 16q) and turned into (q - 32) * sc by ONE fma:
+// (1024 + 16q) * (sc/16) - 96 sc.  Both constants are exact in fp16 for every
+// int8 sc (96 sc = 3 * 32 * sc needs <= 9 significand bits, |96 sc| <= 12288),
+// so the result is the single rounding of the exact integer (q - 32) * sc.
 struct Q6Lane {
   uint32_t w[24];
-  uint32_t sc2[4][2];  // fp16x2 (sc, sc) for sub-block 4q+j, row g / g+8
+  uint32_t s16[4][2];  // fp16x2 (sc/16, sc/16) for sub-block 4q+j, row g / g+8
+  uint32_t c96[4][2];  // fp16x2 (-96 sc, -96 sc)
   uint32_t d;          // fp16 d of row g (lo) and row g+8 (hi)
 };
+
+constexpr uint32_t kMinus96 = 0xD600D600u;  // fp16x2 (-96, -96)
 
 __device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& s) {
 #pragma unroll
   for (int p = 0; p < 6; ++p) {
-    const uint4 v = lds128(chunk + (p * 32 + lane) * 16);
+    const uint4 v = *reinterpret_cast<const uint4*>(chunk + (p * 32 + lane) * 16);
     s.w[4 * p + 0] = v.x;
     s.w[4 * p + 1] = v.y;
     s.w[4 * p + 2] = v.z;
     s.w[4 * p + 3] = v.w;
   }
-  const uint2 sc = lds64(chunk + 3072 + lane * 8);
+  const uint2 sc = *reinterpret_cast<const uint2*>(chunk + 3072 + lane * 8);
   // biased byte b = sc + 128 -> fp16 1024 + b -> minus 1152 = sc (exact)
-  s.sc2[0][0] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4040u), kMinus1152);
-  s.sc2[0][1] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4141u), kMinus1152);
-  s.sc2[1][0] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4242u), kMinus1152);
-  s.sc2[1][1] = hadd2_u(prmt(sc.x, 0x64646464u, 0x4343u), kMinus1152);
-  s.sc2[2][0] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4040u), kMinus1152);
-  s.sc2[2][1] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4141u), kMinus1152);
-  s.sc2[3][0] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4242u), kMinus1152);
-  s.sc2[3][1] = hadd2_u(prmt(sc.y, 0x64646464u, 0x4343u), kMinus1152);
-  s.d = lds32(chunk + 3328 + (lane >> 2) * 4);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t word = j < 2 ? sc.x : sc.y;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t bsel = 2u * (j & 1) + r;
+      const uint32_t sc2 = hadd2_u(prmt(word, 0x64646464u, 0x4040u | (bsel << 8) | bsel), kMinus1152);
+      s.s16[j][r] = hmul2_u(sc2, kSixteenth);
+      s.c96[j][r] = hmul2_u(sc2, kMinus96);
+    }
+  }
+  s.d = *reinterpret_cast<const uint32_t*>(chunk + 3328 + (lane >> 2) * 4);
 }
 
-// decode group gam (mmas 2*gam, 2*gam+1)
+// decode group gam (mmas 2*gam, 2*gam+1).  Per half-word the packer stores field A
+// at bits 4-9 (in place), field B at bits 10-15 (moved down by 6) and spare bits
+// 0-3; the split pairs P6/P7 join a low nibble from the spare bits of W0/W1 with
+// two high bits from the spare bits of W2.
 __device__ __forceinline__ void q6_group(const Q6Lane& s, int gam, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
   const uint32_t W0 = s.w[3 * gam], W1 = s.w[3 * gam + 1], W2 = s.w[3 * gam + 2];
-  const uint32_t sg = s.sc2[gam >> 1][0], sg8 = s.sc2[gam >> 1][1];
-  uint32_t p0 = (W0 & 0x003F003Fu) | kMagic;
-  uint32_t p1 = ((W0 >> 6) & 0x003F003Fu) | kMagic;
-  uint32_t p2 = (W1 & 0x003F003Fu) | kMagic;
-  uint32_t p3 = ((W1 >> 6) & 0x003F003Fu) | kMagic;
-  uint32_t p4 = (W2 & 0x003F003Fu) | kMagic;
-  uint32_t p5 = ((W2 >> 6) & 0x003F003Fu) | kMagic;
-  uint32_t p6 = ((W0 >> 12) & 0x000F000Fu) | ((W2 >> 8) & 0x00300030u) | kMagic;
-  uint32_t p7 = ((W1 >> 12) & 0x000F000Fu) | ((W2 >> 10) & 0x00300030u) | kMagic;
-  a0[0] = hmul2_u(hadd2_u(p0, kMinus1056), sg);
-  a0[1] = hmul2_u(hadd2_u(p1, kMinus1056), sg8);
-  a0[2] = hmul2_u(hadd2_u(p2, kMinus1056), sg);
-  a0[3] = hmul2_u(hadd2_u(p3, kMinus1056), sg8);
-  a1[0] = hmul2_u(hadd2_u(p4, kMinus1056), sg);
-  a1[1] = hmul2_u(hadd2_u(p5, kMinus1056), sg8);
-  a1[2] = hmul2_u(hadd2_u(p6, kMinus1056), sg);
-  a1[3] = hmul2_u(hadd2_u(p7, kMinus1056), sg8);
+  const int j = gam >> 1;
+  const uint32_t sg = s.s16[j][0], sg8 = s.s16[j][1];
+  const uint32_t cg = s.c96[j][0], cg8 = s.c96[j][1];
+  const uint32_t p0 = (W0 & 0x03F003F0u) | kMagic;
+  const uint32_t p1 = ((W0 >> 6) & 0x03F003F0u) | kMagic;
+  const uint32_t p2 = (W1 & 0x03F003F0u) | kMagic;
+  const uint32_t p3 = ((W1 >> 6) & 0x03F003F0u) | kMagic;
+  const uint32_t p4 = (W2 & 0x03F003F0u) | kMagic;
+  const uint32_t p5 = ((W2 >> 6) & 0x03F003F0u) | kMagic;
+  const uint32_t p6 = ((W0 << 4) & 0x00F000F0u) | (((W2 << 8) & 0x03000300u) | kMagic);
+  const uint32_t p7 = ((W1 << 4) & 0x00F000F0u) | (((W2 << 6) & 0x03000300u) | kMagic);
+  a0[0] = hfma2_u(p0, sg, cg);
+  a0[1] = hfma2_u(p1, sg8, cg8);
+  a0[2] = hfma2_u(p2, sg, cg);
+  a0[3] = hfma2_u(p3, sg8, cg8);
+  a1[0] = hfma2_u(p4, sg, cg);
+  a1[1] = hfma2_u(p5, sg8, cg8);
+  a1[2] = hfma2_u(p6, sg, cg);
+  a1[3] = hfma2_u(p7, sg8, cg8);
 }
 
 __device__ __forceinline__ float2 q6_block_scale(const Q6Lane& s) {
@@ -187,20 +205,32 @@ __device__ __forceinline__ float2 q6_block_scale(const Q6Lane& s) {
   return __half22float2(h);  // (row g, row g+8)
 }
 
+// IQ3_XXS grid table in shared memory: entry e holds its 4 magnitudes as two fp16x2
+// (exact small integers), replicated kGridCopies times so lane l reads copy l % 16
+// (one LDS.64 per grid entry, two wavefronts per warp, no bank conflicts)
+constexpr int kGridCopies = 16;
+constexpr uint32_t kGridTableBytes = 256u * kGridCopies * 8u;
+
+__device__ __forceinline__ uint2 grid_pair_entry(uint32_t g) {
+  uint2 e;
+  e.x = hadd2_u(prmt(g, 0x64646464u, 0x4140u), kMinus1024);
+  e.y = hadd2_u(prmt(g, 0x64646464u, 0x4342u), kMinus1024);
+  return e;
+}
+
 // IQ3_XXS: per-block lane state
 struct Iq3Lane {
   uint4 qs0, qs1;      // grid indices: row g / row g+8, groups 2q (bytes 0..7) and 2q+1 (8..15)
   uint32_t sw[2][2];   // scale/sign words [row][group]
   uint32_t m2[2][2];   // fp16x2 (2s+1)
-  uint32_t c2[2][2];   // fp16x2 -1024*(2s+1)
   uint32_t par[2][2];  // parity of sign field l at bit 7l
   uint32_t d;
 };
 
 __device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane& s) {
-  s.qs0 = lds128(chunk + lane * 16);
-  s.qs1 = lds128(chunk + 512 + lane * 16);
-  const uint4 sw = lds128(chunk + 1024 + lane * 16);
+  s.qs0 = *reinterpret_cast<const uint4*>(chunk + lane * 16);
+  s.qs1 = *reinterpret_cast<const uint4*>(chunk + 512 + lane * 16);
+  const uint4 sw = *reinterpret_cast<const uint4*>(chunk + 1024 + lane * 16);
   s.sw[0][0] = sw.x;
   s.sw[0][1] = sw.y;
   s.sw[1][0] = sw.z;
@@ -210,16 +240,14 @@ __device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const uint32_t v = s.sw[r][c];
-      const uint32_t mm = ((v >> 28) << 1) | 1u;                    // 2s+1
-      const uint32_t m2 = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
-      s.m2[r][c] = m2;
-      s.c2[r][c] = hmul2_u(m2, kMinus1024);
+      const uint32_t mm = ((v >> 28) << 1) | 1u;  // 2s+1
+      s.m2[r][c] = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
       uint32_t t = v ^ (v >> 1);
       t ^= t >> 2;
-      t ^= t >> 4;                                                 // bit i = xor of bits i..i+7
-      s.par[r][c] = t ^ (v >> 7);                                  // bit 7l = parity of field l
+      t ^= t >> 4;                 // bit i = xor of bits i..i+7
+      s.par[r][c] = t ^ (v >> 7);  // bit 7l = parity of field l
     }
-  s.d = lds32(chunk + 1536 + (lane >> 2) * 4);
+  s.d = *reinterpret_cast<const uint32_t*>(chunk + 1536 + (lane >> 2) * 4);
 }
 
 // sign masks for sign pair i (s8 bits 2i, 2i+1) -> fp16x2 sign bits 15 / 31
@@ -228,22 +256,19 @@ __device__ __forceinline__ uint32_t sign_mask(uint32_t s8, int i) {
   return (s8 * mul) & 0x80008000u;
 }
 
-// decode mma m (0..15) for both rows
-__device__ __forceinline__ void iq3_mma(const Iq3Lane& s, const uint32_t* grid_rep, int lane, int m,
-                                        uint32_t (&a)[4]) {
+// decode mma m (0..15) for both rows; grid_lane = table base + (lane % 16) * 8 bytes
+__device__ __forceinline__ void iq3_mma(const Iq3Lane& s, const uint8_t* grid_lane, int m, uint32_t (&a)[4]) {
   const int c = m >> 3, l = (m >> 1) & 3, e = m & 1;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const uint4 qs = r == 0 ? s.qs0 : s.qs1;
     const uint32_t word = (m >> 2) == 0 ? qs.x : (m >> 2) == 1 ? qs.y : (m >> 2) == 2 ? qs.z : qs.w;
     const uint32_t idx = (word >> (8 * (m & 3))) & 0xFFu;
-    const uint32_t G = grid_rep[idx * 32 + lane];
+    const uint2 G = *reinterpret_cast<const uint2*>(grid_lane + idx * (kGridCopies * 8u));
     const uint32_t v = s.sw[r][c];
-    const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | (((s.par[r][c] >> (7 * l)) & 1u) << 7);
-    const uint32_t lo = hfma2_u(prmt(G, 0x64646464u, 0x4140u), s.m2[r][c], s.c2[r][c]);
-    const uint32_t hi = hfma2_u(prmt(G, 0x64646464u, 0x4342u), s.m2[r][c], s.c2[r][c]);
-    a[r] = lo ^ sign_mask(s8, 2 * e);
-    a[r + 2] = hi ^ sign_mask(s8, 2 * e + 1);
+    const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | ((s.par[r][c] >> (7 * l)) << 7 & 0x80u);
+    a[r] = hmul2_u(G.x, s.m2[r][c]) ^ sign_mask(s8, 2 * e);
+    a[r + 2] = hmul2_u(G.y, s.m2[r][c]) ^ sign_mask(s8, 2 * e + 1);
   }
 }
 

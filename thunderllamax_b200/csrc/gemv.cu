@@ -37,11 +37,14 @@ namespace tlx {
 
 enum Epi : int { EPI_STORE = 0, EPI_GATEUP = 1, EPI_ARGMAX = 2 };
 
+constexpr int kImageRow = 68;                           // uint2 entries per (block, column) row
+constexpr uint32_t kImageRowBytes = kImageRow * 8u;     // 544
+
 struct GemvParams {
   const uint8_t* w0;
   const uint8_t* w1;
   const uint32_t* grid;
-  const uint2* ximg;  // fp16 activation image [NB][16 mma][MC cols][4 quarters] of 4 halves
+  const uint2* ximg;  // fp16 activation image, see image_index
   int M;
   int MC;
   int CG;  // columns per token (1, or 3 for fp32 activations split into fp16 parts)
@@ -62,7 +65,7 @@ struct GemvParams {
   int32_t* accept_out;
   float* partials;
   uint32_t* tile_cnt;
-  uint64_t* cta_best;
+  unsigned long long* gkey;  // [16] running per-token argmax keys (zero between launches)
   uint32_t* done_cnt;
   uint32_t* err;
 };
@@ -79,11 +82,10 @@ __host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int
   SmemLayout L;
   uint32_t off = 0;
   L.xs = off;
-  off += static_cast<uint32_t>(Bs) * 16u * static_cast<uint32_t>(MC) * 32u;
-  off += 512u;  // slack: the unused token columns of the last mma read past the image
+  off += static_cast<uint32_t>(Bs) * static_cast<uint32_t>(MC) * kImageRowBytes;
   off = (off + 127u) & ~127u;
   L.grid = off;
-  if (qt == QT_IQ3_XXS) off += 256u * 32u * 4u;
+  if (qt == QT_IQ3_XXS) off += kGridTableBytes;
   L.ring = off;
   off += static_cast<uint32_t>(wpc) * stages * chunk_bytes(qt) * nmat;
   off = (off + 15u) & ~15u;
@@ -102,16 +104,22 @@ __device__ __forceinline__ int warp_of(int64_t f, int64_t Fs, int Ws) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// image index (uint2 units) of the 4-halves entry holding x[t][k..k+3], k % 4 == 0
+// Activation image: per 256-weight block b and column (token) c one row of 64
+// entries [mma m][quarter q] (4 halves each, x[c][256b + 64q + 4m + 0..3]) padded to
+// 68 entries, so lane (g, q) of an mma reads row g at entry 4m + q: every mma's
+// offset is a compile-time immediate and the 32 lanes hit 32 distinct banks pairs.
+// Index (uint2 units) of the entry holding x[c][k..k+3], k % 4 == 0:
 __host__ __device__ __forceinline__ int64_t image_index(int64_t k, int col, int MC) {
   const int64_t b = k >> 8;
   const int kin = static_cast<int>(k & 255), q = kin >> 6, m = (kin & 63) >> 2;
-  return ((b * 16 + m) * MC + col) * 4 + q;
+  return (b * MC + col) * kImageRow + m * 4 + q;
 }
 
 // ---- activation staging: x[M][K] (f32 / f16 / bf16) -> fp16 image ----
 __global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_t ldx, int M, int CG, int MC, int64_t K,
                                    uint2* __restrict__ img) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t per_tok = K >> 2;
   const int64_t total = static_cast<int64_t>(M) * per_tok;
   for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < total;
@@ -150,11 +158,11 @@ __global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_
 }
 
 // one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B).
-// xb: this lane's B entries of the block (token g, quarter q); mma m at xb[m*mstride],
-// token g+8 at +32 (columns >= MC read garbage that only feeds unused columns)
+// xb0 / xb1: this lane's image rows (tokens g and g+8, clamped to valid columns;
+// clamped columns only feed accumulator columns that are never read) of the block
 template <int QT, int NT, int NMAT>
-__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xb, int mstride,
-                                              const uint32_t* grid_rep, int lane, float (&acc)[NMAT][NT][4]) {
+__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xb0, const uint2* xb1,
+                                              const uint8_t* grid_lane, int lane, float (&acc)[NMAT][NT][4]) {
   float tmp[NMAT][NT][4];
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
@@ -164,11 +172,13 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       for (int i = 0; i < 4; ++i) tmp[a][nt][i] = 0.f;
   float2 scale[NMAT];
   auto load_b = [&](int m, uint32_t (&b)[NT][2]) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 v = lds64(xb + m * mstride + nt * 32);
-      b[nt][0] = v.x;
-      b[nt][1] = v.y;
+    const uint2 v0 = xb0[m * 4];
+    b[0][0] = v0.x;
+    b[0][1] = v0.y;
+    if constexpr (NT == 2) {
+      const uint2 v1 = xb1[m * 4];
+      b[1][0] = v1.x;
+      b[1][1] = v1.y;
     }
   };
   if constexpr (QT == QT_Q6_K) {
@@ -204,7 +214,7 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
 #pragma unroll
       for (int a = 0; a < NMAT; ++a) {
         uint32_t af[4];
-        iq3_mma(s[a], grid_rep, lane, m, af);
+        iq3_mma(s[a], grid_lane, m, af);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], af, b[nt][0], b[nt][1]);
       }
@@ -325,28 +335,22 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   const int64_t t_first = f0 / p.Bs;
   const int bb_first = static_cast<int>(f0 - t_first * p.Bs);
 
-  // activations of this k-segment: one bulk copy of the image slice
-  const uint32_t xbytes = static_cast<uint32_t>(p.Bs) * 16u * static_cast<uint32_t>(p.MC) * 32u;
-  if (threadIdx.x == 0) {
-    mbar_init(xbar, 1);
-    mbar_fence_init();
-    mbar_arrive_expect_tx(xbar, xbytes);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg) + static_cast<size_t>(seg) * xbytes;
-    for (uint32_t off = 0; off < xbytes; off += 32768u)
-      bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
-  }
 
-  // weight ring: issue cursor (it, ibb) walks the same items as the compute cursor
-  int64_t it = t_first;
+  // weight ring: the issue cursor walks the same items as the compute cursor; items
+  // of one tile are consecutive chunks, the next tile of the segment starts
+  // (NB - Bs + 1) chunks after the last one
   int ibb = bb_first;
+  size_t woff = (static_cast<size_t>(t_first) * p.NB + static_cast<size_t>(seg) * p.Bs + bb_first) * CH;
+  const size_t tile_jump = static_cast<size_t>(p.NB - p.Bs + 1) * CH;
   auto issue = [&](int st) {
-    const int64_t off = (it * p.NB + seg * p.Bs + ibb) * static_cast<int64_t>(CH);
     mbar_arrive_expect_tx(&bars[st], STAGE_BYTES);
-    bulk_g2s(ring + st * STAGE_BYTES, p.w0 + off, CH, &bars[st]);
-    if constexpr (NMAT == 2) bulk_g2s(ring + st * STAGE_BYTES + CH, p.w1 + off, CH, &bars[st]);
+    bulk_g2s(ring + st * STAGE_BYTES, p.w0 + woff, CH, &bars[st]);
+    if constexpr (NMAT == 2) bulk_g2s(ring + st * STAGE_BYTES + CH, p.w1 + woff, CH, &bars[st]);
     if (++ibb == p.Bs) {
       ibb = 0;
-      ++it;
+      woff += tile_jump;
+    } else {
+      woff += CH;
     }
   };
   if (lane == 0) {
@@ -358,7 +362,31 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   __syncwarp();
 
   if constexpr (QT == QT_IQ3_XXS) {
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) grid_rep[i] = __ldg(p.grid + (i >> 5));
+    // one global load per entry, then kGridCopies shared copies of its fp16 pairs
+    uint2* tab = reinterpret_cast<uint2*>(grid_rep);
+    if (threadIdx.x < 256) {
+      const uint2 e = grid_pair_entry(__ldg(p.grid + threadIdx.x));
+#pragma unroll
+      for (int c = 0; c < kGridCopies; ++c) tab[threadIdx.x * kGridCopies + c] = e;
+    }
+  }
+
+  // Everything above touches only weights and constants.  With programmatic
+  // dependent launch it overlaps the previous kernel's tail; from here on the
+  // activations, outputs and workspace of the previous kernel in the stream are
+  // read or written, so wait for it to complete.
+  griddep_wait();
+  griddep_launch_dependents();
+
+  // activations of this k-segment: one bulk copy of the image slice
+  const uint32_t xbytes = static_cast<uint32_t>(p.Bs) * static_cast<uint32_t>(p.MC) * kImageRowBytes;
+  if (threadIdx.x == 0) {
+    mbar_init(xbar, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(xbar, xbytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg) + static_cast<size_t>(seg) * xbytes;
+    for (uint32_t off = 0; off < xbytes; off += 32768u)
+      bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
   }
   __syncthreads();
   bool failed = !mbar_wait_bounded(xbar, 0, threadIdx.x == 0 ? p.err : nullptr);
@@ -373,8 +401,13 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   uint64_t best = 0ull;
   int64_t i_fail = failed ? 0 : n_items;
 
-  const int mstride = p.MC * 4;                                    // uint2 entries per mma row of the image
-  const uint2* xlane = xs + (lane >> 2) * 4 + (lane & 3);          // token g, quarter q
+  // this lane's image rows: tokens g and g+8, clamped to the last valid column
+  const int tok0 = (lane >> 2) < p.MC ? (lane >> 2) : p.MC - 1;
+  const int tok1 = (lane >> 2) + 8 < p.MC ? (lane >> 2) + 8 : p.MC - 1;
+  const uint2* xlane0 = xs + tok0 * kImageRow + (lane & 3);
+  const uint2* xlane1 = xs + tok1 * kImageRow + (lane & 3);
+  const int block_stride = p.MC * kImageRow;
+  const uint8_t* grid_lane = reinterpret_cast<const uint8_t*>(grid_rep) + (lane % kGridCopies) * 8;
   int64_t t = t_first;
   int bb = bb_first;
   int piece_bb0 = bb_first;                                        // first block of the current piece
@@ -390,7 +423,8 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
     const uint8_t* chunk[NMAT];
 #pragma unroll
     for (int a = 0; a < NMAT; ++a) chunk[a] = stage + a * CH;
-    compute_block<QT, NT, NMAT>(chunk, xlane + bb * 16 * mstride, mstride, grid_rep, lane, acc);
+    compute_block<QT, NT, NMAT>(chunk, xlane0 + bb * block_stride, xlane1 + bb * block_stride, grid_lane, lane,
+                                acc);
     __syncwarp();
 
     const bool run_end = (bb == p.Bs - 1) || (i == n_items - 1);
@@ -429,25 +463,37 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
               for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
-          for (int s = 0; s < p.S; ++s)
-            for (int j = 0; j < pieces; ++j) {
-              if (s == seg && j == my_j) {
+          // pieces in fixed k order (segment s, piece j); slot loads are issued in
+          // batches of 4 ahead of the in-order adds
+          constexpr int VN = NMAT * NT * 4;
+          const int n_slots = p.S * pieces;
+          const int my_slot_idx = seg * pieces + my_j;
+          for (int base = 0; base < n_slots; base += 4) {
+            float buf[4][VN];
 #pragma unroll
-                for (int a = 0; a < NMAT; ++a)
+            for (int u = 0; u < 4; ++u) {
+              const int sj = base + u;
+              if (sj < n_slots && sj != my_slot_idx) {
+                const int ss = sj / pieces, jj = sj - ss * pieces;
+                const float* sl = p.partials + ((t * p.S + ss) * p.J + jj) * slot_stride + lane;
 #pragma unroll
-                  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) v[a][nt][e] += acc[a][nt][e];
-              } else {
-                const float* sl = p.partials + ((t * p.S + s) * p.J + j) * slot_stride;
-#pragma unroll
-                for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-                  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) v[a][nt][e] += __ldcg(sl + ((a * NT + nt) * 4 + e) * 32 + lane);
+                for (int e = 0; e < VN; ++e) buf[u][e] = __ldcg(sl + e * 32);
               }
             }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int sj = base + u;
+              if (sj < n_slots) {
+#pragma unroll
+                for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                      v[a][nt][e] += sj == my_slot_idx ? acc[a][nt][e] : buf[u][(a * NT + nt) * 4 + e];
+              }
+            }
+          }
           tile_epilogue<NT, NMAT, EPI>(p, t, v, epi, lane, best);
           if (lane == 0) p.tile_cnt[t] = 0u;
         }
@@ -477,18 +523,20 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   }
 
   if constexpr (EPI == EPI_ARGMAX) {
+    // per-token keys: lanes -> warp -> CTA (shared) -> all CTAs (atomicMax on the
+    // global keys; max is order-independent, so the result is deterministic)
     const uint64_t other = __shfl_xor_sync(0xffffffffu, best, 16);
     best = other > best ? other : best;
     if (lane < 16) wbest[warp * 16 + lane] = best;
     __syncthreads();
     uint32_t* flag = reinterpret_cast<uint32_t*>(wbest + WPC * 16);
-    if (threadIdx.x < 16) {
+    if (threadIdx.x < p.M) {
       uint64_t b = 0ull;
       for (int w = 0; w < WPC; ++w) {
         const uint64_t c = wbest[w * 16 + threadIdx.x];
         b = c > b ? c : b;
       }
-      p.cta_best[blockIdx.x * 16 + threadIdx.x] = b;
+      if (b) atomicMax(p.gkey + threadIdx.x, static_cast<unsigned long long>(b));
       __threadfence();
     }
     __syncthreads();
@@ -498,14 +546,11 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
     }
     __syncthreads();
     if (flag[0]) {
+      // the last CTA: every other CTA's atomicMax happened before its arrival
       __threadfence();
       int32_t* idx_s = reinterpret_cast<int32_t*>(flag + 2);
       if (threadIdx.x < p.M) {
-        uint64_t b = 0ull;
-        for (int c = 0; c < gridDim.x; ++c) {
-          const uint64_t k = __ldcg(p.cta_best + c * 16 + threadIdx.x);
-          b = k > b ? k : b;
-        }
+        const uint64_t b = atomicExch(p.gkey + threadIdx.x, 0ull);  // read and re-arm for the next launch
         if (p.out_max) p.out_max[threadIdx.x] = key_value(b);
         if (p.out_idx) p.out_idx[threadIdx.x] = key_index(b);
         if (p.out_keys) p.out_keys[threadIdx.x] = b;
@@ -558,7 +603,7 @@ static int smem_optin() {
   return n;
 }
 
-static constexpr uint32_t kXsBudget = 120u * 1024u;
+static constexpr uint32_t kXsBudget = 124u * 1024u;
 
 // warps per CTA and ring depth per (format, epilogue), sized so the verify-step
 // shapes (k = 5120 with 11 rows; k = 17408 in 4 segments) fit the 227 KB
@@ -611,7 +656,7 @@ static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dt
   const uint32_t smem_limit = static_cast<uint32_t>(smem_optin());
   for (int s = 1; s <= P.NB; ++s) {
     if (P.NB % s) continue;
-    const uint32_t xs = static_cast<uint32_t>(P.NB / s) * 16u * P.MC * 32u;
+    const uint32_t xs = static_cast<uint32_t>(P.NB / s) * P.MC * kImageRowBytes;
     const SmemLayout Ls = smem_layout(qt, P.nmat, P.wpc, P.stages, P.NB / s, P.MC);
     if (xs <= kXsBudget && Ls.total <= smem_limit) {
       P.S = s;
@@ -634,10 +679,9 @@ static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dt
   size_t off = 256;
   P.off_cnt = off;
   off += (static_cast<size_t>(P.T) * 4 + 255) & ~size_t(255);
-  P.off_best = off;
-  off += (static_cast<size_t>(P.C) * 16 * 8 + 255) & ~size_t(255);
+  P.off_best = off;  // end of the region that must be zero before a launch
   P.off_img = off;
-  if (x_dtype != DT_IMAGE) off += (static_cast<size_t>(P.NB) * 16 * P.MC * 32 + 255) & ~size_t(255);
+  if (x_dtype != DT_IMAGE) off += (static_cast<size_t>(P.NB) * P.MC * kImageRowBytes + 255) & ~size_t(255);
   P.off_part = off;
   off += static_cast<size_t>(P.T) * P.S * P.J * P.nmat * P.NT * 4 * 32 * sizeof(float);
   P.ws_bytes = off;
@@ -654,8 +698,7 @@ static int launch_t(const Plan& P, const GemvParams& gp, cudaStream_t stream) {
     if (e != cudaSuccess) return TLX_ERR_LAUNCH;
     configured = P.smem;
   }
-  kern<<<P.C, WPC * 32, P.smem, stream>>>(gp);
-  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+  return launch_pdl(kern, dim3(P.C), dim3(WPC * 32), P.smem, stream, gp);
 }
 
 template <int EPI>
@@ -664,13 +707,31 @@ static int dispatch(int qt, const Plan& P, const GemvParams& gp, cudaStream_t s)
   return P.NT == 1 ? launch_t<QT_IQ3_XXS, 1, EPI>(P, gp, s) : launch_t<QT_IQ3_XXS, 2, EPI>(P, gp, s);
 }
 
+// launch with programmatic stream serialization: the kernel may start while the
+// previous kernel in the stream drains; it waits (griddepcontrol.wait) before
+// touching anything that kernel produces
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 size_t activation_image_bytes(int m, int64_t k, int x_dtype) {
   if (m < 1 || k <= 0 || k % kQK) return 0;
   const int mc = m * cols_per_token(x_dtype);
   if (mc > 16) return 0;
-  return static_cast<size_t>(k / kQK) * 16 * mc * 32;
+  return static_cast<size_t>(k / kQK) * mc * kImageRowBytes;
 }
 
 int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream) {
@@ -682,8 +743,8 @@ int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k,
   const int cg = cols_per_token(x_dtype);
   const int64_t groups = static_cast<int64_t>(m) * (k / 4);
   const int blocks = static_cast<int>(std::min<int64_t>((groups + 255) / 256, 4096));
-  stage_image_kernel<<<blocks, 256, 0, stream>>>(x, x_dtype, ldx, m, cg, m * cg, k, static_cast<uint2*>(image));
-  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+  return launch_pdl(stage_image_kernel, dim3(blocks), dim3(256), 0, stream, x, x_dtype, ldx, m, cg, m * cg, k,
+                    static_cast<uint2*>(image));
 }
 
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
@@ -754,7 +815,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   gp.err = reinterpret_cast<uint32_t*>(wsb);
   gp.done_cnt = reinterpret_cast<uint32_t*>(wsb + 4);
   gp.tile_cnt = reinterpret_cast<uint32_t*>(wsb + P.off_cnt);
-  gp.cta_best = reinterpret_cast<uint64_t*>(wsb + P.off_best);
+  gp.gkey = reinterpret_cast<unsigned long long*>(wsb + 8);
   gp.partials = reinterpret_cast<float*>(wsb + P.off_part);
   if (epi == EPI_STORE) return dispatch<EPI_STORE>(qt, P, gp, stream);
   if (epi == EPI_GATEUP) return dispatch<EPI_GATEUP>(qt, P, gp, stream);

@@ -1,0 +1,180 @@
+"""The verify step sharded across the GPUs of one node (one process per GPU).
+
+The reference is single-GPU (README.md:412-413); this is the B200 node layout:
+
+* FFN gate/up: output rows split by whole 256-row blocks (the gact image a
+  rank produces is exactly the k range of down it consumes).
+* FFN down: split by k (columns) to match; every rank produces a partial
+  11 x 5120 fp32 sum, added by ONE NCCL all-reduce.  Rank 0 adds the residual.
+* LM head: split by vocabulary; each rank's fused head emits 11 packed
+  (max, index) keys with global row ids, ONE NCCL all-gather collects the
+  [world][11] keys and every rank merges them and runs greedy accept
+  (deterministic, identical on all ranks).
+
+Collectives go through ``torch.distributed`` (NCCL on GPUs; gloo in the CPU
+tests of the host-side plumbing) and are captured in the step's CUDA graph.
+No data path uses TMA multicast or peer memory.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .verify import VerifyShape, synth_tiled
+
+
+def block_ranges(n_blocks: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous, near-equal split of n_blocks 256-row blocks over ranks."""
+    return [((n_blocks * r) // world, (n_blocks * (r + 1)) // world) for r in range(world)]
+
+
+def row_ranges(n_rows: int, world: int, quantum: int = 16) -> list[tuple[int, int]]:
+    """Contiguous split of n_rows in multiples of `quantum` rows (the last rank
+    takes the remainder)."""
+    units = (n_rows + quantum - 1) // quantum
+    out = []
+    for r in range(world):
+        u0, u1 = (units * r) // world, (units * (r + 1)) // world
+        out.append((min(u0 * quantum, n_rows), min(u1 * quantum, n_rows)))
+    return out
+
+
+def allreduce_partial(y: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum the per-rank partial down-projection outputs in place."""
+    dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
+
+
+def gather_keys(local_keys: torch.Tensor, all_keys: torch.Tensor, group=None) -> torch.Tensor:
+    """[m] int64 keys of this rank -> [world, m] keys of every rank."""
+    dist.all_gather_into_tensor(all_keys.view(-1), local_keys, group=group)  # concatenated form (NCCL and gloo)
+    return all_keys
+
+
+class ShardedVerifyStep:
+    """VerifyStep over `world` GPUs; this object is rank `rank`'s share."""
+
+    LAUNCHES_PER_STEP = 5 + 1  # stage/gate-up, down, stage/head, merge (+ 2 NCCL collectives)
+    KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
+
+    def __init__(self, shape: VerifyShape, rank: int, world: int, seed: int = 0, weights: dict | None = None,
+                 group=None):
+        ops.require_device()
+        self.shape = s = shape
+        self.rank, self.world, self.group = rank, world, group
+        nb_ffn = s.ffn // 256
+        b0, b1 = block_ranges(nb_ffn, world)[rank]
+        self.f0, self.f1 = 256 * b0, 256 * b1          # this rank's FFN rows / down k range
+        self.v0, self.v1 = row_ranges(s.vocab, world)[rank]
+        self.n_ffn = self.f1 - self.f0
+        self.n_voc = self.v1 - self.v0
+        if self.n_ffn <= 0 or self.n_voc <= 0:
+            raise ValueError(f"rank {rank} of {world} has an empty shard")
+        if weights is None:
+            # synthetic shards: each rank draws its own seeded blocks of its shard shape
+            weights = {"gate": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 1),
+                       "up": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 2),
+                       "down": synth_tiled(s.down_q, s.dim, self.n_ffn, seed * 1000 + 10 * rank + 3),
+                       "head": synth_tiled(s.head_q, self.n_voc, s.dim, seed * 1000 + 10 * rank + 4)}
+        self.w = weights
+        dev = "cuda"
+        self.x = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self.h = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self.res = torch.zeros((s.rows, s.dim), dtype=torch.float32, device=dev)
+        self.drafts = torch.zeros(s.n_drafts, dtype=torch.int32, device=dev)
+        self.gact = ops.Image(s.rows, self.n_ffn, dev)
+        self.y = torch.empty((s.rows, s.dim), dtype=torch.float32, device=dev)
+        self.local_keys = torch.zeros(s.rows, dtype=torch.int64, device=dev)
+        self.all_keys = torch.zeros((world, s.rows), dtype=torch.int64, device=dev)
+        self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
+        self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
+        self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
+        self.ws = {
+            "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, self.n_ffn, s.dim, s.rows),
+            "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, self.n_ffn, s.rows, "image"),
+            "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, self.n_voc, s.dim, s.rows),
+        }
+        self.graph = None
+
+    def algorithmic_bytes_per_rank(self) -> dict:
+        s = self.shape
+        from .synth import row_bytes
+
+        r, d = s.rows, s.dim
+        return {"ffn_gate_up": 2 * self.n_ffn * row_bytes(s.ffn_q, d) + r * d * 2 + r * self.n_ffn * 2,
+                "ffn_down": d * row_bytes(s.down_q, self.n_ffn) + r * self.n_ffn * 2 + r * d * 4 * 2,
+                "head_argmax": self.n_voc * row_bytes(s.head_q, d) + r * d * 2 + r * 8}
+
+    def launch_ffn_gate_up(self):
+        s = self.shape
+        ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, self.n_ffn, self.ws["ffn_gate_up"],
+                        gact=self.gact)
+
+    def launch_ffn_down(self):
+        s = self.shape
+        res = self.res if self.rank == 0 else None
+        ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, self.ws["ffn_down"], y=self.y, residual=res)
+
+    def launch_head_argmax(self):
+        s = self.shape
+        ops.head_argmax(s.head_q, self.w["head"], self.h, self.n_voc, self.ws["head_argmax"],
+                        row_offset=self.v0, out_keys=self.local_keys)
+
+    def launch(self):
+        self.launch_ffn_gate_up()
+        self.launch_ffn_down()
+        allreduce_partial(self.y, self.group)
+        self.launch_head_argmax()
+        gather_keys(self.local_keys, self.all_keys, self.group)
+        ops.argmax_merge(self.all_keys, out_max=self.out_max, out_idx=self.out_idx, drafts=self.drafts,
+                         accept_out=self.accept_out)
+
+    def capture(self):
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                self.launch()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.launch()
+        self.graph = g
+        return g
+
+    def replay(self):
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+
+    def release(self):
+        """Drop the captured graph (it holds NCCL work) before the process group goes."""
+        self.graph = None
+        torch.cuda.synchronize()
+
+    def set_inputs(self, x, h, res=None, drafts=None):
+        self.x.copy_(x, non_blocking=True)
+        self.h.copy_(h, non_blocking=True)
+        if res is not None:
+            self.res.copy_(res, non_blocking=True)
+        if drafts is not None:
+            self.drafts.copy_(drafts, non_blocking=True)
+
+    def step_host(self, x_pinned, h_pinned, drafts_pinned, out_pinned):
+        self.set_inputs(x_pinned, h_pinned, drafts=drafts_pinned)
+        self.replay()
+        out_pinned[:2].copy_(self.accept_out, non_blocking=True)
+        out_pinned[2:].copy_(self.out_idx, non_blocking=True)
+
+
+def shard_gguf_rows(raw: np.ndarray, r0: int, r1: int) -> np.ndarray:
+    """Rows [r0, r1) of a GGUF matrix (row split: gate/up/head)."""
+    return np.ascontiguousarray(raw[r0:r1])
+
+
+def shard_gguf_cols(raw: np.ndarray, k0: int, k1: int, block_bytes: int) -> np.ndarray:
+    """Columns [k0, k1) (multiples of 256) of a GGUF matrix (k split: down)."""
+    return np.ascontiguousarray(raw[:, (k0 // 256) * block_bytes:(k1 // 256) * block_bytes])
