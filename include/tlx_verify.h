@@ -182,6 +182,41 @@ int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, i
                   const float* hd_d0, const float* hd_d1, float* dhd_seed, int32_t* emit, const int32_t* l_hist,
                   int dim, void* stream);
 
+/* ---- MoE verify layer (P <= 8 positions, top-8 of E <= 1024 experts + shared) ----
+ * Router: logits = w_router[E][hidden] (fp32) . h[p] (bf16), top-8 by 8 masked-argmax
+ * passes (strict '>', ties to the lower expert id), gates = exp(l - max) / sum over
+ * the 8, sg = sigmoid(w_shared_gate . h[p]); ids / gates are [p][8] rank-major.
+ * Replaces rt8e256 (engine/mm/MM_P1_rt8e256.cu:14-62).
+ * Experts: IQ4_XS weights in the tile layout (tlx_pack_tiles, qtype 23), one expert
+ * after another: gate / up [E][inner x hidden], down [E][hidden x inner]; the
+ * shared expert has the same shapes (NULL shared_gate: no shared expert).
+ * act = silu(gate h) * (up h), part = down act (fp32), and
+ * y[p] = hres[p] + sum_r gates[p][r] part[p][r] + sg[p] shared[p] in that order.
+ * Replaces shexp8 / gx8e256up4 / gx8e256dn / cmbz2048 (engine/mm/MM_P2_shexp8.cu:8,
+ * engine/mm/MM_P2_gx8e256up4.cu:8-55, engine/mm/MM_P2_gx8e256dn.cu:9-45,
+ * engine/mm/MM_P34_cmbz2048.cu:6-29); sequence engine/mm/MM_P7_lib.py:505-511.
+ * Expert parallelism: only experts in [expert_begin, expert_end) are computed and
+ * combined (pass the shared expert and hres on one rank only); summing y over the
+ * ranks gives the full layer.  kvalues = the 16 IQ4_NL levels (gguf-py table).
+ * The workspace (tlx_moe_workspace_bytes) must be zero-filled once before first
+ * use; its counters re-arm themselves.  Three launches, no host sync, no allocation. */
+size_t tlx_moe_workspace_bytes(int p, int n_experts, int hidden, int inner);
+int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p,
+                  int n_experts, int hidden, int inner, int expert_begin, int expert_end, int with_shared,
+                  int32_t* ids, float* gates, float* sg, void* ws, size_t ws_bytes, void* stream);
+int tlx_moe_experts(const void* gate, const void* up, const void* down, const void* shared_gate,
+                    const void* shared_up, const void* shared_down, const int8_t* kvalues, const float* hres,
+                    int64_t ldr, float* y, int64_t ldy, int p, int n_experts, int hidden, int inner,
+                    int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream);
+int tlx_moe_verify(const float* w_router, const float* w_shared_gate, const void* gate, const void* up,
+                   const void* down, const void* shared_gate, const void* shared_up, const void* shared_down,
+                   const int8_t* kvalues, const void* h, int64_t ldh, const float* hres, int64_t ldr, float* y,
+                   int64_t ldy, int32_t* ids, float* gates, float* sg, int p, int n_experts, int hidden, int inner,
+                   int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream);
+/* device error word of a MoE workspace (bounded-wait timeouts), synchronising `stream` */
+int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, int inner, uint32_t* err_out,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

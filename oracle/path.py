@@ -166,8 +166,8 @@ def moe_verify_f64(h, Wr, wsh, experts_gate, experts_up, experts_down,
     inner = experts_gate.shape[1]
     cache = {}
 
-    def expert(gr, ur, dr):
-        key = (id(gr), id(ur), id(dr))
+    def expert(key, gr, ur, dr):
+        # dequantised once per expert; keyed by expert id ("shared" for the shared one)
         if key not in cache:
             cache[key] = (dequant_iq4xs(gr, H), dequant_iq4xs(ur, H), dequant_iq4xs(dr, inner))
         return cache[key]
@@ -177,10 +177,10 @@ def moe_verify_f64(h, Wr, wsh, experts_gate, experts_up, experts_down,
     for p in range(P):
         for r in range(8):
             e = int(ids[p, r])
-            Wg, Wu, Wd = expert(experts_gate[e], experts_up[e], experts_down[e])
+            Wg, Wu, Wd = expert(e, experts_gate[e], experts_up[e], experts_down[e])
             act = silu_f64(Wg.astype(np.float64) @ h[p]) * (Wu.astype(np.float64) @ h[p])
             parts[p, r] = Wd.astype(np.float64) @ act
-    Sg, Su, Sd = expert(shared_gate, shared_up, shared_down)
+    Sg, Su, Sd = expert("shared", shared_gate, shared_up, shared_down)
     shared = np.zeros((P, H), dtype=np.float64)
     for p in range(P):
         act = silu_f64(Sg.astype(np.float64) @ h[p]) * (Su.astype(np.float64) @ h[p])

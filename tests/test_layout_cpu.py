@@ -38,7 +38,8 @@ def test_error_strings_and_host_argument_checks():
     assert lib.tlx_gemv_workspace_bytes(0, 14, 16, 256, 6, 0) == 0     # fp32 x: m <= 5
 
 
-@pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98)])
+@pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98),
+                                          ("iq4_xs", synth.iq4xs_blocks, 136)])
 def test_pack_unpack_round_trip(qtype, gen, bb):
     rng = np.random.default_rng(1)
     for n in (1, 16, 37):
@@ -160,3 +161,68 @@ def test_iq3_tile_decode_matches_oracle_exactly():
     got = emulate_iq3(tiled, 21, 512)
     ref = oracle.dequant_iq3xxs(raw, 512)
     assert np.array_equal(got, ref)
+
+
+def emulate_iq4(tiled, n_rows, k):
+    """IQ4_XS weights as moe.cu decodes them: lane (g, q), mma m reads qs bytes
+    2m, 2m+1 of its 32-byte slice; byte -> (kv[lo], kv[hi]) fp16 pair times the
+    sub-block scale (ls - 32) in fp16, times d in fp32.  Also checks that the
+    (lane, m, half) -> k map of the activation image covers every k once."""
+    kv = oracle.iq4nl_kvalues().astype(np.float32)
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    hit = np.zeros((T * 16, k), np.int32)
+    ch = tiled.reshape(T, nb, 2176)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                units = [c[(u * 32 + lane) * 16:(u * 32 + lane) * 16 + 16] for u in range(4)]
+                for rr in range(2):
+                    hd = c[2048 + g * 16 + rr * 8:2048 + g * 16 + rr * 8 + 8]
+                    d = np.float32(hd[0:2].view(np.float16)[0])
+                    sh = int(hd[2:4].view(np.uint16)[0])
+                    sl = int(hd[4:8].view(np.uint32)[0])
+                    qs = np.concatenate(units[2 * rr:2 * rr + 2])  # 32 bytes of sub-blocks 2q, 2q+1
+                    for m in range(16):
+                        hh = m >> 3
+                        ls = ((sl >> (8 * q + 4 * hh)) & 15) | (((sh >> (4 * q + 2 * hh)) & 3) << 4)
+                        s16 = np.float16(ls - 32)
+                        k0 = 64 * q + 32 * hh + 2 * (m & 7)
+                        for jb in range(2):
+                            byte = int(qs[2 * m + jb])
+                            for nib, dk in ((byte & 15, 0), (byte >> 4, 16)):
+                                a = np.float16(np.float16(kv[nib]) * s16)
+                                row = t * 16 + g + 8 * rr
+                                kk = b * 256 + k0 + jb + dk
+                                W[row, kk] = d * np.float32(a)
+                                hit[row, kk] += 1
+    assert (hit == 1).all()
+    return W[:n_rows]
+
+
+def test_iq4_tile_decode_matches_oracle():
+    # exact where |kv * (ls - 32)| <= 2048; larger integer products round once in fp16
+    rng = np.random.default_rng(10)
+    raw = synth.iq4xs_blocks(rng, 18, 512)
+    got = emulate_iq4(ops.pack_tiles_host("iq4_xs", raw, 512), 18, 512)
+    ref = oracle.dequant_iq4xs(raw, 512)
+    blk = raw.reshape(18, 2, 136)
+    d = blk[..., 0:2].copy().view(np.float16).astype(np.float32)[..., 0]
+    scale = np.repeat(d, 256, axis=1)
+    small = np.abs(ref) <= 2048 * scale
+    assert small.mean() > 0.5
+    assert np.array_equal(got[small], ref[small])
+    rel = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-30)
+    assert rel.max() <= 2.0 ** -11
+
+
+def test_moe_workspace_rejects_bad_shapes():
+    lib = _lib.lib()
+    assert lib.tlx_moe_workspace_bytes(9, 256, 2048, 512) == 0      # > 8 positions
+    assert lib.tlx_moe_workspace_bytes(5, 4, 2048, 512) == 0        # fewer experts than top-8
+    assert lib.tlx_moe_workspace_bytes(5, 256, 2000, 512) == 0      # hidden not a multiple of 256
+    assert lib.tlx_moe_workspace_bytes(5, 256, 2048, 500) == 0      # inner not a multiple of 256
+    assert lib.tlx_moe_workspace_bytes(5, 256, 2048, 512) > 0

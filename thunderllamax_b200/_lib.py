@@ -55,6 +55,14 @@ _SIGS = {
     "tlx_accept": (c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     "tlx_accept11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                               c_vp, c_vp, c_int, c_vp]),
+    "tlx_moe_workspace_bytes": (c_size, [c_int, c_int, c_int, c_int]),
+    "tlx_moe_route": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp,
+                              c_vp, c_vp, c_size, c_vp]),
+    "tlx_moe_experts": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_int, c_int,
+                                c_int, c_int, c_int, c_int, c_vp, c_size, c_vp]),
+    "tlx_moe_verify": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp,
+                               c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_size, c_vp]),
+    "tlx_moe_workspace_error": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
 }
 
 

@@ -19,6 +19,8 @@ int g_max_ctas = 0;  // 0 = one CTA per SM
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 bool valid_qtype(int qt) { return qt == QT_Q6_K || qt == QT_IQ3_XXS; }
+// formats the tile packers know (IQ4_XS is read by the MoE kernels only)
+bool valid_pack_qtype(int qt) { return valid_qtype(qt) || qt == QT_IQ4_XS; }
 
 // ---- small kernels -----------------------------------------------------------------
 
@@ -139,8 +141,7 @@ __global__ void pack_tiles_kernel(int qt, const uint8_t* __restrict__ src, int64
     rows[r] = row < n_rows ? src + row * stride + static_cast<int64_t>(b) * bb : nullptr;
   }
   uint8_t* out = dst + chunk_id * chunk_bytes(qt);
-  if (qt == QT_Q6_K) pack_q6_lane(rows, threadIdx.x, out);
-  else pack_iq3_lane(rows, threadIdx.x, out);
+  pack_lane(qt, rows, threadIdx.x, out);
 }
 
 }  // namespace
@@ -177,13 +178,13 @@ int tlx_device_check(void) {
 void tlx_set_max_ctas(int n) { g_max_ctas = n < 0 ? 0 : n; }
 
 size_t tlx_tiled_bytes(int qtype, int64_t n_rows, int64_t k) {
-  if (!valid_qtype(qtype) || n_rows <= 0 || k <= 0 || k % kQK) return 0;
+  if (!valid_pack_qtype(qtype) || n_rows <= 0 || k <= 0 || k % kQK) return 0;
   const int64_t tiles = (n_rows + 15) / 16;
   return static_cast<size_t>(tiles) * (k / kQK) * chunk_bytes(qtype);
 }
 
 int tlx_pack_tiles(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst) {
-  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!valid_pack_qtype(qtype)) return TLX_ERR_QTYPE;
   if (!src || !dst) return TLX_ERR_NULL;
   if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
   const int nb = static_cast<int>(k / kQK);
@@ -200,17 +201,14 @@ int tlx_pack_tiles(int qtype, const void* src, int64_t n_rows, int64_t k, int64_
         rows[r] = row < n_rows ? s + row * src_row_stride + static_cast<int64_t>(b) * bb : nullptr;
       }
       uint8_t* out = d + (t * nb + b) * static_cast<int64_t>(chunk_bytes(qtype));
-      for (int lane = 0; lane < 32; ++lane) {
-        if (qtype == QT_Q6_K) pack_q6_lane(rows, lane, out);
-        else pack_iq3_lane(rows, lane, out);
-      }
+      for (int lane = 0; lane < 32; ++lane) pack_lane(qtype, rows, lane, out);
     }
   return TLX_OK;
 }
 
 int tlx_pack_tiles_device(int qtype, const void* src, int64_t n_rows, int64_t k, int64_t src_row_stride, void* dst,
                           void* stream) {
-  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!valid_pack_qtype(qtype)) return TLX_ERR_QTYPE;
   if (!src || !dst) return TLX_ERR_NULL;
   if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
   const int nb = static_cast<int>(k / kQK);
@@ -223,7 +221,7 @@ int tlx_pack_tiles_device(int qtype, const void* src, int64_t n_rows, int64_t k,
 }
 
 int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, void* dst) {
-  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!valid_pack_qtype(qtype)) return TLX_ERR_QTYPE;
   if (!tiled || !dst) return TLX_ERR_NULL;
   if (n_rows <= 0 || k <= 0 || k % kQK) return TLX_ERR_SHAPE;
   const int nb = static_cast<int>(k / kQK);
@@ -237,7 +235,13 @@ int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, vo
     for (int b = 0; b < nb; ++b) {
       const uint8_t* c = s + (t * nb + b) * static_cast<int64_t>(ch);
       uint8_t* blk = d + row * row_bytes + static_cast<int64_t>(b) * bb;
-      if (qtype == QT_IQ3_XXS) {
+      if (qtype == QT_IQ4_XS) {
+        for (int i = 0; i < 8; ++i) blk[i] = c[2048 + g * 16 + rr * 8 + i];
+        for (int q = 0; q < 4; ++q)
+          for (int hf = 0; hf < 2; ++hf)
+            for (int j = 0; j < 16; ++j)
+              blk[8 + 32 * q + 16 * hf + j] = c[((2 * rr + hf) * 32 + 4 * g + q) * 16 + j];
+      } else if (qtype == QT_IQ3_XXS) {
         blk[0] = c[1536 + g * 4 + rr * 2];
         blk[1] = c[1536 + g * 4 + rr * 2 + 1];
         for (int q = 0; q < 4; ++q) {

@@ -37,9 +37,12 @@ constexpr int kTileRows = 16;
 constexpr int kQK = 256;
 constexpr uint32_t kChunkQ6 = 16 * 210;     // 3360
 constexpr uint32_t kChunkIq3 = 16 * 98;     // 1568
+constexpr uint32_t kChunkIq4 = 16 * 136;    // 2176
 
-__host__ __device__ constexpr uint32_t chunk_bytes(int qt) { return qt == QT_Q6_K ? kChunkQ6 : kChunkIq3; }
-__host__ __device__ constexpr uint32_t block_bytes(int qt) { return qt == QT_Q6_K ? 210u : 98u; }
+__host__ __device__ constexpr uint32_t block_bytes(int qt) {
+  return qt == QT_Q6_K ? 210u : (qt == QT_IQ4_XS ? 136u : 98u);
+}
+__host__ __device__ constexpr uint32_t chunk_bytes(int qt) { return 16u * block_bytes(qt); }
 
 // ------------------------------------------------------------------------------------
 // Host packers (plain C++; also used by the C-ABI tlx_pack_tiles).
@@ -118,6 +121,34 @@ TLX_HD inline void pack_iq3_lane(const uint8_t* const rows[16], int lane, uint8_
       out[1536 + g * 4 + rr * 2 + 0] = blk ? blk[0] : 0;
       out[1536 + g * 4 + rr * 2 + 1] = blk ? blk[1] : 0;
     }
+}
+
+// IQ4_XS chunk (GGUF block d f16 | scales_h u16 | scales_l[4] | qs[128]; the MoE
+// expert weights).  Lane l = 4g + q owns sub-blocks 2q and 2q+1 of rows g and g+8,
+// i.e. the 32 contiguous bytes qs[32q .. 32q+32) of each row, stored as four
+// 16-byte units u = 2*rr + half at (u*32 + l)*16 (rr 0: row g, 1: row g+8), so each
+// of the lane's four 16-byte loads is one contiguous 512-byte warp access.  The
+// 8-byte block headers follow at 2048 + 16g (row g) and 2048 + 16g + 8 (row g+8),
+// one 16-byte load for the four lanes of g.  Zero rows are all-zero (d = 0).
+TLX_HD inline void pack_iq4_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint8_t* blk = rows[g + 8 * rr];
+    for (int hf = 0; hf < 2; ++hf)
+      for (int j = 0; j < 16; ++j)
+        out[((2 * rr + hf) * 32 + lane) * 16 + j] = blk ? blk[8 + 32 * q + 16 * hf + j] : 0;
+  }
+  if (q == 0)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      for (int i = 0; i < 8; ++i) out[2048 + g * 16 + rr * 8 + i] = blk ? blk[i] : 0;
+    }
+}
+
+TLX_HD inline void pack_lane(int qt, const uint8_t* const rows[16], int lane, uint8_t* out) {
+  if (qt == QT_Q6_K) pack_q6_lane(rows, lane, out);
+  else if (qt == QT_IQ4_XS) pack_iq4_lane(rows, lane, out);
+  else pack_iq3_lane(rows, lane, out);
 }
 
 // ------------------------------------------------------------------------------------

@@ -1,0 +1,949 @@
+// MoE verify layer (P <= 8 positions) on B200: router, routed + shared IQ4_XS
+// experts, combine.  Three launches chained with programmatic dependent launch:
+//
+//   moe_router_kernel   logits = W_r h (fp32) for all experts plus the shared-expert
+//                       gate row; the last CTA to finish picks the top-8 per position
+//                       (8 masked-argmax passes, strict '>', ties to the lower id),
+//                       gates = softmax over the 8, sg = sigmoid(w_sh . h), and builds
+//                       the SLOT list: one slot per distinct routed expert of this
+//                       rank's range (ascending id) with the positions routed to it,
+//                       then the shared expert.  The CTAs also stage h as the fp16
+//                       activation image the expert kernel reads.
+//   moe_gate_up_kernel  per (slot, 16-row tile): gate and up over all of h for the
+//                       slot's positions, act = silu(g) * u in fp32 plus a running
+//                       max |act| per (position, expert) pair.
+//   moe_down_kernel     builds the fp16 activation image of act with one power-of-two
+//                       scale per pair (act can exceed the fp16 range; the scale
+//                       keeps max |act| at 2^14), then per (slot, 16-row tile of the
+//                       hidden dim): down over act into fp32 parts[pair][row] (scale
+//                       undone exactly); the last slot to finish a tile combines it:
+//                       y = hres + sum_r gates[r] part_r + sg * shared (r ascending).
+//
+// Reference chain engine/mm/MM_P7_lib.py:505-511: rt8e256 (engine/mm/MM_P1_rt8e256.cu:
+// 14-62) -> shexp8 -> gx8e256up4 (engine/mm/MM_P2_gx8e256up4.cu:8-55) -> gx8e256dn
+// (engine/mm/MM_P2_gx8e256dn.cu:9-45) -> cmbz2048 (engine/mm/MM_P34_cmbz2048.cu:6-29).
+// The reference runs one CTA per (position, rank) pair and reads an expert chosen by
+// two positions twice; here each distinct expert is read once for all its positions
+// (the positions are the columns of one mma.m16n8k16 n-tile).
+//
+// Weights: IQ4_XS in the 16-row tile layout of formats.cuh (chunk = 16 rows x one
+// 256-weight block, 2176 B).  Dequantisation: a 256-entry shared table maps one qs
+// byte (two 4-bit IQ4_NL indices, weights j and j+16 of a sub-block) to the fp16 pair
+// (kv[lo], kv[hi]); the table holds one copy per lane at stride 256 B, so the 32
+// lookups of a warp hit 32 distinct banks and the address is a single byte permute.
+// The pair is multiplied by the sub-block scale (ls - 32) in fp16 (exact whenever
+// |kv * (ls - 32)| <= 2048, otherwise one rounding, <= 2^-11 relative); the block
+// scale d multiplies the fp32 mma result.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "common.cuh"
+#include "formats.cuh"
+#include "tlx_internal.h"
+
+namespace tlx {
+namespace {
+
+constexpr int kTopK = 8;
+constexpr int kMaxPos = 8;
+constexpr int kMaxExperts = 1024;
+constexpr int kMaxSlots = kTopK * kMaxPos + 1;  // distinct routed experts <= 8 P, + shared
+constexpr int kExpWarps = 16;                   // warps per expert-kernel CTA
+constexpr int kRouterWarps = 8;                 // experts per router CTA
+constexpr uint32_t kLutBytes = 256u * 256u;     // entry v at 256 v, lane word at + 4 lane
+constexpr uint32_t kRow = 68;                   // uint2 entries per image row (64 + 4 pad)
+constexpr uint32_t kRowBytes = kRow * 8u;
+constexpr uint32_t kChunk = kChunkIq4;          // 2176
+constexpr uint32_t kSmemLimit = 227u * 1024u;
+
+struct MoeMeta {
+  uint32_t router_done;  // CTAs of the router that finished (re-armed by the last)
+  int32_t n_slots;       // routed slots + shared slot
+  int32_t n_routed;
+  int32_t pad0;
+  int32_t ids[kMaxPos * kTopK];
+  float gates[kMaxPos * kTopK];
+  float sg[kMaxPos];
+  int16_t slot_expert[kMaxSlots];  // -1: the shared expert
+  uint8_t slot_count[kMaxSlots];
+  uint8_t slot_tok[kMaxSlots][8];   // positions (columns) of the slot, ascending; unused = column 0
+  uint8_t slot_pair[kMaxSlots][8];  // pair id of each column: 8 p + r, shared 8 P + p
+};
+
+// the slot list, cached in shared memory by the expert kernels
+struct SlotCache {
+  int16_t expert[kMaxSlots];
+  uint8_t count[kMaxSlots];
+  uint8_t tok[kMaxSlots][8];
+  uint8_t pair[kMaxSlots][8];
+  int n_slots;
+};
+
+__device__ __forceinline__ void load_slots(const MoeMeta* mt, SlotCache& sc) {
+  const int n = __ldcg(&mt->n_slots);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    sc.expert[i] = __ldcg(&mt->slot_expert[i]);
+    sc.count[i] = __ldcg(&mt->slot_count[i]);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      sc.tok[i][c] = __ldcg(&mt->slot_tok[i][c]);
+      sc.pair[i][c] = __ldcg(&mt->slot_pair[i][c]);
+    }
+  }
+  if (threadIdx.x == 0) sc.n_slots = n;
+}
+
+struct MoeParams {
+  const float* wr;    // [E][H] fp32 router
+  const float* wsh;   // [H] fp32 shared-expert gate
+  const uint16_t* h;  // [P][ldh] bf16 bits
+  int64_t ldh;
+  const uint8_t* gate;  // tiled IQ4_XS [E][I x H], expert-major
+  const uint8_t* up;
+  const uint8_t* down;   // tiled IQ4_XS [E][H x I]
+  const uint8_t* sgate;  // shared expert (nullptr: none)
+  const uint8_t* sup;
+  const uint8_t* sdown;
+  const int8_t* kvalues;  // IQ4_NL table, 16 entries
+  const float* hres;      // [P][ldr] or nullptr
+  int64_t ldr;
+  float* y;
+  int64_t ldy;
+  int32_t* ids_out;
+  float* gates_out;
+  float* sg_out;
+  int P, E, H, I, e0, e1, with_shared, stages;
+  int64_t gu_bytes, dn_bytes;  // tiled bytes of one expert matrix
+  MoeMeta* meta;
+  float* logits;   // [P][E + 1]
+  uint32_t* cnt;   // [H / 16] combine counters
+  uint32_t* err;
+  uint2* ximg;     // [H/256][P][68]
+  float* actf;     // [9P][I] fp32 act
+  uint32_t* amax;  // [9P] max |act| bits
+  float* parts;    // [9P][H]
+};
+
+// ---- activation image position of k (IQ4 k order) ----
+// mma m of lane quarter q takes the byte pair 2m, 2m+1 of the quarter's 32 qs bytes:
+// sub-block 2q + (m >> 3), bytes j0 = 2 (m & 7), j0 + 1, i.e. the weights
+// k0 = 64q + 32 (m >> 3) + 2 (m & 7) and k0 + 16 (lo / hi nibble of byte j0), k0 + 1
+// and k0 + 17 (byte j0 + 1).  Entry (m, q) = fp16 {x[k0], x[k0+16], x[k0+1], x[k0+17]}.
+__host__ __device__ __forceinline__ void iq4_image_pos(int k, int& b, int& m, int& q, int& pos) {
+  b = k >> 8;
+  const int kin = k & 255;
+  q = kin >> 6;
+  const int r = kin & 63;
+  m = 8 * (r >> 5) + ((r & 15) >> 1);
+  pos = 2 * (r & 1) + ((r >> 4) & 1);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+// table word for one byte of w: address = 256 * byte + 4 * lane, one PRMT
+__device__ __forceinline__ uint32_t lut_get(const uint8_t* lut, uint32_t w, uint32_t lane4, uint32_t sel) {
+  return *reinterpret_cast<const uint32_t*>(lut + __byte_perm(w, lane4, sel));
+}
+
+struct Iq4Lane {
+  uint32_t q[16];    // rows g (0..7) and g+8 (8..15): qs bytes 32q' .. 32q'+32
+  uint32_t s[2][2];  // fp16x2 (ls - 32) of sub-blocks 2q', 2q'+1 for row g / g+8
+  float d[2];
+};
+
+__device__ __forceinline__ void iq4_load(const uint8_t* chunk, int lane, Iq4Lane& L) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint4 v = lds128(chunk + (u * 32 + lane) * 16);
+    L.q[4 * u + 0] = v.x;
+    L.q[4 * u + 1] = v.y;
+    L.q[4 * u + 2] = v.z;
+    L.q[4 * u + 3] = v.w;
+  }
+  const uint4 hd = lds128(chunk + 2048 + (lane >> 2) * 16);
+  const int qq = lane & 3;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint32_t dsh = rr ? hd.z : hd.x, sl = rr ? hd.w : hd.y;
+    L.d[rr] = __half2float(__ushort_as_half(static_cast<unsigned short>(dsh & 0xFFFFu)));
+    const uint32_t sh = dsh >> 16;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint32_t ls = ((sl >> (8 * qq + 4 * hh)) & 15u) | (((sh >> (4 * qq + 2 * hh)) & 3u) << 4);
+      // fp16 1024 + ls in both halves, minus 1056: (ls - 32), exact
+      L.s[rr][hh] = hadd2_u((ls | (ls << 16)) | kMagic, kMinus1056);
+    }
+  }
+}
+
+// A fragment of mma m from the lane's qs words: a0/a2 row g, a1/a3 row g+8
+__device__ __forceinline__ void iq4_a(const Iq4Lane& L, int m, const uint8_t* lut, uint32_t lane4,
+                                      uint32_t (&a)[4]) {
+  const int wi = m >> 1, hh = m >> 3;
+  const uint32_t s0 = 0x7604u | (static_cast<uint32_t>(2 * (m & 1)) << 4);
+  const uint32_t s1 = s0 + 0x10u;
+  a[0] = hmul2_u(lut_get(lut, L.q[wi], lane4, s0), L.s[0][hh]);
+  a[2] = hmul2_u(lut_get(lut, L.q[wi], lane4, s1), L.s[0][hh]);
+  a[1] = hmul2_u(lut_get(lut, L.q[8 + wi], lane4, s0), L.s[1][hh]);
+  a[3] = hmul2_u(lut_get(lut, L.q[8 + wi], lane4, s1), L.s[1][hh]);
+}
+
+// D(16 x 8) += A(16 rows x 256 k of one chunk) . B(image rows of this lane's column)
+__device__ __forceinline__ void iq4_chunk_mma(const Iq4Lane& L, const uint2* xb, const uint8_t* lut, uint32_t lane4,
+                                              float (&t)[4]) {
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const uint2 b = xb[m * 4];
+    uint32_t a[4];
+    iq4_a(L, m, lut, lane4, a);
+    mma16816(t, a, b.x, b.y);
+  }
+}
+
+// gate and up chunks of one block share the activation loads
+__device__ __forceinline__ void iq4_pair_mma(const uint8_t* cg, const uint8_t* cu, const uint2* xb, const uint8_t* lut,
+                                             uint32_t lane4, int lane, float (&ag)[4], float (&au)[4]) {
+  Iq4Lane G, U;
+  iq4_load(cg, lane, G);
+  iq4_load(cu, lane, U);
+  float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const uint2 b = xb[m * 4];
+    uint32_t a[4];
+    iq4_a(G, m, lut, lane4, a);
+    mma16816(tg, a, b.x, b.y);
+    iq4_a(U, m, lut, lane4, a);
+    mma16816(tu, a, b.x, b.y);
+  }
+  ag[0] += G.d[0] * tg[0];
+  ag[1] += G.d[0] * tg[1];
+  ag[2] += G.d[1] * tg[2];
+  ag[3] += G.d[1] * tg[3];
+  au[0] += U.d[0] * tu[0];
+  au[1] += U.d[0] * tu[1];
+  au[2] += U.d[1] * tu[2];
+  au[3] += U.d[1] * tu[3];
+}
+
+// the byte table: entry v -> fp16x2 (kv[v & 15], kv[v >> 4]), one copy per lane
+__device__ __forceinline__ void build_lut(uint8_t* lut, const int8_t* kvalues) {
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+    const int v = i >> 5, c = i & 31;
+    const __half lo = __int2half_rn(static_cast<int>(__ldg(kvalues + (v & 15))));
+    const __half hi = __int2half_rn(static_cast<int>(__ldg(kvalues + (v >> 4))));
+    const uint32_t word =
+        static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+    *reinterpret_cast<uint32_t*>(lut + v * 256 + c * 4) = word;
+  }
+}
+
+// ---------------------------------------------------------------------------- router
+__global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeParams p) {
+  extern __shared__ __align__(16) float rsm[];
+  float* hs = rsm;  // [P][H] fp32
+  __shared__ uint32_t is_last;
+  __shared__ int s_ids[kMaxPos * kTopK];
+  __shared__ int warp_tot[kRouterWarps];
+  __shared__ int n_routed_s;
+  const int P = p.P, H = p.H, E = p.E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_wait();
+  griddep_launch_dependents();
+
+  // the previous step's down kernel has finished with the act maxima: re-arm them
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < 9 * P; i += blockDim.x) p.amax[i] = 0u;
+  for (int i = threadIdx.x; i < P * (H >> 1); i += blockDim.x) {
+    const int t = i / (H >> 1), k2 = i - t * (H >> 1);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(p.h + t * p.ldh + 2 * k2);
+    hs[t * H + 2 * k2] = __uint_as_float(v << 16);
+    hs[t * H + 2 * k2 + 1] = __uint_as_float(v & 0xFFFF0000u);
+  }
+  __syncthreads();
+  // this CTA's share of the fp16 activation image of h (bf16 -> fp16, exact in range)
+  {
+    const int per_tok = H >> 2;
+    for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < P * per_tok; gi += gridDim.x * blockDim.x) {
+      const int t = gi / per_tok, e = gi - t * per_tok;
+      const int b = e >> 6, m = (e & 63) >> 2, q = e & 3;
+      const float* hr = hs + t * H + 256 * b + 64 * q + 32 * (m >> 3) + 2 * (m & 7);
+      const uint32_t lo =
+          static_cast<uint32_t>(f32_to_f16_bits(hr[0])) | (static_cast<uint32_t>(f32_to_f16_bits(hr[16])) << 16);
+      const uint32_t hi =
+          static_cast<uint32_t>(f32_to_f16_bits(hr[1])) | (static_cast<uint32_t>(f32_to_f16_bits(hr[17])) << 16);
+      p.ximg[(b * P + t) * kRow + m * 4 + q] = make_uint2(lo, hi);
+    }
+  }
+
+  // one router row per warp: experts, then the shared-expert gate row (e == E)
+  const int e = blockIdx.x * kRouterWarps + warp;
+  if (e <= E) {
+    const float* row = e < E ? p.wr + static_cast<int64_t>(e) * H : p.wsh;
+    float acc[kMaxPos];
+#pragma unroll
+    for (int t = 0; t < kMaxPos; ++t) acc[t] = 0.f;
+    for (int k = 4 * lane; k < H; k += 128) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(row + k));
+#pragma unroll
+      for (int t = 0; t < kMaxPos; ++t)
+        if (t < P) {
+          const float4 x = *reinterpret_cast<const float4*>(hs + t * H + k);
+          acc[t] = fmaf(w.x, x.x, acc[t]);
+          acc[t] = fmaf(w.y, x.y, acc[t]);
+          acc[t] = fmaf(w.z, x.z, acc[t]);
+          acc[t] = fmaf(w.w, x.w, acc[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxPos; ++t)
+      if (t < P) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) p.logits[t * (E + 1) + e] = v;
+      }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&p.meta->router_done, 1u) == gridDim.x - 1 ? 1u : 0u;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  // ---- the last CTA: top-8, gates, sg, slot list ----
+  MoeMeta* mt = p.meta;
+  float* lg = rsm;                                                     // [P][E + 1] (reuses the h area)
+  uint32_t* tokmask = reinterpret_cast<uint32_t*>(rsm + P * (E + 1));  // [E]
+  for (int i = threadIdx.x; i < P * (E + 1); i += blockDim.x) lg[i] = __ldcg(p.logits + i);
+  for (int i = threadIdx.x; i < E; i += blockDim.x) tokmask[i] = 0u;
+  __syncthreads();
+  for (int t = warp; t < P; t += kRouterWarps) {
+    float* l = lg + t * (E + 1);
+    float vals[kTopK];
+    int ids[kTopK];
+#pragma unroll
+    for (int r = 0; r < kTopK; ++r) {
+      uint64_t best = 0ull;
+      for (int x = lane; x < E; x += 32) {
+        const uint64_t k = argmax_key(l[x], static_cast<uint32_t>(x));
+        best = k > best ? k : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+      }
+      ids[r] = key_index(best);
+      vals[r] = l[ids[r]];
+      __syncwarp();
+      if (lane == 0) l[ids[r]] = __uint_as_float(0x7FC00000u);  // NaN: never selected again
+      __syncwarp();
+    }
+    if (lane == 0) {
+      const float mx = vals[0];
+      float ex[kTopK], s = 0.f;
+#pragma unroll
+      for (int r = 0; r < kTopK; ++r) {
+        ex[r] = expf(vals[r] - mx);
+        s += ex[r];
+      }
+#pragma unroll
+      for (int r = 0; r < kTopK; ++r) {
+        const float g = ex[r] / s;
+        s_ids[t * kTopK + r] = ids[r];
+        mt->ids[t * kTopK + r] = ids[r];
+        mt->gates[t * kTopK + r] = g;
+        if (p.ids_out) p.ids_out[t * kTopK + r] = ids[r];
+        if (p.gates_out) p.gates_out[t * kTopK + r] = g;
+        if (ids[r] >= p.e0 && ids[r] < p.e1) atomicOr(&tokmask[ids[r]], 1u << t);
+      }
+      const float a = l[E];
+      const float sgv = 1.0f / (1.0f + expf(-a));
+      mt->sg[t] = sgv;
+      if (p.sg_out) p.sg_out[t] = sgv;
+    }
+  }
+  __syncthreads();
+  // slots in ascending expert id: block-wide exclusive scan of the used flags
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int x0 = threadIdx.x * per;
+  int c = 0;
+  for (int x = x0; x < x0 + per && x < E; ++x) c += tokmask[x] ? 1 : 0;
+  int incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += warp_tot[w];
+  int u = base + incl - c;
+  for (int x = x0; x < x0 + per && x < E; ++x) {
+    const uint32_t mk = tokmask[x];
+    if (!mk) continue;
+    mt->slot_expert[u] = static_cast<int16_t>(x);
+    uint8_t tok[8], pair[8];
+    int n = 0;
+    for (int t = 0; t < P; ++t)
+      if (mk & (1u << t)) {
+        int r = 0;
+        while (r < kTopK && s_ids[t * kTopK + r] != x) ++r;
+        tok[n] = static_cast<uint8_t>(t);
+        pair[n] = static_cast<uint8_t>(t * kTopK + r);
+        ++n;
+      }
+    for (int c2 = 0; c2 < 8; ++c2) {
+      mt->slot_tok[u][c2] = c2 < n ? tok[c2] : tok[0];
+      mt->slot_pair[u][c2] = c2 < n ? pair[c2] : pair[0];
+    }
+    mt->slot_count[u] = static_cast<uint8_t>(n);
+    ++u;
+  }
+  if (threadIdx.x == blockDim.x - 1) n_routed_s = base + incl;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nr = n_routed_s;
+    mt->n_routed = nr;
+    if (p.with_shared) {
+      mt->slot_expert[nr] = -1;
+      mt->slot_count[nr] = static_cast<uint8_t>(P);
+      for (int t = 0; t < 8; ++t) {
+        const int tt = t < P ? t : 0;
+        mt->slot_tok[nr][t] = static_cast<uint8_t>(tt);
+        mt->slot_pair[nr][t] = static_cast<uint8_t>(kTopK * P + tt);
+      }
+    }
+    mt->n_slots = nr + (p.with_shared ? 1 : 0);
+    mt->router_done = 0u;
+  }
+}
+
+// ------------------------------------------------------------- expert kernels (shared)
+struct ExpLayout {
+  uint32_t img, ring, bars, total;
+};
+
+__host__ __device__ inline ExpLayout exp_layout(uint32_t img_bytes, int stages) {
+  ExpLayout L;
+  L.img = kLutBytes;
+  L.ring = L.img + ((img_bytes + 127u) & ~127u);
+  L.bars = L.ring + static_cast<uint32_t>(kExpWarps * stages) * kChunk;
+  L.total = L.bars + static_cast<uint32_t>(kExpWarps * stages + 1) * 8u;
+  return L;
+}
+
+// Per-warp chunk ring.  The warp's items are i = cta + C (warp + W k); item i is
+// slot i / tiles, tile i % tiles, and reads `per_item` consecutive chunks of one or
+// two matrices (two: gate and up alternate).  Chunk number c (in the warp's order)
+// lives in ring slot c % S; lane 0 issues chunks up to S ahead of the compute cursor.
+struct Ring {
+  uint8_t* ring;
+  uint64_t* bars;
+  int S;
+  int64_t issued, consumed;
+  int item, j, n_items, step, per_item, nmat;  // issue cursor
+  const uint8_t* base0;                        // this item's matrices (tile offset included)
+  const uint8_t* base1;
+};
+
+template <typename BaseFn>
+__device__ __forceinline__ void ring_issue(Ring& R, BaseFn base_of) {
+  while (R.item < R.n_items && R.issued < R.consumed + R.S) {
+    if (R.j == 0) base_of(R.item, R.base0, R.base1);
+    const int slot = static_cast<int>(R.issued % R.S);
+    mbar_arrive_expect_tx(&R.bars[slot], kChunk);
+    const bool second = R.nmat == 2 && (R.j & 1);
+    const int blk = R.nmat == 2 ? (R.j >> 1) : R.j;
+    bulk_g2s(R.ring + slot * kChunk, (second ? R.base1 : R.base0) + static_cast<int64_t>(blk) * kChunk, kChunk,
+             &R.bars[slot]);
+    ++R.issued;
+    if (++R.j == R.per_item) {
+      R.j = 0;
+      R.item += R.step;
+    }
+  }
+}
+
+__device__ __forceinline__ bool ring_wait(Ring& R, int64_t c, uint32_t* err) {
+  return mbar_wait_bounded(&R.bars[c % R.S], static_cast<uint32_t>((c / R.S) & 1), err);
+}
+
+// let every copy the warp issued land before the CTA can exit
+__device__ __forceinline__ void ring_drain(Ring& R) {
+  for (int64_t c = R.consumed; c < R.issued; ++c) ring_wait(R, c, nullptr);
+}
+
+// ------------------------------------------------------------------- gate/up kernel
+__global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const MoeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ SlotCache sc;
+  const int P = p.P, S = p.stages;
+  const int nbh = p.H >> 8, tpe = p.I >> 4;
+  const uint32_t img_bytes = static_cast<uint32_t>(nbh * P) * kRowBytes;
+  const ExpLayout L = exp_layout(img_bytes, S);
+  const uint8_t* lut = smem;
+  uint2* xs = reinterpret_cast<uint2*>(smem + L.img);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + L.bars) + kExpWarps * S;
+  Ring R;
+  R.ring = smem + L.ring + static_cast<uint32_t>(warp * S) * kChunk;
+  R.bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * S;
+  R.S = S;
+
+  build_lut(smem, p.kvalues);
+  if (lane == 0)
+    for (int s = 0; s < S; ++s) mbar_init(&R.bars[s], 1);
+  if (threadIdx.x == 0) mbar_init(xbar, 1);
+  mbar_fence_init();
+
+  // everything above touches only constants; the slot list and the image come from
+  // the router, so wait for it to complete
+  griddep_wait();
+  griddep_launch_dependents();
+  load_slots(p.meta, sc);
+  __syncthreads();
+
+  const int n_items = sc.n_slots * tpe;
+  // only CTAs with work copy the image (warp 0 holds the CTA's first item and waits)
+  if (threadIdx.x == 0 && static_cast<int>(blockIdx.x) < n_items) {
+    mbar_arrive_expect_tx(xbar, img_bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg);
+    for (uint32_t off = 0; off < img_bytes; off += 32768u)
+      bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, std::min(32768u, img_bytes - off), xbar);
+  }
+  const int i_first = blockIdx.x + gridDim.x * warp;
+  R.issued = R.consumed = 0;
+  R.item = i_first;
+  R.j = 0;
+  R.n_items = n_items;
+  R.step = gridDim.x * kExpWarps;
+  R.per_item = 2 * nbh;
+  R.nmat = 2;
+  auto base_of = [&](int item, const uint8_t*& b0, const uint8_t*& b1) {
+    const int u = item / tpe, tau = item - u * tpe;
+    const int e = sc.expert[u];
+    const int64_t off = static_cast<int64_t>(tau) * nbh * kChunk;
+    b0 = (e >= 0 ? p.gate + static_cast<int64_t>(e) * p.gu_bytes : p.sgate) + off;
+    b1 = (e >= 0 ? p.up + static_cast<int64_t>(e) * p.gu_bytes : p.sup) + off;
+  };
+  if (lane == 0) ring_issue(R, base_of);
+  __syncwarp();
+
+  bool failed = false;
+  if (i_first < n_items) failed = !mbar_wait_bounded(xbar, 0, lane == 0 ? p.err : nullptr);
+
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+  const int g = lane >> 2, qq = lane & 3;
+  for (int item = i_first; item < n_items && !failed; item += R.step) {
+    const int u = item / tpe, tau = item - u * tpe;
+    const int cnt = sc.count[u];
+    const uint2* xl = xs + sc.tok[u][g] * kRow + qq;
+    float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = 0; b < nbh; ++b) {
+      const int64_t c0 = R.consumed;
+      if (!ring_wait(R, c0, lane == 0 ? p.err : nullptr) || !ring_wait(R, c0 + 1, lane == 0 ? p.err : nullptr)) {
+        failed = true;
+        break;
+      }
+      iq4_pair_mma(R.ring + (c0 % S) * kChunk, R.ring + ((c0 + 1) % S) * kChunk, xl + b * P * kRow, lut, lane4, lane,
+                   ag, au);
+      R.consumed = c0 + 2;
+      // refill (after the stages' last generic-proxy reads)
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ring_issue(R, base_of);
+      __syncwarp();
+    }
+    if (failed) break;
+    // act = silu(g) * u (fp32) and the per-pair running max |act|
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int col = 2 * qq + h2;
+      const float v0 = silu_f(ag[h2]) * au[h2];          // row g
+      const float v1 = silu_f(ag[2 + h2]) * au[2 + h2];  // row g + 8
+      float mx = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (col < cnt) {
+        const int pair = sc.pair[u][col];
+        float* dst = p.actf + static_cast<int64_t>(pair) * p.I + tau * 16 + g;
+        dst[0] = v0;
+        dst[8] = v1;
+        if (g == 0) atomicMax(p.amax + pair, __float_as_uint(mx));
+      }
+    }
+  }
+  if (failed) ring_drain(R);
+}
+
+// --------------------------------------------------------------- down + combine kernel
+__global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ SlotCache sc;
+  __shared__ float s_inv[9 * kMaxPos];
+  const int P = p.P, S = p.stages, I = p.I;
+  const int nbi = I >> 8, tpd = p.H >> 4;
+  const int npair = 9 * P;
+  const uint32_t img_bytes = static_cast<uint32_t>(nbi * npair) * kRowBytes;
+  const ExpLayout L = exp_layout(img_bytes, S);
+  const uint8_t* lut = smem;
+  uint2* as = reinterpret_cast<uint2*>(smem + L.img);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Ring R;
+  R.ring = smem + L.ring + static_cast<uint32_t>(warp * S) * kChunk;
+  R.bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * S;
+  R.S = S;
+
+  build_lut(smem, p.kvalues);
+  if (lane == 0)
+    for (int s = 0; s < S; ++s) mbar_init(&R.bars[s], 1);
+  mbar_fence_init();
+
+  griddep_wait();
+  griddep_launch_dependents();
+  load_slots(p.meta, sc);
+  __syncthreads();
+  const int n_slots = sc.n_slots;
+  if (n_slots == 0) {
+    // nothing routed to this rank's experts and no shared expert: y = hres (or 0)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P * p.H; i += gridDim.x * blockDim.x) {
+      const int t = i / p.H, r = i - t * p.H;
+      p.y[t * p.ldy + r] = p.hres ? p.hres[t * p.ldr + r] : 0.f;
+    }
+    return;
+  }
+  const int n_items = n_slots * tpd;
+  const int i_first = blockIdx.x + gridDim.x * warp;
+  R.issued = R.consumed = 0;
+  R.item = i_first;
+  R.j = 0;
+  R.n_items = n_items;
+  R.step = gridDim.x * kExpWarps;
+  R.per_item = nbi;
+  R.nmat = 1;
+  auto base_of = [&](int item, const uint8_t*& b0, const uint8_t*& b1) {
+    const int u = item / tpd, tau = item - u * tpd;
+    const int e = sc.expert[u];
+    b0 = (e >= 0 ? p.down + static_cast<int64_t>(e) * p.dn_bytes : p.sdown) + static_cast<int64_t>(tau) * nbi * kChunk;
+    b1 = b0;
+  };
+  // weights do not depend on act: start streaming before the image is built
+  if (lane == 0) ring_issue(R, base_of);
+
+  // act image with one power-of-two scale per pair: max |act| * scale <= 2^14
+  for (int i = threadIdx.x; i < npair; i += blockDim.x) {
+    const float mx = __uint_as_float(__ldcg(p.amax + i));
+    int ex = 0;
+    if (mx > 0.f && mx == mx) frexpf(mx, &ex);
+    s_inv[i] = ldexpf(1.0f, ex - 14);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < npair * (I >> 2); i += blockDim.x) {
+    const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.actf + static_cast<int64_t>(pair) * I + k));
+    const float scl = 1.0f / s_inv[pair];  // exact: a power of two
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int bi, m, q4, pos;
+      iq4_image_pos(k + e, bi, m, q4, pos);
+      reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] = f32_to_f16_bits(vv[e] * scl);
+    }
+  }
+  __syncthreads();
+
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+  const int g = lane >> 2, qq = lane & 3;
+  bool failed = false;
+  for (int item = i_first; item < n_items && !failed; item += R.step) {
+    const int u = item / tpd, tau = item - u * tpd;
+    const int cnt = sc.count[u];
+    const uint2* xl = as + sc.pair[u][g] * kRow + qq;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = 0; b < nbi; ++b) {
+      const int64_t c0 = R.consumed;
+      if (!ring_wait(R, c0, lane == 0 ? p.err : nullptr)) {
+        failed = true;
+        break;
+      }
+      Iq4Lane W;
+      iq4_load(R.ring + (c0 % S) * kChunk, lane, W);
+      float t4[4] = {0.f, 0.f, 0.f, 0.f};
+      iq4_chunk_mma(W, xl + b * npair * kRow, lut, lane4, t4);
+      acc[0] += W.d[0] * t4[0];
+      acc[1] += W.d[0] * t4[1];
+      acc[2] += W.d[1] * t4[2];
+      acc[3] += W.d[1] * t4[3];
+      R.consumed = c0 + 1;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ring_issue(R, base_of);
+      __syncwarp();
+    }
+    if (failed) break;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int col = 2 * qq + (e & 1);
+      if (col < cnt) {
+        const int pair = sc.pair[u][col];
+        const int row = tau * 16 + g + 8 * (e >> 1);
+        p.parts[static_cast<int64_t>(pair) * p.H + row] = acc[e] * s_inv[pair];
+      }
+    }
+    // the last slot to finish this 16-row tile combines it
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(p.cnt + tau, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == static_cast<uint32_t>(n_slots - 1)) {
+      __threadfence();
+      for (int idx = lane; idx < 16 * P; idx += 32) {
+        const int t = idx >> 4, row = tau * 16 + (idx & 15);
+        float a = 0.f;
+        for (int r = 0; r < kTopK; ++r) {
+          const int id = __ldcg(&p.meta->ids[t * kTopK + r]);
+          if (id >= p.e0 && id < p.e1)
+            a += __ldcg(&p.meta->gates[t * kTopK + r]) *
+                 __ldcg(p.parts + static_cast<int64_t>(t * kTopK + r) * p.H + row);
+        }
+        if (p.with_shared)
+          a += __ldcg(&p.meta->sg[t]) * __ldcg(p.parts + static_cast<int64_t>(kTopK * P + t) * p.H + row);
+        p.y[t * p.ldy + row] = p.hres ? p.hres[t * p.ldr + row] + a : a;
+      }
+      if (lane == 0) p.cnt[tau] = 0u;
+    }
+  }
+  if (failed) ring_drain(R);
+}
+
+// ------------------------------------------------------------------------------ host
+struct WsLayout {
+  size_t meta, logits, cnt, err, ximg, actf, amax, parts, total;
+};
+
+inline size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+bool moe_shape_ok(int P, int E, int H, int I) {
+  return P >= 1 && P <= kMaxPos && E >= kTopK && E <= kMaxExperts && H >= 256 && H % 256 == 0 && I >= 256 &&
+         I % 256 == 0 && H <= 16384 && I <= 4096;
+}
+
+WsLayout ws_layout(int P, int E, int H, int I) {
+  WsLayout w;
+  size_t o = 0;
+  w.meta = o;
+  o = up256(o + sizeof(MoeMeta));
+  w.logits = o;
+  o = up256(o + static_cast<size_t>(P) * (E + 1) * 4);
+  w.cnt = o;
+  o = up256(o + static_cast<size_t>(H / 16) * 4);
+  w.err = o;
+  o = up256(o + 4);
+  w.ximg = o;
+  o = up256(o + static_cast<size_t>(H / 256) * P * kRowBytes);
+  w.actf = o;
+  o = up256(o + static_cast<size_t>(9 * P) * I * 4);
+  w.amax = o;
+  o = up256(o + static_cast<size_t>(9 * P) * 4);
+  w.parts = o;
+  o = up256(o + static_cast<size_t>(9 * P) * H * 4);
+  w.total = o;
+  return w;
+}
+
+int stages_for(uint32_t img_bytes, int want) {
+  // dynamic shared memory; the static slot cache and scales take the rest (< 4 KB)
+  for (int s = want; s >= 2; --s)
+    if (exp_layout(img_bytes, s).total <= kSmemLimit - 4096u) return s;
+  return 0;
+}
+
+int launch_ex(const void* kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const MoeParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<MoeParams*>(&p)};
+  return cudaLaunchKernelExC(&cfg, kern, args) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+bool al(const void* q, size_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; }
+
+int setup(const MoeParams& in, int P, int E, int H, int I, int e0, int e1, void* ws, size_t ws_bytes, MoeParams& p) {
+  if (!moe_shape_ok(P, E, H, I)) return TLX_ERR_SHAPE;
+  if (e0 < 0 || e1 > E || e0 > e1) return TLX_ERR_SHAPE;
+  if (!ws) return TLX_ERR_NULL;
+  const WsLayout w = ws_layout(P, E, H, I);
+  if (ws_bytes < w.total) return TLX_ERR_WORKSPACE;
+  if (!al(ws, 256)) return TLX_ERR_ALIGN;
+  p = in;
+  p.P = P;
+  p.E = E;
+  p.H = H;
+  p.I = I;
+  p.e0 = e0;
+  p.e1 = e1;
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  p.meta = reinterpret_cast<MoeMeta*>(b + w.meta);
+  p.logits = reinterpret_cast<float*>(b + w.logits);
+  p.cnt = reinterpret_cast<uint32_t*>(b + w.cnt);
+  p.err = reinterpret_cast<uint32_t*>(b + w.err);
+  p.ximg = reinterpret_cast<uint2*>(b + w.ximg);
+  p.actf = reinterpret_cast<float*>(b + w.actf);
+  p.amax = reinterpret_cast<uint32_t*>(b + w.amax);
+  p.parts = reinterpret_cast<float*>(b + w.parts);
+  p.gu_bytes = static_cast<int64_t>(I / 16) * (H / 256) * kChunk;
+  p.dn_bytes = static_cast<int64_t>(H / 16) * (I / 256) * kChunk;
+  return TLX_OK;
+}
+
+// raise a kernel's dynamic shared memory limit once (not per launch)
+int ensure_smem(const void* kern, size_t bytes, size_t& configured) {
+  if (bytes <= configured) return TLX_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) != cudaSuccess)
+    return TLX_ERR_LAUNCH;
+  configured = bytes;
+  return TLX_OK;
+}
+size_t g_router_smem = 0, g_gate_up_smem = 0, g_down_smem = 0;
+
+int launch_router(const MoeParams& p, cudaStream_t stream) {
+  const size_t smem = std::max(static_cast<size_t>(p.P) * p.H * 4,
+                               static_cast<size_t>(p.P) * (p.E + 1) * 4 + static_cast<size_t>(p.E) * 4);
+  if (smem > kSmemLimit - 4096u) return TLX_ERR_SHAPE;
+  if (ensure_smem(reinterpret_cast<const void*>(moe_router_kernel), smem, g_router_smem)) return TLX_ERR_LAUNCH;
+  const int ctas = (p.E + 1 + kRouterWarps - 1) / kRouterWarps;
+  return launch_ex(reinterpret_cast<const void*>(moe_router_kernel), dim3(ctas), dim3(kRouterWarps * 32), smem,
+                   stream, p);
+}
+
+int launch_experts(MoeParams p, cudaStream_t stream) {
+  const int C = sm_count();
+  {
+    const uint32_t img = static_cast<uint32_t>((p.H / 256) * p.P) * kRowBytes;
+    p.stages = stages_for(img, 4);
+    if (p.stages == 0) return TLX_ERR_SHAPE;
+    const uint32_t smem = exp_layout(img, p.stages).total;
+    if (ensure_smem(reinterpret_cast<const void*>(moe_gate_up_kernel), smem, g_gate_up_smem)) return TLX_ERR_LAUNCH;
+    const int rc = launch_ex(reinterpret_cast<const void*>(moe_gate_up_kernel), dim3(C), dim3(kExpWarps * 32), smem,
+                             stream, p);
+    if (rc) return rc;
+  }
+  {
+    const uint32_t img = static_cast<uint32_t>((p.I / 256) * 9 * p.P) * kRowBytes;
+    p.stages = stages_for(img, 4);
+    if (p.stages == 0) return TLX_ERR_SHAPE;
+    const uint32_t smem = exp_layout(img, p.stages).total;
+    if (ensure_smem(reinterpret_cast<const void*>(moe_down_kernel), smem, g_down_smem)) return TLX_ERR_LAUNCH;
+    return launch_ex(reinterpret_cast<const void*>(moe_down_kernel), dim3(C), dim3(kExpWarps * 32), smem, stream, p);
+  }
+}
+
+}  // namespace
+}  // namespace tlx
+
+using namespace tlx;
+
+extern "C" {
+
+size_t tlx_moe_workspace_bytes(int p, int n_experts, int hidden, int inner) {
+  if (!moe_shape_ok(p, n_experts, hidden, inner)) return 0;
+  return ws_layout(p, n_experts, hidden, inner).total;
+}
+
+int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p,
+                  int n_experts, int hidden, int inner, int expert_begin, int expert_end, int with_shared,
+                  int32_t* ids, float* gates, float* sg, void* ws, size_t ws_bytes, void* stream) {
+  if (!w_router || !w_shared_gate || !h) return TLX_ERR_NULL;
+  MoeParams in = {};
+  in.wr = w_router;
+  in.wsh = w_shared_gate;
+  in.h = static_cast<const uint16_t*>(h);
+  in.ldh = ldh;
+  in.ids_out = ids;
+  in.gates_out = gates;
+  in.sg_out = sg;
+  in.with_shared = with_shared ? 1 : 0;
+  MoeParams prm;
+  int rc = setup(in, p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, prm);
+  if (rc) return rc;
+  if (ldh < hidden || (ldh & 1) || !al(h, 4) || !al(w_router, 16) || !al(w_shared_gate, 16)) return TLX_ERR_ALIGN;
+  return launch_router(prm, static_cast<cudaStream_t>(stream));
+}
+
+int tlx_moe_experts(const void* gate, const void* up, const void* down, const void* shared_gate,
+                    const void* shared_up, const void* shared_down, const int8_t* kvalues, const float* hres,
+                    int64_t ldr, float* y, int64_t ldy, int p, int n_experts, int hidden, int inner,
+                    int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream) {
+  if (!kvalues || !y) return TLX_ERR_NULL;
+  const bool shared = shared_gate != nullptr;
+  if (shared && (!shared_up || !shared_down)) return TLX_ERR_NULL;
+  if (expert_end > expert_begin && (!gate || !up || !down)) return TLX_ERR_NULL;
+  MoeParams in = {};
+  in.gate = static_cast<const uint8_t*>(gate);
+  in.up = static_cast<const uint8_t*>(up);
+  in.down = static_cast<const uint8_t*>(down);
+  in.sgate = static_cast<const uint8_t*>(shared_gate);
+  in.sup = static_cast<const uint8_t*>(shared_up);
+  in.sdown = static_cast<const uint8_t*>(shared_down);
+  in.kvalues = kvalues;
+  in.hres = hres;
+  in.ldr = ldr;
+  in.y = y;
+  in.ldy = ldy;
+  in.with_shared = shared ? 1 : 0;
+  MoeParams prm;
+  int rc = setup(in, p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, prm);
+  if (rc) return rc;
+  for (const void* q : {gate, up, down, shared_gate, shared_up, shared_down})
+    if (q && !al(q, 16)) return TLX_ERR_ALIGN;
+  if (ldy < hidden || (hres && ldr < hidden)) return TLX_ERR_SHAPE;
+  return launch_experts(prm, static_cast<cudaStream_t>(stream));
+}
+
+int tlx_moe_verify(const float* w_router, const float* w_shared_gate, const void* gate, const void* up,
+                   const void* down, const void* shared_gate, const void* shared_up, const void* shared_down,
+                   const int8_t* kvalues, const void* h, int64_t ldh, const float* hres, int64_t ldr, float* y,
+                   int64_t ldy, int32_t* ids, float* gates, float* sg, int p, int n_experts, int hidden, int inner,
+                   int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream) {
+  int rc = tlx_moe_route(w_router, w_shared_gate, h, ldh, p, n_experts, hidden, inner, expert_begin, expert_end,
+                         shared_gate != nullptr, ids, gates, sg, ws, ws_bytes, stream);
+  if (rc) return rc;
+  return tlx_moe_experts(gate, up, down, shared_gate, shared_up, shared_down, kvalues, hres, ldr, y, ldy, p,
+                         n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, stream);
+}
+
+int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, int inner, uint32_t* err_out,
+                            void* stream) {
+  if (!ws || !err_out) return TLX_ERR_NULL;
+  if (!moe_shape_ok(p, n_experts, hidden, inner)) return TLX_ERR_SHAPE;
+  const WsLayout w = ws_layout(p, n_experts, hidden, inner);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(err_out, static_cast<const uint8_t*>(ws) + w.err, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return TLX_ERR_LAUNCH;
+  return cudaStreamSynchronize(s) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+}  // extern "C"
