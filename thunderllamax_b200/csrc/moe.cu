@@ -2,21 +2,24 @@
 // experts, combine.  Three launches chained with programmatic dependent launch:
 //
 //   moe_router_kernel   logits = W_r h (fp32) for all experts plus the shared-expert
-//                       gate row; the last CTA to finish picks the top-8 per position
-//                       (8 masked-argmax passes, strict '>', ties to the lower id),
-//                       gates = softmax over the 8, sg = sigmoid(w_sh . h), and builds
+//                       gate row (one warp per row), and h staged as the fp16
+//                       activation image of the gate/up projection.
+//   moe_gate_up_kernel  every CTA first picks the top-8 per position from the logits
+//                       (8 masked-argmax passes, strict '>', ties to the lower id;
+//                       gates = softmax over the 8; sg = sigmoid(w_sh . h)) and builds
 //                       the SLOT list: one slot per distinct routed expert of this
 //                       rank's range (ascending id) with the positions routed to it,
-//                       then the shared expert.  The CTAs also stage h as the fp16
-//                       activation image the expert kernel reads.
-//   moe_gate_up_kernel  per (slot, 16-row tile): gate and up over all of h for the
-//                       slot's positions, act = silu(g) * u in fp32 plus a running
-//                       max |act| per (position, expert) pair.
-//   moe_down_kernel     builds the fp16 activation image of act with one power-of-two
-//                       scale per pair (act can exceed the fp16 range; the scale
-//                       keeps max |act| at 2^14), then per (slot, 16-row tile of the
-//                       hidden dim): down over act into fp32 parts[pair][row] (scale
-//                       undone exactly); the last slot to finish a tile combines it:
+//                       then the shared expert.  All CTAs compute the same list (no
+//                       serial step); CTA 0 publishes it.  Then per (slot, 16-row
+//                       tile): gate and up for the slot's positions, act = silu(g) u
+//                       in fp32 with a running max |act| per (position, expert) pair;
+//                       the last tile of a slot turns the slot's act into the fp16
+//                       activation image of the down projection with one power-of-two
+//                       scale per pair (act can exceed the fp16 range; the scale keeps
+//                       max |act| at 2^14).
+//   moe_down_kernel     per (slot, 16-row tile of the hidden dim): down over act into
+//                       fp32 parts[pair][row] (scale undone exactly); the last slot to
+//                       finish a tile combines it:
 //                       y = hres + sum_r gates[r] part_r + sg * shared (r ascending).
 //
 // Reference chain engine/mm/MM_P7_lib.py:505-511: rt8e256 (engine/mm/MM_P1_rt8e256.cu:
@@ -52,7 +55,8 @@ constexpr int kMaxPos = 8;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxSlots = kTopK * kMaxPos + 1;  // distinct routed experts <= 8 P, + shared
 constexpr int kExpWarps = 16;                   // warps per expert-kernel CTA
-constexpr int kRouterWarps = 8;                 // experts per router CTA
+constexpr int kRouterWarps = 4;                 // experts per router CTA
+constexpr int kKeysPerLane = 8;                 // register-resident selection keys (E <= 256)
 constexpr uint32_t kLutBytes = 256u * 256u;     // entry v at 256 v, lane word at + 4 lane
 constexpr uint32_t kRow = 68;                   // uint2 entries per image row (64 + 4 pad)
 constexpr uint32_t kRowBytes = kRow * 8u;
@@ -127,19 +131,12 @@ struct MoeParams {
   float* parts;    // [9P][H]
 };
 
-// ---- activation image position of k (IQ4 k order) ----
+// ---- activation image (IQ4 k order) ----
 // mma m of lane quarter q takes the byte pair 2m, 2m+1 of the quarter's 32 qs bytes:
 // sub-block 2q + (m >> 3), bytes j0 = 2 (m & 7), j0 + 1, i.e. the weights
 // k0 = 64q + 32 (m >> 3) + 2 (m & 7) and k0 + 16 (lo / hi nibble of byte j0), k0 + 1
-// and k0 + 17 (byte j0 + 1).  Entry (m, q) = fp16 {x[k0], x[k0+16], x[k0+1], x[k0+17]}.
-__host__ __device__ __forceinline__ void iq4_image_pos(int k, int& b, int& m, int& q, int& pos) {
-  b = k >> 8;
-  const int kin = k & 255;
-  q = kin >> 6;
-  const int r = kin & 63;
-  m = 8 * (r >> 5) + ((r & 15) >> 1);
-  pos = 2 * (r & 1) + ((r >> 4) & 1);
-}
+// and k0 + 17 (byte j0 + 1).  Entry (m, q) of a 256-k block and column holds fp16
+// {x[k0], x[k0+16], x[k0+1], x[k0+17]}; rows of 64 entries padded to 68.
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
@@ -244,60 +241,72 @@ __device__ __forceinline__ void build_lut(uint8_t* lut, const int8_t* kvalues) {
 }
 
 // ---------------------------------------------------------------------------- router
+// Shared memory: [kRouterWarps][H] fp32 router rows | [P][H] bf16 h | barriers.
+__host__ __device__ inline uint32_t router_smem_bytes(int P, int H) {
+  return static_cast<uint32_t>(kRouterWarps * H * 4 + P * H * 2 + (kRouterWarps + 1) * 8);
+}
+
 __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const MoeParams p) {
-  extern __shared__ __align__(16) float rsm[];
-  float* hs = rsm;  // [P][H] fp32
-  __shared__ uint32_t is_last;
-  __shared__ int s_ids[kMaxPos * kTopK];
-  __shared__ int warp_tot[kRouterWarps];
-  __shared__ int n_routed_s;
+  extern __shared__ __align__(128) uint8_t rsm[];
   const int P = p.P, H = p.H, E = p.E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* rows = reinterpret_cast<float*>(rsm);
+  uint16_t* hs = reinterpret_cast<uint16_t*>(rsm + kRouterWarps * H * 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rsm + kRouterWarps * H * 4 + P * H * 2);
+  uint64_t* hbar = bars + kRouterWarps;
+  const int e = blockIdx.x * kRouterWarps + warp;  // this warp's row: an expert, or (e == E) the shared gate
+  if (threadIdx.x == 0) {
+    for (int w = 0; w <= kRouterWarps; ++w) mbar_init(&bars[w], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // the router rows are constants: fetch them before waiting for the previous kernel
+  if (lane == 0 && e <= E) {
+    const float* row = e < E ? p.wr + static_cast<int64_t>(e) * H : p.wsh;
+    mbar_arrive_expect_tx(&bars[warp], static_cast<uint32_t>(H * 4));
+    bulk_g2s(rows + warp * H, row, static_cast<uint32_t>(H * 4), &bars[warp]);
+  }
   griddep_wait();
   griddep_launch_dependents();
 
-  // the previous step's down kernel has finished with the act maxima: re-arm them
+  // the previous step's expert kernels have finished with the act maxima: re-arm them
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < 9 * P; i += blockDim.x) p.amax[i] = 0u;
-  for (int i = threadIdx.x; i < P * (H >> 1); i += blockDim.x) {
-    const int t = i / (H >> 1), k2 = i - t * (H >> 1);
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(p.h + t * p.ldh + 2 * k2);
-    hs[t * H + 2 * k2] = __uint_as_float(v << 16);
-    hs[t * H + 2 * k2 + 1] = __uint_as_float(v & 0xFFFF0000u);
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(hbar, static_cast<uint32_t>(P * H * 2));
+    for (int t = 0; t < P; ++t) bulk_g2s(hs + t * H, p.h + t * p.ldh, static_cast<uint32_t>(H * 2), hbar);
   }
-  __syncthreads();
+  bool ok = mbar_wait_bounded(hbar, 0, threadIdx.x == 0 ? p.err : nullptr);
   // this CTA's share of the fp16 activation image of h (bf16 -> fp16, exact in range)
-  {
+  if (ok) {
     const int per_tok = H >> 2;
+    auto f16 = [&](const uint16_t* q) {
+      return static_cast<uint32_t>(f32_to_f16_bits(__uint_as_float(static_cast<uint32_t>(*q) << 16)));
+    };
     for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < P * per_tok; gi += gridDim.x * blockDim.x) {
-      const int t = gi / per_tok, e = gi - t * per_tok;
-      const int b = e >> 6, m = (e & 63) >> 2, q = e & 3;
-      const float* hr = hs + t * H + 256 * b + 64 * q + 32 * (m >> 3) + 2 * (m & 7);
-      const uint32_t lo =
-          static_cast<uint32_t>(f32_to_f16_bits(hr[0])) | (static_cast<uint32_t>(f32_to_f16_bits(hr[16])) << 16);
-      const uint32_t hi =
-          static_cast<uint32_t>(f32_to_f16_bits(hr[1])) | (static_cast<uint32_t>(f32_to_f16_bits(hr[17])) << 16);
-      p.ximg[(b * P + t) * kRow + m * 4 + q] = make_uint2(lo, hi);
+      const int t = gi / per_tok, ei = gi - t * per_tok;
+      const int b = ei >> 6, m = (ei & 63) >> 2, q = ei & 3;
+      const uint16_t* hr = hs + t * H + 256 * b + 64 * q + 32 * (m >> 3) + 2 * (m & 7);
+      p.ximg[(b * P + t) * kRow + m * 4 + q] = make_uint2(f16(hr) | (f16(hr + 16) << 16), f16(hr + 1) | (f16(hr + 17) << 16));
     }
   }
-
-  // one router row per warp: experts, then the shared-expert gate row (e == E)
-  const int e = blockIdx.x * kRouterWarps + warp;
-  if (e <= E) {
-    const float* row = e < E ? p.wr + static_cast<int64_t>(e) * H : p.wsh;
+  // one router row per warp, fp32 FMAs in k order per lane, then a fixed shuffle tree
+  const bool row_ok = e <= E && mbar_wait_bounded(&bars[warp], 0, lane == 0 ? p.err : nullptr);
+  if (ok && row_ok) {
+    const float* row = rows + warp * H;
     float acc[kMaxPos];
 #pragma unroll
     for (int t = 0; t < kMaxPos; ++t) acc[t] = 0.f;
     for (int k = 4 * lane; k < H; k += 128) {
-      const float4 w = __ldg(reinterpret_cast<const float4*>(row + k));
+      const float4 w = *reinterpret_cast<const float4*>(row + k);
 #pragma unroll
       for (int t = 0; t < kMaxPos; ++t)
         if (t < P) {
-          const float4 x = *reinterpret_cast<const float4*>(hs + t * H + k);
-          acc[t] = fmaf(w.x, x.x, acc[t]);
-          acc[t] = fmaf(w.y, x.y, acc[t]);
-          acc[t] = fmaf(w.z, x.z, acc[t]);
-          acc[t] = fmaf(w.w, x.w, acc[t]);
+          const uint2 xb = *reinterpret_cast<const uint2*>(hs + t * H + k);
+          acc[t] = fmaf(w.x, __uint_as_float(xb.x << 16), acc[t]);
+          acc[t] = fmaf(w.y, __uint_as_float(xb.x & 0xFFFF0000u), acc[t]);
+          acc[t] = fmaf(w.z, __uint_as_float(xb.y << 16), acc[t]);
+          acc[t] = fmaf(w.w, __uint_as_float(xb.y & 0xFFFF0000u), acc[t]);
         }
     }
 #pragma unroll
@@ -309,121 +318,175 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const Moe
         if (lane == 0) p.logits[t * (E + 1) + e] = v;
       }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&p.meta->router_done, 1u) == gridDim.x - 1 ? 1u : 0u;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+}
 
-  // ---- the last CTA: top-8, gates, sg, slot list ----
-  MoeMeta* mt = p.meta;
-  float* lg = rsm;                                                     // [P][E + 1] (reuses the h area)
-  uint32_t* tokmask = reinterpret_cast<uint32_t*>(rsm + P * (E + 1));  // [E]
-  for (int i = threadIdx.x; i < P * (E + 1); i += blockDim.x) lg[i] = __ldcg(p.logits + i);
-  for (int i = threadIdx.x; i < E; i += blockDim.x) tokmask[i] = 0u;
+// ------------------------------------------------------------------ expert selection
+// Shared-memory scratch of the selection: logits [P][E + 1] fp32, then one word per
+// expert: bit t = position t routed to it, bits 8 + 3t .. 10 + 3t = its rank there.
+__host__ __device__ inline uint32_t sel_scratch_bytes(int P, int E) { return static_cast<uint32_t>((P * (E + 1) + E) * 4); }
+
+// Top-8 of every position, gates and sg, then the slot list into `sc`: the shared
+// expert first (slot 0; its weights are known before routing), then one slot per
+// distinct routed expert of [e0, e1) in ascending id.  Called by every thread of the
+// CTA; `publish` writes the routing and the slot list to the workspace and the
+// caller's outputs.  Positions are independent warps; each of the 8 rounds is one
+// masked argmax over the logits (two warp max-reductions of the packed key: the
+// value bits, then the lowest index among equal values).
+__device__ void select_experts(const MoeParams& p, uint8_t* scratch, SlotCache& sc, bool publish) {
+  const int P = p.P, E = p.E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  float* lgs = reinterpret_cast<float*>(scratch);
+  uint32_t* info = reinterpret_cast<uint32_t*>(lgs + P * (E + 1));
+  for (int i = threadIdx.x; i < P * (E + 1); i += blockDim.x) lgs[i] = __ldcg(p.logits + i);
+  for (int i = threadIdx.x; i < E; i += blockDim.x) info[i] = 0u;
   __syncthreads();
-  for (int t = warp; t < P; t += kRouterWarps) {
-    float* l = lg + t * (E + 1);
-    float vals[kTopK];
+  MoeMeta* mt = p.meta;
+  for (int t = warp; t < P; t += nwarps) {
+    float* l = lgs + t * (E + 1);
     int ids[kTopK];
+    float vals[kTopK];
+    if (E <= 32 * kKeysPerLane) {
+      // keys of this lane's experts (lane + 32 j) stay in registers across the rounds
+      uint64_t key[kKeysPerLane];
+#pragma unroll
+      for (int j = 0; j < kKeysPerLane; ++j) {
+        const int x = lane + 32 * j;
+        key[j] = x < E ? argmax_key(l[x], static_cast<uint32_t>(x)) : 0ull;
+      }
+#pragma unroll
+      for (int r = 0; r < kTopK; ++r) {
+        uint64_t best = key[0];
+#pragma unroll
+        for (int j = 1; j < kKeysPerLane; ++j) best = key[j] > best ? key[j] : best;
+        const uint32_t hi = static_cast<uint32_t>(best >> 32), lo = static_cast<uint32_t>(best);
+        const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+        const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+        const uint64_t w = (static_cast<uint64_t>(mh) << 32) | ml;
+#pragma unroll
+        for (int j = 0; j < kKeysPerLane; ++j) key[j] = key[j] == w ? 0ull : key[j];  // never selected again
+        ids[r] = key_index(w);
+        vals[r] = key_value(w);
+      }
+    } else {
+#pragma unroll 1
+      for (int r = 0; r < kTopK; ++r) {
+        uint64_t best = 0ull;
+        for (int x = lane; x < E; x += 32) {
+          const uint64_t k = argmax_key(l[x], static_cast<uint32_t>(x));
+          best = k > best ? k : best;
+        }
+        const uint32_t hi = static_cast<uint32_t>(best >> 32), lo = static_cast<uint32_t>(best);
+        const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+        const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+        const uint64_t w = (static_cast<uint64_t>(mh) << 32) | ml;
+        ids[r] = key_index(w);
+        vals[r] = key_value(w);
+        __syncwarp();
+        if (lane == (ids[r] & 31)) l[ids[r]] = __uint_as_float(0x7FC00000u);  // NaN: never selected again
+        __syncwarp();
+      }
+    }
+    const float mx = vals[0];
+    float ex[kTopK], s = 0.f;
 #pragma unroll
     for (int r = 0; r < kTopK; ++r) {
-      uint64_t best = 0ull;
-      for (int x = lane; x < E; x += 32) {
-        const uint64_t k = argmax_key(l[x], static_cast<uint32_t>(x));
-        best = k > best ? k : best;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const uint64_t k = __shfl_xor_sync(0xffffffffu, best, o);
-        best = k > best ? k : best;
-      }
-      ids[r] = key_index(best);
-      vals[r] = l[ids[r]];
-      __syncwarp();
-      if (lane == 0) l[ids[r]] = __uint_as_float(0x7FC00000u);  // NaN: never selected again
-      __syncwarp();
+      ex[r] = expf(vals[r] - mx);
+      s += ex[r];
     }
-    if (lane == 0) {
-      const float mx = vals[0];
-      float ex[kTopK], s = 0.f;
+    if (lane < kTopK) {  // lane r publishes rank r
+      float g = 0.f;
+      int id = 0;
 #pragma unroll
-      for (int r = 0; r < kTopK; ++r) {
-        ex[r] = expf(vals[r] - mx);
-        s += ex[r];
+      for (int r = 0; r < kTopK; ++r)
+        if (r == lane) {
+          g = ex[r] / s;
+          id = ids[r];
+        }
+      if (id >= p.e0 && id < p.e1) atomicOr(&info[id], (1u << t) | (static_cast<uint32_t>(lane) << (8 + 3 * t)));
+      if (publish) {
+        mt->ids[t * kTopK + lane] = id;
+        mt->gates[t * kTopK + lane] = g;
+        if (p.ids_out) p.ids_out[t * kTopK + lane] = id;
+        if (p.gates_out) p.gates_out[t * kTopK + lane] = g;
       }
-#pragma unroll
-      for (int r = 0; r < kTopK; ++r) {
-        const float g = ex[r] / s;
-        s_ids[t * kTopK + r] = ids[r];
-        mt->ids[t * kTopK + r] = ids[r];
-        mt->gates[t * kTopK + r] = g;
-        if (p.ids_out) p.ids_out[t * kTopK + r] = ids[r];
-        if (p.gates_out) p.gates_out[t * kTopK + r] = g;
-        if (ids[r] >= p.e0 && ids[r] < p.e1) atomicOr(&tokmask[ids[r]], 1u << t);
-      }
-      const float a = l[E];
-      const float sgv = 1.0f / (1.0f + expf(-a));
+    }
+    if (lane == 0 && publish) {
+      const float sgv = 1.0f / (1.0f + expf(-l[E]));
       mt->sg[t] = sgv;
       if (p.sg_out) p.sg_out[t] = sgv;
     }
   }
   __syncthreads();
-  // slots in ascending expert id: block-wide exclusive scan of the used flags
-  const int per = (E + blockDim.x - 1) / blockDim.x;
-  const int x0 = threadIdx.x * per;
-  int c = 0;
-  for (int x = x0; x < x0 + per && x < E; ++x) c += tokmask[x] ? 1 : 0;
-  int incl = c;
+  // slot list, built by warp 0: lane L owns experts [L per, (L + 1) per), a warp scan
+  // gives each lane its first slot
+  if (warp == 0) {
+    const int first = p.with_shared ? 1 : 0;
+    const int per = (E + 31) >> 5;
+    const int x0 = lane * per, x1 = min(E, x0 + per);
+    int c = 0;
+    for (int x = x0; x < x1; ++x) c += info[x] ? 1 : 0;
+    int incl = c;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int u = first + incl - c;
+    for (int x = x0; x < x1; ++x)
+      if (info[x]) sc.expert[u++] = static_cast<int16_t>(x);
+    const int nr = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      if (p.with_shared) {
+        sc.expert[0] = -1;
+        sc.count[0] = static_cast<uint8_t>(P);
+        for (int t = 0; t < 8; ++t) {
+          const int tt = t < P ? t : 0;
+          sc.tok[0][t] = static_cast<uint8_t>(tt);
+          sc.pair[0][t] = static_cast<uint8_t>(kTopK * P + tt);
+        }
+      }
+      sc.n_slots = nr + first;
+    }
   }
-  if (lane == 31) warp_tot[warp] = incl;
   __syncthreads();
-  int base = 0;
-  for (int w = 0; w < warp; ++w) base += warp_tot[w];
-  int u = base + incl - c;
-  for (int x = x0; x < x0 + per && x < E; ++x) {
-    const uint32_t mk = tokmask[x];
-    if (!mk) continue;
-    mt->slot_expert[u] = static_cast<int16_t>(x);
-    uint8_t tok[8], pair[8];
+  // columns of every routed slot: positions ascending, unused columns repeat column 0
+  for (int u = (p.with_shared ? 1 : 0) + threadIdx.x; u < sc.n_slots; u += blockDim.x) {
+    const uint32_t in = info[sc.expert[u]];
     int n = 0;
     for (int t = 0; t < P; ++t)
-      if (mk & (1u << t)) {
-        int r = 0;
-        while (r < kTopK && s_ids[t * kTopK + r] != x) ++r;
-        tok[n] = static_cast<uint8_t>(t);
-        pair[n] = static_cast<uint8_t>(t * kTopK + r);
+      if (in & (1u << t)) {
+        sc.tok[u][n] = static_cast<uint8_t>(t);
+        sc.pair[u][n] = static_cast<uint8_t>(t * kTopK + ((in >> (8 + 3 * t)) & 7u));
         ++n;
       }
-    for (int c2 = 0; c2 < 8; ++c2) {
-      mt->slot_tok[u][c2] = c2 < n ? tok[c2] : tok[0];
-      mt->slot_pair[u][c2] = c2 < n ? pair[c2] : pair[0];
+    sc.count[u] = static_cast<uint8_t>(n);
+    for (int c2 = n; c2 < 8; ++c2) {
+      sc.tok[u][c2] = sc.tok[u][0];
+      sc.pair[u][c2] = sc.pair[u][0];
     }
-    mt->slot_count[u] = static_cast<uint8_t>(n);
-    ++u;
   }
-  if (threadIdx.x == blockDim.x - 1) n_routed_s = base + incl;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int nr = n_routed_s;
-    mt->n_routed = nr;
-    if (p.with_shared) {
-      mt->slot_expert[nr] = -1;
-      mt->slot_count[nr] = static_cast<uint8_t>(P);
-      for (int t = 0; t < 8; ++t) {
-        const int tt = t < P ? t : 0;
-        mt->slot_tok[nr][t] = static_cast<uint8_t>(tt);
-        mt->slot_pair[nr][t] = static_cast<uint8_t>(kTopK * P + tt);
+  if (publish) {
+    for (int i = threadIdx.x; i < sc.n_slots; i += blockDim.x) {
+      mt->slot_expert[i] = sc.expert[i];
+      mt->slot_count[i] = sc.count[i];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        mt->slot_tok[i][c] = sc.tok[i][c];
+        mt->slot_pair[i][c] = sc.pair[i][c];
       }
     }
-    mt->n_slots = nr + (p.with_shared ? 1 : 0);
-    mt->router_done = 0u;
+    if (threadIdx.x == 0) mt->n_slots = sc.n_slots;
   }
+}
+
+// routing alone (tlx_moe_route): one CTA publishes ids / gates / sg and the slots
+__global__ void __launch_bounds__(256) moe_select_kernel(const MoeParams p) {
+  extern __shared__ __align__(16) uint8_t ssm[];
+  __shared__ SlotCache sc;
+  griddep_wait();
+  griddep_launch_dependents();
+  select_experts(p, ssm, sc, true);
 }
 
 // ------------------------------------------------------------- expert kernels (shared)
@@ -482,6 +545,11 @@ __device__ __forceinline__ void ring_drain(Ring& R) {
 }
 
 // ------------------------------------------------------------------- gate/up kernel
+// Work split: the CTA's items are k = 0..Kc-1 (global item blockIdx.x + C k, i.e.
+// slot i / tiles, tile i % tiles); their units (item, 256-block) are divided evenly
+// over the 16 warps, so every warp streams about the same number of chunk pairs.  An
+// item wholly inside one warp's range is finished by that warp; an item split across
+// warps is summed (in warp order, deterministic) by the warp holding its last unit.
 __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const MoeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ SlotCache sc;
@@ -493,14 +561,12 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   uint2* xs = reinterpret_cast<uint2*>(smem + L.img);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + L.bars) + kExpWarps * S;
-  Ring R;
-  R.ring = smem + L.ring + static_cast<uint32_t>(warp * S) * kChunk;
-  R.bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * S;
-  R.S = S;
+  uint8_t* ring = smem + L.ring + static_cast<uint32_t>(warp * S) * kChunk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * S;
 
   build_lut(smem, p.kvalues);
   if (lane == 0)
-    for (int s = 0; s < S; ++s) mbar_init(&R.bars[s], 1);
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
   if (threadIdx.x == 0) mbar_init(xbar, 1);
   mbar_fence_init();
 
@@ -508,80 +574,163 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   // the router, so wait for it to complete
   griddep_wait();
   griddep_launch_dependents();
-  load_slots(p.meta, sc);
-  __syncthreads();
-
-  const int n_items = sc.n_slots * tpe;
-  // only CTAs with work copy the image (warp 0 holds the CTA's first item and waits)
-  if (threadIdx.x == 0 && static_cast<int>(blockIdx.x) < n_items) {
+  // every warp waits for the activation image; copy it while the experts are selected
+  if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(xbar, img_bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg);
     for (uint32_t off = 0; off < img_bytes; off += 32768u)
       bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, std::min(32768u, img_bytes - off), xbar);
   }
-  const int i_first = blockIdx.x + gridDim.x * warp;
-  R.issued = R.consumed = 0;
-  R.item = i_first;
-  R.j = 0;
-  R.n_items = n_items;
-  R.step = gridDim.x * kExpWarps;
-  R.per_item = 2 * nbh;
-  R.nmat = 2;
-  auto base_of = [&](int item, const uint8_t*& b0, const uint8_t*& b1) {
-    const int u = item / tpe, tau = item - u * tpe;
-    const int e = sc.expert[u];
-    const int64_t off = static_cast<int64_t>(tau) * nbh * kChunk;
-    b0 = (e >= 0 ? p.gate + static_cast<int64_t>(e) * p.gu_bytes : p.sgate) + off;
-    b1 = (e >= 0 ? p.up + static_cast<int64_t>(e) * p.gu_bytes : p.sup) + off;
+  // selection scratch: the weight rings (idle until the slot list exists)
+  select_experts(p, smem + L.ring, sc, blockIdx.x == 0);
+  fence_proxy_async_smem();  // the scratch is overwritten by bulk copies next
+  __syncthreads();
+
+  const int C = gridDim.x;
+  const int n_items = sc.n_slots * tpe;
+  const int Kc = static_cast<int>(blockIdx.x) < n_items ? (n_items - 1 - static_cast<int>(blockIdx.x)) / C + 1 : 0;
+  const int Uc = Kc * nbh;
+  const int v0 = warp * Uc / kExpWarps, v1 = (warp + 1) * Uc / kExpWarps;
+  auto warp_of_unit = [&](int v) { return static_cast<int>((static_cast<int64_t>(v + 1) * kExpWarps - 1) / Uc); };
+
+  // chunk stream of this warp: units v0..v1, each gate then up
+  int iv = v0, ij = 0;
+  int64_t issued = 0, consumed = 0;
+  auto issue = [&]() {
+    while (iv < v1 && issued < consumed + S) {
+      const int k = iv / nbh, b = iv - k * nbh;
+      const int i = static_cast<int>(blockIdx.x) + C * k;
+      const int u = i / tpe, tau = i - u * tpe;
+      const int e = sc.expert[u];
+      const uint8_t* base = ij == 0 ? (e >= 0 ? p.gate + static_cast<int64_t>(e) * p.gu_bytes : p.sgate)
+                                    : (e >= 0 ? p.up + static_cast<int64_t>(e) * p.gu_bytes : p.sup);
+      const int slot = static_cast<int>(issued % S);
+      mbar_arrive_expect_tx(&bars[slot], kChunk);
+      bulk_g2s(ring + slot * kChunk, base + (static_cast<int64_t>(tau) * nbh + b) * kChunk, kChunk, &bars[slot]);
+      ++issued;
+      if (++ij == 2) {
+        ij = 0;
+        ++iv;
+      }
+    }
   };
-  if (lane == 0) ring_issue(R, base_of);
+  if (lane == 0) issue();
   __syncwarp();
 
-  bool failed = false;
-  if (i_first < n_items) failed = !mbar_wait_bounded(xbar, 0, lane == 0 ? p.err : nullptr);
+  // every warp waits for the image (the copy must land before the CTA exits)
+  bool failed = !mbar_wait_bounded(xbar, 0, lane == 0 ? p.err : nullptr);
 
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
   const int g = lane >> 2, qq = lane & 3;
-  for (int item = i_first; item < n_items && !failed; item += R.step) {
-    const int u = item / tpe, tau = item - u * tpe;
+
+  // item epilogue on complete sums: act = silu(g) * u (fp32) and the running max |act|
+  // per pair (the down kernel scales each pair's act into fp16 range)
+  auto epilogue = [&](int k, const float (&ag)[4], const float (&au)[4]) {
+    const int i = static_cast<int>(blockIdx.x) + C * k;
+    const int u = i / tpe, tau = i - u * tpe;
     const int cnt = sc.count[u];
-    const uint2* xl = xs + sc.tok[u][g] * kRow + qq;
-    float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int b = 0; b < nbh; ++b) {
-      const int64_t c0 = R.consumed;
-      if (!ring_wait(R, c0, lane == 0 ? p.err : nullptr) || !ring_wait(R, c0 + 1, lane == 0 ? p.err : nullptr)) {
-        failed = true;
-        break;
-      }
-      iq4_pair_mma(R.ring + (c0 % S) * kChunk, R.ring + ((c0 + 1) % S) * kChunk, xl + b * P * kRow, lut, lane4, lane,
-                   ag, au);
-      R.consumed = c0 + 2;
-      // refill (after the stages' last generic-proxy reads)
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) ring_issue(R, base_of);
-      __syncwarp();
-    }
-    if (failed) break;
-    // act = silu(g) * u (fp32) and the per-pair running max |act|
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       const int col = 2 * qq + h2;
-      const float v0 = silu_f(ag[h2]) * au[h2];          // row g
-      const float v1 = silu_f(ag[2 + h2]) * au[2 + h2];  // row g + 8
-      float mx = fmaxf(fabsf(v0), fabsf(v1));
+      const float a0 = silu_f(ag[h2]) * au[h2];          // row g
+      const float a1 = silu_f(ag[2 + h2]) * au[2 + h2];  // row g + 8
+      float mx = fmaxf(fabsf(a0), fabsf(a1));
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       if (col < cnt) {
         const int pair = sc.pair[u][col];
         float* dst = p.actf + static_cast<int64_t>(pair) * p.I + tau * 16 + g;
-        dst[0] = v0;
-        dst[8] = v1;
+        dst[0] = a0;
+        dst[8] = a1;
         if (g == 0) atomicMax(p.amax + pair, __float_as_uint(mx));
       }
     }
+  };
+
+  // partial pieces (items split across warps): [0] the warp's first item, [1] its last
+  float stash0[8], stash1[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) stash0[e] = stash1[e] = 0.f;
+  float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+  int cur_k = -1, piece_v = v0;
+  const uint2* xl = xs;
+  auto finish_piece = [&](int k, int vs, int ve) {
+    if (vs == k * nbh && ve == (k + 1) * nbh) {
+      epilogue(k, ag, au);
+    } else {
+      if (k == v0 / nbh) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          stash0[e] = ag[e];
+          stash0[4 + e] = au[e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          stash1[e] = ag[e];
+          stash1[4 + e] = au[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ag[e] = au[e] = 0.f;
+  };
+  for (int v = v0; v < v1 && !failed; ++v) {
+    const int k = v / nbh, b = v - k * nbh;
+    if (k != cur_k) {
+      if (cur_k >= 0) finish_piece(cur_k, piece_v, v);
+      cur_k = k;
+      piece_v = v;
+      const int i = static_cast<int>(blockIdx.x) + C * k;
+      xl = xs + sc.tok[i / tpe][g] * kRow + qq;
+    }
+    const int64_t c0 = consumed;
+    if (!mbar_wait_bounded(&bars[c0 % S], static_cast<uint32_t>((c0 / S) & 1), lane == 0 ? p.err : nullptr) ||
+        !mbar_wait_bounded(&bars[(c0 + 1) % S], static_cast<uint32_t>(((c0 + 1) / S) & 1),
+                           lane == 0 ? p.err : nullptr)) {
+      failed = true;
+      break;
+    }
+    iq4_pair_mma(ring + (c0 % S) * kChunk, ring + ((c0 + 1) % S) * kChunk, xl + b * P * kRow, lut, lane4, lane, ag,
+                 au);
+    consumed = c0 + 2;
+    // refill (after the stages' last generic-proxy reads)
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) issue();
+    __syncwarp();
   }
-  if (failed) ring_drain(R);
+  if (failed) {
+    // let every copy this warp issued land before the CTA can exit
+    for (int64_t c = consumed; c < issued; ++c)
+      mbar_wait_bounded(&bars[c % S], static_cast<uint32_t>((c / S) & 1), nullptr);
+  } else if (cur_k >= 0) {
+    finish_piece(cur_k, piece_v, v1);
+  }
+  // pieces of split items -> this warp's own (now idle) ring, then the owners sum them
+  float* pieces = reinterpret_cast<float*>(ring);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    pieces[e * 32 + lane] = stash0[e];
+    pieces[(8 + e) * 32 + lane] = stash1[e];
+  }
+  __syncthreads();
+  if (failed || Uc == 0) return;
+  for (int k = 0; k < Kc; ++k) {
+    const int wf = warp_of_unit(k * nbh), wl = warp_of_unit((k + 1) * nbh - 1);
+    if (wl != warp || wf == wl) continue;
+    float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = wf; w <= wl; ++w) {
+      const float* pw = reinterpret_cast<const float*>(smem + L.ring + static_cast<uint32_t>(w * S) * kChunk);
+      const int a = (k == (w * Uc / kExpWarps) / nbh) ? 0 : 1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sg[e] += pw[(a * 8 + e) * 32 + lane];
+        su[e] += pw[(a * 8 + 4 + e) * 32 + lane];
+      }
+    }
+    epilogue(k, sg, su);
+  }
 }
 
 // --------------------------------------------------------------- down + combine kernel
@@ -637,8 +786,8 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   };
   // weights do not depend on act: start streaming before the image is built
   if (lane == 0) ring_issue(R, base_of);
-
-  // act image with one power-of-two scale per pair: max |act| * scale <= 2^14
+  // act image with one power-of-two scale per pair (max |act| * scale <= 2^14);
+  // every CTA builds it from the fp32 act, 12 float4 loads in flight per thread
   for (int i = threadIdx.x; i < npair; i += blockDim.x) {
     const float mx = __uint_as_float(__ldcg(p.amax + i));
     int ex = 0;
@@ -646,20 +795,35 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
     s_inv[i] = ldexpf(1.0f, ex - 14);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < npair * (I >> 2); i += blockDim.x) {
-    const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(p.actf + static_cast<int64_t>(pair) * I + k));
-    const float scl = 1.0f / s_inv[pair];  // exact: a power of two
-    const float vv[4] = {v.x, v.y, v.z, v.w};
+  {
+    const int n4 = npair * (I >> 2);
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 12 * blockDim.x) {
+      float4 v[12];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int bi, m, q4, pos;
-      iq4_image_pos(k + e, bi, m, q4, pos);
-      reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] = f32_to_f16_bits(vv[e] * scl);
+      for (int j = 0; j < 12; ++j) {
+        const int i = i0 + j * blockDim.x;
+        v[j] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(p.actf) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        const int i = i0 + j * blockDim.x;
+        if (i < n4) {
+          const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
+          const float scl = 1.0f / s_inv[pair];  // exact: a power of two
+          const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // position of k + e in the image: block, mma m, quarter q, half within the entry
+            const int kk = k + e, bi = kk >> 8, kin = kk & 255, q4 = kin >> 6, r = kin & 63;
+            const int m = 8 * (r >> 5) + ((r & 15) >> 1), pos = 2 * (r & 1) + ((r >> 4) & 1);
+            reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] =
+                f32_to_f16_bits(vv[e] * scl);
+          }
+        }
+      }
     }
   }
   __syncthreads();
-
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
   const int g = lane >> 2, qq = lane & 3;
   bool failed = false;
@@ -698,9 +862,16 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
         p.parts[static_cast<int64_t>(pair) * p.H + row] = acc[e] * s_inv[pair];
       }
     }
-    // the last slot to finish this 16-row tile combines it
-    __threadfence();
-    __syncwarp();
+  }
+  if (failed) {
+    ring_drain(R);
+    return;
+  }
+  // one fence for all of this warp's parts, then per item: the last slot to finish
+  // a 16-row tile combines it
+  __threadfence();
+  for (int item = i_first; item < n_items; item += R.step) {
+    const int tau = item % tpd;
     uint32_t old = 0;
     if (lane == 0) old = atomicAdd(p.cnt + tau, 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
@@ -827,16 +998,21 @@ int ensure_smem(const void* kern, size_t bytes, size_t& configured) {
   configured = bytes;
   return TLX_OK;
 }
-size_t g_router_smem = 0, g_gate_up_smem = 0, g_down_smem = 0;
+size_t g_router_smem = 0, g_select_smem = 0, g_gate_up_smem = 0, g_down_smem = 0;
 
 int launch_router(const MoeParams& p, cudaStream_t stream) {
-  const size_t smem = std::max(static_cast<size_t>(p.P) * p.H * 4,
-                               static_cast<size_t>(p.P) * (p.E + 1) * 4 + static_cast<size_t>(p.E) * 4);
+  const size_t smem = router_smem_bytes(p.P, p.H);
   if (smem > kSmemLimit - 4096u) return TLX_ERR_SHAPE;
   if (ensure_smem(reinterpret_cast<const void*>(moe_router_kernel), smem, g_router_smem)) return TLX_ERR_LAUNCH;
   const int ctas = (p.E + 1 + kRouterWarps - 1) / kRouterWarps;
   return launch_ex(reinterpret_cast<const void*>(moe_router_kernel), dim3(ctas), dim3(kRouterWarps * 32), smem,
                    stream, p);
+}
+
+int launch_select(const MoeParams& p, cudaStream_t stream) {
+  const size_t smem = sel_scratch_bytes(p.P, p.E);
+  if (ensure_smem(reinterpret_cast<const void*>(moe_select_kernel), smem, g_select_smem)) return TLX_ERR_LAUNCH;
+  return launch_ex(reinterpret_cast<const void*>(moe_select_kernel), dim3(1), dim3(256), smem, stream, p);
 }
 
 int launch_experts(MoeParams p, cudaStream_t stream) {
@@ -845,6 +1021,8 @@ int launch_experts(MoeParams p, cudaStream_t stream) {
     const uint32_t img = static_cast<uint32_t>((p.H / 256) * p.P) * kRowBytes;
     p.stages = stages_for(img, 4);
     if (p.stages == 0) return TLX_ERR_SHAPE;
+    // the selection scratch lives in the (not yet used) weight rings
+    if (sel_scratch_bytes(p.P, p.E) > static_cast<uint32_t>(kExpWarps * p.stages) * kChunk) return TLX_ERR_SHAPE;
     const uint32_t smem = exp_layout(img, p.stages).total;
     if (ensure_smem(reinterpret_cast<const void*>(moe_gate_up_kernel), smem, g_gate_up_smem)) return TLX_ERR_LAUNCH;
     const int rc = launch_ex(reinterpret_cast<const void*>(moe_gate_up_kernel), dim3(C), dim3(kExpWarps * 32), smem,
@@ -873,9 +1051,13 @@ size_t tlx_moe_workspace_bytes(int p, int n_experts, int hidden, int inner) {
   return ws_layout(p, n_experts, hidden, inner).total;
 }
 
-int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p,
-                  int n_experts, int hidden, int inner, int expert_begin, int expert_end, int with_shared,
-                  int32_t* ids, float* gates, float* sg, void* ws, size_t ws_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+// router logits (+ h image); with `select`, also the standalone selection launch
+int route_impl(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p, int n_experts,
+               int hidden, int inner, int expert_begin, int expert_end, int with_shared, int32_t* ids, float* gates,
+               float* sg, void* ws, size_t ws_bytes, void* stream, bool select) {
   if (!w_router || !w_shared_gate || !h) return TLX_ERR_NULL;
   MoeParams in = {};
   in.wr = w_router;
@@ -889,14 +1071,29 @@ int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void*
   MoeParams prm;
   int rc = setup(in, p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, prm);
   if (rc) return rc;
-  if (ldh < hidden || (ldh & 1) || !al(h, 4) || !al(w_router, 16) || !al(w_shared_gate, 16)) return TLX_ERR_ALIGN;
-  return launch_router(prm, static_cast<cudaStream_t>(stream));
+  if (ldh < hidden || (ldh & 7) || !al(h, 16) || !al(w_router, 16) || !al(w_shared_gate, 16)) return TLX_ERR_ALIGN;
+  rc = launch_router(prm, static_cast<cudaStream_t>(stream));
+  if (rc || !select) return rc;
+  return launch_select(prm, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" {
+
+int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p,
+                  int n_experts, int hidden, int inner, int expert_begin, int expert_end, int with_shared,
+                  int32_t* ids, float* gates, float* sg, void* ws, size_t ws_bytes, void* stream) {
+  return route_impl(w_router, w_shared_gate, h, ldh, p, n_experts, hidden, inner, expert_begin, expert_end,
+                    with_shared, ids, gates, sg, ws, ws_bytes, stream, true);
 }
 
-int tlx_moe_experts(const void* gate, const void* up, const void* down, const void* shared_gate,
-                    const void* shared_up, const void* shared_down, const int8_t* kvalues, const float* hres,
-                    int64_t ldr, float* y, int64_t ldy, int p, int n_experts, int hidden, int inner,
-                    int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+int experts_impl(const void* gate, const void* up, const void* down, const void* shared_gate, const void* shared_up,
+                 const void* shared_down, const int8_t* kvalues, const float* hres, int64_t ldr, float* y, int64_t ldy,
+                 int32_t* ids, float* gates, float* sg, int p, int n_experts, int hidden, int inner, int expert_begin,
+                 int expert_end, void* ws, size_t ws_bytes, void* stream) {
   if (!kvalues || !y) return TLX_ERR_NULL;
   const bool shared = shared_gate != nullptr;
   if (shared && (!shared_up || !shared_down)) return TLX_ERR_NULL;
@@ -913,6 +1110,9 @@ int tlx_moe_experts(const void* gate, const void* up, const void* down, const vo
   in.ldr = ldr;
   in.y = y;
   in.ldy = ldy;
+  in.ids_out = ids;
+  in.gates_out = gates;
+  in.sg_out = sg;
   in.with_shared = shared ? 1 : 0;
   MoeParams prm;
   int rc = setup(in, p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, prm);
@@ -922,17 +1122,28 @@ int tlx_moe_experts(const void* gate, const void* up, const void* down, const vo
   if (ldy < hidden || (hres && ldr < hidden)) return TLX_ERR_SHAPE;
   return launch_experts(prm, static_cast<cudaStream_t>(stream));
 }
+}  // namespace
+
+extern "C" {
+
+int tlx_moe_experts(const void* gate, const void* up, const void* down, const void* shared_gate,
+                    const void* shared_up, const void* shared_down, const int8_t* kvalues, const float* hres,
+                    int64_t ldr, float* y, int64_t ldy, int p, int n_experts, int hidden, int inner,
+                    int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream) {
+  return experts_impl(gate, up, down, shared_gate, shared_up, shared_down, kvalues, hres, ldr, y, ldy, nullptr,
+                      nullptr, nullptr, p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, stream);
+}
 
 int tlx_moe_verify(const float* w_router, const float* w_shared_gate, const void* gate, const void* up,
                    const void* down, const void* shared_gate, const void* shared_up, const void* shared_down,
                    const int8_t* kvalues, const void* h, int64_t ldh, const float* hres, int64_t ldr, float* y,
                    int64_t ldy, int32_t* ids, float* gates, float* sg, int p, int n_experts, int hidden, int inner,
                    int expert_begin, int expert_end, void* ws, size_t ws_bytes, void* stream) {
-  int rc = tlx_moe_route(w_router, w_shared_gate, h, ldh, p, n_experts, hidden, inner, expert_begin, expert_end,
-                         shared_gate != nullptr, ids, gates, sg, ws, ws_bytes, stream);
+  int rc = route_impl(w_router, w_shared_gate, h, ldh, p, n_experts, hidden, inner, expert_begin, expert_end,
+                      shared_gate != nullptr, ids, gates, sg, ws, ws_bytes, stream, false);
   if (rc) return rc;
-  return tlx_moe_experts(gate, up, down, shared_gate, shared_up, shared_down, kvalues, hres, ldr, y, ldy, p,
-                         n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, stream);
+  return experts_impl(gate, up, down, shared_gate, shared_up, shared_down, kvalues, hres, ldr, y, ldy, ids, gates, sg,
+                      p, n_experts, hidden, inner, expert_begin, expert_end, ws, ws_bytes, stream);
 }
 
 int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, int inner, uint32_t* err_out,
