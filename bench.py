@@ -248,6 +248,43 @@ def time_graph(fn_replay, steps, torch):
     return start.elapsed_time(end) / steps  # ms
 
 
+def measure_moe(args, torch, peak):
+    """BASELINE config 4 (MoE verify layer, 5 positions) on this GPU: graph replays
+    timed with CUDA events; bytes = router + shared + distinct routed experts."""
+    from thunderllamax_b200 import moe, synth
+
+    shape = moe.MoeShape()
+    step = moe.MoeVerifyStep(shape, seed=0)
+    rng = np.random.default_rng(4321)
+    bits = synth.bf16_normal(rng, (shape.positions, shape.hidden))
+    h = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
+    hres = torch.from_numpy(rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32))
+    step.set_inputs(h.cuda(), hres.cuda())
+    step.capture()
+    for _ in range(5):
+        step.replay()
+    n = max(20, min(2000, args.steps))
+    ms = time_graph(step.replay, n, torch)
+    touched = step.touched_bytes()
+    out = {"workload": "MoE verify layer: fp32 router 2048->256 top-8 + shared, IQ4_XS experts 2048->512->2048, "
+                       "5 positions",
+           "us_per_step": round(ms * 1000, 2), "bytes_per_step": touched,
+           "gbs": round(touched / (ms * 1e-3) / 1e9, 1),
+           "frac_of_peak": round(touched / (ms * 1e-3) / 1e9 / peak, 4),
+           "launches_per_step": step.LAUNCHES_PER_STEP, "err_word": step.ws.error()}
+    if not args.no_cpu:
+        import oracle
+
+        t0 = time.perf_counter()
+        oracle.moe_verify_f64(synth.bf16_bits_to_f32(bits).astype(np.float64), step.host["wr"], step.host["wsh"],
+                              step.host["gate"], step.host["up"], step.host["down"], step.host["sgate"],
+                              step.host["sup"], step.host["sdown"], hres=hres.numpy())
+        cpu_s = time.perf_counter() - t0
+        out["cpu_baseline"] = {"us_per_step": round(cpu_s * 1e6, 1), "cores": 1, "kind": "port",
+                               "sample": "one full MoE step of the numpy f64 oracle"}
+    return out
+
+
 def run_ours(args):
     import torch
 
@@ -366,6 +403,9 @@ def run_ours(args):
         gbs, us = port.rate()
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port", "sample": port.sample_text(),
                "us_per_step": round(us, 1)}
+    extras = {}
+    if rank == 0 and ws == 1 and not args.no_moe:
+        extras["moe_verify"] = measure_moe(args, torch, peak)
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
@@ -389,6 +429,7 @@ def run_ours(args):
               "e2e": {"value": round(total_w / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                       "us_per_step": round(e2e_ms * 1000, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
               "gpu_launches": step.LAUNCHES_PER_STEP * args.steps,
+              "extras": extras,
               "clocks": clocks})
     if ws > 1:
         import torch.distributed as dist
@@ -405,6 +446,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-port baseline")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE layer (config 4) measurement")
     # smaller shapes for profiler captures only; the benchmark line uses the defaults
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
