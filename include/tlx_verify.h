@@ -217,6 +217,24 @@ int tlx_moe_verify(const float* w_router, const float* w_shared_gate, const void
 int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, int inner, uint32_t* err_out,
                             void* stream);
 
+/* ---- prefill-sized FFN contraction (tcgen05 tensor cores) ---------------------------
+ * Many tokens at once: the GEMM runs as D[row][token] = W . X^T with the weights
+ * dequantised to fp16 in shared memory (one fp16 rounding per weight: the exact
+ * integer part times the block scale), tokens staged as fp16 by TMA, fp32
+ * accumulators in tensor memory.  n_rows % 128 == 0, k % 256 == 0, any m >= 1;
+ * x is bf16 (converted to fp16 in the workspace) or fp16 (ldx % 8 == 0).
+ * The workspace (tlx_prefill_workspace_bytes) holds a device error word (zero it
+ * once) and the fp16 copy of bf16 tokens.
+ * act[t][r] = fp16(silu((Wg x_t)[r]) * (Wu x_t)[r]) for IQ3_XXS gate/up, and
+ * y[t][r] = (W x_t)[r] (fp32) for IQ3_XXS or Q6_K W.  Replaces pf_gemm3 / pf_gemm3m
+ * (engine/pf_gemm3.cu:4-26, :219; engine/pf_gemm3m.cu:184-229). */
+size_t tlx_prefill_workspace_bytes(int m, int64_t k);
+int tlx_prefill_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,
+                            int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* act, int64_t ld_act,
+                            void* ws, size_t ws_bytes, void* stream);
+int tlx_prefill_gemm(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                     int64_t n_rows, int64_t k, float* y, int64_t ldy, void* ws, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

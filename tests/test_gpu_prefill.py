@@ -1,0 +1,89 @@
+"""GPU parity of the tcgen05 prefill contraction (BASELINE config 5 shapes, cut
+down) against the numpy oracle on identical seeded inputs, through the C ABI.
+
+The kernels round every dequantised weight to fp16 once (integer part times the
+block scale) and the gate/up output to fp16; tokens are exact in fp16.  Contract:
+max|err| <= 2e-3 * ||row||_2 per token row of the float64 oracle; a tighter
+1e-3 bound (about two fp16 roundings of the largest products) is asserted too."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from thunderllamax_b200 import ops, prefill, synth
+
+pytestmark = pytest.mark.gpu
+
+CONTRACT = 2e-3
+TIGHT = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    ops.require_device()
+    yield
+
+
+def tokens(rng, m, k):
+    bits = synth.bf16_normal(rng, (m, k))
+    return torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16), \
+        synth.bf16_bits_to_f32(bits).astype(np.float64)
+
+
+def check_rows(got, ref, tol):
+    err = np.abs(got.astype(np.float64) - ref).max(axis=1)
+    norm = np.linalg.norm(ref, axis=1)
+    assert (err <= tol * norm).all(), float((err / norm).max())
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 512), (300, 128, 256), (1, 384, 768), (513, 256, 1024)])
+def test_prefill_gate_up_iq3(m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    rg, ru = synth.iq3xxs_blocks(rng, n, k), synth.iq3xxs_blocks(rng, n, k)
+    x_t, x64 = tokens(rng, m, k)
+    ws = prefill.PrefillWorkspace(m, k)
+    act = prefill.gate_up("iq3_xxs", ops.pack_tiles("iq3_xxs", rg, k), ops.pack_tiles("iq3_xxs", ru, k), x_t, n, ws)
+    torch.cuda.synchronize()
+    assert ws.error() == 0
+    g = oracle.matvec_f64(oracle.dequant_iq3xxs(rg, k), x64)
+    u = oracle.matvec_f64(oracle.dequant_iq3xxs(ru, k), x64)
+    ref = oracle.silu_f64(g) * u
+    got = act.float().cpu().numpy()
+    check_rows(got, ref, CONTRACT)
+    check_rows(got, ref, TIGHT)
+
+
+@pytest.mark.parametrize("qtype,m,n,k", [("q6_k", 256, 256, 512), ("q6_k", 300, 128, 1024), ("iq3_xxs", 77, 256, 512)])
+def test_prefill_gemm(qtype, m, n, k):
+    rng = np.random.default_rng(7 + m + n)
+    raw = synth.BLOCK_GEN[qtype](rng, n, k)
+    bits = synth.bf16_normal(rng, (m, k))
+    x16 = synth.bf16_bits_to_f32(bits).astype(np.float16)          # fp16 tokens (like the gate/up act)
+    x_t = torch.from_numpy(x16).cuda()
+    ws = prefill.PrefillWorkspace(m, k)
+    y = prefill.gemm(qtype, ops.pack_tiles(qtype, raw, k), x_t, n, ws)
+    torch.cuda.synchronize()
+    assert ws.error() == 0
+    ref = oracle.matvec_f64(oracle.dequant(qtype, raw, k), x16.astype(np.float64))
+    got = y.cpu().numpy()
+    check_rows(got, ref, CONTRACT)
+    check_rows(got, ref, TIGHT)
+
+
+def test_prefill_ffn_small_chain_and_repeat():
+    shape = prefill.PrefillShape(tokens=260, dim=512, ffn=768)
+    step = prefill.PrefillFFN(shape, seed=3)
+    rng = np.random.default_rng(9)
+    x_t, x64 = tokens(rng, shape.tokens, shape.dim)
+    step.x.copy_(x_t)
+    step.launch()
+    torch.cuda.synchronize()
+    y0 = step.y.clone()
+    step.launch()
+    torch.cuda.synchronize()
+    assert torch.equal(step.y, y0)                                    # deterministic
+    rg = ops.unpack_tiles_host("iq3_xxs", step.w["gate"].cpu().numpy(), shape.ffn, shape.dim, 2 * 98)
+    ru = ops.unpack_tiles_host("iq3_xxs", step.w["up"].cpu().numpy(), shape.ffn, shape.dim, 2 * 98)
+    rd = ops.unpack_tiles_host("q6_k", step.w["down"].cpu().numpy(), shape.dim, shape.ffn, 3 * 210)
+    _, y_ref = oracle.ffn_f64(x64, rg, ru, rd)
+    check_rows(step.y.cpu().numpy(), y_ref, CONTRACT)

@@ -63,6 +63,11 @@ _SIGS = {
     "tlx_moe_verify": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp,
                                c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_size, c_vp]),
     "tlx_moe_workspace_error": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp]),
+    "tlx_prefill_workspace_bytes": (c_size, [c_int, c_i64]),
+    "tlx_prefill_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64,
+                                        c_vp, c_size, c_vp]),
+    "tlx_prefill_gemm": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp,
+                                 c_size, c_vp]),
 }
 
 

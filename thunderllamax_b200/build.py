@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libtlx_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
-SOURCES = ["gemv.cu", "capi.cu", "moe.cu", "noalloc.cu"]
+SOURCES = ["gemv.cu", "capi.cu", "moe.cu", "prefill.cu", "noalloc.cu"]
 
 
 def nvcc() -> str:
@@ -42,7 +42,7 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

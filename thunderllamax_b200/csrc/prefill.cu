@@ -1,0 +1,627 @@
+// Prefill-sized FFN contraction (many tokens) on the 5th-generation tensor cores.
+//
+//   act[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r]   IQ3_XXS / Q6_K gate and up, fp16 act
+//   y[t][r]   = (W x_t)[r]                      any of the two formats, fp32 y
+//
+// The GEMM is computed transposed, D[row][token] = W . X^T, so the dequantised
+// weights are the A operand (M = 128 rows per tile) and the tokens the B operand
+// (N = 256 per tile): one dequantised weight tile feeds 256 tokens.  Per CTA
+// (persistent, one per SM, tiles in row-major order so the CTAs working on one
+// weight tile at a time share it through L2):
+//
+//   warp 0       bulk-copies the packed weight chunks of the next 256-k block into a
+//                double-buffered staging area, and TMA-loads the token tile
+//                (fp16, 128-byte swizzle) of every 64-k step;
+//   warps 8..15  dequantise the staged chunks of each 64-k step to fp16 (the decode
+//                of the matvec kernels: exact integer part times the block scale,
+//                one fp16 rounding per weight) and write them in the UMMA K-major
+//                128-byte-swizzle layout;
+//   warp 1       one thread issues tcgen05.mma (kind::f16, fp32 accumulators in
+//                TMEM: gate at columns 0..255, up at 256..511) and commits each
+//                stage back to the producers;
+//   warps 4..7   read the accumulators (tcgen05.ld, one 32-lane quarter each),
+//                apply silu(g) * u or store y.
+//
+// Every wait is bounded: on timeout a thread raises ERR_MBAR_TIMEOUT, the CTA
+// abandons its remaining tiles, waits for its issued tensor-core work and frees
+// its TMEM.  No cluster multicast.  Reference: the prefill GEMM pool of
+// engine/pf_gemm3.cu:4-26, :219 and engine/pf_gemm3m.cu:184-229 (IQ3 dequant to
+// fp16 shared memory, mma.sync m16n8k16, SiLU epilogue).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "formats.cuh"
+#include "tlx_internal.h"
+
+namespace tlx {
+namespace {
+
+constexpr int kPfRows = 128;   // weight rows per tile (UMMA M)
+constexpr int kPfTok = 256;    // tokens per tile (UMMA N)
+constexpr int kKStep = 64;       // k per pipeline stage (one 128-byte swizzle atom)
+constexpr int kWarps = 16;
+constexpr int kDequantWarp0 = 8;  // warps 8..15
+constexpr int kEpiWarp0 = 4;      // warps 4..7
+constexpr uint32_t kPollLimit = kMbarPollLimit;
+
+// ---------------------------------------------------------------- tcgen05 / TMA
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, kind::f16, fp32 accumulate
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` once every tcgen05.mma issued so far by this thread has completed
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// 2-D tiled TMA load (no multicast) completing on an mbarrier
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1u) << 16;                // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;        // stride byte offset: next 8-row group
+  d |= static_cast<uint64_t>(1u) << 46;                // descriptor version (Blackwell)
+  d |= static_cast<uint64_t>(2u) << 61;                // layout: 128-byte swizzle
+  return d;
+}
+// instruction descriptor, kind::f16: fp16 A and B (K-major), fp32 D, M x N
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kPfTok >> 3) << 17) |
+                            (static_cast<uint32_t>(kPfRows >> 4) << 24);
+
+// byte offset of (row r, 16-byte chunk c) inside a K-major 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kPollLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// dequantise mma steps [M0, M0 + MPER) of one (16-row tile, row pair g) for the 64-k
+// slice owned by decode lane vlane, writing rows r0, r1 of the swizzled A tile
+template <int QT, int M0, int MPER>
+__device__ __forceinline__ void dequant_task(const uint8_t* ch, int vlane, const uint8_t* grid_lane, uint8_t* adst,
+                                             int r0, int r1) {
+  if constexpr (QT == QT_IQ3_XXS) {
+    Iq3Lane st;
+    iq3_load(ch, vlane, st);
+    const float2 sc = iq3_block_scale(st);
+    const uint32_t s0 = h2_bits(__float2half2_rn(sc.x)), s1 = h2_bits(__float2half2_rn(sc.y));
+#pragma unroll
+    for (int mm = 0; mm < MPER; mm += 2) {
+      uint32_t a[4], b2[4];
+      iq3_mma(st, grid_lane, M0 + mm, a);
+      iq3_mma(st, grid_lane, M0 + mm + 1, b2);
+      const int c = (M0 + mm) >> 1;
+      *reinterpret_cast<uint4*>(adst + sw128_off(r0, c)) =
+          make_uint4(hmul2_u(a[0], s0), hmul2_u(a[2], s0), hmul2_u(b2[0], s0), hmul2_u(b2[2], s0));
+      *reinterpret_cast<uint4*>(adst + sw128_off(r1, c)) =
+          make_uint4(hmul2_u(a[1], s1), hmul2_u(a[3], s1), hmul2_u(b2[1], s1), hmul2_u(b2[3], s1));
+    }
+  } else {
+    Q6Lane st;
+    q6_load(ch, vlane, st);
+    const float2 sc = q6_block_scale(st);
+    const uint32_t s0 = h2_bits(__float2half2_rn(sc.x)), s1 = h2_bits(__float2half2_rn(sc.y));
+#pragma unroll
+    for (int gg = 0; gg < MPER / 2; ++gg) {
+      uint32_t a[4], b2[4];
+      q6_group(st, (M0 >> 1) + gg, a, b2);
+      const int c = (M0 >> 1) + gg;
+      *reinterpret_cast<uint4*>(adst + sw128_off(r0, c)) =
+          make_uint4(hmul2_u(a[0], s0), hmul2_u(a[2], s0), hmul2_u(b2[0], s0), hmul2_u(b2[2], s0));
+      *reinterpret_cast<uint4*>(adst + sw128_off(r1, c)) =
+          make_uint4(hmul2_u(a[1], s1), hmul2_u(a[3], s1), hmul2_u(b2[1], s1), hmul2_u(b2[3], s1));
+    }
+  }
+}
+
+struct PrefillParams {
+  const uint8_t* w0;   // tiled weights (gate, or the single matrix)
+  const uint8_t* w1;   // tiled up weights (gate/up mode)
+  const uint32_t* grid;
+  int M, N, K;         // tokens, weight rows, k
+  void* out;           // fp16 act [M][ldo] (gate/up) or fp32 y [M][ldo]
+  int64_t ldo;
+  uint32_t* err;
+};
+
+template <int QT, int NMAT>
+struct Smem {
+  static constexpr uint32_t kA = NMAT * kPfRows * 128;          // dequantised weights per stage
+  static constexpr uint32_t kB = kPfTok * 128;                   // token tile per stage
+  static constexpr uint32_t kStage = kA + kB;
+  static constexpr int kStages = NMAT == 2 ? 2 : 3;
+  static constexpr uint32_t kStaging = NMAT * 8 * chunk_bytes(QT);  // one 256-k block of packed chunks
+  static constexpr uint32_t kStagingAl = (kStaging + 1023u) & ~1023u;
+  static constexpr uint32_t kGrid = QT == QT_IQ3_XXS ? kGridTableBytes : 0u;
+  static constexpr uint32_t kStagesOff = 0;
+  static constexpr uint32_t kStagingOff = kStagesOff + kStages * kStage;
+  static constexpr uint32_t kGridOff = kStagingOff + 2 * kStagingAl;
+  static constexpr uint32_t kBarOff = kGridOff + kGrid;
+  // full[S], empty[S], stg_full[2], stg_empty[2], acc_full, acc_empty, done, tmem holder, abort
+  static constexpr uint32_t kBytes = kBarOff + (2 * kStages + 7) * 8 + 16;
+  static constexpr uint32_t kAlloc = kBytes + 1024;  // slack to align the base to 1024
+};
+
+template <int QT, int NMAT>
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tok_map, const PrefillParams p) {
+  using L = Smem<QT, NMAT>;
+  constexpr int S = L::kStages;
+  constexpr uint32_t kCols = NMAT * kPfTok;  // TMEM columns (fp32 accumulators)
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* stg_full = bars + 2 * S;
+  uint64_t* stg_empty = bars + 2 * S + 2;
+  uint64_t* acc_full = bars + 2 * S + 4;
+  uint64_t* acc_empty = bars + 2 * S + 5;
+  uint64_t* done = bars + 2 * S + 6;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
+  volatile uint32_t* abort_flag = tmem_holder + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.K >> 8;                       // 256-k blocks
+  const int kt_per_tile = p.K / kKStep;
+  const int row_tiles = p.N / kPfRows;
+  const int tok_tiles = (p.M + kPfTok - 1) / kPfTok;
+  const int n_tiles = row_tiles * tok_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1 + (kWarps - kDequantWarp0));
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&stg_full[b], 1);
+      mbar_init(&stg_empty[b], kWarps - kDequantWarp0);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(done, 1);
+    *abort_flag = 0u;
+    mbar_fence_init();
+  }
+  if constexpr (QT == QT_IQ3_XXS) {
+    uint2* tab = reinterpret_cast<uint2*>(smem + L::kGridOff);
+    if (threadIdx.x < 256) {
+      const uint2 e = grid_pair_entry(__ldg(p.grid + threadIdx.x));
+#pragma unroll
+      for (int c = 0; c < kGridCopies; ++c) tab[threadIdx.x * kGridCopies + c] = e;
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  griddep_wait();
+  griddep_launch_dependents();
+
+  auto fail = [&]() {
+    atomicOr(p.err, ERR_MBAR_TIMEOUT);
+    *abort_flag = 1u;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      // entries e = (tile of this CTA, 256-k block) in order; entry e's packed chunks go
+      // to staging buffer e & 1, issued one entry ahead of its token tiles
+      const int my_tiles = static_cast<int>(blockIdx.x) < n_tiles
+                               ? (n_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                               : 0;
+      const uint32_t n_entries = static_cast<uint32_t>(my_tiles) * nb;
+      const uint32_t chunk = chunk_bytes(QT);
+      uint32_t staged = 0, kt_global = 0;
+      auto stage_entry = [&](uint32_t e) -> bool {
+        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(e / nb) * static_cast<int>(gridDim.x);
+        const int b = static_cast<int>(e % nb), rt = tile / tok_tiles;
+        const int buf = static_cast<int>(e & 1);
+        if (!wait_bounded(&stg_empty[buf], ((e >> 1) & 1) ^ 1)) return false;
+        uint8_t* dst = smem + L::kStagingOff + buf * L::kStagingAl;
+        mbar_arrive_expect_tx(&stg_full[buf], NMAT * 8 * chunk);
+        for (int mat = 0; mat < NMAT; ++mat) {
+          const uint8_t* w = mat == 0 ? p.w0 : p.w1;
+          for (int t16 = 0; t16 < 8; ++t16) {
+            const int64_t tile16 = static_cast<int64_t>(rt) * 8 + t16;
+            bulk_g2s(dst + (mat * 8 + t16) * chunk, w + (tile16 * nb + b) * chunk, chunk, &stg_full[buf]);
+          }
+        }
+        return true;
+      };
+      for (uint32_t e = 0; e < n_entries && !*abort_flag; ++e) {
+        while (staged <= e + 1 && staged < n_entries) {
+          if (!stage_entry(staged)) {
+            fail();
+            break;
+          }
+          ++staged;
+        }
+        if (*abort_flag) break;
+        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(e / nb) * static_cast<int>(gridDim.x);
+        const int b = static_cast<int>(e % nb), tt = tile % tok_tiles;
+        for (int q = 0; q < 4; ++q, ++kt_global) {
+          const int s = static_cast<int>(kt_global % S);
+          if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) {
+            fail();
+            break;
+          }
+          uint8_t* bdst = smem + L::kStagesOff + s * L::kStage + L::kA;
+          mbar_arrive_expect_tx(&full[s], L::kB);
+          tma_load_2d(bdst, &tok_map, (b * 4 + q) * kKStep, tt * kPfTok, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t kt_global = 0, tiles_done = 0;
+      for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, ++tiles_done) {
+        if (!wait_bounded(acc_empty, (tiles_done & 1) ^ 1)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < kt_per_tile && !*abort_flag; ++kt, ++kt_global) {
+          const int s = static_cast<int>(kt_global % S);
+          if (!wait_bounded(&full[s], (kt_global / S) & 1)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + L::kStagesOff + s * L::kStage);
+          const uint32_t b0 = a0 + L::kA;
+#pragma unroll
+          for (int kk = 0; kk < kKStep / 16; ++kk) {
+            const uint64_t bdesc = sw128_desc(b0 + kk * 32);
+#pragma unroll
+            for (int mat = 0; mat < NMAT; ++mat) {
+              const uint64_t adesc = sw128_desc(a0 + mat * kPfRows * 128 + kk * 32);
+              umma_f16(tmem + mat * kPfTok, adesc, bdesc, kIdesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        umma_commit(acc_full);     // accumulators complete
+      }
+      // every issued MMA has completed before TMEM is released
+      umma_commit(done);
+      if (!wait_bounded(done, 0)) fail();
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------- epilogue
+    const int wq = warp & 3;  // TMEM lane quarter of this warp
+    uint32_t tiles_done = 0;
+    for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, ++tiles_done) {
+      const int rt = tile / tok_tiles, tt = tile - rt * tok_tiles;
+      if (!wait_bounded(acc_full, tiles_done & 1)) {
+        if (lane == 0) fail();
+        break;
+      }
+      tc_fence_after();
+      const int row = rt * kPfRows + wq * 32 + lane;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+      for (int c0 = 0; c0 < kPfTok; c0 += 16) {
+        uint32_t g[16];
+        tmem_ld16(tbase + c0, g);
+        if constexpr (NMAT == 2) {
+          uint32_t u[16];
+          tmem_ld16(tbase + kPfTok + c0, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = tt * kPfTok + c0 + j;
+            if (tok < p.M) {
+              const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+              const float a = gv / (1.0f + expf(-gv)) * uv;
+              static_cast<__half*>(p.out)[tok * p.ldo + row] = __float2half_rn(a);
+            }
+          }
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int tok = tt * kPfTok + c0 + j;
+            if (tok < p.M) static_cast<float*>(p.out)[tok * p.ldo + row] = __uint_as_float(g[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+  } else if (warp >= kDequantWarp0) {
+    // ----------------------------------------------------------------- dequantise
+    // task = (matrix, 16-row tile t, row pair g) of the stage's 128 x 64 slice; with
+    // 256 threads each task is shared by 256 / (NMAT * 64) threads over its 16 mma steps
+    constexpr int kTasks = NMAT * 64;
+    constexpr int kSplit = 256 / kTasks;       // 2 (gate/up) or 4
+    constexpr int kMPer = 16 / kSplit;          // mma steps per thread: 8 or 4
+    const int dt = threadIdx.x - kDequantWarp0 * 32;
+    const int task = dt / kSplit, part = dt - task * kSplit;
+    const int mat = task >> 6, t16 = (task >> 3) & 7, g = task & 7;
+    const uint8_t* grid_lane = smem + L::kGridOff + (lane % kGridCopies) * 8;
+    uint32_t kt_global = 0, blk_global = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles && ok && !*abort_flag; tile += gridDim.x) {
+      for (int b = 0; b < nb && ok; ++b, ++blk_global) {
+        const int buf = static_cast<int>(blk_global & 1);
+        if (!wait_bounded(&stg_full[buf], (blk_global >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ch = smem + L::kStagingOff + buf * L::kStagingAl + (mat * 8 + t16) * chunk_bytes(QT);
+        for (int q = 0; q < 4 && ok; ++q, ++kt_global) {
+          const int s = static_cast<int>(kt_global % S);
+          if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* adst = smem + L::kStagesOff + s * L::kStage + mat * kPfRows * 128;
+          const int vlane = 4 * g + q;  // the decode lane that owns k in [64q, 64q + 64)
+          const int r0 = 16 * t16 + g, r1 = r0 + 8;
+          if constexpr (kSplit == 2) {
+            if (part == 0) dequant_task<QT, 0, kMPer>(ch, vlane, grid_lane, adst, r0, r1);
+            else dequant_task<QT, kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1);
+          } else {
+            switch (part) {
+              case 0: dequant_task<QT, 0, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
+              case 1: dequant_task<QT, kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
+              case 2: dequant_task<QT, 2 * kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
+              default: dequant_task<QT, 3 * kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
+            }
+          }
+          // generic-proxy writes -> visible to the tensor core (async proxy)
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[s]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&stg_empty[buf]);
+      }
+    }
+    if (!ok && lane == 0) fail();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// ---- bf16 -> fp16 token staging (exact for |x| in the fp16 normal range) ----
+__global__ void to_f16_kernel(const uint16_t* __restrict__ x, int64_t ldx, int M, int K, __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t per = K >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < static_cast<int64_t>(M) * per;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / per, k8 = i - t * per;
+    const uint4 v = *reinterpret_cast<const uint4*>(x + t * ldx + 8 * k8);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+      o[j] = h2_bits(h);
+    }
+    *reinterpret_cast<uint4*>(out + t * K + 8 * k8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------------------ host
+// the driver's tensor-map encoder, looked up through the runtime (the library does
+// not link the driver library, so it loads on machines without a GPU driver)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+bool make_tok_map(CUtensorMap* map, const void* base, int M, int K, int64_t ld_elems) {
+  const EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKStep), static_cast<cuuint32_t>(kPfTok)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_pdl_raw(const void* kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kern, args) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int QT, int NMAT>
+int launch_prefill(const CUtensorMap& map, const PrefillParams& p, int max_ctas, cudaStream_t stream) {
+  using L = Smem<QT, NMAT>;
+  auto kern = prefill_kernel<QT, NMAT>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::kAlloc)) !=
+        cudaSuccess)
+      return TLX_ERR_LAUNCH;
+    configured = true;
+  }
+  const int tiles = (p.N / kPfRows) * ((p.M + kPfTok - 1) / kPfTok);
+  int ctas = sms();
+  if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
+  if (ctas > tiles) ctas = tiles;
+  CUtensorMap m = map;
+  PrefillParams q = p;
+  void* args[] = {&m, &q};
+  return launch_pdl_raw(reinterpret_cast<const void*>(kern), dim3(ctas), dim3(kWarps * 32), L::kAlloc, stream, args);
+}
+
+bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+}  // namespace
+
+size_t prefill_x_bytes(int m, int64_t k) { return static_cast<size_t>(m) * static_cast<size_t>(k) * 2; }
+
+// act[m][n_rows] (fp16) = silu(Wg x) * (Wu x), or y[m][n_rows] (fp32) = W x
+int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x,
+                int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* out, int64_t ldo, void* ws,
+                size_t ws_bytes, uint32_t* err, int max_ctas, cudaStream_t stream) {
+  if (qt != QT_IQ3_XXS && qt != QT_Q6_K) return TLX_ERR_QTYPE;
+  if (gate_up && qt != QT_IQ3_XXS) return TLX_ERR_QTYPE;  // two packed Q6_K stagings do not fit beside the stages
+  if (!w0 || !x || !out || !err || (gate_up && !w1) || (qt == QT_IQ3_XXS && !grid)) return TLX_ERR_NULL;
+  if (m < 1 || n_rows < kPfRows || n_rows % kPfRows || k < 256 || k % 256 || k > (1 << 20) ||
+      n_rows > (1 << 20) || m > (1 << 20))
+    return TLX_ERR_SHAPE;
+  if (ldo < n_rows) return TLX_ERR_SHAPE;
+  if (!al16(w0) || (w1 && !al16(w1)) || !al16(x)) return TLX_ERR_ALIGN;
+  const void* xf16 = x;
+  int64_t ldx16 = ldx;
+  if (x_dtype == DT_BF16) {
+    if (!ws || ws_bytes < prefill_x_bytes(m, k)) return TLX_ERR_WORKSPACE;
+    if (ldx < k || ldx % 8 || !al16(ws)) return TLX_ERR_ALIGN;
+    const int64_t groups = static_cast<int64_t>(m) * (k / 8);
+    const int blocks = static_cast<int>(groups / 256 + 1 < 4096 ? groups / 256 + 1 : 4096);
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    int mm = m, kk = static_cast<int>(k);
+    __half* o = static_cast<__half*>(ws);
+    void* args[] = {&xb, &ldx, &mm, &kk, &o};
+    const int rc = launch_pdl_raw(reinterpret_cast<const void*>(to_f16_kernel), dim3(blocks), dim3(256), 0, stream,
+                                  args);
+    if (rc) return rc;
+    xf16 = ws;
+    ldx16 = k;
+  } else if (x_dtype == DT_F16) {
+    if (ldx < k || ldx % 8) return TLX_ERR_ALIGN;
+  } else {
+    return TLX_ERR_DTYPE;
+  }
+  CUtensorMap map;
+  if (!make_tok_map(&map, xf16, m, static_cast<int>(k), ldx16)) return TLX_ERR_ALIGN;
+  PrefillParams p;
+  p.w0 = static_cast<const uint8_t*>(w0);
+  p.w1 = static_cast<const uint8_t*>(w1);
+  p.grid = grid;
+  p.M = m;
+  p.N = static_cast<int>(n_rows);
+  p.K = static_cast<int>(k);
+  p.out = out;
+  p.ldo = ldo;
+  p.err = err;
+  if (gate_up) return launch_prefill<QT_IQ3_XXS, 2>(map, p, max_ctas, stream);
+  return qt == QT_IQ3_XXS ? launch_prefill<QT_IQ3_XXS, 1>(map, p, max_ctas, stream)
+                          : launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, stream);
+}
+
+}  // namespace tlx
+
+using namespace tlx;
+
+namespace {
+constexpr size_t kPfErrBytes = 256;  // the workspace starts with the device error word
+}
+
+extern "C" {
+
+size_t tlx_prefill_workspace_bytes(int m, int64_t k) {
+  if (m < 1 || k < 256 || k % 256) return 0;
+  return kPfErrBytes + prefill_x_bytes(m, k);
+}
+
+int tlx_prefill_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,
+                            int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* act, int64_t ld_act,
+                            void* ws, size_t ws_bytes, void* stream) {
+  if (!ws) return TLX_ERR_NULL;
+  if (ws_bytes < kPfErrBytes) return TLX_ERR_WORKSPACE;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  return run_prefill(1, qtype, w_gate, w_up, grid, x, x_dtype, ldx, m, n_rows, k, act, ld_act, w + kPfErrBytes,
+                     ws_bytes - kPfErrBytes, reinterpret_cast<uint32_t*>(w), 0, static_cast<cudaStream_t>(stream));
+}
+
+int tlx_prefill_gemm(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                     int64_t n_rows, int64_t k, float* y, int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+  if (!ws) return TLX_ERR_NULL;
+  if (ws_bytes < kPfErrBytes) return TLX_ERR_WORKSPACE;
+  uint8_t* wb = static_cast<uint8_t*>(ws);
+  return run_prefill(0, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, y, ldy, wb + kPfErrBytes,
+                     ws_bytes - kPfErrBytes, reinterpret_cast<uint32_t*>(wb), 0, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
