@@ -226,7 +226,8 @@ int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, in
  * The workspace (tlx_prefill_workspace_bytes) holds a device error word (zero it
  * once) and the fp16 copy of bf16 tokens.
  * act[t][r] = fp16(silu((Wg x_t)[r]) * (Wu x_t)[r]) for IQ3_XXS gate/up, and
- * y[t][r] = (W x_t)[r] (fp32) for IQ3_XXS or Q6_K W.  Replaces pf_gemm3 / pf_gemm3m
+ * y[t][r] = (W x_t)[r] (fp32) for Q6_K W (the down projection); other formats
+ * return TLX_ERR_QTYPE.  Replaces pf_gemm3 / pf_gemm3m
  * (engine/pf_gemm3.cu:4-26, :219; engine/pf_gemm3m.cu:184-229). */
 size_t tlx_prefill_workspace_bytes(int m, int64_t k);
 int tlx_prefill_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,

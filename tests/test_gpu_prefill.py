@@ -53,7 +53,7 @@ def test_prefill_gate_up_iq3(m, n, k):
     check_rows(got, ref, TIGHT)
 
 
-@pytest.mark.parametrize("qtype,m,n,k", [("q6_k", 256, 256, 512), ("q6_k", 300, 128, 1024), ("iq3_xxs", 77, 256, 512)])
+@pytest.mark.parametrize("qtype,m,n,k", [("q6_k", 256, 256, 512), ("q6_k", 300, 128, 1024), ("q6_k", 77, 256, 768)])
 def test_prefill_gemm(qtype, m, n, k):
     rng = np.random.default_rng(7 + m + n)
     raw = synth.BLOCK_GEN[qtype](rng, n, k)
@@ -87,3 +87,14 @@ def test_prefill_ffn_small_chain_and_repeat():
     rd = ops.unpack_tiles_host("q6_k", step.w["down"].cpu().numpy(), shape.dim, shape.ffn, 3 * 210)
     _, y_ref = oracle.ffn_f64(x64, rg, ru, rd)
     check_rows(step.y.cpu().numpy(), y_ref, CONTRACT)
+
+
+def test_prefill_rejects_unsupported_formats():
+    from thunderllamax_b200 import _lib
+    x = torch.zeros((16, 256), dtype=torch.float16, device="cuda")
+    ws = prefill.PrefillWorkspace(16, 256)
+    w = torch.zeros(ops.tiled_bytes("iq3_xxs", 128, 256), dtype=torch.uint8, device="cuda")
+    with pytest.raises(_lib.TLXError):
+        prefill.gemm("iq3_xxs", w, x, 128, ws)          # single-matrix path is Q6_K
+    with pytest.raises(_lib.TLXError):
+        prefill.gate_up("q6_k", w, w, x, 128, ws)       # gate/up path is IQ3_XXS

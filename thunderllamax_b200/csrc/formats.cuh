@@ -179,16 +179,8 @@ struct Q6Lane {
 
 constexpr uint32_t kMinus96 = 0xD600D600u;  // fp16x2 (-96, -96)
 
-__device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& s) {
-#pragma unroll
-  for (int p = 0; p < 6; ++p) {
-    const uint4 v = *reinterpret_cast<const uint4*>(chunk + (p * 32 + lane) * 16);
-    s.w[4 * p + 0] = v.x;
-    s.w[4 * p + 1] = v.y;
-    s.w[4 * p + 2] = v.z;
-    s.w[4 * p + 3] = v.w;
-  }
-  const uint2 sc = *reinterpret_cast<const uint2*>(chunk + 3072 + lane * 8);
+// the lane's biased sub-scale bytes -> fp16x2 (sc/16) and (-96 sc) per sub-block / row
+__device__ __forceinline__ void q6_scales(const uint2 sc, Q6Lane& s) {
   // biased byte b = sc + 128 -> fp16 1024 + b -> minus 1152 = sc (exact)
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -201,6 +193,18 @@ __device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& 
       s.c96[j][r] = hmul2_u(sc2, kMinus96);
     }
   }
+}
+
+__device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& s) {
+#pragma unroll
+  for (int p = 0; p < 6; ++p) {
+    const uint4 v = *reinterpret_cast<const uint4*>(chunk + (p * 32 + lane) * 16);
+    s.w[4 * p + 0] = v.x;
+    s.w[4 * p + 1] = v.y;
+    s.w[4 * p + 2] = v.z;
+    s.w[4 * p + 3] = v.w;
+  }
+  q6_scales(*reinterpret_cast<const uint2*>(chunk + 3072 + lane * 8), s);
   s.d = *reinterpret_cast<const uint32_t*>(chunk + 3328 + (lane >> 2) * 4);
 }
 
@@ -258,10 +262,8 @@ struct Iq3Lane {
   uint32_t d;
 };
 
-__device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane& s) {
-  s.qs0 = *reinterpret_cast<const uint4*>(chunk + lane * 16);
-  s.qs1 = *reinterpret_cast<const uint4*>(chunk + 512 + lane * 16);
-  const uint4 sw = *reinterpret_cast<const uint4*>(chunk + 1024 + lane * 16);
+// the lane's scale/sign words -> (2s+1) fp16x2 and sign-field parities
+__device__ __forceinline__ void iq3_words(const uint4 sw, Iq3Lane& s) {
   s.sw[0][0] = sw.x;
   s.sw[0][1] = sw.y;
   s.sw[1][0] = sw.z;
@@ -278,6 +280,12 @@ __device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane
       t ^= t >> 4;                 // bit i = xor of bits i..i+7
       s.par[r][c] = t ^ (v >> 7);  // bit 7l = parity of field l
     }
+}
+
+__device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane& s) {
+  s.qs0 = *reinterpret_cast<const uint4*>(chunk + lane * 16);
+  s.qs1 = *reinterpret_cast<const uint4*>(chunk + 512 + lane * 16);
+  iq3_words(*reinterpret_cast<const uint4*>(chunk + 1024 + lane * 16), s);
   s.d = *reinterpret_cast<const uint32_t*>(chunk + 1536 + (lane >> 2) * 4);
 }
 

@@ -1,7 +1,7 @@
 // Prefill-sized FFN contraction (many tokens) on the 5th-generation tensor cores.
 //
-//   act[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r]   IQ3_XXS / Q6_K gate and up, fp16 act
-//   y[t][r]   = (W x_t)[r]                      any of the two formats, fp32 y
+//   act[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r]   IQ3_XXS gate and up, fp16 act
+//   y[t][r]   = (W x_t)[r]                      Q6_K (the down projection), fp32 y
 //
 // The GEMM is computed transposed, D[row][token] = W . X^T, so the dequantised
 // weights are the A operand (M = 128 rows per tile) and the tokens the B operand
@@ -9,13 +9,12 @@
 // (persistent, one per SM, tiles in row-major order so the CTAs working on one
 // weight tile at a time share it through L2):
 //
-//   warp 0       bulk-copies the packed weight chunks of the next 256-k block into a
-//                double-buffered staging area, and TMA-loads the token tile
-//                (fp16, 128-byte swizzle) of every 64-k step;
-//   warps 8..15  dequantise the staged chunks of each 64-k step to fp16 (the decode
-//                of the matvec kernels: exact integer part times the block scale,
-//                one fp16 rounding per weight) and write them in the UMMA K-major
-//                128-byte-swizzle layout;
+//   warp 0       TMA-loads the token tile (fp16, 128-byte swizzle) of every 64-k step;
+//   warps 8..15  dequantise each 64-k step to fp16 (the decode of the matvec kernels:
+//                exact integer part times the block scale, one fp16 rounding per
+//                weight) and write it in the UMMA K-major 128-byte-swizzle layout;
+//                each thread reads its decode lane's bytes of the packed chunk from
+//                global memory one step ahead, so no staging buffer is needed;
 //   warp 1       one thread issues tcgen05.mma (kind::f16, fp32 accumulators in
 //                TMEM: gate at columns 0..255, up at 256..511) and commits each
 //                stage back to the producers;
@@ -32,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "common.cuh"
 #include "formats.cuh"
@@ -119,43 +119,138 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+// for long waits (the epilogue waits a whole tile): back off between polls so the
+// waiting warps leave the issue slots to the dequantising warps (bounded: ~seconds)
+__device__ __forceinline__ bool wait_bounded_sleepy(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < (kPollLimit >> 4); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(512);
+  }
+  return false;
+}
 
-// dequantise mma steps [M0, M0 + MPER) of one (16-row tile, row pair g) for the 64-k
-// slice owned by decode lane vlane, writing rows r0, r1 of the swizzled A tile
-template <int QT, int M0, int MPER>
-__device__ __forceinline__ void dequant_task(const uint8_t* ch, int vlane, const uint8_t* grid_lane, uint8_t* adst,
-                                             int r0, int r1) {
-  if constexpr (QT == QT_IQ3_XXS) {
-    Iq3Lane st;
-    iq3_load(ch, vlane, st);
-    const float2 sc = iq3_block_scale(st);
-    const uint32_t s0 = h2_bits(__float2half2_rn(sc.x)), s1 = h2_bits(__float2half2_rn(sc.y));
+// The part of one decode lane's bytes of a packed chunk (k in [64q, 64q + 64) of
+// the block, rows g and g+8) that one dequantising thread needs, read from global
+// memory two steps ahead of use.
+//   IQ3_XXS, part p of 2: scale group p (mma steps 8p .. 8p+7)
+//   Q6_K,    part j of 4: sub-block j (mma steps 4j .. 4j+3, groups 2j and 2j+1)
+struct Iq3Part {
+  uint2 q0, q1;      // grid indices of group p, row g / row g+8
+  uint32_t sw0, sw1; // scale/sign word of group p, row g / row g+8
+  uint32_t d;        // fp16 d of row g (lo) and g+8 (hi)
+};
+struct Q6Part {
+  uint4 ua, ub;      // the lane's 16-byte units holding words 6j .. 6j+5
+  uint32_t sc;       // biased sub-scales of sub-block j, row g (byte 0) / g+8 (byte 1)
+  uint32_t d;
+};
+template <int QT>
+using PartT = typename std::conditional<QT == QT_IQ3_XXS, Iq3Part, Q6Part>::type;
+
+__device__ __forceinline__ void load_part(const uint8_t* ch, int vlane, int part, Iq3Part& r) {
+  r.q0 = __ldg(reinterpret_cast<const uint2*>(ch + vlane * 16 + 8 * part));
+  r.q1 = __ldg(reinterpret_cast<const uint2*>(ch + 512 + vlane * 16 + 8 * part));
+  r.sw0 = __ldg(reinterpret_cast<const uint32_t*>(ch + 1024 + vlane * 16 + 4 * part));
+  r.sw1 = __ldg(reinterpret_cast<const uint32_t*>(ch + 1024 + vlane * 16 + 8 + 4 * part));
+  r.d = __ldg(reinterpret_cast<const uint32_t*>(ch + 1536 + (vlane >> 2) * 4));
+}
+__device__ __forceinline__ void load_part(const uint8_t* ch, int vlane, int part, Q6Part& r) {
+  const int ua = (3 * part) >> 1;  // 6j / 4
+  r.ua = __ldg(reinterpret_cast<const uint4*>(ch + (ua * 32 + vlane) * 16));
+  r.ub = __ldg(reinterpret_cast<const uint4*>(ch + ((ua + 1) * 32 + vlane) * 16));
+  r.sc = __ldg(reinterpret_cast<const uint16_t*>(ch + 3072 + vlane * 8 + 2 * part));
+  r.d = __ldg(reinterpret_cast<const uint32_t*>(ch + 3328 + (vlane >> 2) * 4));
+}
+
+// rows r0, r1 of the swizzled A tile, 16-byte chunk c: 8 consecutive k per row
+__device__ __forceinline__ void store_rows(uint8_t* adst, int r0, int r1, int c, const uint32_t (&a)[4],
+                                           const uint32_t (&b)[4], uint32_t s0, uint32_t s1) {
+  *reinterpret_cast<uint4*>(adst + sw128_off(r0, c)) =
+      make_uint4(hmul2_u(a[0], s0), hmul2_u(a[2], s0), hmul2_u(b[0], s0), hmul2_u(b[2], s0));
+  *reinterpret_cast<uint4*>(adst + sw128_off(r1, c)) =
+      make_uint4(hmul2_u(a[1], s1), hmul2_u(a[3], s1), hmul2_u(b[1], s1), hmul2_u(b[3], s1));
+}
+
+// IQ3_XXS, group p: mma steps 8p .. 8p+7 (the decode of iq3_mma restricted to one group)
+__device__ __forceinline__ void dequant_iq3_part(const Iq3Part& r, int part, const uint8_t* grid_lane, uint8_t* adst,
+                                                 int r0, int r1) {
+  uint32_t m2[2], par[2];
+  const uint32_t sw[2] = {r.sw0, r.sw1};
 #pragma unroll
-    for (int mm = 0; mm < MPER; mm += 2) {
-      uint32_t a[4], b2[4];
-      iq3_mma(st, grid_lane, M0 + mm, a);
-      iq3_mma(st, grid_lane, M0 + mm + 1, b2);
-      const int c = (M0 + mm) >> 1;
-      *reinterpret_cast<uint4*>(adst + sw128_off(r0, c)) =
-          make_uint4(hmul2_u(a[0], s0), hmul2_u(a[2], s0), hmul2_u(b2[0], s0), hmul2_u(b2[2], s0));
-      *reinterpret_cast<uint4*>(adst + sw128_off(r1, c)) =
-          make_uint4(hmul2_u(a[1], s1), hmul2_u(a[3], s1), hmul2_u(b2[1], s1), hmul2_u(b2[3], s1));
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint32_t v = sw[rr];
+    const uint32_t mm = ((v >> 28) << 1) | 1u;
+    m2[rr] = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
+    uint32_t t = v ^ (v >> 1);
+    t ^= t >> 2;
+    t ^= t >> 4;
+    par[rr] = t ^ (v >> 7);
+  }
+  const __half2 dh = *reinterpret_cast<const __half2*>(&r.d);
+  const float2 df = __half22float2(dh);
+  const uint32_t s0 = h2_bits(__float2half2_rn(df.x * 0.25f)), s1 = h2_bits(__float2half2_rn(df.y * 0.25f));
+  auto decode = [&](int ml, uint32_t (&a)[4]) {
+    const int l = (ml >> 1) & 3, e = ml & 1;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint2 q = rr == 0 ? r.q0 : r.q1;
+      const uint32_t word = ml < 4 ? q.x : q.y;
+      const uint32_t idx = (word >> (8 * (ml & 3))) & 0xFFu;
+      const uint2 G = *reinterpret_cast<const uint2*>(grid_lane + idx * (kGridCopies * 8u));
+      const uint32_t v = sw[rr];
+      const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | ((par[rr] >> (7 * l)) << 7 & 0x80u);
+      a[rr] = hmul2_u(G.x, m2[rr]) ^ sign_mask(s8, 2 * e);
+      a[rr + 2] = hmul2_u(G.y, m2[rr]) ^ sign_mask(s8, 2 * e + 1);
     }
+  };
+#pragma unroll
+  for (int ml = 0; ml < 8; ml += 2) {
+    uint32_t a[4], b[4];
+    decode(ml, a);
+    decode(ml + 1, b);
+    store_rows(adst, r0, r1, 4 * part + (ml >> 1), a, b, s0, s1);
+  }
+}
+
+// Q6_K, sub-block j: groups 2j and 2j+1 (q6_group restricted to one sub-block)
+__device__ __forceinline__ void dequant_q6_part(const Q6Part& r, int part, uint8_t* adst, int r0, int r1) {
+  uint32_t w[6];
+  if (part & 1) {
+    w[0] = r.ua.z; w[1] = r.ua.w; w[2] = r.ub.x; w[3] = r.ub.y; w[4] = r.ub.z; w[5] = r.ub.w;
   } else {
-    Q6Lane st;
-    q6_load(ch, vlane, st);
-    const float2 sc = q6_block_scale(st);
-    const uint32_t s0 = h2_bits(__float2half2_rn(sc.x)), s1 = h2_bits(__float2half2_rn(sc.y));
+    w[0] = r.ua.x; w[1] = r.ua.y; w[2] = r.ua.z; w[3] = r.ua.w; w[4] = r.ub.x; w[5] = r.ub.y;
+  }
+  uint32_t sg[2], cg[2];
 #pragma unroll
-    for (int gg = 0; gg < MPER / 2; ++gg) {
-      uint32_t a[4], b2[4];
-      q6_group(st, (M0 >> 1) + gg, a, b2);
-      const int c = (M0 >> 1) + gg;
-      *reinterpret_cast<uint4*>(adst + sw128_off(r0, c)) =
-          make_uint4(hmul2_u(a[0], s0), hmul2_u(a[2], s0), hmul2_u(b2[0], s0), hmul2_u(b2[2], s0));
-      *reinterpret_cast<uint4*>(adst + sw128_off(r1, c)) =
-          make_uint4(hmul2_u(a[1], s1), hmul2_u(a[3], s1), hmul2_u(b2[1], s1), hmul2_u(b2[3], s1));
-    }
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint32_t sc2 = hadd2_u(prmt(r.sc, 0x64646464u, 0x4040u | (rr << 8) | rr), kMinus1152);
+    sg[rr] = hmul2_u(sc2, kSixteenth);
+    cg[rr] = hmul2_u(sc2, kMinus96);
+  }
+  const __half2 dh = *reinterpret_cast<const __half2*>(&r.d);
+  const float2 df = __half22float2(dh);
+  const uint32_t s0 = h2_bits(__float2half2_rn(df.x)), s1 = h2_bits(__float2half2_rn(df.y));
+#pragma unroll
+  for (int gg = 0; gg < 2; ++gg) {
+    const uint32_t W0 = w[3 * gg], W1 = w[3 * gg + 1], W2 = w[3 * gg + 2];
+    const uint32_t p0 = (W0 & 0x03F003F0u) | kMagic;
+    const uint32_t p1 = ((W0 >> 6) & 0x03F003F0u) | kMagic;
+    const uint32_t p2 = (W1 & 0x03F003F0u) | kMagic;
+    const uint32_t p3 = ((W1 >> 6) & 0x03F003F0u) | kMagic;
+    const uint32_t p4 = (W2 & 0x03F003F0u) | kMagic;
+    const uint32_t p5 = ((W2 >> 6) & 0x03F003F0u) | kMagic;
+    const uint32_t p6 = ((W0 << 4) & 0x00F000F0u) | (((W2 << 8) & 0x03000300u) | kMagic);
+    const uint32_t p7 = ((W1 << 4) & 0x00F000F0u) | (((W2 << 6) & 0x03000300u) | kMagic);
+    uint32_t a[4], b[4];
+    a[0] = hfma2_u(p0, sg[0], cg[0]);
+    a[1] = hfma2_u(p1, sg[1], cg[1]);
+    a[2] = hfma2_u(p2, sg[0], cg[0]);
+    a[3] = hfma2_u(p3, sg[1], cg[1]);
+    b[0] = hfma2_u(p4, sg[0], cg[0]);
+    b[1] = hfma2_u(p5, sg[1], cg[1]);
+    b[2] = hfma2_u(p6, sg[0], cg[0]);
+    b[3] = hfma2_u(p7, sg[1], cg[1]);
+    store_rows(adst, r0, r1, 2 * part + gg, a, b, s0, s1);
   }
 }
 
@@ -171,19 +266,16 @@ struct PrefillParams {
 
 template <int QT, int NMAT>
 struct Smem {
-  static constexpr uint32_t kA = NMAT * kPfRows * 128;          // dequantised weights per stage
-  static constexpr uint32_t kB = kPfTok * 128;                   // token tile per stage
+  static constexpr uint32_t kA = NMAT * kPfRows * 128;  // dequantised weights per stage
+  static constexpr uint32_t kB = kPfTok * 128;          // token tile per stage
   static constexpr uint32_t kStage = kA + kB;
-  static constexpr int kStages = NMAT == 2 ? 2 : 3;
-  static constexpr uint32_t kStaging = NMAT * 8 * chunk_bytes(QT);  // one 256-k block of packed chunks
-  static constexpr uint32_t kStagingAl = (kStaging + 1023u) & ~1023u;
+  static constexpr int kStages = NMAT == 2 ? 3 : 4;
   static constexpr uint32_t kGrid = QT == QT_IQ3_XXS ? kGridTableBytes : 0u;
   static constexpr uint32_t kStagesOff = 0;
-  static constexpr uint32_t kStagingOff = kStagesOff + kStages * kStage;
-  static constexpr uint32_t kGridOff = kStagingOff + 2 * kStagingAl;
+  static constexpr uint32_t kGridOff = kStagesOff + kStages * kStage;
   static constexpr uint32_t kBarOff = kGridOff + kGrid;
-  // full[S], empty[S], stg_full[2], stg_empty[2], acc_full, acc_empty, done, tmem holder, abort
-  static constexpr uint32_t kBytes = kBarOff + (2 * kStages + 7) * 8 + 16;
+  // full[S], empty[S], acc_full, acc_empty, done, tmem holder + abort flag
+  static constexpr uint32_t kBytes = kBarOff + (2 * kStages + 3) * 8 + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // slack to align the base to 1024
 };
 
@@ -198,12 +290,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
-  uint64_t* stg_full = bars + 2 * S;
-  uint64_t* stg_empty = bars + 2 * S + 2;
-  uint64_t* acc_full = bars + 2 * S + 4;
-  uint64_t* acc_empty = bars + 2 * S + 5;
-  uint64_t* done = bars + 2 * S + 6;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
+  uint64_t* acc_full = bars + 2 * S;
+  uint64_t* acc_empty = bars + 2 * S + 1;
+  uint64_t* done = bars + 2 * S + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
   volatile uint32_t* abort_flag = tmem_holder + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -217,10 +307,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1 + (kWarps - kDequantWarp0));
       mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&stg_full[b], 1);
-      mbar_init(&stg_empty[b], kWarps - kDequantWarp0);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
@@ -255,50 +341,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      // entries e = (tile of this CTA, 256-k block) in order; entry e's packed chunks go
-      // to staging buffer e & 1, issued one entry ahead of its token tiles
-      const int my_tiles = static_cast<int>(blockIdx.x) < n_tiles
-                               ? (n_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-                               : 0;
-      const uint32_t n_entries = static_cast<uint32_t>(my_tiles) * nb;
-      const uint32_t chunk = chunk_bytes(QT);
-      uint32_t staged = 0, kt_global = 0;
-      auto stage_entry = [&](uint32_t e) -> bool {
-        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(e / nb) * static_cast<int>(gridDim.x);
-        const int b = static_cast<int>(e % nb), rt = tile / tok_tiles;
-        const int buf = static_cast<int>(e & 1);
-        if (!wait_bounded(&stg_empty[buf], ((e >> 1) & 1) ^ 1)) return false;
-        uint8_t* dst = smem + L::kStagingOff + buf * L::kStagingAl;
-        mbar_arrive_expect_tx(&stg_full[buf], NMAT * 8 * chunk);
-        for (int mat = 0; mat < NMAT; ++mat) {
-          const uint8_t* w = mat == 0 ? p.w0 : p.w1;
-          for (int t16 = 0; t16 < 8; ++t16) {
-            const int64_t tile16 = static_cast<int64_t>(rt) * 8 + t16;
-            bulk_g2s(dst + (mat * 8 + t16) * chunk, w + (tile16 * nb + b) * chunk, chunk, &stg_full[buf]);
-          }
-        }
-        return true;
-      };
-      for (uint32_t e = 0; e < n_entries && !*abort_flag; ++e) {
-        while (staged <= e + 1 && staged < n_entries) {
-          if (!stage_entry(staged)) {
-            fail();
-            break;
-          }
-          ++staged;
-        }
-        if (*abort_flag) break;
-        const int tile = static_cast<int>(blockIdx.x) + static_cast<int>(e / nb) * static_cast<int>(gridDim.x);
-        const int b = static_cast<int>(e % nb), tt = tile % tok_tiles;
-        for (int q = 0; q < 4; ++q, ++kt_global) {
+      uint32_t kt_global = 0;
+      for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+        const int tt = tile % tok_tiles;
+        for (int kt = 0; kt < kt_per_tile && !*abort_flag; ++kt, ++kt_global) {
           const int s = static_cast<int>(kt_global % S);
           if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) {
             fail();
             break;
           }
-          uint8_t* bdst = smem + L::kStagesOff + s * L::kStage + L::kA;
           mbar_arrive_expect_tx(&full[s], L::kB);
-          tma_load_2d(bdst, &tok_map, (b * 4 + q) * kKStep, tt * kPfTok, &full[s]);
+          tma_load_2d(smem + L::kStagesOff + s * L::kStage + L::kA, &tok_map, kt * kKStep, tt * kPfTok, &full[s]);
         }
       }
     }
@@ -344,7 +397,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     uint32_t tiles_done = 0;
     for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, ++tiles_done) {
       const int rt = tile / tok_tiles, tt = tile - rt * tok_tiles;
-      if (!wait_bounded(acc_full, tiles_done & 1)) {
+      if (!wait_bounded_sleepy(acc_full, tiles_done & 1)) {
         if (lane == 0) fail();
         break;
       }
@@ -363,7 +416,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             const int tok = tt * kPfTok + c0 + j;
             if (tok < p.M) {
               const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-              const float a = gv / (1.0f + expf(-gv)) * uv;
+              const float a = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
               static_cast<__half*>(p.out)[tok * p.ldo + row] = __float2half_rn(a);
             }
           }
@@ -382,53 +435,69 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
   } else if (warp >= kDequantWarp0) {
     // ----------------------------------------------------------------- dequantise
-    // task = (matrix, 16-row tile t, row pair g) of the stage's 128 x 64 slice; with
-    // 256 threads each task is shared by 256 / (NMAT * 64) threads over its 16 mma steps
-    constexpr int kTasks = NMAT * 64;
-    constexpr int kSplit = 256 / kTasks;       // 2 (gate/up) or 4
-    constexpr int kMPer = 16 / kSplit;          // mma steps per thread: 8 or 4
+    // task = (matrix, 16-row tile t, row pair g) of the stage's 128 x 64 slice, split
+    // in parts: IQ3_XXS (gate/up, 128 tasks) by scale group (2 parts), Q6_K (64 tasks)
+    // by sub-block (4 parts); 256 threads either way
+    static_assert((QT == QT_IQ3_XXS && NMAT == 2) || (QT == QT_Q6_K && NMAT == 1), "prefill combination");
+    constexpr int kSplit = QT == QT_IQ3_XXS ? 2 : 4;
     const int dt = threadIdx.x - kDequantWarp0 * 32;
     const int task = dt / kSplit, part = dt - task * kSplit;
     const int mat = task >> 6, t16 = (task >> 3) & 7, g = task & 7;
     const uint8_t* grid_lane = smem + L::kGridOff + (lane % kGridCopies) * 8;
-    uint32_t kt_global = 0, blk_global = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < n_tiles && ok && !*abort_flag; tile += gridDim.x) {
-      for (int b = 0; b < nb && ok; ++b, ++blk_global) {
-        const int buf = static_cast<int>(blk_global & 1);
-        if (!wait_bounded(&stg_full[buf], (blk_global >> 1) & 1)) {
-          ok = false;
-          break;
+    const uint8_t* wmat = mat == 0 ? p.w0 : p.w1;
+    const uint32_t chunk = chunk_bytes(QT);
+    const int r0 = 16 * t16 + g, r1 = r0 + 8;
+    // position in this CTA's k-step sequence: tile, 256-k block, quarter (decode lane 4g + q)
+    struct Pos {
+      int tile, b, q;
+    };
+    auto advance = [&](Pos& ps) {
+      if (++ps.q == 4) {
+        ps.q = 0;
+        if (++ps.b == nb) {
+          ps.b = 0;
+          ps.tile += gridDim.x;
         }
-        const uint8_t* ch = smem + L::kStagingOff + buf * L::kStagingAl + (mat * 8 + t16) * chunk_bytes(QT);
-        for (int q = 0; q < 4 && ok; ++q, ++kt_global) {
-          const int s = static_cast<int>(kt_global % S);
-          if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          uint8_t* adst = smem + L::kStagesOff + s * L::kStage + mat * kPfRows * 128;
-          const int vlane = 4 * g + q;  // the decode lane that owns k in [64q, 64q + 64)
-          const int r0 = 16 * t16 + g, r1 = r0 + 8;
-          if constexpr (kSplit == 2) {
-            if (part == 0) dequant_task<QT, 0, kMPer>(ch, vlane, grid_lane, adst, r0, r1);
-            else dequant_task<QT, kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1);
-          } else {
-            switch (part) {
-              case 0: dequant_task<QT, 0, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
-              case 1: dequant_task<QT, kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
-              case 2: dequant_task<QT, 2 * kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
-              default: dequant_task<QT, 3 * kMPer, kMPer>(ch, vlane, grid_lane, adst, r0, r1); break;
-            }
-          }
-          // generic-proxy writes -> visible to the tensor core (async proxy)
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full[s]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&stg_empty[buf]);
       }
+    };
+    auto fetch = [&](const Pos& ps, PartT<QT>& r) {
+      if (ps.tile < n_tiles) {
+        const int rt = ps.tile / tok_tiles;
+        load_part(wmat + (static_cast<int64_t>(rt * 8 + t16) * nb + ps.b) * chunk, 4 * g + ps.q, part, r);
+      }
+    };
+    Pos cur{static_cast<int>(blockIdx.x), 0, 0};
+    Pos pre = cur;
+    PartT<QT> bufA, bufB, bufC;
+    fetch(pre, bufA);
+    advance(pre);
+    fetch(pre, bufB);
+    advance(pre);
+    uint32_t kt_global = 0;
+    bool ok = true;
+    // one step: decode `use` into the stage, prefetch two steps ahead into `fill`
+    auto step = [&](const PartT<QT>& use, PartT<QT>& fill) -> bool {
+      fetch(pre, fill);
+      advance(pre);
+      const int s = static_cast<int>(kt_global % S);
+      if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) return false;
+      uint8_t* adst = smem + L::kStagesOff + s * L::kStage + mat * kPfRows * 128;
+      if constexpr (QT == QT_IQ3_XXS) dequant_iq3_part(use, part, grid_lane, adst, r0, r1);
+      else dequant_q6_part(use, part, adst, r0, r1);
+      // generic-proxy writes -> visible to the tensor core (async proxy)
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+      advance(cur);
+      ++kt_global;
+      return true;
+    };
+    while (cur.tile < n_tiles && ok && !*abort_flag) {
+      ok = step(bufA, bufC);
+      if (!ok || cur.tile >= n_tiles || *abort_flag) break;
+      ok = step(bufB, bufA);
+      if (!ok || cur.tile >= n_tiles || *abort_flag) break;
+      ok = step(bufC, bufB);
     }
     if (!ok && lane == 0) fail();
   }
@@ -545,7 +614,8 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
                 int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* out, int64_t ldo, void* ws,
                 size_t ws_bytes, uint32_t* err, int max_ctas, cudaStream_t stream) {
   if (qt != QT_IQ3_XXS && qt != QT_Q6_K) return TLX_ERR_QTYPE;
-  if (gate_up && qt != QT_IQ3_XXS) return TLX_ERR_QTYPE;  // two packed Q6_K stagings do not fit beside the stages
+  // gate/up: IQ3_XXS (the grid table and two matrices per stage); single matrix: Q6_K
+  if ((gate_up && qt != QT_IQ3_XXS) || (!gate_up && qt != QT_Q6_K)) return TLX_ERR_QTYPE;
   if (!w0 || !x || !out || !err || (gate_up && !w1) || (qt == QT_IQ3_XXS && !grid)) return TLX_ERR_NULL;
   if (m < 1 || n_rows < kPfRows || n_rows % kPfRows || k < 256 || k % 256 || k > (1 << 20) ||
       n_rows > (1 << 20) || m > (1 << 20))
@@ -586,8 +656,7 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   p.ldo = ldo;
   p.err = err;
   if (gate_up) return launch_prefill<QT_IQ3_XXS, 2>(map, p, max_ctas, stream);
-  return qt == QT_IQ3_XXS ? launch_prefill<QT_IQ3_XXS, 1>(map, p, max_ctas, stream)
-                          : launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, stream);
+  return launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, stream);
 }
 
 }  // namespace tlx
