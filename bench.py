@@ -285,6 +285,34 @@ def measure_moe(args, torch, peak):
     return out
 
 
+def measure_prefill(args, torch, weights):
+    """BASELINE config 5 (2048-token FFN, tcgen05): CUDA events around the two GEMM
+    launches (+ bf16 -> fp16 token staging); FLOPs = 2 * tokens * dim * ffn * 3."""
+    from thunderllamax_b200 import prefill, synth
+
+    shape = prefill.PrefillShape()
+    step = prefill.PrefillFFN(shape, weights=weights)
+    rng = np.random.default_rng(777)
+    step.x.copy_(torch.from_numpy(synth.bf16_normal(rng, (shape.tokens, shape.dim)).view(np.int16))
+                 .view(torch.bfloat16))
+    for _ in range(3):
+        step.launch()
+    n = 20
+    ms = time_graph(step.launch, n, torch)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+        peak, kind = float(peaks["bf16_tflops"]), "measured cuBLAS bf16 burst"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    tflops = shape.flops() / (ms * 1e-3) / 1e12
+    return {"workload": "prefill FFN: 2048 tokens, IQ3_XXS gate/up 5120->17408 (+SiLU) -> Q6_K down 17408->5120, "
+                        "fp16 tcgen05 with fp32 TMEM accumulators",
+            "ms_per_step": round(ms, 4), "flops_per_step": shape.flops(), "tflops": round(tflops, 1),
+            "peak_tflops": peak, "peak_kind": kind, "frac_of_peak": round(tflops / peak, 4),
+            "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
+
+
 def run_ours(args):
     import torch
 
@@ -406,6 +434,8 @@ def run_ours(args):
     extras = {}
     if rank == 0 and ws == 1 and not args.no_moe:
         extras["moe_verify"] = measure_moe(args, torch, peak)
+    if rank == 0 and ws == 1 and not args.no_prefill and shape.ffn == 17408 and shape.dim == 5120:
+        extras["prefill_ffn"] = measure_prefill(args, torch, {k: step.w[k] for k in ("gate", "up", "down")})
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
@@ -447,6 +477,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-port baseline")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE layer (config 4) measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill contraction (config 5) measurement")
     # smaller shapes for profiler captures only; the benchmark line uses the defaults
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
