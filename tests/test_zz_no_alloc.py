@@ -89,13 +89,20 @@ def test_noalloc_head_matches_workspace_entry_point(qtype, vocab, k):
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
+    # Both refusals happen on the host before any pointer is used or any kernel is
+    # launched (the weight buffer below is far smaller than either shape).
     ops.require_device()
     rng = np.random.default_rng(0)
     w = ops.pack_tiles("q6_k", synth.q6k_blocks(rng, 16, 256), 256)
-    x = torch.zeros((11, 5120), dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros((11, 256), dtype=torch.bfloat16, device="cuda")
     d = torch.zeros(10, dtype=torch.int32, device="cuda")
     out = torch.empty(11, dtype=torch.int32, device="cuda")
-    # a 2M-row head would need ~256 MB of scratch: refused on the host, nothing launched
-    rc = noalloc_fn()(14, p(w), None, p(x), 30, 5120, 11, 2_000_000, 5120, 0, None, p(out), None, p(d), 10, None,
-                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    # k = 2^20: the staged activation image alone (32 MB) exceeds the 24 MB scratch
+    k = 1 << 20
+    assert _lib.lib().tlx_gemv_workspace_bytes(ops.MODE_ARGMAX, 14, 16, k, 11, 30) > SCRATCH_BYTES
+    rc = noalloc_fn()(14, p(w), None, p(x), 30, k, 11, 16, k, 0, None, p(out), None, p(d), 10, None, stream)
     assert rc == -5, _lib.lib().tlx_error_string(rc).decode()   # TLX_ERR_WORKSPACE
+    # more than 16 columns: refused as a shape error
+    rc = noalloc_fn()(14, p(w), None, p(x), 30, 256, 17, 16, 256, 0, None, p(out), None, p(d), 10, None, stream)
+    assert rc != 0
