@@ -23,7 +23,7 @@ enum : uint32_t {
   ERR_BAD_PARAM = 2u,      // device-side parameter check failed
 };
 
-constexpr uint32_t kMbarPollLimit = 1u << 22;  // ~ seconds of try_wait suspends
+constexpr uint32_t kMbarPollLimit = 1u << 22;  // polls of <= kTryWaitHintNs each: a few seconds at most
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -46,15 +46,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// one poll; true once the phase with the given parity has completed
+// one poll; true once the phase with the given parity has completed.  A thread
+// whose phase is still open is suspended for up to kTryWaitHintNs (it resumes as
+// soon as the phase completes), so waiting warps leave the issue slots to others.
+constexpr uint32_t kTryWaitHintNs = 1000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kTryWaitHintNs)
       : "memory");
   return ok != 0;
 }

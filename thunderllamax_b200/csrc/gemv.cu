@@ -505,8 +505,9 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[a][nt][e] = 0.f;
     }
-    // refill the stage (after its last generic-proxy use) with the item STAGES ahead
-    fence_proxy_async_smem();
+    // refill the stage with the item STAGES ahead.  Every lane's reads of the stage
+    // have returned (their values fed the mma); no proxy fence is needed before an
+    // async-proxy write that follows generic-proxy reads.
     __syncwarp();
     if (lane == 0 && i + STAGES < n_items) issue(st);
     if (++bb == p.Bs) {
