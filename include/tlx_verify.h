@@ -159,9 +159,18 @@ int tlx_head_argmax_noalloc(int qtype, const void* w, const uint32_t* grid, cons
                             void* stream);
 
 /* ---- argmax over materialised logits (amx3 / h_argmax) -----------------------------
- * amds[t] = argmax_v logits[t*ld + v] (fp32 or fp16 logits), strict '>' so the
- * lowest index wins ties and NaN never wins.  engine/amx3.cu:117-142. */
+ * amds[t] = argmax_v logits[t*ld + v] (fp32 or fp16 logits): the reference scan
+ * from best = -1e30 with a strict '>', so the lowest index wins ties, NaN / -inf /
+ * values <= -1e30 never win and a row without a candidate yields 0.
+ * engine/amx3.cu:117-142. */
 int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld, int32_t* amds, void* stream);
+
+/* h_argmax (T = 1): the same argmax of one row logits[0..n), then the decode-loop
+ * side effects tok_slot[0] = idx, tok_hist[pos_slot[0]] = idx, pos_slot[0] += 1
+ * (device ints, stream-ordered).  Replaces engine/h_argmax.cu:13-42 (there the
+ * vocabulary is fixed at 248320 fp16 logits). */
+int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, int32_t* pos_slot, int32_t* tok_hist,
+                 void* stream);
 
 /* merge per-shard argmax keys [n_shards][m] (after an all-gather) -> global
  * (max, idx) and optional accept, same rules as tlx_head_argmax. */

@@ -56,15 +56,29 @@ def head_logits_f64(X, w_raw, qtype="q6_k", chunk_rows=16384):
 
 
 def argmax_rows(logits: np.ndarray):
-    """Per-row (max, index): strict '>' scan, so the LOWEST index wins ties and
-    NaN never wins (engine/amx3.cu:117-142, engine/h_argmax.cu:19-33; the fused
-    head's packed key gives the same lowest-row tie-break,
-    engine/mm/MM_P6_h6kam.cu:76-80).  A row of all-NaN yields index 0."""
+    """Per-row (max, index) of the reference scan: best starts at -1e30 and only a
+    strictly greater value (or an equal one at a lower index) replaces it, so the
+    LOWEST index wins ties and NaN, -inf and values <= -1e30 never win; a row with
+    no candidate yields index 0 (engine/amx3.cu:124-139, engine/h_argmax.cu:20-33;
+    the fused head's packed key gives the same lowest-row tie-break,
+    engine/mm/MM_P6_h6kam.cu:76-80)."""
     L = np.asarray(logits, dtype=np.float64)
-    clean = np.where(np.isnan(L), -np.inf, L)
+    with np.errstate(invalid="ignore"):
+        cand = L > -1e30
+    clean = np.where(cand, L, -np.inf)
     idx = np.argmax(clean, axis=1).astype(np.int32)
     mx = L[np.arange(L.shape[0]), idx]
     return mx, idx
+
+
+def h_argmax(logits_row, tok_hist, pos):
+    """h_argmax (T = 1) with its side effects (engine/h_argmax.cu:13-42): the
+    argmax of one row of logits (argmax_rows rules), then tok_slot = idx,
+    tok_hist[pos] = idx, pos + 1.  Returns (idx, tok_hist', pos')."""
+    idx = int(argmax_rows(np.asarray(logits_row)[None, :])[1][0])
+    hist = np.array(tok_hist, dtype=np.int32, copy=True)
+    hist[pos] = idx
+    return idx, hist, pos + 1
 
 
 def head_argmax(X, w_raw, qtype="q6_k", row_offset=0):

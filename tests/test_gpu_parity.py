@@ -235,11 +235,40 @@ def test_fused_head_matches_unfused_logits_path():
 
 
 def test_argmax_rows_ties_and_nan():
-    lg = torch.tensor([[1.0, 3.0, 3.0, float("nan")], [float("nan")] * 4, [-0.0, 0.0, -1.0, -2.0]],
-                      device="cuda")
-    amds = ops.argmax_rows(lg)
+    nan, inf = float("nan"), float("inf")
+    lg = torch.tensor([[1.0, 3.0, 3.0, nan], [nan] * 4, [-0.0, 0.0, -1.0, -2.0],
+                       [nan, -inf, -inf, nan], [-inf, -5.0, nan, -5.0], [inf, 1.0, inf, 2.0]], device="cuda")
+    for t in (lg, lg.half()):
+        amds = ops.argmax_rows(t)
+        torch.cuda.synchronize()
+        assert amds.cpu().tolist() == list(oracle.argmax_rows(t.float().cpu().numpy())[1])
+
+
+def test_h_argmax_side_effects():
+    # the reference's vocabulary (248320 fp16 logits), ties planted above the maximum
+    rng = np.random.default_rng(21)
+    V = 248320
+    lg = rng.standard_normal(V).astype(np.float16)
+    top = rng.choice(V, 3, replace=False)
+    lg[top] = np.float16(9.5)
+    lg[rng.choice(V, 5, replace=False)] = np.float16(np.nan)
+    hist = np.full(64, -1, dtype=np.int32)
+    t_lg = torch.from_numpy(lg).cuda()
+    tok = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([17], dtype=torch.int32, device="cuda")
+    t_hist = torch.from_numpy(hist).cuda()
+    ref_idx, ref_hist, ref_pos = oracle.h_argmax(lg, hist, 17)
+    assert ref_idx == int(top.min())
+    ops.h_argmax(t_lg, tok, pos, t_hist)
+    # a second call appends at the advanced position (a row with no candidate -> 0)
+    empty = torch.full((V,), float("-inf"), dtype=torch.float16, device="cuda")
+    ops.h_argmax(empty, tok, pos, t_hist)
     torch.cuda.synchronize()
-    assert amds.cpu().tolist() == list(oracle.argmax_rows(lg.cpu().numpy())[1])
+    ref2_idx, ref_hist, ref_pos = oracle.h_argmax(empty.cpu().numpy(), ref_hist, ref_pos)
+    assert ref2_idx == 0
+    assert tok.item() == 0 and pos.item() == ref_pos == 19
+    assert np.array_equal(t_hist.cpu().numpy(), ref_hist)
+    assert ref_hist[17] == ref_idx
 
 
 def test_accept_kernels():

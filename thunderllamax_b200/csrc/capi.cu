@@ -77,10 +77,10 @@ __global__ void accept11k_kernel(const int32_t* __restrict__ amds, const int32_t
   }
 }
 
-// per-row argmax over materialised logits (engine/amx3.cu:117-142): one CTA per row
+// argmax key of one row of materialised logits, reduced over the CTA (valid in
+// thread 0): the amx3 / h_argmax scan rules through argmax_key
 template <typename T>
-__global__ void argmax_rows_kernel(const T* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ amds) {
-  const T* row = logits + blockIdx.x * ld;
+__device__ uint64_t row_argmax_key(const T* __restrict__ row, int64_t n) {
   uint64_t best = 0ull;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
     float v;
@@ -96,10 +96,31 @@ __global__ void argmax_rows_kernel(const T* __restrict__ logits, int64_t n, int6
   __shared__ uint64_t wb[32];
   if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint64_t b = 0ull;
+  uint64_t b = 0ull;
+  if (threadIdx.x == 0)
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = wb[w] > b ? wb[w] : b;
-    amds[blockIdx.x] = key_index(b);
+  return b;
+}
+
+// per-row argmax over materialised logits (engine/amx3.cu:117-142): one CTA per row
+template <typename T>
+__global__ void argmax_rows_kernel(const T* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ amds) {
+  const uint64_t b = row_argmax_key(logits + blockIdx.x * ld, n);
+  if (threadIdx.x == 0) amds[blockIdx.x] = key_index(b);
+}
+
+// h_argmax (T = 1, engine/h_argmax.cu:13-42): the argmax of one row, then the
+// decode-loop side effects tok_slot = idx, tok_hist[pos] = idx, pos_slot = pos + 1
+template <typename T>
+__global__ void h_argmax_kernel(const T* __restrict__ logits, int64_t n, int32_t* __restrict__ tok_slot,
+                                int32_t* __restrict__ pos_slot, int32_t* __restrict__ tok_hist) {
+  const uint64_t b = row_argmax_key(logits, n);
+  if (threadIdx.x == 0) {
+    const int32_t idx = key_index(b);
+    const int32_t pos = pos_slot[0];
+    tok_slot[0] = idx;
+    tok_hist[pos] = idx;
+    pos_slot[0] = pos + 1;
   }
 }
 
@@ -343,6 +364,21 @@ int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* 
   return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
                   TLX_DT_F32, 0, row_offset, out_max, out_idx, out_keys, drafts, n_drafts, accept_out, ws, ws_bytes, g_max_ctas,
                   as_stream(stream));
+}
+
+int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, int32_t* pos_slot, int32_t* tok_hist,
+                 void* stream) {
+  if (!logits || !tok_slot || !pos_slot || !tok_hist) return TLX_ERR_NULL;
+  if (n <= 0 || n > 0xFFFFFFFFll) return TLX_ERR_SHAPE;
+  if (dtype == TLX_DT_F32)
+    h_argmax_kernel<float><<<1, 1024, 0, as_stream(stream)>>>(static_cast<const float*>(logits), n, tok_slot,
+                                                                pos_slot, tok_hist);
+  else if (dtype == TLX_DT_F16)
+    h_argmax_kernel<__half><<<1, 1024, 0, as_stream(stream)>>>(static_cast<const __half*>(logits), n, tok_slot,
+                                                                 pos_slot, tok_hist);
+  else
+    return TLX_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
 int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld, int32_t* amds, void* stream) {

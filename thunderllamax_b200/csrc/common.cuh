@@ -130,10 +130,13 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 
 // ---- argmax keys ----
 // key = order(v) << 32 | (0xFFFFFFFF - idx): u64 max picks the largest value and,
-// among equal values, the LOWEST index.  NaN maps to 0 so it never wins; -0 is
+// among equal values, the LOWEST index.  Only v > -1e30 is a candidate (the
+// reference scans start from best = -1e30 with a strict '>': NaN, -inf and
+// anything <= -1e30 never win, and a row without a candidate yields index 0,
+// engine/amx3.cu:124-128, engine/h_argmax.cu:20-24); those map to key 0.  -0 is
 // folded onto +0 so signed zeros tie like they compare.
 __device__ __forceinline__ uint64_t argmax_key(float v, uint32_t idx) {
-  if (v != v) return 0ull;
+  if (!(v > -1e30f)) return 0ull;
   v = v + 0.0f;
   uint32_t u = __float_as_uint(v);
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);

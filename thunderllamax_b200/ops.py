@@ -235,6 +235,22 @@ def argmax_rows(logits: torch.Tensor, amds: torch.Tensor = None) -> torch.Tensor
     return amds
 
 
+def h_argmax(logits: torch.Tensor, tok_slot: torch.Tensor, pos_slot: torch.Tensor, tok_hist: torch.Tensor) -> None:
+    """h_argmax(logits, tok_slot, pos_slot, tok_hist): argmax of one row of logits,
+    then tok_slot[0] = idx, tok_hist[pos_slot[0]] = idx, pos_slot[0] += 1 (all on the
+    device, stream-ordered; engine/h_argmax.cu argument order)."""
+    if logits.dim() != 1 or not logits.is_contiguous():
+        raise TLXError("h_argmax takes one contiguous row of logits")
+    dt = {torch.float32: TLX_DT_F32, torch.float16: TLX_DT_F16}.get(logits.dtype)
+    if dt is None:
+        raise TLXError("logits must be fp32 or fp16")
+    for t in (tok_slot, pos_slot, tok_hist):
+        if t.dtype != torch.int32 or t.device != logits.device:
+            raise TLXError("tok_slot / pos_slot / tok_hist are int32 tensors on the logits' device")
+    check(_lib.lib().tlx_h_argmax(_ptr(logits), dt, logits.numel(), _ptr(tok_slot), _ptr(pos_slot), _ptr(tok_hist),
+                                  _stream(logits)), "h_argmax")
+
+
 def argmax_merge(keys: torch.Tensor, out_max=None, out_idx=None, drafts=None, accept_out=None):
     n_shards, m = keys.shape
     dev = keys.device
@@ -260,5 +276,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
