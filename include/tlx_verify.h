@@ -191,6 +191,17 @@ int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, i
                   const float* hd_d0, const float* hd_d1, float* dhd_seed, int32_t* emit, const int32_t* l_hist,
                   int dim, void* stream);
 
+/* acceptsel11k: commit the accepted GDN state (engine/acceptsel11k.cu:8-40).
+ * rec4 is [n_blocks][5][rec_elems] fp32 and conv4 [n_blocks][5][conv_elems] fp32,
+ * slot 4 the live one; with m = m_slot[0] (device int, 0..10):
+ *   rec4[b][4]  <- m <= 4 ? rec4[b][m]  : rec_x[m - 5][b]   (rec6x .. rec11x)
+ *   conv4[b][4] <- m <= 3 ? conv4[b][m] : conv_x[m - 4][b]  (conv5x .. conv11x)
+ * conv_x / rec_x are HOST arrays of 7 / 6 device pointers, each [n_blocks][elems].
+ * The reference fixes n_blocks = 48, rec_elems = 786432, conv_elems = 30720.
+ * An m outside 0..10 copies nothing. */
+int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const float* const* conv_x,
+                     const float* const* rec_x, int n_blocks, int64_t rec_elems, int64_t conv_elems, void* stream);
+
 /* ---- MoE verify layer (P <= 8 positions, top-8 of E <= 1024 experts + shared) ----
  * Router: logits = w_router[E][hidden] (fp32) . h[p] (bf16), top-8 by 8 masked-argmax
  * passes (strict '>', ties to the lower expert id), gates = exp(l - max) / sum over

@@ -71,6 +71,20 @@ def argmax_rows(logits: np.ndarray):
     return mx, idx
 
 
+def acceptsel11k(rec4, conv4, m, conv_x, rec_x):
+    """acceptsel11k (engine/acceptsel11k.cu:8-40): slot m of the GDN state becomes the
+    live slot 4.  rec4 [B][5][R], conv4 [B][5][C]; rec from rec4[:, m] for m <= 4,
+    else rec_x[m - 5] (rec6x .. rec11x); conv from conv4[:, m] for m <= 3, else
+    conv_x[m - 4] (conv5x .. conv11x).  Returns the new (rec4, conv4)."""
+    rec4 = np.array(rec4, copy=True)
+    conv4 = np.array(conv4, copy=True)
+    if not 0 <= m <= 10:
+        return rec4, conv4
+    rec4[:, 4] = rec4[:, m] if m <= 4 else np.asarray(rec_x[m - 5])
+    conv4[:, 4] = conv4[:, m] if m <= 3 else np.asarray(conv_x[m - 4])
+    return rec4, conv4
+
+
 def h_argmax(logits_row, tok_hist, pos):
     """h_argmax (T = 1) with its side effects (engine/h_argmax.cu:13-42): the
     argmax of one row of logits (argmax_rows rules), then tok_slot = idx,

@@ -271,6 +271,48 @@ def test_h_argmax_side_effects():
     assert ref_hist[17] == ref_idx
 
 
+def _sel_buffers(B, R, C, seed):
+    rng = np.random.default_rng(seed)
+    rec4 = rng.standard_normal((B, 5, R)).astype(np.float32)
+    conv4 = rng.standard_normal((B, 5, C)).astype(np.float32)
+    rec_x = [rng.standard_normal((B, R)).astype(np.float32) for _ in range(6)]
+    conv_x = [rng.standard_normal((B, C)).astype(np.float32) for _ in range(7)]
+    return rec4, conv4, rec_x, conv_x
+
+
+@pytest.mark.parametrize("B,R,C", [(3, 1000, 100), (2, 1001, 37)])   # vector and scalar copies
+def test_acceptsel11k_every_m(B, R, C):
+    rec4, conv4, rec_x, conv_x = _sel_buffers(B, R, C, B + R)
+    for m in list(range(11)) + [11, -1]:
+        t_rec, t_conv = torch.from_numpy(rec4).cuda(), torch.from_numpy(conv4).cuda()
+        m_slot = torch.tensor([m], dtype=torch.int32, device="cuda")
+        ops.acceptsel11k(t_rec, t_conv, m_slot, [torch.from_numpy(x).cuda() for x in conv_x],
+                         [torch.from_numpy(x).cuda() for x in rec_x], n_blocks=B, rec_elems=R, conv_elems=C)
+        torch.cuda.synchronize()
+        want_r, want_c = oracle.acceptsel11k(rec4, conv4, m, conv_x, rec_x)
+        assert np.array_equal(t_rec.cpu().numpy(), want_r), m
+        assert np.array_equal(t_conv.cpu().numpy(), want_c), m
+
+
+def test_acceptsel11k_reference_size():
+    # 48 blocks x (786432 + 30720) fp32: ~157 MB read and written, compared bitwise
+    # on the device against torch copies
+    B, R, C = ops.GDN_BLOCKS, ops.GDN_REC, ops.GDN_CONV
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rec4 = torch.randn((B, 5, R), device="cuda", generator=g)
+    conv4 = torch.randn((B, 5, C), device="cuda", generator=g)
+    rec_x = [torch.randn((B, R), device="cuda", generator=g) for _ in range(6)]
+    conv_x = [torch.randn((B, C), device="cuda", generator=g) for _ in range(7)]
+    for m in (2, 7):
+        want_r, want_c = rec4.clone(), conv4.clone()
+        want_r[:, 4] = rec4[:, m] if m < 5 else rec_x[m - 5]
+        want_c[:, 4] = conv4[:, m] if m < 4 else conv_x[m - 4]
+        got_r, got_c = rec4.clone(), conv4.clone()
+        ops.acceptsel11k(got_r, got_c, torch.tensor([m], dtype=torch.int32, device="cuda"), conv_x, rec_x)
+        torch.cuda.synchronize()
+        assert torch.equal(got_r, want_r) and torch.equal(got_c, want_c), m
+
+
 def test_accept_kernels():
     amds_np = np.arange(100, 111, dtype=np.int32)
     amds = torch.from_numpy(amds_np).cuda()

@@ -52,6 +52,7 @@ _SIGS = {
                                 c_vp, c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
     "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
     "tlx_h_argmax": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "tlx_acceptsel11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
     "tlx_argmax_merge": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
     "tlx_accept": (c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     "tlx_accept11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

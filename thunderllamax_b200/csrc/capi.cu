@@ -77,6 +77,40 @@ __global__ void accept11k_kernel(const int32_t* __restrict__ amds, const int32_t
   }
 }
 
+// acceptsel11k (engine/acceptsel11k.cu:8-40): the accepted GDN state slot m becomes
+// the live slot 4.  rec: m <= 4 from rec4[b][m], m = 5..10 from rec{m+1}x[b]; conv:
+// m <= 3 from conv4[b][m], m = 4..10 from conv{m+1}x[b].  An HBM-bound copy over
+// all blocks at once (grid-stride, 16-byte vectors when every buffer allows).
+struct SelPtrs {
+  const float* conv_x[7];  // conv5x .. conv11x
+  const float* rec_x[6];   // rec6x .. rec11x
+};
+
+template <typename V>
+__global__ void acceptsel_kernel(float* __restrict__ rec4, float* __restrict__ conv4,
+                                 const int32_t* __restrict__ m_slot, const SelPtrs src, int n_blocks,
+                                 int64_t rec_v, int64_t conv_v) {
+  const int m = m_slot[0];
+  if (m < 0 || m > 10) return;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  // rec: slot m -> slot 4 (m == 4 is the live slot itself: nothing to copy)
+  if (m != 4) {
+    for (int64_t i = t0; i < n_blocks * rec_v; i += stride) {
+      const int64_t b = i / rec_v, e = i - b * rec_v;
+      const V* s = m < 5 ? reinterpret_cast<const V*>(rec4) + (b * 5 + m) * rec_v
+                         : reinterpret_cast<const V*>(src.rec_x[m - 5]) + b * rec_v;
+      reinterpret_cast<V*>(rec4)[(b * 5 + 4) * rec_v + e] = s[e];
+    }
+  }
+  for (int64_t i = t0; i < n_blocks * conv_v; i += stride) {
+    const int64_t b = i / conv_v, e = i - b * conv_v;
+    const V* s = m < 4 ? reinterpret_cast<const V*>(conv4) + (b * 5 + m) * conv_v
+                       : reinterpret_cast<const V*>(src.conv_x[m - 4]) + b * conv_v;
+    reinterpret_cast<V*>(conv4)[(b * 5 + 4) * conv_v + e] = s[e];
+  }
+}
+
 // argmax key of one row of materialised logits, reduced over the CTA (valid in
 // thread 0): the amx3 / h_argmax scan rules through argmax_key
 template <typename T>
@@ -364,6 +398,36 @@ int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* 
   return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
                   TLX_DT_F32, 0, row_offset, out_max, out_idx, out_keys, drafts, n_drafts, accept_out, ws, ws_bytes, g_max_ctas,
                   as_stream(stream));
+}
+
+int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const float* const* conv_x,
+                     const float* const* rec_x, int n_blocks, int64_t rec_elems, int64_t conv_elems, void* stream) {
+  if (!rec4 || !conv4 || !m_slot || !conv_x || !rec_x) return TLX_ERR_NULL;
+  if (n_blocks <= 0 || rec_elems <= 0 || conv_elems <= 0) return TLX_ERR_SHAPE;
+  SelPtrs src;
+  bool vec = (rec_elems % 4) == 0 && (conv_elems % 4) == 0 && (reinterpret_cast<uintptr_t>(rec4) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(conv4) & 15) == 0;
+  for (int i = 0; i < 7; ++i) {
+    if (!conv_x[i]) return TLX_ERR_NULL;
+    src.conv_x[i] = conv_x[i];
+    vec = vec && (reinterpret_cast<uintptr_t>(conv_x[i]) & 15) == 0;
+  }
+  for (int i = 0; i < 6; ++i) {
+    if (!rec_x[i]) return TLX_ERR_NULL;
+    src.rec_x[i] = rec_x[i];
+    vec = vec && (reinterpret_cast<uintptr_t>(rec_x[i]) & 15) == 0;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const dim3 grid(static_cast<unsigned>(sms > 0 ? sms * 8 : 1184)), block(256);
+  if (vec)
+    acceptsel_kernel<float4><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, n_blocks, rec_elems / 4,
+                                                                     conv_elems / 4);
+  else
+    acceptsel_kernel<float><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, n_blocks, rec_elems,
+                                                                    conv_elems);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
 int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, int32_t* pos_slot, int32_t* tok_hist,

@@ -135,8 +135,17 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
     def acc36(amds, drafts, mb, eb, K):
         ops.accept(amds, drafts, int(K), mb=mb, eb=eb)
 
+    def acceptsel11k(rec4, conv4, m_slot, *scratch):
+        # engine/acceptsel11k.cu:8-40: conv5x..conv11x then rec6x..rec11x, as the reference
+        ops.acceptsel11k(rec4, conv4, m_slot, scratch[:7], scratch[7:13])
+
+    def h_argmax(logits, tok_slot, pos_slot, tok_hist):
+        # engine/h_argmax.cu:13-42 (T = 1 decode tail)
+        ops.h_argmax(logits, tok_slot, pos_slot, tok_hist)
+
     progs = {"ffn8v11": ffn8v11, "down8nw32_11": down8nw32_11, "head8v11": head8v11, "amx3": amx3,
-             "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36}
+             "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36, "acceptsel11k": acceptsel11k,
+             "h_argmax": h_argmax}
     return {k: Prog(k, v) for k, v in progs.items()}
 
 

@@ -251,6 +251,28 @@ def h_argmax(logits: torch.Tensor, tok_slot: torch.Tensor, pos_slot: torch.Tenso
                                   _stream(logits)), "h_argmax")
 
 
+GDN_BLOCKS, GDN_REC, GDN_CONV = 48, 786432, 30720  # engine/acceptsel11k.cu:22-38
+
+
+def acceptsel11k(rec4: torch.Tensor, conv4: torch.Tensor, m_slot: torch.Tensor, conv_x, rec_x,
+                 n_blocks: int = GDN_BLOCKS, rec_elems: int = GDN_REC, conv_elems: int = GDN_CONV) -> None:
+    """acceptsel11k(rec4, conv4, m_slot, conv5x..conv11x, rec6x..rec11x): the accepted
+    GDN state slot m_slot[0] becomes the live slot 4 (device-side, stream-ordered)."""
+    conv_x, rec_x = list(conv_x), list(rec_x)
+    if len(conv_x) != 7 or len(rec_x) != 6:
+        raise TLXError("acceptsel11k takes 7 conv scratch buffers (conv5x..11x) and 6 rec (rec6x..11x)")
+    for t, n in [(rec4, n_blocks * 5 * rec_elems), (conv4, n_blocks * 5 * conv_elems)] + \
+                [(t, n_blocks * conv_elems) for t in conv_x] + [(t, n_blocks * rec_elems) for t in rec_x]:
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < n:
+            raise TLXError("acceptsel11k buffers are contiguous fp32 of the stated sizes")
+    if m_slot.dtype != torch.int32:
+        raise TLXError("m_slot is int32")
+    cx = (ctypes.c_void_p * 7)(*[t.data_ptr() for t in conv_x])
+    rx = (ctypes.c_void_p * 6)(*[t.data_ptr() for t in rec_x])
+    check(_lib.lib().tlx_acceptsel11k(_ptr(rec4), _ptr(conv4), _ptr(m_slot), cx, rx, n_blocks, rec_elems, conv_elems,
+                                      _stream(rec4)), "acceptsel11k")
+
+
 def argmax_merge(keys: torch.Tensor, out_max=None, out_idx=None, drafts=None, accept_out=None):
     n_shards, m = keys.shape
     dev = keys.device
@@ -276,5 +298,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
