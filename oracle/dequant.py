@@ -94,7 +94,42 @@ def dequant_iq4xs(raw: np.ndarray, k: int) -> np.ndarray:
     return w.reshape(n, k).astype(np.float32)
 
 
-_DQ = {"iq3_xxs": dequant_iq3xxs, "q6_k": dequant_q6k, "iq4_xs": dequant_iq4xs}
+def _scale_min_k4(sc: np.ndarray):
+    """The 12 packed scale bytes of a K-quant block -> (scale, min) uint8 [..., 8]:
+    sub-blocks 0..3 take the low 6 bits of bytes j / j+4; 4..7 join a nibble of
+    byte j+4 with the top 2 bits of byte j-4 / j (ggml get_scale_min_k4)."""
+    s = np.empty(sc.shape[:-1] + (8,), dtype=np.uint8)
+    m = np.empty_like(s)
+    s[..., :4] = sc[..., 0:4] & 63
+    m[..., :4] = sc[..., 4:8] & 63
+    s[..., 4:] = (sc[..., 8:12] & 0xF) | ((sc[..., 0:4] >> 6) << 4)
+    m[..., 4:] = (sc[..., 8:12] >> 4) | ((sc[..., 4:8] >> 6) << 4)
+    return s, m
+
+
+def dequant_q4k(raw: np.ndarray, k: int) -> np.ndarray:
+    """Q4_K rows (d f16 | dmin f16 | scales[12] | qs[128]) -> f32 [n, k].
+
+    Sub-block s (32 weights): w = (d * sc_s) * q - dmin * mn_s, q the low nibbles of
+    qs[32j .. 32j+32) for s = 2j and the high nibbles for s = 2j+1.  Follows the
+    v-row branch of engine/aq3k8v11.cu:156-172 and the reference's numpy port
+    engine/mm/mm_mtp_anchor.py:47-80 (dq_q4_k_np), including its fp32 evaluation
+    order (one rounding, in the subtraction)."""
+    n = raw.shape[0]
+    nb = k // QK
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 144)
+    d = _f16(blk[..., 0:2])                                      # [n, nb]
+    dmin = _f16(blk[..., 2:4])
+    sc, mn = _scale_min_k4(blk[..., 4:16])                        # [n, nb, 8]
+    qs = blk[..., 16:144].reshape(n, nb, 4, 32)
+    q = np.stack([qs & 0xF, qs >> 4], axis=3).reshape(n, nb, 8, 32).astype(np.float32)
+    d1 = d[..., None] * sc.astype(np.float32)                     # exact in fp32
+    m1 = dmin[..., None] * mn.astype(np.float32)                  # exact in fp32
+    w = d1[..., None] * q - m1[..., None]
+    return w.reshape(n, k).astype(np.float32)
+
+
+_DQ = {"iq3_xxs": dequant_iq3xxs, "q6_k": dequant_q6k, "iq4_xs": dequant_iq4xs, "q4_k": dequant_q4k}
 
 
 def dequant(qtype: str, raw: np.ndarray, k: int, chunk_rows: int = 8192) -> np.ndarray:

@@ -7,8 +7,8 @@ Run in a container where the reference tree is mounted (default
 
 It imports the reference's OWN numpy ports -- engine/mm/MM_P2_ports.py
 (dq_q6_k, gxup4_ref, gxdn4_ref, gxdn6_ref, rt_prod_ref, cmb_ref),
-engine/mm/MM_P0_d2_repack.py (dq_iq4_xs) and engine/pack_w4.py
-(dequant_iq3xxs) -- with the ggml tables they would take from tinygrad injected
+engine/mm/MM_P0_d2_repack.py (dq_iq4_xs), engine/pack_w4.py
+(dequant_iq3xxs) and engine/mm/mm_mtp_anchor.py (dq_q4_k_np) -- with the ggml tables they would take from tinygrad injected
 from gguf-py, runs them on seeded synthetic blocks, and writes the inputs and
 outputs to tests/golden/golden_v1.npz.  Nothing at test time reads the
 reference tree; the tests only read the .npz.
@@ -45,6 +45,20 @@ def load_reference():
     P2.get_tables = lambda: tables
     pack_w4._GRID = np.asarray(quants.IQ3_XXS.grid, dtype=np.float32).reshape(256, 4)
     return P0, P2, pack_w4, quants
+
+
+def reference_q4k_port(P0):
+    """dq_q4_k_np and its helper from engine/mm/mm_mtp_anchor.py, taken from that
+    file as written (the module's own imports need the reference's model tree, so
+    only these two definitions are compiled and run)."""
+    import ast
+
+    path = os.path.join(REF, "engine", "mm", "mm_mtp_anchor.py")
+    tree = ast.parse(open(path).read(), path)
+    defs = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in ("_get_scale_min_k4", "dq_q4_k_np")]
+    ns = {"np": np, "_f16": P0._f16}
+    exec(compile(ast.Module(body=defs, type_ignores=[]), path, "exec"), ns)
+    return ns["dq_q4_k_np"]
 
 
 def region_repack_iq3(raw: np.ndarray, k: int) -> np.ndarray:
@@ -106,6 +120,14 @@ def main():
 
     gates, sg, part, shared = cmb_inputs()
     g["cmb_ref"] = P2.cmb_ref(gates, sg, part, shared)
+
+    # Q4_K (the v rows of aq3k8v11): the reference's numpy port dq_q4_k_np
+    # (engine/mm/mm_mtp_anchor.py:47-80), run as defined there, and gguf-py
+    rng4 = np.random.default_rng(20261202)
+    q4 = synth.q4k_blocks(rng4, 8, 512)
+    g["q4k_raw"] = q4
+    g["q4k_ref"] = reference_q4k_port(P0)(q4, 512)
+    g["q4k_gguf_f32"] = quants.dequantize(q4, quants.GGMLQuantizationType.Q4_K).reshape(8, 512)
 
     out = os.path.join(HERE, "golden_v1.npz")
     np.savez_compressed(out, **g)

@@ -98,3 +98,10 @@ def test_argmax_tie_and_nan_rules():
     lg = np.array([[1.0, 3.0, 3.0, np.nan], [np.nan, np.nan, np.nan, np.nan], [-0.0, 0.0, -1, -2]])
     mx, idx = oracle.argmax_rows(lg)
     assert list(idx) == [1, 0, 0]
+
+
+def test_q4k_dequant_bit_exact(golden):
+    # the reference's numpy port (engine/mm/mm_mtp_anchor.py dq_q4_k_np) and gguf-py
+    got = oracle.dequant_q4k(golden["q4k_raw"], 512)
+    assert np.array_equal(got.view(np.uint32), golden["q4k_ref"].astype(np.float32).view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), golden["q4k_gguf_f32"].astype(np.float32).view(np.uint32))

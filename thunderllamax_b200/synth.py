@@ -23,8 +23,8 @@ from __future__ import annotations
 import numpy as np
 
 QK = 256
-BLOCK_BYTES = {"iq3_xxs": 98, "q6_k": 210, "iq4_xs": 136}
-GGML_TYPE = {"iq3_xxs": 18, "q6_k": 14, "iq4_xs": 23}
+BLOCK_BYTES = {"iq3_xxs": 98, "q6_k": 210, "iq4_xs": 136, "q4_k": 144}
+GGML_TYPE = {"iq3_xxs": 18, "q6_k": 14, "iq4_xs": 23, "q4_k": 12}
 
 
 def row_bytes(qtype: str, k: int) -> int:
@@ -64,7 +64,18 @@ def iq4xs_blocks(rng: np.random.Generator, n_rows: int, k: int) -> np.ndarray:
     return blk.reshape(n_rows, nb * 136)
 
 
-BLOCK_GEN = {"iq3_xxs": iq3xxs_blocks, "q6_k": q6k_blocks, "iq4_xs": iq4xs_blocks}
+def q4k_blocks(rng: np.random.Generator, n_rows: int, k: int) -> np.ndarray:
+    """Q4_K blocks (d f16 | dmin f16 | scales[12] | qs[128]): random 6-bit scales and
+    mins, d and dmin of the magnitude a trained checkpoint's v projection has."""
+    nb = k // QK
+    blk = np.empty((n_rows, nb, 144), dtype=np.uint8)
+    blk[..., 0:2] = _f16_bytes(rng.uniform(1e-4, 1e-3, (n_rows, nb)))
+    blk[..., 2:4] = _f16_bytes(rng.uniform(1e-4, 1e-3, (n_rows, nb)))
+    blk[..., 4:144] = rng.integers(0, 256, (n_rows, nb, 140), dtype=np.uint8)
+    return blk.reshape(n_rows, nb * 144)
+
+
+BLOCK_GEN = {"iq3_xxs": iq3xxs_blocks, "q6_k": q6k_blocks, "iq4_xs": iq4xs_blocks, "q4_k": q4k_blocks}
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
