@@ -24,6 +24,7 @@ extern "C" {
 #endif
 
 /* ggml type ids (GGUF tensor types) */
+#define TLX_Q4_K 12   /* STORE GEMV only (the attention v rows) */
 #define TLX_Q6_K 14
 #define TLX_IQ3_XXS 18
 #define TLX_IQ4_XS 23
@@ -35,6 +36,9 @@ extern "C" {
  * or tlx_ffn_gate_up with gact_dtype = TLX_DT_IMAGE): x points at the image, ldx
  * is ignored, one column per token */
 #define TLX_DT_IMAGE 100
+/* (Q4_K GEMVs also read the per-sub-block sums of x that tlx_stage_activations
+ * writes into the image; an image written by tlx_ffn_gate_up carries none, so give
+ * a Q4_K GEMV raw activations or a tlx_stage_activations image.) */
 /* gemv modes for tlx_gemv_workspace_bytes */
 #define TLX_MODE_STORE 0
 #define TLX_MODE_GATE_UP 1
@@ -190,6 +194,21 @@ int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, i
                   int32_t* cyc_slot, int32_t* pos_slot, int32_t* cur_slot, int32_t* tok_hist, float* h_seed,
                   const float* hd_d0, const float* hd_d1, float* dhd_seed, int32_t* emit, const int32_t* l_hist,
                   int dim, void* stream);
+
+/* aq3k8v11: the attention q / k / v projections of the probe trunk over m rows
+ * (engine/aq3k8v11.cu:88-179): q = Wq x (IQ3_XXS, nq rows), k = Wk x (IQ3_XXS, nk
+ * rows), v = Wv x (Q4_K, nv rows) for x [m][k] fp16 or bf16 (ld ldx); outputs fp16
+ * [m][nq] / [m][nk] / [m][nv].  Weights tiled (tlx_pack_tiles).  x is staged once
+ * and the three GEMVs share it.  Workspace: tlx_aq3k8v11_workspace_bytes, zeroed
+ * once (tlx_workspace_init) and reused.  The reference shapes are nq = 12288,
+ * nk = nv = 1024, k = 5120, m = 11. */
+size_t tlx_aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype);
+int tlx_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
+                 int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
+                 void* v_out, void* ws, size_t ws_bytes, void* stream);
+/* the workspace's error bits (OR over the three GEMVs; synchronous read) */
+int tlx_aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype,
+                       uint32_t* err_out);
 
 /* acceptsel11k: commit the accepted GDN state (engine/acceptsel11k.cu:8-40).
  * rec4 is [n_blocks][5][rec_elems] fp32 and conv4 [n_blocks][5][conv_elems] fp32,

@@ -47,10 +47,10 @@ def check_rows(got, ref, tight=TIGHT):
         assert err <= tight * nrm, (t, err, nrm)
 
 
-GEN = {"q6_k": synth.q6k_blocks, "iq3_xxs": synth.iq3xxs_blocks}
+GEN = {"q6_k": synth.q6k_blocks, "iq3_xxs": synth.iq3xxs_blocks, "q4_k": synth.q4k_blocks}
 
 
-@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs"])
+@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k"])
 @pytest.mark.parametrize("n,k,m,dtype", [
     (16, 256, 1, torch.bfloat16),
     (100, 512, 3, torch.bfloat16),
@@ -72,7 +72,7 @@ def test_gemv_vs_oracle(qtype, n, k, m, dtype):
     check_rows(y.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs"])
+@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k"])
 def test_gemv_split_tiles_and_segments(qtype):
     # few CTAs + long k: tiles split across warps and k-segments, reduced by the
     # last arriving piece in fixed order; residual epilogue; results repeatable
@@ -269,6 +269,38 @@ def test_h_argmax_side_effects():
     assert tok.item() == 0 and pos.item() == ref_pos == 19
     assert np.array_equal(t_hist.cpu().numpy(), ref_hist)
     assert ref_hist[17] == ref_idx
+
+
+@pytest.mark.parametrize("nq,nk,nv,k,dtype", [(256, 128, 160, 512, torch.float16), (12288, 1024, 1024, 5120, torch.bfloat16)])
+def test_aq3k8v11_vs_oracle(nq, nk, nv, k, dtype):
+    # the attention q / k (IQ3_XXS) / v (Q4_K) projections over 11 rows, fp16 outputs
+    rng = np.random.default_rng(nq + nv)
+    m = 11
+    rq, rk, rv = synth.iq3xxs_blocks(rng, nq, k), synth.iq3xxs_blocks(rng, nk, k), synth.q4k_blocks(rng, nv, k)
+    x, x64 = x_tensor(rng, m, k, dtype)
+    wq, wk, wv = ops.pack_tiles("iq3_xxs", rq, k), ops.pack_tiles("iq3_xxs", rk, k), ops.pack_tiles("q4_k", rv, k)
+    proj = ops.AttnProjections(m, k, nq, nk, nv, dtype)
+    q, kk, v = proj(wq, wk, wv, x)
+    q2, kk2, v2 = proj(wq, wk, wv, x)
+    torch.cuda.synchronize()
+    assert proj.error() == 0
+    for got, raw, qt in ((q, rq, "iq3_xxs"), (kk, rk, "iq3_xxs"), (v, rv, "q4_k")):
+        ref = oracle.matvec_f64(oracle.dequant(qt, raw, k), x64)
+        check_rows(got.float().cpu().numpy(), ref, tight=1e-3)   # fp16 outputs: one fp16 rounding
+    assert torch.equal(q, q2) and torch.equal(kk, kk2) and torch.equal(v, v2)
+
+
+def test_q4k_gemv_reads_a_staged_image():
+    # a tlx_stage_activations image carries the sub-block sums the Q4_K min term reads
+    rng = np.random.default_rng(31)
+    n, k, m = 300, 1024, 11
+    raw = synth.q4k_blocks(rng, n, k)
+    x, x64 = x_tensor(rng, m, k, torch.bfloat16)
+    w = ops.pack_tiles("q4_k", raw, k)
+    img = ops.stage(x)
+    y = ops.gemv("q4_k", w, img, n, ops.Workspace.for_shape(ops.MODE_STORE, "q4_k", n, k, m, "image"))
+    torch.cuda.synchronize()
+    check_rows(y.cpu().numpy(), oracle.matvec_f64(oracle.dequant("q4_k", raw, k), x64))
 
 
 def _sel_buffers(B, R, C, seed):

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 import oracle
+from oracle.dequant import _scale_min_k4
 from thunderllamax_b200 import _lib, ops, synth
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -39,7 +40,7 @@ def test_error_strings_and_host_argument_checks():
 
 
 @pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98),
-                                          ("iq4_xs", synth.iq4xs_blocks, 136)])
+                                          ("iq4_xs", synth.iq4xs_blocks, 136), ("q4_k", synth.q4k_blocks, 144)])
 def test_pack_unpack_round_trip(qtype, gen, bb):
     rng = np.random.default_rng(1)
     for n in (1, 16, 37):
@@ -127,6 +128,44 @@ def emulate_iq3(tiled, n_rows, k):
                             kk = b * 256 + 64 * q + 4 * m + j
                             W[row, kk] = (d16[g, rr] * np.float32(0.25)) * np.float32(a)
     return W[:n_rows]
+
+
+def emulate_q4k(tiled, n_rows, k):
+    """Q4_K as the device decodes it (formats.cuh q4_load / q4_mma): the exact
+    integers sc * v per weight and the sub-block mins, combined as d * (sc v) - dmin * mn
+    (the kernel applies d and dmin to the sums; per weight this is the same value)."""
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    ch = tiled.reshape(T, nb, 2304)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                for rr in range(2):
+                    row = g + 8 * rr
+                    hdr = c[2048 + 16 * row:2064 + 16 * row]
+                    d = np.float32(hdr[0:2].view(np.float16)[0])
+                    dmin = np.float32(hdr[2:4].view(np.float16)[0])
+                    sc, mn = _scale_min_k4(hdr[4:16][None])
+                    qs = np.concatenate([c[((2 * rr + hf) * 32 + lane) * 16:][:16] for hf in range(2)])
+                    for m in range(16):
+                        s_ = 2 * q + (m >> 3)
+                        for i in range(4):
+                            byte = int(qs[4 * (m & 7) + i])
+                            v = (byte & 0xF) if m < 8 else (byte >> 4)
+                            a = np.float32(int(sc[0, s_]) * v)          # exact fp16 integer
+                            kk = b * 256 + 64 * q + 4 * m + i
+                            W[t * 16 + row, kk] = d * a - dmin * np.float32(int(mn[0, s_]))
+    return W[:n_rows]
+
+
+def test_q4k_tile_decode_matches_oracle_exactly():
+    rng = np.random.default_rng(10)
+    raw = synth.q4k_blocks(rng, 19, 512)
+    got = emulate_q4k(ops.pack_tiles_host("q4_k", raw, 512), 19, 512)
+    assert np.array_equal(got.view(np.uint32), oracle.dequant_q4k(raw, 512).view(np.uint32))
 
 
 def test_q6_tile_decode_matches_oracle_exactly():

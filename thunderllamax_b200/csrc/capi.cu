@@ -18,7 +18,7 @@ int g_max_ctas = 0;  // 0 = one CTA per SM
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-bool valid_qtype(int qt) { return qt == QT_Q6_K || qt == QT_IQ3_XXS; }
+bool valid_qtype(int qt) { return qt == QT_Q6_K || qt == QT_IQ3_XXS || qt == QT_Q4_K; }
 // formats the tile packers know (IQ4_XS is read by the MoE kernels only)
 bool valid_pack_qtype(int qt) { return valid_qtype(qt) || qt == QT_IQ4_XS; }
 
@@ -290,7 +290,13 @@ int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, vo
     for (int b = 0; b < nb; ++b) {
       const uint8_t* c = s + (t * nb + b) * static_cast<int64_t>(ch);
       uint8_t* blk = d + row * row_bytes + static_cast<int64_t>(b) * bb;
-      if (qtype == QT_IQ4_XS) {
+      if (qtype == QT_Q4_K) {
+        for (int i = 0; i < 16; ++i) blk[i] = c[2048 + r * 16 + i];
+        for (int q = 0; q < 4; ++q)
+          for (int hf = 0; hf < 2; ++hf)
+            for (int j = 0; j < 16; ++j)
+              blk[16 + 32 * q + 16 * hf + j] = c[((2 * rr + hf) * 32 + 4 * g + q) * 16 + j];
+      } else if (qtype == QT_IQ4_XS) {
         for (int i = 0; i < 8; ++i) blk[i] = c[2048 + g * 16 + rr * 8 + i];
         for (int q = 0; q < 4; ++q)
           for (int hf = 0; hf < 2; ++hf)
@@ -428,6 +434,22 @@ int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const flo
     acceptsel_kernel<float><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, n_blocks, rec_elems,
                                                                     conv_elems);
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+size_t tlx_aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype) {
+  return aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, g_max_ctas);
+}
+
+int tlx_aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype,
+                       uint32_t* err_out) {
+  return aq3k8v11_error(ws, m, k, nq, nk, nv, x_dtype, g_max_ctas, err_out);
+}
+
+int tlx_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
+                 int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
+                 void* v_out, void* ws, size_t ws_bytes, void* stream) {
+  return run_aq3k8v11(wq, wk, wv, grid, x, x_dtype, ldx, m, k, nq, nk, nv, q_out, k_out, v_out, ws, ws_bytes,
+                      g_max_ctas, as_stream(stream));
 }
 
 int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, int32_t* pos_slot, int32_t* tok_hist,

@@ -31,16 +31,17 @@
 
 namespace tlx {
 
-enum QType : int { QT_Q6_K = 14, QT_IQ3_XXS = 18, QT_IQ4_XS = 23 };
+enum QType : int { QT_Q4_K = 12, QT_Q6_K = 14, QT_IQ3_XXS = 18, QT_IQ4_XS = 23 };
 
 constexpr int kTileRows = 16;
 constexpr int kQK = 256;
 constexpr uint32_t kChunkQ6 = 16 * 210;     // 3360
 constexpr uint32_t kChunkIq3 = 16 * 98;     // 1568
 constexpr uint32_t kChunkIq4 = 16 * 136;    // 2176
+constexpr uint32_t kChunkQ4 = 16 * 144;     // 2304
 
 __host__ __device__ constexpr uint32_t block_bytes(int qt) {
-  return qt == QT_Q6_K ? 210u : (qt == QT_IQ4_XS ? 136u : 98u);
+  return qt == QT_Q6_K ? 210u : (qt == QT_IQ4_XS ? 136u : (qt == QT_Q4_K ? 144u : 98u));
 }
 __host__ __device__ constexpr uint32_t chunk_bytes(int qt) { return 16u * block_bytes(qt); }
 
@@ -145,9 +146,31 @@ TLX_HD inline void pack_iq4_lane(const uint8_t* const rows[16], int lane, uint8_
     }
 }
 
+// Q4_K chunk (GGUF block d f16 | dmin f16 | scales[12] | qs[128]; the v rows of the
+// attention projection).  Lane l = 4g + q owns sub-blocks 2q (low nibbles) and 2q+1
+// (high nibbles) of rows g and g+8: the 32 bytes qs[32q .. 32q+32) of each row,
+// stored as four 16-byte units u = 2*rr + half at (u*32 + l)*16 (the IQ4_XS lane
+// placement).  Row r's 16-byte block header (d, dmin, the 12 packed scale/min
+// bytes) follows at 2048 + 16r.  Zero rows are all-zero (d = dmin = 0).
+TLX_HD inline void pack_q4k_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint8_t* blk = rows[g + 8 * rr];
+    for (int hf = 0; hf < 2; ++hf)
+      for (int j = 0; j < 16; ++j)
+        out[((2 * rr + hf) * 32 + lane) * 16 + j] = blk ? blk[16 + 32 * q + 16 * hf + j] : 0;
+  }
+  if (q == 0)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      for (int i = 0; i < 16; ++i) out[2048 + (g + 8 * rr) * 16 + i] = blk ? blk[i] : 0;
+    }
+}
+
 TLX_HD inline void pack_lane(int qt, const uint8_t* const rows[16], int lane, uint8_t* out) {
   if (qt == QT_Q6_K) pack_q6_lane(rows, lane, out);
   else if (qt == QT_IQ4_XS) pack_iq4_lane(rows, lane, out);
+  else if (qt == QT_Q4_K) pack_q4k_lane(rows, lane, out);
   else pack_iq3_lane(rows, lane, out);
 }
 
@@ -315,6 +338,83 @@ __device__ __forceinline__ float2 iq3_block_scale(const Iq3Lane& s) {
   const __half2 h = *reinterpret_cast<const __half2*>(&s.d);
   const float2 f = __half22float2(h);
   return make_float2(f.x * 0.25f, f.y * 0.25f);   // d * (2s+1)/4 = (d/4) * (2s+1)
+}
+
+// Q4_K: per-block lane state.  A low nibble v is decoded as the fp16 1024 + v and a
+// high nibble as 1024 + 16v (mantissa offset 4); one fma per pair then gives the
+// exact integer sc * v: (1024 + v) * sc - 1024 sc, resp. (1024 + 16v) * (sc/16) -
+// 64 sc (sc, mn <= 63: every constant and product is an exact fp16 integer).  The
+// min term -dmin * sum_s mn_s * sum_{k in s} x_k is one more mma per block: A' holds
+// the lane's mins (k' = sub-block, duplicated for the two fp16 parts of each sum),
+// B' the activation image's sub-block sums (entries 64..67 of each row).
+struct Q4Lane {
+  uint32_t w[2][8];    // qs words of rows g / g+8 (bytes 4i .. 4i+3 of the lane's 32)
+  uint32_t slo[2], clo[2], shi[2], chi[2];  // fp16x2 fma constants per row
+  uint32_t mn[2];      // fp16x2 (mn_{2q}, mn_{2q+1}) per row
+  float d[2], dmin[2];
+};
+
+// 6-bit (scale, min) of sub-block j from the 12 packed bytes in words h1..h3 (bytes
+// 4..15 of the block header: h1 = scales[0..3], h2 = [4..7], h3 = [8..11])
+__device__ __forceinline__ void q4_scale_min(uint32_t h1, uint32_t h2, uint32_t h3, int j, uint32_t& sc,
+                                             uint32_t& mn) {
+  const int jj = j & 3;
+  const uint32_t b0 = (h1 >> (8 * jj)) & 0xFFu;   // scales[jj]
+  const uint32_t b4 = (h2 >> (8 * jj)) & 0xFFu;   // scales[jj + 4]
+  const uint32_t b8 = (h3 >> (8 * jj)) & 0xFFu;   // scales[jj + 8]
+  if (j < 4) {
+    sc = b0 & 63u;
+    mn = b4 & 63u;
+  } else {
+    sc = (b8 & 0xFu) | ((b0 >> 6) << 4);
+    mn = (b8 >> 4) | ((b4 >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ void q4_load(const uint8_t* chunk, int lane, Q4Lane& s) {
+  const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const uint4 v = *reinterpret_cast<const uint4*>(chunk + ((2 * rr + hf) * 32 + lane) * 16);
+      s.w[rr][4 * hf + 0] = v.x;
+      s.w[rr][4 * hf + 1] = v.y;
+      s.w[rr][4 * hf + 2] = v.z;
+      s.w[rr][4 * hf + 3] = v.w;
+    }
+    const uint4 h = *reinterpret_cast<const uint4*>(chunk + 2048 + (g + 8 * rr) * 16);
+    const __half2 dd = *reinterpret_cast<const __half2*>(&h.x);
+    s.d[rr] = __low2float(dd);
+    s.dmin[rr] = __high2float(dd);
+    uint32_t sc0, mn0, sc1, mn1;
+    q4_scale_min(h.y, h.z, h.w, 2 * q, sc0, mn0);
+    q4_scale_min(h.y, h.z, h.w, 2 * q + 1, sc1, mn1);
+    const __half f0 = __uint2half_rn(sc0), f1 = __uint2half_rn(sc1);
+    s.slo[rr] = h2_bits(__halves2half2(f0, f0));
+    s.clo[rr] = h2_bits(__halves2half2(__float2half_rn(-1024.0f * sc0), __float2half_rn(-1024.0f * sc0)));
+    s.shi[rr] = h2_bits(__halves2half2(__float2half_rn(sc1 * 0.0625f), __float2half_rn(sc1 * 0.0625f)));
+    s.chi[rr] = h2_bits(__halves2half2(__float2half_rn(-64.0f * sc1), __float2half_rn(-64.0f * sc1)));
+    s.mn[rr] = h2_bits(__halves2half2(__uint2half_rn(mn0), __uint2half_rn(mn1)));
+  }
+}
+
+// decode mma m (0..15): k = 64q + 4m + {0..3} = element 4(m & 7) + {0..3} of
+// sub-block 2q (m < 8, low nibbles) or 2q+1 (m >= 8, high nibbles)
+__device__ __forceinline__ void q4_mma(const Q4Lane& s, int m, uint32_t (&a)[4]) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint32_t w = s.w[rr][m & 7];
+    const uint32_t p01 = prmt(w, 0u, 0x4140u);  // bytes 0, 1 -> low bytes of the halves
+    const uint32_t p23 = prmt(w, 0u, 0x4342u);
+    if (m < 8) {
+      a[rr] = hfma2_u((p01 & 0x000F000Fu) | kMagic, s.slo[rr], s.clo[rr]);
+      a[rr + 2] = hfma2_u((p23 & 0x000F000Fu) | kMagic, s.slo[rr], s.clo[rr]);
+    } else {
+      a[rr] = hfma2_u((p01 & 0x00F000F0u) | kMagic, s.shi[rr], s.chi[rr]);
+      a[rr + 2] = hfma2_u((p23 & 0x00F000F0u) | kMagic, s.shi[rr], s.chi[rr]);
+    }
+  }
 }
 
 #endif  // __CUDACC__

@@ -157,6 +157,33 @@ __global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_
   }
 }
 
+// Per-sub-block sums of the staged activations, for Q4_K's min term: entry 64 + q of
+// image row (block b, column c) = {hi(S_2q), hi(S_2q+1), lo(S_2q), lo(S_2q+1)} where
+// S_s = sum of x[c][256b + 32s .. +32) over the fp16 values in the image (summed in
+// fp32) and hi / lo its two-fp16 split, so the min-term mma sees S to ~2^-22.
+__global__ void stage_sums_kernel(int NB, int MC, uint2* __restrict__ img) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int64_t total = static_cast<int64_t>(NB) * MC * 4;
+  for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < total;
+       gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int q = static_cast<int>(gi & 3);
+    uint2* row = img + (gi >> 2) * kImageRow;
+    float sum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const uint2 e = row[m * 4 + q];
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&e.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&e.y));
+      sum[m >> 3] += (a.x + a.y) + (b.x + b.y);
+    }
+    const __half h0 = __float2half_rn(sum[0]), h1 = __float2half_rn(sum[1]);
+    const __half l0 = __float2half_rn(sum[0] - __half2float(h0)), l1 = __float2half_rn(sum[1] - __half2float(h1));
+    const __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+    row[64 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&hh), *reinterpret_cast<const uint32_t*>(&ll));
+  }
+}
+
 // one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B).
 // xb0 / xb1: this lane's image rows (tokens g and g+8, clamped to valid columns;
 // clamped columns only feed accumulator columns that are never read) of the block
@@ -181,7 +208,42 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       b[1][1] = v1.y;
     }
   };
-  if constexpr (QT == QT_Q6_K) {
+  if constexpr (QT == QT_Q4_K) {
+    // Q4_K (single matrix): acc += d * sum (sc q) x  -  dmin * sum_s mn_s xsum_s
+    static_assert(NMAT == 1, "Q4_K is read by the STORE epilogue only");
+    Q4Lane s;
+    q4_load(chunk[0], lane, s);
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      uint32_t b[NT][2];
+      load_b(m, b);
+      uint32_t af[4];
+      q4_mma(s, m, af);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816(tmp[0][nt], af, b[nt][0], b[nt][1]);
+    }
+    // min term: A' = the lane's mins (sub-blocks 2q, 2q+1; k' and 8 + k' alike), B' =
+    // the image's per-sub-block sums of x in two fp16 parts (entry 64 + q)
+    float tmin[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmin[nt][i] = 0.f;
+    {
+      uint32_t b[NT][2];
+      load_b(16, b);
+      const uint32_t am[4] = {s.mn[0], s.mn[1], s.mn[0], s.mn[1]};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816(tmin[nt], am, b[nt][0], b[nt][1]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[0][nt][0] = fmaf(-s.dmin[0], tmin[nt][0], fmaf(s.d[0], tmp[0][nt][0], acc[0][nt][0]));
+      acc[0][nt][1] = fmaf(-s.dmin[0], tmin[nt][1], fmaf(s.d[0], tmp[0][nt][1], acc[0][nt][1]));
+      acc[0][nt][2] = fmaf(-s.dmin[1], tmin[nt][2], fmaf(s.d[1], tmp[0][nt][2], acc[0][nt][2]));
+      acc[0][nt][3] = fmaf(-s.dmin[1], tmin[nt][3], fmaf(s.d[1], tmp[0][nt][3], acc[0][nt][3]));
+    }
+  } else if constexpr (QT == QT_Q6_K) {
 #pragma unroll
     for (int a = 0; a < NMAT; ++a) {
       Q6Lane s;
@@ -220,6 +282,7 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       }
     }
   }
+  if constexpr (QT != QT_Q4_K) {
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
 #pragma unroll
@@ -229,6 +292,7 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       acc[a][nt][2] = fmaf(scale[a].y, tmp[a][nt][2], acc[a][nt][2]);
       acc[a][nt][3] = fmaf(scale[a].y, tmp[a][nt][3], acc[a][nt][3]);
     }
+  }
 }
 
 // tile epilogue on complete sums (fragment order in registers); epi = 1 KB per matrix of
@@ -615,6 +679,9 @@ template <> struct Cfg<QT_Q6_K, EPI_STORE> { static constexpr int WPC = 16, STAG
 template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 16, STAGES = 2; };
 template <> struct Cfg<QT_Q6_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
 template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_Q4_K, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_Q4_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };   // (not launched)
+template <> struct Cfg<QT_Q4_K, EPI_ARGMAX> { static constexpr int WPC = 16, STAGES = 2; };  // (not launched)
 template <> struct Cfg<QT_IQ3_XXS, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 3; };
 template <> struct Cfg<QT_IQ3_XXS, EPI_GATEUP> { static constexpr int WPC = 12, STAGES = 2; };
 
@@ -631,6 +698,7 @@ static void cfg_for(int qt, int epi, int& wpc, int& stages) {
   TLX_CFG(QT_IQ3_XXS, EPI_STORE)
   TLX_CFG(QT_IQ3_XXS, EPI_ARGMAX)
   TLX_CFG(QT_IQ3_XXS, EPI_GATEUP)
+  TLX_CFG(QT_Q4_K, EPI_STORE)
 #undef TLX_CFG
   wpc = 8;
   stages = 2;
@@ -639,7 +707,8 @@ static void cfg_for(int qt, int epi, int& wpc, int& stages) {
 static int cols_per_token(int x_dtype) { return x_dtype == DT_F32 ? 3 : 1; }
 
 static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, Plan& P) {
-  if (qt != QT_Q6_K && qt != QT_IQ3_XXS) return TLX_ERR_QTYPE;
+  if (qt != QT_Q6_K && qt != QT_IQ3_XXS && qt != QT_Q4_K) return TLX_ERR_QTYPE;
+  if (qt == QT_Q4_K && epi != EPI_STORE) return TLX_ERR_QTYPE;  // Q4_K: plain matvec (v rows)
   if (n_rows <= 0 || k <= 0 || (k % kQK) != 0) return TLX_ERR_SHAPE;
   if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16 && x_dtype != DT_IMAGE) return TLX_ERR_DTYPE;
   P.CG = cols_per_token(x_dtype);
@@ -704,6 +773,8 @@ static int launch_t(const Plan& P, const GemvParams& gp, cudaStream_t stream) {
 
 template <int EPI>
 static int dispatch(int qt, const Plan& P, const GemvParams& gp, cudaStream_t s) {
+  if constexpr (EPI == EPI_STORE)
+    if (qt == QT_Q4_K) return P.NT == 1 ? launch_t<QT_Q4_K, 1, EPI>(P, gp, s) : launch_t<QT_Q4_K, 2, EPI>(P, gp, s);
   if (qt == QT_Q6_K) return P.NT == 1 ? launch_t<QT_Q6_K, 1, EPI>(P, gp, s) : launch_t<QT_Q6_K, 2, EPI>(P, gp, s);
   return P.NT == 1 ? launch_t<QT_IQ3_XXS, 1, EPI>(P, gp, s) : launch_t<QT_IQ3_XXS, 2, EPI>(P, gp, s);
 }
@@ -735,7 +806,17 @@ size_t activation_image_bytes(int m, int64_t k, int x_dtype) {
   return static_cast<size_t>(k / kQK) * mc * kImageRowBytes;
 }
 
+static int stage_image(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, bool sums,
+                       cudaStream_t stream);
+
+// the public staging entry: the image carries the Q4_K sub-block sums too, so any
+// GEMV (Q4_K included) can read it
 int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream) {
+  return stage_image(x, x_dtype, ldx, m, k, image, true, stream);
+}
+
+static int stage_image(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, bool sums,
+                       cudaStream_t stream) {
   if (!x || !image) return TLX_ERR_NULL;
   if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
   if (activation_image_bytes(m, k, x_dtype) == 0) return TLX_ERR_SHAPE;
@@ -744,8 +825,13 @@ int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k,
   const int cg = cols_per_token(x_dtype);
   const int64_t groups = static_cast<int64_t>(m) * (k / 4);
   const int blocks = static_cast<int>(std::min<int64_t>((groups + 255) / 256, 4096));
-  return launch_pdl(stage_image_kernel, dim3(blocks), dim3(256), 0, stream, x, x_dtype, ldx, m, cg, m * cg, k,
-                    static_cast<uint2*>(image));
+  int rc = launch_pdl(stage_image_kernel, dim3(blocks), dim3(256), 0, stream, x, x_dtype, ldx, m, cg, m * cg, k,
+                      static_cast<uint2*>(image));
+  if (rc || !sums) return rc;
+  const int nb = static_cast<int>(k / kQK);
+  const int64_t items = static_cast<int64_t>(nb) * m * cg * 4;
+  return launch_pdl(stage_sums_kernel, dim3(static_cast<unsigned>(std::min<int64_t>((items + 255) / 256, 1024))),
+                    dim3(256), 0, stream, nb, m * cg, static_cast<uint2*>(image));
 }
 
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
@@ -780,7 +866,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint2* ximg = static_cast<const uint2*>(x);
   if (x_dtype != DT_IMAGE) {
-    rc = stage_activations(x, x_dtype, ldx, m, k, wsb + P.off_img, stream);
+    rc = stage_image(x, x_dtype, ldx, m, k, wsb + P.off_img, qt == QT_Q4_K, stream);
     if (rc) return rc;
     ximg = reinterpret_cast<const uint2*>(wsb + P.off_img);
   }
@@ -821,6 +907,63 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   if (epi == EPI_STORE) return dispatch<EPI_STORE>(qt, P, gp, stream);
   if (epi == EPI_GATEUP) return dispatch<EPI_GATEUP>(qt, P, gp, stream);
   return dispatch<EPI_ARGMAX>(qt, P, gp, stream);
+}
+
+// ---- aq3k8v11: q / k (IQ3_XXS) and v (Q4_K) projections over one staged x ----
+static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
+
+size_t aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas) {
+  if (x_dtype != DT_F16 && x_dtype != DT_BF16) return 0;
+  const size_t img = activation_image_bytes(m, k, x_dtype);
+  const size_t wq = gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas);
+  const size_t wk = gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas);
+  const size_t wv = gemv_workspace_bytes(EPI_STORE, QT_Q4_K, nv, k, m, DT_IMAGE, max_ctas);
+  if (!img || !wq || !wk || !wv) return 0;
+  return al256(img) + al256(wq) + al256(wk) + al256(wv);
+}
+
+int run_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
+                 int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
+                 void* v_out, void* ws, size_t ws_bytes, int max_ctas, cudaStream_t stream) {
+  if (!wq || !wk || !wv || !grid || !x || !q_out || !k_out || !v_out || !ws) return TLX_ERR_NULL;
+  if (x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
+  const size_t need = aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, max_ctas);
+  if (need == 0) return TLX_ERR_SHAPE;
+  if (ws_bytes < need) return TLX_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return TLX_ERR_ALIGN;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  uint8_t* img = p;
+  p += al256(activation_image_bytes(m, k, x_dtype));
+  const size_t bq = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas));
+  const size_t bk = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas));
+  const size_t bv = al256(gemv_workspace_bytes(EPI_STORE, QT_Q4_K, nv, k, m, DT_IMAGE, max_ctas));
+  // x staged once, with the Q4_K sub-block sums; the three projections read it
+  int rc = stage_image(x, x_dtype, ldx, m, k, img, true, stream);
+  if (rc) return rc;
+  rc = run_gemv(EPI_STORE, QT_IQ3_XXS, wq, nullptr, grid, img, DT_IMAGE, 0, m, nq, k, nullptr, 0, q_out, DT_F16, nq,
+                0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p, bq, max_ctas, stream);
+  if (rc) return rc;
+  rc = run_gemv(EPI_STORE, QT_IQ3_XXS, wk, nullptr, grid, img, DT_IMAGE, 0, m, nk, k, nullptr, 0, k_out, DT_F16, nk,
+                0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p + bq, bk, max_ctas, stream);
+  if (rc) return rc;
+  return run_gemv(EPI_STORE, QT_Q4_K, wv, nullptr, nullptr, img, DT_IMAGE, 0, m, nv, k, nullptr, 0, v_out, DT_F16,
+                  nv, 0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p + bq + bk, bv, max_ctas, stream);
+}
+
+// the three GEMVs' error words in an aq3k8v11 workspace (OR of the three)
+int aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas,
+                   uint32_t* err_out) {
+  if (!ws || !err_out) return TLX_ERR_NULL;
+  if (aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, max_ctas) == 0) return TLX_ERR_SHAPE;
+  const uint8_t* p = static_cast<const uint8_t*>(ws) + al256(activation_image_bytes(m, k, x_dtype));
+  const size_t bq = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas));
+  const size_t bk = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas));
+  uint32_t e[3] = {0, 0, 0};
+  const size_t off[3] = {0, bq, bq + bk};
+  for (int i = 0; i < 3; ++i)
+    if (cudaMemcpy(&e[i], p + off[i], 4, cudaMemcpyDeviceToHost) != cudaSuccess) return TLX_ERR_LAUNCH;
+  *err_out = e[0] | e[1] | e[2];
+  return TLX_OK;
 }
 
 size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas) {

@@ -135,6 +135,19 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
     def acc36(amds, drafts, mb, eb, K):
         ops.accept(amds, drafts, int(K), mb=mb, eb=eb)
 
+    attn = {}
+
+    def aq3k8v11(wq, wk, wv4, gridf, xh4, qrow4, krow4, vrow4):
+        # engine/aq3k8v11.cu:88-179: q 12288 / k 1024 (IQ3_XXS) and v 1024 (Q4_K) rows,
+        # fp16 xh4 [rows][dim] -> fp16 [rows][n]
+        del gridf
+        nq, nk, nv = qrow4.numel() // rows, krow4.numel() // rows, vrow4.numel() // rows
+        key = (nq, nk, nv)
+        if key not in attn:
+            attn[key] = ops.AttnProjections(rows, dim, nq, nk, nv, torch.float16)
+        attn[key](wq, wk, wv4, xh4.view(rows, dim), q=qrow4.view(rows, nq), k=krow4.view(rows, nk),
+                  v=vrow4.view(rows, nv))
+
     def acceptsel11k(rec4, conv4, m_slot, *scratch):
         # engine/acceptsel11k.cu:8-40: conv5x..conv11x then rec6x..rec11x, as the reference
         ops.acceptsel11k(rec4, conv4, m_slot, scratch[:7], scratch[7:13])
@@ -145,7 +158,7 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
 
     progs = {"ffn8v11": ffn8v11, "down8nw32_11": down8nw32_11, "head8v11": head8v11, "amx3": amx3,
              "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36, "acceptsel11k": acceptsel11k,
-             "h_argmax": h_argmax}
+             "h_argmax": h_argmax, "aq3k8v11": aq3k8v11}
     return {k: Prog(k, v) for k, v in progs.items()}
 
 

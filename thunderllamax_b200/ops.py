@@ -251,6 +251,37 @@ def h_argmax(logits: torch.Tensor, tok_slot: torch.Tensor, pos_slot: torch.Tenso
                                   _stream(logits)), "h_argmax")
 
 
+class AttnProjections:
+    """aq3k8v11: q / k (IQ3_XXS) and v (Q4_K) projections of m rows of x, one staging
+    of x shared by the three GEMVs (tlx_aq3k8v11).  Outputs fp16 [m][n]."""
+
+    def __init__(self, m: int, k: int, nq: int, nk: int, nv: int, x_dtype=torch.float16, device="cuda"):
+        self.m, self.k, self.nq, self.nk, self.nv = int(m), int(k), int(nq), int(nk), int(nv)
+        self.dt = _DT[x_dtype]
+        nb = int(_lib.lib().tlx_aq3k8v11_workspace_bytes(self.m, self.k, self.nq, self.nk, self.nv, self.dt))
+        if nb == 0:
+            raise TLXError(f"unsupported aq3k8v11 shape m={m} k={k} nq={nq} nk={nk} nv={nv} {x_dtype}")
+        self.ws = Workspace(nb, device)
+
+    def __call__(self, wq, wk, wv, x: torch.Tensor, q=None, k=None, v=None):
+        require_device()
+        if x.dim() != 2 or x.stride(1) != 1 or tuple(x.shape) != (self.m, self.k) or _DT.get(x.dtype) != self.dt:
+            raise TLXError("x must be a row-major [m][k] tensor of the workspace's dtype")
+        q = q if q is not None else torch.empty((self.m, self.nq), dtype=torch.float16, device=x.device)
+        k = k if k is not None else torch.empty((self.m, self.nk), dtype=torch.float16, device=x.device)
+        v = v if v is not None else torch.empty((self.m, self.nv), dtype=torch.float16, device=x.device)
+        check(_lib.lib().tlx_aq3k8v11(_ptr(wq), _ptr(wk), _ptr(wv), _ptr(grid(str(x.device))), _ptr(x), self.dt,
+                                      x.stride(0), self.m, self.k, self.nq, self.nk, self.nv, _ptr(q), _ptr(k),
+                                      _ptr(v), _ptr(self.ws.buf), self.ws.nbytes, _stream(x)), "aq3k8v11")
+        return q, k, v
+
+    def error(self) -> int:
+        e = ctypes.c_uint32(0)
+        check(_lib.lib().tlx_aq3k8v11_error(_ptr(self.ws.buf), self.m, self.k, self.nq, self.nk, self.nv, self.dt,
+                                            ctypes.byref(e)), "aq3k8v11_error")
+        return int(e.value)
+
+
 GDN_BLOCKS, GDN_REC, GDN_CONV = 48, 786432, 30720  # engine/acceptsel11k.cu:22-38
 
 
@@ -298,5 +329,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
