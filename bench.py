@@ -313,6 +313,79 @@ def measure_prefill(args, torch, weights):
             "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
 
 
+def _timed_cold(launch, n, torch):
+    """Mean device time (ms) of `launch` with L2 flushed before each call (a 256 MB
+    read outside the timed events, leaving clean lines): for working sets that would
+    otherwise stay in the 126 MB L2 between iterations."""
+    flush = torch.ones(256 << 18, dtype=torch.int32, device="cuda")
+    total = 0.0
+    for _ in range(n):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        launch()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / n
+
+
+def measure_attn_qkv(args, torch, peak):
+    """aq3k8v11 at the reference shape (q 12288 / k 1024 IQ3_XXS, v 1024 Q4_K, k 5120,
+    11 rows, fp16 x): staging + three GEMVs, cold L2; bytes = weights + x + outputs."""
+    from thunderllamax_b200 import ops, synth
+    from thunderllamax_b200.verify import synth_tiled
+
+    m, k, nq, nk, nv = 11, 5120, 12288, 1024, 1024
+    wq, wk, wv = synth_tiled("iq3_xxs", nq, k, 31), synth_tiled("iq3_xxs", nk, k, 32), synth_tiled("q4_k", nv, k, 33)
+    rng = np.random.default_rng(34)
+    x = torch.from_numpy(synth.bf16_bits_to_f32(synth.bf16_normal(rng, (m, k))).astype(np.float16)).cuda()
+    proj = ops.AttnProjections(m, k, nq, nk, nv, torch.float16)
+    outs = [torch.empty((m, n), dtype=torch.float16, device="cuda") for n in (nq, nk, nv)]
+    for _ in range(3):
+        proj(wq, wk, wv, x, *outs)
+    # one CUDA graph for the five launches, so the timed region is device time
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        proj(wq, wk, wv, x, *outs)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        proj(wq, wk, wv, x, *outs)
+    ms = _timed_cold(graph.replay, 20, torch)
+    nbytes = (nq + nk) * synth.row_bytes("iq3_xxs", k) + nv * synth.row_bytes("q4_k", k) + m * k * 2 + m * (nq + nk + nv) * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "aq3k8v11: q 12288 + k 1024 rows IQ3_XXS, v 1024 rows Q4_K, k 5120, 11 fp16 rows",
+            "us_per_call": round(ms * 1000, 2), "bytes_per_call": int(nbytes), "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "launches_per_call": 5, "graph": "CUDA graph replay",
+            "l2": "flushed before each call",
+            "err_word": proj.error()}
+
+
+def measure_acceptsel(args, torch, peak):
+    """acceptsel11k at the reference size (48 GDN blocks x (786432 + 30720) fp32, m = 7):
+    bytes = the slot read + the live slot written."""
+    from thunderllamax_b200 import ops
+
+    B, R, C = ops.GDN_BLOCKS, ops.GDN_REC, ops.GDN_CONV
+    rec4 = torch.zeros((B, 5, R), device="cuda")
+    conv4 = torch.zeros((B, 5, C), device="cuda")
+    rec_x = [torch.zeros((B, R), device="cuda") for _ in range(6)]
+    conv_x = [torch.zeros((B, C), device="cuda") for _ in range(7)]
+    m_slot = torch.tensor([7], dtype=torch.int32, device="cuda")
+    launch = lambda: ops.acceptsel11k(rec4, conv4, m_slot, conv_x, rec_x)  # noqa: E731
+    for _ in range(3):
+        launch()
+    ms = time_graph(launch, 20, torch)       # 314 MB per call: larger than L2
+    nbytes = 2 * B * (R + C) * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "acceptsel11k: 48 GDN blocks, rec 786432 + conv 30720 fp32 each, slot 7 -> live",
+            "us_per_call": round(ms * 1000, 2), "bytes_per_call": int(nbytes), "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "launches_per_call": 1}
+
+
 def run_ours(args):
     import torch
 
@@ -436,6 +509,9 @@ def run_ours(args):
         extras["moe_verify"] = measure_moe(args, torch, peak)
     if rank == 0 and ws == 1 and not args.no_prefill and shape.ffn == 17408 and shape.dim == 5120:
         extras["prefill_ffn"] = measure_prefill(args, torch, {k: step.w[k] for k in ("gate", "up", "down")})
+    if rank == 0 and ws == 1 and not args.no_extras:
+        extras["attn_qkv"] = measure_attn_qkv(args, torch, peak)
+        extras["acceptsel11k"] = measure_acceptsel(args, torch, peak)
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
@@ -478,6 +554,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-port baseline")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE layer (config 4) measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill contraction (config 5) measurement")
+    ap.add_argument("--no-extras", action="store_true", help="skip the aq3k8v11 / acceptsel11k measurements")
     # smaller shapes for profiler captures only; the benchmark line uses the defaults
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -88,27 +89,33 @@ struct SelPtrs {
 
 template <typename V>
 __global__ void acceptsel_kernel(float* __restrict__ rec4, float* __restrict__ conv4,
-                                 const int32_t* __restrict__ m_slot, const SelPtrs src, int n_blocks,
-                                 int64_t rec_v, int64_t conv_v) {
+                                 const int32_t* __restrict__ m_slot, const SelPtrs src, int64_t rec_v,
+                                 int64_t conv_v) {
+  // blockIdx.y = GDN block b; blockIdx.x strides over that block's rec + conv vectors
   const int m = m_slot[0];
   if (m < 0 || m > 10) return;
+  const int64_t b = blockIdx.y;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   // rec: slot m -> slot 4 (m == 4 is the live slot itself: nothing to copy)
   if (m != 4) {
-    for (int64_t i = t0; i < n_blocks * rec_v; i += stride) {
-      const int64_t b = i / rec_v, e = i - b * rec_v;
-      const V* s = m < 5 ? reinterpret_cast<const V*>(rec4) + (b * 5 + m) * rec_v
-                         : reinterpret_cast<const V*>(src.rec_x[m - 5]) + b * rec_v;
-      reinterpret_cast<V*>(rec4)[(b * 5 + 4) * rec_v + e] = s[e];
+    const V* s = m < 5 ? reinterpret_cast<const V*>(rec4) + (b * 5 + m) * rec_v
+                       : reinterpret_cast<const V*>(src.rec_x[m - 5]) + b * rec_v;
+    V* d = reinterpret_cast<V*>(rec4) + (b * 5 + 4) * rec_v;
+    int64_t i = t0;
+    for (; i + 3 * stride < rec_v; i += 4 * stride) {  // four loads in flight per thread
+      const V v0 = s[i], v1 = s[i + stride], v2 = s[i + 2 * stride], v3 = s[i + 3 * stride];
+      d[i] = v0;
+      d[i + stride] = v1;
+      d[i + 2 * stride] = v2;
+      d[i + 3 * stride] = v3;
     }
+    for (; i < rec_v; i += stride) d[i] = s[i];
   }
-  for (int64_t i = t0; i < n_blocks * conv_v; i += stride) {
-    const int64_t b = i / conv_v, e = i - b * conv_v;
-    const V* s = m < 4 ? reinterpret_cast<const V*>(conv4) + (b * 5 + m) * conv_v
-                       : reinterpret_cast<const V*>(src.conv_x[m - 4]) + b * conv_v;
-    reinterpret_cast<V*>(conv4)[(b * 5 + 4) * conv_v + e] = s[e];
-  }
+  const V* s = m < 4 ? reinterpret_cast<const V*>(conv4) + (b * 5 + m) * conv_v
+                     : reinterpret_cast<const V*>(src.conv_x[m - 4]) + b * conv_v;
+  V* d = reinterpret_cast<V*>(conv4) + (b * 5 + 4) * conv_v;
+  for (int64_t i = t0; i < conv_v; i += stride) d[i] = s[i];
 }
 
 // argmax key of one row of materialised logits, reduced over the CTA (valid in
@@ -423,16 +430,18 @@ int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const flo
     src.rec_x[i] = rec_x[i];
     vec = vec && (reinterpret_cast<uintptr_t>(rec_x[i]) & 15) == 0;
   }
+  if (n_blocks > 65535) return TLX_ERR_SHAPE;
+  // ~ 8 CTAs per SM in total, spread over the blocks
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const dim3 grid(static_cast<unsigned>(sms > 0 ? sms * 8 : 1184)), block(256);
+  const int per_block = std::max(1, (sms > 0 ? sms : 148) * 8 / n_blocks);
+  const dim3 grid(static_cast<unsigned>(per_block), static_cast<unsigned>(n_blocks)), block(256);
   if (vec)
-    acceptsel_kernel<float4><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, n_blocks, rec_elems / 4,
+    acceptsel_kernel<float4><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, rec_elems / 4,
                                                                      conv_elems / 4);
   else
-    acceptsel_kernel<float><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, n_blocks, rec_elems,
-                                                                    conv_elems);
+    acceptsel_kernel<float><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, rec_elems, conv_elems);
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
