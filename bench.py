@@ -364,6 +364,74 @@ def measure_attn_qkv(args, torch, peak):
             "err_word": proj.error()}
 
 
+def _graph_of(fn, torch):
+    """Capture fn (after one eager call on a side stream) as a CUDA graph."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
+
+
+def measure_gdn_qkv(args, torch, peak):
+    """q5g8v11 at the reference shape (qkv 10240 rows Q5_K, gate 6144 rows IQ3_XXS,
+    k 5120, 11 fp16 rows): staging + two GEMVs, cold L2; bytes = weights + x + outputs."""
+    from thunderllamax_b200 import ops, synth
+    from thunderllamax_b200.verify import synth_tiled
+
+    m, k, nqkv, ngate = 11, 5120, 10240, 6144
+    wqkv, wg = synth_tiled("q5_k", nqkv, k, 41), synth_tiled("iq3_xxs", ngate, k, 42)
+    rng = np.random.default_rng(43)
+    x = torch.from_numpy(synth.bf16_bits_to_f32(synth.bf16_normal(rng, (m, k))).astype(np.float16)).cuda()
+    proj = ops.GdnProjections(m, k, nqkv, ngate, torch.float16)
+    outs = [torch.empty((m, n), dtype=torch.float16, device="cuda") for n in (nqkv, ngate)]
+    for _ in range(3):
+        proj(wqkv, wg, x, *outs)
+    graph = _graph_of(lambda: proj(wqkv, wg, x, *outs), torch)
+    ms = _timed_cold(graph.replay, 20, torch)
+    wbytes = nqkv * synth.row_bytes("q5_k", k) + ngate * synth.row_bytes("iq3_xxs", k)
+    nbytes = wbytes + m * k * 2 + m * (nqkv + ngate) * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "q5g8v11: qkv 10240 rows Q5_K + gate 6144 rows IQ3_XXS, k 5120, 11 fp16 rows",
+            "us_per_call": round(ms * 1000, 2), "bytes_per_call": int(nbytes), "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "launches_per_call": 4, "graph": "CUDA graph replay",
+            "l2": "flushed before each call", "err_word": proj.error()}
+
+
+def measure_o_proj(args, torch, peak):
+    """op38nw32_11 (IQ3_XXS) and k3aonw32_11 (Q8_0): attn_out [11][5120] = W z with
+    z [11][6144] fp16, fp16 out, one GEMV each (its staging included), cold L2."""
+    from thunderllamax_b200 import ops, synth
+    from thunderllamax_b200.verify import synth_tiled
+
+    m, n, k = 11, 5120, 6144
+    rng = np.random.default_rng(44)
+    z = torch.from_numpy(synth.bf16_bits_to_f32(synth.bf16_normal(rng, (m, k))).astype(np.float16)).cuda()
+    out = {}
+    for qt, seed in (("iq3_xxs", 45), ("q8_0", 46)):
+        w = synth_tiled(qt, n, k, seed)
+        ws = ops.Workspace.for_shape(ops.MODE_STORE, qt, n, k, m, torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device="cuda")
+        fn = lambda: ops.gemv(qt, w, z, n, ws, y=y)  # noqa: E731
+        for _ in range(3):
+            fn()
+        graph = _graph_of(fn, torch)
+        ms = _timed_cold(graph.replay, 20, torch)
+        nbytes = n * synth.row_bytes(qt, k) + m * k * 2 + m * n * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out["op38nw32_11" if qt == "iq3_xxs" else "k3aonw32_11"] = {
+            "qtype": qt, "us_per_call": round(ms * 1000, 2), "bytes_per_call": int(nbytes), "gbs": round(gbs, 1),
+            "frac_of_peak": round(gbs / peak, 4), "err_word": ws.error()}
+        del graph
+    out["workload"] = "GDN o-projection 5120 x 6144, 11 fp16 rows, CUDA graph replay, L2 flushed before each call"
+    return out
+
+
 def measure_acceptsel(args, torch, peak):
     """acceptsel11k at the reference size (48 GDN blocks x (786432 + 30720) fp32, m = 7):
     bytes = the slot read + the live slot written."""
@@ -512,6 +580,8 @@ def run_ours(args):
     if rank == 0 and ws == 1 and not args.no_extras:
         extras["attn_qkv"] = measure_attn_qkv(args, torch, peak)
         extras["acceptsel11k"] = measure_acceptsel(args, torch, peak)
+        extras["gdn_qkv"] = measure_gdn_qkv(args, torch, peak)
+        extras["o_proj"] = measure_o_proj(args, torch, peak)
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,

@@ -24,7 +24,10 @@ extern "C" {
 #endif
 
 /* ggml type ids (GGUF tensor types) */
+#define TLX_Q8_0 8    /* STORE GEMV only (the GDN o-projection rows); one "block"
+                        of the layout = 8 GGUF blocks (272 B per 256 weights) */
 #define TLX_Q4_K 12   /* STORE GEMV only (the attention v rows) */
+#define TLX_Q5_K 13   /* STORE GEMV only (the GDN qkv rows) */
 #define TLX_Q6_K 14
 #define TLX_IQ3_XXS 18
 #define TLX_IQ4_XS 23
@@ -36,9 +39,10 @@ extern "C" {
  * or tlx_ffn_gate_up with gact_dtype = TLX_DT_IMAGE): x points at the image, ldx
  * is ignored, one column per token */
 #define TLX_DT_IMAGE 100
-/* (Q4_K GEMVs also read the per-sub-block sums of x that tlx_stage_activations
- * writes into the image; an image written by tlx_ffn_gate_up carries none, so give
- * a Q4_K GEMV raw activations or a tlx_stage_activations image.) */
+/* (Q4_K / Q5_K GEMVs also read the per-sub-block sums of x that
+ * tlx_stage_activations writes into the image; an image written by tlx_ffn_gate_up
+ * carries none, so give a Q4_K / Q5_K GEMV raw activations or a
+ * tlx_stage_activations image.) */
 /* gemv modes for tlx_gemv_workspace_bytes */
 #define TLX_MODE_STORE 0
 #define TLX_MODE_GATE_UP 1
@@ -66,7 +70,8 @@ int tlx_version(void);
 void tlx_set_max_ctas(int n);
 
 /* ---- weight layout ------------------------------------------------------------
- * GGUF rows (ggml block_iq3_xxs 98 B / block_q6_K 210 B per 256 weights) ->
+ * GGUF rows (ggml block_iq3_xxs 98 B / block_q6_K 210 B / block_q4_K 144 B /
+ * block_q5_K 176 B per 256 weights, block_q8_0 34 B per 32) ->
  * B200 tile layout (16-row tiles, one 16*block_bytes chunk per tile and block,
  * same byte count as GGUF plus zero rows up to a multiple of 16).  Replaces the
  * offline repackers engine/pack_w1c.py:18-45 (IQ3 row regions, Q6_K 212-B pad)
@@ -112,7 +117,10 @@ int tlx_stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_
  * |x| in [2^-24 * 2^7, 65504]); fp32 activations are split exactly into three
  * fp16 parts.
  * Replaces down8nw32_11(wd, gridf, gact, hh, y) engine/down8nw32_11.cu:88-126
- * (residual = hh) and head8v11(w, xh, logits) engine/head8v11.cu:88-121. */
+ * (residual = hh), head8v11(w, xh, logits) engine/head8v11.cu:88-121 and the GDN
+ * o-projections op38nw32_11(wo, gridf, z, attn_out) engine/op38nw32_11.cu:88-120
+ * (IQ3_XXS) / k3aonw32_11(wq8, z, attn_out) engine/k3aonw32_11.cu:88-116 (Q8_0;
+ * weights rounded to fp16(d q) as the reference does), fp16 z and output. */
 int tlx_gemv(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
              int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y, int y_dtype, int64_t ldy,
              void* ws, size_t ws_bytes, void* stream);
@@ -209,6 +217,20 @@ int tlx_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t*
 /* the workspace's error bits (OR over the three GEMVs; synchronous read) */
 int tlx_aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype,
                        uint32_t* err_out);
+
+/* q5g8v11: the GDN block's input projections of the probe trunk over m rows
+ * (engine/q5g8v11.cu:68-150): qkv = Wqkv x (Q5_K, nqkv rows) and gate = Wg x
+ * (IQ3_XXS, ngate rows) for x [m][k] fp16 or bf16 (ld ldx); outputs fp16 [m][nqkv]
+ * and [m][ngate].  Weights tiled (tlx_pack_tiles, qtypes TLX_Q5_K / TLX_IQ3_XXS).
+ * x is staged once for both GEMVs.  Workspace: tlx_q5g8v11_workspace_bytes, zeroed
+ * once (tlx_workspace_init) and reused.  The reference shapes are nqkv = 10240,
+ * ngate = 6144, k = 5120, m = 11. */
+size_t tlx_q5g8v11_workspace_bytes(int m, int64_t k, int64_t nqkv, int64_t ngate, int x_dtype);
+int tlx_q5g8v11(const void* wqkv, const void* wgate, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
+                int m, int64_t k, int64_t nqkv, int64_t ngate, void* qkv_out, void* gate_out, void* ws,
+                size_t ws_bytes, void* stream);
+/* the workspace's error bits (OR over the two GEMVs; synchronous read) */
+int tlx_q5g8v11_error(const void* ws, int m, int64_t k, int64_t nqkv, int64_t ngate, int x_dtype, uint32_t* err_out);
 
 /* acceptsel11k: commit the accepted GDN state (engine/acceptsel11k.cu:8-40).
  * rec4 is [n_blocks][5][rec_elems] fp32 and conv4 [n_blocks][5][conv_elems] fp32,

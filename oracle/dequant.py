@@ -1,6 +1,6 @@
 """ggml block dequantisation, restated in numpy (oracle; test infrastructure).
 
-All three formats dequantise EXACTLY in fp32: every weight is a product of an
+All six formats dequantise EXACTLY in fp32: every weight is a product of an
 fp16 scale with small integers whose significands fit in 24 bits, so the fp32
 values below equal the real-number values.  The reference's dense GEMVs round
 each weight to fp16 before use (engine/ffn8v11.cu:115-117 ``__float2half``);
@@ -129,7 +129,46 @@ def dequant_q4k(raw: np.ndarray, k: int) -> np.ndarray:
     return w.reshape(n, k).astype(np.float32)
 
 
-_DQ = {"iq3_xxs": dequant_iq3xxs, "q6_k": dequant_q6k, "iq4_xs": dequant_iq4xs, "q4_k": dequant_q4k}
+def dequant_q5k(raw: np.ndarray, k: int) -> np.ndarray:
+    """Q5_K rows (d f16 | dmin f16 | scales[12] | qh[32] | qs[128]) -> f32 [n, k].
+
+    Sub-block s (32 weights, element e): q = nibble + 16 * bit s of qh[e], the nibble
+    being the low one of qs[32j + e] for s = 2j and the high one for s = 2j+1;
+    w = (d * sc_s) * q - dmin * mn_s.  Follows the qkv branch of
+    engine/q5g8v11.cu:76-93 and the reference's numpy restatement
+    engine/chain_sim.py:111-150 (dequant_q5k_rows), in its fp32 evaluation order."""
+    n = raw.shape[0]
+    nb = k // QK
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 176)
+    d = _f16(blk[..., 0:2])
+    dmin = _f16(blk[..., 2:4])
+    sc, mn = _scale_min_k4(blk[..., 4:16])                        # [n, nb, 8]
+    qh = blk[..., 16:48]                                          # [n, nb, 32]
+    qs = blk[..., 48:176].reshape(n, nb, 4, 32)
+    nib = np.stack([qs & 0xF, qs >> 4], axis=3).reshape(n, nb, 8, 32).astype(np.int32)
+    hbit = (qh[:, :, None, :] >> np.arange(8, dtype=np.uint8)[None, None, :, None]) & 1   # [n, nb, 8, 32]
+    q = (nib + 16 * hbit.astype(np.int32)).astype(np.float32)
+    d1 = d[..., None] * sc.astype(np.float32)
+    m1 = dmin[..., None] * mn.astype(np.float32)
+    w = d1[..., None] * q - m1[..., None]
+    return w.reshape(n, k).astype(np.float32)
+
+
+def dequant_q8_0(raw: np.ndarray, k: int) -> np.ndarray:
+    """Q8_0 rows (blocks of 32: d f16 | qs[32] int8) -> f32 [n, k]: w = d * q (exact
+    in fp32).  Follows engine/mm/MM_P2_ports.py:48-54 (dq_q8_0).  The reference's
+    GPU o-projection then rounds each weight to fp16 (engine/k3aonw32_11.cu:100-101);
+    that rounding belongs to the kernel's numerics, not to the format."""
+    n = raw.shape[0]
+    nb = k // 32
+    blk = np.ascontiguousarray(raw).reshape(n, nb, 34)
+    d = _f16(blk[..., 0:2])
+    q = blk[..., 2:34].view(np.int8).astype(np.float32)
+    return (d[..., None] * q).reshape(n, k).astype(np.float32)
+
+
+_DQ = {"iq3_xxs": dequant_iq3xxs, "q6_k": dequant_q6k, "iq4_xs": dequant_iq4xs, "q4_k": dequant_q4k,
+       "q5_k": dequant_q5k, "q8_0": dequant_q8_0}
 
 
 def dequant(qtype: str, raw: np.ndarray, k: int, chunk_rows: int = 8192) -> np.ndarray:

@@ -8,7 +8,8 @@ Run in a container where the reference tree is mounted (default
 It imports the reference's OWN numpy ports -- engine/mm/MM_P2_ports.py
 (dq_q6_k, gxup4_ref, gxdn4_ref, gxdn6_ref, rt_prod_ref, cmb_ref),
 engine/mm/MM_P0_d2_repack.py (dq_iq4_xs), engine/pack_w4.py
-(dequant_iq3xxs) and engine/mm/mm_mtp_anchor.py (dq_q4_k_np) -- with the ggml tables they would take from tinygrad injected
+(dequant_iq3xxs), engine/mm/mm_mtp_anchor.py (dq_q4_k_np) and
+engine/chain_sim.py (dequant_q5k_rows) -- with the ggml tables they would take from tinygrad injected
 from gguf-py, runs them on seeded synthetic blocks, and writes the inputs and
 outputs to tests/golden/golden_v1.npz.  Nothing at test time reads the
 reference tree; the tests only read the .npz.
@@ -59,6 +60,20 @@ def reference_q4k_port(P0):
     ns = {"np": np, "_f16": P0._f16}
     exec(compile(ast.Module(body=defs, type_ignores=[]), path, "exec"), ns)
     return ns["dq_q4_k_np"]
+
+
+def reference_q5k_port():
+    """dequant_q5k_rows from engine/chain_sim.py (the reference's numpy restatement of
+    its Q5_K row dequant), compiled alone as written: the module's own imports need
+    the reference's model tree.  It reads whole 5120-weight rows (20 blocks)."""
+    import ast
+
+    path = os.path.join(REF, "engine", "chain_sim.py")
+    tree = ast.parse(open(path).read(), path)
+    defs = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "dequant_q5k_rows"]
+    ns = {"np": np, "DIM": 5120, "F32": np.float32, "F16": np.float16}
+    exec(compile(ast.Module(body=defs, type_ignores=[]), path, "exec"), ns)
+    return ns["dequant_q5k_rows"]
 
 
 def region_repack_iq3(raw: np.ndarray, k: int) -> np.ndarray:
@@ -128,6 +143,19 @@ def main():
     g["q4k_raw"] = q4
     g["q4k_ref"] = reference_q4k_port(P0)(q4, 512)
     g["q4k_gguf_f32"] = quants.dequantize(q4, quants.GGMLQuantizationType.Q4_K).reshape(8, 512)
+
+    # Q5_K (the GDN qkv rows of q5g8v11): the reference's dequant_q5k_rows
+    # (engine/chain_sim.py:111-150) on whole 5120-weight rows, and gguf-py;
+    # Q8_0 (the o-projection rows of k3aonw32_11): dq_q8_0 (engine/mm/MM_P2_ports.py:48-54)
+    rng5 = np.random.default_rng(20261203)
+    q5 = synth.q5k_blocks(rng5, 3, 5120)
+    g["q5k_raw"] = q5
+    g["q5k_ref"] = reference_q5k_port()(q5, np.arange(3))
+    g["q5k_gguf_f32"] = quants.dequantize(q5, quants.GGMLQuantizationType.Q5_K).reshape(3, 5120)
+    q8 = synth.q8_0_blocks(rng5, 8, 512)
+    g["q8_0_raw"] = q8
+    g["q8_0_ref"] = P2.dq_q8_0(q8, 512)
+    g["q8_0_gguf_f32"] = quants.dequantize(q8, quants.GGMLQuantizationType.Q8_0).reshape(8, 512)
 
     out = os.path.join(HERE, "golden_v1.npz")
     np.savez_compressed(out, **g)

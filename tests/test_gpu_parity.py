@@ -47,10 +47,23 @@ def check_rows(got, ref, tight=TIGHT):
         assert err <= tight * nrm, (t, err, nrm)
 
 
-GEN = {"q6_k": synth.q6k_blocks, "iq3_xxs": synth.iq3xxs_blocks, "q4_k": synth.q4k_blocks}
+GEN = {"q6_k": synth.q6k_blocks, "iq3_xxs": synth.iq3xxs_blocks, "q4_k": synth.q4k_blocks,
+       "q5_k": synth.q5k_blocks, "q8_0": synth.q8_0_blocks}
 
 
-@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k"])
+def check_vs_oracle(qtype, got, raw, k, x64, tight=TIGHT):
+    """Every format decodes exactly except Q8_0, whose weights the kernel rounds to
+    fp16(d q) as the reference's o-projection does (engine/k3aonw32_11.cu:100-101):
+    Q8_0 is held to the contract against the exact weights and to the tight bound
+    against the fp16-rounded ones."""
+    W = oracle.dequant(qtype, raw, k)
+    if qtype == "q8_0":
+        check_rows(got, oracle.matvec_f64(W, x64), tight=CONTRACT)
+        W = W.astype(np.float16).astype(np.float32)
+    check_rows(got, oracle.matvec_f64(W, x64), tight=tight)
+
+
+@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k", "q5_k", "q8_0"])
 @pytest.mark.parametrize("n,k,m,dtype", [
     (16, 256, 1, torch.bfloat16),
     (100, 512, 3, torch.bfloat16),
@@ -63,16 +76,15 @@ def test_gemv_vs_oracle(qtype, n, k, m, dtype):
     rng = np.random.default_rng(n * 7 + k + m)
     raw = GEN[qtype](rng, n, k)
     x, x64 = x_tensor(rng, m, k, dtype)
-    ref = oracle.matvec_f64(oracle.dequant(qtype, raw, k), x64)
     w = ops.pack_tiles(qtype, raw, k)
     ws = ops.Workspace.for_shape(ops.MODE_STORE, qtype, n, k, m, dtype)
     y = ops.gemv(qtype, w, x, n, ws)
     torch.cuda.synchronize()
     assert ws.error() == 0
-    check_rows(y.cpu().numpy(), ref)
+    check_vs_oracle(qtype, y.cpu().numpy(), raw, k, x64)
 
 
-@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k"])
+@pytest.mark.parametrize("qtype", ["q6_k", "iq3_xxs", "q4_k", "q5_k", "q8_0"])
 def test_gemv_split_tiles_and_segments(qtype):
     # few CTAs + long k: tiles split across warps and k-segments, reduced by the
     # last arriving piece in fixed order; residual epilogue; results repeatable
@@ -81,7 +93,10 @@ def test_gemv_split_tiles_and_segments(qtype):
     raw = GEN[qtype](rng, n, k)
     x, x64 = x_tensor(rng, m, k, torch.bfloat16)
     res = rng.standard_normal((m, n), dtype=np.float32)
-    ref = oracle.matvec_f64(oracle.dequant(qtype, raw, k), x64) + res
+    W = oracle.dequant(qtype, raw, k)
+    if qtype == "q8_0":
+        W = W.astype(np.float16).astype(np.float32)    # the kernel's fp16(d q) weights
+    ref = oracle.matvec_f64(W, x64) + res
     w = ops.pack_tiles(qtype, raw, k)
     for ctas in (5, 12, 0):
         ops.set_max_ctas(ctas)
@@ -301,6 +316,58 @@ def test_q4k_gemv_reads_a_staged_image():
     y = ops.gemv("q4_k", w, img, n, ops.Workspace.for_shape(ops.MODE_STORE, "q4_k", n, k, m, "image"))
     torch.cuda.synchronize()
     check_rows(y.cpu().numpy(), oracle.matvec_f64(oracle.dequant("q4_k", raw, k), x64))
+
+
+@pytest.mark.parametrize("nqkv,ngate,k,dtype", [(320, 192, 512, torch.float16), (10240, 6144, 5120, torch.float16),
+                                                (10240, 6144, 5120, torch.bfloat16)])
+def test_q5g8v11_vs_oracle(nqkv, ngate, k, dtype):
+    # the GDN qkv (Q5_K) and gate (IQ3_XXS) projections over 11 rows, fp16 outputs
+    rng = np.random.default_rng(nqkv + ngate)
+    m = 11
+    rqkv, rg = synth.q5k_blocks(rng, nqkv, k), synth.iq3xxs_blocks(rng, ngate, k)
+    x, x64 = x_tensor(rng, m, k, dtype)
+    wqkv, wg = ops.pack_tiles("q5_k", rqkv, k), ops.pack_tiles("iq3_xxs", rg, k)
+    proj = ops.GdnProjections(m, k, nqkv, ngate, dtype)
+    qkv, gate = proj(wqkv, wg, x)
+    qkv2, gate2 = proj(wqkv, wg, x)
+    torch.cuda.synchronize()
+    assert proj.error() == 0
+    for got, raw, qt in ((qkv, rqkv, "q5_k"), (gate, rg, "iq3_xxs")):
+        ref = oracle.matvec_f64(oracle.dequant(qt, raw, k), x64)
+        check_rows(got.float().cpu().numpy(), ref, tight=1e-3)   # fp16 outputs: one fp16 rounding
+    assert torch.equal(qkv, qkv2) and torch.equal(gate, gate2)
+
+
+@pytest.mark.parametrize("qtype", ["iq3_xxs", "q8_0"])
+def test_gdn_o_projection_reference_shape(qtype):
+    # op38nw32_11 (IQ3_XXS) / k3aonw32_11 (Q8_0): attn_out [11][5120] = W z, z [11][6144]
+    # fp16, through the reference-named programs
+    from thunderllamax_b200 import engine0
+    rng = np.random.default_rng(61 if qtype == "q8_0" else 62)
+    m, n, k = 11, 5120, 6144
+    raw = GEN[qtype](rng, n, k)
+    z, z64 = x_tensor(rng, m, k, torch.float16)
+    w = ops.pack_tiles(qtype, raw, k)
+    progs = engine0.load_progs(rows=m, vocab=4096)
+    out = torch.empty((m, n), dtype=torch.float16, device="cuda")
+    if qtype == "q8_0":
+        progs["k3aonw32_11"](w, z.reshape(-1), out.reshape(-1))
+    else:
+        progs["op38nw32_11"](w, None, z.reshape(-1), out.reshape(-1))
+    torch.cuda.synchronize()
+    check_vs_oracle(qtype, out.float().cpu().numpy(), raw, k, z64, tight=1e-3)
+
+
+def test_q5k_gemv_reads_a_staged_image():
+    rng = np.random.default_rng(32)
+    n, k, m = 300, 1024, 11
+    raw = synth.q5k_blocks(rng, n, k)
+    x, x64 = x_tensor(rng, m, k, torch.bfloat16)
+    w = ops.pack_tiles("q5_k", raw, k)
+    img = ops.stage(x)
+    y = ops.gemv("q5_k", w, img, n, ops.Workspace.for_shape(ops.MODE_STORE, "q5_k", n, k, m, "image"))
+    torch.cuda.synchronize()
+    check_rows(y.cpu().numpy(), oracle.matvec_f64(oracle.dequant("q5_k", raw, k), x64))
 
 
 def _sel_buffers(B, R, C, seed):

@@ -40,7 +40,8 @@ def test_error_strings_and_host_argument_checks():
 
 
 @pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98),
-                                          ("iq4_xs", synth.iq4xs_blocks, 136), ("q4_k", synth.q4k_blocks, 144)])
+                                          ("iq4_xs", synth.iq4xs_blocks, 136), ("q4_k", synth.q4k_blocks, 144),
+                                          ("q5_k", synth.q5k_blocks, 176), ("q8_0", synth.q8_0_blocks, 272)])
 def test_pack_unpack_round_trip(qtype, gen, bb):
     rng = np.random.default_rng(1)
     for n in (1, 16, 37):
@@ -159,6 +160,86 @@ def emulate_q4k(tiled, n_rows, k):
                             kk = b * 256 + 64 * q + 4 * m + i
                             W[t * 16 + row, kk] = d * a - dmin * np.float32(int(mn[0, s_]))
     return W[:n_rows]
+
+
+def emulate_q5k(tiled, n_rows, k):
+    """Q5_K as the device decodes it (formats.cuh q4_load<true> / q4_mma<true>): the
+    Q4_K nibble path plus the fifth bit, taken from the regrouped byte of word i with
+    the multiply-and-shift spread q4_mma applies (bits 4 / 20 for the low nibbles,
+    8 / 24 for the high ones), then d * (sc q) - dmin * mn."""
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    ch = tiled.reshape(T, nb, 2816)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                for rr in range(2):
+                    row = g + 8 * rr
+                    hdr = c[2560 + 16 * row:2576 + 16 * row]
+                    d = np.float32(hdr[0:2].view(np.float16)[0])
+                    dmin = np.float32(hdr[2:4].view(np.float16)[0])
+                    sc, mn = _scale_min_k4(hdr[4:16][None])
+                    qs = np.concatenate([c[((2 * rr + hf) * 32 + lane) * 16:][:16] for hf in range(2)])
+                    hb = c[2048 + lane * 16 + rr * 8:][:8]
+                    for m in range(16):
+                        s_ = 2 * q + (m >> 3)
+                        x = (int(hb[m & 7]) * 0x00100001) & 0xFFFFFFFF
+                        if m < 8:
+                            hw = [x & 0x00100010, (x >> 1) & 0x00100010]
+                        else:
+                            hw = [(x << 2) & 0x01000100, (x << 1) & 0x01000100]
+                        for i in range(4):
+                            byte = int(qs[4 * (m & 7) + i])
+                            half = (hw[i >> 1] >> (16 * (i & 1))) & 0xFFFF
+                            if m < 8:
+                                v = (byte & 0xF) | (half & 0x10)          # v + 16 h
+                            else:
+                                v = ((byte >> 4) << 4 | (half & 0x100)) >> 4
+                            a = np.float32(int(sc[0, s_]) * v)
+                            kk = b * 256 + 64 * q + 4 * m + i
+                            W[t * 16 + row, kk] = d * a - dmin * np.float32(int(mn[0, s_]))
+    return W[:n_rows]
+
+
+def emulate_q8(tiled, n_rows, k):
+    """Q8_0 as the device decodes it (formats.cuh q8_load / q8_mma): fp16(d * q)."""
+    nb = k // 256
+    T = (n_rows + 15) // 16
+    W = np.zeros((T * 16, k), np.float32)
+    ch = tiled.reshape(T, nb, 4352)
+    for t in range(T):
+        for b in range(nb):
+            c = ch[t, b]
+            for lane in range(32):
+                g, q = lane >> 2, lane & 3
+                dd = c[4096 + 8 * lane:4104 + 8 * lane].view(np.float16)
+                for rr in range(2):
+                    row = g + 8 * rr
+                    qs = np.concatenate([c[((4 * rr + j) * 32 + lane) * 16:][:16] for j in range(4)]).view(np.int8)
+                    for m in range(16):
+                        d = dd[2 * rr + (m >> 3)]
+                        for i in range(4):
+                            kk = b * 256 + 64 * q + 4 * m + i
+                            W[t * 16 + row, kk] = np.float32(np.float16(np.float32(qs[4 * m + i]) * np.float32(d)))
+    return W[:n_rows]
+
+
+def test_q5k_tile_decode_matches_oracle_exactly():
+    rng = np.random.default_rng(11)
+    raw = synth.q5k_blocks(rng, 19, 512)
+    got = emulate_q5k(ops.pack_tiles_host("q5_k", raw, 512), 19, 512)
+    assert np.array_equal(got.view(np.uint32), oracle.dequant_q5k(raw, 512).view(np.uint32))
+
+
+def test_q8_tile_decode_is_the_fp16_rounded_oracle():
+    rng = np.random.default_rng(12)
+    raw = synth.q8_0_blocks(rng, 21, 512)
+    got = emulate_q8(ops.pack_tiles_host("q8_0", raw, 512), 21, 512)
+    ref = oracle.dequant_q8_0(raw, 512).astype(np.float16).astype(np.float32)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
 def test_q4k_tile_decode_matches_oracle_exactly():

@@ -100,6 +100,20 @@ def test_argmax_tie_and_nan_rules():
     assert list(idx) == [1, 0, 0]
 
 
+def test_q5k_dequant_bit_exact(golden):
+    # the reference's numpy restatement (engine/chain_sim.py dequant_q5k_rows) and gguf-py
+    got = oracle.dequant_q5k(golden["q5k_raw"], 5120)
+    assert np.array_equal(got.view(np.uint32), golden["q5k_ref"].astype(np.float32).view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), golden["q5k_gguf_f32"].astype(np.float32).view(np.uint32))
+
+
+def test_q8_0_dequant_bit_exact(golden):
+    # the reference's numpy port (engine/mm/MM_P2_ports.py dq_q8_0) and gguf-py
+    got = oracle.dequant_q8_0(golden["q8_0_raw"], 512)
+    assert np.array_equal(got.view(np.uint32), golden["q8_0_ref"].astype(np.float32).view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), golden["q8_0_gguf_f32"].astype(np.float32).view(np.uint32))
+
+
 def test_q4k_dequant_bit_exact(golden):
     # the reference's numpy port (engine/mm/mm_mtp_anchor.py dq_q4_k_np) and gguf-py
     got = oracle.dequant_q4k(golden["q4k_raw"], 512)

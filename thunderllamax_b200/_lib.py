@@ -12,10 +12,11 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("TLX_LIB", os.path.join(_HERE, "libtlx_b200.so"))
 
-TLX_Q4_K, TLX_Q6_K, TLX_IQ3_XXS, TLX_IQ4_XS = 12, 14, 18, 23
+TLX_Q8_0, TLX_Q4_K, TLX_Q5_K, TLX_Q6_K, TLX_IQ3_XXS, TLX_IQ4_XS = 8, 12, 13, 14, 18, 23
 TLX_DT_F32, TLX_DT_F16, TLX_DT_BF16, TLX_DT_IMAGE = 0, 1, 30, 100
 MODE_STORE, MODE_GATE_UP, MODE_ARGMAX = 0, 1, 2
-QTYPES = {"q6_k": TLX_Q6_K, "iq3_xxs": TLX_IQ3_XXS, "iq4_xs": TLX_IQ4_XS, "q4_k": TLX_Q4_K}
+QTYPES = {"q6_k": TLX_Q6_K, "iq3_xxs": TLX_IQ3_XXS, "iq4_xs": TLX_IQ4_XS, "q4_k": TLX_Q4_K, "q5_k": TLX_Q5_K,
+          "q8_0": TLX_Q8_0}
 
 
 class TLXError(RuntimeError):
@@ -53,6 +54,10 @@ _SIGS = {
     "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
     "tlx_h_argmax": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "tlx_acceptsel11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "tlx_q5g8v11_workspace_bytes": (c_size, [c_int, c_i64, c_i64, c_i64, c_int]),
+    "tlx_q5g8v11_error": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_vp]),
+    "tlx_q5g8v11": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                            c_size, c_vp]),
     "tlx_aq3k8v11_workspace_bytes": (c_size, [c_int, c_i64, c_i64, c_i64, c_i64, c_int]),
     "tlx_aq3k8v11_error": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_int, c_vp]),
     "tlx_aq3k8v11": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_i64,

@@ -19,7 +19,9 @@ int g_max_ctas = 0;  // 0 = one CTA per SM
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-bool valid_qtype(int qt) { return qt == QT_Q6_K || qt == QT_IQ3_XXS || qt == QT_Q4_K; }
+bool valid_qtype(int qt) {
+  return qt == QT_Q6_K || qt == QT_IQ3_XXS || qt == QT_Q4_K || qt == QT_Q5_K || qt == QT_Q8_0;
+}
 // formats the tile packers know (IQ4_XS is read by the MoE kernels only)
 bool valid_pack_qtype(int qt) { return valid_qtype(qt) || qt == QT_IQ4_XS; }
 
@@ -297,7 +299,32 @@ int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, vo
     for (int b = 0; b < nb; ++b) {
       const uint8_t* c = s + (t * nb + b) * static_cast<int64_t>(ch);
       uint8_t* blk = d + row * row_bytes + static_cast<int64_t>(b) * bb;
-      if (qtype == QT_Q4_K) {
+      if (qtype == QT_Q5_K) {
+        for (int i = 0; i < 16; ++i) blk[i] = c[2560 + r * 16 + i];
+        std::memset(blk + 16, 0, 32);
+        for (int q = 0; q < 4; ++q) {
+          const int lane = 4 * g + q;
+          for (int hf = 0; hf < 2; ++hf)
+            for (int j = 0; j < 16; ++j) blk[48 + 32 * q + 16 * hf + j] = c[((2 * rr + hf) * 32 + lane) * 16 + j];
+          // the fifth-bit byte of word i: bit order as in pack_q5k_lane
+          static const int kLoBit[4] = {4, 0, 5, 1}, kHiBit[4] = {6, 2, 7, 3};
+          for (int i = 0; i < 8; ++i) {
+            const uint8_t hb = c[2048 + lane * 16 + rr * 8 + i];
+            for (int j = 0; j < 4; ++j) {
+              blk[16 + 4 * i + j] |= static_cast<uint8_t>(((hb >> kLoBit[j]) & 1u) << (2 * q));
+              blk[16 + 4 * i + j] |= static_cast<uint8_t>(((hb >> kHiBit[j]) & 1u) << (2 * q + 1));
+            }
+          }
+        }
+      } else if (qtype == QT_Q8_0) {
+        for (int q = 0; q < 4; ++q) {
+          const int lane = 4 * g + q;
+          for (int e = 0; e < 64; ++e)
+            blk[34 * (2 * q + (e >> 5)) + 2 + (e & 31)] = c[((4 * rr + (e >> 4)) * 32 + lane) * 16 + (e & 15)];
+          for (int cc = 0; cc < 2; ++cc)
+            for (int i = 0; i < 2; ++i) blk[34 * (2 * q + cc) + i] = c[4096 + lane * 8 + rr * 4 + cc * 2 + i];
+        }
+      } else if (qtype == QT_Q4_K) {
         for (int i = 0; i < 16; ++i) blk[i] = c[2048 + r * 16 + i];
         for (int q = 0; q < 4; ++q)
           for (int hf = 0; hf < 2; ++hf)
@@ -445,20 +472,58 @@ int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const flo
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
+static void aq3k8v11_set(Projection (&pr)[3], const void* wq, const void* wk, const void* wv, int64_t nq,
+                         int64_t nk, int64_t nv, void* q_out, void* k_out, void* v_out) {
+  pr[0] = {QT_IQ3_XXS, wq, nq, q_out};
+  pr[1] = {QT_IQ3_XXS, wk, nk, k_out};
+  pr[2] = {QT_Q4_K, wv, nv, v_out};
+}
+
 size_t tlx_aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype) {
-  return aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, g_max_ctas);
+  Projection pr[3];
+  aq3k8v11_set(pr, nullptr, nullptr, nullptr, nq, nk, nv, nullptr, nullptr, nullptr);
+  return projections_workspace_bytes(3, pr, m, k, x_dtype, g_max_ctas);
 }
 
 int tlx_aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype,
                        uint32_t* err_out) {
-  return aq3k8v11_error(ws, m, k, nq, nk, nv, x_dtype, g_max_ctas, err_out);
+  Projection pr[3];
+  aq3k8v11_set(pr, nullptr, nullptr, nullptr, nq, nk, nv, nullptr, nullptr, nullptr);
+  return projections_error(ws, 3, pr, m, k, x_dtype, g_max_ctas, err_out);
 }
 
 int tlx_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
                  int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
                  void* v_out, void* ws, size_t ws_bytes, void* stream) {
-  return run_aq3k8v11(wq, wk, wv, grid, x, x_dtype, ldx, m, k, nq, nk, nv, q_out, k_out, v_out, ws, ws_bytes,
-                      g_max_ctas, as_stream(stream));
+  Projection pr[3];
+  aq3k8v11_set(pr, wq, wk, wv, nq, nk, nv, q_out, k_out, v_out);
+  return run_projections(3, pr, grid, x, x_dtype, ldx, m, k, ws, ws_bytes, g_max_ctas, as_stream(stream));
+}
+
+static void q5g8v11_set(Projection (&pr)[2], const void* wqkv, const void* wgate, int64_t nqkv, int64_t ngate,
+                        void* qkv_out, void* gate_out) {
+  pr[0] = {QT_Q5_K, wqkv, nqkv, qkv_out};
+  pr[1] = {QT_IQ3_XXS, wgate, ngate, gate_out};
+}
+
+size_t tlx_q5g8v11_workspace_bytes(int m, int64_t k, int64_t nqkv, int64_t ngate, int x_dtype) {
+  Projection pr[2];
+  q5g8v11_set(pr, nullptr, nullptr, nqkv, ngate, nullptr, nullptr);
+  return projections_workspace_bytes(2, pr, m, k, x_dtype, g_max_ctas);
+}
+
+int tlx_q5g8v11_error(const void* ws, int m, int64_t k, int64_t nqkv, int64_t ngate, int x_dtype, uint32_t* err_out) {
+  Projection pr[2];
+  q5g8v11_set(pr, nullptr, nullptr, nqkv, ngate, nullptr, nullptr);
+  return projections_error(ws, 2, pr, m, k, x_dtype, g_max_ctas, err_out);
+}
+
+int tlx_q5g8v11(const void* wqkv, const void* wgate, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
+                int m, int64_t k, int64_t nqkv, int64_t ngate, void* qkv_out, void* gate_out, void* ws,
+                size_t ws_bytes, void* stream) {
+  Projection pr[2];
+  q5g8v11_set(pr, wqkv, wgate, nqkv, ngate, qkv_out, gate_out);
+  return run_projections(2, pr, grid, x, x_dtype, ldx, m, k, ws, ws_bytes, g_max_ctas, as_stream(stream));
 }
 
 int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, int32_t* pos_slot, int32_t* tok_hist,

@@ -31,7 +31,7 @@
 
 namespace tlx {
 
-enum QType : int { QT_Q4_K = 12, QT_Q6_K = 14, QT_IQ3_XXS = 18, QT_IQ4_XS = 23 };
+enum QType : int { QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q5_K = 13, QT_Q6_K = 14, QT_IQ3_XXS = 18, QT_IQ4_XS = 23 };
 
 constexpr int kTileRows = 16;
 constexpr int kQK = 256;
@@ -39,9 +39,17 @@ constexpr uint32_t kChunkQ6 = 16 * 210;     // 3360
 constexpr uint32_t kChunkIq3 = 16 * 98;     // 1568
 constexpr uint32_t kChunkIq4 = 16 * 136;    // 2176
 constexpr uint32_t kChunkQ4 = 16 * 144;     // 2304
+constexpr uint32_t kChunkQ5 = 16 * 176;     // 2816
+constexpr uint32_t kChunkQ8 = 16 * 272;     // 4352
 
+// bytes of one 256-weight group of a row in GGUF order (Q8_0: eight 34-byte blocks)
 __host__ __device__ constexpr uint32_t block_bytes(int qt) {
-  return qt == QT_Q6_K ? 210u : (qt == QT_IQ4_XS ? 136u : (qt == QT_Q4_K ? 144u : 98u));
+  return qt == QT_Q6_K     ? 210u
+         : qt == QT_IQ4_XS ? 136u
+         : qt == QT_Q4_K   ? 144u
+         : qt == QT_Q5_K   ? 176u
+         : qt == QT_Q8_0   ? 272u
+                           : 98u;
 }
 __host__ __device__ constexpr uint32_t chunk_bytes(int qt) { return 16u * block_bytes(qt); }
 
@@ -167,10 +175,64 @@ TLX_HD inline void pack_q4k_lane(const uint8_t* const rows[16], int lane, uint8_
     }
 }
 
+// Q5_K chunk (GGUF block d f16 | dmin f16 | scales[12] | qh[32] | qs[128]; the GDN
+// qkv rows).  The qs units are placed as in the Q4_K chunk (lane l = 4g + q: the 32
+// bytes qs[32q .. 32q+32) of rows g and g+8 at ((2*rr + half)*32 + l)*16).  The fifth
+// bits of the lane's weights, bit 2q (sub-block 2q, low nibbles) and bit 2q+1
+// (sub-block 2q+1, high nibbles) of qh[e] for e = 0..31, are regrouped per 4-weight
+// word i (e = 4i + j): one byte per (row, i) at 2048 + l*16 + rr*8 + i with bits
+//   0: lo(j=1)  1: lo(3)  2: hi(1)  3: hi(3)  4: lo(0)  5: lo(2)  6: hi(0)  7: hi(2),
+// the order in which q5_mma spreads them to the fp16 halves (a multiply by
+// 0x00100001 and three shifts).  Row r's 16-byte header (d, dmin, scales) follows
+// at 2560 + 16r.  Zero rows are all-zero.
+TLX_HD inline uint8_t q5_hbyte(const uint8_t* qh, int q, int i) {
+  auto lo = [&](int j) { return static_cast<uint32_t>((qh[4 * i + j] >> (2 * q)) & 1u); };
+  auto hi = [&](int j) { return static_cast<uint32_t>((qh[4 * i + j] >> (2 * q + 1)) & 1u); };
+  return static_cast<uint8_t>(lo(1) | lo(3) << 1 | hi(1) << 2 | hi(3) << 3 | lo(0) << 4 | lo(2) << 5 | hi(0) << 6 |
+                              hi(2) << 7);
+}
+
+TLX_HD inline void pack_q5k_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint8_t* blk = rows[g + 8 * rr];
+    for (int hf = 0; hf < 2; ++hf)
+      for (int j = 0; j < 16; ++j)
+        out[((2 * rr + hf) * 32 + lane) * 16 + j] = blk ? blk[48 + 32 * q + 16 * hf + j] : 0;
+    for (int i = 0; i < 8; ++i) out[2048 + lane * 16 + rr * 8 + i] = blk ? q5_hbyte(blk + 16, q, i) : 0;
+  }
+  if (q == 0)
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint8_t* blk = rows[g + 8 * rr];
+      for (int i = 0; i < 16; ++i) out[2560 + (g + 8 * rr) * 16 + i] = blk ? blk[i] : 0;
+    }
+}
+
+// Q8_0 chunk: a 256-weight group of a row is eight GGUF blocks (d f16 | qs[32] int8).
+// Lane l = 4g + q owns blocks 2q and 2q+1 (k in [64q, 64q+64)) of rows g and g+8: the
+// 64 quants of each row as four 16-byte units u = 4*rr + j (k = 64q + 16j + 0..15) at
+// (u*32 + l)*16, then the lane's four scales {d(g, 2q), d(g, 2q+1), d(g+8, 2q),
+// d(g+8, 2q+1)} as one 8-byte word at 4096 + 8l.  Zero rows are all-zero.
+TLX_HD inline void pack_q8_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
+  const int g = lane >> 2, q = lane & 3;
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint8_t* grp = rows[g + 8 * rr];
+    for (int j = 0; j < 4; ++j)
+      for (int b = 0; b < 16; ++b) {
+        const int e = 16 * j + b;  // 0..63 within the lane's two blocks
+        out[((4 * rr + j) * 32 + lane) * 16 + b] = grp ? grp[34 * (2 * q + (e >> 5)) + 2 + (e & 31)] : 0;
+      }
+    for (int c = 0; c < 2; ++c)
+      for (int i = 0; i < 2; ++i) out[4096 + lane * 8 + rr * 4 + c * 2 + i] = grp ? grp[34 * (2 * q + c) + i] : 0;
+  }
+}
+
 TLX_HD inline void pack_lane(int qt, const uint8_t* const rows[16], int lane, uint8_t* out) {
   if (qt == QT_Q6_K) pack_q6_lane(rows, lane, out);
   else if (qt == QT_IQ4_XS) pack_iq4_lane(rows, lane, out);
   else if (qt == QT_Q4_K) pack_q4k_lane(rows, lane, out);
+  else if (qt == QT_Q5_K) pack_q5k_lane(rows, lane, out);
+  else if (qt == QT_Q8_0) pack_q8_lane(rows, lane, out);
   else pack_iq3_lane(rows, lane, out);
 }
 
@@ -349,6 +411,7 @@ __device__ __forceinline__ float2 iq3_block_scale(const Iq3Lane& s) {
 // B' the activation image's sub-block sums (entries 64..67 of each row).
 struct Q4Lane {
   uint32_t w[2][8];    // qs words of rows g / g+8 (bytes 4i .. 4i+3 of the lane's 32)
+  uint2 h[2];          // Q5_K only: fifth-bit bytes of rows g / g+8 (byte i: word i)
   uint32_t slo[2], clo[2], shi[2], chi[2];  // fp16x2 fma constants per row
   uint32_t mn[2];      // fp16x2 (mn_{2q}, mn_{2q+1}) per row
   float d[2], dmin[2];
@@ -371,8 +434,15 @@ __device__ __forceinline__ void q4_scale_min(uint32_t h1, uint32_t h2, uint32_t 
   }
 }
 
+template <bool Q5 = false>
 __device__ __forceinline__ void q4_load(const uint8_t* chunk, int lane, Q4Lane& s) {
   const int g = lane >> 2, q = lane & 3;
+  constexpr uint32_t kHdr = Q5 ? 2560u : 2048u;
+  if constexpr (Q5) {
+    const uint4 hb = *reinterpret_cast<const uint4*>(chunk + 2048 + lane * 16);
+    s.h[0] = make_uint2(hb.x, hb.y);
+    s.h[1] = make_uint2(hb.z, hb.w);
+  }
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
 #pragma unroll
@@ -383,7 +453,7 @@ __device__ __forceinline__ void q4_load(const uint8_t* chunk, int lane, Q4Lane& 
       s.w[rr][4 * hf + 2] = v.z;
       s.w[rr][4 * hf + 3] = v.w;
     }
-    const uint4 h = *reinterpret_cast<const uint4*>(chunk + 2048 + (g + 8 * rr) * 16);
+    const uint4 h = *reinterpret_cast<const uint4*>(chunk + kHdr + (g + 8 * rr) * 16);
     const __half2 dd = *reinterpret_cast<const __half2*>(&h.x);
     s.d[rr] = __low2float(dd);
     s.dmin[rr] = __high2float(dd);
@@ -400,20 +470,71 @@ __device__ __forceinline__ void q4_load(const uint8_t* chunk, int lane, Q4Lane& 
 }
 
 // decode mma m (0..15): k = 64q + 4m + {0..3} = element 4(m & 7) + {0..3} of
-// sub-block 2q (m < 8, low nibbles) or 2q+1 (m >= 8, high nibbles)
+// sub-block 2q (m < 8, low nibbles) or 2q+1 (m >= 8, high nibbles).  Q5_K adds the
+// fifth bit h above the nibble: 1024 + v + 16h (low) resp. 1024 + 16(v + 16h)
+// (high), still exact fp16 integers below 2048, so the same fma constants apply.
+template <bool Q5 = false>
 __device__ __forceinline__ void q4_mma(const Q4Lane& s, int m, uint32_t (&a)[4]) {
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const uint32_t w = s.w[rr][m & 7];
     const uint32_t p01 = prmt(w, 0u, 0x4140u);  // bytes 0, 1 -> low bytes of the halves
     const uint32_t p23 = prmt(w, 0u, 0x4342u);
-    if (m < 8) {
-      a[rr] = hfma2_u((p01 & 0x000F000Fu) | kMagic, s.slo[rr], s.clo[rr]);
-      a[rr + 2] = hfma2_u((p23 & 0x000F000Fu) | kMagic, s.slo[rr], s.clo[rr]);
-    } else {
-      a[rr] = hfma2_u((p01 & 0x00F000F0u) | kMagic, s.shi[rr], s.chi[rr]);
-      a[rr + 2] = hfma2_u((p23 & 0x00F000F0u) | kMagic, s.shi[rr], s.chi[rr]);
+    uint32_t h01 = 0u, h23 = 0u;
+    if constexpr (Q5) {
+      const int i = m & 7;
+      const uint32_t word = i < 4 ? s.h[rr].x : s.h[rr].y;
+      const uint32_t x = ((word >> (8 * (i & 3))) & 0xFFu) * 0x00100001u;  // byte at bits 0..7 and 20..27
+      if (m < 8) {
+        h01 = x & 0x00100010u;          // bit 4 <- lo(0), bit 20 <- lo(1)
+        h23 = (x >> 1) & 0x00100010u;   // bit 4 <- lo(2), bit 20 <- lo(3)
+      } else {
+        h01 = (x << 2) & 0x01000100u;   // bit 8 <- hi(0), bit 24 <- hi(1)
+        h23 = (x << 1) & 0x01000100u;   // bit 8 <- hi(2), bit 24 <- hi(3)
+      }
     }
+    if (m < 8) {
+      a[rr] = hfma2_u((p01 & 0x000F000Fu) | h01 | kMagic, s.slo[rr], s.clo[rr]);
+      a[rr + 2] = hfma2_u((p23 & 0x000F000Fu) | h23 | kMagic, s.slo[rr], s.clo[rr]);
+    } else {
+      a[rr] = hfma2_u((p01 & 0x00F000F0u) | h01 | kMagic, s.shi[rr], s.chi[rr]);
+      a[rr + 2] = hfma2_u((p23 & 0x00F000F0u) | h23 | kMagic, s.shi[rr], s.chi[rr]);
+    }
+  }
+}
+
+// Q8_0: per-block lane state.  A weight is fp16(d * q), the value the reference's
+// o-projection rounds to before its half multiply (engine/k3aonw32_11.cu:100-101):
+// q + 128 is placed in an fp16 mantissa (1024 + q + 128), 1152 is subtracted
+// (exact), and one fp16 multiply by d rounds the exact product once.
+struct Q8Lane {
+  uint4 u[2][4];       // quants of rows g / g+8: unit j = k 64q + 16j + 0..15
+  uint32_t d[2][2];    // fp16x2 (d, d) of block 2q + c for rows g / g+8
+};
+
+__device__ __forceinline__ void q8_load(const uint8_t* chunk, int lane, Q8Lane& s) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s.u[rr][j] = *reinterpret_cast<const uint4*>(chunk + ((4 * rr + j) * 32 + lane) * 16);
+  const uint2 dd = *reinterpret_cast<const uint2*>(chunk + 4096 + lane * 8);
+  s.d[0][0] = prmt(dd.x, 0u, 0x1010u);   // d(g, 2q) in both halves
+  s.d[0][1] = prmt(dd.x, 0u, 0x3232u);   // d(g, 2q+1)
+  s.d[1][0] = prmt(dd.y, 0u, 0x1010u);   // d(g+8, 2q)
+  s.d[1][1] = prmt(dd.y, 0u, 0x3232u);   // d(g+8, 2q+1)
+}
+
+// decode mma m (0..15): k = 64q + 4m + {0..3}, block 2q + (m >> 3)
+__device__ __forceinline__ void q8_mma(const Q8Lane& s, int m, uint32_t (&a)[4]) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const uint4 u = s.u[rr][m >> 2];
+    const uint32_t w = (m & 3) == 0 ? u.x : (m & 3) == 1 ? u.y : (m & 3) == 2 ? u.z : u.w;
+    const uint32_t p01 = (prmt(w, 0u, 0x4140u) ^ 0x00800080u) | kMagic;   // 1024 + q + 128
+    const uint32_t p23 = (prmt(w, 0u, 0x4342u) ^ 0x00800080u) | kMagic;
+    const uint32_t dd = s.d[rr][m >> 3];
+    a[rr] = hmul2_u(hadd2_u(p01, kMinus1152), dd);
+    a[rr + 2] = hmul2_u(hadd2_u(p23, kMinus1152), dd);
   }
 }
 

@@ -208,17 +208,32 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       b[1][1] = v1.y;
     }
   };
-  if constexpr (QT == QT_Q4_K) {
-    // Q4_K (single matrix): acc += d * sum (sc q) x  -  dmin * sum_s mn_s xsum_s
-    static_assert(NMAT == 1, "Q4_K is read by the STORE epilogue only");
-    Q4Lane s;
-    q4_load(chunk[0], lane, s);
+  if constexpr (QT == QT_Q8_0) {
+    // Q8_0 (single matrix): the fragments are the rounded weights fp16(d q)
+    static_assert(NMAT == 1, "Q8_0 is read by the STORE epilogue only");
+    Q8Lane s;
+    q8_load(chunk[0], lane, s);
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
       uint32_t b[NT][2];
       load_b(m, b);
       uint32_t af[4];
-      q4_mma(s, m, af);
+      q8_mma(s, m, af);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma16816(acc[0][nt], af, b[nt][0], b[nt][1]);
+    }
+  } else if constexpr (QT == QT_Q4_K || QT == QT_Q5_K) {
+    // Q4_K / Q5_K (single matrix): acc += d * sum (sc q) x  -  dmin * sum_s mn_s xsum_s
+    static_assert(NMAT == 1, "Q4_K / Q5_K are read by the STORE epilogue only");
+    constexpr bool Q5 = QT == QT_Q5_K;
+    Q4Lane s;
+    q4_load<Q5>(chunk[0], lane, s);
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      uint32_t b[NT][2];
+      load_b(m, b);
+      uint32_t af[4];
+      q4_mma<Q5>(s, m, af);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma16816(tmp[0][nt], af, b[nt][0], b[nt][1]);
     }
@@ -282,7 +297,7 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
       }
     }
   }
-  if constexpr (QT != QT_Q4_K) {
+  if constexpr (QT == QT_Q6_K || QT == QT_IQ3_XXS) {
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
 #pragma unroll
@@ -680,6 +695,8 @@ template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 16, STA
 template <> struct Cfg<QT_Q6_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
 template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
 template <> struct Cfg<QT_Q4_K, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_Q5_K, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
+template <> struct Cfg<QT_Q8_0, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
 template <> struct Cfg<QT_Q4_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };   // (not launched)
 template <> struct Cfg<QT_Q4_K, EPI_ARGMAX> { static constexpr int WPC = 16, STAGES = 2; };  // (not launched)
 template <> struct Cfg<QT_IQ3_XXS, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 3; };
@@ -699,6 +716,8 @@ static void cfg_for(int qt, int epi, int& wpc, int& stages) {
   TLX_CFG(QT_IQ3_XXS, EPI_ARGMAX)
   TLX_CFG(QT_IQ3_XXS, EPI_GATEUP)
   TLX_CFG(QT_Q4_K, EPI_STORE)
+  TLX_CFG(QT_Q5_K, EPI_STORE)
+  TLX_CFG(QT_Q8_0, EPI_STORE)
 #undef TLX_CFG
   wpc = 8;
   stages = 2;
@@ -707,8 +726,9 @@ static void cfg_for(int qt, int epi, int& wpc, int& stages) {
 static int cols_per_token(int x_dtype) { return x_dtype == DT_F32 ? 3 : 1; }
 
 static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, Plan& P) {
-  if (qt != QT_Q6_K && qt != QT_IQ3_XXS && qt != QT_Q4_K) return TLX_ERR_QTYPE;
-  if (qt == QT_Q4_K && epi != EPI_STORE) return TLX_ERR_QTYPE;  // Q4_K: plain matvec (v rows)
+  if (qt != QT_Q6_K && qt != QT_IQ3_XXS && qt != QT_Q4_K && qt != QT_Q5_K && qt != QT_Q8_0) return TLX_ERR_QTYPE;
+  // Q4_K / Q5_K / Q8_0: plain matvecs (v, GDN qkv and o-projection rows)
+  if ((qt == QT_Q4_K || qt == QT_Q5_K || qt == QT_Q8_0) && epi != EPI_STORE) return TLX_ERR_QTYPE;
   if (n_rows <= 0 || k <= 0 || (k % kQK) != 0) return TLX_ERR_SHAPE;
   if (x_dtype != DT_F32 && x_dtype != DT_F16 && x_dtype != DT_BF16 && x_dtype != DT_IMAGE) return TLX_ERR_DTYPE;
   P.CG = cols_per_token(x_dtype);
@@ -773,8 +793,11 @@ static int launch_t(const Plan& P, const GemvParams& gp, cudaStream_t stream) {
 
 template <int EPI>
 static int dispatch(int qt, const Plan& P, const GemvParams& gp, cudaStream_t s) {
-  if constexpr (EPI == EPI_STORE)
+  if constexpr (EPI == EPI_STORE) {
     if (qt == QT_Q4_K) return P.NT == 1 ? launch_t<QT_Q4_K, 1, EPI>(P, gp, s) : launch_t<QT_Q4_K, 2, EPI>(P, gp, s);
+    if (qt == QT_Q5_K) return P.NT == 1 ? launch_t<QT_Q5_K, 1, EPI>(P, gp, s) : launch_t<QT_Q5_K, 2, EPI>(P, gp, s);
+    if (qt == QT_Q8_0) return P.NT == 1 ? launch_t<QT_Q8_0, 1, EPI>(P, gp, s) : launch_t<QT_Q8_0, 2, EPI>(P, gp, s);
+  }
   if (qt == QT_Q6_K) return P.NT == 1 ? launch_t<QT_Q6_K, 1, EPI>(P, gp, s) : launch_t<QT_Q6_K, 2, EPI>(P, gp, s);
   return P.NT == 1 ? launch_t<QT_IQ3_XXS, 1, EPI>(P, gp, s) : launch_t<QT_IQ3_XXS, 2, EPI>(P, gp, s);
 }
@@ -866,7 +889,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint2* ximg = static_cast<const uint2*>(x);
   if (x_dtype != DT_IMAGE) {
-    rc = stage_image(x, x_dtype, ldx, m, k, wsb + P.off_img, qt == QT_Q4_K, stream);
+    rc = stage_image(x, x_dtype, ldx, m, k, wsb + P.off_img, qt == QT_Q4_K || qt == QT_Q5_K, stream);
     if (rc) return rc;
     ximg = reinterpret_cast<const uint2*>(wsb + P.off_img);
   }
@@ -909,60 +932,70 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   return dispatch<EPI_ARGMAX>(qt, P, gp, stream);
 }
 
-// ---- aq3k8v11: q / k (IQ3_XXS) and v (Q4_K) projections over one staged x ----
+// ---- projections over one staged x: aq3k8v11 (q / k IQ3_XXS, v Q4_K) and q5g8v11
+// (qkv Q5_K, gate IQ3_XXS).  Workspace: [image][ws of projection 0][ws 1]..., each
+// region 256-byte aligned.
 static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
 
-size_t aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas) {
+size_t projections_workspace_bytes(int n, const Projection* pr, int m, int64_t k, int x_dtype, int max_ctas) {
   if (x_dtype != DT_F16 && x_dtype != DT_BF16) return 0;
+  if (n < 1 || n > kMaxProjections) return 0;
   const size_t img = activation_image_bytes(m, k, x_dtype);
-  const size_t wq = gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas);
-  const size_t wk = gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas);
-  const size_t wv = gemv_workspace_bytes(EPI_STORE, QT_Q4_K, nv, k, m, DT_IMAGE, max_ctas);
-  if (!img || !wq || !wk || !wv) return 0;
-  return al256(img) + al256(wq) + al256(wk) + al256(wv);
+  if (!img) return 0;
+  size_t total = al256(img);
+  for (int i = 0; i < n; ++i) {
+    const size_t w = gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas);
+    if (!w) return 0;
+    total += al256(w);
+  }
+  return total;
 }
 
-int run_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
-                 int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
-                 void* v_out, void* ws, size_t ws_bytes, int max_ctas, cudaStream_t stream) {
-  if (!wq || !wk || !wv || !grid || !x || !q_out || !k_out || !v_out || !ws) return TLX_ERR_NULL;
+int run_projections(int n, const Projection* pr, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                    int64_t k, void* ws, size_t ws_bytes, int max_ctas, cudaStream_t stream) {
+  if (!x || !ws) return TLX_ERR_NULL;
+  for (int i = 0; i < n; ++i) {
+    if (!pr[i].w || !pr[i].out) return TLX_ERR_NULL;
+    if (pr[i].qt == QT_IQ3_XXS && !grid) return TLX_ERR_NULL;
+  }
   if (x_dtype != DT_F16 && x_dtype != DT_BF16) return TLX_ERR_DTYPE;
-  const size_t need = aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, max_ctas);
+  const size_t need = projections_workspace_bytes(n, pr, m, k, x_dtype, max_ctas);
   if (need == 0) return TLX_ERR_SHAPE;
   if (ws_bytes < need) return TLX_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return TLX_ERR_ALIGN;
-  uint8_t* p = static_cast<uint8_t*>(ws);
-  uint8_t* img = p;
-  p += al256(activation_image_bytes(m, k, x_dtype));
-  const size_t bq = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas));
-  const size_t bk = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas));
-  const size_t bv = al256(gemv_workspace_bytes(EPI_STORE, QT_Q4_K, nv, k, m, DT_IMAGE, max_ctas));
-  // x staged once, with the Q4_K sub-block sums; the three projections read it
-  int rc = stage_image(x, x_dtype, ldx, m, k, img, true, stream);
+  bool sums = false;
+  for (int i = 0; i < n; ++i) sums = sums || pr[i].qt == QT_Q4_K || pr[i].qt == QT_Q5_K;
+  uint8_t* img = static_cast<uint8_t*>(ws);
+  uint8_t* p = img + al256(activation_image_bytes(m, k, x_dtype));
+  // x staged once (with the sub-block sums when a K-quant reads it); every
+  // projection reads the image
+  int rc = stage_image(x, x_dtype, ldx, m, k, img, sums, stream);
   if (rc) return rc;
-  rc = run_gemv(EPI_STORE, QT_IQ3_XXS, wq, nullptr, grid, img, DT_IMAGE, 0, m, nq, k, nullptr, 0, q_out, DT_F16, nq,
-                0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p, bq, max_ctas, stream);
-  if (rc) return rc;
-  rc = run_gemv(EPI_STORE, QT_IQ3_XXS, wk, nullptr, grid, img, DT_IMAGE, 0, m, nk, k, nullptr, 0, k_out, DT_F16, nk,
-                0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p + bq, bk, max_ctas, stream);
-  if (rc) return rc;
-  return run_gemv(EPI_STORE, QT_Q4_K, wv, nullptr, nullptr, img, DT_IMAGE, 0, m, nv, k, nullptr, 0, v_out, DT_F16,
-                  nv, 0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, p + bq + bk, bv, max_ctas, stream);
+  for (int i = 0; i < n; ++i) {
+    const size_t b = al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas));
+    rc = run_gemv(EPI_STORE, pr[i].qt, pr[i].w, nullptr, pr[i].qt == QT_IQ3_XXS ? grid : nullptr, img, DT_IMAGE, 0, m,
+                  pr[i].n_rows, k, nullptr, 0, pr[i].out, DT_F16, pr[i].n_rows, 0, nullptr, nullptr, nullptr, nullptr,
+                  0, nullptr, p, b, max_ctas, stream);
+    if (rc) return rc;
+    p += b;
+  }
+  return TLX_OK;
 }
 
-// the three GEMVs' error words in an aq3k8v11 workspace (OR of the three)
-int aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas,
-                   uint32_t* err_out) {
+// the projections' error words in their workspace (OR over the projections)
+int projections_error(const void* ws, int n, const Projection* pr, int m, int64_t k, int x_dtype, int max_ctas,
+                      uint32_t* err_out) {
   if (!ws || !err_out) return TLX_ERR_NULL;
-  if (aq3k8v11_workspace_bytes(m, k, nq, nk, nv, x_dtype, max_ctas) == 0) return TLX_ERR_SHAPE;
+  if (projections_workspace_bytes(n, pr, m, k, x_dtype, max_ctas) == 0) return TLX_ERR_SHAPE;
   const uint8_t* p = static_cast<const uint8_t*>(ws) + al256(activation_image_bytes(m, k, x_dtype));
-  const size_t bq = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nq, k, m, DT_IMAGE, max_ctas));
-  const size_t bk = al256(gemv_workspace_bytes(EPI_STORE, QT_IQ3_XXS, nk, k, m, DT_IMAGE, max_ctas));
-  uint32_t e[3] = {0, 0, 0};
-  const size_t off[3] = {0, bq, bq + bk};
-  for (int i = 0; i < 3; ++i)
-    if (cudaMemcpy(&e[i], p + off[i], 4, cudaMemcpyDeviceToHost) != cudaSuccess) return TLX_ERR_LAUNCH;
-  *err_out = e[0] | e[1] | e[2];
+  uint32_t e = 0;
+  for (int i = 0; i < n; ++i) {
+    uint32_t ei = 0;
+    if (cudaMemcpy(&ei, p, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return TLX_ERR_LAUNCH;
+    e |= ei;
+    p += al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas));
+  }
+  *err_out = e;
   return TLX_OK;
 }
 

@@ -17,12 +17,19 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
              const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
              cudaStream_t stream);
 size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
-size_t aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas);
-int aq3k8v11_error(const void* ws, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype, int max_ctas,
-                   uint32_t* err_out);
-int run_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
-                 int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
-                 void* v_out, void* ws, size_t ws_bytes, int max_ctas, cudaStream_t stream);
+// one matvec of a projection group: n_rows rows of qtype qt, fp16 output [m][n_rows]
+struct Projection {
+  int qt;
+  const void* w;
+  int64_t n_rows;
+  void* out;
+};
+constexpr int kMaxProjections = 4;
+size_t projections_workspace_bytes(int n, const Projection* pr, int m, int64_t k, int x_dtype, int max_ctas);
+int run_projections(int n, const Projection* pr, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                    int64_t k, void* ws, size_t ws_bytes, int max_ctas, cudaStream_t stream);
+int projections_error(const void* ws, int n, const Projection* pr, int m, int64_t k, int x_dtype, int max_ctas,
+                      uint32_t* err_out);
 size_t activation_image_bytes(int m, int64_t k, int x_dtype);
 int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream);
 size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);

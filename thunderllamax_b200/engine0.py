@@ -148,6 +148,34 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
         attn[key](wq, wk, wv4, xh4.view(rows, dim), q=qrow4.view(rows, nq), k=krow4.view(rows, nk),
                   v=vrow4.view(rows, nv))
 
+    gdn = {}
+
+    def q5g8v11(wq5, wq3g, gridf, xh4, qkv4, gate4):
+        # engine/q5g8v11.cu:68-150: qkv 10240 (Q5_K) and gate 6144 (IQ3_XXS) rows,
+        # fp16 xh4 [rows][dim] -> fp16 [rows][n]
+        del gridf
+        nqkv, ngate = qkv4.numel() // rows, gate4.numel() // rows
+        if (nqkv, ngate) not in gdn:
+            gdn[(nqkv, ngate)] = ops.GdnProjections(rows, dim, nqkv, ngate, torch.float16)
+        gdn[(nqkv, ngate)](wq5, wq3g, xh4.view(rows, dim), qkv=qkv4.view(rows, nqkv), gate=gate4.view(rows, ngate))
+
+    oproj_ws = {}
+
+    def _oproj(qtype, w, z4, attn_out4):
+        kz = z4.numel() // rows
+        if (qtype, kz) not in oproj_ws:
+            oproj_ws[(qtype, kz)] = ops.Workspace.for_shape(ops.MODE_STORE, qtype, dim, kz, rows, torch.float16)
+        ops.gemv(qtype, w, z4.view(rows, kz), dim, oproj_ws[(qtype, kz)], y=attn_out4.view(rows, dim))
+
+    def op38nw32_11(wo, gridf, z4, attn_out4):
+        # engine/op38nw32_11.cu:88-120: GDN o-projection, IQ3_XXS 5120 x 6144, fp16 in/out
+        del gridf
+        _oproj("iq3_xxs", wo, z4, attn_out4)
+
+    def k3aonw32_11(wq8, z4, attn_out4):
+        # engine/k3aonw32_11.cu:88-116: GDN o-projection, Q8_0 5120 x 6144, fp16 in/out
+        _oproj("q8_0", wq8, z4, attn_out4)
+
     def acceptsel11k(rec4, conv4, m_slot, *scratch):
         # engine/acceptsel11k.cu:8-40: conv5x..conv11x then rec6x..rec11x, as the reference
         ops.acceptsel11k(rec4, conv4, m_slot, scratch[:7], scratch[7:13])
@@ -158,7 +186,8 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
 
     progs = {"ffn8v11": ffn8v11, "down8nw32_11": down8nw32_11, "head8v11": head8v11, "amx3": amx3,
              "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36, "acceptsel11k": acceptsel11k,
-             "h_argmax": h_argmax, "aq3k8v11": aq3k8v11}
+             "h_argmax": h_argmax, "aq3k8v11": aq3k8v11, "q5g8v11": q5g8v11, "op38nw32_11": op38nw32_11,
+             "k3aonw32_11": k3aonw32_11}
     return {k: Prog(k, v) for k, v in progs.items()}
 
 

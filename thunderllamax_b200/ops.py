@@ -114,7 +114,8 @@ class Workspace:
 
 def plan(mode: int, qtype, n_rows: int, k: int, m: int, x_dtype=torch.bfloat16) -> dict:
     info = (ctypes.c_int32 * 12)()
-    check(_lib.lib().tlx_gemv_plan(mode, qtype_id(qtype), n_rows, k, m, _DT[x_dtype], info, 12), "plan")
+    dt = TLX_DT_IMAGE if x_dtype == "image" else _DT[x_dtype]
+    check(_lib.lib().tlx_gemv_plan(mode, qtype_id(qtype), n_rows, k, m, dt, info, 12), "plan")
     keys = ["tiles", "blocks", "segments", "blocks_per_segment", "ctas", "ctas_per_segment", "max_pieces",
             "columns", "ntiles", "warps_per_cta", "stages", "smem"]
     return dict(zip(keys, list(info)))
@@ -282,6 +283,36 @@ class AttnProjections:
         return int(e.value)
 
 
+class GdnProjections:
+    """q5g8v11: the GDN block's qkv (Q5_K) and gate (IQ3_XXS) projections of m rows of
+    x, one staging of x shared by the two GEMVs (tlx_q5g8v11).  Outputs fp16 [m][n]."""
+
+    def __init__(self, m: int, k: int, nqkv: int, ngate: int, x_dtype=torch.float16, device="cuda"):
+        self.m, self.k, self.nqkv, self.ngate = int(m), int(k), int(nqkv), int(ngate)
+        self.dt = _DT[x_dtype]
+        nb = int(_lib.lib().tlx_q5g8v11_workspace_bytes(self.m, self.k, self.nqkv, self.ngate, self.dt))
+        if nb == 0:
+            raise TLXError(f"unsupported q5g8v11 shape m={m} k={k} nqkv={nqkv} ngate={ngate} {x_dtype}")
+        self.ws = Workspace(nb, device)
+
+    def __call__(self, wqkv, wgate, x: torch.Tensor, qkv=None, gate=None):
+        require_device()
+        if x.dim() != 2 or x.stride(1) != 1 or tuple(x.shape) != (self.m, self.k) or _DT.get(x.dtype) != self.dt:
+            raise TLXError("x must be a row-major [m][k] tensor of the workspace's dtype")
+        qkv = qkv if qkv is not None else torch.empty((self.m, self.nqkv), dtype=torch.float16, device=x.device)
+        gate = gate if gate is not None else torch.empty((self.m, self.ngate), dtype=torch.float16, device=x.device)
+        check(_lib.lib().tlx_q5g8v11(_ptr(wqkv), _ptr(wgate), _ptr(grid(str(x.device))), _ptr(x), self.dt,
+                                     x.stride(0), self.m, self.k, self.nqkv, self.ngate, _ptr(qkv), _ptr(gate),
+                                     _ptr(self.ws.buf), self.ws.nbytes, _stream(x)), "q5g8v11")
+        return qkv, gate
+
+    def error(self) -> int:
+        e = ctypes.c_uint32(0)
+        check(_lib.lib().tlx_q5g8v11_error(_ptr(self.ws.buf), self.m, self.k, self.nqkv, self.ngate, self.dt,
+                                           ctypes.byref(e)), "q5g8v11_error")
+        return int(e.value)
+
+
 GDN_BLOCKS, GDN_REC, GDN_CONV = 48, 786432, 30720  # engine/acceptsel11k.cu:22-38
 
 
@@ -329,5 +360,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]

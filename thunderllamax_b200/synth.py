@@ -23,8 +23,9 @@ from __future__ import annotations
 import numpy as np
 
 QK = 256
-BLOCK_BYTES = {"iq3_xxs": 98, "q6_k": 210, "iq4_xs": 136, "q4_k": 144}
-GGML_TYPE = {"iq3_xxs": 18, "q6_k": 14, "iq4_xs": 23, "q4_k": 12}
+# bytes per 256 weights of a row (q8_0: eight 34-byte GGUF blocks)
+BLOCK_BYTES = {"iq3_xxs": 98, "q6_k": 210, "iq4_xs": 136, "q4_k": 144, "q5_k": 176, "q8_0": 272}
+GGML_TYPE = {"iq3_xxs": 18, "q6_k": 14, "iq4_xs": 23, "q4_k": 12, "q5_k": 13, "q8_0": 8}
 
 
 def row_bytes(qtype: str, k: int) -> int:
@@ -75,7 +76,30 @@ def q4k_blocks(rng: np.random.Generator, n_rows: int, k: int) -> np.ndarray:
     return blk.reshape(n_rows, nb * 144)
 
 
-BLOCK_GEN = {"iq3_xxs": iq3xxs_blocks, "q6_k": q6k_blocks, "iq4_xs": iq4xs_blocks, "q4_k": q4k_blocks}
+def q5k_blocks(rng: np.random.Generator, n_rows: int, k: int) -> np.ndarray:
+    """Q5_K blocks (d f16 | dmin f16 | scales[12] | qh[32] | qs[128]): random 6-bit
+    scales and mins, uniform 5-bit quants, d and dmin as for Q4_K."""
+    nb = k // QK
+    blk = np.empty((n_rows, nb, 176), dtype=np.uint8)
+    blk[..., 0:2] = _f16_bytes(rng.uniform(1e-4, 1e-3, (n_rows, nb)))
+    blk[..., 2:4] = _f16_bytes(rng.uniform(1e-4, 1e-3, (n_rows, nb)))
+    blk[..., 4:176] = rng.integers(0, 256, (n_rows, nb, 172), dtype=np.uint8)
+    return blk.reshape(n_rows, nb * 176)
+
+
+def q8_0_blocks(rng: np.random.Generator, n_rows: int, k: int) -> np.ndarray:
+    """Q8_0 blocks (d f16 | qs[32] int8) for k weights per row: d of the magnitude
+    an o-projection's 32-weight blocks have (max |w| / 127 for w ~ N(0, 0.02)),
+    quants over the full int8 range (-128 included)."""
+    nb = k // 32
+    blk = np.empty((n_rows, nb, 34), dtype=np.uint8)
+    blk[..., 0:2] = _f16_bytes(rng.uniform(2e-4, 8e-4, (n_rows, nb)))
+    blk[..., 2:34] = rng.integers(0, 256, (n_rows, nb, 32), dtype=np.uint8)
+    return blk.reshape(n_rows, nb * 34)
+
+
+BLOCK_GEN = {"iq3_xxs": iq3xxs_blocks, "q6_k": q6k_blocks, "iq4_xs": iq4xs_blocks, "q4_k": q4k_blocks,
+             "q5_k": q5k_blocks, "q8_0": q8_0_blocks}
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
