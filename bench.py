@@ -432,6 +432,45 @@ def measure_o_proj(args, torch, peak):
     return out
 
 
+def measure_lookup(args, torch, peak):
+    """lookup11_nw32 (the K = 10 n-gram drafter) over a 100K-token history with the
+    suffix planted near the start (the whole range is scanned); CUDA graph replay.
+    Bytes = the history scanned (4 B per start)."""
+    import time
+    from thunderllamax_b200 import ops
+    import oracle
+
+    n = 100_000
+    rng = np.random.default_rng(47)
+    h = rng.integers(0, 50_000, n).astype(np.int32)
+    h[n - 8:n] = h[1000:1008]
+    hist = torch.from_numpy(h).cuda()
+    pos = torch.tensor([n], dtype=torch.int32, device="cuda")
+    cyc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ring = torch.zeros(10, dtype=torch.int32, device="cuda")
+    l_hist = torch.zeros(4, dtype=torch.int32, device="cuda")
+    lk = ops.Lookup(10)
+    fn = lambda: lk(hist, pos, cyc, ring, l_hist)  # noqa: E731
+    for _ in range(3):
+        fn()
+
+    def twenty():
+        for _ in range(20):
+            fn()
+    graph = _graph_of(twenty, torch)          # 20 back-to-back launches per replay
+    ms = time_graph(graph.replay, 10, torch) / 20
+    t0 = time.perf_counter()
+    ref = oracle.lookup_ngram(h, n, 10, 19)
+    cpu_ms = (time.perf_counter() - t0) * 1000
+    ok = int(l_hist[0]) == ref[0] and np.array_equal(ring.cpu().numpy(), ref[1])
+    return {"workload": "lookup11_nw32: K = 10 drafts from a 100000-token history (8-token suffix, full scan)",
+            "us_per_call": round(ms * 1000, 2), "bytes_per_call": 4 * n,
+            "gbs": round(4 * n / (ms * 1e-3) / 1e9, 1), "launches_per_call": 1, "graph": "CUDA graph replay",
+            "matches_oracle": bool(ok),
+            "cpu_baseline": {"us_per_call": round(cpu_ms * 1000, 1), "cores": 1, "kind": "port",
+                             "sample": "the numpy oracle on the same history"}}
+
+
 def measure_acceptsel(args, torch, peak):
     """acceptsel11k at the reference size (48 GDN blocks x (786432 + 30720) fp32, m = 7):
     bytes = the slot read + the live slot written."""
@@ -582,6 +621,7 @@ def run_ours(args):
         extras["acceptsel11k"] = measure_acceptsel(args, torch, peak)
         extras["gdn_qkv"] = measure_gdn_qkv(args, torch, peak)
         extras["o_proj"] = measure_o_proj(args, torch, peak)
+        extras["lookup11"] = measure_lookup(args, torch, peak)
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,

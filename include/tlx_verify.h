@@ -232,6 +232,22 @@ int tlx_q5g8v11(const void* wqkv, const void* wgate, const uint32_t* grid, const
 /* the workspace's error bits (OR over the two GEMVs; synchronous read) */
 int tlx_q5g8v11_error(const void* ws, int m, int64_t k, int64_t nqkv, int64_t ngate, int x_dtype, uint32_t* err_out);
 
+/* n-gram draft proposal (lookup{K+1}_nw32, engine/lookup11_nw32.cu:8-60; the
+ * K = 4..9 siblings engine/lookup5_nw32.cu .. lookup10_nw32.cu differ only in K
+ * and scan_end).  With pos = pos_slot[0] and the suffix s = tok_hist[pos-8 ..
+ * pos-1]: every start i in [0, pos - scan_end] is scored by the length l (0..8)
+ * of the common prefix of tok_hist[i .. i+7] and s; the largest (l, i) wins
+ * (longest, then most recent).  l_hist[cyc_slot[0]] = l + 1, or 1000000 + pos
+ * when pos < scan_end; on l = 8, drafts[j] = tok_hist[i + 8 + j] for j <
+ * n_drafts (the dring0..dring{K-1} buffers, contiguous here).  The reference's
+ * scan_end is 8 + K for K <= 7 and 9 + K for K >= 8 (lookup11: K = 10,
+ * scan_end = 19).  hist_len = tokens the buffer holds (16-byte aligned); a
+ * device pos beyond it writes nothing.  Workspace: tlx_lookup_workspace_bytes,
+ * zeroed once (tlx_workspace_init) and reused; one launch, stream-ordered. */
+size_t tlx_lookup_workspace_bytes(void);
+int tlx_lookup(const int32_t* tok_hist, int64_t hist_len, const int32_t* pos_slot, const int32_t* cyc_slot,
+               int32_t* drafts, int n_drafts, int scan_end, int32_t* l_hist, void* ws, size_t ws_bytes, void* stream);
+
 /* acceptsel11k: commit the accepted GDN state (engine/acceptsel11k.cu:8-40).
  * rec4 is [n_blocks][5][rec_elems] fp32 and conv4 [n_blocks][5][conv_elems] fp32,
  * slot 4 the live one; with m = m_slot[0] (device int, 0..10):

@@ -21,6 +21,6 @@ from .dequant import (  # noqa: F401
     dequant_iq3xxs, dequant_q6k, dequant_iq4xs, dequant_q4k, dequant_q5k, dequant_q8_0, dequant,
 )
 from .path import (  # noqa: F401
-    matvec_f64, ffn_f64, head_logits_f64, argmax_rows, h_argmax, acceptsel11k, head_argmax, accept, accept11k,
+    matvec_f64, ffn_f64, head_logits_f64, argmax_rows, h_argmax, acceptsel11k, lookup_ngram, head_argmax, accept, accept11k,
     router_top8, moe_verify_f64, silu_f64, min_top2_gap,
 )

@@ -71,6 +71,33 @@ def argmax_rows(logits: np.ndarray):
     return mx, idx
 
 
+def lookup_ngram(tok_hist, pos: int, n_drafts: int, scan_end: int):
+    """n-gram draft proposal of engine/lookup11_nw32.cu:17-58 (and its K = 4..9
+    siblings, which differ only in K and scan_end).
+
+    Suffix s = hist[pos-8 .. pos-1]; every start i in [0, pos - scan_end] scores
+    l = the length of the common prefix of hist[i .. i+7] and s (the nested ifs of
+    lines 28-35); the winner is the largest (l, i) (the key (l << 20) | i, line 36,
+    maximised over the CTA, lines 38-41).  Returns (l_hist value, drafts): l_hist =
+    1000000 + pos when pos < scan_end, else l + 1 (line 45); drafts = hist[i+8 ..
+    i+8+K-1] when l >= 8 (lines 46-57), else None (the ring is left unchanged)."""
+    h = np.asarray(tok_hist, dtype=np.int64)
+    if pos < scan_end:
+        return 1000000 + pos, None
+    s = h[pos - 8:pos]
+    iend = pos - scan_end
+    starts = np.arange(iend + 1)
+    # l = number of leading positions j with hist[i+j] == s[j]
+    eq = np.stack([h[starts + j] == s[j] for j in range(8)], axis=1)      # [n, 8]
+    l = np.where(eq.all(axis=1), 8, np.argmin(eq, axis=1))
+    best_l = int(l.max())
+    if best_l == 0:
+        return 1, None
+    i = int(starts[l == best_l].max())
+    drafts = h[i + 8:i + 8 + n_drafts].astype(np.int32) if best_l >= 8 else None
+    return best_l + 1, drafts
+
+
 def acceptsel11k(rec4, conv4, m, conv_x, rec_x):
     """acceptsel11k (engine/acceptsel11k.cu:8-40): slot m of the GDN state becomes the
     live slot 4.  rec4 [B][5][R], conv4 [B][5][C]; rec from rec4[:, m] for m <= 4,

@@ -54,6 +54,8 @@ _SIGS = {
     "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
     "tlx_h_argmax": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "tlx_acceptsel11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "tlx_lookup_workspace_bytes": (c_size, []),
+    "tlx_lookup": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_size, c_vp]),
     "tlx_q5g8v11_workspace_bytes": (c_size, [c_int, c_i64, c_i64, c_i64, c_int]),
     "tlx_q5g8v11_error": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_int, c_vp]),
     "tlx_q5g8v11": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,

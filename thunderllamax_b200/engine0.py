@@ -176,6 +176,20 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
         # engine/k3aonw32_11.cu:88-116: GDN o-projection, Q8_0 5120 x 6144, fp16 in/out
         _oproj("q8_0", wq8, z4, attn_out4)
 
+    lookups = {}
+
+    def make_lookup(n):
+        # engine/lookup{n}_nw32.cu: (tok_hist, pos_slot, cur_slot, dring0..dring{n-2}, l_hist, cyc_slot)
+        k = n - 1
+
+        def lookup(tok_hist, pos_slot, cur_slot, *rest):
+            del cur_slot  # read but unused by the reference kernels too
+            drings, l_hist, cyc_slot = rest[:k], rest[k], rest[k + 1]
+            if k not in lookups:
+                lookups[k] = ops.Lookup(k)
+            lookups[k](tok_hist, pos_slot, cyc_slot, _contig_drafts(list(drings)), l_hist)
+        return lookup
+
     def acceptsel11k(rec4, conv4, m_slot, *scratch):
         # engine/acceptsel11k.cu:8-40: conv5x..conv11x then rec6x..rec11x, as the reference
         ops.acceptsel11k(rec4, conv4, m_slot, scratch[:7], scratch[7:13])
@@ -188,6 +202,8 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
              "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36, "acceptsel11k": acceptsel11k,
              "h_argmax": h_argmax, "aq3k8v11": aq3k8v11, "q5g8v11": q5g8v11, "op38nw32_11": op38nw32_11,
              "k3aonw32_11": k3aonw32_11}
+    for n in range(5, 12):
+        progs[f"lookup{n}_nw32"] = make_lookup(n)
     return {k: Prog(k, v) for k, v in progs.items()}
 
 

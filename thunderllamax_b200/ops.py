@@ -313,6 +313,34 @@ class GdnProjections:
         return int(e.value)
 
 
+# lookup{K+1}_nw32: K drafts and the scan end (starts i <= pos - scan_end), per the
+# reference kernels engine/lookup5_nw32.cu .. engine/lookup11_nw32.cu
+LOOKUP_SCAN_END = {4: 12, 5: 13, 6: 14, 7: 15, 8: 17, 9: 18, 10: 19}
+
+
+class Lookup:
+    """n-gram draft proposal over the device token history (tlx_lookup): on an
+    8-token suffix match the next K history tokens become the drafts; l_hist[cyc]
+    records the match length + 1.  One launch, stream-ordered, workspace reused."""
+
+    def __init__(self, n_drafts: int = 10, scan_end: int = None, device="cuda"):
+        self.k = int(n_drafts)
+        self.scan_end = int(scan_end if scan_end is not None else LOOKUP_SCAN_END[self.k])
+        self.ws = Workspace(int(_lib.lib().tlx_lookup_workspace_bytes()), device)
+
+    def __call__(self, tok_hist: torch.Tensor, pos_slot: torch.Tensor, cyc_slot: torch.Tensor,
+                 drafts: torch.Tensor, l_hist: torch.Tensor) -> None:
+        require_device()
+        for t in (tok_hist, pos_slot, cyc_slot, drafts, l_hist):
+            if t.dtype != torch.int32 or not t.is_contiguous():
+                raise TLXError("lookup buffers are contiguous int32")
+        if drafts.numel() < self.k:
+            raise TLXError(f"drafts holds {drafts.numel()} < {self.k} entries")
+        check(_lib.lib().tlx_lookup(_ptr(tok_hist), tok_hist.numel(), _ptr(pos_slot), _ptr(cyc_slot), _ptr(drafts),
+                                    self.k, self.scan_end, _ptr(l_hist), _ptr(self.ws.buf), self.ws.nbytes,
+                                    _stream(tok_hist)), "lookup")
+
+
 GDN_BLOCKS, GDN_REC, GDN_CONV = 48, 786432, 30720  # engine/acceptsel11k.cu:22-38
 
 
@@ -360,5 +388,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "Lookup", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
