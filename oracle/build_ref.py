@@ -21,9 +21,18 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 REF = os.environ.get("TLX_REFERENCE", "/root/reference")
 
-# kernels whose every access was checked by reading against the shapes the tests
-# launch them with (integer / index work of the verify cycle)
-KERNELS = [f"lookup{n}_nw32" for n in range(5, 12)]
+# (engine-relative source, kernel name): kernels whose every access was checked by
+# reading against the shapes the tests launch them with (integer / index / copy work
+# of the verify cycle).  Fixed shapes compiled into them: amx3 / h_argmax read
+# 248320 fp16 logits per row, accept11k copies 5120-float rows, acceptsel11k
+# copies [48][5] x (786432 + 30720) floats and indexes its slot by m in 0..10.
+KERNELS = [(f"lookup{n}_nw32.cu", f"lookup{n}_nw32") for n in range(5, 12)] + [
+    ("accept11k.cu", "accept11k"),
+    ("acceptsel11k.cu", "acceptsel11k"),
+    ("h_argmax.cu", "h_argmax"),
+    ("amx3.cu", "amx3"),
+    ("mm/MM_P7_acc36.cu", "acc36"),
+]
 
 
 def build(verbose: bool = False) -> list[str]:
@@ -33,8 +42,8 @@ def build(verbose: bool = False) -> list[str]:
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     os.makedirs(OUT, exist_ok=True)
     built = []
-    for name in KERNELS:
-        src = os.path.join(src_dir, name + ".cu")
+    for rel, name in KERNELS:
+        src = os.path.join(src_dir, rel)
         if not os.path.exists(src):
             continue
         out = os.path.join(OUT, name + ".cubin")
