@@ -6,6 +6,8 @@
 #include <cstring>
 #include <vector>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "formats.cuh"
 #include "tlx_internal.h"
@@ -122,49 +124,129 @@ __global__ void acceptsel_kernel(float* __restrict__ rec4, float* __restrict__ c
 
 // argmax key of one row of materialised logits, reduced over the CTA (valid in
 // thread 0): the amx3 / h_argmax scan rules through argmax_key
+// Row argmax over materialised logits: one thread-block cluster of kArgmaxCluster
+// CTAs per row.  Each CTA scans an interleaved share of the row with 16-byte loads
+// (four in flight per thread) and reduces its key (argmax_key: candidates v >
+// -1e30, lowest index on ties) through warp shuffles and shared memory; rank 0
+// reads the other CTAs' keys from distributed shared memory.  No global scratch,
+// so concurrent calls never share state.
+constexpr int kArgmaxCluster = 8;
+constexpr int kArgmaxThreads = 512;
+
 template <typename T>
-__device__ uint64_t row_argmax_key(const T* __restrict__ row, int64_t n) {
+__device__ __forceinline__ uint64_t scan_keys(const T* __restrict__ row, int64_t n, int rank, bool vec) {
+  constexpr int V = 16 / sizeof(T);
   uint64_t best = 0ull;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    float v;
-    if constexpr (sizeof(T) == 2) v = __half2float(row[i]);
-    else v = row[i];
+  const int64_t t = static_cast<int64_t>(rank) * kArgmaxThreads + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(kArgmaxCluster) * kArgmaxThreads;
+  auto take = [&](float v, int64_t i) {
     const uint64_t k = argmax_key(v, static_cast<uint32_t>(i));
     best = k > best ? k : best;
+  };
+  if (vec) {
+    const int64_t nv = n / V;   // whole 16-byte vectors
+#pragma unroll 4
+    for (int64_t u = t; u < nv; u += stride) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + u);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      if constexpr (sizeof(T) == 2) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[j]));
+          take(f.x, u * V + 2 * j);
+          take(f.y, u * V + 2 * j + 1);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) take(__uint_as_float(ws[j]), u * V + j);
+      }
+    }
+    for (int64_t i = nv * V + t; i < n; i += stride) {
+      if constexpr (sizeof(T) == 2) take(__half2float(row[i]), i);
+      else take(row[i], i);
+    }
+  } else {
+    for (int64_t i = t; i < n; i += stride) {
+      if constexpr (sizeof(T) == 2) take(__half2float(row[i]), i);
+      else take(row[i], i);
+    }
   }
   for (int o = 16; o > 0; o >>= 1) {
     const uint64_t k = __shfl_xor_sync(0xffffffffu, best, o);
     best = k > best ? k : best;
   }
-  __shared__ uint64_t wb[32];
+  return best;
+}
+
+// the cluster's key for its row (valid in thread 0 of rank 0); every thread of the
+// cluster must call it (it holds two cluster barriers)
+template <typename T>
+__device__ uint64_t cluster_row_key(const T* __restrict__ row, int64_t n, bool vec) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = static_cast<int>(cl.block_rank());
+  __shared__ uint64_t wb[kArgmaxThreads / 32];
+  __shared__ uint64_t cta_key;
+  const uint64_t best = scan_keys(row, n, rank, vec);
   if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t b = 0ull;
+    for (int w = 0; w < kArgmaxThreads / 32; ++w) b = wb[w] > b ? wb[w] : b;
+    cta_key = b;
+  }
+  cl.sync();   // every CTA's key is in its shared memory
   uint64_t b = 0ull;
-  if (threadIdx.x == 0)
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) b = wb[w] > b ? wb[w] : b;
+  if (rank == 0 && threadIdx.x == 0)
+    for (int r = 0; r < kArgmaxCluster; ++r) {
+      const uint64_t k = *cl.map_shared_rank(&cta_key, r);
+      b = k > b ? k : b;
+    }
+  cl.sync();   // rank 0 has read every CTA's key before any CTA exits
   return b;
 }
 
-// per-row argmax over materialised logits (engine/amx3.cu:117-142): one CTA per row
+// per-row argmax (engine/amx3.cu:117-142): cluster blockIdx.x / kArgmaxCluster = row
 template <typename T>
-__global__ void argmax_rows_kernel(const T* __restrict__ logits, int64_t n, int64_t ld, int32_t* __restrict__ amds) {
-  const uint64_t b = row_argmax_key(logits + blockIdx.x * ld, n);
-  if (threadIdx.x == 0) amds[blockIdx.x] = key_index(b);
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const T* __restrict__ logits, int64_t n,
+                                                                     int64_t ld, bool vec,
+                                                                     int32_t* __restrict__ amds) {
+  const int row = blockIdx.x / kArgmaxCluster;
+  const uint64_t b = cluster_row_key(logits + row * ld, n, vec);
+  if (blockIdx.x % kArgmaxCluster == 0 && threadIdx.x == 0) amds[row] = key_index(b);
 }
 
 // h_argmax (T = 1, engine/h_argmax.cu:13-42): the argmax of one row, then the
 // decode-loop side effects tok_slot = idx, tok_hist[pos] = idx, pos_slot = pos + 1
 template <typename T>
-__global__ void h_argmax_kernel(const T* __restrict__ logits, int64_t n, int32_t* __restrict__ tok_slot,
-                                int32_t* __restrict__ pos_slot, int32_t* __restrict__ tok_hist) {
-  const uint64_t b = row_argmax_key(logits, n);
-  if (threadIdx.x == 0) {
+__global__ void __launch_bounds__(kArgmaxThreads) h_argmax_kernel(const T* __restrict__ logits, int64_t n, bool vec,
+                                                                  int32_t* __restrict__ tok_slot,
+                                                                  int32_t* __restrict__ pos_slot,
+                                                                  int32_t* __restrict__ tok_hist) {
+  const uint64_t b = cluster_row_key(logits, n, vec);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
     const int32_t idx = key_index(b);
     const int32_t pos = pos_slot[0];
     tok_slot[0] = idx;
     tok_hist[pos] = idx;
     pos_slot[0] = pos + 1;
   }
+}
+
+template <typename Kern, typename... Args>
+int launch_clusters(Kern kern, int rows, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows * kArgmaxCluster));
+  cfg.blockDim = dim3(kArgmaxThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kArgmaxCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
 __global__ void argmax_merge_kernel(const uint64_t* __restrict__ keys, int n_shards, int m,
@@ -530,27 +612,29 @@ int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, in
                  void* stream) {
   if (!logits || !tok_slot || !pos_slot || !tok_hist) return TLX_ERR_NULL;
   if (n <= 0 || n > 0xFFFFFFFFll) return TLX_ERR_SHAPE;
+  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   if (dtype == TLX_DT_F32)
-    h_argmax_kernel<float><<<1, 1024, 0, as_stream(stream)>>>(static_cast<const float*>(logits), n, tok_slot,
-                                                                pos_slot, tok_hist);
-  else if (dtype == TLX_DT_F16)
-    h_argmax_kernel<__half><<<1, 1024, 0, as_stream(stream)>>>(static_cast<const __half*>(logits), n, tok_slot,
-                                                                 pos_slot, tok_hist);
-  else
-    return TLX_ERR_DTYPE;
-  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+    return launch_clusters(h_argmax_kernel<float>, 1, as_stream(stream), static_cast<const float*>(logits), n, vec,
+                           tok_slot, pos_slot, tok_hist);
+  if (dtype == TLX_DT_F16)
+    return launch_clusters(h_argmax_kernel<__half>, 1, as_stream(stream), static_cast<const __half*>(logits), n, vec,
+                           tok_slot, pos_slot, tok_hist);
+  return TLX_ERR_DTYPE;
 }
 
 int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld, int32_t* amds, void* stream) {
   if (!logits || !amds) return TLX_ERR_NULL;
-  if (m <= 0 || n <= 0 || ld < n || n > 0xFFFFFFFFll) return TLX_ERR_SHAPE;
+  if (m <= 0 || n <= 0 || ld < n || n > 0xFFFFFFFFll || m > (1 << 24)) return TLX_ERR_SHAPE;
+  const size_t es = dtype == TLX_DT_F32 ? 4 : 2;
+  // 16-byte loads when every row starts on a 16-byte boundary
+  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (static_cast<size_t>(ld) * es) % 16 == 0;
   if (dtype == TLX_DT_F32)
-    argmax_rows_kernel<float><<<m, 1024, 0, as_stream(stream)>>>(static_cast<const float*>(logits), n, ld, amds);
-  else if (dtype == TLX_DT_F16)
-    argmax_rows_kernel<__half><<<m, 1024, 0, as_stream(stream)>>>(static_cast<const __half*>(logits), n, ld, amds);
-  else
-    return TLX_ERR_DTYPE;
-  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+    return launch_clusters(argmax_rows_kernel<float>, m, as_stream(stream), static_cast<const float*>(logits), n, ld,
+                           vec, amds);
+  if (dtype == TLX_DT_F16)
+    return launch_clusters(argmax_rows_kernel<__half>, m, as_stream(stream), static_cast<const __half*>(logits), n,
+                           ld, vec, amds);
+  return TLX_ERR_DTYPE;
 }
 
 int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
