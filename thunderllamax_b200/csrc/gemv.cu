@@ -543,14 +543,17 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 #pragma unroll
               for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
           // pieces in fixed k order (segment s, piece j); slot loads are issued in
-          // batches of 4 ahead of the in-order adds
+          // batches of UB slots ahead of the in-order adds (2 for the two-matrix
+          // gate/up, whose 4-slot batch would push the kernel past its register
+          // budget into spills)
           constexpr int VN = NMAT * NT * 4;
+          constexpr int UB = VN >= 16 ? 2 : 4;
           const int n_slots = p.S * pieces;
           const int my_slot_idx = seg * pieces + my_j;
-          for (int base = 0; base < n_slots; base += 4) {
-            float buf[4][VN];
+          for (int base = 0; base < n_slots; base += UB) {
+            float buf[UB][VN];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < UB; ++u) {
               const int sj = base + u;
               if (sj < n_slots && sj != my_slot_idx) {
                 const int ss = sj / pieces, jj = sj - ss * pieces;
@@ -560,7 +563,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
               }
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < UB; ++u) {
               const int sj = base + u;
               if (sj < n_slots) {
 #pragma unroll
