@@ -313,6 +313,82 @@ def measure_prefill(args, torch, weights):
             "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
 
 
+def measure_sharded_extras(args, torch, ws, rank, peak):
+    """At N > 1: the MoE verify layer expert parallel and the prefill FFN tensor
+    parallel over all ranks (ShardedMoeVerifyStep / ShardedPrefillFFN, one NCCL
+    all-reduce each), CUDA-graph replays timed with CUDA events on every rank, the
+    max over ranks reported.  Every rank runs this, in the same order."""
+    import torch.distributed as dist
+    from thunderllamax_b200 import synth
+    from thunderllamax_b200.dist import ShardedMoeVerifyStep, ShardedPrefillFFN
+    from thunderllamax_b200.moe import MoeShape
+    from thunderllamax_b200.prefill import PrefillShape
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    out = {}
+    if not args.no_moe:
+        shape = MoeShape()
+        step = ShardedMoeVerifyStep(shape, rank, ws, seed=0)
+        rng = np.random.default_rng(4321)
+        bits = synth.bf16_normal(rng, (shape.positions, shape.hidden))
+        hres = rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32)
+        step.set_inputs(torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda(),
+                        torch.from_numpy(hres).cuda())
+        step.capture()
+        for _ in range(5):
+            step.replay()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(time_graph(step.replay, max(20, min(2000, args.steps)), torch))
+        touched = sum_over_ranks(step.touched_bytes())
+        out["moe_verify"] = {"workload": f"MoE verify layer, expert parallel over {ws} GPUs "
+                                         f"({shape.experts // ws} experts per rank), router replicated, "
+                                         "one NCCL all-reduce of the fp32 partials",
+                             "us_per_step": round(ms * 1000, 2), "bytes_per_step": int(touched),
+                             "gbs": round(touched / (ms * 1e-3) / 1e9, 1),
+                             "frac_of_peak": round(touched / (ms * 1e-3) / 1e9 / (peak * ws), 4),
+                             "timing": "CUDA graph replay, max over ranks", "err_word": step.local.ws.error()}
+        step.release()
+        del step
+    if not args.no_prefill:
+        shape = PrefillShape()
+        step = ShardedPrefillFFN(shape, rank, ws, seed=0)
+        rng = np.random.default_rng(777)
+        step.set_inputs(torch.from_numpy(synth.bf16_normal(rng, (shape.tokens, shape.dim)).view(np.int16))
+                        .view(torch.bfloat16).cuda())
+        step.capture()
+        for _ in range(3):
+            step.replay()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(time_graph(step.replay, 20, torch))
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                bf16_peak, kind = float(json.load(f)["bf16_tflops"]), "measured cuBLAS bf16 burst"
+        except Exception:
+            bf16_peak, kind = 1590.0, "fallback"
+        tflops = shape.flops() / (ms * 1e-3) / 1e12
+        out["prefill_ffn"] = {"workload": f"prefill FFN 2048 tokens, tensor parallel over {ws} GPUs (gate/up rows, "
+                                          "down k), one NCCL all-reduce of the 2048 x 5120 fp32 partials",
+                              "ms_per_step": round(ms, 4), "flops_per_step": shape.flops(),
+                              "tflops": round(tflops, 1), "peak_tflops": bf16_peak * ws, "peak_kind": kind + " x N",
+                              "frac_of_peak": round(tflops / (bf16_peak * ws), 4),
+                              "timing": "CUDA graph replay, max over ranks",
+                              "err_word": [step.ws.error(), step.ws_down.error()]}
+        step.release()
+        del step
+    return out
+
+
 def _timed_cold(launch, n, torch):
     """Mean device time (ms) of `launch` with L2 flushed before each call (a 256 MB
     read outside the timed events, leaving clean lines): for working sets that would
@@ -622,6 +698,9 @@ def run_ours(args):
         extras["gdn_qkv"] = measure_gdn_qkv(args, torch, peak)
         extras["o_proj"] = measure_o_proj(args, torch, peak)
         extras["lookup11"] = measure_lookup(args, torch, peak)
+    if ws > 1:
+        step.release()
+        extras.update(measure_sharded_extras(args, torch, ws, rank, peak))
     clocks = clk.summary()
     if rank == 0:
         emit({"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,

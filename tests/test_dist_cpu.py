@@ -104,3 +104,91 @@ def test_two_rank_sharded_step_equals_unsharded_oracle():
         assert p_.exitcode == 0
     assert err < 1e-12
     assert idx == idx_ref
+
+
+def _spawn(target, world=2, timeout=240):
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.path.join(here, "golden"),
+                                                os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p_ in procs:
+        p_.start()
+    out = []
+    try:
+        for _ in range(world):
+            out.append(q.get(timeout=timeout))
+    finally:
+        for p_ in procs:
+            p_.join(timeout=60)
+    assert all(p_.exitcode == 0 for p_ in procs)
+    return out
+
+
+def _moe_worker(rank, world, port, q):
+    # expert parallel: this rank's routed experts (+ shared and residual on rank 0),
+    # summed by the all-reduce, equal the whole layer
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        E, H, I, P = 16, 256, 256, 3
+        Wr = rng.normal(0, 0.05, (E, H)).astype(np.float32)
+        wsh = rng.normal(0, 0.05, H).astype(np.float32)
+        gate = synth.iq4xs_blocks(rng, E * I, H).reshape(E, I, -1)
+        up = synth.iq4xs_blocks(rng, E * I, H).reshape(E, I, -1)
+        down = synth.iq4xs_blocks(rng, E * H, I).reshape(E, H, -1)
+        sg_, su_, sd_ = synth.iq4xs_blocks(rng, I, H), synth.iq4xs_blocks(rng, I, H), synth.iq4xs_blocks(rng, H, I)
+        h = rng.standard_normal((P, H))
+        hres = rng.standard_normal((P, H))
+        full = oracle.moe_verify_f64(h, Wr, wsh, gate, up, down, sg_, su_, sd_, hres=hres)
+        e0, e1 = tdist.expert_ranges(E, world)[rank]
+        part = np.zeros((P, H))
+        for p in range(P):
+            for r in range(8):
+                if e0 <= full["ids"][p, r] < e1:
+                    part[p] += full["gates"][p, r] * full["parts"][p, r]
+        if rank == 0:
+            shared = full["y"] - hres - np.einsum("pr,prh->ph", full["gates"], full["parts"])
+            part += shared + hres
+        y = torch.from_numpy(part)
+        tdist.allreduce_partial(y)
+        q.put((rank, float(np.abs(y.numpy() - full["y"]).max() / np.abs(full["y"]).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_expert_parallel_moe_equals_layer():
+    for rank, err in _spawn(_moe_worker):
+        assert err < 1e-12, (rank, err)
+
+
+def _prefill_worker(rank, world, port, q):
+    # tensor parallel prefill FFN: gate/up rows and down k split by 256-row blocks
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(12)
+        T, H, F = 5, 256, 1024
+        rg, ru = synth.iq3xxs_blocks(rng, F, H), synth.iq3xxs_blocks(rng, F, H)
+        rd = synth.q6k_blocks(rng, H, F)
+        x = synth.bf16_bits_to_f32(synth.bf16_normal(rng, (T, H))).astype(np.float64)
+        b0, b1 = tdist.block_ranges(F // 256, world)[rank]
+        f0, f1 = 256 * b0, 256 * b1
+        g = oracle.matvec_f64(oracle.dequant_iq3xxs(tdist.shard_gguf_rows(rg, f0, f1), H), x)
+        u = oracle.matvec_f64(oracle.dequant_iq3xxs(tdist.shard_gguf_rows(ru, f0, f1), H), x)
+        wd = oracle.dequant_q6k(tdist.shard_gguf_cols(rd, f0, f1, 210), f1 - f0)
+        y = torch.from_numpy(oracle.matvec_f64(wd, oracle.silu_f64(g) * u))
+        tdist.allreduce_partial(y)
+        _, y_ref = oracle.ffn_f64(x, rg, ru, rd)
+        q.put((rank, float(np.abs(y.numpy() - y_ref).max() / np.abs(y_ref).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_tensor_parallel_prefill_equals_ffn():
+    for rank, err in _spawn(_prefill_worker):
+        assert err < 1e-12, (rank, err)

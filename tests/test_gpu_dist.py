@@ -97,3 +97,109 @@ def test_sharded_verify_step_two_gpus():
         assert err <= 2e-3 and err <= 1e-4, (rank, err)
         assert idx == idx_ref, rank
         assert acc == acc_ref, rank
+
+
+def _spawn_gpu(target, world=2):
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.path.join(here, "golden"),
+                                                os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p_ in procs:
+        p_.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=300))
+    finally:
+        for p_ in procs:
+            p_.join(timeout=60)
+    assert all(p_.exitcode == 0 for p_ in procs)
+    return results
+
+
+def _init(rank, world, port):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    return dist
+
+
+def _moe_rank(rank, world, port, q):
+    dist = _init(rank, world, port)
+    try:
+        import oracle
+        from thunderllamax_b200 import dist as tdist
+        from thunderllamax_b200 import moe, synth
+        shape = moe.MoeShape(positions=5, experts=32, hidden=1024, inner=512)
+        host = moe.synth_host(shape, seed=21)
+        step = tdist.ShardedMoeVerifyStep(shape, rank, world, host=host)
+        rng = np.random.default_rng(22)
+        bits = synth.bf16_normal(rng, (shape.positions, shape.hidden))
+        hres = rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32)
+        step.set_inputs(torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16),
+                        torch.from_numpy(hres).cuda())
+        step.capture()
+        for _ in range(3):
+            step.replay()
+        torch.cuda.synchronize()
+        h64 = synth.bf16_bits_to_f32(bits).astype(np.float64)
+        ref = oracle.moe_verify_f64(h64, host["wr"], host["wsh"], host["gate"], host["up"], host["down"],
+                                    host["sgate"], host["sup"], host["sdown"], hres=hres)
+        y = step.y.cpu().numpy().astype(np.float64)
+        err = float((np.abs(y - ref["y"]).max(axis=1) / np.linalg.norm(ref["y"], axis=1)).max())
+        step.release()
+        q.put((rank, err, step.local.ws.error()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_moe_two_gpus():
+    for rank, err, werr in _spawn_gpu(_moe_rank):
+        assert err <= 2e-3 and err <= 2e-4, (rank, err)
+        assert werr == 0
+
+
+def _prefill_rank(rank, world, port, q):
+    dist = _init(rank, world, port)
+    try:
+        import oracle
+        from thunderllamax_b200 import dist as tdist
+        from thunderllamax_b200 import ops, synth
+        from thunderllamax_b200.prefill import PrefillShape
+        s = PrefillShape(tokens=300, dim=1024, ffn=2048)
+        rng = np.random.default_rng(23)
+        rg, ru = synth.iq3xxs_blocks(rng, s.ffn, s.dim), synth.iq3xxs_blocks(rng, s.ffn, s.dim)
+        rd = synth.q6k_blocks(rng, s.dim, s.ffn)
+        b0, b1 = tdist.block_ranges(s.ffn // 256, world)[rank]
+        f0, f1 = 256 * b0, 256 * b1
+        w = {"gate": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(rg, f0, f1), s.dim),
+             "up": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(ru, f0, f1), s.dim),
+             "down": ops.pack_tiles("q6_k", tdist.shard_gguf_cols(rd, f0, f1, 210), f1 - f0)}
+        step = tdist.ShardedPrefillFFN(s, rank, world, weights=w)
+        xb = synth.bf16_normal(rng, (s.tokens, s.dim))
+        step.set_inputs(torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16))
+        step.capture()
+        step.replay()
+        torch.cuda.synchronize()
+        _, y_ref = oracle.ffn_f64(synth.bf16_bits_to_f32(xb).astype(np.float64), rg, ru, rd)
+        y = step.y.cpu().numpy().astype(np.float64)
+        err = float((np.abs(y - y_ref).max(axis=1) / np.linalg.norm(y_ref, axis=1)).max())
+        step.release()
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_prefill_two_gpus():
+    for rank, err in _spawn_gpu(_prefill_rank):
+        assert err <= 2e-3 and err <= 1e-3, (rank, err)

@@ -11,6 +11,20 @@ The reference is single-GPU (README.md:412-413); this is the B200 node layout:
   [world][11] keys and every rank merges them and runs greedy accept
   (deterministic, identical on all ranks).
 
+The MoE verify layer (config 4) and the prefill FFN (config 5) shard the same way:
+
+* MoE: expert parallel.  The router is replicated (every rank computes the same
+  top-8); rank r runs only the routed experts of its contiguous range
+  [e0, e1) and rank 0 also the shared expert and the residual; ONE all-reduce of
+  the [positions][hidden] fp32 partials gives the layer.  Token dispatch moves no
+  data: the verify step's positions are replicated on every rank.
+* Prefill FFN: tensor parallel.  gate/up split by whole 256-row blocks, down by
+  the matching k range; each rank's tcgen05 down GEMM writes a partial
+  [tokens][dim] fp32 sum, added by ONE all-reduce.
+
+The summation order of an all-reduce differs from the single-GPU combine, so
+sharded results agree with the one-GPU path to fp32 rounding, not bit for bit.
+
 Collectives go through ``torch.distributed`` (NCCL on GPUs; gloo in the CPU
 tests of the host-side plumbing) and are captured in the step's CUDA graph.
 No data path uses TMA multicast or peer memory.
@@ -178,3 +192,107 @@ def shard_gguf_rows(raw: np.ndarray, r0: int, r1: int) -> np.ndarray:
 def shard_gguf_cols(raw: np.ndarray, k0: int, k1: int, block_bytes: int) -> np.ndarray:
     """Columns [k0, k1) (multiples of 256) of a GGUF matrix (k split: down)."""
     return np.ascontiguousarray(raw[:, (k0 // 256) * block_bytes:(k1 // 256) * block_bytes])
+
+
+class _GraphStep:
+    """Capture / replay / release of one rank's step as a CUDA graph (the graph holds
+    NCCL work, so release it before the process group is destroyed)."""
+
+    graph = None
+
+    def capture(self):
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                self.launch()
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.launch()
+        self.graph = g
+        return g
+
+    def replay(self):
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+
+    def release(self):
+        self.graph = None
+        torch.cuda.synchronize()
+
+
+def expert_ranges(n_experts: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous expert ranges per rank (32 of 256 per rank at 8 ranks)."""
+    return block_ranges(n_experts, world)
+
+
+class ShardedMoeVerifyStep(_GraphStep):
+    """The MoE verify layer, expert parallel: this rank's experts, then one
+    all-reduce of the partial layer output."""
+
+    def __init__(self, shape=None, rank: int = 0, world: int = 1, seed: int = 0, host: dict | None = None,
+                 group=None):
+        from .moe import MoeShape, MoeVerifyStep, synth_host
+
+        shape = shape if shape is not None else MoeShape()
+        self.shape, self.rank, self.world, self.group = shape, rank, world, group
+        self.e0, self.e1 = expert_ranges(shape.experts, world)[rank]
+        host = host if host is not None else synth_host(shape, seed)
+        self.local = MoeVerifyStep(shape, host=host, e0=self.e0, e1=self.e1, shared=(rank == 0))
+        self.y = self.local.y
+
+    def launch(self):
+        self.local.launch()
+        allreduce_partial(self.y, self.group)
+
+    def set_inputs(self, h, hres=None):
+        self.local.set_inputs(h, hres if self.rank == 0 else None)
+
+    def touched_bytes(self) -> int:
+        return self.local.touched_bytes()
+
+
+class ShardedPrefillFFN(_GraphStep):
+    """The prefill FFN, tensor parallel: this rank's gate/up rows and down k range,
+    then one all-reduce of the partial [tokens][dim] output."""
+
+    def __init__(self, shape=None, rank: int = 0, world: int = 1, seed: int = 0, weights: dict | None = None,
+                 group=None):
+        from .prefill import PrefillShape, PrefillWorkspace
+
+        ops.require_device()
+        s = self.shape = shape if shape is not None else PrefillShape()
+        self.rank, self.world, self.group = rank, world, group
+        b0, b1 = block_ranges(s.ffn // 256, world)[rank]
+        self.f0, self.f1 = 256 * b0, 256 * b1
+        self.n_ffn = self.f1 - self.f0
+        if self.n_ffn <= 0:
+            raise ValueError(f"rank {rank} of {world} has an empty FFN shard")
+        if weights is None:
+            weights = {"gate": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 1),
+                       "up": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 2),
+                       "down": synth_tiled(s.down_q, s.dim, self.n_ffn, seed * 1000 + 10 * rank + 3)}
+        self.w = weights
+        self.x = torch.zeros((s.tokens, s.dim), dtype=torch.bfloat16, device="cuda")
+        self.act = torch.empty((s.tokens, self.n_ffn), dtype=torch.float16, device="cuda")
+        self.y = torch.empty((s.tokens, s.dim), dtype=torch.float32, device="cuda")
+        self.ws = PrefillWorkspace(s.tokens, s.dim)
+        self.ws_down = PrefillWorkspace(s.tokens, self.n_ffn)
+
+    def flops_per_rank(self) -> int:
+        s = self.shape
+        return 2 * s.tokens * s.dim * self.n_ffn * 3
+
+    def launch(self):
+        from .prefill import gate_up, gemm
+
+        s = self.shape
+        gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, self.n_ffn, self.ws, act=self.act)
+        gemm(s.down_q, self.w["down"], self.act, s.dim, self.ws_down, y=self.y)
+        allreduce_partial(self.y, self.group)
+
+    def set_inputs(self, x):
+        self.x.copy_(x, non_blocking=True)
