@@ -248,6 +248,33 @@ size_t tlx_lookup_workspace_bytes(void);
 int tlx_lookup(const int32_t* tok_hist, int64_t hist_len, const int32_t* pos_slot, const int32_t* cyc_slot,
                int32_t* drafts, int n_drafts, int scan_end, int32_t* l_hist, void* ws, size_t ws_bytes, void* stream);
 
+/* Split-KV int8 attention of the full-attention layers over `rows` verify rows
+ * (engine/spk_preqh.cu:13-90, engine/spk_g4hm.cu, engine/skv_split.cu:176-199):
+ * 24 query heads, 4 KV heads, head dim 256, rotary on dims 0..63.  The cache is
+ * kv [8][ctx][256] bytes (int8 q + 128; heads 0..3 K, 4..7 V) with scales
+ * sc [8][ctx][8] fp16 (one per 32 dims); pos = pos_slot[0] on the device.
+ * tlx_attn_pre: qrow [rows][12288] fp16 (per head 256 q then 256 gate values),
+ *   krow / vrow [rows][1024] fp16, qnw / knw [256] fp32 norm weights, freqs [32]
+ *   fp32 rotary frequencies -> qw16 [rows][24][256] fp16 (normed, rotated, x 1/16)
+ *   and the rows' K / V appended to the cache at pos .. pos + rows - 1 (positions
+ *   outside [0, ctx) are not written).  Replaces spk_pre11 (its fp32 qw output is
+ *   not produced; the attention reads qw16).
+ * tlx_attn_split: per KV head and key range, online-softmax partials of the causal
+ *   attention (row t sees keys 0 .. pos + t) into the workspace (spk_a11).
+ * tlx_attn_combine: merge the partials, times sigmoid(gate), into ao [rows][6144]
+ *   fp16 (spk_c11).  tlx_attn_decode = split + combine.
+ * rows <= 16.  Workspace: tlx_attn_workspace_bytes(rows), 16-byte aligned; needs no
+ * zeroing. */
+size_t tlx_attn_workspace_bytes(int rows);
+int tlx_attn_pre(const void* qrow, const void* krow, const void* vrow, const float* qnw, const float* knw,
+                 const float* freqs, const int32_t* pos_slot, int rows, int64_t ctx, void* kv, void* sc, void* qw16,
+                 void* stream);
+int tlx_attn_split(const void* kv, const void* sc, const void* qw16, const int32_t* pos_slot, int rows, int64_t ctx,
+                   void* ws, size_t ws_bytes, void* stream);
+int tlx_attn_combine(const void* ws, size_t ws_bytes, const void* qrow, int rows, void* ao, void* stream);
+int tlx_attn_decode(const void* kv, const void* sc, const void* qw16, const void* qrow, const int32_t* pos_slot,
+                    int rows, int64_t ctx, void* ao, void* ws, size_t ws_bytes, void* stream);
+
 /* acceptsel11k: commit the accepted GDN state (engine/acceptsel11k.cu:8-40).
  * rec4 is [n_blocks][5][rec_elems] fp32 and conv4 [n_blocks][5][conv_elems] fp32,
  * slot 4 the live one; with m = m_slot[0] (device int, 0..10):

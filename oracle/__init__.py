@@ -24,3 +24,4 @@ from .path import (  # noqa: F401
     matvec_f64, ffn_f64, head_logits_f64, argmax_rows, h_argmax, acceptsel11k, lookup_ngram, head_argmax, accept, accept11k,
     router_top8, moe_verify_f64, silu_f64, min_top2_gap,
 )
+from .attention import attn_pre, attn_decode, rope_freqs, dequant_cache  # noqa: F401,E402

@@ -33,6 +33,33 @@ KERNELS = [(f"lookup{n}_nw32.cu", f"lookup{n}_nw32") for n in range(5, 12)] + [
     ("amx3.cu", "amx3"),
     ("mm/MM_P7_acc36.cu", "acc36"),
 ]
+# the ROWS = 11 split-KV attention set, with the compile-time shapes the reference
+# builds it with (engine/build_k11.py: CTXK = 100352, S = 256 chunks of 392 keys,
+# TILE 32, 32 warps); the kernels read and write only inside [8][CTXK] caches and
+# [4][S][66] partials, which the tests allocate at exactly these sizes
+ATTN_CTX, ATTN_S = 100352, 256
+ATTN_KERNELS = [
+    ("spk_preqh.cu", "spk_pre11", ["-DKPRE=spk_pre11", f"-DCTXK={ATTN_CTX}", "-DROWS=11"]),
+    ("spk_g4hm.cu", "spk_a11", ["-DKNAME=spk_a11", f"-DCTXK={ATTN_CTX}", "-DROWS=11", f"-DS={ATTN_S}",
+                                f"-DCH={ATTN_CTX // ATTN_S}", "-DTILE=32", "-DNW=32"]),
+    ("skv_split.cu:K2S", "spk_c11", ["-DK2S=spk_c11", f"-DCTXK={ATTN_CTX}", "-DROWS=11", f"-DS={ATTN_S}",
+                                 f"-DCH={ATTN_CTX // ATTN_S}", "-DUNROLL=4"]),
+]
+
+
+def _one_kernel(src: str, macro: str, out: str) -> str:
+    """The file's preamble plus the one kernel whose name is `macro` (what the
+    reference's own build does for its multi-kernel files, engine/build_k11.py
+    split_skv), written as a build input under oracle/_ref."""
+    text = open(src).read()
+    head = 'extern "C" __global__'
+    first = text.find(head)
+    bodies = text[first:].split(head)[1:]
+    body = [b for b in bodies if f") {macro}(" in b.split("\n", 1)[0]]
+    assert len(body) == 1, (src, macro)
+    with open(out, "w") as f:
+        f.write(text[:first] + head + body[0].rstrip() + "\n")
+    return out
 
 
 def build(verbose: bool = False) -> list[str]:
@@ -42,15 +69,19 @@ def build(verbose: bool = False) -> list[str]:
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     os.makedirs(OUT, exist_ok=True)
     built = []
-    for rel, name in KERNELS:
-        src = os.path.join(src_dir, rel)
+    for rel, name, defs in [(r, n, []) for r, n in KERNELS] + ATTN_KERNELS:
+        src = os.path.join(src_dir, rel.split(":")[0])
         if not os.path.exists(src):
             continue
+        if ":" in rel:
+            src = _one_kernel(src, rel.split(":")[1], os.path.join(OUT, name + ".cu"))
         out = os.path.join(OUT, name + ".cubin")
-        cmd = [nvcc, "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-o", out, src]
+        cmd = [nvcc, "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", *defs, "-o", out, src]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+        if ":" in rel:
+            os.remove(src)   # the extracted input is not kept
         built.append(out)
     return built
 

@@ -54,6 +54,11 @@ _SIGS = {
     "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
     "tlx_h_argmax": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "tlx_acceptsel11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "tlx_attn_workspace_bytes": (c_size, [c_int]),
+    "tlx_attn_pre": (c_int, [c_vp] * 7 + [c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "tlx_attn_split": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp, c_size, c_vp]),
+    "tlx_attn_combine": (c_int, [c_vp, c_size, c_vp, c_int, c_vp, c_vp]),
+    "tlx_attn_decode": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp, c_vp, c_size, c_vp]),
     "tlx_lookup_workspace_bytes": (c_size, []),
     "tlx_lookup": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_size, c_vp]),
     "tlx_q5g8v11_workspace_bytes": (c_size, [c_int, c_i64, c_i64, c_i64, c_int]),

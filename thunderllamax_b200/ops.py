@@ -341,6 +341,55 @@ class Lookup:
                                     _stream(tok_hist)), "lookup")
 
 
+class Attention:
+    """Split-KV int8 attention of the full-attention layers for `rows` verify rows
+    (tlx_attn_pre / tlx_attn_split / tlx_attn_combine): the int8 KV cache
+    kv [8][ctx][256] uint8 with scales sc [8][ctx][8] fp16, pos on the device."""
+
+    HEADS, KV_HEADS, HEAD_DIM = 24, 4, 256
+
+    def __init__(self, rows: int, ctx: int, device="cuda"):
+        self.rows, self.ctx = int(rows), int(ctx)
+        nb = int(_lib.lib().tlx_attn_workspace_bytes(self.rows))
+        if nb == 0:
+            raise TLXError(f"unsupported attention rows={rows}")
+        self.ws = Workspace(nb, device)
+
+    def new_cache(self, device="cuda"):
+        kv = torch.full((8, self.ctx, 256), 128, dtype=torch.uint8, device=device)
+        sc = torch.zeros((8, self.ctx, 8), dtype=torch.float16, device=device)
+        return kv, sc
+
+    def pre(self, qrow, krow, vrow, qnw, knw, freqs, pos_slot, kv, sc, qw16=None):
+        require_device()
+        if qw16 is None:
+            qw16 = torch.empty((self.rows, self.HEADS, 256), dtype=torch.float16, device=qrow.device)
+        check(_lib.lib().tlx_attn_pre(_ptr(qrow), _ptr(krow), _ptr(vrow), _ptr(qnw), _ptr(knw), _ptr(freqs),
+                                      _ptr(pos_slot), self.rows, self.ctx, _ptr(kv), _ptr(sc), _ptr(qw16),
+                                      _stream(qrow)), "attn_pre")
+        return qw16
+
+    def split(self, kv, sc, qw16, pos_slot):
+        check(_lib.lib().tlx_attn_split(_ptr(kv), _ptr(sc), _ptr(qw16), _ptr(pos_slot), self.rows, self.ctx,
+                                        _ptr(self.ws.buf), self.ws.nbytes, _stream(kv)), "attn_split")
+
+    def combine(self, qrow, ao=None):
+        if ao is None:
+            ao = torch.empty((self.rows, self.HEADS * 256), dtype=torch.float16, device=qrow.device)
+        check(_lib.lib().tlx_attn_combine(_ptr(self.ws.buf), self.ws.nbytes, _ptr(qrow), self.rows, _ptr(ao),
+                                          _stream(qrow)), "attn_combine")
+        return ao
+
+    def decode(self, kv, sc, qw16, qrow, pos_slot, ao=None):
+        require_device()
+        if ao is None:
+            ao = torch.empty((self.rows, self.HEADS * 256), dtype=torch.float16, device=qrow.device)
+        check(_lib.lib().tlx_attn_decode(_ptr(kv), _ptr(sc), _ptr(qw16), _ptr(qrow), _ptr(pos_slot), self.rows,
+                                         self.ctx, _ptr(ao), _ptr(self.ws.buf), self.ws.nbytes, _stream(kv)),
+              "attn_decode")
+        return ao
+
+
 GDN_BLOCKS, GDN_REC, GDN_CONV = 48, 786432, 30720  # engine/acceptsel11k.cu:22-38
 
 
@@ -388,5 +437,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "Lookup", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "Lookup", "Attention", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
