@@ -547,6 +547,49 @@ def measure_lookup(args, torch, peak):
                              "sample": "the numpy oracle on the same history"}}
 
 
+def measure_attention(args, torch, peak):
+    """Split-KV int8 attention of one full-attention layer for the 11 verify rows at
+    32K and 100K tokens of context (spk_pre11 + spk_a11 + spk_c11 as tlx_attn_pre +
+    tlx_attn_split + tlx_attn_combine), 10 layers per CUDA graph replay.  Bytes =
+    the K / V cache rows and scales read."""
+    from thunderllamax_b200 import ops
+    import oracle
+
+    rows, ctx = 11, 100352
+    rng = np.random.default_rng(48)
+    q = torch.from_numpy(rng.standard_normal((rows, 12288)).astype(np.float16)).cuda()
+    k = torch.from_numpy(rng.standard_normal((rows, 1024)).astype(np.float16)).cuda()
+    v = torch.from_numpy(rng.standard_normal((rows, 1024)).astype(np.float16)).cuda()
+    qn, kn = torch.ones(256, device="cuda"), torch.ones(256, device="cuda")
+    fr = torch.from_numpy(oracle.rope_freqs()).cuda()
+    kv = torch.randint(1, 256, (8, ctx, 256), dtype=torch.uint8, device="cuda")
+    sc = (torch.rand((8, ctx, 8), device="cuda") * 0.02 + 0.01).half()
+    at = ops.Attention(rows, ctx)
+    out = {"workload": "full-attention layer, 11 verify rows, 24 q / 4 KV heads x 256, int8 KV cache",
+           "graph": "CUDA graph replay, 10 layers per replay"}
+    for pos in (32000, 100000):
+        pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        qw16 = torch.empty((rows, 24, 256), dtype=torch.float16, device="cuda")
+        ao = torch.empty((rows, 6144), dtype=torch.float16, device="cuda")
+
+        def layer():
+            at.pre(q, k, v, qn, kn, fr, pos_t, kv, sc, qw16)
+            at.decode(kv, sc, qw16, q, pos_t, ao)
+        layer()
+
+        def ten():
+            for _ in range(10):
+                layer()
+        graph = _graph_of(ten, torch)
+        ms = time_graph(graph.replay, 5, torch) / 10
+        nbytes = 8 * (pos + rows) * (256 + 16)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[f"ctx_{pos}"] = {"us_per_layer": round(ms * 1000, 2), "kv_bytes": nbytes, "gbs": round(gbs, 1),
+                             "frac_of_peak": round(gbs / peak, 4), "launches_per_layer": 3}
+        del graph
+    return out
+
+
 def measure_acceptsel(args, torch, peak):
     """acceptsel11k at the reference size (48 GDN blocks x (786432 + 30720) fp32, m = 7):
     bytes = the slot read + the live slot written."""
@@ -698,6 +741,7 @@ def run_ours(args):
         extras["gdn_qkv"] = measure_gdn_qkv(args, torch, peak)
         extras["o_proj"] = measure_o_proj(args, torch, peak)
         extras["lookup11"] = measure_lookup(args, torch, peak)
+        extras["attention"] = measure_attention(args, torch, peak)
     if ws > 1:
         step.release()
         extras.update(measure_sharded_extras(args, torch, ws, rank, peak))

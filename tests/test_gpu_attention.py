@@ -157,3 +157,29 @@ def test_attention_rejects_bad_arguments():
     rc = lib.tlx_attn_decode(kv.data_ptr(), sc.data_ptr(), x.data_ptr(), x.data_ptr(), pos.data_ptr(), 0, 256,
                              x.data_ptr(), at.ws.buf.data_ptr(), at.ws.nbytes, None)
     assert rc == -1      # TLX_ERR_SHAPE
+
+
+def test_engine0_spk_programs():
+    # the reference-named programs with the reference's argument lists
+    from thunderllamax_b200 import engine0
+    rows, ctx, pos = 11, 1024, 300
+    rng = np.random.default_rng(9)
+    qrow, krow, vrow, qnw, knw = inputs(rng, rows)
+    kv, sc = random_cache(rng, ctx, pos)
+    q_t, k_t, v_t, qn_t, kn_t, fr_t = dev(qrow, krow, vrow, qnw, knw, oracle.rope_freqs())
+    pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    progs = engine0.load_progs(rows=rows, vocab=4096)
+    kv_p, sc_p = dev(kv, sc)
+    qw = torch.zeros((rows, 24, 256), dtype=torch.float32, device="cuda")
+    qw16 = torch.zeros((rows, 24, 256), dtype=torch.float16, device="cuda")
+    R = 6 * rows
+    pm, ps = (torch.zeros(4 * 256 * R, device="cuda") for _ in range(2))
+    pa = torch.zeros(16, device="cuda")
+    ao = torch.zeros(rows * 6144, dtype=torch.float16, device="cuda")
+    progs["spk_pre11"](q_t, k_t, v_t, qn_t, kn_t, fr_t, kv_p, sc_p, pos_t, qw, qw16, global_size=24)
+    progs["spk_a11"](kv_p, sc_p, qw16, pos_t, pm, ps, pa)
+    progs["spk_c11"](pm, ps, pa, q_t, ao)
+    _, kv_l, sc_l, ao_l = run_lib(rows, ctx, qrow, krow, vrow, qnw, knw, kv, sc, pos)
+    torch.cuda.synchronize()
+    assert np.array_equal(kv_p.cpu().numpy(), kv_l)
+    assert np.array_equal(ao.view(rows, 6144).cpu().numpy().view(np.int16), ao_l.view(np.int16))

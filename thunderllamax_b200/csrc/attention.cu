@@ -122,7 +122,10 @@ constexpr uint32_t kOffK = 0;
 constexpr uint32_t kOffV = kOffK + kTile * 512;
 constexpr uint32_t kOffQ = kOffV + kTile * 512;
 constexpr uint32_t kOffS = kOffQ + kMaxR * 512;
-constexpr uint32_t kOffP = kOffS + kMaxR * kTile * 4;
+// score rows are kSStride floats apart: the fragment writes (rows 2q, keys g) and
+// the softmax reads (8 rows per 16-byte phase) then fall on distinct banks
+constexpr int kSStride = kTile + 4;
+constexpr uint32_t kOffP = kOffS + kMaxR * kSStride * 4;
 constexpr uint32_t kOffCor = kOffP + kMaxR * kTile * 2;
 constexpr uint32_t kSplitSmem = kOffCor + kMaxR * 4;
 
@@ -213,8 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_split_kernel(const SplitArgs
     *reinterpret_cast<uint4*>(sm + kOffQ + sw32(r, c)) = v;
   }
 
-  // row owner state: 4 threads per row (tid >> 2), 16 keys each
-  const int orow = tid >> 2, osub = tid & 3;
+  // row owner state: 4 threads per row, lanes l, l ^ 8, l ^ 16, l ^ 24 of a warp
+  // (8 rows per warp), keys osub * 4 + 16 j + 0..3
+  const int orow = (tid & 7) + 8 * (tid >> 5), osub = (tid >> 3) & 3;
   const bool owner = orow < R;
   const int ot = owner ? orow % T : 0;
   float m_run = -1e30f, l_run = 0.f;
@@ -280,28 +284,33 @@ __global__ void __launch_bounds__(kThreads, 1) attn_split_kernel(const SplitArgs
       // c0 / c1: key mb*16 + g, rows nb*8 + 2q, +1; c2 / c3: key + 8
       float* S = reinterpret_cast<float*>(sm + kOffS);
       const int key = mb * 16 + (lane >> 2), row = nb * 8 + 2 * (lane & 3);
-      S[row * kTile + key] = c[0];
-      S[(row + 1) * kTile + key] = c[1];
-      S[row * kTile + key + 8] = c[2];
-      S[(row + 1) * kTile + key + 8] = c[3];
+      S[row * kSStride + key] = c[0];
+      S[(row + 1) * kSStride + key] = c[1];
+      S[row * kSStride + key + 8] = c[2];
+      S[(row + 1) * kSStride + key + 8] = c[3];
     }
     __syncthreads();
 
     // ---- online softmax per row (4 threads x 16 keys) ----
     if (orow < NB * 8) {
       const float* S = reinterpret_cast<const float*>(sm + kOffS);
-      const int64_t kbase = tile * kTile + osub * 16;
       const int64_t lim = std::min<int64_t>(total, static_cast<int64_t>(pos) + ot + 1);   // keys < lim
       float s[16];
       float mx = -1e30f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const bool ok = owner && kbase + i < lim;
-        s[i] = ok ? S[orow * kTile + osub * 16 + i] : -1e30f;
-        mx = fmaxf(mx, s[i]);
+      for (int j = 0; j < 4; ++j) {
+        const int k0 = osub * 4 + 16 * j;
+        const float4 v = *reinterpret_cast<const float4*>(S + orow * kSStride + k0);
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool ok = owner && tile * kTile + k0 + i < lim;
+          s[4 * j + i] = ok ? vv[i] : -1e30f;
+          mx = fmaxf(mx, s[4 * j + i]);
+        }
       }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float mn = fmaxf(m_run, mx);
       const float cor = __expf(m_run - mn);
       float sum = 0.f;
@@ -314,12 +323,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_split_kernel(const SplitArgs
         const __half2 h = __floats2half2_rn(p0, p1);
         ph[i >> 1] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
       l_run = l_run * cor + sum;
       m_run = mn;
-      *reinterpret_cast<uint4*>(sm + kOffP + sw8(orow, 2 * osub)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-      *reinterpret_cast<uint4*>(sm + kOffP + sw8(orow, 2 * osub + 1)) = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)   // keys osub * 4 + 16 j .. + 3: half of chunk 2 j + osub / 2
+        *reinterpret_cast<uint2*>(sm + kOffP + sw8(orow, 2 * j + (osub >> 1)) + (osub & 1) * 8) =
+            make_uint2(ph[2 * j], ph[2 * j + 1]);
       if (osub == 0) reinterpret_cast<float*>(sm + kOffCor)[orow] = cor;
     }
     __syncthreads();

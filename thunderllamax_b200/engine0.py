@@ -190,6 +190,34 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
             lookups[k](tok_hist, pos_slot, cyc_slot, _contig_drafts(list(drings)), l_hist)
         return lookup
 
+    attn = {}   # rows -> the Attention whose workspace spk_a11 filled last
+
+    def _attn(rows, kv):
+        ctx = kv.numel() // (8 * 256)
+        key = (rows, ctx)
+        if attn.get("obj", {}).get(key) is None:
+            attn.setdefault("obj", {})[key] = ops.Attention(rows, ctx)
+        attn[rows] = attn["obj"][key]
+        return attn[rows]
+
+    def spk_pre11(qrow, krow, vrow, qnw, knw, freqs, kv, sc, pos_slot, qw, qw16):
+        # engine/spk_preqh.cu:13-90 (the fp32 qw output is not produced; spk_a11 reads qw16)
+        del qw
+        n = qrow.numel() // 12288
+        _attn(n, kv).pre(qrow, krow, vrow, qnw, knw, freqs, pos_slot, kv, sc, qw16)
+
+    def spk_a11(kv, sc, qw16, pos_slot, pm, ps, pA):
+        # engine/spk_g4hm.cu: partials go to the library's workspace, not pm / ps / pA
+        del pm, ps, pA
+        n = qw16.numel() // (24 * 256)
+        _attn(n, kv).split(kv, sc, qw16, pos_slot)
+
+    def spk_c11(pm, ps, pA, qrow, ao):
+        # engine/skv_split.cu:176-199: combine + sigmoid gate -> ao [rows][6144] fp16
+        del pm, ps, pA
+        n = qrow.numel() // 12288
+        attn[n].combine(qrow, ao.view(n, 6144))
+
     def acceptsel11k(rec4, conv4, m_slot, *scratch):
         # engine/acceptsel11k.cu:8-40: conv5x..conv11x then rec6x..rec11x, as the reference
         ops.acceptsel11k(rec4, conv4, m_slot, scratch[:7], scratch[7:13])
@@ -201,7 +229,7 @@ def load_progs(dim=5120, ffn=17408, vocab=151936, rows=11, ffn_q="iq3_xxs", down
     progs = {"ffn8v11": ffn8v11, "down8nw32_11": down8nw32_11, "head8v11": head8v11, "amx3": amx3,
              "head_argmax": head_argmax, "accept11k": accept11k, "acc36": acc36, "acceptsel11k": acceptsel11k,
              "h_argmax": h_argmax, "aq3k8v11": aq3k8v11, "q5g8v11": q5g8v11, "op38nw32_11": op38nw32_11,
-             "k3aonw32_11": k3aonw32_11}
+             "k3aonw32_11": k3aonw32_11, "spk_pre11": spk_pre11, "spk_a11": spk_a11, "spk_c11": spk_c11}
     for n in range(5, 12):
         progs[f"lookup{n}_nw32"] = make_lookup(n)
     return {k: Prog(k, v) for k, v in progs.items()}
