@@ -778,6 +778,27 @@ def run_ours(args):
     return 0
 
 
+def profile_attention(pos: int) -> int:
+    """A small driver for ncu: the attention split kernel alone at context `pos`
+    (11 rows, ctx 100352, random int8 cache and scales, qw16 N(0, 1) / 16)."""
+    import torch
+    from thunderllamax_b200 import ops
+
+    rows, ctx = 11, 100352
+    if not 0 <= pos <= ctx - rows:
+        raise SystemExit(f"--profile-attention POS must be in [0, {ctx - rows}]")
+    kv = torch.randint(1, 256, (8, ctx, 256), dtype=torch.uint8, device="cuda")
+    sc = (torch.rand((8, ctx, 8), device="cuda") * 0.02 + 0.01).half()
+    qw16 = (torch.randn((rows, 24, 256), device="cuda") / 16).half()
+    pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    at = ops.Attention(rows, ctx)
+    for _ in range(2):
+        at.split(kv, sc, qw16, pos_t)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_attention": pos, "ok": True}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -789,9 +810,13 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill contraction (config 5) measurement")
     ap.add_argument("--no-extras", action="store_true", help="skip the aq3k8v11 / acceptsel11k measurements")
     # smaller shapes for profiler captures only; the benchmark line uses the defaults
+    ap.add_argument("--profile-attention", type=int, default=None, metavar="POS",
+                    help="profiling case: one warm-up and one tlx_attn_split launch at context POS, then exit")
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
     args = ap.parse_args()
+    if args.profile_attention is not None:
+        return profile_attention(args.profile_attention)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
