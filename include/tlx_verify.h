@@ -263,8 +263,9 @@ int tlx_lookup(const int32_t* tok_hist, int64_t hist_len, const int32_t* pos_slo
  *   attention (row t sees keys 0 .. pos + t) into the workspace (spk_a11).
  * tlx_attn_combine: merge the partials, times sigmoid(gate), into ao [rows][6144]
  *   fp16 (spk_c11).  tlx_attn_decode = split + combine.
- * rows <= 16.  Workspace: tlx_attn_workspace_bytes(rows), 16-byte aligned; needs no
- * zeroing. */
+ * rows <= 16.  Workspace: tlx_attn_workspace_bytes(rows), 256-byte aligned, zeroed
+ * once (tlx_workspace_init); its first word holds the error bits of the split
+ * kernel's bounded waits (tlx_workspace_error). */
 size_t tlx_attn_workspace_bytes(int rows);
 int tlx_attn_pre(const void* qrow, const void* krow, const void* vrow, const float* qnw, const float* knw,
                  const float* freqs, const int32_t* pos_slot, int rows, int64_t ctx, void* kv, void* sc, void* qw16,

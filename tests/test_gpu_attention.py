@@ -65,6 +65,7 @@ def run_lib(rows, ctx, qrow, krow, vrow, qnw, knw, kv, sc, pos):
     ao = at.decode(kv_t, sc_t, qw16, q_t, pos_t)
     ao2 = at.decode(kv_t, sc_t, qw16, q_t, pos_t)
     torch.cuda.synchronize()
+    assert at.error() == 0
     assert torch.equal(ao, ao2)                     # deterministic
     return qw16.cpu().numpy(), kv_t.cpu().numpy(), sc_t.cpu().numpy(), ao.cpu().numpy()
 
@@ -134,6 +135,7 @@ def test_attention_vs_reference_kernels(pos):
     qw16_l = at.pre(q_t, k_t, v_t, qn_t, kn_t, fr_t, pos_t, kv_l, sc_l)
     ao_l = at.decode(kv_l, sc_l, qw16_l, q_t, pos_t)
     torch.cuda.synchronize()
+    assert at.error() == 0
     # the pre step follows the reference kernel's arithmetic: bit-exact
     assert torch.equal(qw16_l.view(torch.int16), qw16_r.view(torch.int16))
     assert torch.equal(kv_l, kv_r)

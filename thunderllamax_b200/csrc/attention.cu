@@ -11,22 +11,17 @@
 //                    The per-row sum of squares is reduced in the reference's order
 //                    (xor butterfly per warp, then over the 8 warp sums), so qw16 and
 //                    the cache bytes equal the reference kernel's.
-// attn_split_kernel  one CTA per (KV head, key range): the range [pos + T) / P is
-//                    walked in 64-key tiles; scores S^T = K . Q^T with the keys as the
-//                    mma M dimension and the 6 T query rows of the head group as N
-//                    (66 rows -> 9 n-blocks of 8, not 5 m-blocks of 16), online
-//                    softmax per row (causal: row t sees keys <= pos + t), O^T += V^T
-//                    . P^T with the 256 dims as M (one 16-dim block per warp).  K / V
-//                    are dequantised to fp16(q * scale) in shared memory (XOR-swizzled
-//                    16-byte chunks, ldmatrix), the next tile's bytes prefetched into
-//                    registers while the current one is computed.  Writes (max, sum,
-//                    unnormalised output) per row.
+// attn_tc_kernel     one CTA per (KV head, key range): the range of [0, pos + T) is
+//                    walked in 64-key tiles on tcgen05 (see below), online softmax
+//                    per query row (causal: row t sees keys <= pos + t); writes (max,
+//                    sum, unnormalised output) per row.
 // attn_combine_kernel one CTA per (head, token): merges the P partials of its row,
 //                    times sigmoid of the gate half of the head's q projection row,
 //                    fp16 out.
-#include "tlx_internal.h"
-
 #include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "tlx_internal.h"
 
 #include <algorithm>
 
@@ -38,8 +33,6 @@ constexpr int kQRow = 2 * kHd * kHeads;   // 12288: per head 256 q then 256 gate
 constexpr int kKRow = kHd * kKvHeads;     // 1024
 constexpr int kMaxRows = 16;              // verify rows T
 constexpr int kMaxR = kGroup * kMaxRows;  // 96 query rows per KV head
-constexpr int kMaxNB = kMaxR / 8;         // 12 n-blocks
-constexpr int kTile = 64;                 // keys per tile
 constexpr int kWarps = 16, kThreads = kWarps * 32;
 
 // ---------------------------------------------------------------- pre kernel
@@ -114,275 +107,411 @@ __global__ void __launch_bounds__(256) attn_pre_kernel(const __half* __restrict_
          sc + (static_cast<int64_t>(kKvHeads + g) * ctx + l) * 8);
 }
 
-// ---------------------------------------------------------------- split kernel
-// shared memory (bytes): K tile, V tile, Q rows (fp16, 32 chunks of 16 B per row,
-// chunk index XOR (row & 7)); S (fp32 [96][64]); P (fp16 [96][64], 8 chunks per row,
-// swizzled); per-row correction
-constexpr uint32_t kOffK = 0;
-constexpr uint32_t kOffV = kOffK + kTile * 512;
-constexpr uint32_t kOffQ = kOffV + kTile * 512;
-constexpr uint32_t kOffS = kOffQ + kMaxR * 512;
-// score rows are kSStride floats apart: the fragment writes (rows 2q, keys g) and
-// the softmax reads (8 rows per 16-byte phase) then fall on distinct banks
-constexpr int kSStride = kTile + 4;
-constexpr uint32_t kOffP = kOffS + kMaxR * kSStride * 4;
-constexpr uint32_t kOffCor = kOffP + kMaxR * kTile * 2;
-constexpr uint32_t kSplitSmem = kOffCor + kMaxR * 4;
+// ---------------------------------------------------------------- tcgen05 split kernel
+// One CTA (16 warps) per (KV head, key range), one per SM.  The scores S = Q . K^T
+// of the 6 T query rows (M = 128 TMEM lanes, 66 used for T = 11) against a 64-key
+// tile (N = 64, K = 256) and the output O += P . V (N = 256 dims, K = 64 keys) run
+// as tcgen05 MMAs with fp32 accumulators in tensor memory: S double-buffered in
+// columns 0..127, O in columns 128..383.  Operands are fp16 in shared memory,
+// K-major with the 128-byte swizzle: Q [128 rows][256 dims] staged once, K [64
+// keys][256 dims] and V^T [256 dims][64 keys] double-buffered, P [128 rows][64 keys].
+//   warp 0 (one thread)   issues the MMAs: S(i+1) ahead of O += P(i) V(i)
+//   warps 4..7            softmax: thread = query row = TMEM lane; the row's max and
+//                         sum stay in the thread.  The reference max moves only when
+//                         a tile's max exceeds it by more than 8 (e^8 keeps P in fp16
+//                         range), and only then is the row of O rescaled in TMEM.
+//   warps 8..15           producers: int8 K / V -> fp16(q * scale) into the next
+//                         buffer (V transposed through registers), the tile after
+//                         next prefetched into registers.
+// Every wait is bounded; on a timeout the CTA raises the error word, the MMA thread
+// drains every issued MMA and TMEM is freed before exit.
+constexpr int kTcTile = 64;
+constexpr int kTcRows = 128;
+constexpr uint32_t kQAtom = kTcRows * 128;            // 16 KB: 128 rows x 64 dims
+constexpr uint32_t kKAtom = kTcTile * 128;            // 8 KB: 64 keys x 64 dims
+constexpr uint32_t kOffTQ = 0;                        // 4 atoms
+constexpr uint32_t kOffTK = kOffTQ + 4 * kQAtom;      // 2 buffers x 4 atoms
+constexpr uint32_t kOffTV = kOffTK + 2 * 4 * kKAtom;  // 2 buffers x [256][64] (32 KB)
+constexpr uint32_t kOffTP = kOffTV + 2 * 256 * 128;   // [128][64] (16 KB)
+constexpr uint32_t kOffTBar = kOffTP + kTcRows * 128;
+constexpr uint32_t kTcSmem = kOffTBar + 128 + 1024;   // barriers, TMEM holder, abort flag; 1 KB alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 128;
+// instruction descriptors (kind::f16: fp16 A / B K-major, fp32 D, M x N)
+constexpr uint32_t kIdescQK = (1u << 4) | (static_cast<uint32_t>(kTcTile >> 3) << 17) | (static_cast<uint32_t>(kTcRows >> 4) << 24);
+constexpr uint32_t kIdescPV = (1u << 4) | (static_cast<uint32_t>(256 >> 3) << 17) | (static_cast<uint32_t>(kTcRows >> 4) << 24);
+constexpr float kLazy = 8.f;   // rescale O only when the row max grows by more than this
 
-__device__ __forceinline__ uint32_t sw32(int row, int chunk) {   // rows of 32 chunks
-  return static_cast<uint32_t>(row * 512 + ((chunk ^ (row & 7)) << 4));
+__device__ __forceinline__ uint32_t sw128(int r, int c) {   // (row, 16-byte chunk) in a K-major 128-B swizzled atom
+  return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
-__device__ __forceinline__ uint32_t sw8(int row, int chunk) {    // rows of 8 chunks
-  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);   // start address
+  d |= static_cast<uint64_t>(1u) << 16;                  // leading byte offset (unused: swizzled K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;          // stride byte offset: next 8-row group
+  d |= static_cast<uint64_t>(1u) << 46;                  // descriptor version
+  d |= static_cast<uint64_t>(2u) << 61;                  // 128-byte swizzle
+  return d;
 }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+__device__ __forceinline__ void tc_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
 }
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                        uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMbarPollLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
 }
 
-// 16 int8 cache bytes (q + 128) and their fp16 scale -> 16 fp16 fp16(q * scale)
-__device__ __forceinline__ void dq16(const uint4 b, __half s, uint4& lo, uint4& hi) {
-  const __half2 s2 = __half2half2(s);
-  const __half2 c1152 = __float2half2_rn(1152.f);
-  const uint32_t w[4] = {b.x, b.y, b.z, b.w};
-  uint32_t o[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t p0 = __byte_perm(w[i], 0x64646464u, 0x5140u);   // bytes 0, 1 -> 1024 + b
-    const uint32_t p1 = __byte_perm(w[i], 0x64646464u, 0x7362u);   // bytes 2, 3
-    const __half2 h0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p0), c1152), s2);
-    const __half2 h1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p1), c1152), s2);
-    o[2 * i] = *reinterpret_cast<const uint32_t*>(&h0);
-    o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&h1);
-  }
-  lo = make_uint4(o[0], o[1], o[2], o[3]);
-  hi = make_uint4(o[4], o[5], o[6], o[7]);
-}
-
-struct SplitArgs {
+struct TcArgs {
   const uint8_t* kv;
   const __half* sc;
   const __half* qw16;
   const int32_t* pos_slot;
   int64_t ctx;
   int T, parts;
+  uint32_t* err;
   float* pm;   // [4][parts][96]
   float* ps;
   float* pa;   // [4][parts][96][256]
 };
 
-__global__ void __launch_bounds__(kThreads, 1) attn_split_kernel(const SplitArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];
+// fp16 pair (k, k + 1) of 8 dequantised values: bytes (q + 128) of one 8-byte word
+__device__ __forceinline__ void dq8(uint2 w, __half2 s2, uint32_t (&o)[4]) {
+  const __half2 c1152 = __float2half2_rn(1152.f);
+  const uint32_t in[2] = {w.x, w.y};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t p0 = __byte_perm(in[i], 0x64646464u, 0x5140u);
+    const uint32_t p1 = __byte_perm(in[i], 0x64646464u, 0x7362u);
+    const __half2 h0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p0), c1152), s2);
+    const __half2 h1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p1), c1152), s2);
+    o[2 * i] = *reinterpret_cast<const uint32_t*>(&h0);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smraw[];
+  uint8_t* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffTBar);
+  uint64_t* kv_full = bar;        // [2] producers -> MMA
+  uint64_t* kv_empty = bar + 2;   // [2] PV commit -> producers
+  uint64_t* s_full = bar + 4;     // [2] QK commit -> softmax
+  uint64_t* s_free = bar + 6;     // [2] softmax read S -> MMA
+  uint64_t* p_full = bar + 8;     // softmax wrote P -> MMA
+  uint64_t* pv_done = bar + 9;    // PV commit -> softmax
+  uint64_t* done = bar + 10;      // final drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 11);
+  volatile uint32_t* abort_flag = tmem_holder + 1;
+
   const int g = blockIdx.y, part = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int T = a.T, R = kGroup * T, NB = (R + 7) >> 3;
+  const int T = a.T, R = kGroup * T;
   const int pos = a.pos_slot[0];
-  const int64_t total = std::min<int64_t>(static_cast<int64_t>(pos) + T, a.ctx);   // keys that exist
-  // this CTA's key range, in whole tiles
-  const int64_t ntiles_all = total > 0 ? (total + kTile - 1) / kTile : 0;
+  const int64_t total = std::min<int64_t>(static_cast<int64_t>(pos) + T, a.ctx);
+  const int64_t ntiles_all = total > 0 ? (total + kTcTile - 1) / kTcTile : 0;
   const int64_t t0 = ntiles_all * part / a.parts, t1 = ntiles_all * (part + 1) / a.parts;
-  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(sm));
+  const int n = static_cast<int>(t1 - t0);
+  const uint32_t sbase = smem_u32(sm);
   const uint8_t* Kc = a.kv + static_cast<int64_t>(g) * a.ctx * kHd;
   const uint8_t* Vc = a.kv + static_cast<int64_t>(kKvHeads + g) * a.ctx * kHd;
   const __half* Ks = a.sc + static_cast<int64_t>(g) * a.ctx * 8;
   const __half* Vs = a.sc + static_cast<int64_t>(kKvHeads + g) * a.ctx * 8;
+  const int64_t pb = (static_cast<int64_t>(g) * a.parts + part) * kMaxR;
 
-  // stage Q rows r = hl * T + t (zero rows up to NB * 8)
-  for (int i = tid; i < NB * 8 * 32; i += kThreads) {
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 8);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(done, 1);
+    *abort_flag = 0u;
+    mbar_fence_init();
+  }
+  // Q rows r = hl * T + t (zero beyond R), 4 atoms of 64 dims
+  for (int i = tid; i < kTcRows * 32; i += kThreads) {
     const int r = i >> 5, c = i & 31;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (r < R) {
       const int hl = r / T, t = r - hl * T;
       v = *reinterpret_cast<const uint4*>(a.qw16 + (static_cast<int64_t>(t) * kHeads + g * kGroup + hl) * kHd + c * 8);
     }
-    *reinterpret_cast<uint4*>(sm + kOffQ + sw32(r, c)) = v;
+    *reinterpret_cast<uint4*>(sm + kOffTQ + (c >> 3) * kQAtom + sw128(r, c & 7)) = v;
   }
-
-  // row owner state: 4 threads per row, lanes l, l ^ 8, l ^ 16, l ^ 24 of a warp
-  // (8 rows per warp), keys osub * 4 + 16 j + 0..3
-  const int orow = (tid & 7) + 8 * (tid >> 5), osub = (tid >> 3) & 3;
-  const bool owner = orow < R;
-  const int ot = owner ? orow % T : 0;
-  float m_run = -1e30f, l_run = 0.f;
-  // PV accumulators: warp = 16-dim block, all n-blocks (rows)
-  float acc[kMaxNB][4];
-#pragma unroll
-  for (int nb = 0; nb < kMaxNB; ++nb)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[nb][i] = 0.f;
-
-  // staging map: 2048 16-byte chunks per tile (K then V, key-major), 4 per thread
-  uint4 pre[4];
-  __half pres[4];
-  auto fetch = [&](int64_t tile) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = tid + j * kThreads;          // 0..2047
-      const int isv = c >> 10, key = (c >> 4) & 63, ch = c & 15;
-      const int64_t l = tile * kTile + key;
-      if (l < total) {
-        const uint8_t* src = (isv ? Vc : Kc) + l * kHd + ch * 16;
-        pre[j] = __ldg(reinterpret_cast<const uint4*>(src));
-        pres[j] = (isv ? Vs : Ks)[l * 8 + (ch >> 1)];
-      } else {
-        pre[j] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);   // q = 0
-        pres[j] = __float2half(0.f);
-      }
-    }
-  };
-  auto store = [&]() {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = tid + j * kThreads;
-      const int isv = c >> 10, key = (c >> 4) & 63, ch = c & 15;
-      uint4 lo, hi;
-      dq16(pre[j], pres[j], lo, hi);
-      uint8_t* base = sm + (isv ? kOffV : kOffK);
-      *reinterpret_cast<uint4*>(base + sw32(key, 2 * ch)) = lo;
-      *reinterpret_cast<uint4*>(base + sw32(key, 2 * ch + 1)) = hi;
-    }
+  fence_proxy_async_smem();
+  if (warp == 0) tc_alloc(tmem_holder, kTmemCols);
+  tc_before();
+  __syncthreads();
+  tc_after();
+  const uint32_t tmem = *tmem_holder;
+  auto fail = [&]() {
+    atomicOr(a.err, 1u);
+    *abort_flag = 1u;
   };
 
-  if (t0 < t1) fetch(t0);
-  for (int64_t tile = t0; tile < t1; ++tile) {
-    __syncthreads();   // the previous tile's K / V / P are consumed
-    store();
-    __syncthreads();
-    if (tile + 1 < t1) fetch(tile + 1);   // in flight during this tile's math
-
-    // ---- scores S^T[key][row] = K . Q^T: items (key block mb, row block nb) ----
-    for (int it = warp; it < 4 * NB; it += kWarps) {
-      const int mb = it & 3, nb = it >> 2;
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+  if (warp == 0) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n > 0) {
+      auto issue_qk = [&](int j) -> bool {
+        const int b = j & 1;
+        const uint32_t u = static_cast<uint32_t>(j >> 1);
+        if (!tc_wait(&kv_full[b], u & 1) || !tc_wait(&s_free[b], (u & 1) ^ 1)) return false;
+        tc_after();
+        const uint32_t kb = sbase + kOffTK + b * 4 * kKAtom;
 #pragma unroll
-      for (int ks = 0; ks < 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1;
-        const int arow = mb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        ldsm_x4(sbase + kOffK + sw32(arow, 2 * ks + (lane >> 4)), a0, a1, a2, a3);
-        const int brow = nb * 8 + (lane & 7);
-        ldsm_x2(sbase + kOffQ + sw32(brow, 2 * ks + ((lane >> 3) & 1)), b0, b1);
-        mma_f16(c, a0, a1, a2, a3, b0, b1);
+        for (int s = 0; s < 16; ++s) {
+          const uint64_t ad = sw128_desc(sbase + kOffTQ + (s >> 2) * kQAtom + (s & 3) * 32);
+          const uint64_t bd = sw128_desc(kb + (s >> 2) * kKAtom + (s & 3) * 32);
+          tc_mma(tmem + kColS + b * kTcTile, ad, bd, kIdescQK, s > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[b]);
+        return true;
+      };
+      bool ok = issue_qk(0);
+      for (int i = 0; i < n && ok && !*abort_flag; ++i) {
+        if (i + 1 < n && !(ok = issue_qk(i + 1))) break;
+        if (!(ok = tc_wait(p_full, i & 1))) break;
+        tc_after();
+        const int b = i & 1;
+        const uint32_t vb = sbase + kOffTV + b * 256 * 128;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma(tmem + kColO, sw128_desc(sbase + kOffTP + kk * 32), sw128_desc(vb + kk * 32), kIdescPV,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(pv_done);
+        tc_commit(&kv_empty[b]);
       }
-      // c0 / c1: key mb*16 + g, rows nb*8 + 2q, +1; c2 / c3: key + 8
-      float* S = reinterpret_cast<float*>(sm + kOffS);
-      const int key = mb * 16 + (lane >> 2), row = nb * 8 + 2 * (lane & 3);
-      S[row * kSStride + key] = c[0];
-      S[(row + 1) * kSStride + key] = c[1];
-      S[row * kSStride + key + 8] = c[2];
-      S[(row + 1) * kSStride + key + 8] = c[3];
+      if (!ok) fail();
+      tc_commit(done);   // every issued MMA has completed before TMEM is released
+      if (!tc_wait(done, 0)) fail();
     }
-    __syncthreads();
-
-    // ---- online softmax per row (4 threads x 16 keys) ----
-    if (orow < NB * 8) {
-      const float* S = reinterpret_cast<const float*>(sm + kOffS);
-      const int64_t lim = std::min<int64_t>(total, static_cast<int64_t>(pos) + ot + 1);   // keys < lim
-      float s[16];
-      float mx = -1e30f;
+  } else if (warp >= 4 && warp < 8) {
+    // --------------------------------------------------------------- softmax
+    const int qd = warp - 4, row = qd * 32 + lane;
+    const uint32_t lanebase = static_cast<uint32_t>(qd * 32) << 16;
+    const bool valid = row < R;
+    const int t = valid ? row % T : 0;
+    const int64_t lim = std::min<int64_t>(total, static_cast<int64_t>(pos) + t + 1);   // keys < lim
+    float m_ref = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n && ok && !*abort_flag; ++i) {
+      const int b = i & 1;
+      const uint32_t u = static_cast<uint32_t>(i >> 1);
+      if (!(ok = tc_wait(&s_full[b], u & 1))) break;
+      tc_after();
+      float s[kTcTile];
+#pragma unroll
+      for (int c = 0; c < kTcTile / 16; ++c) {
+        uint32_t r[16];
+        tc_ld16(tmem + lanebase + kColS + b * kTcTile + c * 16, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s[c * 16 + j] = __uint_as_float(r[j]);
+      }
+      tc_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      const int64_t k0 = (t0 + i) * kTcTile;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kTcTile; ++j) {
+        if (!(valid && k0 + j < lim)) s[j] = -INFINITY;
+        mt = fmaxf(mt, s[j]);
+      }
+      // O (rows of earlier tiles) and P are free once the previous PV completed
+      if (i > 0 && !(ok = tc_wait(pv_done, (i - 1) & 1))) break;
+      tc_after();
+      if (mt > m_ref + kLazy || (m_ref == -INFINITY && mt > -INFINITY)) {
+        if (m_ref != -INFINITY && i > 0) {   // rescale this row of O and the running sum
+          const float cor = __expf(m_ref - mt);
+          l_run *= cor;
+#pragma unroll 1
+          for (int c = 0; c < 16; ++c) {
+            uint32_t r[16];
+            tc_ld16(tmem + lanebase + kColO + c * 16, r);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * cor);
+            tc_st16(tmem + lanebase + kColO + c * 16, r);
+          }
+          tc_wait_st();
+        }
+        m_ref = mt;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {   // keys 8c .. 8c + 7 -> one 16-byte chunk of P
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float p0 = s[8 * c + 2 * j] == -INFINITY ? 0.f : __expf(s[8 * c + 2 * j] - m_ref);
+          const float p1 = s[8 * c + 2 * j + 1] == -INFINITY ? 0.f : __expf(s[8 * c + 2 * j + 1] - m_ref);
+          sum += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          w[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(sm + kOffTP + sw128(row, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_run += sum;
+      fence_proxy_async_smem();
+      tc_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!ok) fail();
+    // partials: (max, sum) and the unnormalised output row
+    if (n > 0 && ok && !*abort_flag && tc_wait(pv_done, (n - 1) & 1)) {
+      tc_after();
+#pragma unroll 1
+      for (int c = 0; c < 16; ++c) {
+        uint32_t r[16];
+        tc_ld16(tmem + lanebase + kColO + c * 16, r);
+        tc_wait_ld();
+        if (valid) {
+          float4* dst = reinterpret_cast<float4*>(a.pa + (pb + row) * kHd + c * 16);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
+      }
+      if (valid) {
+        a.pm[pb + row] = m_ref == -INFINITY ? -1e30f : m_ref;
+        a.ps[pb + row] = l_run;
+      }
+    } else if (valid) {
+      if (n > 0 && !*abort_flag) fail();
+      a.pm[pb + row] = -1e30f;   // no key in this range (or an aborted CTA): contributes nothing
+      a.ps[pb + row] = 0.f;
+      for (int c = 0; c < kHd; c += 4) *reinterpret_cast<float4*>(a.pa + (pb + row) * kHd + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    tc_before();
+  } else if (warp >= 8) {
+    // -------------------------------------------------------------- producers
+    const int ptid = tid - 256;
+    const int vk = ptid & 7, vd = ptid >> 3;   // V unit: keys 8 vk .. +7, dims 8 vd .. +7
+    uint4 kq[4];
+    __half ks[4];
+    uint2 vq[8];
+    __half vsc[8];
+    auto fetch = [&](int i) {
+      const int64_t kbase = (t0 + i) * kTcTile;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int k0 = osub * 4 + 16 * j;
-        const float4 v = *reinterpret_cast<const float4*>(S + orow * kSStride + k0);
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const bool ok = owner && tile * kTile + k0 + i < lim;
-          s[4 * j + i] = ok ? vv[i] : -1e30f;
-          mx = fmaxf(mx, s[4 * j + i]);
+        const int c = ptid + j * 256, key = c >> 4, ch = c & 15;
+        const int64_t l = kbase + key;
+        if (l < total) {
+          kq[j] = __ldg(reinterpret_cast<const uint4*>(Kc + l * kHd + ch * 16));
+          ks[j] = Ks[l * 8 + (ch >> 1)];
+        } else {
+          kq[j] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+          ks[j] = __float2half(0.f);
         }
       }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float mn = fmaxf(m_run, mx);
-      const float cor = __expf(m_run - mn);
-      float sum = 0.f;
-      uint32_t ph[8];
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        const float p0 = s[i] > -1e29f ? __expf(s[i] - mn) : 0.f;
-        const float p1 = s[i + 1] > -1e29f ? __expf(s[i + 1] - mn) : 0.f;
-        sum += p0 + p1;
-        const __half2 h = __floats2half2_rn(p0, p1);
-        ph[i >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      l_run = l_run * cor + sum;
-      m_run = mn;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)   // keys osub * 4 + 16 j .. + 3: half of chunk 2 j + osub / 2
-        *reinterpret_cast<uint2*>(sm + kOffP + sw8(orow, 2 * j + (osub >> 1)) + (osub & 1) * 8) =
-            make_uint2(ph[2 * j], ph[2 * j + 1]);
-      if (osub == 0) reinterpret_cast<float*>(sm + kOffCor)[orow] = cor;
-    }
-    __syncthreads();
-
-    // ---- O^T[dim][row] = cor * O^T + V^T . P^T: warp = dims warp*16 .. +15 ----
-    {
-      const float* cor = reinterpret_cast<const float*>(sm + kOffCor);
-      uint32_t va[4][4];
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {   // 16-key steps; A = V^T via transposed loads
-        const int key = kk * 16 + (lane & 7) + (lane >> 4) * 8;
-        ldsm_x4_t(sbase + kOffV + sw32(key, warp * 2 + ((lane >> 3) & 1)), va[kk][0], va[kk][1], va[kk][2],
-                  va[kk][3]);
-      }
-#pragma unroll
-      for (int nb = 0; nb < kMaxNB; ++nb) {
-        if (nb < NB) {
-          const float c0 = cor[nb * 8 + 2 * (lane & 3)], c1 = cor[nb * 8 + 2 * (lane & 3) + 1];
-          acc[nb][0] *= c0;
-          acc[nb][1] *= c1;
-          acc[nb][2] *= c0;
-          acc[nb][3] *= c1;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            uint32_t b0, b1;
-            ldsm_x2(sbase + kOffP + sw8(nb * 8 + (lane & 7), 2 * kk + ((lane >> 3) & 1)), b0, b1);
-            mma_f16(acc[nb], va[kk][0], va[kk][1], va[kk][2], va[kk][3], b0, b1);
-          }
+      for (int k = 0; k < 8; ++k) {
+        const int64_t l = kbase + vk * 8 + k;
+        if (l < total) {
+          vq[k] = __ldg(reinterpret_cast<const uint2*>(Vc + l * kHd + vd * 8));
+          vsc[k] = Vs[l * 8 + (vd >> 2)];
+        } else {
+          vq[k] = make_uint2(0x80808080u, 0x80808080u);
+          vsc[k] = __float2half(0.f);
         }
       }
+    };
+    bool ok = true;
+    if (n > 0) fetch(0);
+    for (int i = 0; i < n && ok && !*abort_flag; ++i) {
+      const int b = i & 1;
+      const uint32_t u = static_cast<uint32_t>(i >> 1);
+      uint4 kq_c[4];
+      __half ks_c[4];
+      uint2 vq_c[8];
+      __half vsc_c[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { kq_c[j] = kq[j]; ks_c[j] = ks[j]; }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { vq_c[k] = vq[k]; vsc_c[k] = vsc[k]; }
+      if (i + 1 < n) fetch(i + 1);   // in flight while this tile is written
+      if (!(ok = tc_wait(&kv_empty[b], (u & 1) ^ 1))) break;
+      uint8_t* kb = sm + kOffTK + b * 4 * kKAtom;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = ptid + j * 256, key = c >> 4, ch = c & 15;
+        const __half2 s2 = __half2half2(ks_c[j]);
+        uint32_t lo[4], hi[4];
+        dq8(make_uint2(kq_c[j].x, kq_c[j].y), s2, lo);
+        dq8(make_uint2(kq_c[j].z, kq_c[j].w), s2, hi);
+        uint8_t* atom = kb + (ch >> 2) * kKAtom;   // dims 16 ch .. + 15 lie in atom ch / 4
+        *reinterpret_cast<uint4*>(atom + sw128(key, (ch & 3) * 2)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(atom + sw128(key, (ch & 3) * 2 + 1)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      // V unit: 8 keys x 8 dims, transposed to V^T rows (one 16-byte chunk of 8 keys per dim)
+      uint32_t vv[8][4];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dq8(vq_c[k], __half2half2(vsc_c[k]), vv[k]);
+      uint8_t* vbuf = sm + kOffTV + b * 256 * 128;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        uint32_t w[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m)   // keys 2m, 2m + 1 of dim d
+          w[m] = __byte_perm(vv[2 * m][d >> 1], vv[2 * m + 1][d >> 1], (d & 1) ? 0x7632u : 0x5410u);
+        *reinterpret_cast<uint4*>(vbuf + sw128(vd * 8 + d, vk)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kv_full[b]);
     }
+    if (!ok) fail();
   }
 
-  // ---- partials: (max, sum) per row, unnormalised output [row][256] ----
-  const int64_t pb = (static_cast<int64_t>(g) * a.parts + part) * kMaxR;
-  if (owner && osub == 0) {
-    a.pm[pb + orow] = m_run;
-    a.ps[pb + orow] = l_run;
-  }
-#pragma unroll
-  for (int nb = 0; nb < kMaxNB; ++nb) {
-    if (nb < NB) {
-      const int row = nb * 8 + 2 * (lane & 3), dim = warp * 16 + (lane >> 2);
-      if (row < R) {
-        a.pa[(pb + row) * kHd + dim] = acc[nb][0];
-        a.pa[(pb + row) * kHd + dim + 8] = acc[nb][2];
-      }
-      if (row + 1 < R) {
-        a.pa[(pb + row + 1) * kHd + dim] = acc[nb][1];
-        a.pa[(pb + row + 1) * kHd + dim + 8] = acc[nb][3];
-      }
-    }
+  tc_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_after();
+    tc_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -409,6 +538,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
 }
 
 int parts_for(int sms) { return std::max(1, sms / kKvHeads); }
+constexpr size_t kAttnErrBytes = 256;   // the workspace starts with the device error word
 
 int sm_count_dev() {
   int dev = 0, sms = 148;
@@ -422,7 +552,7 @@ int sm_count_dev() {
 size_t attn_workspace_bytes(int rows) {
   if (rows < 1 || rows > kMaxRows) return 0;
   const size_t parts = static_cast<size_t>(parts_for(sm_count_dev()));
-  return kKvHeads * parts * kMaxR * (2 + kHd) * sizeof(float);
+  return kAttnErrBytes + kKvHeads * parts * kMaxR * (2 + kHd) * sizeof(float);
 }
 
 int run_attn_pre(const void* qrow, const void* krow, const void* vrow, const float* qnw, const float* knw,
@@ -437,12 +567,12 @@ int run_attn_pre(const void* qrow, const void* krow, const void* vrow, const flo
 }
 
 static int split_args(const void* kv, const void* sc, const void* qw16, const int32_t* pos_slot, int rows,
-                      int64_t ctx, void* ws, size_t ws_bytes, SplitArgs& a) {
+                      int64_t ctx, void* ws, size_t ws_bytes, TcArgs& a) {
   if (!kv || !sc || !qw16 || !pos_slot || !ws) return TLX_ERR_NULL;
   if (rows < 1 || rows > kMaxRows || ctx < 1) return TLX_ERR_SHAPE;
   if (ws_bytes < attn_workspace_bytes(rows)) return TLX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(kv) & 15) || (reinterpret_cast<uintptr_t>(qw16) & 15) ||
-      (reinterpret_cast<uintptr_t>(ws) & 15))
+      (reinterpret_cast<uintptr_t>(ws) & 255))
     return TLX_ERR_ALIGN;
   const int parts = parts_for(sm_count_dev());
   a.kv = static_cast<const uint8_t*>(kv);
@@ -452,7 +582,8 @@ static int split_args(const void* kv, const void* sc, const void* qw16, const in
   a.ctx = ctx;
   a.T = rows;
   a.parts = parts;
-  float* f = static_cast<float*>(ws);
+  a.err = static_cast<uint32_t*>(ws);
+  float* f = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAttnErrBytes);
   a.pm = f;
   a.ps = f + static_cast<size_t>(kKvHeads) * parts * kMaxR;
   a.pa = f + static_cast<size_t>(2) * kKvHeads * parts * kMaxR;
@@ -461,17 +592,17 @@ static int split_args(const void* kv, const void* sc, const void* qw16, const in
 
 int run_attn_split(const void* kv, const void* sc, const void* qw16, const int32_t* pos_slot, int rows, int64_t ctx,
                    void* ws, size_t ws_bytes, cudaStream_t stream) {
-  SplitArgs a;
+  TcArgs a;
   const int rc = split_args(kv, sc, qw16, pos_slot, rows, ctx, ws, ws_bytes, a);
   if (rc) return rc;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSplitSmem)) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kTcSmem)) != cudaSuccess)
       return TLX_ERR_LAUNCH;
     configured = true;
   }
-  attn_split_kernel<<<dim3(a.parts, kKvHeads), kThreads, kSplitSmem, stream>>>(a);
+  attn_tc_kernel<<<dim3(a.parts, kKvHeads), kThreads, kTcSmem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 
@@ -480,7 +611,7 @@ int run_attn_combine(const void* ws, size_t ws_bytes, const void* qrow, int rows
   if (rows < 1 || rows > kMaxRows) return TLX_ERR_SHAPE;
   if (ws_bytes < attn_workspace_bytes(rows)) return TLX_ERR_WORKSPACE;
   const int parts = parts_for(sm_count_dev());
-  const float* f = static_cast<const float*>(ws);
+  const float* f = reinterpret_cast<const float*>(static_cast<const uint8_t*>(ws) + kAttnErrBytes);
   attn_combine_kernel<<<dim3(kHeads, rows), 256, 0, stream>>>(
       f, f + static_cast<size_t>(kKvHeads) * parts * kMaxR, f + static_cast<size_t>(2) * kKvHeads * parts * kMaxR,
       parts, rows, static_cast<const __half*>(qrow), static_cast<__half*>(ao));

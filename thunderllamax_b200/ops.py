@@ -380,6 +380,10 @@ class Attention:
                                           _stream(qrow)), "attn_combine")
         return ao
 
+    def error(self) -> int:
+        """The split kernel's error bits (a bounded wait that gave up); synchronous."""
+        return self.ws.error()
+
     def decode(self, kv, sc, qw16, qrow, pos_slot, ao=None):
         require_device()
         if ao is None:
