@@ -127,16 +127,15 @@ __global__ void __launch_bounds__(256) attn_pre_kernel(const __half* __restrict_
 // drains every issued MMA and TMEM is freed before exit.
 constexpr int kTcTile = 64;
 constexpr int kTcRows = 128;
-constexpr uint32_t kQAtom = kTcRows * 128;            // 16 KB: 128 rows x 64 dims
 constexpr uint32_t kKAtom = kTcTile * 128;            // 8 KB: 64 keys x 64 dims
-constexpr uint32_t kOffTQ = 0;                        // 4 atoms
-constexpr uint32_t kOffTK = kOffTQ + 4 * kQAtom;      // 2 buffers x 4 atoms
-constexpr uint32_t kOffTV = kOffTK + 2 * 4 * kKAtom;  // 2 buffers x [256][64] (32 KB)
-constexpr uint32_t kOffTP = kOffTV + 2 * 256 * 128;   // [128][64] (16 KB)
+constexpr int kKvBufs = 3;                            // K / V tiles in flight
+constexpr uint32_t kOffTK = 0;                        // kKvBufs buffers x 4 atoms
+constexpr uint32_t kOffTV = kOffTK + kKvBufs * 4 * kKAtom;  // kKvBufs buffers x [256][64] (32 KB)
+constexpr uint32_t kOffTP = kOffTV + kKvBufs * 256 * 128;   // [128][64] (16 KB)
 constexpr uint32_t kOffTBar = kOffTP + kTcRows * 128;
 constexpr uint32_t kTcSmem = kOffTBar + 128 + 1024;   // barriers, TMEM holder, abort flag; 1 KB alignment slack
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 128;
+constexpr uint32_t kColS = 0, kColO = 128, kColQ = 384;   // Q: 256 fp16 per lane = 128 columns
 // instruction descriptors (kind::f16: fp16 A / B K-major, fp32 D, M x N)
 constexpr uint32_t kIdescQK = (1u << 4) | (static_cast<uint32_t>(kTcTile >> 3) << 17) | (static_cast<uint32_t>(kTcRows >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (static_cast<uint32_t>(256 >> 3) << 17) | (static_cast<uint32_t>(kTcRows >> 4) << 24);
@@ -171,6 +170,14 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] . B[smem desc]^T (A: one row per lane, k packed two fp16 per column)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
@@ -192,6 +199,12 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16])
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kMbarPollLimit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -230,14 +243,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smraw[];
   uint8_t* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffTBar);
-  uint64_t* kv_full = bar;        // [2] producers -> MMA
-  uint64_t* kv_empty = bar + 2;   // [2] PV commit -> producers
-  uint64_t* s_full = bar + 4;     // [2] QK commit -> softmax
-  uint64_t* s_free = bar + 6;     // [2] softmax read S -> MMA
-  uint64_t* p_full = bar + 8;     // softmax wrote P -> MMA
-  uint64_t* pv_done = bar + 9;    // PV commit -> softmax
-  uint64_t* done = bar + 10;      // final drain
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 11);
+  uint64_t* kv_full = bar;                   // [kKvBufs] producers -> MMA
+  uint64_t* kv_empty = bar + kKvBufs;        // [kKvBufs] PV commit -> producers
+  uint64_t* s_full = bar + 2 * kKvBufs;      // [2] QK commit -> softmax
+  uint64_t* s_free = s_full + 2;             // [2] softmax read S -> MMA
+  uint64_t* p_full = s_full + 4;             // softmax wrote P -> MMA
+  uint64_t* pv_done = s_full + 5;            // PV commit -> softmax
+  uint64_t* done = s_full + 6;               // final drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 7);
+  static_assert((2 * kKvBufs + 7) * 8 + 8 <= 128, "barrier area");
   volatile uint32_t* abort_flag = tmem_holder + 1;
 
   const int g = blockIdx.y, part = blockIdx.x;
@@ -256,9 +270,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
   const int64_t pb = (static_cast<int64_t>(g) * a.parts + part) * kMaxR;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKvBufs; ++i) {
       mbar_init(&kv_full[i], 8);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
     }
@@ -268,22 +284,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
     *abort_flag = 0u;
     mbar_fence_init();
   }
-  // Q rows r = hl * T + t (zero beyond R), 4 atoms of 64 dims
-  for (int i = tid; i < kTcRows * 32; i += kThreads) {
-    const int r = i >> 5, c = i & 31;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (r < R) {
-      const int hl = r / T, t = r - hl * T;
-      v = *reinterpret_cast<const uint4*>(a.qw16 + (static_cast<int64_t>(t) * kHeads + g * kGroup + hl) * kHd + c * 8);
-    }
-    *reinterpret_cast<uint4*>(sm + kOffTQ + (c >> 3) * kQAtom + sw128(r, c & 7)) = v;
-  }
-  fence_proxy_async_smem();
   if (warp == 0) tc_alloc(tmem_holder, kTmemCols);
   tc_before();
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tmem_holder;
+  if (warp >= 4 && warp < 8) {
+    // Q into TMEM columns kColQ..: lane = query row r = hl * T + t (zero beyond R)
+    const int r = (warp - 4) * 32 + lane;
+    const uint4* src = nullptr;
+    if (r < R) {
+      const int hl = r / T, t = r - hl * T;
+      src = reinterpret_cast<const uint4*>(a.qw16 + (static_cast<int64_t>(t) * kHeads + g * kGroup + hl) * kHd);
+    }
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {   // 32 dims = 16 columns per store
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = src ? src[c * 4 + j] : make_uint4(0u, 0u, 0u, 0u);
+        w[4 * j] = v.x;
+        w[4 * j + 1] = v.y;
+        w[4 * j + 2] = v.z;
+        w[4 * j + 3] = v.w;
+      }
+      tc_st16(tmem + (static_cast<uint32_t>((warp - 4) * 32) << 16) + kColQ + c * 16, w);
+    }
+    tc_wait_st();
+  }
+  tc_before();
+  __syncthreads();
+  tc_after();
   auto fail = [&]() {
     atomicOr(a.err, 1u);
     *abort_flag = 1u;
@@ -293,16 +324,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0 && n > 0) {
       auto issue_qk = [&](int j) -> bool {
-        const int b = j & 1;
-        const uint32_t u = static_cast<uint32_t>(j >> 1);
-        if (!tc_wait(&kv_full[b], u & 1) || !tc_wait(&s_free[b], (u & 1) ^ 1)) return false;
+        const int b = j & 1, kb_i = j % kKvBufs;
+        const uint32_t u = static_cast<uint32_t>(j >> 1), ku = static_cast<uint32_t>(j / kKvBufs);
+        if (!tc_wait(&kv_full[kb_i], ku & 1) || !tc_wait(&s_free[b], (u & 1) ^ 1)) return false;
         tc_after();
-        const uint32_t kb = sbase + kOffTK + b * 4 * kKAtom;
+        const uint32_t kb = sbase + kOffTK + kb_i * 4 * kKAtom;
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
-          const uint64_t ad = sw128_desc(sbase + kOffTQ + (s >> 2) * kQAtom + (s & 3) * 32);
           const uint64_t bd = sw128_desc(kb + (s >> 2) * kKAtom + (s & 3) * 32);
-          tc_mma(tmem + kColS + b * kTcTile, ad, bd, kIdescQK, s > 0 ? 1u : 0u);
+          tc_mma_ts(tmem + kColS + b * kTcTile, tmem + kColQ + s * 8, bd, kIdescQK, s > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[b]);
         return true;
@@ -312,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
         if (i + 1 < n && !(ok = issue_qk(i + 1))) break;
         if (!(ok = tc_wait(p_full, i & 1))) break;
         tc_after();
-        const int b = i & 1;
+        const int b = i % kKvBufs;
         const uint32_t vb = sbase + kOffTV + b * 256 * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -339,25 +369,38 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
       const uint32_t u = static_cast<uint32_t>(i >> 1);
       if (!(ok = tc_wait(&s_full[b], u & 1))) break;
       tc_after();
-      float s[kTcTile];
-#pragma unroll
-      for (int c = 0; c < kTcTile / 16; ++c) {
-        uint32_t r[16];
-        tc_ld16(tmem + lanebase + kColS + b * kTcTile + c * 16, r);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) s[c * 16 + j] = __uint_as_float(r[j]);
-      }
+      // the tile's 64 scores of this row: four TMEM loads, one wait
+      uint32_t r0[16], r1[16], r2[16], r3[16];
+      tc_ld16(tmem + lanebase + kColS + b * kTcTile + 0, r0);
+      tc_ld16(tmem + lanebase + kColS + b * kTcTile + 16, r1);
+      tc_ld16(tmem + lanebase + kColS + b * kTcTile + 32, r2);
+      tc_ld16(tmem + lanebase + kColS + b * kTcTile + 48, r3);
+      tc_wait_ld();
       tc_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);
-      const int64_t k0 = (t0 + i) * kTcTile;
-      float mt = -INFINITY;
+      float s[kTcTile];
 #pragma unroll
-      for (int j = 0; j < kTcTile; ++j) {
-        if (!(valid && k0 + j < lim)) s[j] = -INFINITY;
-        mt = fmaxf(mt, s[j]);
+      for (int j = 0; j < 16; ++j) {
+        s[j] = __uint_as_float(r0[j]);
+        s[16 + j] = __uint_as_float(r1[j]);
+        s[32 + j] = __uint_as_float(r2[j]);
+        s[48 + j] = __uint_as_float(r3[j]);
       }
+      // keys k0 + j exist for this row while j < rem (causal limit and cache end)
+      const int64_t k0 = (t0 + i) * kTcTile;
+      const int rem = valid ? static_cast<int>(std::max<int64_t>(0, std::min<int64_t>(kTcTile, lim - k0))) : 0;
+      if (rem < kTcTile) {
+#pragma unroll
+        for (int j = 0; j < kTcTile; ++j)
+          if (j >= rem) s[j] = -INFINITY;
+      }
+      float mx[8];   // 8 independent max chains, then a tree
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx[j] = s[j];
+#pragma unroll
+      for (int j = 8; j < kTcTile; ++j) mx[j & 7] = fmaxf(mx[j & 7], s[j]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       // O (rows of earlier tiles) and P are free once the previous PV completed
       if (i > 0 && !(ok = tc_wait(pv_done, (i - 1) & 1))) break;
       tc_after();
@@ -378,21 +421,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
         }
         m_ref = mt;
       }
-      float sum = 0.f;
+      // p = e^(s - m) = 2^(s log2 e - m log2 e): one fma and one ex2 per key; a
+      // missing key (-inf) gives 2^-inf = 0 (and a row without keys so far has all
+      // scores -inf, so its offset is taken as 0)
+      const float kLog2e = 1.4426950408889634f;
+      const float off = m_ref == -INFINITY ? 0.f : -m_ref * kLog2e;
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};   // independent partial sums
 #pragma unroll
       for (int c = 0; c < 8; ++c) {   // keys 8c .. 8c + 7 -> one 16-byte chunk of P
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float p0 = s[8 * c + 2 * j] == -INFINITY ? 0.f : __expf(s[8 * c + 2 * j] - m_ref);
-          const float p1 = s[8 * c + 2 * j + 1] == -INFINITY ? 0.f : __expf(s[8 * c + 2 * j + 1] - m_ref);
-          sum += p0 + p1;
+          const float p0 = ex2_approx(fmaf(s[8 * c + 2 * j], kLog2e, off));
+          const float p1 = ex2_approx(fmaf(s[8 * c + 2 * j + 1], kLog2e, off));
+          sums[j] += p0 + p1;
           const __half2 h = __floats2half2_rn(p0, p1);
           w[j] = *reinterpret_cast<const uint32_t*>(&h);
         }
         *reinterpret_cast<uint4*>(sm + kOffTP + sw128(row, c)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run += sum;
+      l_run += (sums[0] + sums[1]) + (sums[2] + sums[3]);
       fence_proxy_async_smem();
       tc_before();
       __syncwarp();
@@ -463,8 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TcArgs a) {
     bool ok = true;
     if (n > 0) fetch(0);
     for (int i = 0; i < n && ok && !*abort_flag; ++i) {
-      const int b = i & 1;
-      const uint32_t u = static_cast<uint32_t>(i >> 1);
+      const int b = i % kKvBufs;
+      const uint32_t u = static_cast<uint32_t>(i / kKvBufs);
       uint4 kq_c[4];
       __half ks_c[4];
       uint2 vq_c[8];
