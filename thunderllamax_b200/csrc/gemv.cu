@@ -938,7 +938,54 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
 // ---- projections over one staged x: aq3k8v11 (q / k IQ3_XXS, v Q4_K) and q5g8v11
 // (qkv Q5_K, gate IQ3_XXS).  Workspace: [image][ws of projection 0][ws 1]..., each
 // region 256-byte aligned.
+//
+// The projections run side by side: after the staging kernel the stream forks into
+// one side stream per projection (event record / wait, so a CUDA graph capture
+// turns them into parallel branches) and joins again.  Each GEMV gets a share of
+// the CTA budget in proportion to its weight bytes, so the small ones no longer
+// pay a full-grid launch of their own one after the other.
 static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
+
+static int projection_ctas(int n, const Projection* pr, int64_t k, int max_ctas, int i) {
+  const int total = max_ctas > 0 ? max_ctas : sm_count();
+  if (n <= 1) return total;
+  double all = 0.0, mine = 0.0;
+  for (int j = 0; j < n; ++j) {
+    const double b = static_cast<double>(pr[j].n_rows) * static_cast<double>(k / 256) * block_bytes(pr[j].qt);
+    all += b;
+    if (j == i) mine = b;
+  }
+  const int c = all > 0.0 ? static_cast<int>(total * mine / all) : 1;
+  return std::max(1, std::min(total, c));
+}
+
+namespace {
+constexpr int kMaxDevices = 16;
+struct SideStreams {
+  bool ok = false;
+  cudaStream_t s[kMaxProjections];
+  cudaEvent_t fork, join[kMaxProjections];
+};
+std::mutex g_side_mu;   // one fork / join sequence at a time (the events are shared)
+SideStreams g_side[kMaxDevices];
+std::once_flag g_side_once[kMaxDevices];
+
+// this device's side streams, created on first use; nullptr if that failed (the
+// projections then run one after the other on the caller's stream)
+SideStreams* side_streams() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  SideStreams& ss = g_side[dev];
+  std::call_once(g_side_once[dev], [&ss] {
+    bool ok = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; i < kMaxProjections && ok; ++i)
+      ok = cudaStreamCreateWithFlags(&ss.s[i], cudaStreamNonBlocking) == cudaSuccess &&
+           cudaEventCreateWithFlags(&ss.join[i], cudaEventDisableTiming) == cudaSuccess;
+    ss.ok = ok;
+  });
+  return ss.ok ? &ss : nullptr;
+}
+}  // namespace
 
 size_t projections_workspace_bytes(int n, const Projection* pr, int m, int64_t k, int x_dtype, int max_ctas) {
   if (x_dtype != DT_F16 && x_dtype != DT_BF16) return 0;
@@ -947,7 +994,8 @@ size_t projections_workspace_bytes(int n, const Projection* pr, int m, int64_t k
   if (!img) return 0;
   size_t total = al256(img);
   for (int i = 0; i < n; ++i) {
-    const size_t w = gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas);
+    const size_t w =
+        gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, projection_ctas(n, pr, k, max_ctas, i));
     if (!w) return 0;
     total += al256(w);
   }
@@ -974,11 +1022,25 @@ int run_projections(int n, const Projection* pr, const uint32_t* grid, const voi
   // projection reads the image
   int rc = stage_image(x, x_dtype, ldx, m, k, img, sums, stream);
   if (rc) return rc;
+  SideStreams* ss = n > 1 ? side_streams() : nullptr;
+  std::unique_lock<std::mutex> lock(g_side_mu, std::defer_lock);
+  if (ss) {
+    lock.lock();
+    if (cudaEventRecord(ss->fork, stream) != cudaSuccess) return TLX_ERR_LAUNCH;
+  }
   for (int i = 0; i < n; ++i) {
-    const size_t b = al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas));
+    const int ctas = projection_ctas(n, pr, k, max_ctas, i);
+    const size_t b = al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, ctas));
+    cudaStream_t st = stream;
+    if (ss) {
+      st = ss->s[i];
+      if (cudaStreamWaitEvent(st, ss->fork, 0) != cudaSuccess) return TLX_ERR_LAUNCH;
+    }
     rc = run_gemv(EPI_STORE, pr[i].qt, pr[i].w, nullptr, pr[i].qt == QT_IQ3_XXS ? grid : nullptr, img, DT_IMAGE, 0, m,
                   pr[i].n_rows, k, nullptr, 0, pr[i].out, DT_F16, pr[i].n_rows, 0, nullptr, nullptr, nullptr, nullptr,
-                  0, nullptr, p, b, max_ctas, stream);
+                  0, nullptr, p, b, ctas, st);
+    if (ss && (cudaEventRecord(ss->join[i], st) != cudaSuccess || cudaStreamWaitEvent(stream, ss->join[i], 0) != cudaSuccess))
+      return TLX_ERR_LAUNCH;   // joined even after a failed launch, so no side branch is left open
     if (rc) return rc;
     p += b;
   }
@@ -996,7 +1058,7 @@ int projections_error(const void* ws, int n, const Projection* pr, int m, int64_
     uint32_t ei = 0;
     if (cudaMemcpy(&ei, p, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return TLX_ERR_LAUNCH;
     e |= ei;
-    p += al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, max_ctas));
+    p += al256(gemv_workspace_bytes(EPI_STORE, pr[i].qt, pr[i].n_rows, k, m, DT_IMAGE, projection_ctas(n, pr, k, max_ctas, i)));
   }
   *err_out = e;
   return TLX_OK;
