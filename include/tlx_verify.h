@@ -209,7 +209,11 @@ int tlx_accept11k(const int32_t* amds, const int32_t* drafts, const float* xA, i
  * [m][nq] / [m][nk] / [m][nv].  Weights tiled (tlx_pack_tiles).  x is staged once
  * and the three GEMVs share it.  Workspace: tlx_aq3k8v11_workspace_bytes, zeroed
  * once (tlx_workspace_init) and reused.  The reference shapes are nq = 12288,
- * nk = nv = 1024, k = 5120, m = 11. */
+ * nk = nv = 1024, k = 5120, m = 11.  After the staging the GEMVs run side by side
+ * on internal side streams (one per projection, created once per device) forked
+ * from `stream` by an event and joined back into it, so the call stays ordered on
+ * `stream` and a CUDA graph capture records parallel branches; tlx_q5g8v11 does
+ * the same. */
 size_t tlx_aq3k8v11_workspace_bytes(int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, int x_dtype);
 int tlx_aq3k8v11(const void* wq, const void* wk, const void* wv, const uint32_t* grid, const void* x, int x_dtype,
                  int64_t ldx, int m, int64_t k, int64_t nq, int64_t nk, int64_t nv, void* q_out, void* k_out,
