@@ -513,3 +513,41 @@ def test_verify_step_pipeline_vs_oracle():
     check_rows(step.y.cpu().numpy(), y_ref, tight=1e-4)
     assert np.array_equal(step.out_idx.cpu().numpy(), idx_ref)
     assert step.accept_out.cpu().tolist() == list(oracle.accept(idx_ref, drafts_np))
+
+
+def test_verify_step_host_path_copies_every_call():
+    # step_host (H2D inputs, graph replay, D2H of the accept record and argmax ids)
+    # returns what the device path returns, and picks up new contents of the same
+    # pinned buffers on every call
+    from thunderllamax_b200.verify import VerifyShape, VerifyStep
+
+    rng = np.random.default_rng(7)
+    s = VerifyShape(dim=1024, ffn=2048, vocab=5003, rows=11)
+    w = {"gate": ops.pack_tiles("iq3_xxs", synth.iq3xxs_blocks(rng, s.ffn, s.dim), s.dim),
+         "up": ops.pack_tiles("iq3_xxs", synth.iq3xxs_blocks(rng, s.ffn, s.dim), s.dim),
+         "down": ops.pack_tiles("q6_k", synth.q6k_blocks(rng, s.dim, s.ffn), s.ffn)}
+    rh = synth.q6k_blocks(rng, s.vocab, s.dim)
+    w["head"] = ops.pack_tiles("q6_k", rh, s.dim)
+    step = VerifyStep(s, weights=w)
+    xp = torch.empty((s.rows, s.dim), dtype=torch.bfloat16).pin_memory()
+    hp = torch.empty_like(xp).pin_memory()
+    dp = torch.empty(s.n_drafts, dtype=torch.int32).pin_memory()
+    outp = torch.empty(2 + s.rows, dtype=torch.int32).pin_memory()
+    for trial in range(3):
+        x, _ = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+        h, h64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+        _, idx_ref, _ = oracle.head_argmax(h64, rh, "q6_k")
+        drafts_np = idx_ref[:s.n_drafts].copy()
+        drafts_np[trial + 2] = (drafts_np[trial + 2] + 1) % s.vocab
+        xp.copy_(x.cpu())
+        hp.copy_(h.cpu())
+        dp.copy_(torch.from_numpy(drafts_np))
+        step.step_host(xp, hp, dp, outp)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(outp[2:].numpy(), idx_ref)
+        assert outp[:2].tolist() == list(oracle.accept(idx_ref, drafts_np))
+        # the device path on the same inputs gives the same record
+        step.set_inputs(x, h, drafts=torch.from_numpy(drafts_np).cuda())
+        step.replay()
+        torch.cuda.synchronize()
+        assert step.accept_out.cpu().tolist() == outp[:2].tolist()
