@@ -942,8 +942,9 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
 // The projections run side by side: after the staging kernel the stream forks into
 // one side stream per projection (event record / wait, so a CUDA graph capture
 // turns them into parallel branches) and joins again.  Each GEMV gets a share of
-// the CTA budget in proportion to its weight bytes, so the small ones no longer
-// pay a full-grid launch of their own one after the other.
+// the CTA budget in proportion to the rows it decodes (the GEMVs are bound by
+// decode and issue, not by bytes; Q4_K rows count 1.47 times), so the small ones
+// no longer pay a full-grid launch of their own one after the other.
 static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
 
 static int projection_ctas(int n, const Projection* pr, int64_t k, int max_ctas, int i) {
@@ -951,7 +952,9 @@ static int projection_ctas(int n, const Projection* pr, int64_t k, int max_ctas,
   if (n <= 1) return total;
   double all = 0.0, mine = 0.0;
   for (int j = 0; j < n; ++j) {
-    const double b = static_cast<double>(pr[j].n_rows) * static_cast<double>(k / 256) * block_bytes(pr[j].qt);
+    // cost in IQ3_XXS-row equivalents (same k for all); the Q4_K factor is its byte
+    // ratio to IQ3_XXS (144 / 98), which measured best for the 1024-row v projection
+    const double b = static_cast<double>(pr[j].n_rows) * (pr[j].qt == QT_Q4_K ? 144.0 / 98.0 : 1.0);
     all += b;
     if (j == i) mine = b;
   }
