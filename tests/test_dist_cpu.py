@@ -192,3 +192,12 @@ def _prefill_worker(rank, world, port, q):
 def test_two_rank_tensor_parallel_prefill_equals_ffn():
     for rank, err in _spawn(_prefill_worker):
         assert err < 1e-12, (rank, err)
+
+
+def test_four_rank_expert_and_tensor_parallel_partitions():
+    # the same two sharded layers over four gloo ranks (the partitions at N = 4:
+    # a quarter of the experts, one 256-row block of the FFN per rank)
+    for rank, err in _spawn(_moe_worker, world=4):
+        assert err < 1e-12, ("moe", rank, err)
+    for rank, err in _spawn(_prefill_worker, world=4):
+        assert err < 1e-12, ("prefill", rank, err)
