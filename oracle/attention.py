@@ -48,7 +48,14 @@ def _norm_rope(v, w, ang):
 
 
 def _quant8(x):
-    """Per 32-dim group: scale = fp16(max|x| / 127) (1e-8 if zero), q = rint(x / scale)."""
+    """Per 32-dim group: scale = fp16(max|x| / 127), or fp16(1e-8) for an all-zero
+    group; byte = rint(clamp(x / scale, -127, 127)) + 128 (engine/spk_preqh.cu:77-83).
+
+    fp16(1e-8) is 0 (below the smallest fp16 subnormal), so an all-zero group divides
+    0 by 0.  The reference clamps with fmaxf / fminf, which return the non-NaN
+    operand: NaN -> fmaxf(NaN, -127) = -127 -> byte 1.  Likewise a non-zero group
+    whose scale underflows to 0 gives +-inf -> +-127 for its non-zero entries.
+    np.fmax / np.fmin have the same NaN rule."""
     q = np.empty(HD, dtype=np.uint8)
     s = np.empty(HD // 32, dtype=np.float16)
     for gi in range(HD // 32):
@@ -56,7 +63,9 @@ def _quant8(x):
         m = np.abs(seg).max()
         sc = np.float16(m / 127.0 if m > 0 else 1e-8)
         s[gi] = sc
-        qi = np.clip(np.rint(seg / np.float64(sc)), -127, 127).astype(np.int64)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            r = seg / np.float64(sc)
+        qi = np.rint(np.fmin(np.fmax(r, -127.0), 127.0)).astype(np.int64)
         q[gi * 32:(gi + 1) * 32] = (qi + 128).astype(np.uint8)
     return q, s
 

@@ -52,23 +52,24 @@ def dequant_q6k(raw: np.ndarray, k: int) -> np.ndarray:
     Weight i = 128h + 32j + l (h half, j quarter, l 0..31):
     q = ((ql[64h + 32(j&1) + l] >> 4(j>>1)) & 15) | (((qh[32h + l] >> 2j) & 3) << 4),
     w = (d * sc[i >> 4]) * (q - 32).  Reference engine/mm/MM_P2_ports.py:21-45
-    (``dq_q6_k``) and engine/mm/MM_P6_h6kam.cu:45-56.
+    (``dq_q6_k``) and engine/mm/MM_P6_h6kam.cu:45-56.  The index arithmetic is
+    done by reshapes: ql viewed as [h][j & 1][l] shifted by 4(j >> 1) gives the low
+    nibbles in weight order [h][j >> 1][j & 1][l] = [h][j][l]; qh viewed as [h][l]
+    shifted by 2j gives the high bits in [h][j][l].
     """
     n = raw.shape[0]
     nb = k // QK
     blk = np.ascontiguousarray(raw).reshape(n, nb, 210)
-    ql = blk[..., 0:128].astype(np.int32)
-    qh = blk[..., 128:192].astype(np.int32)
+    ql = blk[..., 0:128].reshape(n, nb, 2, 1, 2, 32)
+    qh = blk[..., 128:192].reshape(n, nb, 2, 1, 32)
+    lo = (ql >> np.array([0, 4], np.uint8).reshape(2, 1, 1)) & 15                # [n, nb, h, j>>1, j&1, l]
+    hi = (qh >> np.array([0, 2, 4, 6], np.uint8).reshape(4, 1)) & 3              # [n, nb, h, j, l]
+    q = (lo.reshape(n, nb, QK) | (hi.reshape(n, nb, QK) << 4)).view(np.int8) - np.int8(32)
     sc = blk[..., 192:208].view(np.int8).astype(np.float32)
     d = _f16(blk[..., 208:210])
-    i = np.arange(QK)
-    h, j, l = i >> 7, (i >> 5) & 3, i & 31
-    lo = (ql[..., 64 * h + 32 * (j & 1) + l] >> (4 * (j >> 1))) & 15
-    hi = (qh[..., 32 * h + l] >> (2 * j)) & 3
-    q = (lo | (hi << 4)) - 32                                          # [n, nb, 256]
     t = d[..., None] * sc                                              # [n, nb, 16] (d*sc first)
-    w = t[..., i >> 4] * q.astype(np.float32)
-    return w.reshape(n, k).astype(np.float32)
+    w = t[..., None] * q.reshape(n, nb, 16, 16).astype(np.float32)
+    return w.reshape(n, k)
 
 
 def dequant_iq4xs(raw: np.ndarray, k: int) -> np.ndarray:

@@ -185,3 +185,39 @@ def test_engine0_spk_programs():
     torch.cuda.synchronize()
     assert np.array_equal(kv_p.cpu().numpy(), kv_l)
     assert np.array_equal(ao.view(rows, 6144).cpu().numpy().view(np.int16), ao_l.view(np.int16))
+
+
+def test_attention_all_zero_groups():
+    # an all-zero 32-dim group quantises with scale fp16(1e-8) = 0; the reference's
+    # fmaxf / fminf clamp turns 0 / 0 into -127, byte 1 (engine/spk_preqh.cu:77-83).
+    # K head 1 is zero for every row (its RMS norm is then 0 as well) and V groups 0
+    # and 5 of head 2 are zero; the cache bytes must match the oracle (and the
+    # reference kernel, when its cubin is built) bit for bit, and decoding a cache
+    # with zero scales stays finite.
+    rows, ctx, pos = 11, REF_CTX, 700
+    rng = np.random.default_rng(31)
+    qrow, krow, vrow, qnw, knw = inputs(rng, rows)
+    krow[:, 256:512] = 0
+    vrow[:, 512:544] = 0
+    vrow[:, 512 + 160:512 + 192] = 0
+    kv, sc = random_cache(rng, ctx, pos)
+    qw16, kv_lib, sc_lib, ao = run_lib(rows, ctx, qrow, krow, vrow, qnw, knw, kv, sc, pos)
+    new = slice(pos, pos + rows)
+    assert (kv_lib[1, new] == 1).all() and (sc_lib[1, new] == 0).all()
+    assert (kv_lib[4 + 2, new, 0:32] == 1).all() and (kv_lib[4 + 2, new, 160:192] == 1).all()
+    kv_o, sc_o = kv.copy(), sc.copy()
+    oracle.attn_pre(qrow, krow, vrow, qnw, knw, oracle.rope_freqs(), pos, kv_o, sc_o)
+    assert np.array_equal(kv_lib[1, new], kv_o[1, new]) and np.array_equal(kv_lib[6, new], kv_o[6, new])
+    assert np.isfinite(ao.astype(np.float64)).all()
+    ref = oracle.attn_decode(qw16, kv_lib, sc_lib, qrow, pos)
+    check_rows(ao.astype(np.float64), ref, CONTRACT)
+    if refkernels.have("spk_pre11"):
+        q_t, k_t, v_t, qn_t, kn_t, fr_t = dev(qrow, krow, vrow, qnw, knw, oracle.rope_freqs())
+        kv_r, sc_r = dev(kv, sc)
+        pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        qw = torch.zeros((rows, 24, 256), dtype=torch.float32, device="cuda")
+        qw16_r = torch.zeros((rows, 24, 256), dtype=torch.float16, device="cuda")
+        refkernels.launch("spk_pre11", 24, 256, [q_t, k_t, v_t, qn_t, kn_t, fr_t, kv_r, sc_r, pos_t, qw, qw16_r])
+        torch.cuda.synchronize()
+        assert np.array_equal(kv_r.cpu().numpy(), kv_lib)
+        assert np.array_equal(sc_r.cpu().numpy().view(np.int16), sc_lib.view(np.int16))

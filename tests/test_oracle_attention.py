@@ -10,11 +10,23 @@ from oracle.attention import HD, _norm_rope, _quant8
 def test_quant8_round_trip():
     rng = np.random.default_rng(1)
     x = rng.standard_normal(HD) * 2.0
-    x[:32] = 0.0                                  # an all-zero group takes the 1e-8 scale
-    q, s = _quant8(x)
+    x[:32] = 0.0                                  # an all-zero group takes the fp16(1e-8) = 0 scale
+    with np.errstate(all="raise"):                # no undefined cast on the way
+        q, s = _quant8(x)
     back = (q.astype(np.float64) - 128) * np.repeat(s.astype(np.float64), 32)
     assert np.all(np.abs(back - x) <= np.repeat(s.astype(np.float64), 32) * 0.5 + 1e-12)
-    assert s[0] == np.float16(1e-8) and (q[:32] == 128).all()
+    # the reference kernel's 0 / 0 = NaN clamps to -127 through fmaxf (byte 1)
+    assert s[0] == np.float16(1e-8) == 0 and (q[:32] == 1).all()
+
+
+def test_quant8_underflowing_scale():
+    # a group whose max|x| / 127 underflows fp16: non-zero entries saturate, zeros
+    # go to byte 1 (0 / 0 -> NaN -> -127), exactly as the reference's clamp does
+    x = np.zeros(HD)
+    x[0], x[1] = 1e-7, -1e-7
+    q, s = _quant8(x)
+    assert s[0] == 0
+    assert q[0] == 255 and q[1] == 1 and (q[2:32] == 1).all()
 
 
 def test_rope_keeps_pair_norms():
