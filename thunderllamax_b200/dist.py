@@ -87,11 +87,12 @@ class ShardedVerifyStep:
         if self.n_ffn <= 0 or self.n_voc <= 0:
             raise ValueError(f"rank {rank} of {world} has an empty shard")
         if weights is None:
-            # synthetic shards: each rank draws its own seeded blocks of its shard shape
-            weights = {"gate": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 1),
-                       "up": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 2),
-                       "down": synth_tiled(s.down_q, s.dim, self.n_ffn, seed * 1000 + 10 * rank + 3),
-                       "head": synth_tiled(s.head_q, self.n_voc, s.dim, seed * 1000 + 10 * rank + 4)}
+            # this rank's slices of the ONE seeded model VerifyStep(seed) uses: gate/up
+            # rows [f0, f1), down columns [f0, f1), head rows [v0, v1)
+            weights = {"gate": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 1, rows=(self.f0, self.f1)),
+                       "up": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 2, rows=(self.f0, self.f1)),
+                       "down": synth_tiled(s.down_q, s.dim, s.ffn, seed + 3, cols=(self.f0, self.f1)),
+                       "head": synth_tiled(s.head_q, s.vocab, s.dim, seed + 4, rows=(self.v0, self.v1))}
         self.w = weights
         dev = "cuda"
         self.x = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
@@ -144,6 +145,36 @@ class ShardedVerifyStep:
         gather_keys(self.local_keys, self.all_keys, self.group)
         ops.argmax_merge(self.all_keys, out_max=self.out_max, out_idx=self.out_idx, drafts=self.drafts,
                          accept_out=self.accept_out)
+
+    COLLECTIVES = "NCCL all-reduce of the down partials + NCCL all-gather of the head keys"
+
+    def launch_allreduce(self):
+        allreduce_partial(self.y, self.group)
+
+    def launch_gather_merge(self):
+        gather_keys(self.local_keys, self.all_keys, self.group)
+        ops.argmax_merge(self.all_keys, out_max=self.out_max, out_idx=self.out_idx, drafts=self.drafts,
+                         accept_out=self.accept_out)
+
+    def phase_times(self, time_graph, graph_of, max_over_ranks, torch_mod, reps: int = 20, replays: int = 5):
+        """Device time (us, max over ranks) of each piece of the step alone, each
+        captured `reps` times back to back in its own graph: the three GEMVs, the
+        all-reduce, the key all-gather + merge, and the whole step; `gap` is the step
+        minus the sum of the pieces (launch ramps and waits between them)."""
+        out = {}
+        pieces = [("ffn_gate_up", self.launch_ffn_gate_up), ("ffn_down", self.launch_ffn_down),
+                  ("head_argmax", self.launch_head_argmax), ("allreduce_y", self.launch_allreduce),
+                  ("gather_merge_keys", self.launch_gather_merge)]
+        for name, fn in pieces:
+            g = graph_of(lambda fn=fn: [fn() for _ in range(reps)], torch_mod)
+            g.replay()
+            out[name] = round(max_over_ranks(time_graph(g.replay, replays, torch_mod) / reps) * 1000, 2)
+            del g
+        out["step"] = round(max_over_ranks(time_graph(self.replay, replays * reps, torch_mod)) * 1000, 2)
+        out["gap"] = round(out["step"] - sum(v for k, v in out.items() if k != "step"), 2)
+        parts = {k: v for k, v in out.items() if k not in ("step",)}
+        out["limiter"] = max(parts, key=parts.get)
+        return out
 
     def capture(self):
         stream = torch.cuda.Stream()
@@ -272,12 +303,13 @@ class ShardedPrefillFFN(_GraphStep):
         if self.n_ffn <= 0:
             raise ValueError(f"rank {rank} of {world} has an empty FFN shard")
         if weights is None:
-            weights = {"gate": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 1),
-                       "up": synth_tiled(s.ffn_q, self.n_ffn, s.dim, seed * 1000 + 10 * rank + 2),
-                       "down": synth_tiled(s.down_q, s.dim, self.n_ffn, seed * 1000 + 10 * rank + 3)}
+            # this rank's slices of the seeded model PrefillFFN(seed) uses
+            weights = {"gate": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 1, rows=(self.f0, self.f1)),
+                       "up": synth_tiled(s.ffn_q, s.ffn, s.dim, seed + 2, rows=(self.f0, self.f1)),
+                       "down": synth_tiled(s.down_q, s.dim, s.ffn, seed + 3, cols=(self.f0, self.f1))}
         self.w = weights
         self.x = torch.zeros((s.tokens, s.dim), dtype=torch.bfloat16, device="cuda")
-        self.act = torch.empty((s.tokens, self.n_ffn), dtype=torch.float16, device="cuda")
+        self.act = torch.empty((s.tokens, self.n_ffn), dtype=torch.float32, device="cuda")
         self.y = torch.empty((s.tokens, s.dim), dtype=torch.float32, device="cuda")
         self.ws = PrefillWorkspace(s.tokens, s.dim)
         self.ws_down = PrefillWorkspace(s.tokens, self.n_ffn)

@@ -102,6 +102,32 @@ BLOCK_GEN = {"iq3_xxs": iq3xxs_blocks, "q6_k": q6k_blocks, "iq4_xs": iq4xs_block
              "q5_k": q5k_blocks, "q8_0": q8_0_blocks}
 
 
+# Seeded matrices are drawn in row chunks of this many rows, each chunk from its own
+# generator (seed, chunk index): any row range of a model can be generated alone
+# (a rank's vocabulary shard, a sampled test row) and equals those rows of the whole.
+CHUNK_ROWS = 8192
+
+
+def chunk_rng(seed: int, chunk: int) -> np.random.Generator:
+    return np.random.default_rng(np.random.SeedSequence([int(seed), int(chunk)]))
+
+
+def matrix_rows(qtype: str, n_rows: int, k: int, seed: int, r0: int = 0, r1: int | None = None) -> np.ndarray:
+    """Rows [r0, r1) of the seeded synthetic (n_rows x k) GGUF matrix of `qtype`."""
+    r1 = n_rows if r1 is None else r1
+    if not 0 <= r0 <= r1 <= n_rows:
+        raise ValueError(f"rows [{r0}, {r1}) outside [0, {n_rows})")
+    out = np.empty((r1 - r0, row_bytes(qtype, k)), dtype=np.uint8)
+    if r1 == r0:
+        return out
+    for c in range(r0 // CHUNK_ROWS, (r1 - 1) // CHUNK_ROWS + 1):
+        c0, c1 = c * CHUNK_ROWS, min((c + 1) * CHUNK_ROWS, n_rows)
+        raw = BLOCK_GEN[qtype](chunk_rng(seed, c), c1 - c0, k)
+        a, b = max(c0, r0), min(c1, r1)
+        out[a - r0:b - r0] = raw[a - c0:b - c0]
+    return out
+
+
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even fp32 -> bf16, returned as uint16 bit patterns."""
     u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)

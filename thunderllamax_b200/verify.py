@@ -53,18 +53,27 @@ class VerifyShape:
                 "head_argmax": wb["head"] + r * d * 2 + r * 8}
 
 
-def synth_tiled(qtype: str, n_rows: int, k: int, seed: int, chunk_rows: int = 8192) -> torch.Tensor:
-    """Seeded synthetic GGUF blocks, generated in row chunks and repacked on the
-    device straight into one tiled buffer (no full-size host copy)."""
-    out = torch.empty(ops.tiled_bytes(qtype, n_rows, k), dtype=torch.uint8, device="cuda")
-    rng = np.random.default_rng(seed)
-    per_tile = ops.tiled_bytes(qtype, 16, k)
-    chunk_rows -= chunk_rows % 16
-    for r0 in range(0, n_rows, chunk_rows):
-        n = min(chunk_rows, n_rows - r0)
-        raw = synth.BLOCK_GEN[qtype](rng, n, k)
-        t = ops.pack_tiles(qtype, raw, k)
-        off = (r0 // 16) * per_tile
+def synth_tiled(qtype: str, n_rows: int, k: int, seed: int, rows: tuple[int, int] | None = None,
+                cols: tuple[int, int] | None = None) -> torch.Tensor:
+    """The seeded synthetic (n_rows x k) GGUF matrix (synth.matrix_rows), or its row
+    range `rows` / column range `cols` (multiples of 256: a k shard), repacked on
+    the device into one tiled buffer, one 8192-row chunk at a time."""
+    r0, r1 = rows if rows is not None else (0, n_rows)
+    k0, k1 = cols if cols is not None else (0, k)
+    if k0 % synth.QK or k1 % synth.QK or not 0 <= k0 < k1 <= k:
+        raise ValueError(f"column range [{k0}, {k1}) is not a 256-aligned part of [0, {k})")
+    kk = k1 - k0
+    bb = synth.BLOCK_BYTES[qtype]           # bytes per 256 weights of a row
+    out = torch.empty(ops.tiled_bytes(qtype, r1 - r0, kk), dtype=torch.uint8, device="cuda")
+    per_tile = ops.tiled_bytes(qtype, 16, kk)
+    step = synth.CHUNK_ROWS
+    for a in range(r0, r1, step):
+        b = min(a + step - (a % step), r1)
+        raw = synth.matrix_rows(qtype, n_rows, k, seed, a, b)
+        if cols is not None:
+            raw = np.ascontiguousarray(raw[:, (k0 // synth.QK) * bb:(k1 // synth.QK) * bb])
+        t = ops.pack_tiles(qtype, raw, kk)
+        off = ((a - r0) // 16) * per_tile
         out[off:off + t.numel()].copy_(t)
     return out
 
