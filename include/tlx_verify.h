@@ -163,12 +163,20 @@ int tlx_head_argmax(int qtype, const void* w, const uint32_t* grid, const void* 
  * capture); every call clears the array's counters on `stream` and allocates
  * nothing.  All calls share the one array: calls that can overlap on the GPU
  * (different streams, concurrent graphs) race and must be serialised by the
- * caller. */
+ * caller.  The grid follows tlx_set_max_ctas like tlx_head_argmax's.  The array's
+ * address is looked up once per device and kept: a cudaDeviceReset (or any other
+ * reset of the device's primary context) is not supported afterwards. */
 #define TLX_NOALLOC_SCRATCH_BYTES (24u << 20)
 int tlx_head_argmax_noalloc(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
                             int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
                             uint64_t* out_keys, const int32_t* drafts, int n_drafts, int32_t* accept_out,
                             void* stream);
+/* The error word of the last tlx_head_argmax_noalloc call on the current device
+ * (what tlx_workspace_error reports for the regular entry point): 0 = fine,
+ * TLX_WS_ERR_MBAR_TIMEOUT = a bounded wait gave up and the call's outputs are not
+ * valid.  Read it before the next call on that device, which clears it.  Waits for
+ * `stream`.  No reference counterpart. */
+int tlx_head_argmax_noalloc_error(uint32_t* err_out, void* stream);
 
 /* ---- argmax over materialised logits (amx3 / h_argmax) -----------------------------
  * amds[t] = argmax_v logits[t*ld + v] (fp32 or fp16 logits): the reference scan
@@ -331,10 +339,15 @@ int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, in
  * dequantised to fp16 in shared memory (one fp16 rounding per weight: the exact
  * integer part times the block scale), tokens staged as fp16 by TMA, fp32
  * accumulators in tensor memory.  n_rows % 128 == 0, k % 256 == 0, any m >= 1;
- * x is bf16 (converted to fp16 in the workspace) or fp16 (ldx % 8 == 0).
- * The workspace (tlx_prefill_workspace_bytes) holds a device error word (zero it
- * once) and the fp16 copy of bf16 tokens.
- * act[t][r] = fp16(silu((Wg x_t)[r]) * (Wu x_t)[r]) for IQ3_XXS gate/up, and
+ * x is fp16, bf16 or fp32 (ldx % 8 == 0).  bf16 and fp32 rows are staged to fp16 in
+ * the workspace with a power-of-two scale per token row, so that rows beyond the
+ * fp16 range (max |x| >= 2^15) are carried with one fp16 rounding (none for bf16);
+ * the epilogue multiplies the scale back.  The workspace
+ * (tlx_prefill_workspace_bytes) holds a device error word (zero it once), the fp16
+ * copy of the tokens and their scales.
+ * act[t][r] = silu((Wg x_t)[r]) * (Wu x_t)[r] in fp32 for IQ3_XXS gate/up (fp32: the
+ * product of two large projections can exceed the fp16 range; the down GEMM reads
+ * it back through the scaled staging), and
  * y[t][r] = (W x_t)[r] (fp32) for Q6_K W (the down projection); other formats
  * return TLX_ERR_QTYPE.  Replaces pf_gemm3 / pf_gemm3m
  * (engine/pf_gemm3.cu:4-26, :219; engine/pf_gemm3m.cu:184-229). */

@@ -2,7 +2,8 @@
 down) against the numpy oracle on identical seeded inputs, through the C ABI.
 
 The kernels round every dequantised weight to fp16 once (integer part times the
-block scale) and the gate/up output to fp16; tokens are exact in fp16.  Contract:
+block scale); the gate/up act is fp32, and bf16 / fp32 tokens are staged to fp16
+with a power-of-two scale per row (one fp16 rounding, none for bf16).  Contract:
 max|err| <= 2e-3 * ||row||_2 per token row of the float64 oracle; a tighter
 1e-3 bound (about two fp16 roundings of the largest products) is asserted too."""
 import numpy as np
@@ -98,3 +99,29 @@ def test_prefill_rejects_unsupported_formats():
         prefill.gemm("iq3_xxs", w, x, 128, ws)          # single-matrix path is Q6_K
     with pytest.raises(_lib.TLXError):
         prefill.gate_up("q6_k", w, w, x, 128, ws)       # gate/up path is IQ3_XXS
+
+
+def test_prefill_gemm_rows_beyond_fp16_range():
+    # bf16 and fp32 rows whose values exceed the fp16 range (the gate/up act of
+    # large-weight inputs does): staged with a power-of-two scale per row, multiplied
+    # back in the epilogue; a row inside the fp16 range keeps scale 1
+    rng = np.random.default_rng(91)
+    m, n, k = 40, 256, 1024
+    raw = synth.q6k_blocks(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= (10.0 ** rng.uniform(-2, 7, m)).astype(np.float32)[:, None]   # row scales 1e-2 .. 1e7
+    x[0] *= 0
+    bits = synth.f32_to_bf16_bits(x)
+    w = ops.pack_tiles("q6_k", raw, k)
+    W = oracle.dequant("q6_k", raw, k)
+    for x_t, x64 in ((torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16),
+                      synth.bf16_bits_to_f32(bits).astype(np.float64)),
+                     (torch.from_numpy(x).cuda(), x.astype(np.float64))):
+        ws = prefill.PrefillWorkspace(m, k)
+        y = prefill.gemm("q6_k", w, x_t, n, ws)
+        torch.cuda.synchronize()
+        assert ws.error() == 0
+        got = y.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert np.array_equal(got[0], np.zeros(n, np.float32))
+        check_rows(got[1:], oracle.matvec_f64(W, x64)[1:], TIGHT)

@@ -1,6 +1,6 @@
 // Prefill-sized FFN contraction (many tokens) on the 5th-generation tensor cores.
 //
-//   act[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r]   IQ3_XXS gate and up, fp16 act
+//   act[t][r] = silu(Wg x_t)[r] * (Wu x_t)[r]   IQ3_XXS gate and up, fp32 act
 //   y[t][r]   = (W x_t)[r]                      Q6_K (the down projection), fp32 y
 //
 // The GEMM is computed transposed, D[row][token] = W . X^T, so the dequantised
@@ -27,6 +27,7 @@
 // engine/pf_gemm3.cu:4-26, :219 and engine/pf_gemm3m.cu:184-229 (IQ3 dequant to
 // fp16 shared memory, mma.sync m16n8k16, SiLU epilogue).
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -259,8 +260,9 @@ struct PrefillParams {
   const uint8_t* w1;   // tiled up weights (gate/up mode)
   const uint32_t* grid;
   int M, N, K;         // tokens, weight rows, k
-  void* out;           // fp16 act [M][ldo] (gate/up) or fp32 y [M][ldo]
+  void* out;           // fp32 act [M][ldo] (gate/up) or fp32 y [M][ldo]
   int64_t ldo;
+  const float* row_scale;  // per-token power-of-two scale of the staged tokens (nullptr: 1)
   uint32_t* err;
 };
 
@@ -415,9 +417,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
           for (int j = 0; j < 16; ++j) {
             const int tok = tt * kPfTok + c0 + j;
             if (tok < p.M) {
-              const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-              const float a = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
-              static_cast<__half*>(p.out)[tok * p.ldo + row] = __float2half_rn(a);
+              const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
+              const float gv = __uint_as_float(g[j]) * sc, uv = __uint_as_float(u[j]) * sc;
+              static_cast<float*>(p.out)[tok * p.ldo + row] = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
             }
           }
         } else {
@@ -425,7 +427,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int tok = tt * kPfTok + c0 + j;
-            if (tok < p.M) static_cast<float*>(p.out)[tok * p.ldo + row] = __uint_as_float(g[j]);
+            if (tok < p.M) {
+              const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
+              static_cast<float*>(p.out)[tok * p.ldo + row] = __uint_as_float(g[j]) * sc;
+            }
           }
         }
       }
@@ -510,23 +515,66 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   }
 }
 
-// ---- bf16 -> fp16 token staging (exact for |x| in the fp16 normal range) ----
-__global__ void to_f16_kernel(const uint16_t* __restrict__ x, int64_t ldx, int M, int K, __half* __restrict__ out) {
+// ---- bf16 / fp32 -> fp16 token staging with a power-of-two scale per token row ----
+// Rows can hold values beyond the fp16 range (the fp32 gate/up act of large-weight
+// inputs does).  One CTA per row: max |x| over the row, then s = max(0, E - 14) for
+// max |x| in [2^E, 2^(E+1)), and the row is stored as fp16(x * 2^-s): a single fp16
+// rounding (none for bf16, whose 8 significant bits fit), with the scaled values
+// below 2^15; only entries more than 2^28 times smaller than the row's maximum lose
+// bits as fp16 subnormals.  row_scale[t] = 2^s, which the GEMM epilogue multiplies
+// back.  Rows whose maximum fits fp16 get s = 0 (the plain conversion).
+template <bool F32>
+__global__ void __launch_bounds__(256) to_f16_kernel(const void* __restrict__ xv, int64_t ldx, int M, int K,
+                                                     __half* __restrict__ out, float* __restrict__ row_scale) {
   griddep_wait();
   griddep_launch_dependents();
-  const int64_t per = K >> 3;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < static_cast<int64_t>(M) * per;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = i / per, k8 = i - t * per;
-    const uint4 v = *reinterpret_cast<const uint4*>(x + t * ldx + 8 * k8);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
+  __shared__ uint32_t red[8];
+  const int per = K >> 3;  // 8 values per step
+  for (int t = blockIdx.x; t < M; t += gridDim.x) {
+    // 8 values of the row as fp32
+    auto load8 = [&](int i, float (&v)[8]) {
+      if constexpr (F32) {
+        const float4* r = reinterpret_cast<const float4*>(static_cast<const float*>(xv) + t * ldx + 8 * i);
+        const float4 a = r[0], b = r[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xv) + t * ldx + 8 * i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
-      o[j] = h2_bits(h);
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = __uint_as_float(w[j] << 16);
+          v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+      }
+    };
+    uint32_t mx = 0;  // max |x| as fp32 magnitude bits (monotone; inf / NaN compare highest)
+    for (int i = threadIdx.x; i < per; i += blockDim.x) {
+      float v[8];
+      load8(i, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = max(mx, __float_as_uint(v[j]) & 0x7FFFFFFFu);
     }
-    *reinterpret_cast<uint4*>(out + t * K + 8 * k8) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = max(mx, red[w]);
+    __syncthreads();
+    const int e = static_cast<int>(mx >> 23) - 127;               // unbiased exponent of max |x|
+    const int sh = (mx < 0x7F800000u && e > 14) ? e - 14 : 0;    // inf / NaN rows: no scale
+    const float down = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);   // 2^-sh
+    if (threadIdx.x == 0) row_scale[t] = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
+    __half* orow = out + static_cast<int64_t>(t) * K;
+    for (int i = threadIdx.x; i < per; i += blockDim.x) {
+      float v[8];
+      load8(i, v);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = h2_bits(__floats2half2_rn(v[2 * j] * down, v[2 * j + 1] * down));
+      *reinterpret_cast<uint4*>(orow + 8 * i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
@@ -607,9 +655,15 @@ bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
 }  // namespace
 
-size_t prefill_x_bytes(int m, int64_t k) { return static_cast<size_t>(m) * static_cast<size_t>(k) * 2; }
+// workspace after the error word: the fp16 tokens, then one float scale per token
+size_t prefill_x_bytes(int m, int64_t k) {
+  return ((static_cast<size_t>(m) * static_cast<size_t>(k) * 2 + 255) & ~size_t(255)) + static_cast<size_t>(m) * 4;
+}
+size_t prefill_scale_offset(int m, int64_t k) {
+  return (static_cast<size_t>(m) * static_cast<size_t>(k) * 2 + 255) & ~size_t(255);
+}
 
-// act[m][n_rows] (fp16) = silu(Wg x) * (Wu x), or y[m][n_rows] (fp32) = W x
+// act[m][n_rows] (fp32) = silu(Wg x) * (Wu x), or y[m][n_rows] (fp32) = W x
 int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x,
                 int x_dtype, int64_t ldx, int m, int64_t n_rows, int64_t k, void* out, int64_t ldo, void* ws,
                 size_t ws_bytes, uint32_t* err, int max_ctas, cudaStream_t stream) {
@@ -624,20 +678,23 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   if (!al16(w0) || (w1 && !al16(w1)) || !al16(x)) return TLX_ERR_ALIGN;
   const void* xf16 = x;
   int64_t ldx16 = ldx;
-  if (x_dtype == DT_BF16) {
+  const float* row_scale = nullptr;
+  if (x_dtype == DT_BF16 || x_dtype == DT_F32) {
     if (!ws || ws_bytes < prefill_x_bytes(m, k)) return TLX_ERR_WORKSPACE;
     if (ldx < k || ldx % 8 || !al16(ws)) return TLX_ERR_ALIGN;
-    const int64_t groups = static_cast<int64_t>(m) * (k / 8);
-    const int blocks = static_cast<int>(groups / 256 + 1 < 4096 ? groups / 256 + 1 : 4096);
-    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    const int blocks = m < 65536 ? m : 65536;
+    const void* xb = x;
     int mm = m, kk = static_cast<int>(k);
     __half* o = static_cast<__half*>(ws);
-    void* args[] = {&xb, &ldx, &mm, &kk, &o};
-    const int rc = launch_pdl_raw(reinterpret_cast<const void*>(to_f16_kernel), dim3(blocks), dim3(256), 0, stream,
-                                  args);
+    float* sc = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + prefill_scale_offset(m, k));
+    void* args[] = {&xb, &ldx, &mm, &kk, &o, &sc};
+    const void* kern = x_dtype == DT_F32 ? reinterpret_cast<const void*>(to_f16_kernel<true>)
+                                         : reinterpret_cast<const void*>(to_f16_kernel<false>);
+    const int rc = launch_pdl_raw(kern, dim3(blocks), dim3(256), 0, stream, args);
     if (rc) return rc;
     xf16 = ws;
     ldx16 = k;
+    row_scale = sc;
   } else if (x_dtype == DT_F16) {
     if (ldx < k || ldx % 8) return TLX_ERR_ALIGN;
   } else {
@@ -654,6 +711,7 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   p.K = static_cast<int>(k);
   p.out = out;
   p.ldo = ldo;
+  p.row_scale = row_scale;
   p.err = err;
   if (gate_up) return launch_prefill<QT_IQ3_XXS, 2>(map, p, max_ctas, stream);
   return launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, stream);

@@ -1,6 +1,6 @@
 """Prefill-sized FFN contraction on the tcgen05 tensor cores.
 
-    act = silu(X Wg^T) * (X Wu^T)     IQ3_XXS 5120 -> 17408, fp16 act
+    act = silu(X Wg^T) * (X Wu^T)     IQ3_XXS 5120 -> 17408, fp32 act
     Y   = act Wd^T                    Q6_K 17408 -> 5120, fp32
 
 for 2048 tokens: the reference's prefill GEMM pool (engine/pf_gemm3.cu,
@@ -34,7 +34,7 @@ class PrefillShape:
 
 
 class PrefillWorkspace:
-    """Device error word + fp16 staging of bf16 tokens (zeroed once)."""
+    """Device error word + fp16 staging of bf16 tokens and their per-row scales (zeroed once)."""
 
     def __init__(self, m: int, k: int, device="cuda"):
         nb = int(_lib.lib().tlx_prefill_workspace_bytes(m, k))
@@ -55,18 +55,22 @@ def _x_args(x: torch.Tensor):
         return TLX_DT_BF16
     if x.dtype == torch.float16:
         return TLX_DT_F16
-    raise TLXError(f"prefill tokens are bf16 or fp16, not {x.dtype}")
+    if x.dtype == torch.float32:
+        return _lib.TLX_DT_F32
+    raise TLXError(f"prefill tokens are bf16, fp16 or fp32, not {x.dtype}")
 
 
 def gate_up(qtype, w_gate: torch.Tensor, w_up: torch.Tensor, x: torch.Tensor, n_rows: int, ws: PrefillWorkspace,
             act: torch.Tensor = None) -> torch.Tensor:
-    """act[t][r] = fp16(silu((Wg x_t)[r]) * (Wu x_t)[r]); weights tiled (ops.pack_tiles)."""
+    """act[t][r] = silu((Wg x_t)[r]) * (Wu x_t)[r] in fp32; weights tiled (ops.pack_tiles).  fp32 because the
+    product of two large projections can leave the fp16 range; gemm() stages it back to fp16 with a
+    power-of-two scale per row."""
     ops.require_device()
     q = ops.qtype_id(qtype)
     dt = _x_args(x)
     m, k = x.shape
     if act is None:
-        act = torch.empty((m, n_rows), dtype=torch.float16, device=x.device)
+        act = torch.empty((m, n_rows), dtype=torch.float32, device=x.device)
     g = ops.grid(str(x.device)) if q == _lib.TLX_IQ3_XXS else None
     rc = _lib.lib().tlx_prefill_ffn_gate_up(q, ops._ptr(w_gate), ops._ptr(w_up), ops._ptr(g), ops._ptr(x), dt,
                                             x.stride(0), m, n_rows, k, ops._ptr(act), act.stride(0),
@@ -106,7 +110,7 @@ class PrefillFFN:
             "down": synth_tiled(s.down_q, s.dim, s.ffn, seed + 3),
         }
         self.x = torch.zeros((s.tokens, s.dim), dtype=torch.bfloat16, device="cuda")
-        self.act = torch.empty((s.tokens, s.ffn), dtype=torch.float16, device="cuda")
+        self.act = torch.empty((s.tokens, s.ffn), dtype=torch.float32, device="cuda")
         self.y = torch.empty((s.tokens, s.dim), dtype=torch.float32, device="cuda")
         self.ws = PrefillWorkspace(s.tokens, s.dim)
         self.ws_down = PrefillWorkspace(s.tokens, s.ffn)
