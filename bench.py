@@ -48,150 +48,227 @@ def measured_peak():
 
 # ------------------------------------------------------------------ clocks ----
 class ClockSampler:
+    """SM clock, power and clock-event reasons of this rank's GPU, sampled from a
+    background thread while the timed legs run.  NVML (nvidia_ml_py) is polled every
+    2 ms, so even a few-millisecond timed region gets samples; without NVML,
+    ``nvidia-smi -lms 50`` is read instead.  Read-only: no GPU setting is touched."""
+
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
+        self.gpu, self.period = gpu_index, period_s
+        self.proc, self.samples, self.stop = None, [], threading.Event()
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        p = torch.cuda.get_device_properties(self.gpu)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _poll_nvml(self, nv, hd):
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(hd, nv.NVML_CLOCK_SM))
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(hd, nv.NVML_CLOCK_SM)), mx,
+                                     nv.nvmlDeviceGetPowerUsage(hd) / 1000.0, int(get_reasons(hd))))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def _read_smi(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            try:
+                bits = sum(self.REASONS[nm] for nm, v in zip(("hw_slowdown", "hw_thermal_slowdown",
+                                                              "sw_thermal_slowdown", "sw_power_cap"), parts[5:9])
+                           if v.lower() == "active")
+                self.samples.append((float(parts[1]), float(parts[2]), float(parts[3]), bits))
+            except (ValueError, IndexError):
+                continue
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            nv, hd = self._nvml_handle()
+            self.t = threading.Thread(target=self._poll_nvml, args=(nv, hd), daemon=True)
+            self.source = "nvml, 2 ms"
         except Exception:
-            self.proc = None
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                              "--format=csv,noheader,nounits", "-lms", "50"],
+                                             stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.t = threading.Thread(target=self._read_smi, daemon=True)
+                self.source = "nvidia-smi, 50 ms"
+            except Exception:
+                return self
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.source is not None:
+            self.t.join(timeout=5)
 
     def summary(self):
-        if not self.lines:
+        if not self.samples:
             return None
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted(nm for nm, bit in self.REASONS.items() if any(s[3] & bit for s in self.samples))
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": max(s[1] for s in self.samples),
+                "power_w_max": round(max(s[2] for s in self.samples), 1), "reasons": reasons,
+                "samples": len(self.samples), "source": self.source,
+                "window": "the timed step replays, the per-kernel graphs and the end-to-end steps"}
 
 
 # ------------------------------------------------------------- CPU port ------
-def _cpu_chunk(args):
-    """Oracle dequant + float64 matvec of one seeded chunk (runs in a worker)."""
-    qtype, n_rows, k, m, seed = args
+# The verify step on host cores: the reference's numpy path, restated by the oracle
+# package (GGUF blocks dequantised to fp32 as engine/pack_w4.py:39-69 and
+# engine/mm/MM_P2_ports.py:21-45 do, then an fp32 matmul, ``W.astype(f32) @ xh`` of
+# lineage/a3a/a3a_bench.py:176).  Every matrix is split by rows over worker
+# processes; each worker generates its own rows of the seeded model once
+# (synth.matrix_rows, the rows the GPU arm packs) and keeps them.  One step is the
+# whole workload, nothing scaled or extrapolated:
+#   phase 1  gate/up rows -> act = silu(g) * u;  head rows -> per-token (max, row)
+#   phase 2  down rows over the full act, + residual
+# then the host merges the head's (max, row) pairs (strict >, lowest row on ties,
+# as engine/amx3.cu:124-128) and runs greedy accept (engine/accept11k.cu:25-36).
+
+DEQUANT_ROWS = 2048          # rows dequantised at a time (bounded fp32 temporaries)
+
+
+def _matrices(dims, seed):
+    """name -> (qtype, n_rows, k, seed) of VerifyStep(seed)'s model."""
+    dim, ffn, vocab, ffn_q, down_q, head_q = dims
+    return {"gate": (ffn_q, ffn, dim, seed + 1), "up": (ffn_q, ffn, dim, seed + 2),
+            "down": (down_q, dim, ffn, seed + 3), "head": (head_q, vocab, dim, seed + 4)}
+
+
+def _cpu_worker(conn, dims, seed, mine):
+    """One host process of CpuVerifyStep: owns rows mine[name] = (r0, r1) of each matrix."""
     from threadpoolctl import threadpool_limits
 
     import oracle
     from thunderllamax_b200 import synth
 
+    mats = _matrices(dims, seed)
+    raw = {nm: synth.matrix_rows(q, n, k, sd, *mine[nm]) for nm, (q, n, k, sd) in mats.items()}
+
+    def matmul_rows(nm, x):
+        """[rows of mine][tokens] = W[rows] @ x^T in fp32, dequantising DEQUANT_ROWS at a time."""
+        q, _, k, _ = mats[nm]
+        r = raw[nm]
+        out = np.empty((r.shape[0], x.shape[0]), dtype=np.float32)
+        for a in range(0, r.shape[0], DEQUANT_ROWS):
+            W = oracle.dequant(q, r[a:a + DEQUANT_ROWS], k)
+            out[a:a + W.shape[0]] = W @ x.T
+        return out
+
+    conn.send("ready")
     with threadpool_limits(1):
-        rng = np.random.default_rng(seed)
-        raw = synth.BLOCK_GEN[qtype](rng, n_rows, k)
-        x = rng.standard_normal((m, k)).astype(np.float32)
-        t0 = time.perf_counter()
-        W = oracle.dequant(qtype, raw, k)
-        y = oracle.matvec_f64(W, x)
-        if qtype == "q6_k" and n_rows > 1:
-            oracle.argmax_rows(y)
-        dt = time.perf_counter() - t0
-    return raw.nbytes, dt
+        while True:
+            msg = conn.recv()
+            if msg[0] == "stop":
+                break
+            if msg[0] == "phase1":
+                x, h = msg[1], msg[2]
+                g, u = matmul_rows("gate", x), matmul_rows("up", x)
+                with np.errstate(over="ignore"):                                  # exp(-g) -> inf: act -> -0
+                    act = (g / (np.float32(1) + np.exp(-g))) * u               # [rows][tokens]
+                lg = matmul_rows("head", h)                                       # [rows][tokens]
+                best = np.argmax(lg, axis=0)                                      # first (lowest) row of the max
+                conn.send((act, lg[best, np.arange(lg.shape[1])], best + mine["head"][0]))
+            elif msg[0] == "phase2":
+                conn.send(matmul_rows("down", msg[1]))
 
 
-def _plan(shape):
-    return [("gate", shape.ffn_q, shape.ffn, shape.dim), ("up", shape.ffn_q, shape.ffn, shape.dim),
-            ("down", shape.down_q, shape.dim, shape.ffn), ("head", shape.head_q, shape.vocab, shape.dim)]
+class CpuVerifyStep:
+    """The K=11 verify step on `procs` host processes (one thread each)."""
 
+    def __init__(self, shape, seed: int, procs: int):
+        import multiprocessing as mp
 
-class CpuPort:
-    """The oracle port timed on host cores: per matrix of the step, seeded chunks
-    of rows are dequantised and multiplied (f64) in worker processes; the per-core
-    throughput of each matrix is extrapolated to the full step by bytes."""
+        self.shape, self.procs = shape, max(1, int(procs))
+        dims = (shape.dim, shape.ffn, shape.vocab, shape.ffn_q, shape.down_q, shape.head_q)
+        mats = _matrices(dims, seed)
+        split = {nm: [((n * i) // self.procs, (n * (i + 1)) // self.procs) for i in range(self.procs)]
+                 for nm, (_, n, _, _) in mats.items()}
+        ctx = mp.get_context("spawn")
+        self.conns, self.workers = [], []
+        for i in range(self.procs):
+            a, b = ctx.Pipe()
+            w = ctx.Process(target=_cpu_worker, args=(b, dims, seed, {nm: split[nm][i] for nm in split}), daemon=True)
+            w.start()
+            self.conns.append(a)
+            self.workers.append(w)
+        for c in self.conns:
+            if c.recv() != "ready":
+                raise RuntimeError("CPU worker failed to start")
 
-    def __init__(self, shape, procs: int, rows_per_job: int = 128):
-        self.shape, self.procs, self.rows = shape, max(1, procs), rows_per_job
-        self.ex = None
-        if self.procs > 1:
-            from concurrent.futures import ProcessPoolExecutor
-            import multiprocessing as mp
-
-            self.ex = ProcessPoolExecutor(self.procs, mp_context=mp.get_context("spawn"))
-        self.acc = {}
-        self.jobs_done = 0
-        self.wall = 0.0
-        self.sample_bytes = 0
-
-    def run(self, n_jobs: int, seed0: int = 0):
-        """One bounded step: n_jobs chunks spread over the four matrices by bytes."""
-        wb = self.shape.weight_bytes()
-        plan = _plan(self.shape)
-        total = sum(wb.values())
-        jobs = []
-        for i in range(n_jobs):
-            # deterministic byte-proportional choice of the matrix
-            pos = ((i + 0.5) / n_jobs) * total
-            for name, q, n, k in plan:
-                if pos < wb[name]:
-                    break
-                pos -= wb[name]
-            jobs.append((name, (q, self.rows, k, self.shape.rows, seed0 + i)))
-        t0 = time.perf_counter()
-        if self.ex is not None:
-            res = list(self.ex.map(_cpu_chunk, [a for _, a in jobs]))
-        else:
-            res = [_cpu_chunk(a) for _, a in jobs]
-        wall = time.perf_counter() - t0
-        self.wall += wall
-        for (name, _), (b, dt) in zip(jobs, res):
-            bb, tt = self.acc.get(name, (0, 0.0))
-            self.acc[name] = (bb + b, tt + dt)
-            self.sample_bytes += b
-        self.jobs_done += len(jobs)
-        return wall
-
-    def rate(self):
-        wb = self.shape.weight_bytes()
-        known = {nm: v for nm, v in self.acc.items() if v[1] > 0}
-        mean_rate = sum(v[0] for v in known.values()) / sum(v[1] for v in known.values())
-        core_s = sum(wb[nm] / (known[nm][0] / known[nm][1] if nm in known else mean_rate) for nm in wb)
-        step_s = core_s / self.procs
-        return sum(wb.values()) / step_s / 1e9, step_s * 1e6
-
-    def sample_text(self):
-        return (f"{self.sample_bytes / 1e6:.1f} MB of seeded GGUF blocks in {self.jobs_done} chunks of {self.rows} "
-                f"rows spread over gate/up/down/head by bytes; oracle dequant + f64 matvec (+argmax) on "
-                f"{self.procs} process(es), {self.wall:.1f} s wall; per-matrix core throughput extrapolated to "
-                f"the full step by bytes")
+    def step(self, x, h, res, drafts):
+        """x, h [tokens][dim] fp32 (the bf16 rows), res [tokens][dim] fp32, drafts int32.
+        Returns (y [tokens][dim], ids [tokens], (m, bonus))."""
+        for c in self.conns:
+            c.send(("phase1", x, h))
+        parts = [c.recv() for c in self.conns]
+        act = np.concatenate([p[0] for p in parts], axis=0).T.copy()            # [tokens][ffn]
+        for c in self.conns:
+            c.send(("phase2", act))
+        y = np.concatenate([c.recv() for c in self.conns], axis=0).T + res
+        best_v = np.full(x.shape[0], -np.inf, dtype=np.float32)
+        best_i = np.zeros(x.shape[0], dtype=np.int64)
+        for _, v, i in parts:                                                      # workers in row order
+            take = v > best_v
+            best_v = np.where(take, v, best_v)
+            best_i = np.where(take, i, best_i)
+        m = 0
+        while m < len(drafts) and best_i[m] == drafts[m]:
+            m += 1
+        return y, best_i, (m, int(best_i[m]))
 
     def close(self):
-        if self.ex is not None:
-            self.ex.shutdown()
+        for c in self.conns:
+            try:
+                c.send(("stop",))
+            except Exception:
+                pass
+        for w in self.workers:
+            w.join(timeout=10)
+
+
+def _cpu_inputs(shape, seed=1234):
+    """The GPU arm's step inputs (same seeds), as fp32 host arrays."""
+    from thunderllamax_b200 import synth
+
+    rng = np.random.default_rng(seed)
+    x = synth.bf16_bits_to_f32(synth.bf16_normal(rng, (shape.rows, shape.dim)))
+    h = synth.bf16_bits_to_f32(synth.bf16_normal(rng, (shape.rows, shape.dim)))
+    return x, h, np.zeros((shape.rows, shape.dim), np.float32)
+
+
+def time_cpu_steps(cpu, shape, warmup, steps, drafts=None):
+    """Mean wall time (s) of `steps` whole CPU verify steps after `warmup` ones."""
+    x, h, res = _cpu_inputs(shape)
+    drafts = np.zeros(shape.n_drafts, np.int32) if drafts is None else drafts
+    for _ in range(warmup):
+        cpu.step(x, h, res, drafts)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out = cpu.step(x, h, res, drafts)
+    return (time.perf_counter() - t0) / max(1, steps), out
 
 
 # ------------------------------------------------------------- helpers -------
@@ -206,6 +283,17 @@ def emit(obj):
     print(json.dumps(obj), flush=True)
 
 
+WORKLOAD = ("K=11 verify step: IQ3_XXS gate/up 17408x5120 (+SiLU) -> Q6_K down 5120x17408 -> Q6_K head "
+            "151936x5120 fused argmax + greedy accept")
+
+
+def bench_config(shape, ws):
+    """The `config` both arms print (identical keys and values for the same run)."""
+    return {"workload": WORKLOAD, "rows": shape.rows, "ffn": shape.ffn, "vocab": shape.vocab,
+            "weight_bytes_per_step": sum(shape.weight_bytes().values()),
+            "parallelism": f"tp{ws}" if ws > 1 else "single"}
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     from thunderllamax_b200.verify import VerifyShape
@@ -214,25 +302,24 @@ def run_reference(args):
     if rank != 0:
         return 0
     procs = os.cpu_count() or 1
-    port = CpuPort(shape, procs)
-    for i in range(args.warmup):
-        port.run(procs, seed0=10_000 * (i + 1))
-    port.acc, port.sample_bytes, port.jobs_done, port.wall = {}, 0, 0, 0.0
-    for i in range(args.steps):
-        port.run(procs, seed0=1_000_000 + 1000 * i)
-    gbs, us = port.rate()
-    sample = port.sample_text()
-    port.close()
+    cpu = CpuVerifyStep(shape, 0, procs)
+    try:
+        sec, _ = time_cpu_steps(cpu, shape, args.warmup, args.steps)
+    finally:
+        cpu.close()
     total = sum(shape.weight_bytes().values())
+    gbs = total / sec / 1e9
+    sample = (f"{args.steps} whole verify steps (all four matrices, {total / 1e6:.0f} MB of GGUF blocks each) after "
+              f"{args.warmup} warm-up steps; numpy fp32 dequant + fp32 matmul (the reference's numpy path, restated "
+              f"by the oracle package) in {procs} worker processes of one thread each (os.cpu_count() = "
+              f"{os.cpu_count()}); wall clock per step")
     emit({"metric": METRIC, "impl": "reference", "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
-          "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1000, 3),
-          "us_per_step": round(us, 1), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-          "dtype": "f64", "data": "synthetic (seeded GGUF-layout blocks per BASELINE configs 2+3)",
-          "config": {"workload": "K=11 verify step: IQ3_XXS gate/up 17408x5120 (+SiLU) -> Q6_K down 5120x17408 "
-                                 "-> Q6_K head 151936x5120 fused argmax + greedy accept",
-                     "rows": shape.rows, "weight_bytes_per_step": total},
-          "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": procs, "kind": "port",
-                           "sample": sample},
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1000, 3),
+          "us_per_step": round(sec * 1e6, 1), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+          "dtype": "f32", "data": "synthetic (seeded GGUF-layout IQ3_XXS/Q6_K blocks and bf16 N(0,1) rows per "
+                                  "BASELINE configs 2+3)",
+          "config": bench_config(shape, ws),
+          "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": procs, "kind": "port", "sample": sample},
           "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
     return 0
 
@@ -619,10 +706,11 @@ def run_ours(args):
     if args.gpus != ws and ws > 1:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
     torch.cuda.set_device(local)
-    from thunderllamax_b200 import ops, synth
-    from thunderllamax_b200.verify import VerifyShape
+    from thunderllamax_b200 import synth
+    from thunderllamax_b200.verify import VerifyShape, VerifyStep
 
     shape = VerifyShape(vocab=args.vocab, ffn=args.ffn)
+    dist = None
     if ws > 1:
         import datetime
 
@@ -630,62 +718,62 @@ def run_ours(args):
         from thunderllamax_b200.dist import ShardedVerifyStep
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-        step = ShardedVerifyStep(shape, rank, ws, seed=0)
-    else:
-        from thunderllamax_b200.verify import VerifyStep
 
-        step = VerifyStep(shape, seed=0)
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    step = ShardedVerifyStep(shape, rank, ws, seed=0) if ws > 1 else VerifyStep(shape, seed=0)
 
     rng = np.random.default_rng(1234)
     x_bits = synth.bf16_normal(rng, (shape.rows, shape.dim))
     h_bits = synth.bf16_normal(rng, (shape.rows, shape.dim))
     x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16)
     h = torch.from_numpy(h_bits.view(np.int16)).view(torch.bfloat16)
-    drafts = torch.from_numpy(rng.integers(0, shape.vocab, shape.n_drafts).astype(np.int32))
+    # drafts per the head + accept configuration: j ~ U{0..10}; drafts before j are the
+    # head's argmax of their row (from one untimed pass), later ones uniform ids
+    step.set_inputs(x.cuda(), h.cuda(), drafts=torch.zeros(shape.n_drafts, dtype=torch.int32).cuda())
+    step.launch()
+    torch.cuda.synchronize()
+    amds = step.out_idx.cpu().numpy()
+    d_np, draft_j = synth.drafts_for(amds, shape.n_drafts, shape.vocab, np.random.default_rng(4321))
+    drafts = torch.from_numpy(d_np)
     step.set_inputs(x.cuda(), h.cuda(), drafts=drafts.cuda())
     step.capture()
 
-    def barrier():
-        if ws > 1:
-            import torch.distributed as dist
+    check = None
+    if ws > 1:
+        check = check_unsharded(step, shape, x, h, drafts, rank, torch, dist)
 
-            dist.barrier()
-        torch.cuda.synchronize()
-
+    clk = ClockSampler(local).__enter__()     # runs across every timed leg below (step, kernels, e2e)
     for _ in range(max(3, args.warmup)):
         step.replay()
     barrier()
-    with ClockSampler(local) as clk:
-        ms = time_graph(step.replay, args.steps, torch)
-        barrier()
-    ms_max = ms
-    if ws > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms = time_graph(step.replay, args.steps, torch)
+    barrier()
+    ms_max = max_over_ranks(ms)
+    accepted = step.accept_out.cpu().tolist()
 
     # per-kernel durations: each kernel captured R times back to back in its own
     # graph, replayed with CUDA events on the launching stream
     per_kernel = {}
     R = 20
     for name in step.KERNELS:
-        fn = getattr(step, f"launch_{name}")
-        s_ = torch.cuda.Stream()
-        s_.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s_):
-            fn()
-        torch.cuda.current_stream().wait_stream(s_)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for _ in range(R):
-                fn()
+        g = _graph_of(lambda fn=getattr(step, f"launch_{name}"): [fn() for _ in range(R)], torch)
         g.replay()
-        per_kernel[name] = time_graph(g.replay, max(3, args.steps // R), torch) / R
+        per_kernel[name] = max_over_ranks(time_graph(g.replay, max(3, args.steps // R), torch) / R)
         del g
+    phases = None
     if ws > 1:
+        phases = step.phase_times(time_graph, _graph_of, max_over_ranks, torch)
         step.replay()
         torch.cuda.synchronize()
 
@@ -703,15 +791,10 @@ def run_ours(args):
         torch.cuda.current_stream().synchronize()
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if ws > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     h2d = x.numel() * 2 + h.numel() * 2 + drafts.numel() * 4
     d2h = outp.numel() * 4
+    clk.__exit__(None, None, None)
 
     total_w = sum(shape.weight_bytes().values())
     value = total_w / (ms_max * 1e-3) / 1e9
@@ -725,12 +808,22 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        port = CpuPort(shape, 1)
-        port.run(48)
-        gbs, us = port.rate()
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port", "sample": port.sample_text(),
-               "us_per_step": round(us, 1)}
-    extras = {}
+        port = CpuVerifyStep(shape, 0, 1)
+        try:
+            sec, out = time_cpu_steps(port, shape, 0, 1, drafts=d_np)
+        finally:
+            port.close()
+        cpu = {"value": round(total_w / sec / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": "one whole verify step (all four matrices) on one host core: numpy fp32 dequant + fp32 "
+                         "matmul, the reference's numpy path restated by the oracle package; wall clock, "
+                         "nothing extrapolated",
+               "us_per_step": round(sec * 1e6, 1), "argmax_ids_match_gpu": bool(np.array_equal(out[1], amds))}
+    extras = {"drafts": {"recipe": "j ~ U{0..10}; drafts before j = the head's argmax, later uniform ids",
+                         "j": draft_j, "accepted": accepted[0], "bonus": accepted[1]}}
+    if check is not None:
+        extras["matches_unsharded"] = check
+    if phases is not None:
+        extras["phases"] = phases
     if rank == 0 and ws == 1 and not args.no_moe:
         extras["moe_verify"] = measure_moe(args, torch, peak)
     if rank == 0 and ws == 1 and not args.no_prefill and shape.ffn == 17408 and shape.dim == 5120:
@@ -751,12 +844,11 @@ def run_ours(args):
               "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "us_per_step": round(ms_max * 1000, 2),
               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16xf16->f32 (u8 blocks)",
               "data": "synthetic (seeded GGUF-layout IQ3_XXS/Q6_K blocks and bf16 N(0,1) rows per BASELINE configs 2+3)",
-              "config": {"workload": "K=11 verify step: IQ3_XXS gate/up 17408x5120 (+SiLU) -> Q6_K down 5120x17408 "
-                                     "-> Q6_K head 151936x5120 fused argmax + greedy accept",
-                         "rows": shape.rows, "ffn": shape.ffn, "vocab": shape.vocab, "weight_bytes_per_step": total_w,
-                         "parallelism": f"tp{ws}" if ws > 1 else "single",
+              "config": bench_config(shape, ws),
+              "timing": {"graph": f"CUDA graph replay, {step.LAUNCHES_PER_STEP} launches/step"
+                                  + (f" ({step.COLLECTIVES})" if ws > 1 else ""),
                          "l2": f"weights {total_w / 1e6:.0f} MB > 126 MB L2 (no flush needed)",
-                         "graph": f"CUDA graph replay, {step.LAUNCHES_PER_STEP} launches/step" + (" + 2 NCCL collectives" if ws > 1 else "")},
+                         "device_time": "CUDA events around the K replays, max over ranks"},
               "frac_of_hbm": round(value / ws / peak, 4), "frac_of_8tbs": round(value / ws / 8000.0, 4),
               "roofline": {"bound": "hbm", "kernel": "head_argmax", "achieved": round(achieved, 1),
                            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -771,11 +863,43 @@ def run_ours(args):
               "extras": extras,
               "clocks": clocks})
     if ws > 1:
-        import torch.distributed as dist
-
         step.release()
         dist.destroy_process_group()
     return 0
+
+
+def check_unsharded(step, shape, x, h, drafts, rank, torch, dist):
+    """At N > 1: the merged argmax ids and accept record of the sharded step against
+    a one-GPU VerifyStep over the full (same seeded) model on rank 0, same inputs;
+    y to fp32 rounding (the all-reduce sums the k shards in another order)."""
+    from thunderllamax_b200.verify import VerifyStep
+
+    step.replay()
+    torch.cuda.synchronize()
+    got = torch.cat([step.out_idx, step.accept_out]).cpu()
+    y = step.y.clone()
+    ok = torch.ones(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.float64, device="cuda")
+    if rank == 0:
+        full = VerifyStep(shape, seed=0)
+        full.set_inputs(x.cuda(), h.cuda(), drafts=drafts.cuda())
+        full.launch()
+        torch.cuda.synchronize()
+        ref = torch.cat([full.out_idx, full.accept_out]).cpu()
+        ok[0] = int(torch.equal(ref, got))
+        err[0] = float(((y - full.y).abs().amax(dim=1) / full.y.norm(dim=1)).max())
+        del full
+        torch.cuda.empty_cache()
+    dist.broadcast(ok, 0)
+    dist.broadcast(err, 0)
+    # every rank's merged ids must equal rank 0's (they merge the same gathered keys)
+    mine = got.cuda().to(torch.int64)
+    lo, hi = mine.clone(), mine.clone()
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    return {"ids_and_accept_equal": bool(ok.item()) and bool(torch.equal(lo, hi)),
+            "y_max_err_over_row_norm": float(err.item()),
+            "reference": "one-GPU VerifyStep over the full seeded model on rank 0, same inputs and drafts"}
 
 
 def profile_attention(pos: int) -> int:
