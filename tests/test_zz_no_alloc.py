@@ -32,6 +32,17 @@ def noalloc_fn():
     return fn
 
 
+def noalloc_error():
+    """The scratch error word of the last no-alloc call on this device."""
+    fn = _lib.lib().tlx_head_argmax_noalloc_error
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    v = ctypes.c_uint32(0xFFFFFFFF)
+    rc = fn(ctypes.byref(v), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, _lib.lib().tlx_error_string(rc).decode()
+    return int(v.value)
+
+
 def p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -59,9 +70,20 @@ def run_regular(qtype, w, x, n_rows, row_offset, drafts, ws):
     return {"max": mx, "idx": idx, "keys": keys, "acc": acc}
 
 
-@pytest.mark.parametrize("qtype,vocab,k", [("q6_k", 20011, 1024), ("iq3_xxs", 9000, 512), ("q6_k", 151936, 5120)])
-def test_noalloc_head_matches_workspace_entry_point(qtype, vocab, k):
+@pytest.mark.parametrize("qtype,vocab,k,ctas", [("q6_k", 20011, 1024, 0), ("iq3_xxs", 9000, 512, 0),
+                                                ("q6_k", 151936, 5120, 0), ("q6_k", 20011, 1024, 37)])
+def test_noalloc_head_matches_workspace_entry_point(qtype, vocab, k, ctas):
+    # ctas = 37: both entry points run under the same tlx_set_max_ctas cap (a smaller
+    # grid, so more tiles split across CTAs), reset afterwards
     ops.require_device()
+    ops.set_max_ctas(ctas)
+    try:
+        _compare(qtype, vocab, k)
+    finally:
+        ops.set_max_ctas(0)
+
+
+def _compare(qtype, vocab, k):
     m = 11
     rng = np.random.default_rng(vocab + k)
     if vocab * k > 50_000_000:
@@ -81,6 +103,7 @@ def test_noalloc_head_matches_workspace_entry_point(qtype, vocab, k):
         ref = run_regular(qtype, w, x, vocab, 500, drafts, ws)
         got = run_noalloc(qtype, w, x, vocab, 500, drafts)
         torch.cuda.synchronize()
+        assert noalloc_error() == 0 and ws.error() == 0
         assert torch.equal(got["idx"], ref["idx"]), (call, got["idx"], ref["idx"])
         assert torch.equal(got["keys"], ref["keys"])
         np.testing.assert_allclose(got["max"].cpu().numpy(), ref["max"].cpu().numpy(), rtol=1e-6, atol=0)

@@ -45,6 +45,7 @@ _SIGS = {
     "tlx_stage_activations": (c_int, [c_vp, c_int, c_i64, c_int, c_i64, c_vp, c_vp]),
     "tlx_head_argmax_noalloc": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp,
                                         c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
+    "tlx_head_argmax_noalloc_error": (c_int, [c_vp, c_vp]),
     "tlx_gemv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp, c_int,
                          c_i64, c_vp, c_size, c_vp]),
     "tlx_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_int,

@@ -292,6 +292,11 @@ __global__ void pack_tiles_kernel(int qt, const uint8_t* __restrict__ src, int64
 
 }  // namespace
 
+namespace tlx {
+// the CTA cap tlx_set_max_ctas set (0 = one CTA per SM), for the other entry points
+int max_ctas_setting() { return g_max_ctas; }
+}  // namespace tlx
+
 extern "C" {
 
 const char* tlx_error_string(int code) {

@@ -53,7 +53,9 @@ extern "C" int tlx_head_argmax_noalloc(int qtype, const void* w, const uint32_t*
                                        int64_t ldx, int m, int64_t n_rows, int64_t k, int64_t row_offset,
                                        float* out_max, int32_t* out_idx, uint64_t* out_keys, const int32_t* drafts,
                                        int n_drafts, int32_t* accept_out, void* stream) {
-  const size_t need = tlx::gemv_workspace_bytes(kEpiArgmax, qtype, n_rows, k, m, x_dtype, 0);
+  // the same grid as tlx_head_argmax: honour the tlx_set_max_ctas cap
+  const int max_ctas = tlx::max_ctas_setting();
+  const size_t need = tlx::gemv_workspace_bytes(kEpiArgmax, qtype, n_rows, k, m, x_dtype, max_ctas);
   if (need == 0) return TLX_ERR_SHAPE;
   if (need > kScratchBytes) return TLX_ERR_WORKSPACE;  // shape needs more than the built-in scratch
   void* ws = nullptr;
@@ -61,10 +63,24 @@ extern "C" int tlx_head_argmax_noalloc(int qtype, const void* w, const uint32_t*
   if (rc != TLX_OK) return rc;
   // the array keeps whatever the previous call left: zero the arrival counters
   // and the error word (stream-ordered; partials are written before they are read)
-  const size_t zero = tlx::gemv_counter_bytes(kEpiArgmax, qtype, n_rows, k, m, x_dtype, 0);
+  const size_t zero = tlx::gemv_counter_bytes(kEpiArgmax, qtype, n_rows, k, m, x_dtype, max_ctas);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(ws, 0, zero, s) != cudaSuccess) return TLX_ERR_LAUNCH;
   return tlx::run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
                        TLX_DT_F32, 0, row_offset, out_max, out_idx, out_keys, drafts, n_drafts, accept_out, ws,
-                       kScratchBytes, 0, s);
+                       kScratchBytes, max_ctas, s);
+}
+
+// The error word of the current device's scratch (word 0): bit 0 = a bounded wait
+// for a weight copy gave up, so that call's results are not to be trusted.  The
+// next tlx_head_argmax_noalloc call on this device clears it, so read it in
+// between.  Waits for `stream` to drain.
+extern "C" int tlx_head_argmax_noalloc_error(uint32_t* err_out, void* stream) {
+  if (!err_out) return TLX_ERR_NULL;
+  void* ws = nullptr;
+  int rc = scratch_for_current_device(&ws);
+  if (rc != TLX_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(err_out, ws, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) return TLX_ERR_LAUNCH;
+  return cudaStreamSynchronize(s) == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }

@@ -33,6 +33,8 @@ int projections_error(const void* ws, int n, const Projection* pr, int m, int64_
 size_t activation_image_bytes(int m, int64_t k, int x_dtype);
 int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, cudaStream_t stream);
 size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
+// the CTA cap set by tlx_set_max_ctas (0 = one CTA per SM)
+int max_ctas_setting();
 int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
                    int n_info);
 
