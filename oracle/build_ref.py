@@ -1,6 +1,6 @@
 """Compile reference kernels into oracle/_ref/ (test infrastructure only).
 
-    python oracle/build_ref.py            # TLX_REFERENCE overrides /root/reference
+    python oracle/build_ref.py   # reference tree: TLX_REFERENCE, else ../reference beside the repository
 
 Each listed kernel is one self-contained .cu file of the reference tree
 (engine/<name>.cu, extern "C"); nvcc compiles it as written, from where it
@@ -18,8 +18,10 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+REPO_ROOT = os.path.dirname(HERE)
 OUT = os.path.join(HERE, "_ref")
-REF = os.environ.get("TLX_REFERENCE", "/root/reference")
+# the reference checkout: TLX_REFERENCE, else a "reference" directory beside this repository
+REF = os.environ.get("TLX_REFERENCE") or os.path.normpath(os.path.join(REPO_ROOT, "..", "reference"))
 
 # (engine-relative source, kernel name): kernels whose every access was checked by
 # reading against the shapes the tests launch them with (integer / index / copy work

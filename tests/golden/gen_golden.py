@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the oracle to the reference.
 
-Run in a container where the reference tree is mounted (default
-/root/reference, override with TLX_REFERENCE):
+Run where the reference tree is available (TLX_REFERENCE, else a "reference"
+directory beside this repository):
 
     python tests/golden/gen_golden.py
 
@@ -22,13 +22,15 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+REPO_ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, HERE)
 
 from thunderllamax_b200 import synth  # noqa: E402
 from inputs import cmb_inputs, router_inputs  # noqa: E402
 
-REF = os.environ.get("TLX_REFERENCE", "/root/reference")
+# the reference checkout: TLX_REFERENCE, else a "reference" directory beside this repository
+REF = os.environ.get("TLX_REFERENCE") or os.path.normpath(os.path.join(REPO_ROOT, "..", "reference"))
 
 
 def load_reference():
