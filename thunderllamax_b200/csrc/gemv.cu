@@ -37,14 +37,37 @@ namespace tlx {
 
 enum Epi : int { EPI_STORE = 0, EPI_GATEUP = 1, EPI_ARGMAX = 2 };
 
-constexpr int kImageRow = 68;                           // uint2 entries per (block, column) row
-constexpr uint32_t kImageRowBytes = kImageRow * 8u;     // 544
+// Activation image.  Per 256-weight block b and column c one 512-byte row of 64
+// uint2 entries; entry (mma step m, lane quarter q) holds the 4 halves
+// x[c][256b + 64q + 4m + 0..3].  The entries of steps 2j and 2j+1 of one quarter are
+// adjacent, so one 16-byte load gives the B fragments of two mma steps, and the
+// 64-byte groups of pair j are swapped between even and odd columns (j ^ (c & 1)):
+// the two columns that one 8-lane load phase reads (tokens g and g+1) then fall in
+// different bank halves.  After the whole image, 4 entries per (block, column) hold
+// the Q4_K / Q5_K sub-block sums (written by the staging kernel on request).
+constexpr int kImageRow = 64;                       // uint2 entries per (block, column) row
+constexpr uint32_t kImageRowBytes = kImageRow * 8u;   // 512
+constexpr uint32_t kSumRowBytes = 32;                 // sums of one (block, column)
+
+__host__ __device__ __forceinline__ int image_entry(int m, int q, int col) {
+  return ((((m >> 1) ^ (col & 1))) << 3) | (q << 1) | (m & 1);
+}
+// uint2 index of the entry holding x[c][k..k+3], k % 4 == 0
+__host__ __device__ __forceinline__ int64_t image_index(int64_t k, int col, int MC) {
+  const int64_t b = k >> 8;
+  const int kin = static_cast<int>(k & 255), q = kin >> 6, m = (kin & 63) >> 2;
+  return (b * MC + col) * kImageRow + image_entry(m, q, col);
+}
+// uint2 index of the sums entry of (block b, column c, quarter q) in an image of NB blocks
+__host__ __device__ __forceinline__ int64_t sums_index(int64_t b, int col, int q, int NB, int MC) {
+  return static_cast<int64_t>(NB) * MC * kImageRow + (b * MC + col) * 4 + q;
+}
 
 struct GemvParams {
   const uint8_t* w0;
   const uint8_t* w1;
   const uint32_t* grid;
-  const uint2* ximg;  // fp16 activation image, see image_index
+  const uint2* ximg;  // fp16 activation image (image_index / sums_index)
   int M;
   int MC;
   int CG;  // columns per token (1, or 3 for fp32 activations split into fp16 parts)
@@ -70,19 +93,23 @@ struct GemvParams {
   uint32_t* err;
 };
 
+__host__ __device__ constexpr bool needs_sums(int qt) { return qt == QT_Q4_K || qt == QT_Q5_K; }
+
 // ---- shared-memory layout (same arithmetic on host and device) ----
-// The epilogue of a tile reuses the ring stage its last block was read from (the
-// next copy into that stage is issued only after the epilogue), so there is no
-// separate scratch region.
+// A warp loads each chunk into registers and hands its ring stage back at once, so
+// the epilogue works on registers; only fp32 activations (CG > 1: a token's value is
+// the sum of several columns) need the per-warp scratch region `epi`.
 struct SmemLayout {
-  uint32_t xs, grid, ring, bars, best, total;
+  uint32_t xs, sums, grid, ring, bars, best, epi, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int stages, int Bs, int MC) {
+__host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int stages, int Bs, int MC, int CG) {
   SmemLayout L;
   uint32_t off = 0;
   L.xs = off;
   off += static_cast<uint32_t>(Bs) * static_cast<uint32_t>(MC) * kImageRowBytes;
+  L.sums = off;
+  if (needs_sums(qt)) off += static_cast<uint32_t>(Bs) * static_cast<uint32_t>(MC) * kSumRowBytes;
   off = (off + 127u) & ~127u;
   L.grid = off;
   if (qt == QT_IQ3_XXS) off += kGridTableBytes;
@@ -93,6 +120,8 @@ __host__ __device__ inline SmemLayout smem_layout(int qt, int nmat, int wpc, int
   off += static_cast<uint32_t>(wpc) * stages * 8u + 8u;  // + the activation-image barrier
   L.best = off;
   off += static_cast<uint32_t>(wpc) * 16u * 8u + 128u;  // + done flag and 16 final ids
+  L.epi = off;
+  if (CG > 1) off += static_cast<uint32_t>(wpc) * nmat * 1024u;
   L.total = off;
   return L;
 }
@@ -103,17 +132,6 @@ __device__ __forceinline__ int warp_of(int64_t f, int64_t Fs, int Ws) {
 }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
-
-// Activation image: per 256-weight block b and column (token) c one row of 64
-// entries [mma m][quarter q] (4 halves each, x[c][256b + 64q + 4m + 0..3]) padded to
-// 68 entries, so lane (g, q) of an mma reads row g at entry 4m + q: every mma's
-// offset is a compile-time immediate and the 32 lanes hit 32 distinct banks pairs.
-// Index (uint2 units) of the entry holding x[c][k..k+3], k % 4 == 0:
-__host__ __device__ __forceinline__ int64_t image_index(int64_t k, int col, int MC) {
-  const int64_t b = k >> 8;
-  const int kin = static_cast<int>(k & 255), q = kin >> 6, m = (kin & 63) >> 2;
-  return (b * MC + col) * kImageRow + m * 4 + q;
-}
 
 // ---- activation staging: x[M][K] (f32 / f16 / bf16) -> fp16 image ----
 __global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_t ldx, int M, int CG, int MC, int64_t K,
@@ -157,10 +175,10 @@ __global__ void stage_image_kernel(const void* __restrict__ x, int dtype, int64_
   }
 }
 
-// Per-sub-block sums of the staged activations, for Q4_K's min term: entry 64 + q of
-// image row (block b, column c) = {hi(S_2q), hi(S_2q+1), lo(S_2q), lo(S_2q+1)} where
-// S_s = sum of x[c][256b + 32s .. +32) over the fp16 values in the image (summed in
-// fp32) and hi / lo its two-fp16 split, so the min-term mma sees S to ~2^-22.
+// Per-sub-block sums of the staged activations, for Q4_K's min term: sums entry q of
+// (block b, column c) = {hi(S_2q), hi(S_2q+1), lo(S_2q), lo(S_2q+1)} where S_s = sum of
+// x[c][256b + 32s .. +32) over the fp16 values in the image (summed in fp32) and
+// hi / lo its two-fp16 split, so the min-term mma sees S to ~2^-22.
 __global__ void stage_sums_kernel(int NB, int MC, uint2* __restrict__ img) {
   griddep_wait();
   griddep_launch_dependents();
@@ -168,28 +186,89 @@ __global__ void stage_sums_kernel(int NB, int MC, uint2* __restrict__ img) {
   for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < total;
        gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int q = static_cast<int>(gi & 3);
-    uint2* row = img + (gi >> 2) * kImageRow;
+    const int64_t bc = gi >> 2;
+    const int col = static_cast<int>(bc % MC);
+    const int64_t b = bc / MC;
+    const uint2* row = img + bc * kImageRow;
     float sum[2] = {0.f, 0.f};
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
-      const uint2 e = row[m * 4 + q];
+      const uint2 e = row[image_entry(m, q, col)];
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&e.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&e.y));
-      sum[m >> 3] += (a.x + a.y) + (b.x + b.y);
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&e.y));
+      sum[m >> 3] += (a.x + a.y) + (c.x + c.y);
     }
     const __half h0 = __float2half_rn(sum[0]), h1 = __float2half_rn(sum[1]);
     const __half l0 = __float2half_rn(sum[0] - __half2float(h0)), l1 = __float2half_rn(sum[1] - __half2float(h1));
     const __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
-    row[64 + q] = make_uint2(*reinterpret_cast<const uint32_t*>(&hh), *reinterpret_cast<const uint32_t*>(&ll));
+    img[sums_index(b, col, q, NB, MC)] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&hh), *reinterpret_cast<const uint32_t*>(&ll));
   }
 }
 
-// one 256-weight block of one chunk set: acc[mat] += d_row * (A_int . B).
-// xb0 / xb1: this lane's image rows (tokens g and g+8, clamped to valid columns;
-// clamped columns only feed accumulator columns that are never read) of the block
+// ---- one chunk set (NMAT chunks of one 16-row tile and 256-weight block) ----
+// load_lane copies the calling lane's part of the chunks from the ring stage into
+// registers (after which the stage can be refilled); compute_lane decodes them into
+// exact-integer fp16 A fragments and runs the mma steps against the image rows.
+template <int QT, int NMAT>
+struct LaneData;
+template <int NMAT>
+struct LaneData<QT_Q6_K, NMAT> {
+  Q6Lane s[NMAT];
+};
+template <int NMAT>
+struct LaneData<QT_IQ3_XXS, NMAT> {
+  Iq3Lane s[NMAT];
+};
+template <int NMAT>
+struct LaneData<QT_Q4_K, NMAT> {
+  Q4Lane s;
+};
+template <int NMAT>
+struct LaneData<QT_Q5_K, NMAT> {
+  Q4Lane s;
+};
+template <int NMAT>
+struct LaneData<QT_Q8_0, NMAT> {
+  Q8Lane s;
+};
+
+template <int QT, int NMAT>
+__device__ __forceinline__ void load_lane(const uint8_t* stage, int lane, LaneData<QT, NMAT>& L) {
+  constexpr uint32_t CH = chunk_bytes(QT);
+  if constexpr (QT == QT_Q6_K) {
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) q6_load(stage + a * CH, lane, L.s[a]);
+  } else if constexpr (QT == QT_IQ3_XXS) {
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) iq3_load(stage + a * CH, lane, L.s[a]);
+  } else if constexpr (QT == QT_Q8_0) {
+    static_assert(NMAT == 1, "Q8_0 is read by the STORE epilogue only");
+    q8_load(stage, lane, L.s);
+  } else {
+    static_assert(NMAT == 1, "Q4_K / Q5_K are read by the STORE epilogue only");
+    q4_load<QT == QT_Q5_K>(stage, lane, L.s);
+  }
+}
+
+// B fragments of mma steps 2j and 2j+1 for both token groups: xE / xO are this lane's
+// image row addresses (shared space) for even / odd pairs j of the current block
+template <int NT>
+__device__ __forceinline__ void load_b_pair(const uint32_t (&xE)[NT], const uint32_t (&xO)[NT], int j,
+                                            uint4 (&b)[NT]) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint32_t addr = ((j & 1) ? xO[nt] : xE[nt]) + static_cast<uint32_t>(j) * 64u;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(b[nt].x), "=r"(b[nt].y), "=r"(b[nt].z), "=r"(b[nt].w)
+                 : "r"(addr));
+  }
+}
+
 template <int QT, int NT, int NMAT>
-__device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT], const uint2* xb0, const uint2* xb1,
-                                              const uint8_t* grid_lane, int lane, float (&acc)[NMAT][NT][4]) {
+__device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const uint32_t (&xE)[NT],
+                                             const uint32_t (&xO)[NT], const uint32_t (&xsum)[NT],
+                                             const uint8_t* grid_lane, float (&acc)[NMAT][NT][4]) {
   float tmp[NMAT][NT][4];
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
@@ -197,124 +276,201 @@ __device__ __forceinline__ void compute_block(const uint8_t* const (&chunk)[NMAT
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) tmp[a][nt][i] = 0.f;
-  float2 scale[NMAT];
-  auto load_b = [&](int m, uint32_t (&b)[NT][2]) {
-    const uint2 v0 = xb0[m * 4];
-    b[0][0] = v0.x;
-    b[0][1] = v0.y;
-    if constexpr (NT == 2) {
-      const uint2 v1 = xb1[m * 4];
-      b[1][0] = v1.x;
-      b[1][1] = v1.y;
-    }
-  };
-  if constexpr (QT == QT_Q8_0) {
-    // Q8_0 (single matrix): the fragments are the rounded weights fp16(d q)
-    static_assert(NMAT == 1, "Q8_0 is read by the STORE epilogue only");
-    Q8Lane s;
-    q8_load(chunk[0], lane, s);
+  if constexpr (QT == QT_Q6_K) {
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      uint32_t b[NT][2];
-      load_b(m, b);
-      uint32_t af[4];
-      q8_mma(s, m, af);
+    for (int j = 0; j < 8; ++j) {
+      uint4 b[NT];
+      load_b_pair<NT>(xE, xO, j, b);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma16816(acc[0][nt], af, b[nt][0], b[nt][1]);
+      for (int a = 0; a < NMAT; ++a) {
+        uint32_t a0[4], a1[4];
+        q6_group(L.s[a], j, a0, a1);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816(tmp[a][nt], a0, b[nt].x, b[nt].y);
+          mma16816(tmp[a][nt], a1, b[nt].z, b[nt].w);
+        }
+      }
     }
-  } else if constexpr (QT == QT_Q4_K || QT == QT_Q5_K) {
-    // Q4_K / Q5_K (single matrix): acc += d * sum (sc q) x  -  dmin * sum_s mn_s xsum_s
-    static_assert(NMAT == 1, "Q4_K / Q5_K are read by the STORE epilogue only");
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) {
+      const float2 sc = q6_block_scale(L.s[a]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[a][nt][0] = fmaf(sc.x, tmp[a][nt][0], acc[a][nt][0]);
+        acc[a][nt][1] = fmaf(sc.x, tmp[a][nt][1], acc[a][nt][1]);
+        acc[a][nt][2] = fmaf(sc.y, tmp[a][nt][2], acc[a][nt][2]);
+        acc[a][nt][3] = fmaf(sc.y, tmp[a][nt][3], acc[a][nt][3]);
+      }
+    }
+  } else if constexpr (QT == QT_IQ3_XXS) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 b[NT];
+      load_b_pair<NT>(xE, xO, j, b);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int a = 0; a < NMAT; ++a) {
+          uint32_t af[4];
+          iq3_mma(L.s[a], grid_lane, 2 * j + h, af);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma16816(tmp[a][nt], af, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < NMAT; ++a) {
+      const float2 sc = iq3_block_scale(L.s[a]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[a][nt][0] = fmaf(sc.x, tmp[a][nt][0], acc[a][nt][0]);
+        acc[a][nt][1] = fmaf(sc.x, tmp[a][nt][1], acc[a][nt][1]);
+        acc[a][nt][2] = fmaf(sc.y, tmp[a][nt][2], acc[a][nt][2]);
+        acc[a][nt][3] = fmaf(sc.y, tmp[a][nt][3], acc[a][nt][3]);
+      }
+    }
+  } else if constexpr (QT == QT_Q8_0) {
+    // the fragments are the rounded weights fp16(d q)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 b[NT];
+      load_b_pair<NT>(xE, xO, j, b);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t af[4];
+        q8_mma(L.s, 2 * j + h, af);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(acc[0][nt], af, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
+      }
+    }
+  } else {
+    // Q4_K / Q5_K: acc += d * sum (sc q) x  -  dmin * sum_s mn_s xsum_s
     constexpr bool Q5 = QT == QT_Q5_K;
-    Q4Lane s;
-    q4_load<Q5>(chunk[0], lane, s);
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      uint32_t b[NT][2];
-      load_b(m, b);
-      uint32_t af[4];
-      q4_mma<Q5>(s, m, af);
+    for (int j = 0; j < 8; ++j) {
+      uint4 b[NT];
+      load_b_pair<NT>(xE, xO, j, b);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma16816(tmp[0][nt], af, b[nt][0], b[nt][1]);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t af[4];
+        q4_mma<Q5>(L.s, 2 * j + h, af);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[0][nt], af, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
+      }
     }
     // min term: A' = the lane's mins (sub-blocks 2q, 2q+1; k' and 8 + k' alike), B' =
-    // the image's per-sub-block sums of x in two fp16 parts (entry 64 + q)
+    // the per-sub-block sums of x in two fp16 parts (sums entry q of the block)
     float tmin[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) tmin[nt][i] = 0.f;
-    {
-      uint32_t b[NT][2];
-      load_b(16, b);
-      const uint32_t am[4] = {s.mn[0], s.mn[1], s.mn[0], s.mn[1]};
+    const uint32_t am[4] = {L.s.mn[0], L.s.mn[1], L.s.mn[0], L.s.mn[1]};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma16816(tmin[nt], am, b[nt][0], b[nt][1]);
+    for (int nt = 0; nt < NT; ++nt) {
+      uint32_t s0, s1;
+      asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(s0), "=r"(s1) : "r"(xsum[nt]));
+      mma16816(tmin[nt], am, s0, s1);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      acc[0][nt][0] = fmaf(-s.dmin[0], tmin[nt][0], fmaf(s.d[0], tmp[0][nt][0], acc[0][nt][0]));
-      acc[0][nt][1] = fmaf(-s.dmin[0], tmin[nt][1], fmaf(s.d[0], tmp[0][nt][1], acc[0][nt][1]));
-      acc[0][nt][2] = fmaf(-s.dmin[1], tmin[nt][2], fmaf(s.d[1], tmp[0][nt][2], acc[0][nt][2]));
-      acc[0][nt][3] = fmaf(-s.dmin[1], tmin[nt][3], fmaf(s.d[1], tmp[0][nt][3], acc[0][nt][3]));
-    }
-  } else if constexpr (QT == QT_Q6_K) {
-#pragma unroll
-    for (int a = 0; a < NMAT; ++a) {
-      Q6Lane s;
-      q6_load(chunk[a], lane, s);
-#pragma unroll
-      for (int gam = 0; gam < 8; ++gam) {
-        uint32_t a0[4], a1[4];
-        q6_group(s, gam, a0, a1);
-        uint32_t b[NT][2];
-        load_b(2 * gam, b);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a0, b[nt][0], b[nt][1]);
-        load_b(2 * gam + 1, b);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], a1, b[nt][0], b[nt][1]);
-      }
-      scale[a] = q6_block_scale(s);
-    }
-  } else {
-    Iq3Lane s[NMAT];
-#pragma unroll
-    for (int a = 0; a < NMAT; ++a) {
-      iq3_load(chunk[a], lane, s[a]);
-      scale[a] = iq3_block_scale(s[a]);
-    }
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      uint32_t b[NT][2];
-      load_b(m, b);
-#pragma unroll
-      for (int a = 0; a < NMAT; ++a) {
-        uint32_t af[4];
-        iq3_mma(s[a], grid_lane, m, af);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816(tmp[a][nt], af, b[nt][0], b[nt][1]);
-      }
-    }
-  }
-  if constexpr (QT == QT_Q6_K || QT == QT_IQ3_XXS) {
-#pragma unroll
-  for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      acc[a][nt][0] = fmaf(scale[a].x, tmp[a][nt][0], acc[a][nt][0]);
-      acc[a][nt][1] = fmaf(scale[a].x, tmp[a][nt][1], acc[a][nt][1]);
-      acc[a][nt][2] = fmaf(scale[a].y, tmp[a][nt][2], acc[a][nt][2]);
-      acc[a][nt][3] = fmaf(scale[a].y, tmp[a][nt][3], acc[a][nt][3]);
+      acc[0][nt][0] = fmaf(-L.s.dmin[0], tmin[nt][0], fmaf(L.s.d[0], tmp[0][nt][0], acc[0][nt][0]));
+      acc[0][nt][1] = fmaf(-L.s.dmin[0], tmin[nt][1], fmaf(L.s.d[0], tmp[0][nt][1], acc[0][nt][1]));
+      acc[0][nt][2] = fmaf(-L.s.dmin[1], tmin[nt][2], fmaf(L.s.d[1], tmp[0][nt][2], acc[0][nt][2]));
+      acc[0][nt][3] = fmaf(-L.s.dmin[1], tmin[nt][3], fmaf(L.s.d[1], tmp[0][nt][3], acc[0][nt][3]));
     }
   }
 }
 
-// tile epilogue on complete sums (fragment order in registers); epi = 1 KB per matrix of
-// shared scratch owned by this warp
+// ---- epilogue of a complete 16-row tile from the fragment registers ----
+// v[a][nt][e]: lane (g, q) holds rows g (e = 0, 1) and g + 8 (e = 2, 3) of columns
+// 8 nt + 2q + (e & 1); here a column is a token.
 template <int NT, int NMAT, int EPI>
-__device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4],
-                                              float* epi, int lane, uint64_t& best) {
+__device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4], int lane,
+                                              uint64_t (&best)[2 * NT]) {
+  const int g = lane >> 2, q = lane & 3;
+  const int64_t row0 = t * kTileRows;
+  if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 8 * nt + 2 * q + (e & 1);
+        const int64_t row = row0 + g + 8 * (e >> 1);
+        if (col < p.M && row < p.n_rows) {
+          const uint64_t key = argmax_key(v[0][nt][e], static_cast<uint32_t>(p.row_offset + row));
+          uint64_t& b = best[2 * nt + (e & 1)];
+          b = key > b ? key : b;
+        }
+      }
+  } else if constexpr (EPI == EPI_GATEUP) {
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nt][e] = silu_f(v[0][nt][e]) * v[1][nt][e];
+    if (p.y_img) {
+      // 4 consecutive rows of one token are one entry of the consumer's image: lanes
+      // g = 4i .. 4i+3 (same q) hold them, and lane g = 4i gathers and stores
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float r1 = __shfl_down_sync(0xffffffffu, o[nt][e], 4);
+          const float r2 = __shfl_down_sync(0xffffffffu, o[nt][e], 8);
+          const float r3 = __shfl_down_sync(0xffffffffu, o[nt][e], 12);
+          const int col = 8 * nt + 2 * q + (e & 1);
+          if ((g & 3) == 0 && col < p.M) {
+            const __half2 h01 = __floats2half2_rn(o[nt][e], r1), h23 = __floats2half2_rn(r2, r3);
+            p.y_img[image_index(row0 + g + 8 * (e >> 1), col, p.M)] =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+          }
+        }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = 8 * nt + 2 * q + (e & 1);
+          const int64_t row = row0 + g + 8 * (e >> 1);
+          if (col < p.M && row < p.n_rows) {
+            if (p.y_f16)
+              static_cast<__half*>(p.y)[col * p.ldy + row] = __float2half_rn(o[nt][e]);
+            else
+              static_cast<float*>(p.y)[col * p.ldy + row] = o[nt][e];
+          }
+        }
+    }
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 8 * nt + 2 * q + (e & 1);
+        const int64_t row = row0 + g + 8 * (e >> 1);
+        if (col < p.M && row < p.n_rows) {
+          float val = v[0][nt][e];
+          if (p.residual) val += p.residual[col * p.ldr + row];
+          if (p.y_f16)
+            static_cast<__half*>(p.y)[col * p.ldy + row] = __float2half_rn(val);
+          else
+            static_cast<float*>(p.y)[col * p.ldy + row] = val;
+        }
+      }
+  }
+}
+
+// fp32 activations (CG > 1 fp16 columns per token): sum each token's columns through
+// the warp's scratch, then the token-column epilogue
+template <int NT, int NMAT, int EPI>
+__device__ __forceinline__ void tile_finish(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4], int lane,
+                                            float* epi, uint64_t (&best)[2 * NT]) {
+  if (p.CG == 1) {
+    tile_epilogue<NT, NMAT, EPI>(p, t, v, lane, best);
+    return;
+  }
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
@@ -325,65 +481,22 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, co
       *reinterpret_cast<float2*>(epi + a * 256 + (g + 8) * 16 + col) = make_float2(v[a][nt][2], v[a][nt][3]);
     }
   __syncwarp();
-  const int64_t row0 = t * kTileRows;
-  auto value = [&](int a, int r, int tk) {
-    float val = 0.f;
-    for (int c = 0; c < p.CG; ++c) val += epi[a * 256 + r * 16 + tk * p.CG + c];
-    return val;
-  };
-  if constexpr (EPI == EPI_ARGMAX) {
-    const int tk = lane & 15, rh = lane >> 4;
-    if (tk < p.M) {
+  float vt[NMAT][NT][4];
 #pragma unroll
-      for (int r8 = 0; r8 < 8; ++r8) {
-        const int r = rh * 8 + r8;
-        if (row0 + r < p.n_rows) {
-          const uint64_t key = argmax_key(value(0, r, tk), static_cast<uint32_t>(p.row_offset + row0 + r));
-          best = key > best ? key : best;
-        }
-      }
-    }
-  } else if constexpr (EPI == EPI_GATEUP) {
-    if (p.y_img) {
-      // 4 consecutive rows of one token -> one image entry of the consumer's activations
-      for (int idx = lane; idx < 4 * p.M; idx += 32) {
-        const int r4 = idx & 3, tk = idx >> 2;
-        float o[4];
+  for (int a = 0; a < NMAT; ++a)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = silu_f(value(0, 4 * r4 + e, tk)) * value(1, 4 * r4 + e, tk);
-        const __half2 h01 = __floats2half2_rn(o[0], o[1]);
-        const __half2 h23 = __floats2half2_rn(o[2], o[3]);
-        p.y_img[image_index(row0 + 4 * r4, tk, p.M)] =
-            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = 8 * nt + 2 * q + (e & 1);
+        const int row = g + 8 * (e >> 1);
+        float s = 0.f;
+        if (tok < p.M)
+          for (int c = 0; c < p.CG; ++c) s += epi[a * 256 + row * 16 + tok * p.CG + c];
+        vt[a][nt][e] = s;
       }
-    } else {
-      for (int idx = lane; idx < 16 * p.M; idx += 32) {
-        const int r = idx & 15, tk = idx >> 4;
-        const int64_t row = row0 + r;
-        if (row < p.n_rows) {
-          const float val = silu_f(value(0, r, tk)) * value(1, r, tk);
-          if (p.y_f16)
-            static_cast<__half*>(p.y)[tk * p.ldy + row] = __float2half_rn(val);
-          else
-            static_cast<float*>(p.y)[tk * p.ldy + row] = val;
-        }
-      }
-    }
-  } else {
-    for (int idx = lane; idx < 16 * p.M; idx += 32) {
-      const int r = idx & 15, tk = idx >> 4;
-      const int64_t row = row0 + r;
-      if (row < p.n_rows) {
-        float val = value(0, r, tk);
-        if (p.residual) val += p.residual[tk * p.ldr + row];
-        if (p.y_f16)
-          static_cast<__half*>(p.y)[tk * p.ldy + row] = __float2half_rn(val);
-        else
-          static_cast<float*>(p.y)[tk * p.ldy + row] = val;
-      }
-    }
-  }
   __syncwarp();
+  tile_epilogue<NT, NMAT, EPI>(p, t, vt, lane, best);
 }
 
 template <int QT, int NT, int EPI, int WPC, int STAGES>
@@ -392,15 +505,16 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   constexpr uint32_t CH = chunk_bytes(QT);
   constexpr uint32_t STAGE_BYTES = CH * NMAT;
   extern __shared__ __align__(128) uint8_t smem[];
-  const SmemLayout L = smem_layout(QT, NMAT, WPC, STAGES, p.Bs, p.MC);
-  uint2* xs = reinterpret_cast<uint2*>(smem + L.xs);
+  const SmemLayout L = smem_layout(QT, NMAT, WPC, STAGES, p.Bs, p.MC, p.CG);
   uint32_t* grid_rep = reinterpret_cast<uint32_t*>(smem + L.grid);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = smem + L.ring + static_cast<uint32_t>(warp) * STAGES * STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * STAGES;
   uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + L.bars) + WPC * STAGES;
   uint64_t* wbest = reinterpret_cast<uint64_t*>(smem + L.best);
+  float* epi = reinterpret_cast<float*>(smem + L.epi) + warp * NMAT * 256;
 
+  // ---- this warp's items: a contiguous range of (tile, block) of its k-segment ----
   const int seg = blockIdx.x / p.Cs;
   const int cta_in_seg = blockIdx.x - seg * p.Cs;
   const int64_t Fs = static_cast<int64_t>(p.T) * p.Bs;
@@ -410,26 +524,23 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   const bool active = wseg < Ws;
   const int64_t f0 = active ? static_cast<int64_t>(wseg) * Fs / Ws : 0;
   const int64_t f1 = active ? static_cast<int64_t>(wseg + 1) * Fs / Ws : 0;
-  const int64_t n_items = f1 - f0;
-  const int64_t t_first = f0 / p.Bs;
-  const int bb_first = static_cast<int>(f0 - t_first * p.Bs);
+  const int n_items = static_cast<int>(f1 - f0);
+  int64_t t = f0 / p.Bs;
+  int bb = static_cast<int>(f0 - t * p.Bs);
 
-
-  // weight ring: the issue cursor walks the same items as the compute cursor; items
-  // of one tile are consecutive chunks, the next tile of the segment starts
-  // (NB - Bs + 1) chunks after the last one
-  int ibb = bb_first;
-  size_t woff = (static_cast<size_t>(t_first) * p.NB + static_cast<size_t>(seg) * p.Bs + bb_first) * CH;
-  const size_t tile_jump = static_cast<size_t>(p.NB - p.Bs + 1) * CH;
+  // weight copy cursor (lane 0): the items of a tile are consecutive chunks; after the
+  // segment's last block the next tile of the segment starts NB - Bs chunks further
+  size_t woff = (static_cast<size_t>(t) * p.NB + static_cast<size_t>(seg) * p.Bs + bb) * CH;
+  int w_left = p.Bs - bb;
+  const size_t tile_skip = static_cast<size_t>(p.NB - p.Bs) * CH;
   auto issue = [&](int st) {
     mbar_arrive_expect_tx(&bars[st], STAGE_BYTES);
     bulk_g2s(ring + st * STAGE_BYTES, p.w0 + woff, CH, &bars[st]);
     if constexpr (NMAT == 2) bulk_g2s(ring + st * STAGE_BYTES + CH, p.w1 + woff, CH, &bars[st]);
-    if (++ibb == p.Bs) {
-      ibb = 0;
-      woff += tile_jump;
-    } else {
-      woff += CH;
+    woff += CH;
+    if (--w_left == 0) {
+      w_left = p.Bs;
+      woff += tile_skip;
     }
   };
   if (lane == 0) {
@@ -457,160 +568,209 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   griddep_wait();
   griddep_launch_dependents();
 
-  // activations of this k-segment: one bulk copy of the image slice
+  // activations of this k-segment (and their sub-block sums): bulk copies of the
+  // image slices
   const uint32_t xbytes = static_cast<uint32_t>(p.Bs) * static_cast<uint32_t>(p.MC) * kImageRowBytes;
+  const uint32_t sbytes = needs_sums(QT) ? static_cast<uint32_t>(p.Bs) * static_cast<uint32_t>(p.MC) * kSumRowBytes : 0u;
   if (threadIdx.x == 0) {
     mbar_init(xbar, 1);
     mbar_fence_init();
-    mbar_arrive_expect_tx(xbar, xbytes);
+    mbar_arrive_expect_tx(xbar, xbytes + sbytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg) + static_cast<size_t>(seg) * xbytes;
     for (uint32_t off = 0; off < xbytes; off += 32768u)
-      bulk_g2s(reinterpret_cast<uint8_t*>(xs) + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
+      bulk_g2s(smem + L.xs + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
+    if (sbytes) {
+      const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(p.ximg) +
+                            static_cast<size_t>(p.NB) * p.MC * kImageRowBytes + static_cast<size_t>(seg) * sbytes;
+      for (uint32_t off = 0; off < sbytes; off += 32768u)
+        bulk_g2s(smem + L.sums + off, ssrc + off, sbytes - off < 32768u ? sbytes - off : 32768u, xbar);
+    }
   }
   __syncthreads();
   bool failed = !mbar_wait_bounded(xbar, 0, threadIdx.x == 0 ? p.err : nullptr);
 
-  float acc[NMAT][NT][4];
+  // this lane's image rows (shared addresses): tokens g and g + 8, clamped to the last
+  // valid column (clamped columns only feed accumulator columns that are never read);
+  // pairs j of the 64-byte groups are swapped in odd columns
+  const int g = lane >> 2, q = lane & 3;
+  uint32_t xE[NT], xO[NT], xS[NT];
+  {
+    const uint32_t xs0 = smem_u32(smem + L.xs), ss0 = smem_u32(smem + L.sums);
 #pragma unroll
-  for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[a][nt][i] = 0.f;
-  uint64_t best = 0ull;
-  int64_t i_fail = failed ? 0 : n_items;
-
-  // this lane's image rows: tokens g and g+8, clamped to the last valid column
-  const int tok0 = (lane >> 2) < p.MC ? (lane >> 2) : p.MC - 1;
-  const int tok1 = (lane >> 2) + 8 < p.MC ? (lane >> 2) + 8 : p.MC - 1;
-  const uint2* xlane0 = xs + tok0 * kImageRow + (lane & 3);
-  const uint2* xlane1 = xs + tok1 * kImageRow + (lane & 3);
-  const int block_stride = p.MC * kImageRow;
-  const uint8_t* grid_lane = reinterpret_cast<const uint8_t*>(grid_rep) + (lane % kGridCopies) * 8;
-  int64_t t = t_first;
-  int bb = bb_first;
-  int piece_bb0 = bb_first;                                        // first block of the current piece
-  for (int64_t i = 0; i < n_items && !failed; ++i) {
-    const int st = static_cast<int>(i % STAGES);
-    const uint32_t ph = static_cast<uint32_t>((i / STAGES) & 1);
-    if (!mbar_wait_bounded(&bars[st], ph, lane == 0 ? p.err : nullptr)) {
-      failed = true;
-      i_fail = i;
-      break;
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = g + 8 * nt < p.MC ? g + 8 * nt : p.MC - 1;
+      const uint32_t rowb = xs0 + static_cast<uint32_t>(col) * kImageRowBytes + q * 16u;
+      xE[nt] = rowb + (col & 1) * 64u;
+      xO[nt] = rowb - (col & 1) * 64u;
+      xS[nt] = ss0 + (static_cast<uint32_t>(col) * 4u + q) * 8u;
     }
-    uint8_t* stage = ring + st * STAGE_BYTES;
-    const uint8_t* chunk[NMAT];
-#pragma unroll
-    for (int a = 0; a < NMAT; ++a) chunk[a] = stage + a * CH;
-    compute_block<QT, NT, NMAT>(chunk, xlane0 + bb * block_stride, xlane1 + bb * block_stride, grid_lane, lane,
-                                acc);
-    __syncwarp();
+  }
+  const uint32_t blk_stride = static_cast<uint32_t>(p.MC) * kImageRowBytes;
+  const uint32_t sblk_stride = static_cast<uint32_t>(p.MC) * kSumRowBytes;
+  const uint8_t* grid_lane = reinterpret_cast<const uint8_t*>(grid_rep) + (lane % kGridCopies) * 8;
 
-    const bool run_end = (bb == p.Bs - 1) || (i == n_items - 1);
-    if (run_end) {
-      // ---- a piece of tile t ends here; the stage just read is the epilogue scratch ----
-      float* epi = reinterpret_cast<float*>(stage);
-      const int64_t run0 = t * p.Bs;
-      const bool whole = (p.S == 1) && (piece_bb0 == 0) && (bb == p.Bs - 1);
-      if (whole) {
-        tile_epilogue<NT, NMAT, EPI>(p, t, acc, epi, lane, best);
-      } else {
-        const int w_first = warp_of(run0, Fs, Ws);
-        const int w_last = warp_of(run0 + p.Bs - 1, Fs, Ws);
-        const int pieces = w_last - w_first + 1;
-        const int my_j = wseg - w_first;
-        const int total = pieces * p.S;
-        const int64_t slot_stride = static_cast<int64_t>(NMAT) * NT * 4 * 32;
-        float* my_slot = p.partials + ((t * p.S + seg) * p.J + my_j) * slot_stride;
+  uint64_t best[2 * NT];
 #pragma unroll
-        for (int a = 0; a < NMAT; ++a)
+  for (int i = 0; i < 2 * NT; ++i) best[i] = 0ull;
+  int slot = 0;
+  uint32_t phase = 0;
+  int done = 0, fail_at = 0;
+  while (done < n_items && !failed) {
+    const int run = n_items - done < p.Bs - bb ? n_items - done : p.Bs - bb;   // blocks of tile t in a row
+    float acc[NMAT][NT][4];
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+    for (int a = 0; a < NMAT; ++a)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) my_slot[((a * NT + nt) * 4 + e) * 32 + lane] = acc[a][nt][e];
-        __threadfence();
-        __syncwarp();
-        uint32_t old = 0;
-        if (lane == 0) old = atomicAdd(p.tile_cnt + t, 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == static_cast<uint32_t>(total - 1)) {
-          __threadfence();
-          float v[NMAT][NT][4];
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int a = 0; a < NMAT; ++a)
+        for (int i = 0; i < 4; ++i) acc[a][nt][i] = 0.f;
+    uint32_t bE[NT], bO[NT], bS[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
-          // pieces in fixed k order (segment s, piece j); slot loads are issued in
-          // batches of UB slots ahead of the in-order adds (2 for the two-matrix
-          // gate/up, whose 4-slot batch would push the kernel past its register
-          // budget into spills)
-          constexpr int VN = NMAT * NT * 4;
-          constexpr int UB = VN >= 16 ? 2 : 4;
-          const int n_slots = p.S * pieces;
-          const int my_slot_idx = seg * pieces + my_j;
-          for (int base = 0; base < n_slots; base += UB) {
-            float buf[UB][VN];
-#pragma unroll
-            for (int u = 0; u < UB; ++u) {
-              const int sj = base + u;
-              if (sj < n_slots && sj != my_slot_idx) {
-                const int ss = sj / pieces, jj = sj - ss * pieces;
-                const float* sl = p.partials + ((t * p.S + ss) * p.J + jj) * slot_stride + lane;
-#pragma unroll
-                for (int e = 0; e < VN; ++e) buf[u][e] = __ldcg(sl + e * 32);
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < UB; ++u) {
-              const int sj = base + u;
-              if (sj < n_slots) {
-#pragma unroll
-                for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-                  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                      v[a][nt][e] += sj == my_slot_idx ? acc[a][nt][e] : buf[u][(a * NT + nt) * 4 + e];
-              }
-            }
-          }
-          tile_epilogue<NT, NMAT, EPI>(p, t, v, epi, lane, best);
-          if (lane == 0) p.tile_cnt[t] = 0u;
-        }
+    for (int nt = 0; nt < NT; ++nt) {
+      bE[nt] = xE[nt] + bb * blk_stride;
+      bO[nt] = xO[nt] + bb * blk_stride;
+      bS[nt] = xS[nt] + bb * sblk_stride;
+    }
+    for (int r = 0; r < run; ++r) {
+      if (!mbar_wait_bounded(&bars[slot], phase, lane == 0 ? p.err : nullptr)) {
+        failed = true;
+        fail_at = done + r;
+        break;
       }
+      LaneData<QT, NMAT> Ld;
+      load_lane<QT, NMAT>(ring + slot * STAGE_BYTES, lane, Ld);
+      // every lane's reads of the stage are ordered before the refill (warp barrier,
+      // then the generic -> async proxy fence of the issuing lane)
+      __syncwarp();
+      if (lane == 0 && done + r + STAGES < n_items) {
+        fence_proxy_async_smem();
+        issue(slot);
+      }
+      if (++slot == STAGES) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      compute_lane<QT, NT, NMAT>(Ld, bE, bO, bS, grid_lane, acc);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        bE[nt] += blk_stride;
+        bO[nt] += blk_stride;
+        bS[nt] += sblk_stride;
+      }
+    }
+    if (failed) break;
+
+    // ---- blocks [bb, bb + run) of tile t are summed ----
+    const bool whole = (p.S == 1) && (bb == 0) && (run == p.Bs);
+    if (whole) {
+      tile_finish<NT, NMAT, EPI>(p, t, acc, lane, epi, best);
+    } else {
+      // a piece of a split tile: fragment-ordered partials, the last arriver adds all
+      // pieces in fixed k order (segment, piece) and runs the epilogue
+      const int64_t run0 = t * p.Bs;
+      const int w_first = warp_of(run0, Fs, Ws);
+      const int w_last = warp_of(run0 + p.Bs - 1, Fs, Ws);
+      const int pieces = w_last - w_first + 1;
+      const int my_j = wseg - w_first;
+      const int total = pieces * p.S;
+      const int64_t slot_stride = static_cast<int64_t>(NMAT) * NT * 4 * 32;
+      float* my_slot = p.partials + ((t * p.S + seg) * p.J + my_j) * slot_stride;
 #pragma unroll
       for (int a = 0; a < NMAT; ++a)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[a][nt][e] = 0.f;
+          for (int e = 0; e < 4; ++e) my_slot[((a * NT + nt) * 4 + e) * 32 + lane] = acc[a][nt][e];
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(p.tile_cnt + t, 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == static_cast<uint32_t>(total - 1)) {
+        __threadfence();
+        float v[NMAT][NT][4];
+#pragma unroll
+        for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[a][nt][e] = 0.f;
+        // slot loads are issued in batches of UB slots ahead of the in-order adds (2
+        // for the two-matrix gate/up, whose 4-slot batch would spill registers)
+        constexpr int VN = NMAT * NT * 4;
+        constexpr int UB = VN >= 16 ? 2 : 4;
+        const int n_slots = p.S * pieces;
+        const int my_slot_idx = seg * pieces + my_j;
+        for (int base = 0; base < n_slots; base += UB) {
+          float buf[UB][VN];
+#pragma unroll
+          for (int u = 0; u < UB; ++u) {
+            const int sj = base + u;
+            if (sj < n_slots && sj != my_slot_idx) {
+              const int ss = sj / pieces, jj = sj - ss * pieces;
+              const float* sl = p.partials + ((t * p.S + ss) * p.J + jj) * slot_stride + lane;
+#pragma unroll
+              for (int e = 0; e < VN; ++e) buf[u][e] = __ldcg(sl + e * 32);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < UB; ++u) {
+            const int sj = base + u;
+            if (sj < n_slots) {
+#pragma unroll
+              for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    v[a][nt][e] += sj == my_slot_idx ? acc[a][nt][e] : buf[u][(a * NT + nt) * 4 + e];
+            }
+          }
+        }
+        tile_finish<NT, NMAT, EPI>(p, t, v, lane, epi, best);
+        if (lane == 0) p.tile_cnt[t] = 0u;
+      }
     }
-    // refill the stage with the item STAGES ahead.  Every lane's reads of the stage
-    // have returned (their values fed the mma); no proxy fence is needed before an
-    // async-proxy write that follows generic-proxy reads.
-    __syncwarp();
-    if (lane == 0 && i + STAGES < n_items) issue(st);
-    if (++bb == p.Bs) {
+    done += run;
+    bb += run;
+    if (bb == p.Bs) {
       bb = 0;
       ++t;
     }
-    if (run_end) piece_bb0 = bb;
   }
 
   if (failed) {
-    // let every copy this warp issued land before the CTA can exit
-    for (int64_t i = i_fail; i < n_items && i < i_fail + STAGES; ++i)
-      mbar_wait_bounded(&bars[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), nullptr);
+    // let every copy this warp issued land before the CTA can exit: items fail_at ..
+    // fail_at + STAGES - 1 (those that exist) were issued and not consumed
+    for (int i = fail_at; i < n_items && i < fail_at + STAGES; ++i) {
+      mbar_wait_bounded(&bars[slot], phase, nullptr);
+      if (++slot == STAGES) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
   }
 
   if constexpr (EPI == EPI_ARGMAX) {
-    // per-token keys: lanes -> warp -> CTA (shared) -> all CTAs (atomicMax on the
-    // global keys; max is order-independent, so the result is deterministic)
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, 16);
-    best = other > best ? other : best;
-    if (lane < 16) wbest[warp * 16 + lane] = best;
+    // per-token keys: lanes -> warp (max over g of the lanes sharing q) -> CTA (shared)
+    // -> all CTAs (atomicMax on the global keys; max is order-independent, so the
+    // result is deterministic)
+#pragma unroll
+    for (int i = 0; i < 2 * NT; ++i)
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        const uint64_t o = __shfl_xor_sync(0xffffffffu, best[i], off);
+        best[i] = o > best[i] ? o : best[i];
+      }
+    if (g == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int tok = 8 * nt + 2 * q + j;
+          if (tok < 16) wbest[warp * 16 + tok] = best[2 * nt + j];
+        }
+    }
     __syncthreads();
     uint32_t* flag = reinterpret_cast<uint32_t*>(wbest + WPC * 16);
     if (threadIdx.x < p.M) {
@@ -750,7 +910,7 @@ static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dt
   for (int s = 1; s <= P.NB; ++s) {
     if (P.NB % s) continue;
     const uint32_t xs = static_cast<uint32_t>(P.NB / s) * P.MC * kImageRowBytes;
-    const SmemLayout Ls = smem_layout(qt, P.nmat, P.wpc, P.stages, P.NB / s, P.MC);
+    const SmemLayout Ls = smem_layout(qt, P.nmat, P.wpc, P.stages, P.NB / s, P.MC, P.CG);
     if (xs <= kXsBudget && Ls.total <= smem_limit) {
       P.S = s;
       break;
@@ -767,14 +927,14 @@ static int make_plan(int qt, int epi, int64_t n_rows, int64_t k, int m, int x_dt
   const int64_t weff = std::min<int64_t>(Fs, static_cast<int64_t>(P.Cs) * P.wpc);
   const int64_t per_warp = Fs / weff;
   P.J = static_cast<int>(std::min<int64_t>(P.Bs, P.Bs / std::max<int64_t>(1, per_warp) + 2));
-  const SmemLayout L = smem_layout(qt, P.nmat, P.wpc, P.stages, P.Bs, P.MC);
+  const SmemLayout L = smem_layout(qt, P.nmat, P.wpc, P.stages, P.Bs, P.MC, P.CG);
   P.smem = L.total;
   size_t off = 256;
   P.off_cnt = off;
   off += (static_cast<size_t>(P.T) * 4 + 255) & ~size_t(255);
   P.off_best = off;  // end of the region that must be zero before a launch
   P.off_img = off;
-  if (x_dtype != DT_IMAGE) off += (static_cast<size_t>(P.NB) * P.MC * kImageRowBytes + 255) & ~size_t(255);
+  if (x_dtype != DT_IMAGE) off += (static_cast<size_t>(P.NB) * P.MC * (kImageRowBytes + kSumRowBytes) + 255) & ~size_t(255);
   P.off_part = off;
   off += static_cast<size_t>(P.T) * P.S * P.J * P.nmat * P.NT * 4 * 32 * sizeof(float);
   P.ws_bytes = off;
@@ -829,7 +989,7 @@ size_t activation_image_bytes(int m, int64_t k, int x_dtype) {
   if (m < 1 || k <= 0 || k % kQK) return 0;
   const int mc = m * cols_per_token(x_dtype);
   if (mc > 16) return 0;
-  return static_cast<size_t>(k / kQK) * mc * kImageRowBytes;
+  return static_cast<size_t>(k / kQK) * mc * (kImageRowBytes + kSumRowBytes);
 }
 
 static int stage_image(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, void* image, bool sums,
