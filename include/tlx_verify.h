@@ -197,6 +197,46 @@ int tlx_h_argmax(const void* logits, int dtype, int64_t n, int32_t* tok_slot, in
 int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
                      const int32_t* drafts, int n_drafts, int32_t* accept_out, void* stream);
 
+/* ---- the sharded verify step over peer memory (one process per GPU) ---------------
+ * Every rank owns one communication buffer of tlx_peer_buffer_bytes(world, m, ny)
+ * bytes (zeroed once, 256-byte aligned) and maps every other rank's buffer into its
+ * process (tlx_ipc_handle on the owner, tlx_ipc_open on the others); peer_bufs[r] is
+ * rank r's buffer as mapped in the calling process.  The step replaces NCCL's
+ * all-reduce of the down partials and all-gather of the head keys (the collectives of
+ * the row / k / vocabulary split):
+ *   tlx_gemv_peer         the down projection shard (k split): its fp32 partial y goes
+ *                         straight into every rank's buffer with ordinary stores over
+ *                         NVLink, and its last CTA raises this rank's flag there;
+ *   tlx_head_argmax_peer  the vocabulary shard of the fused head: every CTA then adds
+ *                         the ranks' partials (rank order, + residual) into y, and the
+ *                         last CTA exchanges the 11 argmax keys with every rank, merges
+ *                         them and runs greedy accept (the same result on every rank).
+ * Call them in this order once per step on every rank (the down kernel of the next
+ * step may run while a peer still reads the previous step's slots: they are
+ * double-buffered).  Waits on peers are bounded; on timeout the workspace error word
+ * gets TLX_WS_ERR_PEER_TIMEOUT.  No reference counterpart: the reference runs on one
+ * GPU (README.md:412-413). */
+#define TLX_WS_ERR_PEER_TIMEOUT 4u
+size_t tlx_peer_buffer_bytes(int world, int m, int64_t ny);
+size_t tlx_ipc_handle_bytes(void);
+/* handle_out (tlx_ipc_handle_bytes) names the allocation holding ptr; offset_out = ptr
+ * minus the allocation's base */
+int tlx_ipc_handle(const void* ptr, void* handle_out, uint64_t* offset_out);
+/* maps a peer's allocation (peer access enabled); *ptr_out = its base + offset */
+int tlx_ipc_open(const void* handle, uint64_t offset, void** base_out, void** ptr_out);
+int tlx_ipc_close(void* base);
+/* a zeroed communication buffer that is an allocation of its own (set-up time only) */
+int tlx_peer_buffer_alloc(size_t bytes, void** out);
+int tlx_peer_buffer_free(void* p);
+int tlx_gemv_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, void* ws, size_t ws_bytes,
+                  void* stream);
+int tlx_head_argmax_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
+                         int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
+                         const int32_t* drafts, int n_drafts, int32_t* accept_out, int world, int rank,
+                         void* const* peer_bufs, int64_t ny, const float* residual, int64_t ldr, float* y,
+                         int64_t ldy, void* ws, size_t ws_bytes, void* stream);
+
 /* ---- greedy acceptance ------------------------------------------------------------
  * acc36: m = longest prefix amds[s] == drafts[s], s < k; mb[0] = m;
  * eb[0] = m, eb[1] = amds[m].  engine/mm/MM_P7_acc36.cu:11-25. */

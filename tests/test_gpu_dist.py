@@ -1,6 +1,10 @@
-"""The sharded verify step on 2 GPUs (NCCL) against the oracle: FFN rows/k split
-with one all-reduce, vocabulary split with one key all-gather, merge + accept on
-every rank.  Skipped on single-GPU boxes."""
+"""The sharded verify step on 2..8 GPUs against the oracle: FFN rows / k split,
+vocabulary split, the partials and argmax keys exchanged over peer memory inside
+the kernels (comm="peer") or by NCCL collectives plus a merge kernel
+(comm="nccl"); every rank must hold the same ids, accept record and y.  World
+sizes beyond the box's GPU count are skipped.  A single-GPU test drives the peer
+kernels' bounded waits into their timeout (a flag nothing sets) and checks the
+error word."""
 import os
 import socket
 
@@ -20,7 +24,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, comm="peer", steps=3):
     import datetime
 
     import torch.distributed as dist
@@ -48,7 +52,7 @@ def _rank(rank, world, port, q):
              "up": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(ru, f0, f1), s.dim),
              "down": ops.pack_tiles("q6_k", tdist.shard_gguf_cols(rd, f0, f1, 210), f1 - f0),
              "head": ops.pack_tiles("q6_k", tdist.shard_gguf_rows(rh, v0, v1), s.dim)}
-        step = tdist.ShardedVerifyStep(s, rank, world, weights=w)
+        step = tdist.ShardedVerifyStep(s, rank, world, weights=w, comm=comm)
         x64 = synth.bf16_bits_to_f32(xb).astype(np.float64)
         h64 = synth.bf16_bits_to_f32(hb).astype(np.float64)
         _, idx_ref, _ = oracle.head_argmax(h64, rh, "q6_k")
@@ -58,23 +62,32 @@ def _rank(rank, world, port, q):
                         torch.from_numpy(hb.view(np.int16)).cuda().view(torch.bfloat16),
                         res=torch.from_numpy(res).cuda(), drafts=torch.from_numpy(drafts).cuda())
         step.capture()
-        for _ in range(3):
+        ys = []
+        for _ in range(steps):       # several steps: the peer slots alternate by step parity
             step.replay()
-        torch.cuda.synchronize()
+            torch.cuda.synchronize()
+            ys.append(step.y.clone())
         _, y_ref = oracle.ffn_f64(x64, rg, ru, rd, residual=res)
         y = step.y.cpu().numpy()
         err = float((np.abs(y - y_ref).max(axis=1) / np.linalg.norm(y_ref, axis=1)).max())
+        same = all(torch.equal(ys[0], t) for t in ys[1:])
+        werr = [w_.error() for w_ in step.ws.values()]
         out = (rank, err, step.out_idx.cpu().tolist(), idx_ref.tolist(), step.accept_out.cpu().tolist(),
-               list(oracle.accept(idx_ref, drafts)))
+               list(oracle.accept(idx_ref, drafts)), same, werr, y.tobytes())
         step.release()
         q.put(out)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_verify_step_two_gpus():
-    world = 2
+WORLDS = [w for w in (2, 4, 8)]
+
+
+@pytest.mark.parametrize("comm", ["peer", "nccl"])
+@pytest.mark.parametrize("world", WORLDS)
+def test_sharded_verify_step(world, comm):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.path.join(here, "golden"),
@@ -82,21 +95,73 @@ def test_sharded_verify_step_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, comm)) for r in range(world)]
     for p_ in procs:
         p_.start()
     results = []
     try:
         for _ in range(world):
-            results.append(q.get(timeout=240))
+            results.append(q.get(timeout=300))
     finally:
         for p_ in procs:
             p_.join(timeout=60)
     assert all(p_.exitcode == 0 for p_ in procs)
-    for rank, err, idx, idx_ref, acc, acc_ref in results:
+    for rank, err, idx, idx_ref, acc, acc_ref, same, werr, _ in results:
         assert err <= 2e-3 and err <= 1e-4, (rank, err)
         assert idx == idx_ref, rank
         assert acc == acc_ref, rank
+        assert same, f"rank {rank}: y differs between steps"
+        assert werr == [0, 0, 0], (rank, werr)
+    # every rank holds the same y (the partials are added in rank order everywhere)
+    assert len({r[-1] for r in results}) == 1
+
+
+def test_peer_wait_times_out_into_error_word():
+    # Failure detection without a GPU fault: rank 0 of a 2-rank step whose rank 1 never
+    # runs.  Both buffers live on this GPU; the down kernel sends its partial and raises
+    # its flag, the head kernel then waits for rank 1's down flag and keys, which nothing
+    # sets: the bounded waits give up, raise TLX_WS_ERR_PEER_TIMEOUT in the workspace
+    # error word and the kernel returns (the context stays usable).
+    import ctypes
+
+    from thunderllamax_b200 import _lib, ops, synth
+
+    ops.require_device()
+    L = _lib.lib()
+    m, dim, ffn, vocab = 11, 512, 512, 1000
+    nb = int(L.tlx_peer_buffer_bytes(2, m, dim))
+    bufs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        _lib.check(L.tlx_peer_buffer_alloc(nb, ctypes.byref(p)), "alloc")
+        bufs.append(p.value)
+    ptrs = (ctypes.c_void_p * 2)(*bufs)
+    try:
+        rng = np.random.default_rng(3)
+        wd = ops.pack_tiles("q6_k", synth.q6k_blocks(rng, dim, ffn), ffn)
+        wh = ops.pack_tiles("q6_k", synth.q6k_blocks(rng, vocab, dim), dim)
+        img = ops.stage(torch.randn((m, ffn), device="cuda").half())
+        ws_d = ops.Workspace.for_shape(ops.MODE_STORE, "q6_k", dim, ffn, m, "image")
+        ws_h = ops.Workspace.for_shape(ops.MODE_ARGMAX, "q6_k", vocab, dim, m)
+        h = torch.randn((m, dim), device="cuda").half()
+        y = torch.zeros((m, dim), device="cuda")
+        idx = torch.zeros(m, dtype=torch.int32, device="cuda")
+        s = ops._stream(h)
+        _lib.check(L.tlx_gemv_peer(ops.qtype_id("q6_k"), ops._ptr(wd), None, ops._ptr(img.buf), _lib.TLX_DT_IMAGE,
+                                   0, m, dim, ffn, 2, 0, ptrs, ops._ptr(ws_d.buf), ws_d.nbytes, s), "gemv_peer")
+        _lib.check(L.tlx_head_argmax_peer(ops.qtype_id("q6_k"), ops._ptr(wh), None, ops._ptr(h), _lib.TLX_DT_F16,
+                                          dim, m, vocab, dim, 0, None, ops._ptr(idx), None, 0, None, 2, 0, ptrs,
+                                          dim, None, 0, ops._ptr(y), dim, ops._ptr(ws_h.buf), ws_h.nbytes, s),
+                   "head_argmax_peer")
+        torch.cuda.synchronize()
+        assert ws_d.error() == 0
+        assert ws_h.error() & 4, ws_h.error()          # TLX_WS_ERR_PEER_TIMEOUT
+        # the context is still usable
+        assert torch.equal(torch.ones(4, device="cuda").sum().cpu(), torch.tensor(4.0))
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            L.tlx_peer_buffer_free(b)
 
 
 def _spawn_gpu(target, world=2):

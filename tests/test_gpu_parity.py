@@ -551,3 +551,20 @@ def test_verify_step_host_path_copies_every_call():
         step.replay()
         torch.cuda.synchronize()
         assert step.accept_out.cpu().tolist() == outp[:2].tolist()
+
+
+@pytest.mark.parametrize("qtype,n,k,rows,cols", [("q6_k", 20000, 512, (8704, 17408), None),
+                                                 ("iq3_xxs", 20000, 512, (16, 8208), None),
+                                                 ("q6_k", 512, 17408, None, (8704, 17408)),
+                                                 ("q6_k", 300, 2048, (0, 300), (256, 1024))])
+def test_synth_tiled_slices_one_model(qtype, n, k, rows, cols):
+    # a shard of the seeded model (rows and / or a 256-aligned column range) equals the
+    # same slice of the whole matrix, across the 8192-row generation chunks
+    from thunderllamax_b200.verify import synth_tiled
+    r0, r1 = rows if rows else (0, n)
+    k0, k1 = cols if cols else (0, k)
+    whole = synth.matrix_rows(qtype, n, k, 99)
+    bb = synth.BLOCK_BYTES[qtype]
+    ref = np.ascontiguousarray(whole[r0:r1, (k0 // 256) * bb:(k1 // 256) * bb])
+    got = synth_tiled(qtype, n, k, 99, rows=rows, cols=cols)
+    assert torch.equal(got, ops.pack_tiles(qtype, ref, k1 - k0))

@@ -642,6 +642,52 @@ int tlx_argmax_rows(const void* logits, int dtype, int m, int64_t n, int64_t ld,
   return TLX_ERR_DTYPE;
 }
 
+size_t tlx_peer_buffer_bytes(int world, int m, int64_t ny) { return peer_buffer_bytes(world, m, ny); }
+
+// the PeerParams of a call: host array of the ranks' buffers as mapped here
+static int make_peer(int world, int rank, void* const* bufs, int m, int64_t ny, PeerParams& pr) {
+  if (!bufs) return TLX_ERR_NULL;
+  if (world < 2 || world > kMaxPeers || rank < 0 || rank >= world) return TLX_ERR_SHAPE;
+  pr = PeerParams{};
+  pr.world = world;
+  pr.rank = rank;
+  for (int r = 0; r < world; ++r) pr.base[r] = static_cast<uint8_t*>(bufs[r]);
+  pr.m = m;
+  pr.ny = ny;
+  return TLX_OK;
+}
+
+int tlx_gemv_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
+                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, void* ws, size_t ws_bytes,
+                  void* stream) {
+  PeerParams pr;
+  const int rc = make_peer(world, rank, peer_bufs, m, n_rows, pr);
+  if (rc) return rc;
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  return run_gemv(kEpiStore, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr, TLX_DT_F32,
+                  n_rows, 0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, ws, ws_bytes, g_max_ctas,
+                  as_stream(stream), &pr);
+}
+
+int tlx_head_argmax_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
+                         int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
+                         const int32_t* drafts, int n_drafts, int32_t* accept_out, int world, int rank,
+                         void* const* peer_bufs, int64_t ny, const float* residual, int64_t ldr, float* y,
+                         int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+  PeerParams pr;
+  const int rc = make_peer(world, rank, peer_bufs, m, ny, pr);
+  if (rc) return rc;
+  if (!y) return TLX_ERR_NULL;
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  pr.residual = residual;
+  pr.ldr = ldr;
+  pr.y = y;
+  pr.ldy = ldy;
+  return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
+                  TLX_DT_F32, 0, row_offset, out_max, out_idx, nullptr, drafts, n_drafts, accept_out, ws, ws_bytes,
+                  g_max_ctas, as_stream(stream), &pr);
+}
+
 int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
                      const int32_t* drafts, int n_drafts, int32_t* accept_out, void* stream) {
   if (!keys) return TLX_ERR_NULL;

@@ -21,6 +21,7 @@ namespace tlx {
 enum : uint32_t {
   ERR_MBAR_TIMEOUT = 1u,   // a bulk copy never completed within the poll budget
   ERR_BAD_PARAM = 2u,      // device-side parameter check failed
+  ERR_PEER_TIMEOUT = 4u,   // a peer's flag never arrived within the poll budget
 };
 
 constexpr uint32_t kMbarPollLimit = 1u << 22;  // polls of <= kTryWaitHintNs each: a few seconds at most

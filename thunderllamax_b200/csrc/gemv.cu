@@ -63,6 +63,49 @@ __host__ __device__ __forceinline__ int64_t sums_index(int64_t b, int col, int q
   return static_cast<int64_t>(NB) * MC * kImageRow + (b * MC + col) * 4 + q;
 }
 
+// ---- peer exchange of the sharded verify step (one process per GPU, world > 1) ----
+// Every rank owns one buffer of peer_buffer_bytes(world, m, ny); base[r] is rank r's
+// buffer as mapped in this process.  Layout (bytes):
+//   0     epoch: steps completed on this rank (local)
+//   64    arrival counter of the down kernel's CTAs (local)
+//   256   down flags [2][kMaxPeers], 16 bytes apart: rank r's partial y of the step
+//         with parity p is complete in this buffer once flag [p][r] == epoch + 1
+//   512   key flags  [2][kMaxPeers], the same for rank r's argmax keys
+//   1024  keys [2][kMaxPeers][16] u64
+//   4096  y partials [2][world][m][ny] fp32
+// Partials and keys are double-buffered by step parity: a rank can be at most one
+// step ahead of another, because every step waits for all ranks' partials.
+constexpr uint32_t kPeerEpoch = 0, kPeerDownCnt = 64, kPeerDownFlags = 256, kPeerKeyFlags = 512, kPeerKeys = 1024,
+                   kPeerY = 4096;
+
+size_t peer_buffer_bytes(int world, int m, int64_t ny) {
+  if (world < 2 || world > kMaxPeers || m < 1 || m > 16 || ny < 1) return 0;
+  return kPeerY + 2ull * static_cast<size_t>(world) * static_cast<size_t>(m) * static_cast<size_t>(ny) * 4ull;
+}
+
+__device__ __forceinline__ uint32_t* peer_flag(uint8_t* buf, uint32_t off, uint32_t par, int src) {
+  return reinterpret_cast<uint32_t*>(buf + off + (par * kMaxPeers + src) * 16u);
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// bounded wait until a peer has set *flag to v (the flag lives in this rank's own
+// buffer); on timeout raise ERR_PEER_TIMEOUT and go on (the step's results are then
+// not valid, but nothing hangs)
+__device__ __forceinline__ bool wait_peer_flag(const uint32_t* flag, uint32_t v, uint32_t* err) {
+  for (uint32_t i = 0; i < kMbarPollLimit; ++i) {
+    if (ld_acquire_sys(flag) == v) return true;
+    __nanosleep(64);
+  }
+  if (err) atomicOr(err, ERR_PEER_TIMEOUT);
+  return false;
+}
+
 struct GemvParams {
   const uint8_t* w0;
   const uint8_t* w1;
@@ -91,9 +134,12 @@ struct GemvParams {
   unsigned long long* gkey;  // [16] running per-token argmax keys (zero between launches)
   uint32_t* done_cnt;
   uint32_t* err;
+  PeerParams peer;           // world <= 1: no exchange
 };
 
 __host__ __device__ constexpr bool needs_sums(int qt) { return qt == QT_Q4_K || qt == QT_Q5_K; }
+
+
 
 // ---- shared-memory layout (same arithmetic on host and device) ----
 // A warp loads each chunk into registers and hands its ring stage back at once, so
@@ -389,7 +435,7 @@ __device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const 
 // 8 nt + 2q + (e & 1); here a column is a token.
 template <int NT, int NMAT, int EPI>
 __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4], int lane,
-                                              uint64_t (&best)[2 * NT]) {
+                                              uint64_t (&best)[2 * NT], uint32_t par) {
   const int g = lane >> 2, q = lane & 3;
   const int64_t row0 = t * kTileRows;
   if constexpr (EPI == EPI_ARGMAX) {
@@ -443,6 +489,21 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, co
           }
         }
     }
+  } else if (p.peer.world > 1) {
+    // sharded down projection: this rank's partial of the tile goes to every rank's
+    // buffer (slot [par][rank]); the head kernel adds the slots in rank order
+    const PeerParams& pr = p.peer;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 8 * nt + 2 * q + (e & 1);
+        const int64_t row = row0 + g + 8 * (e >> 1);
+        if (col < p.M && row < p.n_rows) {
+          const int64_t off = ((static_cast<int64_t>(par) * pr.world + pr.rank) * pr.m + col) * pr.ny + row;
+          for (int r = 0; r < pr.world; ++r) reinterpret_cast<float*>(pr.base[r] + kPeerY)[off] = v[0][nt][e];
+        }
+      }
   } else {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -466,9 +527,9 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, co
 // the warp's scratch, then the token-column epilogue
 template <int NT, int NMAT, int EPI>
 __device__ __forceinline__ void tile_finish(const GemvParams& p, int64_t t, const float (&v)[NMAT][NT][4], int lane,
-                                            float* epi, uint64_t (&best)[2 * NT]) {
+                                            float* epi, uint64_t (&best)[2 * NT], uint32_t par) {
   if (p.CG == 1) {
-    tile_epilogue<NT, NMAT, EPI>(p, t, v, lane, best);
+    tile_epilogue<NT, NMAT, EPI>(p, t, v, lane, best, par);
     return;
   }
   const int g = lane >> 2, q = lane & 3;
@@ -496,7 +557,7 @@ __device__ __forceinline__ void tile_finish(const GemvParams& p, int64_t t, cons
         vt[a][nt][e] = s;
       }
   __syncwarp();
-  tile_epilogue<NT, NMAT, EPI>(p, t, vt, lane, best);
+  tile_epilogue<NT, NMAT, EPI>(p, t, vt, lane, best, par);
 }
 
 template <int QT, int NT, int EPI, int WPC, int STAGES>
@@ -567,6 +628,10 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   // read or written, so wait for it to complete.
   griddep_wait();
   griddep_launch_dependents();
+  // sharded step: this step's number on this rank (it selects the parity slots)
+  const uint32_t ep = p.peer.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.peer.base[p.peer.rank] + kPeerEpoch)
+                                       : 0u;
+  const uint32_t par = ep & 1u;
 
   // activations of this k-segment (and their sub-block sums): bulk copies of the
   // image slices
@@ -579,7 +644,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.ximg) + static_cast<size_t>(seg) * xbytes;
     for (uint32_t off = 0; off < xbytes; off += 32768u)
       bulk_g2s(smem + L.xs + off, src + off, xbytes - off < 32768u ? xbytes - off : 32768u, xbar);
-    if (sbytes) {
+    if constexpr (needs_sums(QT)) {
       const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(p.ximg) +
                             static_cast<size_t>(p.NB) * p.MC * kImageRowBytes + static_cast<size_t>(seg) * sbytes;
       for (uint32_t off = 0; off < sbytes; off += 32768u)
@@ -663,7 +728,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
     // ---- blocks [bb, bb + run) of tile t are summed ----
     const bool whole = (p.S == 1) && (bb == 0) && (run == p.Bs);
     if (whole) {
-      tile_finish<NT, NMAT, EPI>(p, t, acc, lane, epi, best);
+      tile_finish<NT, NMAT, EPI>(p, t, acc, lane, epi, best, par);
     } else {
       // a piece of a split tile: fragment-ordered partials, the last arriver adds all
       // pieces in fixed k order (segment, piece) and runs the epilogue
@@ -727,7 +792,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
             }
           }
         }
-        tile_finish<NT, NMAT, EPI>(p, t, v, lane, epi, best);
+        tile_finish<NT, NMAT, EPI>(p, t, v, lane, epi, best, par);
         if (lane == 0) p.tile_cnt[t] = 0u;
       }
     }
@@ -747,6 +812,25 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       if (++slot == STAGES) {
         slot = 0;
         phase ^= 1u;
+      }
+    }
+  }
+
+  if constexpr (EPI == EPI_STORE) {
+    if (p.peer.world > 1) {
+      // the partials of this CTA's tiles are written to every rank: make them visible
+      // at system scope, count the CTAs, and the last one raises this rank's down flag
+      // (slot [par][rank]) in every rank's buffer
+      const PeerParams& pr = p.peer;
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        uint32_t* cnt = reinterpret_cast<uint32_t*>(pr.base[pr.rank] + kPeerDownCnt);
+        if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
+          __threadfence_system();
+          for (int r = 0; r < pr.world; ++r) st_release_sys(peer_flag(pr.base[r], kPeerDownFlags, par, pr.rank), ep + 1u);
+          *cnt = 0u;
+        }
       }
     }
   }
@@ -782,6 +866,24 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       if (b) atomicMax(p.gkey + threadIdx.x, static_cast<unsigned long long>(b));
       __threadfence();
     }
+    const PeerParams& pr = p.peer;
+    if (pr.world > 1) {
+      // sharded step: y = residual + the ranks' partials of the down projection (in
+      // rank order), this CTA's slice, once every rank's down flag of this step is up
+      if (threadIdx.x < pr.world)
+        wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerDownFlags, par, threadIdx.x), ep + 1u, p.err);
+      __syncthreads();
+      const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
+      const int64_t per = (total + gridDim.x - 1) / gridDim.x;
+      const int64_t i0 = blockIdx.x * per, i1 = i0 + per < total ? i0 + per : total;
+      const float* part = reinterpret_cast<const float*>(pr.base[pr.rank] + kPeerY) + par * pr.world * total;
+      for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
+        float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
+        for (int r = 0; r < pr.world; ++r) s += __ldcv(part + r * total + i);
+        pr.y[tok * pr.ldy + row] = s;
+      }
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
       const uint32_t old = atomicAdd(p.done_cnt, 1u);
@@ -792,8 +894,31 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       // the last CTA: every other CTA's atomicMax happened before its arrival
       __threadfence();
       int32_t* idx_s = reinterpret_cast<int32_t*>(flag + 2);
+      uint64_t b = 0ull;
+      if (threadIdx.x < p.M) b = atomicExch(p.gkey + threadIdx.x, 0ull);  // read and re-arm for the next launch
+      if (pr.world > 1) {
+        // this rank's keys to every rank (slot [par][rank]), then the merge of all
+        // ranks' keys (max: the same result on every rank)
+        if (threadIdx.x < p.M)
+          for (int r = 0; r < pr.world; ++r)
+            reinterpret_cast<uint64_t*>(pr.base[r] + kPeerKeys)[(par * kMaxPeers + pr.rank) * 16 + threadIdx.x] = b;
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0)
+          for (int r = 0; r < pr.world; ++r) st_release_sys(peer_flag(pr.base[r], kPeerKeyFlags, par, pr.rank), ep + 1u);
+        if (threadIdx.x < pr.world)
+          wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerKeyFlags, par, threadIdx.x), ep + 1u, p.err);
+        __syncthreads();
+        if (threadIdx.x < p.M) {
+          const uint64_t* keys = reinterpret_cast<const uint64_t*>(pr.base[pr.rank] + kPeerKeys);
+          for (int r = 0; r < pr.world; ++r) {
+            const uint64_t c = __ldcv(reinterpret_cast<const unsigned long long*>(keys + (par * kMaxPeers + r) * 16 +
+                                                                                   threadIdx.x));
+            b = c > b ? c : b;
+          }
+        }
+      }
       if (threadIdx.x < p.M) {
-        const uint64_t b = atomicExch(p.gkey + threadIdx.x, 0ull);  // read and re-arm for the next launch
         if (p.out_max) p.out_max[threadIdx.x] = key_value(b);
         if (p.out_idx) p.out_idx[threadIdx.x] = key_index(b);
         if (p.out_keys) p.out_keys[threadIdx.x] = b;
@@ -808,6 +933,8 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
           p.accept_out[1] = idx_s[m];
         }
         *p.done_cnt = 0u;
+        // the step is complete on this rank
+        if (pr.world > 1) *reinterpret_cast<volatile uint32_t*>(pr.base[pr.rank] + kPeerEpoch) = ep + 1u;
       }
     }
   }
@@ -854,7 +981,7 @@ static constexpr uint32_t kXsBudget = 124u * 1024u;
 template <int QT, int EPI>
 struct Cfg;
 template <> struct Cfg<QT_Q6_K, EPI_STORE> { static constexpr int WPC = 16, STAGES = 2; };
-template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 16, STAGES = 2; };
+template <> struct Cfg<QT_Q6_K, EPI_ARGMAX> { static constexpr int WPC = 12, STAGES = 2; };
 template <> struct Cfg<QT_Q6_K, EPI_GATEUP> { static constexpr int WPC = 8, STAGES = 2; };
 template <> struct Cfg<QT_IQ3_XXS, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
 template <> struct Cfg<QT_Q4_K, EPI_STORE> { static constexpr int WPC = 12, STAGES = 3; };
@@ -1024,14 +1151,14 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
              int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,
              int y_dtype, int64_t ldy, int64_t row_offset, float* out_max, int32_t* out_idx, uint64_t* out_keys,
              const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
-             cudaStream_t stream) {
+             cudaStream_t stream, const PeerParams* peer) {
   Plan P;
   int rc = make_plan(qt, epi, n_rows, k, m, x_dtype, max_ctas, P);
   if (rc) return rc;
   if (!w0 || !x || !ws) return TLX_ERR_NULL;
   if (epi == EPI_GATEUP && !w1) return TLX_ERR_NULL;
   if (qt == QT_IQ3_XXS && !grid) return TLX_ERR_NULL;
-  if (epi != EPI_ARGMAX && !y) return TLX_ERR_NULL;
+  if (epi != EPI_ARGMAX && !y && !(peer && epi == EPI_STORE)) return TLX_ERR_NULL;
   if (epi == EPI_STORE && y_dtype != DT_F32 && y_dtype != DT_F16) return TLX_ERR_DTYPE;
   if (epi == EPI_GATEUP && y_dtype != DT_F32 && y_dtype != DT_F16 && y_dtype != DT_IMAGE) return TLX_ERR_DTYPE;
   if (epi == EPI_GATEUP && y_dtype == DT_IMAGE && (n_rows % kQK) != 0) return TLX_ERR_SHAPE;
@@ -1048,6 +1175,17 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   if (residual && ldr < n_rows) return TLX_ERR_SHAPE;
   if (epi == EPI_ARGMAX && accept_out && (!drafts || n_drafts < 0 || n_drafts + 1 > m)) return TLX_ERR_SHAPE;
   if (epi == EPI_ARGMAX && (row_offset < 0 || row_offset + n_rows > (int64_t(1) << 32) - 1)) return TLX_ERR_SHAPE;
+  if (peer) {
+    // sharded step: the down projection (STORE, fp32 partial, no residual) or the head
+    if (epi == EPI_GATEUP || peer->world < 2 || peer->world > kMaxPeers || peer->rank < 0 ||
+        peer->rank >= peer->world || peer->m != m || peer->ny < 1)
+      return TLX_ERR_SHAPE;
+    for (int r = 0; r < peer->world; ++r)
+      if (!peer->base[r] || !aligned(peer->base[r], 256)) return TLX_ERR_ALIGN;
+    if (epi == EPI_STORE && (peer->ny != n_rows || residual || y_dtype != DT_F32)) return TLX_ERR_SHAPE;
+    if (epi == EPI_ARGMAX && (!peer->y || peer->ldy < peer->ny || (peer->residual && peer->ldr < peer->ny)))
+      return TLX_ERR_SHAPE;
+  }
 
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const uint2* ximg = static_cast<const uint2*>(x);
@@ -1090,6 +1228,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   gp.tile_cnt = reinterpret_cast<uint32_t*>(wsb + P.off_cnt);
   gp.gkey = reinterpret_cast<unsigned long long*>(wsb + 8);
   gp.partials = reinterpret_cast<float*>(wsb + P.off_part);
+  if (peer) gp.peer = *peer;
   if (epi == EPI_STORE) return dispatch<EPI_STORE>(qt, P, gp, stream);
   if (epi == EPI_GATEUP) return dispatch<EPI_GATEUP>(qt, P, gp, stream);
   return dispatch<EPI_ARGMAX>(qt, P, gp, stream);

@@ -11,11 +11,28 @@ namespace tlx {
 
 enum : int { DT_F32 = TLX_DT_F32, DT_F16 = TLX_DT_F16, DT_BF16 = TLX_DT_BF16, DT_IMAGE = TLX_DT_IMAGE };
 
+// Peer exchange of the sharded verify step (one process per GPU): base[r] = rank r's
+// communication buffer (peer_buffer_bytes) as mapped in this process.  The down
+// projection (STORE) sends its partial y to every rank; the head (ARGMAX) adds the
+// ranks' partials (+ residual) into y and merges the ranks' argmax keys.
+constexpr int kMaxPeers = 8;
+struct PeerParams {
+  int world, rank;
+  uint8_t* base[kMaxPeers];
+  int m;                  // tokens of the y partials
+  int64_t ny;             // y row length (the down projection's rows)
+  const float* residual;  // head: y = residual + the ranks' partials in rank order
+  int64_t ldr;
+  float* y;
+  int64_t ldy;
+};
+size_t peer_buffer_bytes(int world, int m, int64_t ny);
+
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
              int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,
              int y_dtype, int64_t ldy, int64_t row_offset, float* out_max, int32_t* out_idx, uint64_t* out_keys,
              const int32_t* drafts, int n_drafts, int32_t* accept_out, void* ws, size_t ws_bytes, int max_ctas,
-             cudaStream_t stream);
+             cudaStream_t stream, const PeerParams* peer = nullptr);
 size_t gemv_workspace_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
 // one matvec of a projection group: n_rows rows of qtype qt, fp16 output [m][n_rows]
 struct Projection {

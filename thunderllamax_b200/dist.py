@@ -55,6 +55,60 @@ def row_ranges(n_rows: int, world: int, quantum: int = 16) -> list[tuple[int, in
     return out
 
 
+class PeerComm:
+    """The communication buffers of the sharded verify step over peer memory: one per
+    rank on its own GPU (tlx_peer_buffer_alloc), every peer's mapped into this process
+    through a CUDA IPC handle exchanged over the process group.  `ptrs` is the array of
+    the `world` buffers as seen from this process (the kernels write the peers' slots
+    with ordinary stores over NVLink and read only their own buffer)."""
+
+    def __init__(self, rank: int, world: int, m: int, ny: int, group=None):
+        import ctypes
+
+        from . import _lib
+
+        self._lib = L = _lib.lib()
+        nb = int(L.tlx_peer_buffer_bytes(world, m, ny))
+        if nb == 0:
+            raise ValueError(f"no peer buffer for world={world} m={m} ny={ny}")
+        buf = ctypes.c_void_p()
+        _lib.check(L.tlx_peer_buffer_alloc(nb, ctypes.byref(buf)), "peer_buffer_alloc")
+        self.local, self.nbytes = buf.value, nb
+        hsize = int(L.tlx_ipc_handle_bytes())
+        handle = (ctypes.c_uint8 * hsize)()
+        off = ctypes.c_uint64()
+        _lib.check(L.tlx_ipc_handle(self.local, handle, ctypes.byref(off)), "ipc_handle")
+        infos = [None] * world
+        dist.all_gather_object(infos, (bytes(handle), int(off.value)), group=group)
+        self.opened, ptrs = [], []
+        for r, (h, o) in enumerate(infos):
+            if r == rank:
+                ptrs.append(self.local)
+                continue
+            hb = (ctypes.c_uint8 * hsize).from_buffer_copy(h)
+            base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(L.tlx_ipc_open(hb, o, ctypes.byref(base), ctypes.byref(ptr)), "ipc_open")
+            self.opened.append(base.value)
+            ptrs.append(ptr.value)
+        self.ptrs = (ctypes.c_void_p * world)(*ptrs)
+        # every buffer is zeroed and mapped everywhere before any step writes into it
+        dist.barrier(group=group)
+
+    def close(self, group=None):
+        """Collective: every rank's GPU idle, every mapping of every buffer closed,
+        then each rank frees its own buffer."""
+        if self.local is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=group)          # no kernel of any rank still writes into a peer buffer
+        for b in self.opened:
+            self._lib.tlx_ipc_close(b)
+        self.opened = []
+        dist.barrier(group=group)          # every mapping of this rank's buffer is closed
+        self._lib.tlx_peer_buffer_free(self.local)
+        self.local = None
+
+
 def allreduce_partial(y: torch.Tensor, group=None) -> torch.Tensor:
     """Sum the per-rank partial down-projection outputs in place."""
     dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
@@ -68,14 +122,25 @@ def gather_keys(local_keys: torch.Tensor, all_keys: torch.Tensor, group=None) ->
 
 
 class ShardedVerifyStep:
-    """VerifyStep over `world` GPUs; this object is rank `rank`'s share."""
+    """VerifyStep over `world` GPUs; this object is rank `rank`'s share.
 
-    LAUNCHES_PER_STEP = 5 + 1  # stage/gate-up, down, stage/head, merge (+ 2 NCCL collectives)
+    comm = "peer" (default): the down projection's partials and the head's argmax keys
+    travel through peer memory inside the two kernels (PeerComm, tlx_gemv_peer,
+    tlx_head_argmax_peer): no NCCL call and no merge kernel in the step.
+    comm = "nccl": one NCCL all-reduce of the partials and one all-gather of the keys,
+    then a merge kernel (the collective-library baseline of the same split)."""
+
     KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
 
     def __init__(self, shape: VerifyShape, rank: int, world: int, seed: int = 0, weights: dict | None = None,
-                 group=None):
+                 group=None, comm: str = "peer"):
         ops.require_device()
+        if comm not in ("peer", "nccl"):
+            raise ValueError(f"comm must be 'peer' or 'nccl', not {comm!r}")
+        self.comm = comm
+        self.LAUNCHES_PER_STEP = 5 if comm == "peer" else 6   # stage/gate-up, down, stage/head (+ merge)
+        self.COLLECTIVES = ("down partials and head keys over peer memory inside the kernels" if comm == "peer"
+                            else "NCCL all-reduce of the down partials + NCCL all-gather of the head keys")
         self.shape = s = shape
         self.rank, self.world, self.group = rank, world, group
         nb_ffn = s.ffn // 256
@@ -111,6 +176,7 @@ class ShardedVerifyStep:
             "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, self.n_ffn, s.rows, "image"),
             "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, self.n_voc, s.dim, s.rows),
         }
+        self.peer = PeerComm(rank, world, s.rows, s.dim, group) if comm == "peer" else None
         self.graph = None
 
     def algorithmic_bytes_per_rank(self) -> dict:
@@ -137,8 +203,38 @@ class ShardedVerifyStep:
         ops.head_argmax(s.head_q, self.w["head"], self.h, self.n_voc, self.ws["head_argmax"],
                         row_offset=self.v0, out_keys=self.local_keys)
 
+    def launch_ffn_down_peer(self):
+        """This rank's down partial into every rank's buffer (tlx_gemv_peer)."""
+        from . import _lib
+
+        s = self.shape
+        w = self.ws["ffn_down"]
+        _lib.check(_lib.lib().tlx_gemv_peer(ops.qtype_id(s.down_q), ops._ptr(self.w["down"]), None,
+                                            ops._ptr(self.gact), _lib.TLX_DT_IMAGE, 0, s.rows, s.dim, self.n_ffn,
+                                            self.world, self.rank, self.peer.ptrs, ops._ptr(w.buf), w.nbytes,
+                                            ops._stream(self.x)), "gemv_peer")
+
+    def launch_head_argmax_peer(self):
+        """This rank's vocabulary shard of the head, then y = residual + the ranks' down
+        partials and the merge of the ranks' keys + accept (tlx_head_argmax_peer)."""
+        from . import _lib
+
+        s = self.shape
+        w = self.ws["head_argmax"]
+        dt, ldx = ops._x_args(self.h)
+        g = ops.grid("cuda") if s.head_q == "iq3_xxs" else None
+        _lib.check(_lib.lib().tlx_head_argmax_peer(
+            ops.qtype_id(s.head_q), ops._ptr(self.w["head"]), ops._ptr(g), ops._ptr(self.h), dt, ldx, s.rows,
+            self.n_voc, s.dim, self.v0, ops._ptr(self.out_max), ops._ptr(self.out_idx), ops._ptr(self.drafts),
+            s.n_drafts, ops._ptr(self.accept_out), self.world, self.rank, self.peer.ptrs, s.dim, ops._ptr(self.res),
+            s.dim, ops._ptr(self.y), s.dim, ops._ptr(w.buf), w.nbytes, ops._stream(self.h)), "head_argmax_peer")
+
     def launch(self):
         self.launch_ffn_gate_up()
+        if self.comm == "peer":
+            self.launch_ffn_down_peer()
+            self.launch_head_argmax_peer()
+            return
         self.launch_ffn_down()
         allreduce_partial(self.y, self.group)
         self.launch_head_argmax()
@@ -158,13 +254,20 @@ class ShardedVerifyStep:
 
     def phase_times(self, time_graph, graph_of, max_over_ranks, torch_mod, reps: int = 20, replays: int = 5):
         """Device time (us, max over ranks) of each piece of the step alone, each
-        captured `reps` times back to back in its own graph: the three GEMVs, the
-        all-reduce, the key all-gather + merge, and the whole step; `gap` is the step
-        minus the sum of the pieces (launch ramps and waits between them)."""
+        captured `reps` times back to back in its own graph, and of the whole step; `gap`
+        is the step minus the sum of the pieces.  The GEMVs are timed as their local
+        (exchange-free) launches; with comm = "nccl" the collectives are timed alone too,
+        with comm = "peer" the exchange lives inside the step's kernels, so the gap is
+        the exchange plus the launch ramps."""
         out = {}
         pieces = [("ffn_gate_up", self.launch_ffn_gate_up), ("ffn_down", self.launch_ffn_down),
-                  ("head_argmax", self.launch_head_argmax), ("allreduce_y", self.launch_allreduce),
-                  ("gather_merge_keys", self.launch_gather_merge)]
+                  ("head_argmax", self.launch_head_argmax)]
+        if self.comm == "nccl":
+            pieces += [("allreduce_y", self.launch_allreduce), ("gather_merge_keys", self.launch_gather_merge)]
+        # the same three kernels chained as in the step but without any exchange: the
+        # step minus this is what the exchange costs
+        chain = ("kernels_chained_no_exchange",
+                 lambda: (self.launch_ffn_gate_up(), self.launch_ffn_down(), self.launch_head_argmax()))
         for name, fn in pieces:
             g = graph_of(lambda fn=fn: [fn() for _ in range(reps)], torch_mod)
             g.replay()
@@ -174,6 +277,10 @@ class ShardedVerifyStep:
         out["gap"] = round(out["step"] - sum(v for k, v in out.items() if k != "step"), 2)
         parts = {k: v for k, v in out.items() if k not in ("step",)}
         out["limiter"] = max(parts, key=parts.get)
+        g = graph_of(lambda: [chain[1]() for _ in range(reps)], torch_mod)
+        g.replay()
+        out[chain[0]] = round(max_over_ranks(time_graph(g.replay, replays, torch_mod) / reps) * 1000, 2)
+        del g
         return out
 
     def capture(self):
@@ -196,9 +303,13 @@ class ShardedVerifyStep:
         self.graph.replay()
 
     def release(self):
-        """Drop the captured graph (it holds NCCL work) before the process group goes."""
+        """Drop the captured graph (it may hold NCCL work) before the process group goes,
+        and unmap / free the peer buffers."""
         self.graph = None
         torch.cuda.synchronize()
+        if self.peer is not None:
+            self.peer.close(self.group)
+            self.peer = None
 
     def set_inputs(self, x, h, res=None, drafts=None):
         self.x.copy_(x, non_blocking=True)

@@ -67,14 +67,16 @@ def synth_tiled(qtype: str, n_rows: int, k: int, seed: int, rows: tuple[int, int
     out = torch.empty(ops.tiled_bytes(qtype, r1 - r0, kk), dtype=torch.uint8, device="cuda")
     per_tile = ops.tiled_bytes(qtype, 16, kk)
     step = synth.CHUNK_ROWS
-    for a in range(r0, r1, step):
-        b = min(a + step - (a % step), r1)
+    a = r0
+    while a < r1:
+        b = min(a - (a % step) + step, r1)          # to the next chunk boundary
         raw = synth.matrix_rows(qtype, n_rows, k, seed, a, b)
         if cols is not None:
             raw = np.ascontiguousarray(raw[:, (k0 // synth.QK) * bb:(k1 // synth.QK) * bb])
         t = ops.pack_tiles(qtype, raw, kk)
         off = ((a - r0) // 16) * per_tile
         out[off:off + t.numel()].copy_(t)
+        a = b
     return out
 
 
