@@ -902,6 +902,30 @@ def check_unsharded(step, shape, x, h, drafts, rank, torch, dist):
             "reference": "one-GPU VerifyStep over the full seeded model on rank 0, same inputs and drafts"}
 
 
+def profile_gemv(which: str, vocab: int, ffn: int) -> int:
+    """A small driver for ncu: one of the verify step's three GEMVs alone (the bench's
+    seeded model at --vocab / --ffn, inputs N(0, 1) bf16), launched four times
+    eagerly (three warm-up launches, then the one to capture), then exit."""
+    import numpy as np
+    import torch
+    from thunderllamax_b200 import synth
+    from thunderllamax_b200.verify import VerifyShape, VerifyStep
+
+    step = VerifyStep(VerifyShape(vocab=vocab, ffn=ffn), seed=0)
+    rng = np.random.default_rng(2323)
+    rows = [torch.from_numpy(synth.bf16_normal(rng, (step.shape.rows, step.shape.dim)).view(np.int16))
+            .cuda().view(torch.bfloat16) for _ in range(2)]
+    step.set_inputs(rows[0], rows[1])
+    step.launch()                                  # every input the chosen kernel reads
+    fn = {"gate_up": step.launch_ffn_gate_up, "down": step.launch_ffn_down, "head": step.launch_head_argmax}[which]
+    for _ in range(4):
+        fn()
+    torch.cuda.synchronize()
+    bad = {k: w.error() for k, w in step.ws.items() if w.error()}
+    print(json.dumps({"profile_gemv": which, "vocab": vocab, "ffn": ffn, "ok": not bad, "errors": bad}))
+    return 0 if not bad else 1
+
+
 def profile_attention(pos: int) -> int:
     """A small driver for ncu: the attention split kernel alone at context `pos`
     (11 rows, ctx 100352, random int8 cache and scales, qw16 N(0, 1) / 16)."""
@@ -936,11 +960,15 @@ def main():
     # smaller shapes for profiler captures only; the benchmark line uses the defaults
     ap.add_argument("--profile-attention", type=int, default=None, metavar="POS",
                     help="profiling case: one warm-up and one tlx_attn_split launch at context POS, then exit")
+    ap.add_argument("--profile-gemv", choices=["gate_up", "down", "head"], default=None,
+                    help="profiling case: one verify GEMV alone (a full step first, then four launches), then exit")
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
     args = ap.parse_args()
     if args.profile_attention is not None:
         return profile_attention(args.profile_attention)
+    if args.profile_gemv is not None:
+        return profile_gemv(args.profile_gemv, args.vocab, args.ffn)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

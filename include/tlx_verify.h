@@ -199,25 +199,32 @@ int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, 
 
 /* ---- the sharded verify step over peer memory (one process per GPU) ---------------
  * Every rank owns one communication buffer of tlx_peer_buffer_bytes(world, m, ny)
- * bytes (zeroed once, 256-byte aligned) and maps every other rank's buffer into its
- * process (tlx_ipc_handle on the owner, tlx_ipc_open on the others); peer_bufs[r] is
- * rank r's buffer as mapped in the calling process.  The step replaces NCCL's
- * all-reduce of the down partials and all-gather of the head keys (the collectives of
- * the row / k / vocabulary split):
+ * bytes (tlx_peer_buffer_alloc: zeroed, an allocation of its own) and maps every other
+ * rank's buffer into its process (tlx_ipc_handle on the owner, tlx_ipc_open on the
+ * others); peer_bufs[r] is rank r's buffer as mapped in the calling process.  The step
+ * replaces NCCL's all-reduce of the down partials and all-gather of the head keys (the
+ * collectives of the row / k / vocabulary split):
  *   tlx_gemv_peer         the down projection shard (k split): its fp32 partial y goes
  *                         straight into every rank's buffer with ordinary stores over
  *                         NVLink, and its last CTA raises this rank's flag there;
- *   tlx_head_argmax_peer  the vocabulary shard of the fused head: every CTA then adds
- *                         the ranks' partials (rank order, + residual) into y, and the
- *                         last CTA exchanges the 11 argmax keys with every rank, merges
- *                         them and runs greedy accept (the same result on every rank).
- * Call them in this order once per step on every rank (the down kernel of the next
- * step may run while a peer still reads the previous step's slots: they are
- * double-buffered).  Waits on peers are bounded; on timeout the workspace error word
- * gets TLX_WS_ERR_PEER_TIMEOUT.  No reference counterpart: the reference runs on one
- * GPU (README.md:412-413). */
+ *   tlx_head_argmax_peer  the vocabulary shard of the fused head; its last CTA sends
+ *                         the 11 argmax keys to every rank, merges all ranks' keys and
+ *                         runs greedy accept (the same result on every rank);
+ *   tlx_peer_finish       after both, on the same stream: y = residual + the ranks'
+ *                         partials in rank order (the same bits on every rank), and the
+ *                         step counter advances.
+ * The FFN (gate/up, tlx_gemv_peer) and the head are independent and may run on two
+ * streams at once with split CTA budgets (max_ctas > 0 caps a launch's grid; 0 = the
+ * tlx_set_max_ctas setting); tlx_peer_finish must follow both.  Waits are only on other
+ * GPUs' flags, never on another kernel of the same GPU, and are bounded: on timeout the
+ * error word (workspace word 0, or err for tlx_peer_finish) gets
+ * TLX_WS_ERR_PEER_TIMEOUT.  No reference counterpart: the reference runs on one GPU
+ * (README.md:412-413). */
 #define TLX_WS_ERR_PEER_TIMEOUT 4u
 size_t tlx_peer_buffer_bytes(int world, int m, int64_t ny);
+/* a zeroed communication buffer that is an allocation of its own (set-up time only) */
+int tlx_peer_buffer_alloc(size_t bytes, void** out);
+int tlx_peer_buffer_free(void* p);
 size_t tlx_ipc_handle_bytes(void);
 /* handle_out (tlx_ipc_handle_bytes) names the allocation holding ptr; offset_out = ptr
  * minus the allocation's base */
@@ -225,17 +232,15 @@ int tlx_ipc_handle(const void* ptr, void* handle_out, uint64_t* offset_out);
 /* maps a peer's allocation (peer access enabled); *ptr_out = its base + offset */
 int tlx_ipc_open(const void* handle, uint64_t offset, void** base_out, void** ptr_out);
 int tlx_ipc_close(void* base);
-/* a zeroed communication buffer that is an allocation of its own (set-up time only) */
-int tlx_peer_buffer_alloc(size_t bytes, void** out);
-int tlx_peer_buffer_free(void* p);
 int tlx_gemv_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
-                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, void* ws, size_t ws_bytes,
-                  void* stream);
+                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, int max_ctas, void* ws,
+                  size_t ws_bytes, void* stream);
 int tlx_head_argmax_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
                          int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
                          const int32_t* drafts, int n_drafts, int32_t* accept_out, int world, int rank,
-                         void* const* peer_bufs, int64_t ny, const float* residual, int64_t ldr, float* y,
-                         int64_t ldy, void* ws, size_t ws_bytes, void* stream);
+                         void* const* peer_bufs, int max_ctas, void* ws, size_t ws_bytes, void* stream);
+int tlx_peer_finish(int world, int rank, void* const* peer_bufs, int m, int64_t ny, const float* residual,
+                    int64_t ldr, float* y, int64_t ldy, uint32_t* err, void* stream);
 
 /* ---- greedy acceptance ------------------------------------------------------------
  * acc36: m = longest prefix amds[s] == drafts[s], s < k; mb[0] = m;
@@ -383,8 +388,11 @@ int tlx_moe_workspace_error(const void* ws, int p, int n_experts, int hidden, in
  * the workspace with a power-of-two scale per token row, so that rows beyond the
  * fp16 range (max |x| >= 2^15) are carried with one fp16 rounding (none for bf16);
  * the epilogue multiplies the scale back.  The workspace
- * (tlx_prefill_workspace_bytes) holds a device error word (zero it once), the fp16
- * copy of the tokens and their scales.
+ * (tlx_prefill_workspace_bytes; zero it once) holds a device error word, the fp16
+ * copy of the tokens and their scales, and the split region: when the tiles do not
+ * fill the last wave of SMs, the tiles of that wave run as k pieces on the idle SMs
+ * and the last piece of each tile sums the pieces' fp32 partials in piece order
+ * (deterministic); its counters are left zeroed.
  * act[t][r] = silu((Wg x_t)[r]) * (Wu x_t)[r] in fp32 for IQ3_XXS gate/up (fp32: the
  * product of two large projections can exceed the fp16 range; the down GEMM reads
  * it back through the scaled staging), and

@@ -71,7 +71,7 @@ def _rank(rank, world, port, q, comm="peer", steps=3):
         y = step.y.cpu().numpy()
         err = float((np.abs(y - y_ref).max(axis=1) / np.linalg.norm(y_ref, axis=1)).max())
         same = all(torch.equal(ys[0], t) for t in ys[1:])
-        werr = [w_.error() for w_ in step.ws.values()]
+        werr = [w_.error() for w_ in step.ws.values()] + [int(step.finish_err.item())]
         out = (rank, err, step.out_idx.cpu().tolist(), idx_ref.tolist(), step.accept_out.cpu().tolist(),
                list(oracle.accept(idx_ref, drafts)), same, werr, y.tobytes())
         step.release()
@@ -111,17 +111,18 @@ def test_sharded_verify_step(world, comm):
         assert idx == idx_ref, rank
         assert acc == acc_ref, rank
         assert same, f"rank {rank}: y differs between steps"
-        assert werr == [0, 0, 0], (rank, werr)
+        assert werr == [0, 0, 0, 0], (rank, werr)
     # every rank holds the same y (the partials are added in rank order everywhere)
     assert len({r[-1] for r in results}) == 1
 
 
 def test_peer_wait_times_out_into_error_word():
     # Failure detection without a GPU fault: rank 0 of a 2-rank step whose rank 1 never
-    # runs.  Both buffers live on this GPU; the down kernel sends its partial and raises
-    # its flag, the head kernel then waits for rank 1's down flag and keys, which nothing
-    # sets: the bounded waits give up, raise TLX_WS_ERR_PEER_TIMEOUT in the workspace
-    # error word and the kernel returns (the context stays usable).
+    # runs.  Both buffers live on this GPU (nothing else runs on it); the down kernel
+    # sends its partial and raises its flag, the head kernel then waits for rank 1's
+    # argmax keys and the finish kernel for rank 1's down partial, which nothing sets:
+    # the bounded waits give up, raise TLX_WS_ERR_PEER_TIMEOUT in their error words and
+    # the kernels return (the context stays usable).
     import ctypes
 
     from thunderllamax_b200 import _lib, ops, synth
@@ -146,125 +147,21 @@ def test_peer_wait_times_out_into_error_word():
         h = torch.randn((m, dim), device="cuda").half()
         y = torch.zeros((m, dim), device="cuda")
         idx = torch.zeros(m, dtype=torch.int32, device="cuda")
+        ferr = torch.zeros(1, dtype=torch.int32, device="cuda")
         s = ops._stream(h)
         _lib.check(L.tlx_gemv_peer(ops.qtype_id("q6_k"), ops._ptr(wd), None, ops._ptr(img.buf), _lib.TLX_DT_IMAGE,
-                                   0, m, dim, ffn, 2, 0, ptrs, ops._ptr(ws_d.buf), ws_d.nbytes, s), "gemv_peer")
+                                   0, m, dim, ffn, 2, 0, ptrs, 0, ops._ptr(ws_d.buf), ws_d.nbytes, s), "gemv_peer")
         _lib.check(L.tlx_head_argmax_peer(ops.qtype_id("q6_k"), ops._ptr(wh), None, ops._ptr(h), _lib.TLX_DT_F16,
-                                          dim, m, vocab, dim, 0, None, ops._ptr(idx), None, 0, None, 2, 0, ptrs,
-                                          dim, None, 0, ops._ptr(y), dim, ops._ptr(ws_h.buf), ws_h.nbytes, s),
-                   "head_argmax_peer")
+                                          dim, m, vocab, dim, 0, None, ops._ptr(idx), None, 0, None, 2, 0, ptrs, 0,
+                                          ops._ptr(ws_h.buf), ws_h.nbytes, s), "head_argmax_peer")
+        _lib.check(L.tlx_peer_finish(2, 0, ptrs, m, dim, None, 0, ops._ptr(y), dim, ops._ptr(ferr), s), "finish")
         torch.cuda.synchronize()
         assert ws_d.error() == 0
-        assert ws_h.error() & 4, ws_h.error()          # TLX_WS_ERR_PEER_TIMEOUT
+        assert ws_h.error() & 4, ws_h.error()          # TLX_WS_ERR_PEER_TIMEOUT (keys)
+        assert int(ferr.item()) & 4, int(ferr.item())   # TLX_WS_ERR_PEER_TIMEOUT (down partial)
         # the context is still usable
         assert torch.equal(torch.ones(4, device="cuda").sum().cpu(), torch.tensor(4.0))
     finally:
         torch.cuda.synchronize()
         for b in bufs:
             L.tlx_peer_buffer_free(b)
-
-
-def _spawn_gpu(target, world=2):
-    here = os.path.dirname(os.path.abspath(__file__))
-    root = os.path.dirname(here)
-    os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.path.join(here, "golden"),
-                                                os.environ.get("PYTHONPATH", "")])
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
-    for p_ in procs:
-        p_.start()
-    results = []
-    try:
-        for _ in range(world):
-            results.append(q.get(timeout=300))
-    finally:
-        for p_ in procs:
-            p_.join(timeout=60)
-    assert all(p_.exitcode == 0 for p_ in procs)
-    return results
-
-
-def _init(rank, world, port):
-    import datetime
-
-    import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
-                            device_id=torch.device("cuda", rank))
-    return dist
-
-
-def _moe_rank(rank, world, port, q):
-    dist = _init(rank, world, port)
-    try:
-        import oracle
-        from thunderllamax_b200 import dist as tdist
-        from thunderllamax_b200 import moe, synth
-        shape = moe.MoeShape(positions=5, experts=32, hidden=1024, inner=512)
-        host = moe.synth_host(shape, seed=21)
-        step = tdist.ShardedMoeVerifyStep(shape, rank, world, host=host)
-        rng = np.random.default_rng(22)
-        bits = synth.bf16_normal(rng, (shape.positions, shape.hidden))
-        hres = rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32)
-        step.set_inputs(torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16),
-                        torch.from_numpy(hres).cuda())
-        step.capture()
-        for _ in range(3):
-            step.replay()
-        torch.cuda.synchronize()
-        h64 = synth.bf16_bits_to_f32(bits).astype(np.float64)
-        ref = oracle.moe_verify_f64(h64, host["wr"], host["wsh"], host["gate"], host["up"], host["down"],
-                                    host["sgate"], host["sup"], host["sdown"], hres=hres)
-        y = step.y.cpu().numpy().astype(np.float64)
-        err = float((np.abs(y - ref["y"]).max(axis=1) / np.linalg.norm(ref["y"], axis=1)).max())
-        step.release()
-        q.put((rank, err, step.local.ws.error()))
-    finally:
-        dist.destroy_process_group()
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_moe_two_gpus():
-    for rank, err, werr in _spawn_gpu(_moe_rank):
-        assert err <= 2e-3 and err <= 2e-4, (rank, err)
-        assert werr == 0
-
-
-def _prefill_rank(rank, world, port, q):
-    dist = _init(rank, world, port)
-    try:
-        import oracle
-        from thunderllamax_b200 import dist as tdist
-        from thunderllamax_b200 import ops, synth
-        from thunderllamax_b200.prefill import PrefillShape
-        s = PrefillShape(tokens=300, dim=1024, ffn=2048)
-        rng = np.random.default_rng(23)
-        rg, ru = synth.iq3xxs_blocks(rng, s.ffn, s.dim), synth.iq3xxs_blocks(rng, s.ffn, s.dim)
-        rd = synth.q6k_blocks(rng, s.dim, s.ffn)
-        b0, b1 = tdist.block_ranges(s.ffn // 256, world)[rank]
-        f0, f1 = 256 * b0, 256 * b1
-        w = {"gate": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(rg, f0, f1), s.dim),
-             "up": ops.pack_tiles("iq3_xxs", tdist.shard_gguf_rows(ru, f0, f1), s.dim),
-             "down": ops.pack_tiles("q6_k", tdist.shard_gguf_cols(rd, f0, f1, 210), f1 - f0)}
-        step = tdist.ShardedPrefillFFN(s, rank, world, weights=w)
-        xb = synth.bf16_normal(rng, (s.tokens, s.dim))
-        step.set_inputs(torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16))
-        step.capture()
-        step.replay()
-        torch.cuda.synchronize()
-        _, y_ref = oracle.ffn_f64(synth.bf16_bits_to_f32(xb).astype(np.float64), rg, ru, rd)
-        y = step.y.cpu().numpy().astype(np.float64)
-        err = float((np.abs(y - y_ref).max(axis=1) / np.linalg.norm(y_ref, axis=1)).max())
-        step.release()
-        q.put((rank, err))
-    finally:
-        dist.destroy_process_group()
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_prefill_two_gpus():
-    for rank, err in _spawn_gpu(_prefill_rank):
-        assert err <= 2e-3 and err <= 1e-3, (rank, err)

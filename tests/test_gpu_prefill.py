@@ -125,3 +125,33 @@ def test_prefill_gemm_rows_beyond_fp16_range():
         assert np.isfinite(got).all()
         assert np.array_equal(got[0], np.zeros(n, np.float32))
         check_rows(got[1:], oracle.matvec_f64(W, x64)[1:], TIGHT)
+
+
+@pytest.mark.parametrize("mode,m,n,k", [("gate_up", 256, 256, 2048), ("gate_up", 300, 128, 4096),
+                                        ("gemm", 300, 256, 4096), ("gemm", 77, 128, 8192)])
+def test_prefill_split_tiles(mode, m, n, k):
+    """Fewer tiles than SMs and a long k: each tile runs as k pieces on separate SMs,
+    the last piece to finish sums the fp32 partials in piece order.  Two calls on the
+    same workspace (the piece counters re-arm) give the same bits."""
+    rng = np.random.default_rng(11 + m + n + k)
+    x_t, x64 = tokens(rng, m, k)
+    ws = prefill.PrefillWorkspace(m, k)
+    if mode == "gate_up":
+        rg, ru = synth.iq3xxs_blocks(rng, n, k), synth.iq3xxs_blocks(rng, n, k)
+        wg, wu = ops.pack_tiles("iq3_xxs", rg, k), ops.pack_tiles("iq3_xxs", ru, k)
+        run = lambda: prefill.gate_up("iq3_xxs", wg, wu, x_t, n, ws)      # noqa: E731
+        ref = oracle.silu_f64(oracle.matvec_f64(oracle.dequant_iq3xxs(rg, k), x64)) * \
+            oracle.matvec_f64(oracle.dequant_iq3xxs(ru, k), x64)
+    else:
+        raw = synth.q6k_blocks(rng, n, k)
+        w = ops.pack_tiles("q6_k", raw, k)
+        run = lambda: prefill.gemm("q6_k", w, x_t, n, ws)                 # noqa: E731
+        ref = oracle.matvec_f64(oracle.dequant("q6_k", raw, k), x64)
+    out0 = run().clone()
+    out1 = run()
+    torch.cuda.synchronize()
+    assert ws.error() == 0
+    assert torch.equal(out0, out1)
+    got = out1.float().cpu().numpy()
+    check_rows(got, ref, CONTRACT)
+    check_rows(got, ref, TIGHT)

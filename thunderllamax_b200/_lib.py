@@ -53,11 +53,11 @@ _SIGS = {
     "tlx_ipc_close": (c_int, [c_vp]),
     "tlx_peer_buffer_alloc": (c_int, [c_size, c_vp]),
     "tlx_peer_buffer_free": (c_int, [c_vp]),
-    "tlx_gemv_peer": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_vp,
-                              c_size, c_vp]),
+    "tlx_gemv_peer": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_int,
+                              c_vp, c_size, c_vp]),
     "tlx_head_argmax_peer": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp,
-                                     c_vp, c_int, c_vp, c_int, c_int, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp,
-                                     c_size, c_vp]),
+                                     c_vp, c_int, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_size, c_vp]),
+    "tlx_peer_finish": (c_int, [c_int, c_int, c_vp, c_int, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp]),
     "tlx_gemv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp, c_int,
                          c_i64, c_vp, c_size, c_vp]),
     "tlx_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_int,

@@ -658,34 +658,44 @@ static int make_peer(int world, int rank, void* const* bufs, int m, int64_t ny, 
 }
 
 int tlx_gemv_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
-                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, void* ws, size_t ws_bytes,
-                  void* stream) {
+                  int64_t n_rows, int64_t k, int world, int rank, void* const* peer_bufs, int max_ctas, void* ws,
+                  size_t ws_bytes, void* stream) {
   PeerParams pr;
   const int rc = make_peer(world, rank, peer_bufs, m, n_rows, pr);
   if (rc) return rc;
   if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
   return run_gemv(kEpiStore, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr, TLX_DT_F32,
-                  n_rows, 0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, ws, ws_bytes, g_max_ctas,
-                  as_stream(stream), &pr);
+                  n_rows, 0, nullptr, nullptr, nullptr, nullptr, 0, nullptr, ws, ws_bytes,
+                  max_ctas > 0 ? max_ctas : g_max_ctas, as_stream(stream), &pr);
 }
 
 int tlx_head_argmax_peer(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx,
                          int m, int64_t n_rows, int64_t k, int64_t row_offset, float* out_max, int32_t* out_idx,
                          const int32_t* drafts, int n_drafts, int32_t* accept_out, int world, int rank,
-                         void* const* peer_bufs, int64_t ny, const float* residual, int64_t ldr, float* y,
-                         int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+                         void* const* peer_bufs, int max_ctas, void* ws, size_t ws_bytes, void* stream) {
+  PeerParams pr;
+  const int rc = make_peer(world, rank, peer_bufs, m, 1, pr);
+  if (rc) return rc;
+  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
+                  TLX_DT_F32, 0, row_offset, out_max, out_idx, nullptr, drafts, n_drafts, accept_out, ws, ws_bytes,
+                  max_ctas > 0 ? max_ctas : g_max_ctas, as_stream(stream), &pr);
+}
+
+int tlx_peer_finish(int world, int rank, void* const* peer_bufs, int m, int64_t ny, const float* residual,
+                    int64_t ldr, float* y, int64_t ldy, uint32_t* err, void* stream) {
   PeerParams pr;
   const int rc = make_peer(world, rank, peer_bufs, m, ny, pr);
   if (rc) return rc;
-  if (!y) return TLX_ERR_NULL;
-  if (!valid_qtype(qtype)) return TLX_ERR_QTYPE;
+  if (!y || !err) return TLX_ERR_NULL;
+  if (m < 1 || m > 16 || ny < 1 || ldy < ny || (residual && ldr < ny)) return TLX_ERR_SHAPE;
+  for (int r = 0; r < world; ++r)
+    if (!pr.base[r] || (reinterpret_cast<uintptr_t>(pr.base[r]) & 255)) return TLX_ERR_ALIGN;
   pr.residual = residual;
   pr.ldr = ldr;
   pr.y = y;
   pr.ldy = ldy;
-  return run_gemv(kEpiArgmax, qtype, w, nullptr, grid, x, x_dtype, ldx, m, n_rows, k, nullptr, 0, nullptr,
-                  TLX_DT_F32, 0, row_offset, out_max, out_idx, nullptr, drafts, n_drafts, accept_out, ws, ws_bytes,
-                  g_max_ctas, as_stream(stream), &pr);
+  return peer_finish(pr, err, as_stream(stream));
 }
 
 int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,

@@ -68,6 +68,7 @@ __host__ __device__ __forceinline__ int64_t sums_index(int64_t b, int col, int q
 // buffer as mapped in this process.  Layout (bytes):
 //   0     epoch: steps completed on this rank (local)
 //   64    arrival counter of the down kernel's CTAs (local)
+//   128   arrival counter of the finish kernel's CTAs (local)
 //   256   down flags [2][kMaxPeers], 16 bytes apart: rank r's partial y of the step
 //         with parity p is complete in this buffer once flag [p][r] == epoch + 1
 //   512   key flags  [2][kMaxPeers], the same for rank r's argmax keys
@@ -75,8 +76,8 @@ __host__ __device__ __forceinline__ int64_t sums_index(int64_t b, int col, int q
 //   4096  y partials [2][world][m][ny] fp32
 // Partials and keys are double-buffered by step parity: a rank can be at most one
 // step ahead of another, because every step waits for all ranks' partials.
-constexpr uint32_t kPeerEpoch = 0, kPeerDownCnt = 64, kPeerDownFlags = 256, kPeerKeyFlags = 512, kPeerKeys = 1024,
-                   kPeerY = 4096;
+constexpr uint32_t kPeerEpoch = 0, kPeerDownCnt = 64, kPeerFinishCnt = 128, kPeerDownFlags = 256,
+                   kPeerKeyFlags = 512, kPeerKeys = 1024, kPeerY = 4096;
 
 size_t peer_buffer_bytes(int world, int m, int64_t ny) {
   if (world < 2 || world > kMaxPeers || m < 1 || m > 16 || ny < 1) return 0;
@@ -867,23 +868,6 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       __threadfence();
     }
     const PeerParams& pr = p.peer;
-    if (pr.world > 1) {
-      // sharded step: y = residual + the ranks' partials of the down projection (in
-      // rank order), this CTA's slice, once every rank's down flag of this step is up
-      if (threadIdx.x < pr.world)
-        wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerDownFlags, par, threadIdx.x), ep + 1u, p.err);
-      __syncthreads();
-      const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
-      const int64_t per = (total + gridDim.x - 1) / gridDim.x;
-      const int64_t i0 = blockIdx.x * per, i1 = i0 + per < total ? i0 + per : total;
-      const float* part = reinterpret_cast<const float*>(pr.base[pr.rank] + kPeerY) + par * pr.world * total;
-      for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
-        float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
-        for (int r = 0; r < pr.world; ++r) s += __ldcv(part + r * total + i);
-        pr.y[tok * pr.ldy + row] = s;
-      }
-    }
     __syncthreads();
     if (threadIdx.x == 0) {
       const uint32_t old = atomicAdd(p.done_cnt, 1u);
@@ -933,9 +917,41 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
           p.accept_out[1] = idx_s[m];
         }
         *p.done_cnt = 0u;
-        // the step is complete on this rank
-        if (pr.world > 1) *reinterpret_cast<volatile uint32_t*>(pr.base[pr.rank] + kPeerEpoch) = ep + 1u;
       }
+    }
+  }
+}
+
+// ---- end of a sharded step: y = residual + the ranks' down partials, epoch + 1 ----
+// Runs after the step's down and head kernels of this rank (stream order), so the only
+// waits are on the other ranks' down flags.  The partials are added in rank order, so
+// every rank computes the same bits.  The last CTA to finish advances the epoch.
+__global__ void __launch_bounds__(256) peer_finish_kernel(const PeerParams pr, uint32_t* err) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ uint32_t last;
+  const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(pr.base[pr.rank] + kPeerEpoch);
+  const uint32_t par = ep & 1u;
+  if (threadIdx.x < pr.world)
+    wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerDownFlags, par, threadIdx.x), ep + 1u, err);
+  __syncthreads();
+  const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
+  const float* part = reinterpret_cast<const float*>(pr.base[pr.rank] + kPeerY) + par * pr.world * total;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
+    float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
+    for (int r = 0; r < pr.world; ++r) s += __ldcv(part + r * total + i);
+    pr.y[tok * pr.ldy + row] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(pr.base[pr.rank] + kPeerFinishCnt);
+    last = atomicAdd(cnt, 1u) == gridDim.x - 1 ? 1u : 0u;
+    if (last) {
+      *cnt = 0u;
+      // every CTA has read the epoch; the step is complete on this rank
+      *reinterpret_cast<volatile uint32_t*>(pr.base[pr.rank] + kPeerEpoch) = ep + 1u;
     }
   }
 }
@@ -1112,6 +1128,13 @@ static int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+int peer_finish(const PeerParams& pr, uint32_t* err, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 64));
+  return launch_pdl(peer_finish_kernel, dim3(blocks), dim3(256), 0, stream, pr, err);
+}
+
+
 size_t activation_image_bytes(int m, int64_t k, int x_dtype) {
   if (m < 1 || k <= 0 || k % kQK) return 0;
   const int mc = m * cols_per_token(x_dtype);
@@ -1178,13 +1201,12 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   if (peer) {
     // sharded step: the down projection (STORE, fp32 partial, no residual) or the head
     if (epi == EPI_GATEUP || peer->world < 2 || peer->world > kMaxPeers || peer->rank < 0 ||
-        peer->rank >= peer->world || peer->m != m || peer->ny < 1)
+        peer->rank >= peer->world || peer->m != m || peer->ny < 1 || (epi == EPI_ARGMAX && m > 16))
       return TLX_ERR_SHAPE;
     for (int r = 0; r < peer->world; ++r)
       if (!peer->base[r] || !aligned(peer->base[r], 256)) return TLX_ERR_ALIGN;
     if (epi == EPI_STORE && (peer->ny != n_rows || residual || y_dtype != DT_F32)) return TLX_ERR_SHAPE;
-    if (epi == EPI_ARGMAX && (!peer->y || peer->ldy < peer->ny || (peer->residual && peer->ldr < peer->ny)))
-      return TLX_ERR_SHAPE;
+
   }
 
   uint8_t* wsb = static_cast<uint8_t*>(ws);

@@ -87,8 +87,9 @@ struct SlotCache {
 };
 
 __device__ __forceinline__ void load_slots(const MoeMeta* mt, SlotCache& sc) {
-  const int n = __ldcg(&mt->n_slots);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  // every entry is loaded whether or not it is in use, so that all loads are in flight
+  // together (one L2 round trip); entries past n_slots are never read
+  for (int i = threadIdx.x; i < kMaxSlots; i += blockDim.x) {
     sc.expert[i] = __ldcg(&mt->slot_expert[i]);
     sc.count[i] = __ldcg(&mt->slot_count[i]);
 #pragma unroll
@@ -97,7 +98,7 @@ __device__ __forceinline__ void load_slots(const MoeMeta* mt, SlotCache& sc) {
       sc.pair[i][c] = __ldcg(&mt->slot_pair[i][c]);
     }
   }
-  if (threadIdx.x == 0) sc.n_slots = n;
+  if (threadIdx.x == 0) sc.n_slots = __ldcg(&mt->n_slots);
 }
 
 struct MoeParams {
@@ -127,7 +128,6 @@ struct MoeParams {
   uint32_t* err;
   uint2* ximg;     // [H/256][P][68]
   float* actf;     // [9P][I] fp32 act
-  uint32_t* amax;  // [9P] max |act| bits
   float* parts;    // [9P][H]
 };
 
@@ -203,11 +203,8 @@ __device__ __forceinline__ void iq4_chunk_mma(const Iq4Lane& L, const uint2* xb,
 }
 
 // gate and up chunks of one block share the activation loads
-__device__ __forceinline__ void iq4_pair_mma(const uint8_t* cg, const uint8_t* cu, const uint2* xb, const uint8_t* lut,
-                                             uint32_t lane4, int lane, float (&ag)[4], float (&au)[4]) {
-  Iq4Lane G, U;
-  iq4_load(cg, lane, G);
-  iq4_load(cu, lane, U);
+__device__ __forceinline__ void iq4_pair_compute(const Iq4Lane& G, const Iq4Lane& U, const uint2* xb,
+                                                 const uint8_t* lut, uint32_t lane4, float (&ag)[4], float (&au)[4]) {
   float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
@@ -269,9 +266,6 @@ __global__ void __launch_bounds__(kRouterWarps * 32) moe_router_kernel(const Moe
   griddep_wait();
   griddep_launch_dependents();
 
-  // the previous step's expert kernels have finished with the act maxima: re-arm them
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i < 9 * P; i += blockDim.x) p.amax[i] = 0u;
   if (threadIdx.x == 0) {
     mbar_arrive_expect_tx(hbar, static_cast<uint32_t>(P * H * 2));
     for (int t = 0; t < P; ++t) bulk_g2s(hs + t * H, p.h + t * p.ldh, static_cast<uint32_t>(H * 2), hbar);
@@ -511,7 +505,10 @@ struct Ring {
   uint8_t* ring;
   uint64_t* bars;
   int S;
-  int64_t issued, consumed;
+  int in_flight;             // chunks issued and not yet handed back (lane 0's count)
+  int i_slot;                // next stage to fill (lane 0)
+  int c_slot;                // next stage to consume (every lane)
+  uint32_t c_phase;
   int item, j, n_items, step, per_item, nmat;  // issue cursor
   const uint8_t* base0;                        // this item's matrices (tile offset included)
   const uint8_t* base1;
@@ -519,15 +516,16 @@ struct Ring {
 
 template <typename BaseFn>
 __device__ __forceinline__ void ring_issue(Ring& R, BaseFn base_of) {
-  while (R.item < R.n_items && R.issued < R.consumed + R.S) {
+  while (R.item < R.n_items && R.in_flight < R.S) {
     if (R.j == 0) base_of(R.item, R.base0, R.base1);
-    const int slot = static_cast<int>(R.issued % R.S);
+    const int slot = R.i_slot;
     mbar_arrive_expect_tx(&R.bars[slot], kChunk);
     const bool second = R.nmat == 2 && (R.j & 1);
     const int blk = R.nmat == 2 ? (R.j >> 1) : R.j;
     bulk_g2s(R.ring + slot * kChunk, (second ? R.base1 : R.base0) + static_cast<int64_t>(blk) * kChunk, kChunk,
              &R.bars[slot]);
-    ++R.issued;
+    if (++R.i_slot == R.S) R.i_slot = 0;
+    ++R.in_flight;
     if (++R.j == R.per_item) {
       R.j = 0;
       R.item += R.step;
@@ -535,13 +533,24 @@ __device__ __forceinline__ void ring_issue(Ring& R, BaseFn base_of) {
   }
 }
 
-__device__ __forceinline__ bool ring_wait(Ring& R, int64_t c, uint32_t* err) {
-  return mbar_wait_bounded(&R.bars[c % R.S], static_cast<uint32_t>((c / R.S) & 1), err);
+__device__ __forceinline__ bool ring_wait(const Ring& R, uint32_t* err) {
+  return mbar_wait_bounded(&R.bars[R.c_slot], R.c_phase, err);
 }
 
-// let every copy the warp issued land before the CTA can exit
+__device__ __forceinline__ void ring_pop(Ring& R) {
+  if (++R.c_slot == R.S) {
+    R.c_slot = 0;
+    R.c_phase ^= 1u;
+  }
+}
+
+// let every copy the warp issued land before the CTA can exit (lane 0 issued them)
 __device__ __forceinline__ void ring_drain(Ring& R) {
-  for (int64_t c = R.consumed; c < R.issued; ++c) ring_wait(R, c, nullptr);
+  if ((threadIdx.x & 31) != 0) return;
+  for (; R.in_flight > 0; --R.in_flight) {
+    mbar_wait_bounded(&R.bars[R.c_slot], R.c_phase, nullptr);
+    ring_pop(R);
+  }
 }
 
 // ------------------------------------------------------------------- gate/up kernel
@@ -593,25 +602,38 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   const int v0 = warp * Uc / kExpWarps, v1 = (warp + 1) * Uc / kExpWarps;
   auto warp_of_unit = [&](int v) { return static_cast<int>((static_cast<int64_t>(v + 1) * kExpWarps - 1) / Uc); };
 
-  // chunk stream of this warp: units v0..v1, each gate then up
-  int iv = v0, ij = 0;
-  int64_t issued = 0, consumed = 0;
+  // chunk stream of this warp: units v0..v1, each gate then up.  Producer state (lane
+  // 0): the unit cursor, the next stage to fill and the chunks in flight; consumer
+  // state (every lane): the next stage to read and its phase
+  int iv = v0, ij = 0, ik = v0 / nbh, ib = v0 - (v0 / nbh) * nbh;
+  int in_flight = 0, i_slot = 0, c_slot = 0;
+  uint32_t c_phase = 0u;
   auto issue = [&]() {
-    while (iv < v1 && issued < consumed + S) {
-      const int k = iv / nbh, b = iv - k * nbh;
-      const int i = static_cast<int>(blockIdx.x) + C * k;
+    while (iv < v1 && in_flight < S) {
+      const int i = static_cast<int>(blockIdx.x) + C * ik;
       const int u = i / tpe, tau = i - u * tpe;
       const int e = sc.expert[u];
       const uint8_t* base = ij == 0 ? (e >= 0 ? p.gate + static_cast<int64_t>(e) * p.gu_bytes : p.sgate)
                                     : (e >= 0 ? p.up + static_cast<int64_t>(e) * p.gu_bytes : p.sup);
-      const int slot = static_cast<int>(issued % S);
-      mbar_arrive_expect_tx(&bars[slot], kChunk);
-      bulk_g2s(ring + slot * kChunk, base + (static_cast<int64_t>(tau) * nbh + b) * kChunk, kChunk, &bars[slot]);
-      ++issued;
+      mbar_arrive_expect_tx(&bars[i_slot], kChunk);
+      bulk_g2s(ring + i_slot * kChunk, base + (static_cast<int64_t>(tau) * nbh + ib) * kChunk, kChunk,
+               &bars[i_slot]);
+      if (++i_slot == S) i_slot = 0;
+      ++in_flight;
       if (++ij == 2) {
         ij = 0;
         ++iv;
+        if (++ib == nbh) {
+          ib = 0;
+          ++ik;
+        }
       }
+    }
+  };
+  auto next_stage = [&]() {
+    if (++c_slot == S) {
+      c_slot = 0;
+      c_phase ^= 1u;
     }
   };
   if (lane == 0) issue();
@@ -623,8 +645,8 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
   const int g = lane >> 2, qq = lane & 3;
 
-  // item epilogue on complete sums: act = silu(g) * u (fp32) and the running max |act|
-  // per pair (the down kernel scales each pair's act into fp16 range)
+  // item epilogue on complete sums: act = silu(g) * u (fp32; the down kernel scales
+  // each pair's act into the fp16 range)
   auto epilogue = [&](int k, const float (&ag)[4], const float (&au)[4]) {
     const int i = static_cast<int>(blockIdx.x) + C * k;
     const int u = i / tpe, tau = i - u * tpe;
@@ -634,15 +656,11 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
       const int col = 2 * qq + h2;
       const float a0 = silu_f(ag[h2]) * au[h2];          // row g
       const float a1 = silu_f(ag[2 + h2]) * au[2 + h2];  // row g + 8
-      float mx = fmaxf(fabsf(a0), fabsf(a1));
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       if (col < cnt) {
         const int pair = sc.pair[u][col];
         float* dst = p.actf + static_cast<int64_t>(pair) * p.I + tau * 16 + g;
         dst[0] = a0;
         dst[8] = a1;
-        if (g == 0) atomicMax(p.amax + pair, __float_as_uint(mx));
       }
     }
   };
@@ -684,26 +702,38 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
       const int i = static_cast<int>(blockIdx.x) + C * k;
       xl = xs + sc.tok[i / tpe][g] * kRow + qq;
     }
-    const int64_t c0 = consumed;
-    if (!mbar_wait_bounded(&bars[c0 % S], static_cast<uint32_t>((c0 / S) & 1), lane == 0 ? p.err : nullptr) ||
-        !mbar_wait_bounded(&bars[(c0 + 1) % S], static_cast<uint32_t>(((c0 + 1) / S) & 1),
-                           lane == 0 ? p.err : nullptr)) {
+    Iq4Lane G, U;
+    if (!mbar_wait_bounded(&bars[c_slot], c_phase, lane == 0 ? p.err : nullptr)) {
       failed = true;
       break;
     }
-    iq4_pair_mma(ring + (c0 % S) * kChunk, ring + ((c0 + 1) % S) * kChunk, xl + b * P * kRow, lut, lane4, lane, ag,
-                 au);
-    consumed = c0 + 2;
-    // refill (after the stages' last generic-proxy reads)
+    iq4_load(ring + c_slot * kChunk, lane, G);
+    next_stage();
+    if (!mbar_wait_bounded(&bars[c_slot], c_phase, lane == 0 ? p.err : nullptr)) {
+      if (lane == 0) --in_flight;  // the gate chunk's stage has landed: nothing to drain there
+      failed = true;
+      break;
+    }
+    iq4_load(ring + c_slot * kChunk, lane, U);
+    next_stage();
+    // both chunks are in registers: hand the stages back (after their last generic-proxy
+    // reads) before computing on them
     fence_proxy_async_smem();
     __syncwarp();
-    if (lane == 0) issue();
-    __syncwarp();
+    if (lane == 0) {
+      in_flight -= 2;
+      issue();
+    }
+    iq4_pair_compute(G, U, xl + b * P * kRow, lut, lane4, ag, au);
   }
   if (failed) {
-    // let every copy this warp issued land before the CTA can exit
-    for (int64_t c = consumed; c < issued; ++c)
-      mbar_wait_bounded(&bars[c % S], static_cast<uint32_t>((c / S) & 1), nullptr);
+    // let every copy this warp issued land before the CTA can exit (lane 0 issued them;
+    // the stages not yet consumed start at the consumer's position)
+    if (lane == 0)
+      for (; in_flight > 0; --in_flight) {
+        mbar_wait_bounded(&bars[c_slot], c_phase, nullptr);
+        next_stage();
+      }
   } else if (cur_k >= 0) {
     finish_piece(cur_k, piece_v, v1);
   }
@@ -738,6 +768,8 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ SlotCache sc;
   __shared__ float s_inv[9 * kMaxPos];
+  __shared__ float s_gate[9 * kMaxPos];
+  __shared__ uint32_t s_max[9 * kMaxPos];  // max |act| bits per pair
   const int P = p.P, S = p.stages, I = p.I;
   const int nbi = I >> 8, tpd = p.H >> 4;
   const int npair = 9 * P;
@@ -756,9 +788,77 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
     for (int s = 0; s < S; ++s) mbar_init(&R.bars[s], 1);
   mbar_fence_init();
 
+  for (int i = threadIdx.x; i < npair; i += blockDim.x) s_max[i] = 0u;
+  __syncthreads();
+
   griddep_wait();
   griddep_launch_dependents();
+  // everything the prologue reads from the earlier kernels is loaded in one round trip:
+  // the slot list, each pair's combine weight, and the first act loads
   load_slots(p.meta, sc);
+  for (int i = threadIdx.x; i < npair; i += blockDim.x) {
+    // combine weight: the router gate of a routed pair whose expert is this rank's,
+    // the shared gate of a shared pair (when the shared expert is here), else 0
+    float gw = 0.f;
+    if (i < kTopK * P) {
+      const int id = __ldcg(&p.meta->ids[i]);
+      const float g = __ldcg(&p.meta->gates[i]);
+      gw = id >= p.e0 && id < p.e1 ? g : 0.f;
+    } else if (p.with_shared) {
+      gw = __ldcg(&p.meta->sg[i - kTopK * P]);
+    }
+    s_gate[i] = gw;
+  }
+  const int n4 = npair * (I >> 2);
+  constexpr int kAct = 12;  // float4 act loads in flight per thread
+  const int round = kAct * static_cast<int>(blockDim.x);
+  float4 v[kAct];
+  auto load_act = [&](int i0) {
+#pragma unroll
+    for (int j = 0; j < kAct; ++j) {
+      const int i = i0 + j * static_cast<int>(blockDim.x);
+      v[j] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(p.actf) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  // max |act| per pair: a warp's 32 float4 lie in one pair (I / 4 is a multiple of 32)
+  auto max_act = [&](int i0) {
+#pragma unroll
+    for (int j = 0; j < kAct; ++j) {
+      const int i = i0 + j * static_cast<int>(blockDim.x);
+      float m = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0 && i < n4) atomicMax(&s_max[i / (I >> 2)], __float_as_uint(m));
+    }
+  };
+  // act image with one power-of-two scale per pair (max |act| * scale <= 2^14)
+  auto convert_act = [&](int i0) {
+#pragma unroll
+    for (int j = 0; j < kAct; ++j) {
+      const int i = i0 + j * static_cast<int>(blockDim.x);
+      if (i < n4) {
+        const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
+        const float scl = 1.0f / s_inv[pair];  // exact: a power of two
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // position of k + e in the image: block, mma m, quarter q, half within the entry
+          const int kk = k + e, bi = kk >> 8, kin = kk & 255, q4 = kin >> 6, r = kin & 63;
+          const int m = 8 * (r >> 5) + ((r & 15) >> 1), pos = 2 * (r & 1) + ((r >> 4) & 1);
+          reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] =
+              f32_to_f16_bits(vv[e] * scl);
+        }
+      }
+    }
+  };
+  // with one round of loads (P <= 5 at I = 512) the act stays in registers; more
+  // positions take a second pass over the act for the conversion
+  load_act(threadIdx.x);
+  max_act(threadIdx.x);
+  for (int i0 = threadIdx.x + round; i0 < n4; i0 += round) {
+    load_act(i0);
+    max_act(i0);
+  }
   __syncthreads();
   const int n_slots = sc.n_slots;
   if (n_slots == 0) {
@@ -771,7 +871,8 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   }
   const int n_items = n_slots * tpd;
   const int i_first = blockIdx.x + gridDim.x * warp;
-  R.issued = R.consumed = 0;
+  R.in_flight = R.i_slot = R.c_slot = 0;
+  R.c_phase = 0u;
   R.item = i_first;
   R.j = 0;
   R.n_items = n_items;
@@ -786,41 +887,19 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   };
   // weights do not depend on act: start streaming before the image is built
   if (lane == 0) ring_issue(R, base_of);
-  // act image with one power-of-two scale per pair (max |act| * scale <= 2^14);
-  // every CTA builds it from the fp32 act, 12 float4 loads in flight per thread
   for (int i = threadIdx.x; i < npair; i += blockDim.x) {
-    const float mx = __uint_as_float(__ldcg(p.amax + i));
+    const float mx = __uint_as_float(s_max[i]);
     int ex = 0;
     if (mx > 0.f && mx == mx) frexpf(mx, &ex);
     s_inv[i] = ldexpf(1.0f, ex - 14);
   }
   __syncthreads();
-  {
-    const int n4 = npair * (I >> 2);
-    for (int i0 = threadIdx.x; i0 < n4; i0 += 12 * blockDim.x) {
-      float4 v[12];
-#pragma unroll
-      for (int j = 0; j < 12; ++j) {
-        const int i = i0 + j * blockDim.x;
-        v[j] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(p.actf) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int j = 0; j < 12; ++j) {
-        const int i = i0 + j * blockDim.x;
-        if (i < n4) {
-          const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
-          const float scl = 1.0f / s_inv[pair];  // exact: a power of two
-          const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            // position of k + e in the image: block, mma m, quarter q, half within the entry
-            const int kk = k + e, bi = kk >> 8, kin = kk & 255, q4 = kin >> 6, r = kin & 63;
-            const int m = 8 * (r >> 5) + ((r & 15) >> 1), pos = 2 * (r & 1) + ((r >> 4) & 1);
-            reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] =
-                f32_to_f16_bits(vv[e] * scl);
-          }
-        }
-      }
+  if (n4 <= round) {
+    convert_act(threadIdx.x);
+  } else {
+    for (int i0 = threadIdx.x; i0 < n4; i0 += round) {
+      load_act(i0);
+      convert_act(i0);
     }
   }
   __syncthreads();
@@ -833,24 +912,26 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
     const uint2* xl = as + sc.pair[u][g] * kRow + qq;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int b = 0; b < nbi; ++b) {
-      const int64_t c0 = R.consumed;
-      if (!ring_wait(R, c0, lane == 0 ? p.err : nullptr)) {
+      if (!ring_wait(R, lane == 0 ? p.err : nullptr)) {
         failed = true;
         break;
       }
       Iq4Lane W;
-      iq4_load(R.ring + (c0 % S) * kChunk, lane, W);
+      iq4_load(R.ring + R.c_slot * kChunk, lane, W);
+      ring_pop(R);
+      // the chunk is in registers: hand the stage back before computing on it
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        --R.in_flight;
+        ring_issue(R, base_of);
+      }
       float t4[4] = {0.f, 0.f, 0.f, 0.f};
       iq4_chunk_mma(W, xl + b * npair * kRow, lut, lane4, t4);
       acc[0] += W.d[0] * t4[0];
       acc[1] += W.d[0] * t4[1];
       acc[2] += W.d[1] * t4[2];
       acc[3] += W.d[1] * t4[3];
-      R.consumed = c0 + 1;
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) ring_issue(R, base_of);
-      __syncwarp();
     }
     if (failed) break;
 #pragma unroll
@@ -870,25 +951,39 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   // one fence for all of this warp's parts, then per item: the last slot to finish
   // a 16-row tile combines it
   __threadfence();
-  for (int item = i_first; item < n_items; item += R.step) {
-    const int tau = item % tpd;
+  // the counters of up to 32 of the warp's items are bumped at once (lane j: the j-th
+  // item), then the warp combines the tiles it completed
+  for (int base = i_first; base < n_items; base += 32 * R.step) {
+    const int mine = base + lane * R.step;
     uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(p.cnt + tau, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == static_cast<uint32_t>(n_slots - 1)) {
-      __threadfence();
-      for (int idx = lane; idx < 16 * P; idx += 32) {
-        const int t = idx >> 4, row = tau * 16 + (idx & 15);
-        float a = 0.f;
-        for (int r = 0; r < kTopK; ++r) {
-          const int id = __ldcg(&p.meta->ids[t * kTopK + r]);
-          if (id >= p.e0 && id < p.e1)
-            a += __ldcg(&p.meta->gates[t * kTopK + r]) *
-                 __ldcg(p.parts + static_cast<int64_t>(t * kTopK + r) * p.H + row);
+    if (mine < n_items) old = atomicAdd(p.cnt + mine % tpd, 1u);
+    uint32_t last = __ballot_sync(0xffffffffu, mine < n_items && old == static_cast<uint32_t>(n_slots - 1));
+    if (last) __threadfence();
+    while (last) {
+      const int tau = (base + (__ffs(last) - 1) * R.step) % tpd;
+      last &= last - 1;
+      // 16 rows x P positions per tile; each output's nine parts are loaded together,
+      // then summed in a fixed order (routed ranks 0..7, then the shared expert)
+#pragma unroll 1
+      for (int it = 0; it < (16 * kMaxPos + 31) / 32; ++it) {
+        const int idx = lane + 32 * it;
+        if (idx < 16 * P) {
+          const int t = idx >> 4, row = tau * 16 + (idx & 15);
+          float pv[kTopK + 1];
+#pragma unroll
+          for (int r = 0; r < kTopK; ++r) pv[r] = __ldcg(p.parts + static_cast<int64_t>(t * kTopK + r) * p.H + row);
+          pv[kTopK] = __ldcg(p.parts + static_cast<int64_t>(kTopK * P + t) * p.H + row);
+          const float hr = p.hres ? p.hres[t * p.ldr + row] : 0.f;
+          float a = 0.f;
+#pragma unroll
+          for (int r = 0; r < kTopK; ++r) {
+            const float gw = s_gate[t * kTopK + r];
+            if (gw != 0.f) a += gw * pv[r];
+          }
+          const float gs = s_gate[kTopK * P + t];
+          if (gs != 0.f) a += gs * pv[kTopK];
+          p.y[t * p.ldy + row] = hr + a;
         }
-        if (p.with_shared)
-          a += __ldcg(&p.meta->sg[t]) * __ldcg(p.parts + static_cast<int64_t>(kTopK * P + t) * p.H + row);
-        p.y[t * p.ldy + row] = p.hres ? p.hres[t * p.ldr + row] + a : a;
       }
       if (lane == 0) p.cnt[tau] = 0u;
     }
@@ -898,7 +993,7 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
 
 // ------------------------------------------------------------------------------ host
 struct WsLayout {
-  size_t meta, logits, cnt, err, ximg, actf, amax, parts, total;
+  size_t meta, logits, cnt, err, ximg, actf, parts, total;
 };
 
 inline size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -923,8 +1018,6 @@ WsLayout ws_layout(int P, int E, int H, int I) {
   o = up256(o + static_cast<size_t>(H / 256) * P * kRowBytes);
   w.actf = o;
   o = up256(o + static_cast<size_t>(9 * P) * I * 4);
-  w.amax = o;
-  o = up256(o + static_cast<size_t>(9 * P) * 4);
   w.parts = o;
   o = up256(o + static_cast<size_t>(9 * P) * H * 4);
   w.total = o;
@@ -983,7 +1076,6 @@ int setup(const MoeParams& in, int P, int E, int H, int I, int e0, int e1, void*
   p.err = reinterpret_cast<uint32_t*>(b + w.err);
   p.ximg = reinterpret_cast<uint2*>(b + w.ximg);
   p.actf = reinterpret_cast<float*>(b + w.actf);
-  p.amax = reinterpret_cast<uint32_t*>(b + w.amax);
   p.parts = reinterpret_cast<float*>(b + w.parts);
   p.gu_bytes = static_cast<int64_t>(I / 16) * (H / 256) * kChunk;
   p.dn_bytes = static_cast<int64_t>(H / 16) * (I / 256) * kChunk;

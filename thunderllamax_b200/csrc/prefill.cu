@@ -264,7 +264,45 @@ struct PrefillParams {
   int64_t ldo;
   const float* row_scale;  // per-token power-of-two scale of the staged tokens (nullptr: 1)
   uint32_t* err;
+  // work list: n_full whole tiles, then the last split_r tiles (the ones that would
+  // leave most SMs idle in a final partial wave) as `pieces` k-ranges each; the
+  // pieces write fp32 partial accumulators and the last one to finish sums them in
+  // piece order (deterministic) and runs the epilogue
+  int n_full, split_r, pieces;
+  uint32_t* cnt;  // [split_r][2]: pieces arrived / departed (the last to depart re-arms both)
+  float* part;    // [split_r][pieces][NMAT][kPfTok tokens][kPfRows rows]
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* q) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(q) : "memory");
+  return v;
+}
+
+struct WorkItem {
+  int tile, kt0, kt1;  // output tile and its k-step range
+  int slot, piece;     // slot < 0: a whole tile
+};
+
+__device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int item, int kt_per_tile) {
+  WorkItem w;
+  if (item < p.n_full) {
+    w.tile = item;
+    w.kt0 = 0;
+    w.kt1 = kt_per_tile;
+    w.slot = -1;
+    w.piece = 0;
+    return w;
+  }
+  const int j = item - p.n_full;
+  w.slot = j / p.pieces;
+  w.piece = j - w.slot * p.pieces;
+  w.tile = p.n_full + w.slot;
+  w.kt0 = w.piece * kt_per_tile / p.pieces;
+  w.kt1 = (w.piece + 1) * kt_per_tile / p.pieces;
+  return w;
+}
+
 
 template <int QT, int NMAT>
 struct Smem {
@@ -277,7 +315,7 @@ struct Smem {
   static constexpr uint32_t kGridOff = kStagesOff + kStages * kStage;
   static constexpr uint32_t kBarOff = kGridOff + kGrid;
   // full[S], empty[S], acc_full, acc_empty, done, tmem holder + abort flag
-  static constexpr uint32_t kBytes = kBarOff + (2 * kStages + 3) * 8 + 16;
+  static constexpr uint32_t kBytes = kBarOff + (2 * kStages + 4) * 8 + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // slack to align the base to 1024
 };
 
@@ -295,7 +333,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   uint64_t* acc_full = bars + 2 * S;
   uint64_t* acc_empty = bars + 2 * S + 1;
   uint64_t* done = bars + 2 * S + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 3);
+  uint64_t* epi_sync = bars + 2 * S + 3;  // the four epilogue warps (split-tile pieces)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   volatile uint32_t* abort_flag = tmem_holder + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -304,6 +343,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int row_tiles = p.N / kPfRows;
   const int tok_tiles = (p.M + kPfTok - 1) / kPfTok;
   const int n_tiles = row_tiles * tok_tiles;
+  const int n_items = p.n_full + p.split_r * p.pieces;
+  (void)n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -313,6 +354,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
     mbar_init(done, 1);
+    mbar_init(epi_sync, 4);
     *abort_flag = 0u;
     mbar_fence_init();
   }
@@ -344,9 +386,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t kt_global = 0;
-      for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
-        const int tt = tile % tok_tiles;
-        for (int kt = 0; kt < kt_per_tile && !*abort_flag; ++kt, ++kt_global) {
+      for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+        const WorkItem wi = work_item(p, item, kt_per_tile);
+        const int tt = wi.tile % tok_tiles;
+        for (int kt = wi.kt0; kt < wi.kt1 && !*abort_flag; ++kt, ++kt_global) {
           const int s = static_cast<int>(kt_global % S);
           if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) {
             fail();
@@ -361,13 +404,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     // ----------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       uint32_t kt_global = 0, tiles_done = 0;
-      for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, ++tiles_done) {
+      for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++tiles_done) {
+        const WorkItem wi = work_item(p, item, kt_per_tile);
         if (!wait_bounded(acc_empty, (tiles_done & 1) ^ 1)) {
           fail();
           break;
         }
         tc_fence_after();
-        for (int kt = 0; kt < kt_per_tile && !*abort_flag; ++kt, ++kt_global) {
+        for (int kt = wi.kt0; kt < wi.kt1 && !*abort_flag; ++kt, ++kt_global) {
           const int s = static_cast<int>(kt_global % S);
           if (!wait_bounded(&full[s], (kt_global / S) & 1)) {
             fail();
@@ -382,7 +426,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 #pragma unroll
             for (int mat = 0; mat < NMAT; ++mat) {
               const uint64_t adesc = sw128_desc(a0 + mat * kPfRows * 128 + kk * 32);
-              umma_f16(tmem + mat * kPfTok, adesc, bdesc, kIdesc, (kt > 0 || kk > 0) ? 1u : 0u);
+              umma_f16(tmem + mat * kPfTok, adesc, bdesc, kIdesc, (kt > wi.kt0 || kk > 0) ? 1u : 0u);
             }
           }
           umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
@@ -396,47 +440,153 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ------------------------------------------------------------------- epilogue
     const int wq = warp & 3;  // TMEM lane quarter of this warp
-    uint32_t tiles_done = 0;
-    for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x, ++tiles_done) {
-      const int rt = tile / tok_tiles, tt = tile - rt * tok_tiles;
+    const int rowl = wq * 32 + lane;  // this thread's row within the tile (its TMEM lane)
+    __shared__ uint32_t s_last;
+    uint32_t tiles_done = 0, epi_phase = 0;
+    // all four epilogue warps at one point (bounded, like every wait here)
+    auto epi_bar = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_sync);
+      const bool ok = wait_bounded(epi_sync, epi_phase);
+      epi_phase ^= 1u;
+      return ok;
+    };
+    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++tiles_done) {
+      const WorkItem wi = work_item(p, item, kt_per_tile);
+      const int rt = wi.tile / tok_tiles, tt = wi.tile - rt * tok_tiles;
       if (!wait_bounded_sleepy(acc_full, tiles_done & 1)) {
         if (lane == 0) fail();
         break;
       }
       tc_fence_after();
-      const int row = rt * kPfRows + wq * 32 + lane;
+      const int row = rt * kPfRows + rowl;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-      for (int c0 = 0; c0 < kPfTok; c0 += 16) {
-        uint32_t g[16];
-        tmem_ld16(tbase + c0, g);
-        if constexpr (NMAT == 2) {
-          uint32_t u[16];
-          tmem_ld16(tbase + kPfTok + c0, u);
-          tmem_wait_ld();
+      if (wi.slot < 0) {
+        for (int c0 = 0; c0 < kPfTok; c0 += 16) {
+          uint32_t g[16];
+          tmem_ld16(tbase + c0, g);
+          if constexpr (NMAT == 2) {
+            uint32_t u[16];
+            tmem_ld16(tbase + kPfTok + c0, u);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int tok = tt * kPfTok + c0 + j;
-            if (tok < p.M) {
-              const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
-              const float gv = __uint_as_float(g[j]) * sc, uv = __uint_as_float(u[j]) * sc;
-              static_cast<float*>(p.out)[tok * p.ldo + row] = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+            for (int j = 0; j < 16; ++j) {
+              const int tok = tt * kPfTok + c0 + j;
+              if (tok < p.M) {
+                const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
+                const float gv = __uint_as_float(g[j]) * sc, uv = __uint_as_float(u[j]) * sc;
+                static_cast<float*>(p.out)[tok * p.ldo + row] = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+              }
+            }
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int tok = tt * kPfTok + c0 + j;
+              if (tok < p.M) {
+                const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
+                static_cast<float*>(p.out)[tok * p.ldo + row] = __uint_as_float(g[j]) * sc;
+              }
             }
           }
-        } else {
-          tmem_wait_ld();
+        }
+      } else {
+        // a piece: its fp32 partial accumulators to the workspace (all 256 token
+        // columns; columns past M hold the zero-filled tokens' zeros)
+        float* pp = p.part + static_cast<int64_t>(wi.slot * p.pieces + wi.piece) * NMAT * (kPfTok * kPfRows);
+        for (int c0 = 0; c0 < kPfTok; c0 += 16) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int tok = tt * kPfTok + c0 + j;
-            if (tok < p.M) {
-              const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
-              static_cast<float*>(p.out)[tok * p.ldo + row] = __uint_as_float(g[j]) * sc;
-            }
+          for (int mat = 0; mat < NMAT; ++mat) {
+            uint32_t g[16];
+            tmem_ld16(tbase + mat * kPfTok + c0, g);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pp[(static_cast<int64_t>(mat) * kPfTok + c0 + j) * kPfRows + rowl] = __uint_as_float(g[j]);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) mbar_arrive(acc_empty);  // TMEM is free for the next item
+      if (wi.slot >= 0) {
+        // every piece of the tile runs in this final wave, one per CTA, all resident:
+        // wait until all have written their partials, then each sums its own share of
+        // the tile's token columns over the pieces in piece order (deterministic)
+        uint32_t* arrive = p.cnt + 2 * wi.slot;
+        uint32_t* depart = arrive + 1;
+        __threadfence();
+        if (!epi_bar()) {
+          if (lane == 0) fail();
+          break;
+        }
+        if (warp == kEpiWarp0 && lane == 0) {
+          atomicAdd(arrive, 1u);
+          bool all = false;
+          for (uint32_t i = 0; i < (kPollLimit >> 4) && !all; ++i) {
+            all = ld_acquire_gpu(arrive) >= static_cast<uint32_t>(p.pieces);
+            if (!all) __nanosleep(256);
+          }
+          s_last = all ? 1u : 0u;
+        }
+        if (!epi_bar()) {
+          if (lane == 0) fail();
+          break;
+        }
+        if (!s_last) {
+          if (lane == 0) fail();
+          break;
+        }
+        __threadfence();
+        const float* pb = p.part + static_cast<int64_t>(wi.slot * p.pieces) * NMAT * (kPfTok * kPfRows);
+        const int c_lo = wi.piece * kPfTok / p.pieces, c_hi = (wi.piece + 1) * kPfTok / p.pieces;
+        constexpr int kTokUnroll = 8;  // token columns whose partial loads are in flight together
+        for (int c0 = c_lo; c0 < c_hi; c0 += kTokUnroll) {
+          float acc[kTokUnroll][NMAT];
+#pragma unroll
+          for (int j = 0; j < kTokUnroll; ++j)
+#pragma unroll
+            for (int mat = 0; mat < NMAT; ++mat) acc[j][mat] = 0.f;
+          for (int q = 0; q < p.pieces; ++q) {
+            float v[kTokUnroll][NMAT];
+#pragma unroll
+            for (int j = 0; j < kTokUnroll; ++j)
+#pragma unroll
+              for (int mat = 0; mat < NMAT; ++mat)
+                v[j][mat] = c0 + j < c_hi
+                                ? __ldcg(pb + ((static_cast<int64_t>(q) * NMAT + mat) * kPfTok + c0 + j) * kPfRows + rowl)
+                                : 0.f;
+#pragma unroll
+            for (int j = 0; j < kTokUnroll; ++j)
+#pragma unroll
+              for (int mat = 0; mat < NMAT; ++mat) acc[j][mat] += v[j][mat];
+          }
+#pragma unroll
+          for (int j = 0; j < kTokUnroll; ++j) {
+            const int tok = tt * kPfTok + c0 + j;
+            if (c0 + j < c_hi && tok < p.M) {
+              const float sc = p.row_scale ? p.row_scale[tok] : 1.0f;
+              float o;
+              if constexpr (NMAT == 2) {
+                const float gv = acc[j][0] * sc, uv = acc[j][1] * sc;
+                o = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
+              } else {
+                o = acc[j][0] * sc;
+              }
+              static_cast<float*>(p.out)[tok * p.ldo + row] = o;
+            }
+          }
+        }
+        // the last piece to leave re-arms both counters for the next launch
+        if (!epi_bar()) {
+          if (lane == 0) fail();
+          break;
+        }
+        if (warp == kEpiWarp0 && lane == 0 && atomicAdd(depart, 1u) == static_cast<uint32_t>(p.pieces - 1)) {
+          *arrive = 0u;
+          *depart = 0u;
+        }
+      }
     }
   } else if (warp >= kDequantWarp0) {
     // ----------------------------------------------------------------- dequantise
@@ -452,26 +602,32 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const uint8_t* wmat = mat == 0 ? p.w0 : p.w1;
     const uint32_t chunk = chunk_bytes(QT);
     const int r0 = 16 * t16 + g, r1 = r0 + 8;
-    // position in this CTA's k-step sequence: tile, 256-k block, quarter (decode lane 4g + q)
+    // position in this CTA's k-step sequence: work item, its tile and k step (256-k
+    // block kt / 4, quarter kt % 4 = decode lane 4g + q)
     struct Pos {
-      int tile, b, q;
+      int item, tile, kt, kt1;
+    };
+    auto start = [&](Pos& ps, int item) {
+      ps.item = item;
+      if (item < n_items) {
+        const WorkItem wi = work_item(p, item, kt_per_tile);
+        ps.tile = wi.tile;
+        ps.kt = wi.kt0;
+        ps.kt1 = wi.kt1;
+      }
     };
     auto advance = [&](Pos& ps) {
-      if (++ps.q == 4) {
-        ps.q = 0;
-        if (++ps.b == nb) {
-          ps.b = 0;
-          ps.tile += gridDim.x;
-        }
-      }
+      if (++ps.kt == ps.kt1) start(ps, ps.item + static_cast<int>(gridDim.x));
     };
     auto fetch = [&](const Pos& ps, PartT<QT>& r) {
-      if (ps.tile < n_tiles) {
+      if (ps.item < n_items) {
         const int rt = ps.tile / tok_tiles;
-        load_part(wmat + (static_cast<int64_t>(rt * 8 + t16) * nb + ps.b) * chunk, 4 * g + ps.q, part, r);
+        load_part(wmat + (static_cast<int64_t>(rt * 8 + t16) * nb + (ps.kt >> 2)) * chunk, 4 * g + (ps.kt & 3), part,
+                  r);
       }
     };
-    Pos cur{static_cast<int>(blockIdx.x), 0, 0};
+    Pos cur;
+    start(cur, static_cast<int>(blockIdx.x));
     Pos pre = cur;
     PartT<QT> bufA, bufB, bufC;
     fetch(pre, bufA);
@@ -497,11 +653,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       ++kt_global;
       return true;
     };
-    while (cur.tile < n_tiles && ok && !*abort_flag) {
+    while (cur.item < n_items && ok && !*abort_flag) {
       ok = step(bufA, bufC);
-      if (!ok || cur.tile >= n_tiles || *abort_flag) break;
+      if (!ok || cur.item >= n_items || *abort_flag) break;
       ok = step(bufB, bufA);
-      if (!ok || cur.tile >= n_tiles || *abort_flag) break;
+      if (!ok || cur.item >= n_items || *abort_flag) break;
       ok = step(bufC, bufB);
     }
     if (!ok && lane == 0) fail();
@@ -630,8 +786,16 @@ int sms() {
   return n > 0 ? n : 148;
 }
 
+constexpr int kMinPieceSteps = 16;  // k steps (64 k each) of the shortest piece of a split tile
+
+// split region of the workspace (after the token staging): two counters per split
+// tile (fewer than ctas), then the partials of at most ctas pieces of two matrices
+size_t split_cnt_bytes(int ctas) { return (static_cast<size_t>(ctas) * 8 + 255) & ~size_t(255); }
+size_t split_bytes(int ctas) { return split_cnt_bytes(ctas) + static_cast<size_t>(ctas) * 2 * kPfTok * kPfRows * 4; }
+
 template <int QT, int NMAT>
-int launch_prefill(const CUtensorMap& map, const PrefillParams& p, int max_ctas, cudaStream_t stream) {
+int launch_prefill(const CUtensorMap& map, const PrefillParams& p, int max_ctas, uint8_t* split_ws,
+                   size_t split_ws_bytes, cudaStream_t stream) {
   using L = Smem<QT, NMAT>;
   auto kern = prefill_kernel<QT, NMAT>;
   static bool configured = false;
@@ -644,9 +808,29 @@ int launch_prefill(const CUtensorMap& map, const PrefillParams& p, int max_ctas,
   const int tiles = (p.N / kPfRows) * ((p.M + kPfTok - 1) / kPfTok);
   int ctas = sms();
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
-  if (ctas > tiles) ctas = tiles;
-  CUtensorMap m = map;
   PrefillParams q = p;
+  // the tiles of a final partial wave are split into k pieces across the idle SMs
+  q.n_full = tiles;
+  q.split_r = 0;
+  q.pieces = 1;
+  q.cnt = nullptr;
+  q.part = nullptr;
+  const int rem = tiles % ctas;
+  if (rem != 0 && split_ws && split_ws_bytes >= split_bytes(ctas)) {
+    int pieces = ctas / rem;
+    const int max_pieces = (p.K / kKStep) / kMinPieceSteps;
+    if (pieces > max_pieces) pieces = max_pieces;
+    if (pieces >= 2) {
+      q.n_full = tiles - rem;
+      q.split_r = rem;
+      q.pieces = pieces;
+      q.cnt = reinterpret_cast<uint32_t*>(split_ws);
+      q.part = reinterpret_cast<float*>(split_ws + split_cnt_bytes(ctas));
+    }
+  }
+  const int items = q.n_full + q.split_r * q.pieces;
+  if (ctas > items) ctas = items;
+  CUtensorMap m = map;
   void* args[] = {&m, &q};
   return launch_pdl_raw(reinterpret_cast<const void*>(kern), dim3(ctas), dim3(kWarps * 32), L::kAlloc, stream, args);
 }
@@ -690,7 +874,10 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
     void* args[] = {&xb, &ldx, &mm, &kk, &o, &sc};
     const void* kern = x_dtype == DT_F32 ? reinterpret_cast<const void*>(to_f16_kernel<true>)
                                          : reinterpret_cast<const void*>(to_f16_kernel<false>);
-    const int rc = launch_pdl_raw(kern, dim3(blocks), dim3(256), 0, stream, args);
+    // an ordinary launch: overlapped with the persistent kernel before it (PDL), the
+    // staging ran about 85 us slower at config 5
+    const int rc = cudaLaunchKernel(kern, dim3(blocks), dim3(256), args, 0, stream) == cudaSuccess ? TLX_OK
+                                                                                         : TLX_ERR_LAUNCH;
     if (rc) return rc;
     xf16 = ws;
     ldx16 = k;
@@ -713,8 +900,17 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   p.ldo = ldo;
   p.row_scale = row_scale;
   p.err = err;
-  if (gate_up) return launch_prefill<QT_IQ3_XXS, 2>(map, p, max_ctas, stream);
-  return launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, stream);
+  // the split region follows the token staging (present in a workspace sized by
+  // tlx_prefill_workspace_bytes; a smaller one runs without splitting)
+  uint8_t* split_ws = nullptr;
+  size_t split_ws_bytes = 0;
+  const size_t split_off = (prefill_x_bytes(m, k) + 255) & ~size_t(255);
+  if (ws && ws_bytes > split_off && al16(ws)) {
+    split_ws = static_cast<uint8_t*>(ws) + split_off;
+    split_ws_bytes = ws_bytes - split_off;
+  }
+  if (gate_up) return launch_prefill<QT_IQ3_XXS, 2>(map, p, max_ctas, split_ws, split_ws_bytes, stream);
+  return launch_prefill<QT_Q6_K, 1>(map, p, max_ctas, split_ws, split_ws_bytes, stream);
 }
 
 }  // namespace tlx
@@ -729,7 +925,7 @@ extern "C" {
 
 size_t tlx_prefill_workspace_bytes(int m, int64_t k) {
   if (m < 1 || k < 256 || k % 256) return 0;
-  return kPfErrBytes + prefill_x_bytes(m, k);
+  return kPfErrBytes + ((prefill_x_bytes(m, k) + 255) & ~size_t(255)) + split_bytes(sms());
 }
 
 int tlx_prefill_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, const uint32_t* grid, const void* x,

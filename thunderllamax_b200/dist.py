@@ -109,6 +109,11 @@ class PeerComm:
         self.local = None
 
 
+def default_ffn_ctas(world: int, sms: int) -> int:
+    """CTAs for the FFN stream of the peer step (the head gets the rest)."""
+    return {2: 48, 4: 64, 8: 64}.get(world, 64) if sms >= 128 else 0
+
+
 def allreduce_partial(y: torch.Tensor, group=None) -> torch.Tensor:
     """Sum the per-rank partial down-projection outputs in place."""
     dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
@@ -133,12 +138,13 @@ class ShardedVerifyStep:
     KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
 
     def __init__(self, shape: VerifyShape, rank: int, world: int, seed: int = 0, weights: dict | None = None,
-                 group=None, comm: str = "peer"):
+                 group=None, comm: str = "peer", ffn_ctas: int | None = None):
         ops.require_device()
         if comm not in ("peer", "nccl"):
             raise ValueError(f"comm must be 'peer' or 'nccl', not {comm!r}")
         self.comm = comm
-        self.LAUNCHES_PER_STEP = 5 if comm == "peer" else 6   # stage/gate-up, down, stage/head (+ merge)
+        # stage/gate-up, down, stage/head, then the finish kernel (peer) or the merge (nccl)
+        self.LAUNCHES_PER_STEP = 6
         self.COLLECTIVES = ("down partials and head keys over peer memory inside the kernels" if comm == "peer"
                             else "NCCL all-reduce of the down partials + NCCL all-gather of the head keys")
         self.shape = s = shape
@@ -171,12 +177,25 @@ class ShardedVerifyStep:
         self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
         self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
         self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
-        self.ws = {
-            "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, self.n_ffn, s.dim, s.rows),
-            "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, self.n_ffn, s.rows, "image"),
-            "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, self.n_voc, s.dim, s.rows),
-        }
+        # peer mode: the FFN (gate/up -> down) and the head run on two streams at once,
+        # each on its own share of the SMs; both are latency-bound at these shard sizes,
+        # so running them side by side hides one's fixed costs behind the other
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        if comm == "peer":
+            self.ffn_ctas = ffn_ctas if ffn_ctas is not None else default_ffn_ctas(world, sms)
+            self.head_ctas = sms - self.ffn_ctas if self.ffn_ctas else 0
+        else:
+            self.ffn_ctas = self.head_ctas = 0
+        with ops.cta_budget(self.ffn_ctas):
+            self.ws = {
+                "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, self.n_ffn, s.dim, s.rows),
+                "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, self.n_ffn, s.rows, "image"),
+            }
+        with ops.cta_budget(self.head_ctas):
+            self.ws["head_argmax"] = ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, self.n_voc, s.dim, s.rows)
         self.peer = PeerComm(rank, world, s.rows, s.dim, group) if comm == "peer" else None
+        self.side = torch.cuda.Stream() if comm == "peer" else None
+        self.finish_err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.graph = None
 
     def algorithmic_bytes_per_rank(self) -> dict:
@@ -190,18 +209,21 @@ class ShardedVerifyStep:
 
     def launch_ffn_gate_up(self):
         s = self.shape
-        ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, self.n_ffn, self.ws["ffn_gate_up"],
-                        gact=self.gact)
+        with ops.cta_budget(self.ffn_ctas):
+            ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, self.n_ffn, self.ws["ffn_gate_up"],
+                            gact=self.gact)
 
     def launch_ffn_down(self):
         s = self.shape
         res = self.res if self.rank == 0 else None
-        ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, self.ws["ffn_down"], y=self.y, residual=res)
+        with ops.cta_budget(self.ffn_ctas):
+            ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, self.ws["ffn_down"], y=self.y, residual=res)
 
     def launch_head_argmax(self):
         s = self.shape
-        ops.head_argmax(s.head_q, self.w["head"], self.h, self.n_voc, self.ws["head_argmax"],
-                        row_offset=self.v0, out_keys=self.local_keys)
+        with ops.cta_budget(self.head_ctas):
+            ops.head_argmax(s.head_q, self.w["head"], self.h, self.n_voc, self.ws["head_argmax"],
+                            row_offset=self.v0, out_keys=self.local_keys)
 
     def launch_ffn_down_peer(self):
         """This rank's down partial into every rank's buffer (tlx_gemv_peer)."""
@@ -211,30 +233,46 @@ class ShardedVerifyStep:
         w = self.ws["ffn_down"]
         _lib.check(_lib.lib().tlx_gemv_peer(ops.qtype_id(s.down_q), ops._ptr(self.w["down"]), None,
                                             ops._ptr(self.gact), _lib.TLX_DT_IMAGE, 0, s.rows, s.dim, self.n_ffn,
-                                            self.world, self.rank, self.peer.ptrs, ops._ptr(w.buf), w.nbytes,
-                                            ops._stream(self.x)), "gemv_peer")
+                                            self.world, self.rank, self.peer.ptrs, self.ffn_ctas, ops._ptr(w.buf),
+                                            w.nbytes, ops._stream(self.x)), "gemv_peer")
 
     def launch_head_argmax_peer(self):
-        """This rank's vocabulary shard of the head, then y = residual + the ranks' down
-        partials and the merge of the ranks' keys + accept (tlx_head_argmax_peer)."""
+        """This rank's vocabulary shard of the head, then the merge of the ranks' keys +
+        greedy accept in its last CTA (tlx_head_argmax_peer)."""
         from . import _lib
 
         s = self.shape
         w = self.ws["head_argmax"]
         dt, ldx = ops._x_args(self.h)
         g = ops.grid("cuda") if s.head_q == "iq3_xxs" else None
-        _lib.check(_lib.lib().tlx_head_argmax_peer(
-            ops.qtype_id(s.head_q), ops._ptr(self.w["head"]), ops._ptr(g), ops._ptr(self.h), dt, ldx, s.rows,
-            self.n_voc, s.dim, self.v0, ops._ptr(self.out_max), ops._ptr(self.out_idx), ops._ptr(self.drafts),
-            s.n_drafts, ops._ptr(self.accept_out), self.world, self.rank, self.peer.ptrs, s.dim, ops._ptr(self.res),
-            s.dim, ops._ptr(self.y), s.dim, ops._ptr(w.buf), w.nbytes, ops._stream(self.h)), "head_argmax_peer")
+        with ops.cta_budget(self.head_ctas):     # the staging of h is sized by the same plan
+            _lib.check(_lib.lib().tlx_head_argmax_peer(
+                ops.qtype_id(s.head_q), ops._ptr(self.w["head"]), ops._ptr(g), ops._ptr(self.h), dt, ldx, s.rows,
+                self.n_voc, s.dim, self.v0, ops._ptr(self.out_max), ops._ptr(self.out_idx), ops._ptr(self.drafts),
+                s.n_drafts, ops._ptr(self.accept_out), self.world, self.rank, self.peer.ptrs, self.head_ctas,
+                ops._ptr(w.buf), w.nbytes, ops._stream(self.h)), "head_argmax_peer")
+
+    def launch_finish(self):
+        """y = residual + the ranks' down partials, and the step counter advances."""
+        from . import _lib
+
+        s = self.shape
+        _lib.check(_lib.lib().tlx_peer_finish(self.world, self.rank, self.peer.ptrs, s.rows, s.dim,
+                                              ops._ptr(self.res), s.dim, ops._ptr(self.y), s.dim,
+                                              ops._ptr(self.finish_err), ops._stream(self.y)), "peer_finish")
 
     def launch(self):
-        self.launch_ffn_gate_up()
         if self.comm == "peer":
+            cur = torch.cuda.current_stream()
+            self.side.wait_stream(cur)
+            with torch.cuda.stream(self.side):
+                self.launch_head_argmax_peer()
+            self.launch_ffn_gate_up()
             self.launch_ffn_down_peer()
-            self.launch_head_argmax_peer()
+            cur.wait_stream(self.side)
+            self.launch_finish()
             return
+        self.launch_ffn_gate_up()
         self.launch_ffn_down()
         allreduce_partial(self.y, self.group)
         self.launch_head_argmax()

@@ -6,6 +6,7 @@ on the CPU or falls back to torch kernels.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import functools
 
@@ -123,6 +124,17 @@ def plan(mode: int, qtype, n_rows: int, k: int, m: int, x_dtype=torch.bfloat16) 
 
 def set_max_ctas(n: int) -> None:
     _lib.lib().tlx_set_max_ctas(int(n))
+
+
+@contextlib.contextmanager
+def cta_budget(n: int):
+    """GEMV launches and workspace sizes inside the block use at most n CTAs (0: one
+    per SM); the setting returns to one per SM afterwards."""
+    set_max_ctas(n)
+    try:
+        yield
+    finally:
+        set_max_ctas(0)
 
 
 class Image:
