@@ -33,9 +33,10 @@ METRIC = "µs per K=11 verify step + weight GB/s (% HBM roofline) at 1/2/4/8 B20
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) per head row of the fused head/argmax launch, from one
-# ncu --set full capture at vocab 32768 (profiles/tile_gemv_verify_small_full.txt:
-# 138.52 MB read + 4.80 MB written), scaled to a launch by its row count
-HEAD_TRAFFIC_BYTES_PER_ROW = (138_524_160 + 4_795_136) / 32768
+# ncu --set full capture of that kernel alone at the full vocabulary 151936
+# (profiles/tile_gemv_head_argmax_full.txt: 640.28 MB read + 6.18 MB written),
+# scaled to a launch by its row count (a vocabulary shard at N > 1)
+HEAD_TRAFFIC_BYTES_PER_ROW = (640_278_528 + 6_181_888) / 151936
 
 
 def measured_peak():
@@ -400,6 +401,48 @@ def measure_prefill(args, torch, weights):
             "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
 
 
+def measure_moe_exchange(torch, dist, shape, ws, max_over_ranks, reps: int = 20):
+    """The MoE layer's cross-GPU exchange alone, two ways, each captured `reps` times
+    in one CUDA graph and timed with CUDA events (max over ranks):
+    - replicated positions (what ShardedMoeVerifyStep does): every rank holds all P
+      positions, computes its experts' share of the layer output, and one NCCL
+      all-reduce sums the [P][hidden] fp32 partials;
+    - token dispatch: positions owned round-robin by ranks, an NCCL all-to-all sends
+      each owner's bf16 rows to every rank (the experts of a position can sit on any
+      rank), and a second all-to-all returns each rank's fp32 partial rows to the
+      owners (which then add them).
+    Every rank takes the same collective steps in the same order."""
+    P, H = shape.positions, shape.hidden
+    per = -(-P // ws)                                # positions per owner, padded
+    y = torch.zeros((P, H), dtype=torch.float32, device="cuda")
+    send_h = torch.zeros((ws * per, H), dtype=torch.bfloat16, device="cuda")
+    recv_h = torch.empty_like(send_h)
+    send_y = torch.zeros((ws * per, H), dtype=torch.float32, device="cuda")
+    recv_y = torch.empty_like(send_y)
+
+    def allreduce():
+        for _ in range(reps):
+            dist.all_reduce(y)
+
+    def a2a():
+        for _ in range(reps):
+            dist.all_to_all_single(recv_h, send_h)
+            dist.all_to_all_single(recv_y, send_y)
+
+    res = {}
+    for name, fn in (("allreduce_replicated_us", allreduce), ("all_to_all_dispatch_combine_us", a2a)):
+        g = _graph_of(fn, torch)
+        g.replay()
+        dist.barrier()
+        res[name] = round(max_over_ranks(time_graph(g.replay, 5, torch) / reps) * 1000, 2)
+        del g
+    torch.cuda.synchronize()
+    res["bytes"] = {"allreduce": P * H * 4, "dispatch": ws * per * H * 2, "combine": ws * per * H * 4}
+    res["chosen"] = ("replicated positions + one all-reduce" if res["allreduce_replicated_us"]
+                     <= res["all_to_all_dispatch_combine_us"] else "token dispatch (all-to-all) would be faster")
+    return res
+
+
 def measure_sharded_extras(args, torch, ws, rank, peak):
     """At N > 1: the MoE verify layer expert parallel and the prefill FFN tensor
     parallel over all ranks (ShardedMoeVerifyStep / ShardedPrefillFFN, one NCCL
@@ -446,6 +489,7 @@ def measure_sharded_extras(args, torch, ws, rank, peak):
                              "timing": "CUDA graph replay, max over ranks", "err_word": step.local.ws.error()}
         step.release()
         del step
+        out["moe_exchange"] = measure_moe_exchange(torch, dist, shape, ws, max_over_ranks)
     if not args.no_prefill:
         shape = PrefillShape()
         step = ShardedPrefillFFN(shape, rank, ws, seed=0)
@@ -853,7 +897,7 @@ def run_ours(args):
               "roofline": {"bound": "hbm", "kernel": "head_argmax", "achieved": round(achieved, 1),
                            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                            "traffic": round(HEAD_TRAFFIC_BYTES_PER_ROW * head_rows),
-                           "traffic_source": "ncu dram__bytes_read+write at vocab 32768, scaled by rows",
+                           "traffic_source": "ncu dram__bytes_read+write of the head kernel at vocab 151936, scaled by rows",
                            "algorithmic_bytes": alg["head_argmax"], "us": round(head_ms * 1000, 2)},
               "kernels": kernels,
               "cpu_baseline": cpu,
@@ -926,6 +970,39 @@ def profile_gemv(which: str, vocab: int, ffn: int) -> int:
     return 0 if not bad else 1
 
 
+def profile_layer(which: str) -> int:
+    """A small driver for ncu: four eager launches of the MoE verify layer (config 4:
+    router, gate/up, down per layer) or of the prefill FFN (config 5: token staging,
+    gate/up, act staging, down), seeded as in the bench, then exit."""
+    import numpy as np
+    import torch
+    from thunderllamax_b200 import synth
+
+    rng = np.random.default_rng(4321)
+    if which == "moe":
+        from thunderllamax_b200 import moe
+
+        step = moe.MoeVerifyStep(moe.MoeShape(), seed=0)
+        s = step.shape
+        h = torch.from_numpy(synth.bf16_normal(rng, (s.positions, s.hidden)).view(np.int16)).cuda()
+        step.set_inputs(h.view(torch.bfloat16), torch.zeros((s.positions, s.hidden), device="cuda"))
+        errs = lambda: [step.ws.error()]                            # noqa: E731
+    else:
+        from thunderllamax_b200 import prefill
+
+        step = prefill.PrefillFFN(prefill.PrefillShape(), seed=0)
+        s = step.shape
+        step.x.copy_(torch.from_numpy(synth.bf16_normal(rng, (s.tokens, s.dim)).view(np.int16)).cuda()
+                     .view(torch.bfloat16))
+        errs = lambda: [step.ws.error(), step.ws_down.error()]     # noqa: E731
+    for _ in range(4):
+        step.launch()
+    torch.cuda.synchronize()
+    bad = [e for e in errs() if e]
+    print(json.dumps({"profile_layer": which, "ok": not bad, "errors": bad}))
+    return 0 if not bad else 1
+
+
 def profile_attention(pos: int) -> int:
     """A small driver for ncu: the attention split kernel alone at context `pos`
     (11 rows, ctx 100352, random int8 cache and scales, qw16 N(0, 1) / 16)."""
@@ -962,6 +1039,8 @@ def main():
                     help="profiling case: one warm-up and one tlx_attn_split launch at context POS, then exit")
     ap.add_argument("--profile-gemv", choices=["gate_up", "down", "head"], default=None,
                     help="profiling case: one verify GEMV alone (a full step first, then four launches), then exit")
+    ap.add_argument("--profile-layer", choices=["moe", "prefill"], default=None,
+                    help="profiling case: four eager MoE-layer or prefill-FFN launches, then exit")
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
     args = ap.parse_args()
@@ -969,6 +1048,8 @@ def main():
         return profile_attention(args.profile_attention)
     if args.profile_gemv is not None:
         return profile_gemv(args.profile_gemv, args.vocab, args.ffn)
+    if args.profile_layer is not None:
+        return profile_layer(args.profile_layer)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -746,9 +746,11 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   }
   __syncthreads();
   if (failed || Uc == 0) return;
-  for (int k = 0; k < Kc; ++k) {
-    const int wf = warp_of_unit(k * nbh), wl = warp_of_unit((k + 1) * nbh - 1);
-    if (wl != warp || wf == wl) continue;
+  // the one split item this warp may finish: the item holding its first unit, when
+  // that item starts in an earlier warp and ends inside this warp's range
+  if (v0 < v1 && v0 % nbh != 0 && (v0 / nbh + 1) * nbh <= v1) {
+    const int k = v0 / nbh;
+    const int wf = warp_of_unit(k * nbh), wl = warp;
     float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
     for (int w = wf; w <= wl; ++w) {
       const float* pw = reinterpret_cast<const float*>(smem + L.ring + static_cast<uint32_t>(w * S) * kChunk);
