@@ -891,6 +891,10 @@ def run_ours(args):
               "config": bench_config(shape, ws),
               "timing": {"graph": f"CUDA graph replay, {step.LAUNCHES_PER_STEP} launches/step"
                                   + (f" ({step.COLLECTIVES})" if ws > 1 else ""),
+                         "schedule": (f"FFN chain (gate/up -> down) on {step.ffn_ctas} SMs beside the head on "
+                                      f"{step.head_ctas} SMs, two graph branches" if step.ffn_ctas
+                                      else "the three GEMVs in sequence on every SM"),
+                         "kernels": "each kernel alone on every SM, 20 launches back to back per graph",
                          "l2": f"weights {total_w / 1e6:.0f} MB > 126 MB L2 (no flush needed)",
                          "device_time": "CUDA events around the K replays, max over ranks"},
               "frac_of_hbm": round(value / ws / peak, 4), "frac_of_8tbs": round(value / ws / 8000.0, 4),

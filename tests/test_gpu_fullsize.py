@@ -125,8 +125,8 @@ def test_config23_verify_step_full_size(model, head_cases):
     step.replay()
     step.replay()                                   # a second replay: same bits
     torch.cuda.synchronize()
-    for nm, w in step.ws.items():
-        assert w.error() == 0, nm
+    for nm, e in step.workspace_errors().items():
+        assert e == 0, nm
     _, y_ref = oracle.ffn_f64(x64, raw["gate"], raw["up"], raw["down"], residual=res)
     y = step.y.cpu().numpy().astype(np.float64)
     for t in range(s.rows):

@@ -486,9 +486,11 @@ def test_host_argument_errors_raise():
         ops.gemv("q6_k", w, x[:, 1:], 32, ws)        # misaligned activations
 
 
-def test_verify_step_pipeline_vs_oracle():
+@pytest.mark.parametrize("ffn_ctas", [None, 0, 20])
+def test_verify_step_pipeline_vs_oracle(ffn_ctas):
     # the graph-captured verify step (stage -> gate/up -> gact image -> down; stage ->
-    # head argmax + accept) at reduced width against the oracle
+    # head argmax + accept) at reduced width against the oracle: the FFN chain beside
+    # the head (default split, a small FFN budget) and all three GEMVs in sequence (0)
     from thunderllamax_b200.verify import VerifyShape, VerifyStep
 
     rng = np.random.default_rng(99)
@@ -497,7 +499,7 @@ def test_verify_step_pipeline_vs_oracle():
     rd, rh = synth.q6k_blocks(rng, s.dim, s.ffn), synth.q6k_blocks(rng, s.vocab, s.dim)
     w = {"gate": ops.pack_tiles("iq3_xxs", rg, s.dim), "up": ops.pack_tiles("iq3_xxs", ru, s.dim),
          "down": ops.pack_tiles("q6_k", rd, s.ffn), "head": ops.pack_tiles("q6_k", rh, s.dim)}
-    step = VerifyStep(s, weights=w)
+    step = VerifyStep(s, weights=w, ffn_ctas=ffn_ctas)
     x, x64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
     h, h64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
     res = rng.standard_normal((s.rows, s.dim), dtype=np.float32)
@@ -513,6 +515,7 @@ def test_verify_step_pipeline_vs_oracle():
     check_rows(step.y.cpu().numpy(), y_ref, tight=1e-4)
     assert np.array_equal(step.out_idx.cpu().numpy(), idx_ref)
     assert step.accept_out.cpu().tolist() == list(oracle.accept(idx_ref, drafts_np))
+    assert not any(step.workspace_errors().values())
 
 
 def test_verify_step_host_path_copies_every_call():

@@ -13,6 +13,15 @@ which is the reference's per-layer ffn8v11r7 -> down8nw32v11r7 pair
 activation-staging kernels and the three GEMVs; gate/up writes gact directly in
 the image format down reads), captured in a CUDA graph (the reference's
 pre-recorded ParityGraph, engine/gcycle.py:22-73).
+
+The FFN chain and the head read different inputs, so the step runs them side by
+side: the stream forks, the head runs on a side stream over `head_ctas` SMs while
+gate/up -> down run on the caller's stream over the other `ffn_ctas` SMs, and the
+streams join (event record / wait, which a graph capture turns into two parallel
+branches).  Each GEMV is bound by per-SM instruction throughput, so splitting the
+SMs costs nothing in total work, while each chain's launch ramp, first-copy
+latency and split-tile tail are hidden behind the other chain's streaming.
+`ffn_ctas=0` runs the three GEMVs one after another on all SMs.
 """
 from __future__ import annotations
 
@@ -80,8 +89,15 @@ def synth_tiled(qtype: str, n_rows: int, k: int, seed: int, rows: tuple[int, int
     return out
 
 
+def default_split_ctas(sms: int) -> int:
+    """CTAs of the FFN chain when it runs beside the head on one GPU (the head gets
+    the rest); 0 (serial) on parts too small to split."""
+    return 45 if sms >= 128 else 0
+
+
 class VerifyStep:
-    def __init__(self, shape: VerifyShape = VerifyShape(), seed: int = 0, weights: dict | None = None):
+    def __init__(self, shape: VerifyShape = VerifyShape(), seed: int = 0, weights: dict | None = None,
+                 ffn_ctas: int | None = None):
         ops.require_device()
         self.shape = s = shape
         self.w = weights if weights is not None else {
@@ -101,35 +117,75 @@ class VerifyStep:
         self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
         self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
         self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
+        # workspaces of the kernels alone on every SM (launch_<kernel>) ...
         self.ws = {
             "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, s.ffn, s.dim, s.rows),
             "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, s.ffn, s.rows, "image"),
             "head_argmax": ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, s.vocab, s.dim, s.rows),
         }
+        # ... and of the step's two chains side by side, each sized by its CTA budget
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        self.ffn_ctas = default_split_ctas(sms) if ffn_ctas is None else int(ffn_ctas)
+        if not 0 <= self.ffn_ctas < sms:
+            raise ValueError(f"ffn_ctas must be in [0, {sms}), not {self.ffn_ctas}")
+        self.head_ctas = sms - self.ffn_ctas if self.ffn_ctas else 0
+        self.side = None
+        self.ws_step = self.ws
+        if self.ffn_ctas:
+            with ops.cta_budget(self.ffn_ctas):
+                self.ws_step = {
+                    "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, s.ffn, s.dim, s.rows),
+                    "ffn_down": ops.Workspace.for_shape(ops.MODE_STORE, s.down_q, s.dim, s.ffn, s.rows, "image"),
+                }
+            with ops.cta_budget(self.head_ctas):
+                self.ws_step["head_argmax"] = ops.Workspace.for_shape(ops.MODE_ARGMAX, s.head_q, s.vocab, s.dim,
+                                                                      s.rows)
+            self.side = torch.cuda.Stream()
         self.graph = None
 
-    # ---- the three launches ----
-    def launch_ffn_gate_up(self):
+    # ---- the three launches (ws: which workspace set; the CTA budget is the caller's) ----
+    def launch_ffn_gate_up(self, ws=None):
         s = self.shape
-        ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, s.ffn, self.ws["ffn_gate_up"], gact=self.gact)
+        ws = self.ws if ws is None else ws
+        ops.ffn_gate_up(s.ffn_q, self.w["gate"], self.w["up"], self.x, s.ffn, ws["ffn_gate_up"], gact=self.gact)
 
-    def launch_ffn_down(self):
+    def launch_ffn_down(self, ws=None):
         s = self.shape
-        ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, self.ws["ffn_down"], y=self.y, residual=self.res)
+        ws = self.ws if ws is None else ws
+        ops.gemv(s.down_q, self.w["down"], self.gact, s.dim, ws["ffn_down"], y=self.y, residual=self.res)
 
-    def launch_head_argmax(self):
+    def launch_head_argmax(self, ws=None):
         s = self.shape
-        ops.head_argmax(s.head_q, self.w["head"], self.h, s.vocab, self.ws["head_argmax"], out_max=self.out_max,
+        ws = self.ws if ws is None else ws
+        ops.head_argmax(s.head_q, self.w["head"], self.h, s.vocab, ws["head_argmax"], out_max=self.out_max,
                         out_idx=self.out_idx, drafts=self.drafts, accept_out=self.accept_out)
 
     KERNELS = ("ffn_gate_up", "ffn_down", "head_argmax")
     # stage(X) + gate/up, down, stage(H) + head
     LAUNCHES_PER_STEP = 5
 
+    def workspace_errors(self) -> dict:
+        """Error words of every workspace the step and the kernels alone use."""
+        out = {f"{k}": w.error() for k, w in self.ws.items()}
+        if self.ws_step is not self.ws:
+            out.update({f"{k}_step": w.error() for k, w in self.ws_step.items()})
+        return out
+
     def launch(self):
-        self.launch_ffn_gate_up()
-        self.launch_ffn_down()
-        self.launch_head_argmax()
+        if not self.ffn_ctas:
+            self.launch_ffn_gate_up()
+            self.launch_ffn_down()
+            self.launch_head_argmax()
+            return
+        cur = torch.cuda.current_stream()
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            with ops.cta_budget(self.head_ctas):
+                self.launch_head_argmax(self.ws_step)
+        with ops.cta_budget(self.ffn_ctas):
+            self.launch_ffn_gate_up(self.ws_step)
+            self.launch_ffn_down(self.ws_step)
+        cur.wait_stream(self.side)
 
     def capture(self):
         """Record the step once as a CUDA graph (after a warm-up launch)."""
