@@ -115,16 +115,24 @@ def emulate_iq3(tiled, n_rows, k):
                     for rr in range(2):
                         idx = c[rr * 512 + lane * 16 + m]
                         G = int(grid[idx])
-                        v = int(sw[rr, cc])
-                        ms = 2 * (v >> 28) + 1
-                        t_ = v ^ (v >> 1)
-                        t_ ^= t_ >> 2
-                        t_ ^= t_ >> 4
-                        par = t_ ^ (v >> 7)
-                        s8 = ((v >> (7 * l)) & 0x7F) | (((par >> (7 * l)) & 1) << 7)
+                        u = int(sw[rr, cc])
+                        # formats.cuh iq3_word: parities of the four fields at once, the
+                        # scale gathered from bits 19 + 4j by one multiply
+                        y0 = u & 0x7777FFFF
+                        y = y0 ^ (y0 >> 16)
+                        y ^= y >> 2
+                        y ^= y >> 1
+                        sg = ((y << 19) & 0x88880000) | y0
+                        gsc = (((u >> 19) & 0x1111) * 0x12481248) & 0xFFFFFFFF
+                        ms = 2 * ((gsc >> 12) & 0xF) + 1
+                        assert ms == 2 * ((gsc >> 28) & 0xF) + 1
                         for j in range(4):
                             mag = (G >> (8 * j)) & 0xFF
-                            a = float(mag * ms) * (-1.0 if (s8 >> (4 * e + j)) & 1 else 1.0)
+                            i = 2 * e + (j >> 1)           # sign pair of the field
+                            # pair_signs: bit 15 (even weight) / 31 (odd weight) after one shift
+                            mask = (sg << (15 - 4 * l - i)) & 0x80008000
+                            neg = (mask >> (31 if j & 1 else 15)) & 1
+                            a = float(mag * ms) * (-1.0 if neg else 1.0)
                             row = t * 16 + g + 8 * rr
                             kk = b * 256 + 64 * q + 4 * m + j
                             W[row, kk] = (d16[g, rr] * np.float32(0.25)) * np.float32(a)

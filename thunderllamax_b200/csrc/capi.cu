@@ -431,7 +431,10 @@ int tlx_unpack_tiles(int qtype, const void* tiled, int64_t n_rows, int64_t k, vo
           for (int cc = 0; cc < 2; ++cc) {
             const int ib = 2 * q + cc;
             for (int j = 0; j < 8; ++j) blk[2 + 8 * ib + j] = c[rr * 512 + lane * 16 + cc * 8 + j];
-            for (int j = 0; j < 4; ++j) blk[66 + 4 * ib + j] = c[1024 + lane * 16 + (rr * 2 + cc) * 4 + j];
+            uint32_t u = 0;
+            for (int j = 0; j < 4; ++j) u |= static_cast<uint32_t>(c[1024 + lane * 16 + (rr * 2 + cc) * 4 + j]) << (8 * j);
+            const uint32_t v = iq3_sign_word_inverse(u);
+            for (int j = 0; j < 4; ++j) blk[66 + 4 * ib + j] = static_cast<uint8_t>(v >> (8 * j));
           }
         }
       } else {

@@ -113,6 +113,31 @@ TLX_HD inline void pack_q6_lane(const uint8_t* const rows[16], int lane, uint8_t
     }
 }
 
+// IQ3_XXS sign / scale word of one 32-weight sub-block, stored in pair order.  GGUF
+// holds four 7-bit sign fields (field l: the signs of weights 8l .. 8l+6 of the
+// sub-block; weight 8l+7 takes the field's parity) and the 4-bit scale at bits
+// 28..31.  The tile word puts the even-weight sign of pair i (weights 8l+2i, 8l+2i+1)
+// of field l at bit 4l + i and the odd-weight sign at bit 16 + 4l + i, so the fp16x2
+// sign mask of a pair is ONE shift, (w << (15 - 4l - i)) & 0x80008000, and the four
+// parities are computed for all fields at once.  The odd sign of pair 3 (the parity)
+// is not stored: its slots 19 + 4j hold scale bit j.  32 bits, as in GGUF.
+TLX_HD inline uint32_t iq3_sign_word(uint32_t v) {
+  uint32_t u = 0;
+  for (int l = 0; l < 4; ++l)
+    for (int b = 0; b < 7; ++b)
+      u |= ((v >> (7 * l + b)) & 1u) << ((b & 1) ? 16 + 4 * l + (b >> 1) : 4 * l + (b >> 1));
+  for (int j = 0; j < 4; ++j) u |= ((v >> (28 + j)) & 1u) << (19 + 4 * j);
+  return u;
+}
+TLX_HD inline uint32_t iq3_sign_word_inverse(uint32_t u) {
+  uint32_t v = 0;
+  for (int l = 0; l < 4; ++l)
+    for (int b = 0; b < 7; ++b)
+      v |= ((u >> ((b & 1) ? 16 + 4 * l + (b >> 1) : 4 * l + (b >> 1))) & 1u) << (7 * l + b);
+  for (int j = 0; j < 4; ++j) v |= ((u >> (19 + 4 * j)) & 1u) << (28 + j);
+  return v;
+}
+
 // IQ3_XXS chunk (GGUF block order d | qs[64] | scales[32]), the part owned by one lane
 TLX_HD inline void pack_iq3_lane(const uint8_t* const rows[16], int lane, uint8_t* out) {
   const int g = lane >> 2, q = lane & 3;
@@ -121,7 +146,11 @@ TLX_HD inline void pack_iq3_lane(const uint8_t* const rows[16], int lane, uint8_
     for (int c = 0; c < 2; ++c) {
       const int ib = 2 * q + c;
       for (int j = 0; j < 8; ++j) out[rr * 512 + lane * 16 + c * 8 + j] = blk ? blk[2 + 8 * ib + j] : 0;
-      for (int j = 0; j < 4; ++j) out[1024 + lane * 16 + (rr * 2 + c) * 4 + j] = blk ? blk[66 + 4 * ib + j] : 0;
+      uint32_t v = 0;
+      if (blk)
+        for (int j = 0; j < 4; ++j) v |= static_cast<uint32_t>(blk[66 + 4 * ib + j]) << (8 * j);
+      const uint32_t u = iq3_sign_word(v);
+      for (int j = 0; j < 4; ++j) out[1024 + lane * 16 + (rr * 2 + c) * 4 + j] = static_cast<uint8_t>(u >> (8 * j));
     }
   }
   if (q == 0)
@@ -249,6 +278,26 @@ constexpr uint32_t kMinus1536 = 0xE600E600u;  // fp16x2 (-1536, -1536) = -(1024 
 constexpr uint32_t kMinus1152 = 0xE480E480u;  // fp16x2 (-1152, -1152) = -(1024 + 128)
 constexpr uint32_t kMinus1024 = 0xE400E400u;  // fp16x2 (-1024, -1024)
 constexpr uint32_t kSixteenth = 0x2C002C00u;  // fp16x2 (1/16, 1/16)
+constexpr uint32_t kMinus72 = 0xD480D480u;    // fp16x2 (-72, -72)
+
+// One-LOP3 bit assembly.  LOP3 takes a single immediate, so `(w & MASK) | 0x64006400`
+// with both constants compiled in costs two LOP3 per decoded register (measured: 147
+// against 83 LOP3 per Q6_K chunk).  The decoders therefore take the fp16 magic
+// 0x64006400 as a run-time register value (`magic`, loaded from the kernel
+// parameters, so the compiler can neither fold it nor split the operation) and
+// assemble each register with one lop3.b32.
+template <uint32_t M>
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t c) {   // (a & M) | c
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(M), "r"(c));
+  return d;
+}
+template <uint32_t M>
+__device__ __forceinline__ uint32_t xor_or(uint32_t a, uint32_t c) {   // (a ^ M) | c
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xBE;" : "=r"(d) : "r"(a), "n"(M), "r"(c));
+  return d;
+}
 
 // Q6_K: per-block lane state.  Every 6-bit field is decoded at mantissa offset 4 of
 // an fp16 half (value 1024 + 16q) and turned into (q - 32) * sc by ONE fma:
@@ -266,16 +315,17 @@ constexpr uint32_t kMinus96 = 0xD600D600u;  // fp16x2 (-96, -96)
 
 // the lane's biased sub-scale bytes -> fp16x2 (sc/16) and (-96 sc) per sub-block / row
 __device__ __forceinline__ void q6_scales(const uint2 sc, Q6Lane& s) {
-  // biased byte b = sc + 128 -> fp16 1024 + b -> minus 1152 = sc (exact)
+  // biased byte b = sc + 128 -> fp16 1024 + b
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t word = j < 2 ? sc.x : sc.y;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const uint32_t bsel = 2u * (j & 1) + r;
-      const uint32_t sc2 = hadd2_u(prmt(word, 0x64646464u, 0x4040u | (bsel << 8) | bsel), kMinus1152);
-      s.s16[j][r] = hmul2_u(sc2, kSixteenth);
-      s.c96[j][r] = hmul2_u(sc2, kMinus96);
+      // (1024 + b) / 16 - 72 = (b - 128) / 16 = sc / 16, then sc / 16 * -1536 = -96 sc:
+      // every intermediate is exact in fp16
+      s.s16[j][r] = hfma2_u(prmt(word, 0x64646464u, 0x4040u | (bsel << 8) | bsel), kSixteenth, kMinus72);
+      s.c96[j][r] = hmul2_u(s.s16[j][r], kMinus1536);
     }
   }
 }
@@ -297,19 +347,20 @@ __device__ __forceinline__ void q6_load(const uint8_t* chunk, int lane, Q6Lane& 
 // at bits 4-9 (in place), field B at bits 10-15 (moved down by 6) and spare bits
 // 0-3; the split pairs P6/P7 join a low nibble from the spare bits of W0/W1 with
 // two high bits from the spare bits of W2.
-__device__ __forceinline__ void q6_group(const Q6Lane& s, int gam, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+__device__ __forceinline__ void q6_group(const Q6Lane& s, int gam, uint32_t magic, uint32_t (&a0)[4],
+                                         uint32_t (&a1)[4]) {
   const uint32_t W0 = s.w[3 * gam], W1 = s.w[3 * gam + 1], W2 = s.w[3 * gam + 2];
   const int j = gam >> 1;
   const uint32_t sg = s.s16[j][0], sg8 = s.s16[j][1];
   const uint32_t cg = s.c96[j][0], cg8 = s.c96[j][1];
-  const uint32_t p0 = (W0 & 0x03F003F0u) | kMagic;
-  const uint32_t p1 = ((W0 >> 6) & 0x03F003F0u) | kMagic;
-  const uint32_t p2 = (W1 & 0x03F003F0u) | kMagic;
-  const uint32_t p3 = ((W1 >> 6) & 0x03F003F0u) | kMagic;
-  const uint32_t p4 = (W2 & 0x03F003F0u) | kMagic;
-  const uint32_t p5 = ((W2 >> 6) & 0x03F003F0u) | kMagic;
-  const uint32_t p6 = ((W0 << 4) & 0x00F000F0u) | (((W2 << 8) & 0x03000300u) | kMagic);
-  const uint32_t p7 = ((W1 << 4) & 0x00F000F0u) | (((W2 << 6) & 0x03000300u) | kMagic);
+  const uint32_t p0 = and_or<0x03F003F0u>(W0, magic);
+  const uint32_t p1 = and_or<0x03F003F0u>(W0 >> 6, magic);
+  const uint32_t p2 = and_or<0x03F003F0u>(W1, magic);
+  const uint32_t p3 = and_or<0x03F003F0u>(W1 >> 6, magic);
+  const uint32_t p4 = and_or<0x03F003F0u>(W2, magic);
+  const uint32_t p5 = and_or<0x03F003F0u>(W2 >> 6, magic);
+  const uint32_t p6 = and_or<0x00F000F0u>(W0 << 4, and_or<0x03000300u>(W2 << 8, magic));
+  const uint32_t p7 = and_or<0x00F000F0u>(W1 << 4, and_or<0x03000300u>(W2 << 6, magic));
   a0[0] = hfma2_u(p0, sg, cg);
   a0[1] = hfma2_u(p1, sg8, cg8);
   a0[2] = hfma2_u(p2, sg, cg);
@@ -341,43 +392,51 @@ __device__ __forceinline__ uint2 grid_pair_entry(uint32_t g) {
 // IQ3_XXS: per-block lane state
 struct Iq3Lane {
   uint4 qs0, qs1;      // grid indices: row g / row g+8, groups 2q (bytes 0..7) and 2q+1 (8..15)
-  uint32_t sw[2][2];   // scale/sign words [row][group]
+  uint32_t sg[2][2];   // sign words [row][group] in pair order, parities filled in
   uint32_t m2[2][2];   // fp16x2 (2s+1)
-  uint32_t par[2][2];  // parity of sign field l at bit 7l
   uint32_t d;
 };
 
-// the lane's scale/sign words -> (2s+1) fp16x2 and sign-field parities
-__device__ __forceinline__ void iq3_words(const uint4 sw, Iq3Lane& s) {
-  s.sw[0][0] = sw.x;
-  s.sw[0][1] = sw.y;
-  s.sw[1][0] = sw.z;
-  s.sw[1][1] = sw.w;
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint32_t v = s.sw[r][c];
-      const uint32_t mm = ((v >> 28) << 1) | 1u;  // 2s+1
-      s.m2[r][c] = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
-      uint32_t t = v ^ (v >> 1);
-      t ^= t >> 2;
-      t ^= t >> 4;                 // bit i = xor of bits i..i+7
-      s.par[r][c] = t ^ (v >> 7);  // bit 7l = parity of field l
-    }
+constexpr uint32_t kTwo = 0x40004000u;          // fp16x2 (2, 2)
+constexpr uint32_t kMinus2047 = 0xE7FFE7FFu;    // fp16x2 (-2047, -2047)
+
+// one stored sign / scale word (iq3_sign_word) -> the full sign word and fp16x2 (2s+1)
+__device__ __forceinline__ void iq3_word(uint32_t u, uint32_t magic, uint32_t& sg, uint32_t& m2) {
+  // parity of field l = xor of its 7 stored bits (4l..4l+3, 16+4l..18+4l), at bit 4l
+  const uint32_t y0 = u & 0x7777FFFFu;
+  uint32_t y = y0 ^ (y0 >> 16);
+  y ^= y >> 2;
+  y ^= y >> 1;
+  sg = and_or<0x88880000u>(y << 19, y0);
+  // scale bits at 19 + 4j -> s at bits 12..15 and 28..31 (one multiply gathers them;
+  // every partial product lands on a bit of its own) -> fp16 1024 + s -> 2 (1024 + s) - 2047
+  const uint32_t gsc = ((u >> 19) & 0x1111u) * 0x12481248u;
+  m2 = hfma2_u(and_or<0x000F000Fu>(gsc >> 12, magic), kTwo, kMinus2047);
 }
 
-__device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, Iq3Lane& s) {
+// the lane's four stored words [row][group]
+__device__ __forceinline__ void iq3_words(const uint4 sw, uint32_t magic, Iq3Lane& s) {
+  iq3_word(sw.x, magic, s.sg[0][0], s.m2[0][0]);
+  iq3_word(sw.y, magic, s.sg[0][1], s.m2[0][1]);
+  iq3_word(sw.z, magic, s.sg[1][0], s.m2[1][0]);
+  iq3_word(sw.w, magic, s.sg[1][1], s.m2[1][1]);
+}
+
+__device__ __forceinline__ void iq3_load(const uint8_t* chunk, int lane, uint32_t magic, Iq3Lane& s) {
   s.qs0 = *reinterpret_cast<const uint4*>(chunk + lane * 16);
   s.qs1 = *reinterpret_cast<const uint4*>(chunk + 512 + lane * 16);
-  iq3_words(*reinterpret_cast<const uint4*>(chunk + 1024 + lane * 16), s);
+  iq3_words(*reinterpret_cast<const uint4*>(chunk + 1024 + lane * 16), magic, s);
   s.d = *reinterpret_cast<const uint32_t*>(chunk + 1536 + (lane >> 2) * 4);
 }
 
-// sign masks for sign pair i (s8 bits 2i, 2i+1) -> fp16x2 sign bits 15 / 31
-__device__ __forceinline__ uint32_t sign_mask(uint32_t s8, int i) {
-  const uint32_t mul = (1u << (15 - 2 * i)) + (1u << (30 - 2 * i));
-  return (s8 * mul) & 0x80008000u;
+// fp16x2 sign mask of pair i (0..3) of field l from a sign word in pair order
+__device__ __forceinline__ uint32_t pair_signs(uint32_t sg, int l, int i) {
+  return (sg << (15 - 4 * l - i)) & 0x80008000u;
+}
+
+// grid entry address: byte k of a qs word picked by one PRMT, then idx * 128 + base
+__device__ __forceinline__ const uint8_t* grid_entry(const uint8_t* grid_lane, uint32_t word, int k) {
+  return grid_lane + prmt(word, 0u, 0x4440u | static_cast<uint32_t>(k)) * (kGridCopies * 8u);
 }
 
 // decode mma m (0..15) for both rows; grid_lane = table base + (lane % 16) * 8 bytes
@@ -387,12 +446,9 @@ __device__ __forceinline__ void iq3_mma(const Iq3Lane& s, const uint8_t* grid_la
   for (int r = 0; r < 2; ++r) {
     const uint4 qs = r == 0 ? s.qs0 : s.qs1;
     const uint32_t word = (m >> 2) == 0 ? qs.x : (m >> 2) == 1 ? qs.y : (m >> 2) == 2 ? qs.z : qs.w;
-    const uint32_t idx = (word >> (8 * (m & 3))) & 0xFFu;
-    const uint2 G = *reinterpret_cast<const uint2*>(grid_lane + idx * (kGridCopies * 8u));
-    const uint32_t v = s.sw[r][c];
-    const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | ((s.par[r][c] >> (7 * l)) << 7 & 0x80u);
-    a[r] = hmul2_u(G.x, s.m2[r][c]) ^ sign_mask(s8, 2 * e);
-    a[r + 2] = hmul2_u(G.y, s.m2[r][c]) ^ sign_mask(s8, 2 * e + 1);
+    const uint2 G = *reinterpret_cast<const uint2*>(grid_entry(grid_lane, word, m & 3));
+    a[r] = hmul2_u(G.x, s.m2[r][c]) ^ pair_signs(s.sg[r][c], l, 2 * e);
+    a[r + 2] = hmul2_u(G.y, s.m2[r][c]) ^ pair_signs(s.sg[r][c], l, 2 * e + 1);
   }
 }
 
@@ -474,31 +530,31 @@ __device__ __forceinline__ void q4_load(const uint8_t* chunk, int lane, Q4Lane& 
 // fifth bit h above the nibble: 1024 + v + 16h (low) resp. 1024 + 16(v + 16h)
 // (high), still exact fp16 integers below 2048, so the same fma constants apply.
 template <bool Q5 = false>
-__device__ __forceinline__ void q4_mma(const Q4Lane& s, int m, uint32_t (&a)[4]) {
+__device__ __forceinline__ void q4_mma(const Q4Lane& s, int m, uint32_t magic, uint32_t (&a)[4]) {
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const uint32_t w = s.w[rr][m & 7];
     const uint32_t p01 = prmt(w, 0u, 0x4140u);  // bytes 0, 1 -> low bytes of the halves
     const uint32_t p23 = prmt(w, 0u, 0x4342u);
-    uint32_t h01 = 0u, h23 = 0u;
+    uint32_t h01 = magic, h23 = magic;   // the fifth bits (Q5_K) with the fp16 magic
     if constexpr (Q5) {
       const int i = m & 7;
       const uint32_t word = i < 4 ? s.h[rr].x : s.h[rr].y;
       const uint32_t x = ((word >> (8 * (i & 3))) & 0xFFu) * 0x00100001u;  // byte at bits 0..7 and 20..27
       if (m < 8) {
-        h01 = x & 0x00100010u;          // bit 4 <- lo(0), bit 20 <- lo(1)
-        h23 = (x >> 1) & 0x00100010u;   // bit 4 <- lo(2), bit 20 <- lo(3)
+        h01 = and_or<0x00100010u>(x, magic);        // bit 4 <- lo(0), bit 20 <- lo(1)
+        h23 = and_or<0x00100010u>(x >> 1, magic);   // bit 4 <- lo(2), bit 20 <- lo(3)
       } else {
-        h01 = (x << 2) & 0x01000100u;   // bit 8 <- hi(0), bit 24 <- hi(1)
-        h23 = (x << 1) & 0x01000100u;   // bit 8 <- hi(2), bit 24 <- hi(3)
+        h01 = and_or<0x01000100u>(x << 2, magic);   // bit 8 <- hi(0), bit 24 <- hi(1)
+        h23 = and_or<0x01000100u>(x << 1, magic);   // bit 8 <- hi(2), bit 24 <- hi(3)
       }
     }
     if (m < 8) {
-      a[rr] = hfma2_u((p01 & 0x000F000Fu) | h01 | kMagic, s.slo[rr], s.clo[rr]);
-      a[rr + 2] = hfma2_u((p23 & 0x000F000Fu) | h23 | kMagic, s.slo[rr], s.clo[rr]);
+      a[rr] = hfma2_u(and_or<0x000F000Fu>(p01, h01), s.slo[rr], s.clo[rr]);
+      a[rr + 2] = hfma2_u(and_or<0x000F000Fu>(p23, h23), s.slo[rr], s.clo[rr]);
     } else {
-      a[rr] = hfma2_u((p01 & 0x00F000F0u) | h01 | kMagic, s.shi[rr], s.chi[rr]);
-      a[rr + 2] = hfma2_u((p23 & 0x00F000F0u) | h23 | kMagic, s.shi[rr], s.chi[rr]);
+      a[rr] = hfma2_u(and_or<0x00F000F0u>(p01, h01), s.shi[rr], s.chi[rr]);
+      a[rr + 2] = hfma2_u(and_or<0x00F000F0u>(p23, h23), s.shi[rr], s.chi[rr]);
     }
   }
 }
@@ -525,13 +581,13 @@ __device__ __forceinline__ void q8_load(const uint8_t* chunk, int lane, Q8Lane& 
 }
 
 // decode mma m (0..15): k = 64q + 4m + {0..3}, block 2q + (m >> 3)
-__device__ __forceinline__ void q8_mma(const Q8Lane& s, int m, uint32_t (&a)[4]) {
+__device__ __forceinline__ void q8_mma(const Q8Lane& s, int m, uint32_t magic, uint32_t (&a)[4]) {
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const uint4 u = s.u[rr][m >> 2];
     const uint32_t w = (m & 3) == 0 ? u.x : (m & 3) == 1 ? u.y : (m & 3) == 2 ? u.z : u.w;
-    const uint32_t p01 = (prmt(w, 0u, 0x4140u) ^ 0x00800080u) | kMagic;   // 1024 + q + 128
-    const uint32_t p23 = (prmt(w, 0u, 0x4342u) ^ 0x00800080u) | kMagic;
+    const uint32_t p01 = xor_or<0x00800080u>(prmt(w, 0u, 0x4140u), magic);   // 1024 + q + 128
+    const uint32_t p23 = xor_or<0x00800080u>(prmt(w, 0u, 0x4342u), magic);
     const uint32_t dd = s.d[rr][m >> 3];
     a[rr] = hmul2_u(hadd2_u(p01, kMinus1152), dd);
     a[rr + 2] = hmul2_u(hadd2_u(p23, kMinus1152), dd);

@@ -136,6 +136,7 @@ struct GemvParams {
   uint32_t* done_cnt;
   uint32_t* err;
   PeerParams peer;           // world <= 1: no exchange
+  uint32_t fp16_magic;       // 0x64006400, passed at run time (and_or in formats.cuh)
 };
 
 __host__ __device__ constexpr bool needs_sums(int qt) { return qt == QT_Q4_K || qt == QT_Q5_K; }
@@ -281,14 +282,14 @@ struct LaneData<QT_Q8_0, NMAT> {
 };
 
 template <int QT, int NMAT>
-__device__ __forceinline__ void load_lane(const uint8_t* stage, int lane, LaneData<QT, NMAT>& L) {
+__device__ __forceinline__ void load_lane(const uint8_t* stage, int lane, uint32_t magic, LaneData<QT, NMAT>& L) {
   constexpr uint32_t CH = chunk_bytes(QT);
   if constexpr (QT == QT_Q6_K) {
 #pragma unroll
     for (int a = 0; a < NMAT; ++a) q6_load(stage + a * CH, lane, L.s[a]);
   } else if constexpr (QT == QT_IQ3_XXS) {
 #pragma unroll
-    for (int a = 0; a < NMAT; ++a) iq3_load(stage + a * CH, lane, L.s[a]);
+    for (int a = 0; a < NMAT; ++a) iq3_load(stage + a * CH, lane, magic, L.s[a]);
   } else if constexpr (QT == QT_Q8_0) {
     static_assert(NMAT == 1, "Q8_0 is read by the STORE epilogue only");
     q8_load(stage, lane, L.s);
@@ -315,7 +316,7 @@ __device__ __forceinline__ void load_b_pair(const uint32_t (&xE)[NT], const uint
 template <int QT, int NT, int NMAT>
 __device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const uint32_t (&xE)[NT],
                                              const uint32_t (&xO)[NT], const uint32_t (&xsum)[NT],
-                                             const uint8_t* grid_lane, float (&acc)[NMAT][NT][4]) {
+                                             const uint8_t* grid_lane, uint32_t magic, float (&acc)[NMAT][NT][4]) {
   float tmp[NMAT][NT][4];
 #pragma unroll
   for (int a = 0; a < NMAT; ++a)
@@ -331,7 +332,7 @@ __device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const 
 #pragma unroll
       for (int a = 0; a < NMAT; ++a) {
         uint32_t a0[4], a1[4];
-        q6_group(L.s[a], j, a0, a1);
+        q6_group(L.s[a], j, magic, a0, a1);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma16816(tmp[a][nt], a0, b[nt].x, b[nt].y);
@@ -387,7 +388,7 @@ __device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t af[4];
-        q8_mma(L.s, 2 * j + h, af);
+        q8_mma(L.s, 2 * j + h, magic, af);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816(acc[0][nt], af, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
       }
@@ -402,7 +403,7 @@ __device__ __forceinline__ void compute_lane(const LaneData<QT, NMAT>& L, const 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t af[4];
-        q4_mma<Q5>(L.s, 2 * j + h, af);
+        q4_mma<Q5>(L.s, 2 * j + h, magic, af);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816(tmp[0][nt], af, h ? b[nt].z : b[nt].x, h ? b[nt].w : b[nt].y);
       }
@@ -675,6 +676,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   const uint32_t sblk_stride = static_cast<uint32_t>(p.MC) * kSumRowBytes;
   const uint8_t* grid_lane = reinterpret_cast<const uint8_t*>(grid_rep) + (lane % kGridCopies) * 8;
 
+  const uint32_t magic = p.fp16_magic;
   uint64_t best[2 * NT];
 #pragma unroll
   for (int i = 0; i < 2 * NT; ++i) best[i] = 0ull;
@@ -704,7 +706,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
         break;
       }
       LaneData<QT, NMAT> Ld;
-      load_lane<QT, NMAT>(ring + slot * STAGE_BYTES, lane, Ld);
+      load_lane<QT, NMAT>(ring + slot * STAGE_BYTES, lane, magic, Ld);
       // every lane's reads of the stage are ordered before the refill (warp barrier,
       // then the generic -> async proxy fence of the issuing lane)
       __syncwarp();
@@ -716,7 +718,7 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
         slot = 0;
         phase ^= 1u;
       }
-      compute_lane<QT, NT, NMAT>(Ld, bE, bO, bS, grid_lane, acc);
+      compute_lane<QT, NT, NMAT>(Ld, bE, bO, bS, grid_lane, magic, acc);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         bE[nt] += blk_stride;
@@ -1245,6 +1247,7 @@ int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* gr
   gp.drafts = drafts;
   gp.n_drafts = n_drafts;
   gp.accept_out = accept_out;
+  gp.fp16_magic = kMagic;
   gp.err = reinterpret_cast<uint32_t*>(wsb);
   gp.done_cnt = reinterpret_cast<uint32_t*>(wsb + 4);
   gp.tile_cnt = reinterpret_cast<uint32_t*>(wsb + P.off_cnt);

@@ -174,19 +174,10 @@ __device__ __forceinline__ void store_rows(uint8_t* adst, int r0, int r1, int c,
 
 // IQ3_XXS, group p: mma steps 8p .. 8p+7 (the decode of iq3_mma restricted to one group)
 __device__ __forceinline__ void dequant_iq3_part(const Iq3Part& r, int part, const uint8_t* grid_lane, uint8_t* adst,
-                                                 int r0, int r1) {
-  uint32_t m2[2], par[2];
-  const uint32_t sw[2] = {r.sw0, r.sw1};
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const uint32_t v = sw[rr];
-    const uint32_t mm = ((v >> 28) << 1) | 1u;
-    m2[rr] = hadd2_u((mm * 0x00010001u) | kMagic, kMinus1024);
-    uint32_t t = v ^ (v >> 1);
-    t ^= t >> 2;
-    t ^= t >> 4;
-    par[rr] = t ^ (v >> 7);
-  }
+                                                 int r0, int r1, uint32_t magic) {
+  uint32_t sg[2], m2[2];
+  iq3_word(r.sw0, magic, sg[0], m2[0]);
+  iq3_word(r.sw1, magic, sg[1], m2[1]);
   const __half2 dh = *reinterpret_cast<const __half2*>(&r.d);
   const float2 df = __half22float2(dh);
   const uint32_t s0 = h2_bits(__float2half2_rn(df.x * 0.25f)), s1 = h2_bits(__float2half2_rn(df.y * 0.25f));
@@ -196,12 +187,9 @@ __device__ __forceinline__ void dequant_iq3_part(const Iq3Part& r, int part, con
     for (int rr = 0; rr < 2; ++rr) {
       const uint2 q = rr == 0 ? r.q0 : r.q1;
       const uint32_t word = ml < 4 ? q.x : q.y;
-      const uint32_t idx = (word >> (8 * (ml & 3))) & 0xFFu;
-      const uint2 G = *reinterpret_cast<const uint2*>(grid_lane + idx * (kGridCopies * 8u));
-      const uint32_t v = sw[rr];
-      const uint32_t s8 = ((v >> (7 * l)) & 0x7Fu) | ((par[rr] >> (7 * l)) << 7 & 0x80u);
-      a[rr] = hmul2_u(G.x, m2[rr]) ^ sign_mask(s8, 2 * e);
-      a[rr + 2] = hmul2_u(G.y, m2[rr]) ^ sign_mask(s8, 2 * e + 1);
+      const uint2 G = *reinterpret_cast<const uint2*>(grid_entry(grid_lane, word, ml & 3));
+      a[rr] = hmul2_u(G.x, m2[rr]) ^ pair_signs(sg[rr], l, 2 * e);
+      a[rr + 2] = hmul2_u(G.y, m2[rr]) ^ pair_signs(sg[rr], l, 2 * e + 1);
     }
   };
 #pragma unroll
@@ -214,7 +202,8 @@ __device__ __forceinline__ void dequant_iq3_part(const Iq3Part& r, int part, con
 }
 
 // Q6_K, sub-block j: groups 2j and 2j+1 (q6_group restricted to one sub-block)
-__device__ __forceinline__ void dequant_q6_part(const Q6Part& r, int part, uint8_t* adst, int r0, int r1) {
+__device__ __forceinline__ void dequant_q6_part(const Q6Part& r, int part, uint8_t* adst, int r0, int r1,
+                                                uint32_t magic) {
   uint32_t w[6];
   if (part & 1) {
     w[0] = r.ua.z; w[1] = r.ua.w; w[2] = r.ub.x; w[3] = r.ub.y; w[4] = r.ub.z; w[5] = r.ub.w;
@@ -224,9 +213,8 @@ __device__ __forceinline__ void dequant_q6_part(const Q6Part& r, int part, uint8
   uint32_t sg[2], cg[2];
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
-    const uint32_t sc2 = hadd2_u(prmt(r.sc, 0x64646464u, 0x4040u | (rr << 8) | rr), kMinus1152);
-    sg[rr] = hmul2_u(sc2, kSixteenth);
-    cg[rr] = hmul2_u(sc2, kMinus96);
+    sg[rr] = hfma2_u(prmt(r.sc, 0x64646464u, 0x4040u | (rr << 8) | rr), kSixteenth, kMinus72);  // sc / 16
+    cg[rr] = hmul2_u(sg[rr], kMinus1536);                                                       // -96 sc
   }
   const __half2 dh = *reinterpret_cast<const __half2*>(&r.d);
   const float2 df = __half22float2(dh);
@@ -234,14 +222,14 @@ __device__ __forceinline__ void dequant_q6_part(const Q6Part& r, int part, uint8
 #pragma unroll
   for (int gg = 0; gg < 2; ++gg) {
     const uint32_t W0 = w[3 * gg], W1 = w[3 * gg + 1], W2 = w[3 * gg + 2];
-    const uint32_t p0 = (W0 & 0x03F003F0u) | kMagic;
-    const uint32_t p1 = ((W0 >> 6) & 0x03F003F0u) | kMagic;
-    const uint32_t p2 = (W1 & 0x03F003F0u) | kMagic;
-    const uint32_t p3 = ((W1 >> 6) & 0x03F003F0u) | kMagic;
-    const uint32_t p4 = (W2 & 0x03F003F0u) | kMagic;
-    const uint32_t p5 = ((W2 >> 6) & 0x03F003F0u) | kMagic;
-    const uint32_t p6 = ((W0 << 4) & 0x00F000F0u) | (((W2 << 8) & 0x03000300u) | kMagic);
-    const uint32_t p7 = ((W1 << 4) & 0x00F000F0u) | (((W2 << 6) & 0x03000300u) | kMagic);
+    const uint32_t p0 = and_or<0x03F003F0u>(W0, magic);
+    const uint32_t p1 = and_or<0x03F003F0u>(W0 >> 6, magic);
+    const uint32_t p2 = and_or<0x03F003F0u>(W1, magic);
+    const uint32_t p3 = and_or<0x03F003F0u>(W1 >> 6, magic);
+    const uint32_t p4 = and_or<0x03F003F0u>(W2, magic);
+    const uint32_t p5 = and_or<0x03F003F0u>(W2 >> 6, magic);
+    const uint32_t p6 = and_or<0x00F000F0u>(W0 << 4, and_or<0x03000300u>(W2 << 8, magic));
+    const uint32_t p7 = and_or<0x00F000F0u>(W1 << 4, and_or<0x03000300u>(W2 << 6, magic));
     uint32_t a[4], b[4];
     a[0] = hfma2_u(p0, sg[0], cg[0]);
     a[1] = hfma2_u(p1, sg[1], cg[1]);
@@ -264,6 +252,7 @@ struct PrefillParams {
   int64_t ldo;
   const float* row_scale;  // per-token power-of-two scale of the staged tokens (nullptr: 1)
   uint32_t* err;
+  uint32_t fp16_magic;  // 0x64006400, passed at run time (and_or in formats.cuh)
   // work list: n_full whole tiles, then the last split_r tiles (the ones that would
   // leave most SMs idle in a final partial wave) as `pieces` k-ranges each; the
   // pieces write fp32 partial accumulators and the last one to finish sums them in
@@ -643,8 +632,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const int s = static_cast<int>(kt_global % S);
       if (!wait_bounded(&empty[s], ((kt_global / S) & 1) ^ 1)) return false;
       uint8_t* adst = smem + L::kStagesOff + s * L::kStage + mat * kPfRows * 128;
-      if constexpr (QT == QT_IQ3_XXS) dequant_iq3_part(use, part, grid_lane, adst, r0, r1);
-      else dequant_q6_part(use, part, adst, r0, r1);
+      if constexpr (QT == QT_IQ3_XXS) dequant_iq3_part(use, part, grid_lane, adst, r0, r1, p.fp16_magic);
+      else dequant_q6_part(use, part, adst, r0, r1, p.fp16_magic);
       // generic-proxy writes -> visible to the tensor core (async proxy)
       fence_proxy_async_smem();
       __syncwarp();
@@ -900,6 +889,7 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   p.ldo = ldo;
   p.row_scale = row_scale;
   p.err = err;
+  p.fp16_magic = kMagic;
   // the split region follows the token staging (present in a workspace sized by
   // tlx_prefill_workspace_bytes; a smaller one runs without splitting)
   uint8_t* split_ws = nullptr;
