@@ -205,14 +205,15 @@ int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, 
  * replaces NCCL's all-reduce of the down partials and all-gather of the head keys (the
  * collectives of the row / k / vocabulary split):
  *   tlx_gemv_peer         the down projection shard (k split): its fp32 partial y goes
- *                         straight into every rank's buffer with ordinary stores over
- *                         NVLink, and its last CTA raises this rank's flag there;
- *   tlx_head_argmax_peer  the vocabulary shard of the fused head; its last CTA sends
- *                         the 11 argmax keys to every rank, merges all ranks' keys and
- *                         runs greedy accept (the same result on every rank);
+ *                         into this rank's own buffer, and its last CTA raises this
+ *                         rank's flag in every rank's buffer (one release store each);
+ *   tlx_head_argmax_peer  the vocabulary shard of the fused head; its last CTA puts the
+ *                         11 argmax keys into this rank's buffer, raises its flag in
+ *                         every rank's buffer, reads all ranks' keys over NVLink, merges
+ *                         them and runs greedy accept (the same result on every rank);
  *   tlx_peer_finish       after both, on the same stream: y = residual + the ranks'
- *                         partials in rank order (the same bits on every rank), and the
- *                         step counter advances.
+ *                         partials read from their buffers over NVLink, in rank order
+ *                         (the same bits on every rank), and the step counter advances.
  * The FFN (gate/up, tlx_gemv_peer) and the head are independent and may run on two
  * streams at once with split CTA budgets (max_ctas > 0 caps a launch's grid; 0 = the
  * tlx_set_max_ctas setting); tlx_peer_finish must follow both.  Waits are only on other

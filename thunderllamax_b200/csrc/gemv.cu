@@ -65,23 +65,27 @@ __host__ __device__ __forceinline__ int64_t sums_index(int64_t b, int col, int q
 
 // ---- peer exchange of the sharded verify step (one process per GPU, world > 1) ----
 // Every rank owns one buffer of peer_buffer_bytes(world, m, ny); base[r] is rank r's
-// buffer as mapped in this process.  Layout (bytes):
+// buffer as mapped in this process.  A rank writes its results into its OWN buffer
+// with ordinary stores and announces them with one release flag per kernel in every
+// rank's buffer; the consumers then read the peers' buffers over NVLink (pull).  Only
+// the flags cross NVLink as stores, so no system-scope fence waits behind a stream of
+// remote stores.  Layout (bytes):
 //   0     epoch: steps completed on this rank (local)
 //   64    arrival counter of the down kernel's CTAs (local)
 //   128   arrival counter of the finish kernel's CTAs (local)
 //   256   down flags [2][kMaxPeers], 16 bytes apart: rank r's partial y of the step
-//         with parity p is complete in this buffer once flag [p][r] == epoch + 1
+//         with parity p is complete in rank r's buffer once flag [p][r] == epoch + 1
 //   512   key flags  [2][kMaxPeers], the same for rank r's argmax keys
-//   1024  keys [2][kMaxPeers][16] u64
-//   4096  y partials [2][world][m][ny] fp32
-// Partials and keys are double-buffered by step parity: a rank can be at most one
-// step ahead of another, because every step waits for all ranks' partials.
+//   1024  keys [2][16] u64: this rank's per-token argmax keys
+//   4096  y partial [2][m][ny] fp32: this rank's down partial
+// Results are double-buffered by step parity: a rank can be at most one step ahead of
+// another, because every step waits for all ranks' partials and keys.
 constexpr uint32_t kPeerEpoch = 0, kPeerDownCnt = 64, kPeerFinishCnt = 128, kPeerDownFlags = 256,
                    kPeerKeyFlags = 512, kPeerKeys = 1024, kPeerY = 4096;
 
 size_t peer_buffer_bytes(int world, int m, int64_t ny) {
   if (world < 2 || world > kMaxPeers || m < 1 || m > 16 || ny < 1) return 0;
-  return kPeerY + 2ull * static_cast<size_t>(world) * static_cast<size_t>(m) * static_cast<size_t>(ny) * 4ull;
+  return kPeerY + 2ull * static_cast<size_t>(m) * static_cast<size_t>(ny) * 4ull;
 }
 
 __device__ __forceinline__ uint32_t* peer_flag(uint8_t* buf, uint32_t off, uint32_t par, int src) {
@@ -492,19 +496,17 @@ __device__ __forceinline__ void tile_epilogue(const GemvParams& p, int64_t t, co
         }
     }
   } else if (p.peer.world > 1) {
-    // sharded down projection: this rank's partial of the tile goes to every rank's
-    // buffer (slot [par][rank]); the head kernel adds the slots in rank order
+    // sharded down projection: this rank's partial of the tile goes to its own buffer
+    // (parity slot); every rank's finish kernel reads it from there
     const PeerParams& pr = p.peer;
+    float* part = reinterpret_cast<float*>(pr.base[pr.rank] + kPeerY) + static_cast<int64_t>(par) * pr.m * pr.ny;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int col = 8 * nt + 2 * q + (e & 1);
         const int64_t row = row0 + g + 8 * (e >> 1);
-        if (col < p.M && row < p.n_rows) {
-          const int64_t off = ((static_cast<int64_t>(par) * pr.world + pr.rank) * pr.m + col) * pr.ny + row;
-          for (int r = 0; r < pr.world; ++r) reinterpret_cast<float*>(pr.base[r] + kPeerY)[off] = v[0][nt][e];
-        }
+        if (col < p.M && row < p.n_rows) part[col * pr.ny + row] = v[0][nt][e];
       }
   } else {
 #pragma unroll
@@ -821,11 +823,11 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 
   if constexpr (EPI == EPI_STORE) {
     if (p.peer.world > 1) {
-      // the partials of this CTA's tiles are written to every rank: make them visible
-      // at system scope, count the CTAs, and the last one raises this rank's down flag
-      // (slot [par][rank]) in every rank's buffer
+      // the partials of this CTA's tiles are in this rank's buffer: order them before
+      // the CTA count; the last CTA makes all of them visible at system scope and
+      // raises this rank's down flag (slot [par][rank]) in every rank's buffer
       const PeerParams& pr = p.peer;
-      __threadfence_system();
+      __threadfence();
       __syncthreads();
       if (threadIdx.x == 0) {
         uint32_t* cnt = reinterpret_cast<uint32_t*>(pr.base[pr.rank] + kPeerDownCnt);
@@ -883,11 +885,10 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       uint64_t b = 0ull;
       if (threadIdx.x < p.M) b = atomicExch(p.gkey + threadIdx.x, 0ull);  // read and re-arm for the next launch
       if (pr.world > 1) {
-        // this rank's keys to every rank (slot [par][rank]), then the merge of all
-        // ranks' keys (max: the same result on every rank)
-        if (threadIdx.x < p.M)
-          for (int r = 0; r < pr.world; ++r)
-            reinterpret_cast<uint64_t*>(pr.base[r] + kPeerKeys)[(par * kMaxPeers + pr.rank) * 16 + threadIdx.x] = b;
+        // this rank's keys into its own buffer (parity slot), one release flag in every
+        // rank's buffer, then the merge of all ranks' keys read from their buffers
+        // (max: the same result on every rank)
+        if (threadIdx.x < p.M) reinterpret_cast<uint64_t*>(pr.base[pr.rank] + kPeerKeys)[par * 16 + threadIdx.x] = b;
         __threadfence_system();
         __syncthreads();
         if (threadIdx.x == 0)
@@ -896,10 +897,10 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
           wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerKeyFlags, par, threadIdx.x), ep + 1u, p.err);
         __syncthreads();
         if (threadIdx.x < p.M) {
-          const uint64_t* keys = reinterpret_cast<const uint64_t*>(pr.base[pr.rank] + kPeerKeys);
           for (int r = 0; r < pr.world; ++r) {
-            const uint64_t c = __ldcv(reinterpret_cast<const unsigned long long*>(keys + (par * kMaxPeers + r) * 16 +
-                                                                                   threadIdx.x));
+            const unsigned long long* keys =
+                reinterpret_cast<const unsigned long long*>(pr.base[r] + kPeerKeys) + par * 16 + threadIdx.x;
+            const uint64_t c = __ldcv(keys);
             b = c > b ? c : b;
           }
         }
@@ -926,8 +927,9 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
 
 // ---- end of a sharded step: y = residual + the ranks' down partials, epoch + 1 ----
 // Runs after the step's down and head kernels of this rank (stream order), so the only
-// waits are on the other ranks' down flags.  The partials are added in rank order, so
-// every rank computes the same bits.  The last CTA to finish advances the epoch.
+// waits are on the other ranks' down flags.  The partials are read from every rank's
+// buffer over NVLink and added in rank order, so every rank computes the same bits.
+// The last CTA to finish advances the epoch.
 __global__ void __launch_bounds__(256) peer_finish_kernel(const PeerParams pr, uint32_t* err) {
   griddep_wait();
   griddep_launch_dependents();
@@ -938,13 +940,33 @@ __global__ void __launch_bounds__(256) peer_finish_kernel(const PeerParams pr, u
     wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerDownFlags, par, threadIdx.x), ep + 1u, err);
   __syncthreads();
   const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
-  const float* part = reinterpret_cast<const float*>(pr.base[pr.rank] + kPeerY) + par * pr.world * total;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
-    float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
-    for (int r = 0; r < pr.world; ++r) s += __ldcv(part + r * total + i);
-    pr.y[tok * pr.ldy + row] = s;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const bool vec = (pr.ny & 3) == 0 && (pr.ldy & 3) == 0 && (!pr.residual || (pr.ldr & 3) == 0) &&
+                   (reinterpret_cast<uintptr_t>(pr.y) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(pr.residual) & 15) == 0;
+  if (vec) {
+    // 16-byte loads: one NVLink read of 16 bytes per rank and 4 outputs
+    for (int64_t i = i0 * 4; i < total; i += stride * 4) {
+      const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
+      float4 s = pr.residual ? *reinterpret_cast<const float4*>(pr.residual + tok * pr.ldr + row)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < pr.world; ++r) {
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(pr.base[r] + kPeerY) + (par * total + i) / 4);
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      *reinterpret_cast<float4*>(pr.y + tok * pr.ldy + row) = s;
+    }
+  } else {
+    for (int64_t i = i0; i < total; i += stride) {
+      const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
+      float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
+      for (int r = 0; r < pr.world; ++r) s += __ldcv(reinterpret_cast<const float*>(pr.base[r] + kPeerY) + par * total + i);
+      pr.y[tok * pr.ldy + row] = s;
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1132,7 +1154,7 @@ static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 
 int peer_finish(const PeerParams& pr, uint32_t* err, cudaStream_t stream) {
   const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 64));
+  const int blocks = static_cast<int>(std::min<int64_t>((total / 4 + 255) / 256, 148));
   return launch_pdl(peer_finish_kernel, dim3(blocks), dim3(256), 0, stream, pr, err);
 }
 

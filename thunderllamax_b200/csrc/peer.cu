@@ -4,9 +4,9 @@
 // cudaMalloc-backed device memory), exports it with tlx_ipc_handle, the handles are
 // exchanged on the host (torch.distributed all_gather_object), and every rank opens
 // every peer's buffer with tlx_ipc_open.  The fused verify kernels then write their
-// partial results straight into the peers' buffers with ordinary stores over
-// NVLink / NVSwitch and raise per-rank flags there (gemv.cu, PeerParams).  No TMA
-// and no multicast touch peer memory.
+// partial results into their own buffer, raise per-rank release flags in every rank's
+// buffer, and read the peers' results over NVLink / NVSwitch with ordinary loads once
+// the flags are up (gemv.cu, PeerParams).  No TMA and no multicast touch peer memory.
 #include <cuda.h>
 #include <cuda_runtime.h>
 

@@ -5,11 +5,11 @@ The reference is single-GPU (README.md:412-413); this is the B200 node layout:
 * FFN gate/up: output rows split by whole 256-row blocks (the gact image a
   rank produces is exactly the k range of down it consumes).
 * FFN down: split by k (columns) to match; every rank produces a partial
-  11 x 5120 fp32 sum, added by ONE NCCL all-reduce.  Rank 0 adds the residual.
+  11 x 5120 fp32 sum, and every rank adds all ranks' partials in rank order
+  (the residual first).
 * LM head: split by vocabulary; each rank's fused head emits 11 packed
-  (max, index) keys with global row ids, ONE NCCL all-gather collects the
-  [world][11] keys and every rank merges them and runs greedy accept
-  (deterministic, identical on all ranks).
+  (max, index) keys with global row ids; every rank merges all ranks' keys and
+  runs greedy accept (deterministic, identical on all ranks).
 
 The MoE verify layer (config 4) and the prefill FFN (config 5) shard the same way:
 
@@ -25,9 +25,15 @@ The MoE verify layer (config 4) and the prefill FFN (config 5) shard the same wa
 The summation order of an all-reduce differs from the single-GPU combine, so
 sharded results agree with the one-GPU path to fp32 rounding, not bit for bit.
 
-Collectives go through ``torch.distributed`` (NCCL on GPUs; gloo in the CPU
-tests of the host-side plumbing) and are captured in the step's CUDA graph.
-No data path uses TMA multicast or peer memory.
+The verify step's default exchange (comm="peer") uses no collective library: every
+rank maps every other rank's communication buffer (CUDA IPC), the down and head
+kernels write their results into their own buffer and raise release flags in every
+rank's buffer, and the finish kernel / the head's last CTA read the peers' results
+over NVLink.  comm="nccl" keeps the all-reduce + all-gather form.  The MoE and
+prefill steps use one NCCL all-reduce each.  Collectives go through
+``torch.distributed`` (NCCL on GPUs; gloo in the CPU tests of the host-side
+plumbing) and are captured in the step's CUDA graph.  No load of peer memory uses
+TMA or multicast.
 """
 from __future__ import annotations
 
@@ -59,8 +65,9 @@ class PeerComm:
     """The communication buffers of the sharded verify step over peer memory: one per
     rank on its own GPU (tlx_peer_buffer_alloc), every peer's mapped into this process
     through a CUDA IPC handle exchanged over the process group.  `ptrs` is the array of
-    the `world` buffers as seen from this process (the kernels write the peers' slots
-    with ordinary stores over NVLink and read only their own buffer)."""
+    the `world` buffers as seen from this process (the kernels write their results into
+    their own buffer, raise a release flag in every rank's buffer and read the peers'
+    results over NVLink once the flags are up)."""
 
     def __init__(self, rank: int, world: int, m: int, ny: int, group=None):
         import ctypes
@@ -226,7 +233,8 @@ class ShardedVerifyStep:
                             row_offset=self.v0, out_keys=self.local_keys)
 
     def launch_ffn_down_peer(self):
-        """This rank's down partial into every rank's buffer (tlx_gemv_peer)."""
+        """This rank's down partial into its own peer buffer, flagged to every rank
+        (tlx_gemv_peer)."""
         from . import _lib
 
         s = self.shape
