@@ -34,9 +34,9 @@ FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) per head row of the fused head/argmax launch, from one
 # ncu --set full capture of that kernel alone at the full vocabulary 151936
-# (profiles/tile_gemv_head_argmax_full.txt: 640.28 MB read + 6.18 MB written),
+# (profiles/tile_gemv_head_argmax_full.txt: 640.37 MB read + 5.62 MB written),
 # scaled to a launch by its row count (a vocabulary shard at N > 1)
-HEAD_TRAFFIC_BYTES_PER_ROW = (640_278_528 + 6_181_888) / 151936
+HEAD_TRAFFIC_BYTES_PER_ROW = (640_373_248 + 5_624_320) / 151936
 
 
 def measured_peak():
