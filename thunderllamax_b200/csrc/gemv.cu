@@ -829,13 +829,18 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
       const PeerParams& pr = p.peer;
       __threadfence();
       __syncthreads();
+      __shared__ uint32_t s_last;
       if (threadIdx.x == 0) {
         uint32_t* cnt = reinterpret_cast<uint32_t*>(pr.base[pr.rank] + kPeerDownCnt);
-        if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
-          __threadfence_system();
-          for (int r = 0; r < pr.world; ++r) st_release_sys(peer_flag(pr.base[r], kPeerDownFlags, par, pr.rank), ep + 1u);
-          *cnt = 0u;
-        }
+        s_last = atomicAdd(cnt, 1u) == gridDim.x - 1 ? 1u : 0u;
+        if (s_last) *cnt = 0u;
+      }
+      __syncthreads();
+      // the last CTA: thread r raises the flag in rank r's buffer, all ranks at once
+      // (each thread's own system-scope fence, then its release store)
+      if (s_last && threadIdx.x < pr.world) {
+        __threadfence_system();
+        st_release_sys(peer_flag(pr.base[threadIdx.x], kPeerDownFlags, par, pr.rank), ep + 1u);
       }
     }
   }
@@ -889,20 +894,25 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
         // rank's buffer, then the merge of all ranks' keys read from their buffers
         // (max: the same result on every rank)
         if (threadIdx.x < p.M) reinterpret_cast<uint64_t*>(pr.base[pr.rank] + kPeerKeys)[par * 16 + threadIdx.x] = b;
-        __threadfence_system();
         __syncthreads();
-        if (threadIdx.x == 0)
-          for (int r = 0; r < pr.world; ++r) st_release_sys(peer_flag(pr.base[r], kPeerKeyFlags, par, pr.rank), ep + 1u);
-        if (threadIdx.x < pr.world)
+        // thread r raises the flag in rank r's buffer (its own fence, then its release
+        // store: all ranks at once), then waits for rank r's flag in this buffer
+        if (threadIdx.x < pr.world) {
+          __threadfence_system();
+          st_release_sys(peer_flag(pr.base[threadIdx.x], kPeerKeyFlags, par, pr.rank), ep + 1u);
           wait_peer_flag(peer_flag(pr.base[pr.rank], kPeerKeyFlags, par, threadIdx.x), ep + 1u, p.err);
+        }
         __syncthreads();
         if (threadIdx.x < p.M) {
-          for (int r = 0; r < pr.world; ++r) {
-            const unsigned long long* keys =
-                reinterpret_cast<const unsigned long long*>(pr.base[r] + kPeerKeys) + par * 16 + threadIdx.x;
-            const uint64_t c = __ldcv(keys);
-            b = c > b ? c : b;
-          }
+          // every rank's key is loaded before any is compared: one NVLink round trip
+          uint64_t c[kMaxPeers];
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r)
+            c[r] = r < pr.world ? __ldcv(reinterpret_cast<const unsigned long long*>(pr.base[r] + kPeerKeys) + par * 16 +
+                                         threadIdx.x)
+                                : 0ull;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r) b = c[r] > b ? c[r] : b;
         }
       }
       if (threadIdx.x < p.M) {
@@ -951,20 +961,33 @@ __global__ void __launch_bounds__(256) peer_finish_kernel(const PeerParams pr, u
       const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
       float4 s = pr.residual ? *reinterpret_cast<const float4*>(pr.residual + tok * pr.ldr + row)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < pr.world; ++r) {
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(pr.base[r] + kPeerY) + (par * total + i) / 4);
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
+      // every rank's partial is loaded before any is added: one NVLink round trip
+      float4 v[kMaxPeers];
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        v[r] = r < pr.world ? __ldcv(reinterpret_cast<const float4*>(pr.base[r] + kPeerY) + (par * total + i) / 4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < pr.world) {
+          s.x += v[r].x;
+          s.y += v[r].y;
+          s.z += v[r].z;
+          s.w += v[r].w;
+        }
       *reinterpret_cast<float4*>(pr.y + tok * pr.ldy + row) = s;
     }
   } else {
     for (int64_t i = i0; i < total; i += stride) {
       const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
       float s = pr.residual ? pr.residual[tok * pr.ldr + row] : 0.f;
-      for (int r = 0; r < pr.world; ++r) s += __ldcv(reinterpret_cast<const float*>(pr.base[r] + kPeerY) + par * total + i);
+      float v[kMaxPeers];
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        v[r] = r < pr.world ? __ldcv(reinterpret_cast<const float*>(pr.base[r] + kPeerY) + par * total + i) : 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < pr.world) s += v[r];
       pr.y[tok * pr.ldy + row] = s;
     }
   }
