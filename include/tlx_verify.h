@@ -345,6 +345,24 @@ int tlx_attn_decode(const void* kv, const void* sc, const void* qw16, const void
 int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const float* const* conv_x,
                      const float* const* rec_x, int n_blocks, int64_t rec_elems, int64_t conv_elems, void* stream);
 
+/* GDN state commit as a slot index (the index form of acceptsel11k; the reference
+ * copies, engine/acceptsel11k.cu:15-39).  A slot table of tlx_gdn_slots_bytes(n_blocks)
+ * bytes (device memory, 8-byte aligned) holds per GDN block b the device addresses of
+ * the rec and conv buffers of the eleven draft positions and of the live state:
+ * tab[(b * 2 + kind) * 12 + s], kind 0 = rec / 1 = conv, s = 0..10 the draft
+ * positions, s = 11 the live state.  tlx_gdn_slots_init writes the reference's fixed
+ * layout (the buffers of tlx_acceptsel11k; rec draft 4 is the live state itself).
+ * tlx_acceptsel11k_flip reads m = m_slot[0] on the device and permutes the table: the
+ * live entry then names the buffer holding draft m's state (what tlx_acceptsel11k
+ * copies into the live slot) and draft m's entry the buffer that held the live state,
+ * free for the next step's draft m.  It moves 8-byte addresses, not the 314 MB of
+ * state; the GDN kernels that read and write the states do so through the table.
+ * An m outside 0..10 changes nothing. */
+size_t tlx_gdn_slots_bytes(int n_blocks);
+int tlx_gdn_slots_init(uint64_t* tab, const float* rec4, const float* conv4, const float* const* conv_x,
+                       const float* const* rec_x, int n_blocks, int64_t rec_elems, int64_t conv_elems, void* stream);
+int tlx_acceptsel11k_flip(uint64_t* tab, const int32_t* m_slot, int n_blocks, void* stream);
+
 /* ---- MoE verify layer (P <= 8 positions, top-8 of E <= 1024 experts + shared) ----
  * Router: logits = w_router[E][hidden] (fp32) . h[p] (bf16), top-8 by 8 masked-argmax
  * passes (strict '>', ties to the lower expert id), gates = exp(l - max) / sum over

@@ -67,6 +67,9 @@ _SIGS = {
     "tlx_argmax_rows": (c_int, [c_vp, c_int, c_int, c_i64, c_i64, c_vp, c_vp]),
     "tlx_h_argmax": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "tlx_acceptsel11k": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "tlx_gdn_slots_bytes": (c_size, [c_int]),
+    "tlx_gdn_slots_init": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp]),
+    "tlx_acceptsel11k_flip": (c_int, [c_vp, c_vp, c_int, c_vp]),
     "tlx_attn_workspace_bytes": (c_size, [c_int]),
     "tlx_attn_pre": (c_int, [c_vp] * 7 + [c_int, c_i64, c_vp, c_vp, c_vp, c_vp]),
     "tlx_attn_split": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_vp, c_size, c_vp]),

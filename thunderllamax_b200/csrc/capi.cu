@@ -122,6 +122,60 @@ __global__ void acceptsel_kernel(float* __restrict__ rec4, float* __restrict__ c
   for (int64_t i = t0; i < conv_v; i += stride) d[i] = s[i];
 }
 
+// GDN state commit as a slot index: the table of every GDN block holds the device
+// addresses of the rec and conv buffers of the eleven draft positions (entries 0..10)
+// and of the live state (entry 11): tab[(b * 2 + kind) * 12 + s], kind 0 = rec, 1 = conv.
+// The flip permutes addresses instead of copying the state (acceptsel11k's 314 MB).
+constexpr int kGdnSlots = 12, kGdnLive = 11;
+
+struct GdnInit {
+  const float* rec4;
+  const float* conv4;
+  const float* conv_x[7];  // conv5x .. conv11x
+  const float* rec_x[6];   // rec6x .. rec11x
+  int64_t rec_elems, conv_elems;
+};
+
+// the reference's fixed layout (engine/acceptsel11k.cu:15-39): rec draft m at
+// rec4[b][m] for m <= 4 (slot 4 is also the live state) and rec{m+1}x[b] above; conv
+// draft m at conv4[b][m] for m <= 3 and conv{m+1}x[b] above, live at conv4[b][4]
+__global__ void gdn_slots_init_kernel(uint64_t* __restrict__ tab, const GdnInit in, int n_blocks) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n_blocks) return;
+  uint64_t* r = tab + static_cast<int64_t>(b) * 2 * kGdnSlots;
+  uint64_t* c = r + kGdnSlots;
+  for (int m = 0; m <= 10; ++m) {
+    const float* rp = m <= 4 ? in.rec4 + (static_cast<int64_t>(b) * 5 + m) * in.rec_elems
+                             : in.rec_x[m - 5] + static_cast<int64_t>(b) * in.rec_elems;
+    const float* cp = m <= 3 ? in.conv4 + (static_cast<int64_t>(b) * 5 + m) * in.conv_elems
+                             : in.conv_x[m - 4] + static_cast<int64_t>(b) * in.conv_elems;
+    r[m] = reinterpret_cast<uint64_t>(rp);
+    c[m] = reinterpret_cast<uint64_t>(cp);
+  }
+  r[kGdnLive] = reinterpret_cast<uint64_t>(in.rec4 + (static_cast<int64_t>(b) * 5 + 4) * in.rec_elems);
+  c[kGdnLive] = reinterpret_cast<uint64_t>(in.conv4 + (static_cast<int64_t>(b) * 5 + 4) * in.conv_elems);
+}
+
+// accept m: the live entry takes draft m's buffer and draft m's entry the old live
+// buffer (free for the next step's draft m).  rec draft 4 is the live state itself in
+// this layout, so the rec flip keeps entries 4 and 11 equal (m == 4: nothing moves).
+__global__ void gdn_flip_kernel(uint64_t* __restrict__ tab, const int32_t* __restrict__ m_slot, int n_blocks) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = m_slot[0];
+  if (b >= n_blocks || m < 0 || m > 10) return;
+  uint64_t* r = tab + static_cast<int64_t>(b) * 2 * kGdnSlots;
+  uint64_t* c = r + kGdnSlots;
+  if (m != 4) {
+    const uint64_t live = r[kGdnLive];
+    r[kGdnLive] = r[m];
+    r[4] = r[m];
+    r[m] = live;
+  }
+  const uint64_t live = c[kGdnLive];
+  c[kGdnLive] = c[m];
+  c[m] = live;
+}
+
 // argmax key of one row of materialised logits, reduced over the CTA (valid in
 // thread 0): the amx3 / h_argmax scan rules through argmax_key
 // Row argmax over materialised logits: one thread-block cluster of kArgmaxCluster
@@ -559,6 +613,40 @@ int tlx_acceptsel11k(float* rec4, float* conv4, const int32_t* m_slot, const flo
                                                                      conv_elems / 4);
   else
     acceptsel_kernel<float><<<grid, block, 0, as_stream(stream)>>>(rec4, conv4, m_slot, src, rec_elems, conv_elems);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+size_t tlx_gdn_slots_bytes(int n_blocks) {
+  return n_blocks > 0 ? static_cast<size_t>(n_blocks) * 2 * kGdnSlots * sizeof(uint64_t) : 0;
+}
+
+int tlx_gdn_slots_init(uint64_t* tab, const float* rec4, const float* conv4, const float* const* conv_x,
+                       const float* const* rec_x, int n_blocks, int64_t rec_elems, int64_t conv_elems, void* stream) {
+  if (!tab || !rec4 || !conv4 || !conv_x || !rec_x) return TLX_ERR_NULL;
+  if (n_blocks <= 0 || rec_elems <= 0 || conv_elems <= 0) return TLX_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(tab) & 7) return TLX_ERR_ALIGN;
+  GdnInit in;
+  in.rec4 = rec4;
+  in.conv4 = conv4;
+  in.rec_elems = rec_elems;
+  in.conv_elems = conv_elems;
+  for (int i = 0; i < 7; ++i) {
+    if (!conv_x[i]) return TLX_ERR_NULL;
+    in.conv_x[i] = conv_x[i];
+  }
+  for (int i = 0; i < 6; ++i) {
+    if (!rec_x[i]) return TLX_ERR_NULL;
+    in.rec_x[i] = rec_x[i];
+  }
+  gdn_slots_init_kernel<<<(n_blocks + 127) / 128, 128, 0, as_stream(stream)>>>(tab, in, n_blocks);
+  return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
+}
+
+int tlx_acceptsel11k_flip(uint64_t* tab, const int32_t* m_slot, int n_blocks, void* stream) {
+  if (!tab || !m_slot) return TLX_ERR_NULL;
+  if (n_blocks <= 0) return TLX_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(tab) & 7) return TLX_ERR_ALIGN;
+  gdn_flip_kernel<<<(n_blocks + 127) / 128, 128, 0, as_stream(stream)>>>(tab, m_slot, n_blocks);
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
 }
 

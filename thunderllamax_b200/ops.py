@@ -428,6 +428,43 @@ def acceptsel11k(rec4: torch.Tensor, conv4: torch.Tensor, m_slot: torch.Tensor, 
                                       _stream(rec4)), "acceptsel11k")
 
 
+class GdnSlots:
+    """GDN state commit as a slot index: a device table of the rec / conv buffer
+    addresses of the eleven draft positions and the live state per GDN block
+    (tlx_gdn_slots_init over the same buffers acceptsel11k takes).  flip(m_slot)
+    makes the live entry name draft m's buffer instead of copying it
+    (tlx_acceptsel11k_flip)."""
+
+    LIVE = 11
+
+    def __init__(self, rec4: torch.Tensor, conv4: torch.Tensor, conv_x, rec_x, n_blocks: int = GDN_BLOCKS,
+                 rec_elems: int = GDN_REC, conv_elems: int = GDN_CONV):
+        conv_x, rec_x = list(conv_x), list(rec_x)
+        if len(conv_x) != 7 or len(rec_x) != 6:
+            raise TLXError("the slot table takes 7 conv scratch buffers (conv5x..11x) and 6 rec (rec6x..11x)")
+        for t, n in [(rec4, n_blocks * 5 * rec_elems), (conv4, n_blocks * 5 * conv_elems)] + \
+                    [(t, n_blocks * conv_elems) for t in conv_x] + [(t, n_blocks * rec_elems) for t in rec_x]:
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < n:
+                raise TLXError("slot-table buffers are contiguous fp32 of the stated sizes")
+        self.n_blocks = n_blocks
+        nb = int(_lib.lib().tlx_gdn_slots_bytes(n_blocks))
+        self.table = torch.empty(nb // 8, dtype=torch.int64, device=rec4.device)
+        cx = (ctypes.c_void_p * 7)(*[t.data_ptr() for t in conv_x])
+        rx = (ctypes.c_void_p * 6)(*[t.data_ptr() for t in rec_x])
+        check(_lib.lib().tlx_gdn_slots_init(_ptr(self.table), _ptr(rec4), _ptr(conv4), cx, rx, n_blocks, rec_elems,
+                                            conv_elems, _stream(rec4)), "gdn_slots_init")
+
+    def flip(self, m_slot: torch.Tensor) -> None:
+        if m_slot.dtype != torch.int32:
+            raise TLXError("m_slot is int32")
+        check(_lib.lib().tlx_acceptsel11k_flip(_ptr(self.table), _ptr(m_slot), self.n_blocks, _stream(self.table)),
+              "acceptsel11k_flip")
+
+    def entries(self) -> torch.Tensor:
+        """[n_blocks][2 (rec, conv)][12] device addresses (host copy)."""
+        return self.table.view(self.n_blocks, 2, 12).cpu()
+
+
 def argmax_merge(keys: torch.Tensor, out_max=None, out_idx=None, drafts=None, accept_out=None):
     n_shards, m = keys.shape
     dev = keys.device
@@ -453,5 +490,5 @@ def accept(amds: torch.Tensor, drafts: torch.Tensor, k: int = None, mb=None, eb=
 
 
 __all__ = ["Workspace", "Image", "stage", "pack_tiles", "pack_tiles_host", "unpack_tiles_host", "tiled_bytes", "gemv", "ffn_gate_up",
-           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "AttnProjections", "GdnProjections", "Lookup", "Attention", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
+           "head_argmax", "argmax_rows", "h_argmax", "acceptsel11k", "GdnSlots", "AttnProjections", "GdnProjections", "Lookup", "Attention", "argmax_merge", "accept", "grid", "plan", "set_max_ctas", "require_device",
            "MODE_STORE", "MODE_GATE_UP", "MODE_ARGMAX"]
