@@ -571,6 +571,29 @@ def measure_attn_qkv(args, torch, peak):
             "err_word": proj.error()}
 
 
+RAMP_S = 0.3
+
+
+def ramp_replays(replay, torch, dist=None) -> int:
+    """Untimed replays for about RAMP_S seconds (the count is rank 0's, broadcast so
+    that every rank replays, and so exchanges, the same number of steps)."""
+    import time
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    replay()
+    torch.cuda.synchronize()
+    one = max(time.perf_counter() - t0, 1e-5)
+    n = torch.tensor([min(20000, max(10, int(RAMP_S / one)))], device="cuda")
+    if dist is not None:
+        dist.broadcast(n, 0)
+    n = int(n.item())
+    for _ in range(n):
+        replay()
+    torch.cuda.synchronize()
+    return n
+
+
 def _graph_of(fn, torch):
     """Capture fn (after one eager call on a side stream) as a CUDA graph."""
     stream = torch.cuda.Stream()
@@ -798,6 +821,10 @@ def run_ours(args):
         check = check_unsharded(step, shape, x, h, drafts, rank, torch, dist)
 
     clk = ClockSampler(local).__enter__()     # runs across every timed leg below (step, kernels, e2e)
+    # the GPU sat idle while the model was generated on the host: untimed replays for
+    # RAMP_S seconds bring its clocks and power state to steady load, then the W
+    # warm-up steps, then the K timed steps (same count on every rank)
+    ramp = ramp_replays(step.replay, torch, dist)
     for _ in range(max(3, args.warmup)):
         step.replay()
     barrier()
@@ -822,16 +849,20 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     # end to end through host buffers (pinned), one host wait per step
-    xp, hp, dp = x.pin_memory(), h.pin_memory(), drafts.pin_memory()
-    outp = torch.empty(2 + shape.rows, dtype=torch.int32).pin_memory()
+    # one pinned buffer for the step's inputs (x | h | drafts) and one for its record:
+    # one H2D and one D2H copy per step
+    inp, outp, views = step.host_buffers()
+    views["x"].copy_(x)
+    views["h"].copy_(h)
+    views["drafts"].copy_(drafts)
     for _ in range(3):
-        step.step_host(xp, hp, dp, outp)
+        step.step_host_packed(inp, outp)
         torch.cuda.current_stream().synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step.step_host(xp, hp, dp, outp)
+        step.step_host_packed(inp, outp)
         torch.cuda.current_stream().synchronize()
     e1.record()
     torch.cuda.synchronize()
@@ -896,7 +927,8 @@ def run_ours(args):
                                       else "the three GEMVs in sequence on every SM"),
                          "kernels": "each kernel alone on every SM, 20 launches back to back per graph",
                          "l2": f"weights {total_w / 1e6:.0f} MB > 126 MB L2 (no flush needed)",
-                         "device_time": "CUDA events around the K replays, max over ranks"},
+                         "device_time": "CUDA events around the K replays, max over ranks",
+                         "ramp": f"{ramp} untimed replays (~{RAMP_S} s) before the W warm-up steps"},
               "frac_of_hbm": round(value / ws / peak, 4), "frac_of_8tbs": round(value / ws / 8000.0, 4),
               "roofline": {"bound": "hbm", "kernel": "head_argmax", "achieved": round(achieved, 1),
                            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),

@@ -556,6 +556,40 @@ def test_verify_step_host_path_copies_every_call():
         assert step.accept_out.cpu().tolist() == outp[:2].tolist()
 
 
+def test_verify_step_packed_host_path():
+    # step_host_packed: one H2D copy of x | h | drafts and one D2H copy of (m, bonus,
+    # ids) per step, new contents of the same pinned buffers on every call, against the
+    # oracle and the device views
+    from thunderllamax_b200.verify import VerifyShape, VerifyStep
+
+    rng = np.random.default_rng(17)
+    s = VerifyShape(dim=1024, ffn=2048, vocab=5003, rows=11)
+    w = {"gate": ops.pack_tiles("iq3_xxs", synth.iq3xxs_blocks(rng, s.ffn, s.dim), s.dim),
+         "up": ops.pack_tiles("iq3_xxs", synth.iq3xxs_blocks(rng, s.ffn, s.dim), s.dim),
+         "down": ops.pack_tiles("q6_k", synth.q6k_blocks(rng, s.dim, s.ffn), s.ffn)}
+    rh = synth.q6k_blocks(rng, s.vocab, s.dim)
+    w["head"] = ops.pack_tiles("q6_k", rh, s.dim)
+    step = VerifyStep(s, weights=w)
+    inp, outp, views = step.host_buffers()
+    assert inp.is_pinned() and outp.is_pinned()
+    assert inp.numel() == 2 * s.rows * s.dim * 2 + s.n_drafts * 4 and outp.numel() == 2 + s.rows
+    for trial in range(3):
+        x, _ = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+        h, h64 = x_tensor(rng, s.rows, s.dim, torch.bfloat16)
+        _, idx_ref, _ = oracle.head_argmax(h64, rh, "q6_k")
+        drafts_np = idx_ref[:s.n_drafts].copy()
+        drafts_np[trial + 4] = (drafts_np[trial + 4] + 1) % s.vocab
+        views["x"].copy_(x.cpu())
+        views["h"].copy_(h.cpu())
+        views["drafts"].copy_(torch.from_numpy(drafts_np))
+        step.step_host_packed(inp, outp)
+        torch.cuda.current_stream().synchronize()
+        assert np.array_equal(outp[2:].numpy(), idx_ref)
+        assert outp[:2].tolist() == list(oracle.accept(idx_ref, drafts_np))
+        assert torch.equal(step.x.cpu(), x.cpu())
+        assert torch.equal(step.drafts.cpu(), torch.from_numpy(drafts_np))
+
+
 @pytest.mark.parametrize("qtype,n,k,rows,cols", [("q6_k", 20000, 512, (8704, 17408), None),
                                                  ("iq3_xxs", 20000, 512, (16, 8208), None),
                                                  ("q6_k", 512, 17408, None, (8704, 17408)),

@@ -42,7 +42,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .verify import VerifyShape, synth_tiled
+from .verify import StepIO, VerifyShape, synth_tiled
 
 
 def block_ranges(n_blocks: int, world: int) -> list[tuple[int, int]]:
@@ -133,7 +133,7 @@ def gather_keys(local_keys: torch.Tensor, all_keys: torch.Tensor, group=None) ->
     return all_keys
 
 
-class ShardedVerifyStep:
+class ShardedVerifyStep(StepIO):
     """VerifyStep over `world` GPUs; this object is rank `rank`'s share.
 
     comm = "peer" (default): the down projection's partials and the head's argmax keys
@@ -173,17 +173,13 @@ class ShardedVerifyStep:
                        "head": synth_tiled(s.head_q, s.vocab, s.dim, seed + 4, rows=(self.v0, self.v1))}
         self.w = weights
         dev = "cuda"
-        self.x = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
-        self.h = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self._alloc_io(s.rows, s.dim, s.n_drafts, dev)      # x, h, drafts, accept_out, out_idx
         self.res = torch.zeros((s.rows, s.dim), dtype=torch.float32, device=dev)
-        self.drafts = torch.zeros(s.n_drafts, dtype=torch.int32, device=dev)
         self.gact = ops.Image(s.rows, self.n_ffn, dev)
         self.y = torch.empty((s.rows, s.dim), dtype=torch.float32, device=dev)
         self.local_keys = torch.zeros(s.rows, dtype=torch.int64, device=dev)
         self.all_keys = torch.zeros((world, s.rows), dtype=torch.int64, device=dev)
         self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
-        self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
-        self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
         # peer mode: the FFN (gate/up -> down) and the head run on two streams at once,
         # each on its own share of the SMs; both are latency-bound at these shard sizes,
         # so running them side by side hides one's fixed costs behind the other

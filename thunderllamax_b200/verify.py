@@ -95,7 +95,43 @@ def default_split_ctas(sms: int) -> int:
     return 45 if sms >= 128 else 0
 
 
-class VerifyStep:
+class StepIO:
+    """The step's host-facing buffers, packed so that a step moves its inputs with ONE
+    host-to-device copy and its record with ONE device-to-host copy: the device input
+    buffer holds x | h (bf16 [rows][dim] each) | drafts (int32), the output buffer the
+    accept record (m, bonus) then the rows' argmax ids (int32), and the kernels read and
+    write views of them.  host_buffers() gives pinned host buffers of the same layouts."""
+
+    def _alloc_io(self, rows: int, dim: int, n_drafts: int, dev="cuda"):
+        xb = rows * dim * 2
+        self._in_bytes = 2 * xb + n_drafts * 4
+        self.inbuf = torch.zeros(self._in_bytes, dtype=torch.uint8, device=dev)
+        self.x = self.inbuf[:xb].view(torch.bfloat16).view(rows, dim)
+        self.h = self.inbuf[xb:2 * xb].view(torch.bfloat16).view(rows, dim)
+        self.drafts = self.inbuf[2 * xb:].view(torch.int32)
+        self.outbuf = torch.zeros(2 + rows, dtype=torch.int32, device=dev)
+        self.accept_out = self.outbuf[:2]
+        self.out_idx = self.outbuf[2:]
+
+    def host_buffers(self):
+        """(in_pinned uint8, out_pinned int32, the in buffer's x / h / drafts views)."""
+        xb = self.x.numel() * 2
+        inp = torch.zeros(self._in_bytes, dtype=torch.uint8).pin_memory()
+        outp = torch.zeros(self.outbuf.numel(), dtype=torch.int32).pin_memory()
+        views = {"x": inp[:xb].view(torch.bfloat16).view(self.x.shape),
+                 "h": inp[xb:2 * xb].view(torch.bfloat16).view(self.h.shape),
+                 "drafts": inp[2 * xb:].view(torch.int32)}
+        return inp, outp, views
+
+    def step_host_packed(self, in_pinned, out_pinned):
+        """End-to-end step through host buffers: ONE H2D copy of x | h | drafts, the
+        graph replay, ONE D2H copy of (m, bonus, argmax ids)."""
+        self.inbuf.copy_(in_pinned, non_blocking=True)
+        self.replay()
+        out_pinned.copy_(self.outbuf, non_blocking=True)
+
+
+class VerifyStep(StepIO):
     def __init__(self, shape: VerifyShape = VerifyShape(), seed: int = 0, weights: dict | None = None,
                  ffn_ctas: int | None = None):
         ops.require_device()
@@ -107,16 +143,12 @@ class VerifyStep:
             "head": synth_tiled(s.head_q, s.vocab, s.dim, seed + 4),
         }
         dev = "cuda"
-        self.x = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
-        self.h = torch.zeros((s.rows, s.dim), dtype=torch.bfloat16, device=dev)
+        self._alloc_io(s.rows, s.dim, s.n_drafts, dev)      # x, h, drafts, accept_out, out_idx
         self.res = torch.zeros((s.rows, s.dim), dtype=torch.float32, device=dev)
-        self.drafts = torch.zeros(s.n_drafts, dtype=torch.int32, device=dev)
         # gate/up writes gact straight into the fp16 activation image down reads
         self.gact = ops.Image(s.rows, s.ffn, dev)
         self.y = torch.empty((s.rows, s.dim), dtype=torch.float32, device=dev)
         self.out_max = torch.empty(s.rows, dtype=torch.float32, device=dev)
-        self.out_idx = torch.empty(s.rows, dtype=torch.int32, device=dev)
-        self.accept_out = torch.empty(2, dtype=torch.int32, device=dev)
         # workspaces of the kernels alone on every SM (launch_<kernel>) ...
         self.ws = {
             "ffn_gate_up": ops.Workspace.for_shape(ops.MODE_GATE_UP, s.ffn_q, s.ffn, s.dim, s.rows),
