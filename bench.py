@@ -466,29 +466,41 @@ def measure_sharded_extras(args, torch, ws, rank, peak):
 
     out = {}
     if not args.no_moe:
+        from thunderllamax_b200.moe import synth_host
+
         shape = MoeShape()
-        step = ShardedMoeVerifyStep(shape, rank, ws, seed=0)
+        host = synth_host(shape, 0)
         rng = np.random.default_rng(4321)
         bits = synth.bf16_normal(rng, (shape.positions, shape.hidden))
         hres = rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32)
-        step.set_inputs(torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda(),
-                        torch.from_numpy(hres).cuda())
-        step.capture()
-        for _ in range(5):
-            step.replay()
-        dist.barrier()
-        torch.cuda.synchronize()
-        ms = max_over_ranks(time_graph(step.replay, max(20, min(2000, args.steps)), torch))
-        touched = sum_over_ranks(step.touched_bytes())
+        res, ys, err = {}, {}, 0
+        for comm in ("peer", "nccl"):
+            step = ShardedMoeVerifyStep(shape, rank, ws, host=host, comm=comm)
+            step.set_inputs(torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda(),
+                            torch.from_numpy(hres).cuda())
+            step.capture()
+            for _ in range(5):
+                step.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            res[comm] = max_over_ranks(time_graph(step.replay, max(20, min(2000, args.steps)), torch))
+            ys[comm] = step.y.clone()
+            touched = sum_over_ranks(step.touched_bytes())
+            err |= step.local.ws.error() | (int(step.finish_err.item()) if comm == "peer" else 0)
+            step.release()
+            del step
+        ms = res["peer"]
+        y_err = float(((ys["peer"] - ys["nccl"]).abs().amax(dim=1) / ys["nccl"].norm(dim=1)).max())
         out["moe_verify"] = {"workload": f"MoE verify layer, expert parallel over {ws} GPUs "
-                                         f"({shape.experts // ws} experts per rank), router replicated, "
-                                         "one NCCL all-reduce of the fp32 partials",
+                                         f"({shape.experts // ws} experts per rank), router replicated, the "
+                                         "ranks' fp32 partials summed over peer memory (tlx_peer_publish + "
+                                         "tlx_peer_finish)",
                              "us_per_step": round(ms * 1000, 2), "bytes_per_step": int(touched),
                              "gbs": round(touched / (ms * 1e-3) / 1e9, 1),
                              "frac_of_peak": round(touched / (ms * 1e-3) / 1e9 / (peak * ws), 4),
-                             "timing": "CUDA graph replay, max over ranks", "err_word": step.local.ws.error()}
-        step.release()
-        del step
+                             "us_per_step_nccl_allreduce": round(res["nccl"] * 1000, 2),
+                             "peer_vs_nccl_y_max_err_over_row_norm": y_err,
+                             "timing": "CUDA graph replay, max over ranks", "err_word": err}
         out["moe_exchange"] = measure_moe_exchange(torch, dist, shape, ws, max_over_ranks)
     if not args.no_prefill:
         shape = PrefillShape()

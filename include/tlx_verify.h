@@ -242,6 +242,13 @@ int tlx_head_argmax_peer(int qtype, const void* w, const uint32_t* grid, const v
                          void* const* peer_bufs, int max_ctas, void* ws, size_t ws_bytes, void* stream);
 int tlx_peer_finish(int world, int rank, void* const* peer_bufs, int m, int64_t ny, const float* residual,
                     int64_t ldr, float* y, int64_t ldy, uint32_t* err, void* stream);
+/* The same exchange for a partial an ordinary kernel wrote (the expert-parallel MoE
+ * layer's output): copies part [m][ny] (row stride ldp) into this rank's buffer and
+ * raises this rank's flag in every rank's buffer; tlx_peer_finish on the same stream
+ * then sums all ranks' partials (an all-reduce without a collective library).  No
+ * reference counterpart: the reference runs one GPU. */
+int tlx_peer_publish(int world, int rank, void* const* peer_bufs, int m, int64_t ny, const float* part, int64_t ldp,
+                     void* stream);
 
 /* ---- greedy acceptance ------------------------------------------------------------
  * acc36: m = longest prefix amds[s] == drafts[s], s < k; mb[0] = m;

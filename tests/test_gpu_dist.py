@@ -116,6 +116,77 @@ def test_sharded_verify_step(world, comm):
     assert len({r[-1] for r in results}) == 1
 
 
+def _moe_rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from thunderllamax_b200 import dist as tdist
+    from thunderllamax_b200 import moe, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        shape = moe.MoeShape(positions=5, experts=64, hidden=1024, inner=512)
+        host = moe.synth_host(shape, 23)
+        rng = np.random.default_rng(23)
+        h = torch.from_numpy(synth.bf16_normal(rng, (shape.positions, shape.hidden)).view(np.int16)).cuda()
+        h = h.view(torch.bfloat16)
+        hres = torch.from_numpy(rng.standard_normal((shape.positions, shape.hidden)).astype(np.float32)).cuda()
+        full = moe.MoeVerifyStep(shape, host=host)
+        full.set_inputs(h, hres)
+        full.launch()
+        step = tdist.ShardedMoeVerifyStep(shape, rank, world, host=host, comm="peer")
+        step.set_inputs(h, hres)
+        step.capture()
+        ys = []
+        for _ in range(3):        # the parity slots alternate by step
+            step.replay()
+            torch.cuda.synchronize()
+            ys.append(step.y.clone())
+        ref = full.y
+        err = float(((ys[-1] - ref).abs().amax(dim=1) / ref.norm(dim=1)).max())
+        same = all(torch.equal(ys[0], t) for t in ys[1:])
+        out = (rank, err, same, int(step.finish_err.item()), step.local.ws.error(), ys[-1].cpu().numpy().tobytes())
+        step.release()
+        q.put(out)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_sharded_moe_peer_exchange(world):
+    # expert-parallel MoE layer, the ranks' partials summed over peer memory: every rank
+    # holds the unsharded layer's y to fp32 rounding, the same bits on every rank and
+    # over repeated steps
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    os.environ["PYTHONPATH"] = os.pathsep.join([root, here, os.environ.get("PYTHONPATH", "")])
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_moe_rank, args=(r, world, port, q)) for r in range(world)]
+    for p_ in procs:
+        p_.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=300))
+    finally:
+        for p_ in procs:
+            p_.join(timeout=60)
+    assert all(p_.exitcode == 0 for p_ in procs)
+    for rank, err, same, ferr, werr, _ in results:
+        assert err <= 1e-5, (rank, err)
+        assert same, rank
+        assert ferr == 0 and werr == 0, (rank, ferr, werr)
+    assert len({r[-1] for r in results}) == 1
+
+
 def test_peer_wait_times_out_into_error_word():
     # Failure detection without a GPU fault: rank 0 of a 2-rank step whose rank 1 never
     # runs.  Both buffers live on this GPU (nothing else runs on it); the down kernel

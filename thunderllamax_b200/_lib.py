@@ -58,6 +58,7 @@ _SIGS = {
     "tlx_head_argmax_peer": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_i64, c_vp, c_vp,
                                      c_vp, c_int, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_size, c_vp]),
     "tlx_peer_finish": (c_int, [c_int, c_int, c_vp, c_int, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp]),
+    "tlx_peer_publish": (c_int, [c_int, c_int, c_vp, c_int, c_i64, c_vp, c_i64, c_vp]),
     "tlx_gemv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp, c_int,
                          c_i64, c_vp, c_size, c_vp]),
     "tlx_ffn_gate_up": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_int,

@@ -789,6 +789,20 @@ int tlx_peer_finish(int world, int rank, void* const* peer_bufs, int m, int64_t 
   return peer_finish(pr, err, as_stream(stream));
 }
 
+int tlx_peer_publish(int world, int rank, void* const* peer_bufs, int m, int64_t ny, const float* part, int64_t ldp,
+                     void* stream) {
+  PeerParams pr;
+  const int rc = make_peer(world, rank, peer_bufs, m, ny, pr);
+  if (rc) return rc;
+  if (!part) return TLX_ERR_NULL;
+  if (m < 1 || m > 16 || ny < 1 || ldp < ny) return TLX_ERR_SHAPE;
+  for (int r = 0; r < world; ++r)
+    if (!pr.base[r] || (reinterpret_cast<uintptr_t>(pr.base[r]) & 255)) return TLX_ERR_ALIGN;
+  pr.residual = part;
+  pr.ldr = ldp;
+  return peer_publish(pr, as_stream(stream));
+}
+
 int tlx_argmax_merge(const uint64_t* keys, int n_shards, int m, float* out_max, int32_t* out_idx,
                      const int32_t* drafts, int n_drafts, int32_t* accept_out, void* stream) {
   if (!keys) return TLX_ERR_NULL;

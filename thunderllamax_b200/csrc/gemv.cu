@@ -935,6 +935,39 @@ __global__ void __launch_bounds__(WPC * 32, 1) tile_gemv_kernel(const GemvParams
   }
 }
 
+// ---- publish a partial for the peers (the exchange half of an all-reduce) ----
+// Copies this rank's partial [m][ny] (pr.residual, row stride pr.ldr) into its own
+// buffer (parity slot of the step), orders it before a CTA count, and the last CTA's
+// threads raise this rank's down flag in every rank's buffer, one rank each.
+// peer_finish_kernel then adds the ranks' partials.  The all-reduce of a layer whose
+// producer writes an ordinary buffer (the expert-parallel MoE layer).
+__global__ void __launch_bounds__(256) peer_publish_kernel(const PeerParams pr) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ uint32_t s_last;
+  const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(pr.base[pr.rank] + kPeerEpoch);
+  const uint32_t par = ep & 1u;
+  const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
+  float* part = reinterpret_cast<float*>(pr.base[pr.rank] + kPeerY) + par * total;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = i / pr.ny, row = i - tok * pr.ny;
+    part[i] = pr.residual[tok * pr.ldr + row];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(pr.base[pr.rank] + kPeerDownCnt);
+    s_last = atomicAdd(cnt, 1u) == gridDim.x - 1 ? 1u : 0u;
+    if (s_last) *cnt = 0u;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x < pr.world) {
+    __threadfence_system();
+    st_release_sys(peer_flag(pr.base[threadIdx.x], kPeerDownFlags, par, pr.rank), ep + 1u);
+  }
+}
+
 // ---- end of a sharded step: y = residual + the ranks' down partials, epoch + 1 ----
 // Runs after the step's down and head kernels of this rank (stream order), so the only
 // waits are on the other ranks' down flags.  The partials are read from every rank's
@@ -1174,6 +1207,12 @@ static int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_
 }
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int peer_publish(const PeerParams& pr, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 64));
+  return launch_pdl(peer_publish_kernel, dim3(blocks), dim3(256), 0, stream, pr);
+}
 
 int peer_finish(const PeerParams& pr, uint32_t* err, cudaStream_t stream) {
   const int64_t total = static_cast<int64_t>(pr.m) * pr.ny;

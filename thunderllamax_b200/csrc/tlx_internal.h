@@ -29,6 +29,8 @@ struct PeerParams {
 size_t peer_buffer_bytes(int world, int m, int64_t ny);
 // end of a sharded step: y = residual + the ranks' down partials (rank order), epoch + 1
 int peer_finish(const PeerParams& pr, uint32_t* err, cudaStream_t stream);
+// a partial (pr.residual, row stride pr.ldr) into this rank's buffer + its flag everywhere
+int peer_publish(const PeerParams& pr, cudaStream_t stream);
 
 int run_gemv(int epi, int qt, const void* w0, const void* w1, const uint32_t* grid, const void* x, int x_dtype,
              int64_t ldx, int m, int64_t n_rows, int64_t k, const float* residual, int64_t ldr, void* y,

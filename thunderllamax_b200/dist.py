@@ -414,23 +414,57 @@ def expert_ranges(n_experts: int, world: int) -> list[tuple[int, int]]:
 
 
 class ShardedMoeVerifyStep(_GraphStep):
-    """The MoE verify layer, expert parallel: this rank's experts, then one
-    all-reduce of the partial layer output."""
+    """The MoE verify layer, expert parallel: this rank's experts, then the sum of the
+    ranks' partial layer outputs.
+
+    comm = "peer" (default at world > 1): the partial goes into this rank's peer
+    buffer with its flag raised in every rank's buffer (tlx_peer_publish), and
+    tlx_peer_finish adds all ranks' partials read over NVLink, in rank order (the
+    same bits on every rank); no collective library in the layer.
+    comm = "nccl": one NCCL all-reduce of the partials."""
 
     def __init__(self, shape=None, rank: int = 0, world: int = 1, seed: int = 0, host: dict | None = None,
-                 group=None):
+                 group=None, comm: str = "peer"):
         from .moe import MoeShape, MoeVerifyStep, synth_host
 
+        if comm not in ("peer", "nccl"):
+            raise ValueError(f"comm must be 'peer' or 'nccl', not {comm!r}")
         shape = shape if shape is not None else MoeShape()
         self.shape, self.rank, self.world, self.group = shape, rank, world, group
+        self.comm = comm if world > 1 else "nccl"
         self.e0, self.e1 = expert_ranges(shape.experts, world)[rank]
         host = host if host is not None else synth_host(shape, seed)
         self.local = MoeVerifyStep(shape, host=host, e0=self.e0, e1=self.e1, shared=(rank == 0))
-        self.y = self.local.y
+        self.peer = None
+        if self.comm == "peer":
+            self.peer = PeerComm(rank, world, shape.positions, shape.hidden, group)
+            self.y = torch.empty_like(self.local.y)
+            self.finish_err = torch.zeros(1, dtype=torch.int32, device=self.y.device)
+        else:
+            self.y = self.local.y
 
     def launch(self):
         self.local.launch()
-        allreduce_partial(self.y, self.group)
+        if self.peer is None:
+            allreduce_partial(self.y, self.group)
+            return
+        from . import _lib
+
+        s, part = self.shape, self.local.y
+        L = _lib.lib()
+        _lib.check(L.tlx_peer_publish(self.world, self.rank, self.peer.ptrs, s.positions, s.hidden, ops._ptr(part),
+                                      s.hidden, ops._stream(part)), "peer_publish")
+        _lib.check(L.tlx_peer_finish(self.world, self.rank, self.peer.ptrs, s.positions, s.hidden, None, 0,
+                                     ops._ptr(self.y), s.hidden, ops._ptr(self.finish_err), ops._stream(part)),
+                   "peer_finish")
+
+    def release(self):
+        """Drop the graph, then unmap / free the peer buffers (collective)."""
+        self.graph = None
+        torch.cuda.synchronize()
+        if self.peer is not None:
+            self.peer.close(self.group)
+            self.peer = None
 
     def set_inputs(self, h, hres=None):
         self.local.set_inputs(h, hres if self.rank == 0 else None)
