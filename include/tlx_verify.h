@@ -387,7 +387,7 @@ int tlx_acceptsel11k_flip(uint64_t* tab, const int32_t* m_slot, int n_blocks, vo
  * combined (pass the shared expert and hres on one rank only); summing y over the
  * ranks gives the full layer.  kvalues = the 16 IQ4_NL levels (gguf-py table).
  * The workspace (tlx_moe_workspace_bytes) must be zero-filled once before first
- * use; its counters re-arm themselves.  Three launches, no host sync, no allocation. */
+ * use; its counters re-arm themselves.  Four launches, no host sync, no allocation. */
 size_t tlx_moe_workspace_bytes(int p, int n_experts, int hidden, int inner);
 int tlx_moe_route(const float* w_router, const float* w_shared_gate, const void* h, int64_t ldh, int p,
                   int n_experts, int hidden, int inner, int expert_begin, int expert_end, int with_shared,

@@ -1,5 +1,5 @@
 // MoE verify layer (P <= 8 positions) on B200: router, routed + shared IQ4_XS
-// experts, combine.  Three launches chained with programmatic dependent launch:
+// experts, combine.  Four launches chained with programmatic dependent launch:
 //
 //   moe_router_kernel   logits = W_r h (fp32) for all experts plus the shared-expert
 //                       gate row (one warp per row), and h staged as the fp16
@@ -12,11 +12,12 @@
 //                       then the shared expert.  All CTAs compute the same list (no
 //                       serial step); CTA 0 publishes it.  Then per (slot, 16-row
 //                       tile): gate and up for the slot's positions, act = silu(g) u
-//                       in fp32 with a running max |act| per (position, expert) pair;
-//                       the last tile of a slot turns the slot's act into the fp16
-//                       activation image of the down projection with one power-of-two
-//                       scale per pair (act can exceed the fp16 range; the scale keeps
-//                       max |act| at 2^14).
+//                       in fp32 into the workspace.
+//   moe_act_image_kernel  one CTA per (position, expert) pair: the pair's act as the
+//                       fp16 activation image of the down projection with one
+//                       power-of-two scale per pair (act can exceed the fp16 range; the
+//                       scale keeps max |act| at 2^14), built once for every down CTA,
+//                       which bulk-copies it into shared memory.
 //   moe_down_kernel     per (slot, 16-row tile of the hidden dim): down over act into
 //                       fp32 parts[pair][row] (scale undone exactly); the last slot to
 //                       finish a tile combines it:
@@ -129,6 +130,8 @@ struct MoeParams {
   uint2* ximg;     // [H/256][P][68]
   float* actf;     // [9P][I] fp32 act
   float* parts;    // [9P][H]
+  uint2* aimg;     // [I/256][9P][68] fp16 act image of the down projection
+  float* ainv;     // [9P] the image's power-of-two scale per pair (act = image * ainv)
 };
 
 // ---- activation image (IQ4 k order) ----
@@ -765,13 +768,52 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_gate_up_kernel(const Mo
   }
 }
 
+// ------------------------------------------------------------------ act image kernel
+// The down projection's B operand, built once per layer instead of in every down CTA:
+// one CTA per (position, expert) pair takes the pair's fp32 act row, its max |act|,
+// a power-of-two scale that keeps it at <= 2^14 (the synthetic act exceeds the fp16
+// range; the scale is exact and undone on the fp32 result), and writes the fp16 image
+// entries (the IQ4 k order above) and the scale to the workspace.  Entry (m, q) of
+// block bi is written by one thread from two float2 loads; a warp's loads cover two
+// contiguous 256-byte runs of the row.
+__global__ void __launch_bounds__(128) moe_act_image_kernel(const MoeParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ float red[4];
+  const int pair = blockIdx.x, npair = 9 * p.P, I = p.I, nbi = I >> 8;
+  const float* a = p.actf + static_cast<int64_t>(pair) * I;
+  float mx = 0.f;
+  for (int i = threadIdx.x * 4; i < I; i += blockDim.x * 4) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(a + i));
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  int ex = 0;
+  if (mx > 0.f && mx == mx) frexpf(mx, &ex);
+  const float inv = ldexpf(1.0f, ex - 14);
+  const float scl = 1.0f / inv;  // exact: a power of two
+  if (threadIdx.x == 0) p.ainv[pair] = inv;
+  for (int e = threadIdx.x; e < nbi * 64; e += blockDim.x) {
+    const int m = e & 15, q = (e >> 4) & 3, bi = e >> 6;
+    const int k0 = 256 * bi + 64 * q + 32 * (m >> 3) + 2 * (m & 7);
+    const float2 lo = __ldcg(reinterpret_cast<const float2*>(a + k0));
+    const float2 hi = __ldcg(reinterpret_cast<const float2*>(a + k0 + 16));
+    p.aimg[(bi * npair + pair) * kRow + m * 4 + q] =
+        make_uint2(f32_to_f16_bits(lo.x * scl) | (static_cast<uint32_t>(f32_to_f16_bits(hi.x * scl)) << 16),
+                   f32_to_f16_bits(lo.y * scl) | (static_cast<uint32_t>(f32_to_f16_bits(hi.y * scl)) << 16));
+  }
+}
+
 // --------------------------------------------------------------- down + combine kernel
 __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ SlotCache sc;
   __shared__ float s_inv[9 * kMaxPos];
   __shared__ float s_gate[9 * kMaxPos];
-  __shared__ uint32_t s_max[9 * kMaxPos];  // max |act| bits per pair
   const int P = p.P, S = p.stages, I = p.I;
   const int nbi = I >> 8, tpd = p.H >> 4;
   const int npair = 9 * P;
@@ -784,19 +826,25 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
   R.ring = smem + L.ring + static_cast<uint32_t>(warp * S) * kChunk;
   R.bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * S;
   R.S = S;
+  uint64_t* ibar = reinterpret_cast<uint64_t*>(smem + L.bars) + kExpWarps * S;
 
   build_lut(smem, p.kvalues);
   if (lane == 0)
     for (int s = 0; s < S; ++s) mbar_init(&R.bars[s], 1);
+  if (threadIdx.x == 0) mbar_init(ibar, 1);
   mbar_fence_init();
-
-  for (int i = threadIdx.x; i < npair; i += blockDim.x) s_max[i] = 0u;
   __syncthreads();
 
   griddep_wait();
   griddep_launch_dependents();
-  // everything the prologue reads from the earlier kernels is loaded in one round trip:
-  // the slot list, each pair's combine weight, and the first act loads
+  // the act image, built once for all CTAs by moe_act_image_kernel: bulk copies into
+  // shared memory while the slot list and the combine weights are loaded
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(ibar, img_bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.aimg);
+    for (uint32_t off = 0; off < img_bytes; off += 32768u)
+      bulk_g2s(reinterpret_cast<uint8_t*>(as) + off, src + off, std::min(32768u, img_bytes - off), ibar);
+  }
   load_slots(p.meta, sc);
   for (int i = threadIdx.x; i < npair; i += blockDim.x) {
     // combine weight: the router gate of a routed pair whose expert is this rank's,
@@ -810,56 +858,7 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
       gw = __ldcg(&p.meta->sg[i - kTopK * P]);
     }
     s_gate[i] = gw;
-  }
-  const int n4 = npair * (I >> 2);
-  constexpr int kAct = 12;  // float4 act loads in flight per thread
-  const int round = kAct * static_cast<int>(blockDim.x);
-  float4 v[kAct];
-  auto load_act = [&](int i0) {
-#pragma unroll
-    for (int j = 0; j < kAct; ++j) {
-      const int i = i0 + j * static_cast<int>(blockDim.x);
-      v[j] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(p.actf) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  // max |act| per pair: a warp's 32 float4 lie in one pair (I / 4 is a multiple of 32)
-  auto max_act = [&](int i0) {
-#pragma unroll
-    for (int j = 0; j < kAct; ++j) {
-      const int i = i0 + j * static_cast<int>(blockDim.x);
-      float m = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0 && i < n4) atomicMax(&s_max[i / (I >> 2)], __float_as_uint(m));
-    }
-  };
-  // act image with one power-of-two scale per pair (max |act| * scale <= 2^14)
-  auto convert_act = [&](int i0) {
-#pragma unroll
-    for (int j = 0; j < kAct; ++j) {
-      const int i = i0 + j * static_cast<int>(blockDim.x);
-      if (i < n4) {
-        const int pair = i / (I >> 2), k = (i - pair * (I >> 2)) * 4;
-        const float scl = 1.0f / s_inv[pair];  // exact: a power of two
-        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          // position of k + e in the image: block, mma m, quarter q, half within the entry
-          const int kk = k + e, bi = kk >> 8, kin = kk & 255, q4 = kin >> 6, r = kin & 63;
-          const int m = 8 * (r >> 5) + ((r & 15) >> 1), pos = 2 * (r & 1) + ((r >> 4) & 1);
-          reinterpret_cast<uint16_t*>(as + (bi * npair + pair) * kRow + m * 4 + q4)[pos] =
-              f32_to_f16_bits(vv[e] * scl);
-        }
-      }
-    }
-  };
-  // with one round of loads (P <= 5 at I = 512) the act stays in registers; more
-  // positions take a second pass over the act for the conversion
-  load_act(threadIdx.x);
-  max_act(threadIdx.x);
-  for (int i0 = threadIdx.x + round; i0 < n4; i0 += round) {
-    load_act(i0);
-    max_act(i0);
+    s_inv[i] = __ldcg(p.ainv + i);
   }
   __syncthreads();
   const int n_slots = sc.n_slots;
@@ -869,6 +868,7 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
       const int t = i / p.H, r = i - t * p.H;
       p.y[t * p.ldy + r] = p.hres ? p.hres[t * p.ldr + r] : 0.f;
     }
+    mbar_wait_bounded(ibar, 0, threadIdx.x == 0 ? p.err : nullptr);  // the image copy lands before exit
     return;
   }
   const int n_items = n_slots * tpd;
@@ -887,27 +887,11 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
     b0 = (e >= 0 ? p.down + static_cast<int64_t>(e) * p.dn_bytes : p.sdown) + static_cast<int64_t>(tau) * nbi * kChunk;
     b1 = b0;
   };
-  // weights do not depend on act: start streaming before the image is built
+  // weights do not depend on act: start streaming, then wait for the image
   if (lane == 0) ring_issue(R, base_of);
-  for (int i = threadIdx.x; i < npair; i += blockDim.x) {
-    const float mx = __uint_as_float(s_max[i]);
-    int ex = 0;
-    if (mx > 0.f && mx == mx) frexpf(mx, &ex);
-    s_inv[i] = ldexpf(1.0f, ex - 14);
-  }
-  __syncthreads();
-  if (n4 <= round) {
-    convert_act(threadIdx.x);
-  } else {
-    for (int i0 = threadIdx.x; i0 < n4; i0 += round) {
-      load_act(i0);
-      convert_act(i0);
-    }
-  }
-  __syncthreads();
+  bool failed = !mbar_wait_bounded(ibar, 0, threadIdx.x == 0 ? p.err : nullptr);
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
   const int g = lane >> 2, qq = lane & 3;
-  bool failed = false;
   for (int item = i_first; item < n_items && !failed; item += R.step) {
     const int u = item / tpd, tau = item - u * tpd;
     const int cnt = sc.count[u];
@@ -995,7 +979,7 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
 
 // ------------------------------------------------------------------------------ host
 struct WsLayout {
-  size_t meta, logits, cnt, err, ximg, actf, parts, total;
+  size_t meta, logits, cnt, err, ximg, actf, parts, aimg, ainv, total;
 };
 
 inline size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -1022,6 +1006,10 @@ WsLayout ws_layout(int P, int E, int H, int I) {
   o = up256(o + static_cast<size_t>(9 * P) * I * 4);
   w.parts = o;
   o = up256(o + static_cast<size_t>(9 * P) * H * 4);
+  w.aimg = o;
+  o = up256(o + static_cast<size_t>(I / 256) * (9 * P) * kRowBytes);
+  w.ainv = o;
+  o = up256(o + static_cast<size_t>(9 * P) * 4);
   w.total = o;
   return w;
 }
@@ -1079,6 +1067,8 @@ int setup(const MoeParams& in, int P, int E, int H, int I, int e0, int e1, void*
   p.ximg = reinterpret_cast<uint2*>(b + w.ximg);
   p.actf = reinterpret_cast<float*>(b + w.actf);
   p.parts = reinterpret_cast<float*>(b + w.parts);
+  p.aimg = reinterpret_cast<uint2*>(b + w.aimg);
+  p.ainv = reinterpret_cast<float*>(b + w.ainv);
   p.gu_bytes = static_cast<int64_t>(I / 16) * (H / 256) * kChunk;
   p.dn_bytes = static_cast<int64_t>(H / 16) * (I / 256) * kChunk;
   return TLX_OK;
@@ -1121,6 +1111,11 @@ int launch_experts(MoeParams p, cudaStream_t stream) {
     if (ensure_smem(reinterpret_cast<const void*>(moe_gate_up_kernel), smem, g_gate_up_smem)) return TLX_ERR_LAUNCH;
     const int rc = launch_ex(reinterpret_cast<const void*>(moe_gate_up_kernel), dim3(C), dim3(kExpWarps * 32), smem,
                              stream, p);
+    if (rc) return rc;
+  }
+  {
+    const int rc = launch_ex(reinterpret_cast<const void*>(moe_act_image_kernel), dim3(9 * p.P), dim3(128), 0, stream,
+                             p);
     if (rc) return rc;
   }
   {

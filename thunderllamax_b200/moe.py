@@ -5,8 +5,8 @@ experts (top-8, softmax gates over the 8, sigmoid shared-expert gate), the 8
 routed SiLU-gated IQ4_XS experts (2048 -> 512 -> 2048) plus the shared expert,
 and the gated combine with the residual.  This is the reference's MoE layer
 sequence rt8e256 -> shexp8 -> gx8e256up4 -> gx8e256dn -> cmbz2048
-(engine/mm/MM_P7_lib.py:505-511), run as three launches of libtlx_b200
-(``tlx_moe_verify``): router, expert gate/up, expert down + combine.
+(engine/mm/MM_P7_lib.py:505-511), run as four launches of libtlx_b200
+(``tlx_moe_verify``): router, expert gate/up, act image, expert down + combine.
 
 Expert parallelism: a rank passes its expert range [e0, e1); only those experts
 are read and combined (the shared expert and the residual on rank 0), and the
@@ -137,7 +137,7 @@ def moe_verify(shape: MoeShape, w: dict, h: torch.Tensor, ws: MoeWorkspace, y: t
 class MoeVerifyStep:
     """One MoE verify layer on one GPU (or one rank's expert range), graph-captured."""
 
-    LAUNCHES_PER_STEP = 3
+    LAUNCHES_PER_STEP = 4
 
     def __init__(self, shape: MoeShape = MoeShape(), seed: int = 0, host: dict = None, e0: int = 0, e1: int = None,
                  shared: bool = True):
