@@ -334,7 +334,25 @@ __device__ void select_experts(const MoeParams& p, uint8_t* scratch, SlotCache& 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   float* lgs = reinterpret_cast<float*>(scratch);
   uint32_t* info = reinterpret_cast<uint32_t*>(lgs + P * (E + 1));
-  for (int i = threadIdx.x; i < P * (E + 1); i += blockDim.x) lgs[i] = __ldcg(p.logits + i);
+  {
+    // every logit is loaded before any is stored: one L2 round trip for up to
+    // 4 x blockDim logits (the P <= 8 x 1025 of the largest shape take two)
+    constexpr int kLd = 4;
+    const int n = P * (E + 1);
+    for (int base = threadIdx.x; base < n; base += kLd * blockDim.x) {
+      float v[kLd];
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int i = base + j * static_cast<int>(blockDim.x);
+        v[j] = i < n ? __ldcg(p.logits + i) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kLd; ++j) {
+        const int i = base + j * static_cast<int>(blockDim.x);
+        if (i < n) lgs[i] = v[j];
+      }
+    }
+  }
   for (int i = threadIdx.x; i < E; i += blockDim.x) info[i] = 0u;
   __syncthreads();
   MoeMeta* mt = p.meta;
@@ -948,27 +966,41 @@ __global__ void __launch_bounds__(kExpWarps * 32, 1) moe_down_kernel(const MoePa
     while (last) {
       const int tau = (base + (__ffs(last) - 1) * R.step) % tpd;
       last &= last - 1;
-      // 16 rows x P positions per tile; each output's nine parts are loaded together,
-      // then summed in a fixed order (routed ranks 0..7, then the shared expert)
+      // 16 rows x P positions per tile; every output's nine parts (and the residual)
+      // are loaded for all of the lane's outputs before any is summed (one L2 round
+      // trip per tile), then summed in a fixed order (routed ranks 0..7, then the
+      // shared expert)
+      constexpr int kIt = (16 * kMaxPos + 31) / 32, kBatch = 2;
 #pragma unroll 1
-      for (int it = 0; it < (16 * kMaxPos + 31) / 32; ++it) {
-        const int idx = lane + 32 * it;
-        if (idx < 16 * P) {
-          const int t = idx >> 4, row = tau * 16 + (idx & 15);
-          float pv[kTopK + 1];
+      for (int it0 = 0; it0 < kIt && 32 * it0 < 16 * P; it0 += kBatch) {
+        float pv[kBatch][kTopK + 2];
 #pragma unroll
-          for (int r = 0; r < kTopK; ++r) pv[r] = __ldcg(p.parts + static_cast<int64_t>(t * kTopK + r) * p.H + row);
-          pv[kTopK] = __ldcg(p.parts + static_cast<int64_t>(kTopK * P + t) * p.H + row);
-          const float hr = p.hres ? p.hres[t * p.ldr + row] : 0.f;
-          float a = 0.f;
+        for (int j = 0; j < kBatch; ++j) {
+          const int idx = lane + 32 * (it0 + j);
+          if (idx < 16 * P) {
+            const int t = idx >> 4, row = tau * 16 + (idx & 15);
 #pragma unroll
-          for (int r = 0; r < kTopK; ++r) {
-            const float gw = s_gate[t * kTopK + r];
-            if (gw != 0.f) a += gw * pv[r];
+            for (int r = 0; r < kTopK; ++r)
+              pv[j][r] = __ldcg(p.parts + static_cast<int64_t>(t * kTopK + r) * p.H + row);
+            pv[j][kTopK] = __ldcg(p.parts + static_cast<int64_t>(kTopK * P + t) * p.H + row);
+            pv[j][kTopK + 1] = p.hres ? p.hres[t * p.ldr + row] : 0.f;
           }
-          const float gs = s_gate[kTopK * P + t];
-          if (gs != 0.f) a += gs * pv[kTopK];
-          p.y[t * p.ldy + row] = hr + a;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int idx = lane + 32 * (it0 + j);
+          if (idx < 16 * P) {
+            const int t = idx >> 4, row = tau * 16 + (idx & 15);
+            float a = 0.f;
+#pragma unroll
+            for (int r = 0; r < kTopK; ++r) {
+              const float gw = s_gate[t * kTopK + r];
+              if (gw != 0.f) a += gw * pv[j][r];
+            }
+            const float gs = s_gate[kTopK * P + t];
+            if (gs != 0.f) a += gs * pv[j][kTopK];
+            p.y[t * p.ldy + row] = pv[j][kTopK + 1] + a;
+          }
         }
       }
       if (lane == 0) p.cnt[tau] = 0u;
