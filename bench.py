@@ -1020,8 +1020,8 @@ def profile_gemv(which: str, vocab: int, ffn: int) -> int:
 
 def profile_layer(which: str) -> int:
     """A small driver for ncu: four eager launches of the MoE verify layer (config 4:
-    router, gate/up, down per layer) or of the prefill FFN (config 5: token staging,
-    gate/up, act staging, down), seeded as in the bench, then exit."""
+    router, gate/up, act image, down per layer) or of the prefill FFN (config 5: token
+    staging, gate/up, act staging, down), seeded as in the bench, then exit."""
     import numpy as np
     import torch
     from thunderllamax_b200 import synth
