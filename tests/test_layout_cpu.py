@@ -39,6 +39,42 @@ def test_error_strings_and_host_argument_checks():
     assert lib.tlx_gemv_workspace_bytes(0, 14, 16, 256, 6, 0) == 0     # fp32 x: m <= 5
 
 
+def test_peer_and_slot_table_host_checks():
+    # the peer exchange and GDN slot-table entry points reject bad arguments on the
+    # host, before any CUDA call (no GPU needed)
+    import ctypes
+
+    lib = _lib.lib()
+    err_null, err_shape, err_align = -8, -1, -2
+    # slot table: 2 x 12 eight-byte addresses per GDN block
+    assert lib.tlx_gdn_slots_bytes(48) == 48 * 2 * 12 * 8
+    assert lib.tlx_gdn_slots_bytes(0) == 0 and lib.tlx_gdn_slots_bytes(-3) == 0
+    six, seven = (ctypes.c_void_p * 6)(*([8] * 6)), (ctypes.c_void_p * 7)(*([8] * 7))
+    assert lib.tlx_gdn_slots_init(None, 8, 8, seven, six, 48, 64, 32, None) == err_null
+    assert lib.tlx_gdn_slots_init(8, 8, 8, seven, six, 0, 64, 32, None) == err_shape
+    assert lib.tlx_gdn_slots_init(12, 8, 8, seven, six, 48, 64, 32, None) == err_align    # table not 8-byte aligned
+    seven_null = (ctypes.c_void_p * 7)(*([8] * 6 + [None]))
+    assert lib.tlx_gdn_slots_init(8, 8, 8, seven_null, six, 48, 64, 32, None) == err_null
+    assert lib.tlx_acceptsel11k_flip(None, 8, 48, None) == err_null
+    assert lib.tlx_acceptsel11k_flip(8, None, 48, None) == err_null
+    assert lib.tlx_acceptsel11k_flip(8, 8, 0, None) == err_shape
+    assert lib.tlx_acceptsel11k_flip(12, 8, 48, None) == err_align
+    # peer exchange: world in 2..8, rank in range, buffers 256-byte aligned, m <= 16
+    assert lib.tlx_peer_buffer_bytes(1, 11, 5120) == 0 and lib.tlx_peer_buffer_bytes(9, 11, 5120) == 0
+    assert lib.tlx_peer_buffer_bytes(2, 17, 5120) == 0
+    assert lib.tlx_peer_buffer_bytes(8, 11, 5120) == 4096 + 2 * 11 * 5120 * 4
+    two = (ctypes.c_void_p * 2)(256, 512)
+    misaligned = (ctypes.c_void_p * 2)(256, 520)
+    assert lib.tlx_peer_publish(2, 0, None, 5, 2048, 256, 2048, None) == err_null
+    assert lib.tlx_peer_publish(1, 0, two, 5, 2048, 256, 2048, None) == err_shape       # world < 2
+    assert lib.tlx_peer_publish(2, 2, two, 5, 2048, 256, 2048, None) == err_shape       # rank out of range
+    assert lib.tlx_peer_publish(2, 0, two, 17, 2048, 256, 2048, None) == err_shape      # m > 16
+    assert lib.tlx_peer_publish(2, 0, two, 5, 2048, 256, 1024, None) == err_shape       # row stride < ny
+    assert lib.tlx_peer_publish(2, 0, two, 5, 2048, None, 2048, None) == err_null
+    assert lib.tlx_peer_publish(2, 0, misaligned, 5, 2048, 256, 2048, None) == err_align
+    assert lib.tlx_peer_finish(2, 0, misaligned, 5, 2048, None, 0, 256, 2048, 256, None) == err_align
+
+
 @pytest.mark.parametrize("qtype,gen,bb", [("q6_k", synth.q6k_blocks, 210), ("iq3_xxs", synth.iq3xxs_blocks, 98),
                                           ("iq4_xs", synth.iq4xs_blocks, 136), ("q4_k", synth.q4k_blocks, 144),
                                           ("q5_k", synth.q5k_blocks, 176), ("q8_0", synth.q8_0_blocks, 272)])
