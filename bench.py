@@ -394,11 +394,41 @@ def measure_prefill(args, torch, weights):
     except Exception:
         peak, kind = 1590.0, "fallback"
     tflops = shape.flops() / (ms * 1e-3) / 1e12
-    return {"workload": "prefill FFN: 2048 tokens, IQ3_XXS gate/up 5120->17408 (+SiLU) -> Q6_K down 17408->5120, "
-                        "fp16 tcgen05 with fp32 TMEM accumulators",
-            "ms_per_step": round(ms, 4), "flops_per_step": shape.flops(), "tflops": round(tflops, 1),
-            "peak_tflops": peak, "peak_kind": kind, "frac_of_peak": round(tflops / peak, 4),
-            "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
+    out = {"workload": "prefill FFN: 2048 tokens, IQ3_XXS gate/up 5120->17408 (+SiLU) -> Q6_K down 17408->5120, "
+                       "fp16 tcgen05 with fp32 TMEM accumulators",
+           "ms_per_step": round(ms, 4), "flops_per_step": shape.flops(), "tflops": round(tflops, 1),
+           "peak_tflops": peak, "peak_kind": kind, "frac_of_peak": round(tflops / peak, 4),
+           "launches_per_step": 3, "err_word": [step.ws.error(), step.ws_down.error()]}
+
+    # the W4A8 tier in place of the fp16 gate/up: fp16 tokens -> int8 (quantiser), then
+    # the gate/up on the linearised codebook (token staging + the tcgen05 contraction)
+    gu_flops = 2 * shape.tokens * shape.dim * shape.ffn * 2
+    x16 = step.x.to(torch.float16)
+    xq = torch.empty((shape.tokens, shape.dim), dtype=torch.int8, device="cuda")
+    sx = torch.empty((shape.tokens, shape.dim // 128), dtype=torch.float32, device="cuda")
+    rs = torch.empty_like(sx, dtype=torch.int32)
+    lut = prefill.lut8()
+
+    def fp16_gate_up():
+        prefill.gate_up(shape.ffn_q, step.w["gate"], step.w["up"], step.x, shape.ffn, step.ws, act=step.act)
+
+    def w4a8_gate_up():
+        prefill.act_quant_q8(x16, xq=xq, sx=sx, rs=rs)
+        prefill.w4a8_gate_up(step.w["gate"], step.w["up"], xq, sx, shape.ffn, step.ws, act=step.act, lut=lut)
+
+    for fn in (fp16_gate_up, w4a8_gate_up):
+        for _ in range(3):
+            fn()
+    ms16 = time_graph(fp16_gate_up, n, torch)
+    ms8 = time_graph(w4a8_gate_up, n, torch)
+    out["w4a8_gate_up"] = {
+        "workload": "gate/up only (5120 -> 17408 x2 + SiLU, 2048 tokens): W4A8 tier (int8 tokens, linearised "
+                    "IQ3_XXS levels; quantiser + token staging + tcgen05 contraction) against the fp16 tier "
+                    "(bf16 -> fp16 staging + the same contraction)",
+        "ms": round(ms8, 4), "tflops": round(gu_flops / (ms8 * 1e-3) / 1e12, 1),
+        "fp16_tier_ms": round(ms16, 4), "fp16_tier_tflops": round(gu_flops / (ms16 * 1e-3) / 1e12, 1),
+        "launches": 3, "err_word": step.ws.error()}
+    return out
 
 
 def measure_moe_exchange(torch, dist, shape, ws, max_over_ranks, reps: int = 20):

@@ -432,6 +432,31 @@ int tlx_prefill_ffn_gate_up(int qtype, const void* w_gate, const void* w_up, con
 int tlx_prefill_gemm(int qtype, const void* w, const uint32_t* grid, const void* x, int x_dtype, int64_t ldx, int m,
                      int64_t n_rows, int64_t k, float* y, int64_t ldy, void* ws, size_t ws_bytes, void* stream);
 
+/* ---- W4A8 prefill tier (int8 tokens x linearised IQ3_XXS levels) ------------------
+ * tlx_act_quant_q8: fp16 x[m][k] (k % 128 == 0, ldx % 4 == 0) -> xq int8 [m][ldq],
+ * sx fp32 [m][k/128], rs int32 [m][k/128].  Per (token, 128-k chunk):
+ * s = max(max|x|, 1e-6) * (1/127) in fp32, xq = clamp(rint(x / s), -127, 127) (IEEE
+ * quotient, ties to even), rs = sum of the stored xq; bit-identical to the reference
+ * quantiser.  Replaces p8q8x (engine/pfk_q8.cu:24-59, launched at
+ * engine/pf_prefill.py:1156).
+ * tlx_prefill_w4a8_gate_up: act[t][r] = silu(g) * u (fp32) with g = sum_k Wg[r][k] *
+ * xq[t][k] * sx[t][k/128] on the weights' linearised codebook: lut8[4 i + j] is the
+ * level (0..15) of IQ3_XXS grid entry i, magnitude j, and a 32-weight group's scale is
+ * d * (0.5 + s) * 0.5 * 4.0507 (the reference builds lut8 as
+ * clip(rint(grid / 4.0507), 0, 15), engine/pf_prefill.py:994).  w_gate / w_up are the
+ * tiled IQ3_XXS weights of tlx_prefill_ffn_gate_up (no second copy of the weights);
+ * n_rows % 128 == 0, k % 256 == 0, ldq % 8 == 0.  The workspace is the prefill
+ * workspace (tlx_prefill_workspace_bytes(m, k), zeroed once).  The contraction runs on
+ * the fp16 tcgen05 path with the quantised operands (each level * (2s+1) exact in fp16,
+ * one fp16 rounding per weight and per token value); the output is fp32 where the
+ * reference writes fp16.  Replaces p8w4ffn7 (engine/p8_w4ffn7.cu:118-255, launched at
+ * engine/pf_prefill.py:1157). */
+int tlx_act_quant_q8(const void* x, int64_t ldx, int m, int64_t k, int8_t* xq, int64_t ldq, float* sx, int32_t* rs,
+                     void* stream);
+int tlx_prefill_w4a8_gate_up(const void* w_gate, const void* w_up, const int8_t* lut8, const int8_t* xq, int64_t ldq,
+                             const float* sx, int m, int64_t n_rows, int64_t k, float* act, int64_t ld_act, void* ws,
+                             size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

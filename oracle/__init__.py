@@ -25,3 +25,4 @@ from .path import (  # noqa: F401
     router_top8, moe_verify_f64, silu_f64, min_top2_gap,
 )
 from .attention import attn_pre, attn_decode, rope_freqs, dequant_cache  # noqa: F401,E402
+from .w4a8 import act_quant_q8, dequant_iq3xxs_lin, dequant_tokens, lut8_levels, w4a8_gate_up_f64  # noqa: F401,E402

@@ -48,6 +48,17 @@ ATTN_KERNELS = [
                                  f"-DCH={ATTN_CTX // ATTN_S}", "-DUNROLL=4"]),
 ]
 
+# the W4A8 prefill pair with the compile-time shapes the reference builds it with
+# (engine/build_p8w4.py:33-38): p8q8x reads [M][5120] fp16 rows and writes [M][5120]
+# int8 plus [M][40] scales and sums, M = its grid; p8w4ffn7 reads two weight planes
+# of [17408 / 8][40][32] 16-byte units, [M][5120] int8 and [M][40] scales, a
+# 1024-byte codebook, and writes [M][17408] fp16 for M = 64 * (grid / 272)
+W4A8_KERNELS = [
+    ("pfk_q8.cu", "p8q8x", ["-DKNAME=p8q8x", "-DKDIM=5120"]),
+    ("p8_w4ffn7.cu", "p8w4ffn7", ["-DKNAME=p8w4ffn7", "-DKDIM=5120", "-DNDIM=17408", "-DNTHR=256", "-DNTILE=64",
+                                  "-DKCH=128", "-DMTILE=64"]),
+]
+
 
 def _one_kernel(src: str, macro: str, out: str) -> str:
     """The file's preamble plus the one kernel whose name is `macro` (what the
@@ -71,7 +82,7 @@ def build(verbose: bool = False) -> list[str]:
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     os.makedirs(OUT, exist_ok=True)
     built = []
-    for rel, name, defs in [(r, n, []) for r, n in KERNELS] + ATTN_KERNELS:
+    for rel, name, defs in [(r, n, []) for r, n in KERNELS] + ATTN_KERNELS + W4A8_KERNELS:
         src = os.path.join(src_dir, rel.split(":")[0])
         if not os.path.exists(src):
             continue

@@ -50,3 +50,28 @@ def launch(name: str, grid: int, block: int, args, stream=None) -> None:
     err, = driver.cuLaunchKernel(fn, grid, 1, 1, block, 1, 1, 0, s, (tuple(vals), tuple(types)), 0)
     assert err == driver.CUresult.CUDA_SUCCESS, err
     torch.cuda.synchronize()
+
+
+def packed7_planes(raw, k: int):
+    """GGUF IQ3_XXS rows -> the packed7 units the reference's p8w4ffn7 reads
+    (layout of engine/pack_w7.py:1-20; pinned by tests/test_oracle_w4a8.py against
+    the reference's pack_tensor).  uint16 [n / 8][k / 128][32][8]: unit r * 4 + c of
+    chunk 2b + h (256-k block b, half h) holds, for row r of the 8-row group, the
+    four qs words 16h + 4c .. 16h + 4c + 3 of block b, then scale word 4h + c as two
+    halves, then d of block b, then zero."""
+    import numpy as np
+
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    n, nb = raw.shape[0], k // 256
+    assert n % 8 == 0
+    blk = raw.reshape(n // 8, 8, nb, 98)                               # [group, r, b, byte]
+    qs = np.ascontiguousarray(blk[..., 2:66]).view(np.uint16)          # [g, r, b, 32]
+    sc = np.ascontiguousarray(blk[..., 66:98]).view(np.uint32)         # [g, r, b, 8]
+    d = np.ascontiguousarray(blk[..., 0:2]).view(np.uint16)[..., 0]    # [g, r, b]
+    out = np.zeros((n // 8, nb, 2, 8, 4, 8), dtype=np.uint16)          # [g, b, h, r, c, slot]
+    out[..., 0:4] = qs.reshape(n // 8, 8, nb, 2, 4, 4).transpose(0, 2, 3, 1, 4, 5)
+    w = sc.reshape(n // 8, 8, nb, 2, 4).transpose(0, 2, 3, 1, 4)
+    out[..., 4] = (w & 0xFFFF).astype(np.uint16)
+    out[..., 5] = (w >> 16).astype(np.uint16)
+    out[..., 6] = d.transpose(0, 2, 1)[:, :, None, :, None]
+    return out.reshape(n // 8, 2 * nb, 32, 8)

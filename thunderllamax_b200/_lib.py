@@ -103,6 +103,9 @@ _SIGS = {
                                         c_vp, c_size, c_vp]),
     "tlx_prefill_gemm": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_int, c_i64, c_i64, c_vp, c_i64, c_vp,
                                  c_size, c_vp]),
+    "tlx_act_quant_q8": (c_int, [c_vp, c_i64, c_int, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "tlx_prefill_w4a8_gate_up": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_i64,
+                                         c_vp, c_size, c_vp]),
 }
 
 

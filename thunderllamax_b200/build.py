@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libtlx_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
-SOURCES = ["gemv.cu", "capi.cu", "moe.cu", "prefill.cu", "noalloc.cu", "lookup.cu", "attention.cu", "peer.cu"]
+SOURCES = ["gemv.cu", "capi.cu", "moe.cu", "prefill.cu", "noalloc.cu", "lookup.cu", "attention.cu", "peer.cu", "w4a8.cu"]
 
 
 def nvcc() -> str:

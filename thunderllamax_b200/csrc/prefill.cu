@@ -876,6 +876,15 @@ int run_prefill(int gate_up, int qt, const void* w0, const void* w1, const uint3
   } else {
     return TLX_ERR_DTYPE;
   }
+  return prefill_on_f16(gate_up, w0, w1, grid, xf16, ldx16, row_scale, m, n_rows, k, out, ldo, ws, ws_bytes, err,
+                        max_ctas, stream);
+}
+
+// the contraction on tokens already in fp16 (row_scale: the per-token power-of-two
+// factor of the staged rows, or nullptr); ws: the workspace after the error word
+int prefill_on_f16(int gate_up, const void* w0, const void* w1, const uint32_t* grid, const void* xf16,
+                   int64_t ldx16, const float* row_scale, int m, int64_t n_rows, int64_t k, void* out, int64_t ldo,
+                   void* ws, size_t ws_bytes, uint32_t* err, int max_ctas, cudaStream_t stream) {
   CUtensorMap map;
   if (!make_tok_map(&map, xf16, m, static_cast<int>(k), ldx16)) return TLX_ERR_ALIGN;
   PrefillParams p;

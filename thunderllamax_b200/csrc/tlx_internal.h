@@ -56,6 +56,17 @@ int stage_activations(const void* x, int x_dtype, int64_t ldx, int m, int64_t k,
 size_t gemv_counter_bytes(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas);
 // the CTA cap set by tlx_set_max_ctas (0 = one CTA per SM)
 int max_ctas_setting();
+
+// prefill contraction (prefill.cu).  Workspace after the error word: the fp16 token
+// image [m][k] (256-byte aligned end), one float scale per token, then the split region.
+size_t prefill_x_bytes(int m, int64_t k);
+size_t prefill_scale_offset(int m, int64_t k);
+// gate/up (gate_up = 1, IQ3_XXS tiles and a 256-entry grid table whose byte j of entry i
+// is magnitude j) or the Q6_K GEMM on tokens already in fp16 (xf16 [m][ldx16]; row_scale:
+// each token's power-of-two factor, or nullptr); shapes checked by the caller
+int prefill_on_f16(int gate_up, const void* w0, const void* w1, const uint32_t* grid, const void* xf16,
+                   int64_t ldx16, const float* row_scale, int m, int64_t n_rows, int64_t k, void* out, int64_t ldo,
+                   void* ws, size_t ws_bytes, uint32_t* err, int max_ctas, cudaStream_t stream);
 int gemv_plan_info(int epi, int qt, int64_t n_rows, int64_t k, int m, int x_dtype, int max_ctas, int32_t* info,
                    int n_info);
 

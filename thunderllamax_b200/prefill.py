@@ -95,6 +95,52 @@ def gemm(qtype, w: torch.Tensor, x: torch.Tensor, n_rows: int, ws: PrefillWorksp
     return y
 
 
+def lut8(device: str = "cuda") -> torch.Tensor:
+    """The W4A8 tier's linearised codebook (int8[1024]) resident on the device."""
+    from .tables import iq3xxs_levels_lut8
+
+    return torch.from_numpy(iq3xxs_levels_lut8().copy()).to(device)
+
+
+def act_quant_q8(x: torch.Tensor, xq: torch.Tensor = None, sx: torch.Tensor = None, rs: torch.Tensor = None):
+    """fp16 x[m, k] -> (xq int8 [m, k], sx fp32 [m, k/128], rs int32 [m, k/128]): per (token, 128-k
+    chunk) s = max(max|x|, 1e-6) / 127, xq = clamp(rint(x / s)), rs = sum of xq (reference p8q8x,
+    engine/pfk_q8.cu:24-59)."""
+    ops.require_device()
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype != torch.float16:
+        raise TLXError("x must be a row-major fp16 [tokens, k] tensor")
+    m, k = x.shape
+    if xq is None:
+        xq = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    if sx is None:
+        sx = torch.empty((m, k // 128), dtype=torch.float32, device=x.device)
+    if rs is None:
+        rs = torch.empty((m, k // 128), dtype=torch.int32, device=x.device)
+    rc = _lib.lib().tlx_act_quant_q8(ops._ptr(x), x.stride(0), m, k, ops._ptr(xq), xq.stride(0), ops._ptr(sx),
+                                     ops._ptr(rs), ops._stream(x))
+    check(rc, "act_quant_q8")
+    return xq, sx, rs
+
+
+def w4a8_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor, n_rows: int,
+                 ws: PrefillWorkspace, act: torch.Tensor = None, lut: torch.Tensor = None) -> torch.Tensor:
+    """act[t][r] = silu(g) * u in fp32 on int8 tokens (xq, sx from act_quant_q8) and the tiled IQ3_XXS
+    weights read through the linearised codebook (reference p8w4ffn7, engine/p8_w4ffn7.cu:118-255)."""
+    ops.require_device()
+    if xq.dim() != 2 or xq.stride(1) != 1 or xq.dtype != torch.int8:
+        raise TLXError("xq must be a row-major int8 [tokens, k] tensor")
+    m, k = xq.shape
+    if act is None:
+        act = torch.empty((m, n_rows), dtype=torch.float32, device=xq.device)
+    if lut is None:
+        lut = lut8(str(xq.device))
+    rc = _lib.lib().tlx_prefill_w4a8_gate_up(ops._ptr(w_gate), ops._ptr(w_up), ops._ptr(lut), ops._ptr(xq),
+                                             xq.stride(0), ops._ptr(sx), m, n_rows, k, ops._ptr(act), act.stride(0),
+                                             ops._ptr(ws.buf), ws.nbytes, ops._stream(xq))
+    check(rc, "prefill_w4a8_gate_up")
+    return act
+
+
 class PrefillFFN:
     """The config-5 FFN on one GPU: gate/up (+SiLU) then down, two launches (+ the
     bf16 -> fp16 token staging)."""

@@ -22,6 +22,18 @@ def iq3xxs_grid_u32() -> np.ndarray:
     return np.ascontiguousarray(g).view(np.uint32).reshape(256).copy()
 
 
+LEVEL_STEP = 4.0507  # W4A8 tier: grid magnitude ~= step * level (engine/p8_w4ffn7.cu:42)
+
+
+@functools.lru_cache(maxsize=None)
+def iq3xxs_levels_lut8() -> np.ndarray:
+    """int8[1024]: the W4A8 tier's linearised IQ3_XXS codebook, level
+    clip(rint(g / 4.0507), 0, 15) of grid entry i, magnitude j at [4 i + j]
+    (built by the reference at engine/pf_prefill.py:994)."""
+    g = iq3xxs_grid_u32().view(np.uint8).astype(np.float32)
+    return np.clip(np.rint(g / np.float32(LEVEL_STEP)), 0, 15).astype(np.int8)
+
+
 @functools.lru_cache(maxsize=None)
 def iq4nl_kvalues() -> np.ndarray:
     from gguf import quants
