@@ -1050,8 +1050,9 @@ def profile_gemv(which: str, vocab: int, ffn: int) -> int:
 
 def profile_layer(which: str) -> int:
     """A small driver for ncu: four eager launches of the MoE verify layer (config 4:
-    router, gate/up, act image, down per layer) or of the prefill FFN (config 5: token
-    staging, gate/up, act staging, down), seeded as in the bench, then exit."""
+    router, gate/up, act image, down per layer), of the prefill FFN (config 5: token
+    staging, gate/up, act staging, down) or of the W4A8 gate/up (token quantiser,
+    staging, gate/up), seeded as in the bench, then exit."""
     import numpy as np
     import torch
     from thunderllamax_b200 import synth
@@ -1065,7 +1066,7 @@ def profile_layer(which: str) -> int:
         h = torch.from_numpy(synth.bf16_normal(rng, (s.positions, s.hidden)).view(np.int16)).cuda()
         step.set_inputs(h.view(torch.bfloat16), torch.zeros((s.positions, s.hidden), device="cuda"))
         errs = lambda: [step.ws.error()]                            # noqa: E731
-    else:
+    elif which == "prefill":
         from thunderllamax_b200 import prefill
 
         step = prefill.PrefillFFN(prefill.PrefillShape(), seed=0)
@@ -1073,6 +1074,25 @@ def profile_layer(which: str) -> int:
         step.x.copy_(torch.from_numpy(synth.bf16_normal(rng, (s.tokens, s.dim)).view(np.int16)).cuda()
                      .view(torch.bfloat16))
         errs = lambda: [step.ws.error(), step.ws_down.error()]     # noqa: E731
+    else:
+        from thunderllamax_b200 import prefill
+
+        ffn = prefill.PrefillFFN(prefill.PrefillShape(), seed=0)
+        s = ffn.shape
+        x16 = torch.from_numpy(synth.bf16_normal(rng, (s.tokens, s.dim)).view(np.int16)).cuda() \
+            .view(torch.bfloat16).to(torch.float16)
+        xq = torch.empty((s.tokens, s.dim), dtype=torch.int8, device="cuda")
+        sx = torch.empty((s.tokens, s.dim // 128), dtype=torch.float32, device="cuda")
+        rs = torch.empty_like(sx, dtype=torch.int32)
+        lut = prefill.lut8()
+
+        class W4a8GateUp:
+            def launch(self):
+                prefill.act_quant_q8(x16, xq=xq, sx=sx, rs=rs)
+                prefill.w4a8_gate_up(ffn.w["gate"], ffn.w["up"], xq, sx, s.ffn, ffn.ws, act=ffn.act, lut=lut)
+
+        step = W4a8GateUp()
+        errs = lambda: [ffn.ws.error()]                              # noqa: E731
     for _ in range(4):
         step.launch()
     torch.cuda.synchronize()
@@ -1117,8 +1137,8 @@ def main():
                     help="profiling case: one warm-up and one tlx_attn_split launch at context POS, then exit")
     ap.add_argument("--profile-gemv", choices=["gate_up", "down", "head"], default=None,
                     help="profiling case: one verify GEMV alone (a full step first, then four launches), then exit")
-    ap.add_argument("--profile-layer", choices=["moe", "prefill"], default=None,
-                    help="profiling case: four eager MoE-layer or prefill-FFN launches, then exit")
+    ap.add_argument("--profile-layer", choices=["moe", "prefill", "w4a8"], default=None,
+                    help="profiling case: four eager MoE-layer, prefill-FFN or W4A8 gate/up launches, then exit")
     ap.add_argument("--vocab", type=int, default=151936, help="head rows (profiling cases only)")
     ap.add_argument("--ffn", type=int, default=17408, help="FFN rows, a multiple of 256 (profiling cases only)")
     args = ap.parse_args()
