@@ -2,7 +2,7 @@
 // codebook, the reference's p8q8x + p8w4ffn7 pair (engine/pfk_q8.cu:24-59,
 // engine/p8_w4ffn7.cu:4-12, 118-255; wired at engine/pf_prefill.py:1155-1158).
 //
-// tlx_act_quant_q8 restates the token quantiser bit for bit: one warp per (token,
+// tlx_act_quant_q8 restates the token quantiser bit for bit: half a warp per (token,
 // 128-k chunk), s = max(max|x|, 1e-6) * (1/127) in fp32, q = clamp(rint(x / s)),
 // the chunk's integer sum.
 //
@@ -33,38 +33,71 @@ namespace {
 constexpr int kChunk = 128;           // tokens are quantised per 128-k chunk
 constexpr float kLevelStep = 4.0507f;  // grid magnitude ~= step * level (engine/p8_w4ffn7.cu:42)
 
-// one warp per (token, chunk): lane l holds k = 4l .. 4l+3 of the chunk
+// Half a warp per (token, chunk): lane l of the half holds k = 8l .. 8l+7 (two 8-byte
+// loads); each warp takes 2 * kQuantSteps chunks per pass and issues all their loads
+// before the first reduction, so enough bytes are in flight to stream HBM.  The
+// max and the integer sum do not depend on the reduction order.
+constexpr int kQuantSteps = 2;
+
 __global__ void __launch_bounds__(256) act_quant_q8_kernel(const __half* __restrict__ x, int64_t ldx, int m, int nch,
                                                            int8_t* __restrict__ xq, int64_t ldq,
                                                            float* __restrict__ sx, int32_t* __restrict__ rs) {
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
   const int64_t units = static_cast<int64_t>(m) * nch;
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); u < units;
-       u += static_cast<int64_t>(gridDim.x) * 8) {
-    const int t = static_cast<int>(u / nch);
-    const int c = static_cast<int>(u - static_cast<int64_t>(t) * nch);
-    const uint2 h = *reinterpret_cast<const uint2*>(x + t * ldx + c * kChunk + 4 * lane);
-    const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-    const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
-    const float f[4] = {f01.x, f01.y, f23.x, f23.y};
-    float am = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
+  const int64_t per_pass = static_cast<int64_t>(gridDim.x) * 8 * (2 * kQuantSteps);
+  for (int64_t base = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (2 * kQuantSteps); base < units;
+       base += per_pass) {
+    uint2 h[kQuantSteps][2];
+    int t[kQuantSteps], c[kQuantSteps];
+    bool ok[kQuantSteps];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float s = fmaxf(am, 1e-6f) * (1.0f / 127.0f);
-    int q[4];
-    uint32_t packed = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      q[j] = min(127, max(-127, __float2int_rn(__fdiv_rn(f[j], s))));   // IEEE quotient, ties to even
-      packed |= (static_cast<uint32_t>(q[j]) & 0xFFu) << (8 * j);
+    for (int j = 0; j < kQuantSteps; ++j) {
+      const int64_t u = base + 2 * j + half;
+      ok[j] = u < units;
+      t[j] = ok[j] ? static_cast<int>(u / nch) : 0;
+      c[j] = ok[j] ? static_cast<int>(u - static_cast<int64_t>(t[j]) * nch) : 0;
+      h[j][0] = h[j][1] = make_uint2(0u, 0u);
+      if (ok[j]) {
+        const uint2* src = reinterpret_cast<const uint2*>(x + t[j] * ldx + c[j] * kChunk + 8 * hl);
+        h[j][0] = src[0];
+        h[j][1] = src[1];
+      }
     }
-    *reinterpret_cast<uint32_t*>(xq + t * ldq + c * kChunk + 4 * lane) = packed;
-    int sum = q[0] + q[1] + q[2] + q[3];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) {
-      sx[static_cast<int64_t>(t) * nch + c] = s;
-      rs[static_cast<int64_t>(t) * nch + c] = sum;
+    for (int j = 0; j < kQuantSteps; ++j) {
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t w = e == 0 ? h[j][0].x : e == 1 ? h[j][0].y : e == 2 ? h[j][1].x : h[j][1].y;
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w));
+        f[2 * e] = v.x;
+        f[2 * e + 1] = v.y;
+      }
+      float am = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));   // within the half
+      const float s = fmaxf(am, 1e-6f) * (1.0f / 127.0f);
+      uint32_t packed[2] = {0u, 0u};
+      int sum = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int q = min(127, max(-127, __float2int_rn(__fdiv_rn(f[e], s))));   // IEEE quotient, ties to even
+        packed[e >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (e & 3));
+        sum += q;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (ok[j]) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(xq + t[j] * ldq + c[j] * kChunk + 8 * hl);
+        dst[0] = packed[0];
+        dst[1] = packed[1];
+        if (hl == 0) {
+          sx[static_cast<int64_t>(t[j]) * nch + c[j]] = s;
+          rs[static_cast<int64_t>(t[j]) * nch + c[j]] = sum;
+        }
+      }
     }
   }
 }
@@ -134,7 +167,9 @@ int tlx_act_quant_q8(const void* x, int64_t ldx, int m, int64_t k, int8_t* xq, i
   if (ldx < k || ldq < k || ldx % 4 || ldq % 4 || !aligned(x, 8) || !aligned(xq, 4)) return TLX_ERR_ALIGN;
   const int nch = static_cast<int>(k / kChunk);
   const int64_t units = static_cast<int64_t>(m) * nch;
-  const int blocks = static_cast<int>(units / 8 < 148 * 16 ? (units + 7) / 8 : 148 * 16);
+  const int64_t per_block = 8 * 2 * kQuantSteps;   // chunks one CTA takes per pass
+  const int blocks = static_cast<int>((units + per_block - 1) / per_block < 148 * 16 ? (units + per_block - 1) / per_block
+                                                                                     : 148 * 16);
   act_quant_q8_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(x), ldx, m,
                                                                              nch, xq, ldq, sx, rs);
   return cudaGetLastError() == cudaSuccess ? TLX_OK : TLX_ERR_LAUNCH;
