@@ -171,3 +171,22 @@ def test_w4a8_gate_up_config5_sampled(config5_weights):
     got = act[:, torch.from_numpy(rows).cuda()].cpu().numpy()
     check_rows(got, ref, CONTRACT)
     check_rows(got, ref, TIGHT)
+
+
+def test_w4a8_wrappers_reject_mismatched_tables():
+    from thunderllamax_b200._lib import TLXError
+
+    m, k, n = 8, 512, 128
+    x = torch.zeros((m, k), dtype=torch.float16, device="cuda")
+    with pytest.raises(TLXError):
+        prefill.act_quant_q8(x, sx=torch.empty((m, k // 256), dtype=torch.float32, device="cuda"))
+    with pytest.raises(TLXError):
+        prefill.act_quant_q8(x, rs=torch.empty((m, k // 128), dtype=torch.float32, device="cuda"))
+    xq, sx, _ = prefill.act_quant_q8(x)
+    w = torch.zeros(16, dtype=torch.uint8, device="cuda")     # never reached: the checks run first
+    ws = prefill.PrefillWorkspace(m, k)
+    with pytest.raises(TLXError):
+        prefill.w4a8_gate_up(w, w, xq, sx[:, :2].contiguous(), n, ws)
+    with pytest.raises(TLXError):
+        prefill.w4a8_gate_up(w, w, xq, sx, n, ws, lut=torch.zeros(512, dtype=torch.int8, device="cuda"))
+    torch.cuda.synchronize()

@@ -102,6 +102,12 @@ def lut8(device: str = "cuda") -> torch.Tensor:
     return torch.from_numpy(iq3xxs_levels_lut8().copy()).to(device)
 
 
+def _check_chunk_table(t: torch.Tensor, dtype, m: int, k: int, name: str):
+    """One value per (token, 128-k chunk), contiguous: the layout the kernels index."""
+    if t.dtype != dtype or tuple(t.shape) != (m, k // 128) or not t.is_contiguous():
+        raise TLXError(f"{name} must be a contiguous {dtype} [tokens, k / 128] tensor")
+
+
 def act_quant_q8(x: torch.Tensor, xq: torch.Tensor = None, sx: torch.Tensor = None, rs: torch.Tensor = None):
     """fp16 x[m, k] -> (xq int8 [m, k], sx fp32 [m, k/128], rs int32 [m, k/128]): per (token, 128-k
     chunk) s = max(max|x|, 1e-6) / 127, xq = clamp(rint(x / s)), rs = sum of xq (reference p8q8x,
@@ -116,6 +122,10 @@ def act_quant_q8(x: torch.Tensor, xq: torch.Tensor = None, sx: torch.Tensor = No
         sx = torch.empty((m, k // 128), dtype=torch.float32, device=x.device)
     if rs is None:
         rs = torch.empty((m, k // 128), dtype=torch.int32, device=x.device)
+    if xq.dtype != torch.int8 or tuple(xq.shape) != (m, k) or xq.stride(1) != 1:
+        raise TLXError("xq must be a row-major int8 [tokens, k] tensor")
+    _check_chunk_table(sx, torch.float32, m, k, "sx")
+    _check_chunk_table(rs, torch.int32, m, k, "rs")
     rc = _lib.lib().tlx_act_quant_q8(ops._ptr(x), x.stride(0), m, k, ops._ptr(xq), xq.stride(0), ops._ptr(sx),
                                      ops._ptr(rs), ops._stream(x))
     check(rc, "act_quant_q8")
@@ -130,10 +140,15 @@ def w4a8_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, xq: torch.Tensor, sx:
     if xq.dim() != 2 or xq.stride(1) != 1 or xq.dtype != torch.int8:
         raise TLXError("xq must be a row-major int8 [tokens, k] tensor")
     m, k = xq.shape
+    _check_chunk_table(sx, torch.float32, m, k, "sx")
     if act is None:
         act = torch.empty((m, n_rows), dtype=torch.float32, device=xq.device)
     if lut is None:
         lut = lut8(str(xq.device))
+    if lut.dtype != torch.int8 or lut.numel() != 1024 or not lut.is_contiguous():
+        raise TLXError("lut must be the 1024-entry int8 codebook (prefill.lut8())")
+    if act.dtype != torch.float32 or act.shape[0] != m or act.shape[1] < n_rows or act.stride(1) != 1:
+        raise TLXError("act must be a row-major fp32 [tokens, >= n_rows] tensor")
     rc = _lib.lib().tlx_prefill_w4a8_gate_up(ops._ptr(w_gate), ops._ptr(w_up), ops._ptr(lut), ops._ptr(xq),
                                              xq.stride(0), ops._ptr(sx), m, n_rows, k, ops._ptr(act), act.stride(0),
                                              ops._ptr(ws.buf), ws.nbytes, ops._stream(xq))
