@@ -190,3 +190,21 @@ def test_w4a8_wrappers_reject_mismatched_tables():
     with pytest.raises(TLXError):
         prefill.w4a8_gate_up(w, w, xq, sx, n, ws, lut=torch.zeros(512, dtype=torch.int8, device="cuda"))
     torch.cuda.synchronize()
+
+
+def test_act_quant_q8_reference_golden_rows_and_ties():
+    """The reference's own quantiser outputs (tests/golden/golden_w4a8.npz: an all-zero
+    chunk, values under the 1e-6 floor, values near the fp16 range, .5 ties), and rows
+    whose every quotient is an exact half-integer (chunk maximum 127, so s = 1)."""
+    gold = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_w4a8.npz"))
+    xq, sx, rs = prefill.act_quant_q8(torch.from_numpy(gold["q8_x"]).cuda())
+    torch.cuda.synchronize()
+    quant_equal(xq, sx, rs, (gold["q8_xq"], gold["q8_sx"], gold["q8_rs"]))
+    rng = np.random.default_rng(17)
+    m, k = 64, 1024
+    x = (rng.integers(-127, 127, (m, k)) + 0.5).astype(np.float16)    # exact half-integers
+    x.reshape(m, k // 128, 128)[:, :, 0] = 127.0
+    xq, sx, rs = prefill.act_quant_q8(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    assert (sx == 1.0).all()
+    quant_equal(xq, sx, rs, oracle.act_quant_q8(x))
