@@ -79,19 +79,11 @@ __global__ void __launch_bounds__(256) act_quant_q8_kernel(const __half* __restr
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));   // within the half
       const float s = fmaxf(am, 1e-6f) * (1.0f / 127.0f);
-      const float r = __frcp_rn(s);
       uint32_t packed[2] = {0u, 0u};
       int sum = 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        // rint of the IEEE quotient fl(x / s), ties to even.  y = fl(x * fl(1/s)) is
-        // within 1.5 * 2^-23 * |x / s| <= 2.3e-5 of fl(x / s) (|x / s| <= 128), so when y
-        // is more than 2^-15 from every half-integer both round to the same integer;
-        // otherwise (and for NaN / inf) the quotient itself is formed.
-        const float y = f[e] * r;
-        const float frac = fabsf(y - truncf(y));
-        const float qf = fabsf(frac - 0.5f) > 3.0517578125e-5f ? y : __fdiv_rn(f[e], s);
-        const int q = min(127, max(-127, __float2int_rn(qf)));
+        const int q = min(127, max(-127, __float2int_rn(__fdiv_rn(f[e], s))));   // IEEE quotient, ties to even
         packed[e >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (e & 3));
         sum += q;
       }
