@@ -433,8 +433,9 @@ int tlx_prefill_gemm(int qtype, const void* w, const uint32_t* grid, const void*
                      int64_t n_rows, int64_t k, float* y, int64_t ldy, void* ws, size_t ws_bytes, void* stream);
 
 /* ---- W4A8 prefill tier (int8 tokens x linearised IQ3_XXS levels) ------------------
- * tlx_act_quant_q8: fp16 x[m][k] (k % 128 == 0, ldx % 4 == 0) -> xq int8 [m][ldq],
- * sx fp32 [m][k/128], rs int32 [m][k/128].  Per (token, 128-k chunk):
+ * tlx_act_quant_q8: fp16 x[m][k] (k % 128 == 0; ldx % 4 == 0, x 8-byte aligned) ->
+ * xq int8 [m][ldq] (ldq % 4 == 0, 4-byte aligned), sx fp32 [m][k/128] and rs int32
+ * [m][k/128] (contiguous).  Per (token, 128-k chunk):
  * s = max(max|x|, 1e-6) * (1/127) in fp32, xq = clamp(rint(x / s), -127, 127) (IEEE
  * quotient, ties to even), rs = sum of the stored xq; bit-identical to the reference
  * quantiser.  Replaces p8q8x (engine/pfk_q8.cu:24-59, launched at
