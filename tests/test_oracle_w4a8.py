@@ -98,3 +98,23 @@ def test_w4a8_entry_points_host_checks():
     assert f(*args(lut=a + 2)) == err_align        # lut8 not 4-byte aligned
     assert f(*args(wg=a + 8)) == err_align         # weights not 16-byte aligned
     assert f(*args(wsb=1024)) == err_ws            # workspace smaller than the token image
+
+
+def test_tier_weights_are_one_fp16_rounding_of_the_reference_weights():
+    # the library's decode of a linearised weight: level * (2s+1) (exact in fp16, at most
+    # 15 * 31), times fp16(d / 4), one fp16 rounding; the factor 4.0507 rides on the
+    # staged token values.  Against the reference's weights (dq_lin, the golden fixture)
+    # that is within 2^-11 relative, plus the fp32 rounding of the reference's own scale.
+    raw = GOLD["lin_raw"]
+    n, nb = raw.shape[0], K // 256
+    blk = raw.reshape(n, nb, 98)
+    d = np.ascontiguousarray(blk[..., 0:2]).view(np.float16)[..., 0]            # [n, nb]
+    sw = np.ascontiguousarray(blk[..., 66:98]).view(np.uint32)                   # [n, nb, 8]
+    m2 = (2 * (sw >> 28) + 1).astype(np.float16)                                 # 2s+1
+    lv = GOLD["lut8"].reshape(256, 4)[blk[..., 2:66]].reshape(n, nb, 8, 32).astype(np.float16)
+    prod = lv * m2[..., None]
+    assert np.array_equal(prod.astype(np.float64), lv.astype(np.float64) * m2[..., None].astype(np.float64))
+    a = prod * (d.astype(np.float32) * np.float32(0.25)).astype(np.float16)[..., None, None]
+    ours = np.abs(a.astype(np.float64).reshape(n, K)) * 4.0507
+    ref = np.abs(GOLD["lin_w"].astype(np.float64))
+    assert (np.abs(ours - ref) <= ref * (2.0 ** -11 + 2.0 ** -21)).all()
